@@ -1,0 +1,149 @@
+/*
+ * chronos_moe.h — C ABI of the sm_100a MoE feed-forward extension.
+ *
+ * One call computes the Chronos MoE feed-forward layer
+ * (chronos/model/moe_chronos.py:95-281, ChronosMOEFeedForward.forward):
+ *
+ *   scores   = softmax(x @ router_w^T [+ router_bias])            (:112)
+ *   topk     = top_k(scores), optional renormalisation            (:124-128)
+ *   shared   = mean_j SwiGLU_j(x)                                 (:90-93)
+ *   y_t      = sum_k w_tk * (a_e * SwiGLU_e(x_t) + (1 - a_e) * shared_t)
+ *              + shared_t                                          (:190-268,
+ *                                                                   chronos/mlx/moe.py:160-166)
+ *
+ * where SwiGLU(x) = down(silu(gate(x)) * up(x)) is the bias-free expert of
+ * the minimind FeedForward (restated at chronos/mlx/moe.py:13-23) and a_e is
+ * the effective availability of routed expert e (1 = resident, 0 = cache
+ * miss served by the shared experts).
+ *
+ * Routing contract (bit-exact, identical on every run): logits are fp32
+ * sums over h = 0..H-1 in increasing order with one fused multiply-add per
+ * element (operands widened to fp32), plus router_bias[e] when given.
+ * Experts are ranked by (logit descending, expert index ascending); the
+ * top-k weights are the fp32 softmax probabilities of the chosen experts,
+ * renormalised by (sum + 1e-20) when norm_topk is set.
+ *
+ * Conventions: every pointer in ChronosMoeArgs is a DEVICE pointer unless
+ * stated otherwise; all matrices are row-major and contiguous with the
+ * nn.Linear [out, in] layout.  The caller allocates every buffer, including
+ * the workspace (size from chronos_moe_workspace_size).  Calls are ordered
+ * on the given stream; nothing here synchronises the host unless the
+ * function's comment says so.  No function aborts, traps or exits.
+ */
+#ifndef CHRONOS_MOE_H_
+#define CHRONOS_MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CHRONOS_MOE_ABI_VERSION 1
+
+/* Return codes. */
+#define CHRONOS_OK 0
+#define CHRONOS_ERR_INVALID_ARG 1
+#define CHRONOS_ERR_WORKSPACE_TOO_SMALL 2
+#define CHRONOS_ERR_CUDA 3
+#define CHRONOS_ERR_EXPERT_NOT_READY 4 /* a device-side ready-flag wait ran out */
+#define CHRONOS_ERR_NCCL 5
+#define CHRONOS_ERR_PIPELINE_TIMEOUT 6 /* an internal pipeline wait ran out */
+
+/* Element types of x, router_w, the expert weights, y and router_probs. */
+#define CHRONOS_DTYPE_BF16 0
+#define CHRONOS_DTYPE_FP16 1
+#define CHRONOS_DTYPE_FP32 2
+
+/* Flags (ChronosMoeArgs.flags). */
+/* topk_idx / topk_weight are INPUTS produced by an earlier
+ * chronos_moe_route call (the host-hook slow path); routing is skipped. */
+#define CHRONOS_FLAG_PREROUTED 0x1
+
+typedef struct ChronosMoeShape {
+    int64_t num_tokens;  /* N = B*S (x.view(-1, H), moe_chronos.py:110-111); 0 is allowed */
+    int32_t hidden;      /* H = hidden_size */
+    int32_t num_experts; /* E = num_experts (routed) */
+    int32_t top_k;       /* k = num_experts_per_tok, 1 <= k <= min(E, 16) */
+    int32_t ffn;         /* F = moe_intermediate_size */
+    int32_t num_shared;  /* S_h = num_shared_experts, 0..8 */
+    int32_t dtype;       /* CHRONOS_DTYPE_* */
+} ChronosMoeShape;
+
+typedef struct ChronosMoeArgs {
+    ChronosMoeShape shape;
+    int32_t norm_topk; /* config.norm_topk_prob (moe_chronos.py:127-128) */
+    int32_t flags;     /* CHRONOS_FLAG_* */
+
+    const void* x;            /* [N, H] */
+    const void* router_w;     /* [E, H]  gate.weight (moe_chronos.py:54) */
+    const float* router_bias; /* [E] fp32 added to the logits, or NULL */
+
+    /* Routed expert weights, stacked: slot p holds one expert.
+     * w_gate/w_up: [P, F, H] (experts[e].gate_proj / up_proj .weight),
+     * w_down: [P, H, F] (experts[e].down_proj.weight). */
+    const void* w_gate;
+    const void* w_up;
+    const void* w_down;
+    int32_t pool_slots;             /* P */
+    const int32_t* slot_of_expert;  /* [E] slot of expert e, or NULL for slot == e.
+                                       A negative slot means "not resident": the
+                                       expert is treated as a = 0 (shared fallback). */
+    /* Shared experts (moe_chronos.py:59-62): [S_h, F, H], [S_h, F, H], [S_h, H, F]. */
+    const void* w_shared_gate;
+    const void* w_shared_up;
+    const void* w_shared_down;
+
+    const float* avail; /* [E] effective availability a_e in [0, 1], or NULL for all 1 */
+
+    /* Expert readiness (chronos/io/expert_store.py:480-543): when ready_flags is
+     * non-NULL the grouped GEMMs wait, per SELECTED expert only, until
+     * ready_flags[e] >= ready_epoch before reading its weights.  A wait longer
+     * than spin_limit_ns records CHRONOS_ERR_EXPERT_NOT_READY in *status and
+     * skips that expert's tiles (its output is then incomplete). */
+    const int32_t* ready_flags;
+    int32_t ready_epoch;
+    int64_t spin_limit_ns; /* <= 0 selects the default (2 s) */
+
+    /* Outputs. */
+    void* y;              /* [N, H], required */
+    void* router_probs;   /* [N, E] softmax probabilities in x dtype, or NULL */
+    int32_t* topk_idx;    /* [N, k], or NULL (an input with CHRONOS_FLAG_PREROUTED) */
+    float* topk_weight;   /* [N, k], or NULL (an input with CHRONOS_FLAG_PREROUTED) */
+    int32_t* expert_counts; /* [E] tokens routed to each expert (all selections), or NULL */
+    float* expert_mass;     /* [E] sum of top-k weights routed to each expert, or NULL */
+
+    void* workspace;       /* >= chronos_moe_workspace_size(&shape) bytes, 256-byte aligned */
+    size_t workspace_bytes;
+    int32_t* status;       /* [1] device word; kernels write a CHRONOS_ERR_* code on a
+                              device-side failure.  The caller zeroes it.  May be NULL. */
+} ChronosMoeArgs;
+
+/* Bytes of workspace one chronos_moe_forward / chronos_moe_route call with
+ * this shape needs (a function of the shape only, never of the routing).
+ * Returns 0 for an invalid shape; chronos_moe_last_error() says why. */
+size_t chronos_moe_workspace_size(const ChronosMoeShape* shape);
+
+/* The whole layer (replaces ChronosMOEFeedForward.forward's arithmetic,
+ * moe_chronos.py:110-268, both the standard and the masked branch). */
+int chronos_moe_forward(const ChronosMoeArgs* args, void* cuda_stream);
+
+/* Routing only (moe_chronos.py:112-128): writes topk_idx, topk_weight and,
+ * when given, router_probs, expert_counts and expert_mass.  Used by hosts
+ * that must see the selected experts before the expert GEMMs run (runtime
+ * hooks `runtime_touch_expert` / `runtime_on_demand_loader`,
+ * moe_chronos.py:228-248).  topk_idx and topk_weight are required. */
+int chronos_moe_route(const ChronosMoeArgs* args, void* cuda_stream);
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* chronos_moe_last_error(void);
+
+/* CHRONOS_MOE_ABI_VERSION of the loaded library. */
+int chronos_moe_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CHRONOS_MOE_H_ */
