@@ -36,6 +36,12 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#if defined(__GNUC__)
+#define CHRONOS_API __attribute__((visibility("default")))
+#else
+#define CHRONOS_API
+#endif
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -101,7 +107,8 @@ typedef struct ChronosMoeArgs {
      * non-NULL the grouped GEMMs wait, per SELECTED expert only, until
      * ready_flags[e] >= ready_epoch before reading its weights.  A wait longer
      * than spin_limit_ns records CHRONOS_ERR_EXPERT_NOT_READY in *status and
-     * skips that expert's tiles (its output is then incomplete). */
+     * the kernel goes on with whatever the slot holds, so that expert's
+     * contribution to this call is undefined (the status says so). */
     const int32_t* ready_flags;
     int32_t ready_epoch;
     int64_t spin_limit_ns; /* <= 0 selects the default (2 s) */
@@ -123,24 +130,28 @@ typedef struct ChronosMoeArgs {
 /* Bytes of workspace one chronos_moe_forward / chronos_moe_route call with
  * this shape needs (a function of the shape only, never of the routing).
  * Returns 0 for an invalid shape; chronos_moe_last_error() says why. */
-size_t chronos_moe_workspace_size(const ChronosMoeShape* shape);
+CHRONOS_API size_t chronos_moe_workspace_size(const ChronosMoeShape* shape);
 
 /* The whole layer (replaces ChronosMOEFeedForward.forward's arithmetic,
  * moe_chronos.py:110-268, both the standard and the masked branch). */
-int chronos_moe_forward(const ChronosMoeArgs* args, void* cuda_stream);
+CHRONOS_API int chronos_moe_forward(const ChronosMoeArgs* args, void* cuda_stream);
 
 /* Routing only (moe_chronos.py:112-128): writes topk_idx, topk_weight and,
  * when given, router_probs, expert_counts and expert_mass.  Used by hosts
  * that must see the selected experts before the expert GEMMs run (runtime
  * hooks `runtime_touch_expert` / `runtime_on_demand_loader`,
  * moe_chronos.py:228-248).  topk_idx and topk_weight are required. */
-int chronos_moe_route(const ChronosMoeArgs* args, void* cuda_stream);
+CHRONOS_API int chronos_moe_route(const ChronosMoeArgs* args, void* cuda_stream);
 
 /* Message of the last failing call on this host thread ("" if none). */
-const char* chronos_moe_last_error(void);
+CHRONOS_API const char* chronos_moe_last_error(void);
 
 /* CHRONOS_MOE_ABI_VERSION of the loaded library. */
-int chronos_moe_abi_version(void);
+CHRONOS_API int chronos_moe_abi_version(void);
+
+/* sizeof(ChronosMoeArgs) as compiled into the library, so an FFI binding can
+ * check its mirror of the struct. */
+CHRONOS_API size_t chronos_moe_args_size(void);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,134 @@
+"""ctypes binding of the C ABI declared in include/chronos_moe.h.
+
+The library is ``project_chronos_b200/libchronos_moe.so`` (built in-tree by
+``project_chronos_b200.build``).  Loading fails loudly: there is no other
+implementation of this layer to fall back to.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libchronos_moe.so")
+
+CHRONOS_OK = 0
+CHRONOS_ERR_INVALID_ARG = 1
+CHRONOS_ERR_WORKSPACE_TOO_SMALL = 2
+CHRONOS_ERR_CUDA = 3
+CHRONOS_ERR_EXPERT_NOT_READY = 4
+CHRONOS_ERR_NCCL = 5
+CHRONOS_ERR_PIPELINE_TIMEOUT = 6
+
+ERROR_NAMES = {
+    CHRONOS_ERR_INVALID_ARG: "CHRONOS_ERR_INVALID_ARG",
+    CHRONOS_ERR_WORKSPACE_TOO_SMALL: "CHRONOS_ERR_WORKSPACE_TOO_SMALL",
+    CHRONOS_ERR_CUDA: "CHRONOS_ERR_CUDA",
+    CHRONOS_ERR_EXPERT_NOT_READY: "CHRONOS_ERR_EXPERT_NOT_READY",
+    CHRONOS_ERR_NCCL: "CHRONOS_ERR_NCCL",
+    CHRONOS_ERR_PIPELINE_TIMEOUT: "CHRONOS_ERR_PIPELINE_TIMEOUT",
+}
+
+DTYPE_BF16 = 0
+DTYPE_FP16 = 1
+DTYPE_FP32 = 2
+
+FLAG_PREROUTED = 0x1
+
+ABI_VERSION = 1
+
+# Functions declared in include/chronos_moe.h (checked against the header by the tests).
+EXPORTS = ("chronos_moe_workspace_size", "chronos_moe_forward", "chronos_moe_route",
+           "chronos_moe_last_error", "chronos_moe_abi_version", "chronos_moe_args_size")
+
+
+class ChronosMoeShape(ctypes.Structure):
+    _fields_ = [
+        ("num_tokens", ctypes.c_int64),
+        ("hidden", ctypes.c_int32),
+        ("num_experts", ctypes.c_int32),
+        ("top_k", ctypes.c_int32),
+        ("ffn", ctypes.c_int32),
+        ("num_shared", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+    ]
+
+
+class ChronosMoeArgs(ctypes.Structure):
+    _fields_ = [
+        ("shape", ChronosMoeShape),
+        ("norm_topk", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
+        ("x", ctypes.c_void_p),
+        ("router_w", ctypes.c_void_p),
+        ("router_bias", ctypes.c_void_p),
+        ("w_gate", ctypes.c_void_p),
+        ("w_up", ctypes.c_void_p),
+        ("w_down", ctypes.c_void_p),
+        ("pool_slots", ctypes.c_int32),
+        ("slot_of_expert", ctypes.c_void_p),
+        ("w_shared_gate", ctypes.c_void_p),
+        ("w_shared_up", ctypes.c_void_p),
+        ("w_shared_down", ctypes.c_void_p),
+        ("avail", ctypes.c_void_p),
+        ("ready_flags", ctypes.c_void_p),
+        ("ready_epoch", ctypes.c_int32),
+        ("spin_limit_ns", ctypes.c_int64),
+        ("y", ctypes.c_void_p),
+        ("router_probs", ctypes.c_void_p),
+        ("topk_idx", ctypes.c_void_p),
+        ("topk_weight", ctypes.c_void_p),
+        ("expert_counts", ctypes.c_void_p),
+        ("expert_mass", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+        ("status", ctypes.c_void_p),
+    ]
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+class ChronosMoeError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"{ERROR_NAMES.get(code, code)}: {message}")
+        self.code = code
+
+
+def load_library(path: str = LIB_PATH):
+    """Load (once) and return the extension; raises if it is missing or stale."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(path):
+            raise RuntimeError(
+                f"chronos MoE CUDA extension not found at {path}; build it with "
+                "`python -m project_chronos_b200.build` (nvcc, sm_100a)")
+        lib = ctypes.CDLL(path)
+        lib.chronos_moe_workspace_size.argtypes = [ctypes.POINTER(ChronosMoeShape)]
+        lib.chronos_moe_workspace_size.restype = ctypes.c_size_t
+        lib.chronos_moe_forward.argtypes = [ctypes.POINTER(ChronosMoeArgs), ctypes.c_void_p]
+        lib.chronos_moe_forward.restype = ctypes.c_int
+        lib.chronos_moe_route.argtypes = [ctypes.POINTER(ChronosMoeArgs), ctypes.c_void_p]
+        lib.chronos_moe_route.restype = ctypes.c_int
+        lib.chronos_moe_last_error.argtypes = []
+        lib.chronos_moe_last_error.restype = ctypes.c_char_p
+        lib.chronos_moe_abi_version.argtypes = []
+        lib.chronos_moe_abi_version.restype = ctypes.c_int
+        lib.chronos_moe_args_size.argtypes = []
+        lib.chronos_moe_args_size.restype = ctypes.c_size_t
+        if lib.chronos_moe_abi_version() != ABI_VERSION:
+            raise RuntimeError("chronos MoE extension ABI version mismatch; rebuild it")
+        if lib.chronos_moe_args_size() != ctypes.sizeof(ChronosMoeArgs):
+            raise RuntimeError("ChronosMoeArgs layout mismatch between the library and the binding")
+        _lib = lib
+        return lib
+
+
+def check(rc: int) -> None:
+    if rc != CHRONOS_OK:
+        msg = load_library().chronos_moe_last_error().decode(errors="replace")
+        raise ChronosMoeError(rc, msg)

@@ -1,0 +1,630 @@
+// chronos_moe.cu — the C ABI (include/chronos_moe.h): argument checks,
+// workspace layout, TMA descriptors and the launch sequence of one MoE layer.
+//
+//   route -> plan -> scatter -> gate/up GEMM [-> act] -> down GEMM -> finalize
+//
+// All launches go to the caller's stream; nothing synchronises the host.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+#include <string>
+#include <unordered_map>
+
+#include "chronos_moe.h"
+#include "common.cuh"
+#include "gemm_simt.cuh"
+#include "gemm_tc.cuh"
+#include "plan.cuh"
+#include "router.cuh"
+
+namespace chronos {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+#define CHRONOS_CUDA_CHECK(expr)                                                              \
+    do {                                                                                      \
+        cudaError_t err_ = (expr);                                                            \
+        if (err_ != cudaSuccess)                                                              \
+            return fail(CHRONOS_ERR_CUDA, "%s failed: %s (%s:%d)", #expr,                     \
+                        cudaGetErrorString(err_), __FILE__, __LINE__);                        \
+    } while (0)
+
+constexpr int kSplitMaxTokens = 64;  // decode batches up to this size may split K
+
+size_t elem_size(int dtype) { return dtype == CHRONOS_DTYPE_FP32 ? 4 : 2; }
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Workspace regions, a function of the shape only.
+struct Layout {
+    size_t grp_count, grp_off, act_rows, act_xrow, act_hrow, act_wslot, act_eid, ustart_gu,
+        ustart_dn, hdr, pos, sel_coef, shared_coef, topk_idx, topk_w, slot_tok, slot_coef, xp,
+        hid, gu, y_acc, total;
+    bool split_capable;
+};
+
+Layout make_layout(const ChronosMoeShape& s) {
+    Layout L{};
+    const size_t N = static_cast<size_t>(s.num_tokens);
+    const size_t E = s.num_experts, K = s.top_k, S = s.num_shared, H = s.hidden, F = s.ffn;
+    const size_t G = E + S;
+    const size_t es = elem_size(s.dtype);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off = align_up(off + bytes, 256);
+        return o;
+    };
+    L.grp_count = take(4 * E);
+    L.grp_off = take(4 * E);
+    L.act_rows = take(4 * G);
+    L.act_xrow = take(4 * G);
+    L.act_hrow = take(4 * G);
+    L.act_wslot = take(4 * G);
+    L.act_eid = take(4 * G);
+    L.ustart_gu = take(4 * (G + 1));
+    L.ustart_dn = take(4 * (G + 1));
+    L.hdr = take(sizeof(PlanHeader));
+    L.pos = take(4 * N * K);
+    L.sel_coef = take(4 * N * K);
+    L.shared_coef = take(4 * N);
+    L.topk_idx = take(4 * N * K);
+    L.topk_w = take(4 * N * K);
+    L.slot_tok = take(4 * (N * K + S * N));
+    L.slot_coef = take(4 * (N * K + S * N));
+    L.xp = take(es * N * K * H);
+    L.hid = take(es * (N * K + S * N) * F);
+    L.split_capable = N <= static_cast<size_t>(kSplitMaxTokens);
+    L.gu = L.split_capable ? take(4 * (N * K + S * N) * 2 * F) : off;
+    L.y_acc = take(4 * N * H);
+    L.total = off;
+    return L;
+}
+
+int validate_shape(const ChronosMoeShape* s) {
+    if (s == nullptr) return fail(CHRONOS_ERR_INVALID_ARG, "shape is NULL");
+    if (s->num_tokens < 0 || s->num_tokens > (int64_t(1) << 24))
+        return fail(CHRONOS_ERR_INVALID_ARG, "num_tokens %lld out of range [0, 2^24]",
+                    static_cast<long long>(s->num_tokens));
+    if (s->num_experts < 1 || s->num_experts > kMaxExperts)
+        return fail(CHRONOS_ERR_INVALID_ARG, "num_experts %d out of range [1, %d]", s->num_experts,
+                    kMaxExperts);
+    if (s->top_k < 1 || s->top_k > kMaxTopK || s->top_k > s->num_experts)
+        return fail(CHRONOS_ERR_INVALID_ARG, "top_k %d out of range [1, min(E, %d)]", s->top_k,
+                    kMaxTopK);
+    if (s->num_shared < 0 || s->num_shared > 8)
+        return fail(CHRONOS_ERR_INVALID_ARG, "num_shared %d out of range [0, 8]", s->num_shared);
+    if (s->hidden < 4 || s->hidden % 4 != 0 || s->hidden > 65536)
+        return fail(CHRONOS_ERR_INVALID_ARG, "hidden %d must be a multiple of 4 in [4, 65536]",
+                    s->hidden);
+    if (s->ffn < 1 || s->ffn > 65536)
+        return fail(CHRONOS_ERR_INVALID_ARG, "ffn %d out of range [1, 65536]", s->ffn);
+    if (s->dtype != CHRONOS_DTYPE_BF16 && s->dtype != CHRONOS_DTYPE_FP16 &&
+        s->dtype != CHRONOS_DTYPE_FP32)
+        return fail(CHRONOS_ERR_INVALID_ARG, "unknown dtype %d", s->dtype);
+    const int64_t slots = s->num_tokens * (s->top_k + s->num_shared);
+    if (slots > (int64_t(1) << 30))
+        return fail(CHRONOS_ERR_INVALID_ARG, "num_tokens * (top_k + num_shared) too large");
+    return CHRONOS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// TMA descriptors (cuTensorMapEncodeTiled through the runtime's driver entry
+// point), cached by (address, extents, box).
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+struct MapKey {
+    uint64_t ptr, rows, cols, box_rows, dtype;
+    bool operator==(const MapKey& o) const {
+        return ptr == o.ptr && rows == o.rows && cols == o.cols && box_rows == o.box_rows &&
+               dtype == o.dtype;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey& k) const {
+        uint64_t h = k.ptr * 0x9E3779B97F4A7C15ull;
+        h ^= k.rows + 0x632BE59BD9B4E019ull + (h << 6) + (h >> 2);
+        h ^= k.cols + (h << 6) + (h >> 2);
+        h ^= k.box_rows * 131 + k.dtype + (h << 6) + (h >> 2);
+        return static_cast<size_t>(h);
+    }
+};
+
+std::mutex g_map_mu;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+// 2-D row-major [rows, cols] tensor, tile box [box_rows, 64 columns], 128-B swizzle.
+int make_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+             int dtype) {
+    const MapKey key{reinterpret_cast<uint64_t>(base), rows, cols, box_rows,
+                     static_cast<uint64_t>(dtype)};
+    {
+        std::lock_guard<std::mutex> lk(g_map_mu);
+        auto it = g_maps.find(key);
+        if (it != g_maps.end()) {
+            *out = it->second;
+            return CHRONOS_OK;
+        }
+    }
+    EncodeTiledFn enc = get_encode_fn();
+    if (enc == nullptr) return fail(CHRONOS_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+        return fail(CHRONOS_ERR_INVALID_ARG, "TMA operand %p is not 16-byte aligned", base);
+    const cuuint64_t dims[2] = {cols, rows == 0 ? 1 : rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTcBK), box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType dt = dtype == CHRONOS_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap m;
+    const CUresult r = enc(&m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(CHRONOS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu",
+                    static_cast<int>(r), static_cast<unsigned long long>(rows),
+                    static_cast<unsigned long long>(cols));
+    {
+        std::lock_guard<std::mutex> lk(g_map_mu);
+        if (g_maps.size() > 4096) g_maps.clear();
+        g_maps.emplace(key, m);
+    }
+    *out = m;
+    return CHRONOS_OK;
+}
+
+int sm_count() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static int cached[64] = {0};
+    if (dev < 64 && cached[dev] > 0) return cached[dev];
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+    if (dev < 64) cached[dev] = n;
+    return n;
+}
+
+template <typename K>
+int set_smem(K kernel, int bytes) {
+    // idempotent; cheap enough to do per launch for the kernels that need > 48 KB
+    CHRONOS_CUDA_CHECK(
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    return CHRONOS_OK;
+}
+
+struct Ptrs {
+    uint8_t* ws;
+    const Layout* L;
+    template <typename P>
+    P* at(size_t off) const { return reinterpret_cast<P*>(ws + off); }
+};
+
+// ---------------------------------------------------------------------------
+// launch helpers
+// ---------------------------------------------------------------------------
+template <typename T>
+int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool prerouted,
+                 int32_t* topk_idx, float* topk_w, bool zero_acc) {
+    const ChronosMoeShape& s = a->shape;
+    RouteParams rp{};
+    rp.x = a->x;
+    rp.w = a->router_w;
+    rp.bias = a->router_bias;
+    rp.avail = a->avail;
+    rp.slot_of_expert = a->slot_of_expert;
+    rp.n = s.num_tokens;
+    rp.h = s.hidden;
+    rp.e = s.num_experts;
+    rp.k = s.top_k;
+    rp.num_shared = s.num_shared;
+    rp.norm_topk = a->norm_topk ? 1 : 0;
+    rp.prerouted = prerouted ? 1 : 0;
+    rp.probs = prerouted ? nullptr : a->router_probs;
+    rp.topk_idx = topk_idx;
+    rp.topk_w = topk_w;
+    rp.counts_all = prerouted ? nullptr : a->expert_counts;
+    rp.mass_all = prerouted ? nullptr : a->expert_mass;
+    rp.grp_count = w.at<int32_t>(w.L->grp_count);
+    rp.pos = w.at<int32_t>(w.L->pos);
+    rp.sel_coef = w.at<float>(w.L->sel_coef);
+    rp.shared_coef = w.at<float>(w.L->shared_coef);
+    rp.y_acc = zero_acc ? w.at<float>(w.L->y_acc) : nullptr;
+    const size_t smem = route_smem_bytes(s.num_experts);
+    if (int rc = set_smem(route_kernel<T>, static_cast<int>(smem))) return rc;
+    const unsigned grid = static_cast<unsigned>((s.num_tokens + kRouteTokens - 1) / kRouteTokens);
+    route_kernel<T><<<grid, kRouteThreads, smem, st>>>(rp);
+    CHRONOS_CUDA_CHECK(cudaGetLastError());
+    return CHRONOS_OK;
+}
+
+template <typename T, int BN, bool GATEUP, bool SPLIT>
+int launch_tc(const CUtensorMap& a0r, const CUtensorMap& a1r, const CUtensorMap& a0s,
+              const CUtensorMap& a1s, const CUtensorMap& br, const CUtensorMap& bs,
+              const TcGemmParams& p, int grid, cudaStream_t st) {
+    constexpr int smem = tc_smem_bytes(BN, GATEUP);
+    auto kern = tc_grouped_gemm<T, BN, GATEUP, SPLIT>;
+    if (int rc = set_smem(kern, smem)) return rc;
+    kern<<<grid, kTcThreads, smem, st>>>(a0r, a1r, a0s, a1s, br, bs, p);
+    CHRONOS_CUDA_CHECK(cudaGetLastError());
+    return CHRONOS_OK;
+}
+
+template <typename T, int BN>
+int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int splits_gu,
+                   int splits_dn, int kt_per_split_gu, int kt_per_split_dn) {
+    const ChronosMoeShape& s = a->shape;
+    const int dt = s.dtype;
+    const uint64_t N = static_cast<uint64_t>(s.num_tokens), H = s.hidden, F = s.ffn;
+    const uint64_t K = s.top_k, S = s.num_shared, P = a->pool_slots;
+    const uint64_t slots = N * K + S * N;
+    CUtensorMap g_r, u_r, g_s, u_s, xp_m, x_m, d_r, d_s, h_m;
+    int rc;
+    if ((rc = make_map(&g_r, a->w_gate, P * F, H, kTcBM, dt))) return rc;
+    if ((rc = make_map(&u_r, a->w_up, P * F, H, kTcBM, dt))) return rc;
+    if ((rc = make_map(&d_r, a->w_down, P * H, F, kTcBM, dt))) return rc;
+    if (S > 0) {
+        if ((rc = make_map(&g_s, a->w_shared_gate, S * F, H, kTcBM, dt))) return rc;
+        if ((rc = make_map(&u_s, a->w_shared_up, S * F, H, kTcBM, dt))) return rc;
+        if ((rc = make_map(&d_s, a->w_shared_down, S * H, F, kTcBM, dt))) return rc;
+    } else {
+        g_s = g_r;
+        u_s = u_r;
+        d_s = d_r;
+    }
+    if ((rc = make_map(&xp_m, w.ws + w.L->xp, N * K, H, BN, dt))) return rc;
+    if ((rc = make_map(&x_m, a->x, N, H, BN, dt))) return rc;
+    if ((rc = make_map(&h_m, w.ws + w.L->hid, slots, F, BN, dt))) return rc;
+
+    TcGemmParams p{};
+    p.hdr = w.at<PlanHeader>(w.L->hdr);
+    p.act_rows = w.at<int32_t>(w.L->act_rows);
+    p.act_xrow = w.at<int32_t>(w.L->act_xrow);
+    p.act_hrow = w.at<int32_t>(w.L->act_hrow);
+    p.act_wslot = w.at<int32_t>(w.L->act_wslot);
+    p.act_eid = w.at<int32_t>(w.L->act_eid);
+    p.f = static_cast<int>(F);
+    p.h = static_cast<int>(H);
+    p.hid = w.ws + w.L->hid;
+    p.gu = w.at<float>(w.L->gu);
+    p.y_acc = w.at<float>(w.L->y_acc);
+    p.slot_tok = w.at<int32_t>(w.L->slot_tok);
+    p.slot_coef = w.at<float>(w.L->slot_coef);
+    p.ready_flags = a->ready_flags;
+    p.ready_epoch = a->ready_epoch;
+    p.ready_limit_ns = a->spin_limit_ns > 0 ? static_cast<uint64_t>(a->spin_limit_ns)
+                                            : 2000000000ull;
+    p.status = a->status;
+    const int grid = sm_count();
+
+    // gate/up
+    TcGemmParams pg = p;
+    pg.ustart = w.at<int32_t>(w.L->ustart_gu);
+    pg.k_tiles = static_cast<int>(H / kTcBK);
+    pg.kt_per_split = kt_per_split_gu;
+    pg.m_tiles = static_cast<int>((F + kTcBM - 1) / kTcBM);
+    pg.w_rows = static_cast<int>(F);
+    pg.out_cols = static_cast<int>(F);
+    const bool split = splits_gu > 1;
+    if (split) {
+        CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + w.L->gu, 0, 4 * slots * 2 * F, st));
+        if ((rc = launch_tc<T, BN, true, true>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st)))
+            return rc;
+        ActParams ap{};
+        ap.gu = w.at<float>(w.L->gu);
+        ap.hid = w.ws + w.L->hid;
+        ap.hdr = p.hdr;
+        ap.n = s.num_tokens;
+        ap.f = s.ffn;
+        ap.k = s.top_k;
+        ap.num_shared = s.num_shared;
+        const int64_t total = static_cast<int64_t>(slots * F);
+        const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4 * grid));
+        act_kernel<T><<<blocks, 256, 0, st>>>(ap);
+        CHRONOS_CUDA_CHECK(cudaGetLastError());
+    } else {
+        if ((rc = launch_tc<T, BN, true, false>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st)))
+            return rc;
+    }
+    (void)splits_dn;
+    // down
+    TcGemmParams pd = p;
+    pd.ustart = w.at<int32_t>(w.L->ustart_dn);
+    pd.k_tiles = static_cast<int>(F / kTcBK);
+    pd.kt_per_split = kt_per_split_dn;
+    pd.m_tiles = static_cast<int>((H + kTcBM - 1) / kTcBM);
+    pd.w_rows = static_cast<int>(H);
+    pd.out_cols = static_cast<int>(H);
+    if ((rc = launch_tc<T, BN, false, false>(d_r, d_r, d_s, d_s, h_m, h_m, pd, grid, st))) return rc;
+    return CHRONOS_OK;
+}
+
+template <typename T>
+int launch_simt(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st) {
+    const ChronosMoeShape& s = a->shape;
+    SimtGemmParams p{};
+    p.hdr = w.at<PlanHeader>(w.L->hdr);
+    p.act_rows = w.at<int32_t>(w.L->act_rows);
+    p.act_hrow = w.at<int32_t>(w.L->act_hrow);
+    p.act_wslot = w.at<int32_t>(w.L->act_wslot);
+    p.act_eid = w.at<int32_t>(w.L->act_eid);
+    p.f = s.ffn;
+    p.h = s.hidden;
+    p.x = a->x;
+    p.hid_in = w.ws + w.L->hid;
+    p.hid_out = w.ws + w.L->hid;
+    p.y_acc = w.at<float>(w.L->y_acc);
+    p.slot_tok = w.at<int32_t>(w.L->slot_tok);
+    p.slot_coef = w.at<float>(w.L->slot_coef);
+    const int grid = 4 * sm_count();
+
+    SimtGemmParams pg = p;
+    pg.ustart = w.at<int32_t>(w.L->ustart_gu);
+    pg.m_tiles = (s.ffn + kSimtTile - 1) / kSimtTile;
+    pg.kdim = s.hidden;
+    pg.out_cols = s.ffn;
+    pg.w0r = a->w_gate;
+    pg.w1r = a->w_up;
+    pg.w0s = a->w_shared_gate;
+    pg.w1s = a->w_shared_up;
+    simt_grouped_gemm<T, true><<<grid, kSimtThreads, 0, st>>>(pg);
+    CHRONOS_CUDA_CHECK(cudaGetLastError());
+
+    SimtGemmParams pd = p;
+    pd.ustart = w.at<int32_t>(w.L->ustart_dn);
+    pd.m_tiles = (s.hidden + kSimtTile - 1) / kSimtTile;
+    pd.kdim = s.ffn;
+    pd.out_cols = s.hidden;
+    pd.w0r = a->w_down;
+    pd.w0s = a->w_shared_down;
+    simt_grouped_gemm<T, false><<<grid, kSimtThreads, 0, st>>>(pd);
+    CHRONOS_CUDA_CHECK(cudaGetLastError());
+    return CHRONOS_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int validate_args(const ChronosMoeArgs* a, bool need_experts) {
+    if (a == nullptr) return fail(CHRONOS_ERR_INVALID_ARG, "args is NULL");
+    if (int rc = validate_shape(&a->shape)) return rc;
+    const ChronosMoeShape& s = a->shape;
+    if (s.num_tokens == 0) return CHRONOS_OK;
+    if (a->x == nullptr || a->router_w == nullptr)
+        return fail(CHRONOS_ERR_INVALID_ARG, "x and router_w are required");
+    if (a->workspace == nullptr && make_layout(s).total > 0)
+        return fail(CHRONOS_ERR_INVALID_ARG, "workspace is NULL");
+    if ((reinterpret_cast<uintptr_t>(a->workspace) & 255) != 0)
+        return fail(CHRONOS_ERR_INVALID_ARG, "workspace must be 256-byte aligned");
+    if (a->workspace_bytes < make_layout(s).total)
+        return fail(CHRONOS_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < %zu required",
+                    a->workspace_bytes, make_layout(s).total);
+    if (!need_experts) return CHRONOS_OK;
+    if (a->y == nullptr) return fail(CHRONOS_ERR_INVALID_ARG, "y is required");
+    if (a->w_gate == nullptr || a->w_up == nullptr || a->w_down == nullptr)
+        return fail(CHRONOS_ERR_INVALID_ARG, "routed expert weights are required");
+    if (a->pool_slots < 1) return fail(CHRONOS_ERR_INVALID_ARG, "pool_slots must be >= 1");
+    if (a->slot_of_expert == nullptr && a->pool_slots < s.num_experts)
+        return fail(CHRONOS_ERR_INVALID_ARG, "pool_slots %d < num_experts %d without slot_of_expert",
+                    a->pool_slots, s.num_experts);
+    if (s.num_shared > 0 &&
+        (a->w_shared_gate == nullptr || a->w_shared_up == nullptr || a->w_shared_down == nullptr))
+        return fail(CHRONOS_ERR_INVALID_ARG, "shared expert weights are required (num_shared=%d)",
+                    s.num_shared);
+    if ((a->flags & CHRONOS_FLAG_PREROUTED) && (a->topk_idx == nullptr || a->topk_weight == nullptr))
+        return fail(CHRONOS_ERR_INVALID_ARG, "CHRONOS_FLAG_PREROUTED needs topk_idx and topk_weight");
+    return CHRONOS_OK;
+}
+
+template <typename T>
+int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
+    const ChronosMoeShape& s = a->shape;
+    const Layout L = make_layout(s);
+    Ptrs w{static_cast<uint8_t*>(a->workspace), &L};
+    const bool prerouted = (a->flags & CHRONOS_FLAG_PREROUTED) != 0;
+    int32_t* topk_idx = a->topk_idx ? a->topk_idx : w.at<int32_t>(L.topk_idx);
+    float* topk_w = a->topk_weight ? a->topk_weight : w.at<float>(L.topk_w);
+    const int64_t N = s.num_tokens;
+
+    const bool tc = (s.dtype != CHRONOS_DTYPE_FP32) && s.hidden % kTcBK == 0 &&
+                    s.ffn % kTcBK == 0 && aligned16(a->x) && aligned16(a->w_gate) &&
+                    aligned16(a->w_up) && aligned16(a->w_down) &&
+                    (s.num_shared == 0 || (aligned16(a->w_shared_gate) &&
+                                           aligned16(a->w_shared_up) &&
+                                           aligned16(a->w_shared_down)));
+    int bn = 128;
+    if (tc) bn = N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128;
+    const int tok_tile = tc ? bn : kSimtTile;
+    const int mt_gu = tc ? (s.ffn + kTcBM - 1) / kTcBM : (s.ffn + kSimtTile - 1) / kSimtTile;
+    const int mt_dn = tc ? (s.hidden + kTcBM - 1) / kTcBM : (s.hidden + kSimtTile - 1) / kSimtTile;
+
+    // K splits for small decode batches: enough units to cover every SM twice
+    int splits_gu = 1, kt_gu = s.hidden / kTcBK;
+    if (tc && L.split_capable) {
+        const int kt_total = s.hidden / kTcBK;
+        const int64_t groups_est = std::min<int64_t>(s.num_experts, N * s.top_k) + s.num_shared;
+        const int target = 2 * sm_count();
+        while (groups_est * mt_gu * splits_gu < target && splits_gu * 2 * 4 <= kt_total)
+            splits_gu *= 2;
+        kt_gu = (kt_total + splits_gu - 1) / splits_gu;
+        splits_gu = (kt_total + kt_gu - 1) / kt_gu;
+    }
+    int splits_dn = 1, kt_dn = s.ffn / kTcBK;
+    if (tc) {
+        const int kt_total = s.ffn / kTcBK;
+        const int64_t groups_est = std::min<int64_t>(s.num_experts, N * s.top_k) + s.num_shared;
+        const int64_t tiles_est = groups_est * ((N + bn - 1) / bn);
+        const int target = 2 * sm_count();
+        while (tiles_est * mt_dn * splits_dn < target && splits_dn * 2 * 4 <= kt_total)
+            splits_dn *= 2;
+        kt_dn = (kt_total + splits_dn - 1) / splits_dn;
+        splits_dn = (kt_total + kt_dn - 1) / kt_dn;
+    }
+
+    int rc;
+    CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + L.grp_count, 0, 4 * s.num_experts, st));
+    if (!prerouted) {
+        if (a->expert_counts)
+            CHRONOS_CUDA_CHECK(cudaMemsetAsync(a->expert_counts, 0, 4 * s.num_experts, st));
+        if (a->expert_mass)
+            CHRONOS_CUDA_CHECK(cudaMemsetAsync(a->expert_mass, 0, 4 * s.num_experts, st));
+    }
+    if ((rc = launch_route<T>(a, w, st, prerouted, topk_idx, topk_w, true))) return rc;
+
+    PlanParams pp{};
+    pp.n = N;
+    pp.e = s.num_experts;
+    pp.k = s.top_k;
+    pp.num_shared = s.num_shared;
+    pp.tok_tile = tok_tile;
+    pp.mt_gu = mt_gu;
+    pp.mt_dn = mt_dn;
+    pp.splits_gu = splits_gu;
+    pp.splits_dn = splits_dn;
+    pp.grp_count = w.at<int32_t>(L.grp_count);
+    pp.slot_of_expert = a->slot_of_expert;
+    pp.hdr = w.at<PlanHeader>(L.hdr);
+    pp.grp_off = w.at<int32_t>(L.grp_off);
+    pp.act_rows = w.at<int32_t>(L.act_rows);
+    pp.act_xrow = w.at<int32_t>(L.act_xrow);
+    pp.act_hrow = w.at<int32_t>(L.act_hrow);
+    pp.act_wslot = w.at<int32_t>(L.act_wslot);
+    pp.act_eid = w.at<int32_t>(L.act_eid);
+    pp.ustart_gu = w.at<int32_t>(L.ustart_gu);
+    pp.ustart_dn = w.at<int32_t>(L.ustart_dn);
+    plan_kernel<<<1, kPlanThreads, 0, st>>>(pp);
+    CHRONOS_CUDA_CHECK(cudaGetLastError());
+
+    ScatterParams sp{};
+    sp.x = a->x;
+    sp.n = N;
+    sp.h = s.hidden;
+    sp.k = s.top_k;
+    sp.num_shared = s.num_shared;
+    sp.topk_idx = topk_idx;
+    sp.pos = w.at<int32_t>(L.pos);
+    sp.sel_coef = w.at<float>(L.sel_coef);
+    sp.shared_coef = w.at<float>(L.shared_coef);
+    sp.grp_off = w.at<int32_t>(L.grp_off);
+    sp.xp = w.ws + L.xp;
+    sp.slot_tok = w.at<int32_t>(L.slot_tok);
+    sp.slot_coef = w.at<float>(L.slot_coef);
+    sp.copy_rows = tc ? 1 : 0;
+    {
+        const int64_t warps = N * s.top_k;
+        const unsigned blocks = static_cast<unsigned>((warps * 32 + kScatterThreads - 1) / kScatterThreads);
+        scatter_kernel<T><<<blocks, kScatterThreads, 0, st>>>(sp);
+        CHRONOS_CUDA_CHECK(cudaGetLastError());
+    }
+
+    if (tc) {
+        if constexpr (std::is_same<T, float>::value) {
+            return fail(CHRONOS_ERR_INVALID_ARG, "internal: fp32 on the tensor-core path");
+        } else {
+            switch (bn) {
+                case 16: rc = launch_tc_pair<T, 16>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn); break;
+                case 32: rc = launch_tc_pair<T, 32>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn); break;
+                case 64: rc = launch_tc_pair<T, 64>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn); break;
+                default: rc = launch_tc_pair<T, 128>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn); break;
+            }
+        }
+    } else {
+        rc = launch_simt<T>(a, w, st);
+    }
+    if (rc) return rc;
+
+    const int64_t count4 = N * s.hidden / 4;
+    const int blocks = static_cast<int>(std::min<int64_t>((count4 + 255) / 256, 8 * sm_count()));
+    finalize_kernel<T><<<blocks, 256, 0, st>>>(w.at<float>(L.y_acc), static_cast<T*>(a->y), count4);
+    CHRONOS_CUDA_CHECK(cudaGetLastError());
+    return CHRONOS_OK;
+}
+
+template <typename T>
+int route_impl(const ChronosMoeArgs* a, cudaStream_t st) {
+    const ChronosMoeShape& s = a->shape;
+    const Layout L = make_layout(s);
+    Ptrs w{static_cast<uint8_t*>(a->workspace), &L};
+    CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + L.grp_count, 0, 4 * s.num_experts, st));
+    if (a->expert_counts)
+        CHRONOS_CUDA_CHECK(cudaMemsetAsync(a->expert_counts, 0, 4 * s.num_experts, st));
+    if (a->expert_mass) CHRONOS_CUDA_CHECK(cudaMemsetAsync(a->expert_mass, 0, 4 * s.num_experts, st));
+    return launch_route<T>(a, w, st, false, a->topk_idx, a->topk_weight, false);
+}
+
+}  // namespace
+}  // namespace chronos
+
+using namespace chronos;
+
+extern "C" size_t chronos_moe_workspace_size(const ChronosMoeShape* shape) {
+    if (validate_shape(shape) != CHRONOS_OK) return 0;
+    return make_layout(*shape).total;
+}
+
+extern "C" int chronos_moe_forward(const ChronosMoeArgs* args, void* cuda_stream) {
+    g_last_error.clear();
+    if (int rc = validate_args(args, true)) return rc;
+    if (args->shape.num_tokens == 0) return CHRONOS_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    switch (args->shape.dtype) {
+        case CHRONOS_DTYPE_BF16: return forward_impl<__nv_bfloat16>(args, st);
+        case CHRONOS_DTYPE_FP16: return forward_impl<__half>(args, st);
+        default: return forward_impl<float>(args, st);
+    }
+}
+
+extern "C" int chronos_moe_route(const ChronosMoeArgs* args, void* cuda_stream) {
+    g_last_error.clear();
+    if (int rc = validate_args(args, false)) return rc;
+    if (args->shape.num_tokens == 0) return CHRONOS_OK;
+    if (args->topk_idx == nullptr || args->topk_weight == nullptr)
+        return fail(CHRONOS_ERR_INVALID_ARG, "chronos_moe_route needs topk_idx and topk_weight");
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    switch (args->shape.dtype) {
+        case CHRONOS_DTYPE_BF16: return route_impl<__nv_bfloat16>(args, st);
+        case CHRONOS_DTYPE_FP16: return route_impl<__half>(args, st);
+        default: return route_impl<float>(args, st);
+    }
+}
+
+extern "C" const char* chronos_moe_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int chronos_moe_abi_version(void) { return CHRONOS_MOE_ABI_VERSION; }
+
+extern "C" size_t chronos_moe_args_size(void) { return sizeof(ChronosMoeArgs); }

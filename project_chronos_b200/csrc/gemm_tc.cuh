@@ -1,0 +1,333 @@
+// gemm_tc.cuh — persistent grouped expert GEMMs on tcgen05 / TMEM, fed by TMA.
+//
+// One kernel template serves both halves of the expert SwiGLU
+// (minimind FeedForward, restated at chronos/mlx/moe.py:13-23):
+//
+//   GATEUP: for every active group (routed expert or shared expert) and every
+//           tile of 128 rows of its gate/up weights x BN token rows,
+//             G = W_gate[rows] . X^T,  U = W_up[rows] . X^T   (two MMAs, one
+//           shared B tile), epilogue h[token][f] = silu(G) * U in the input
+//           dtype (or, with SPLIT, fp32 partial sums reduced into a [slot, 2F]
+//           buffer when K is split across CTAs for small decode batches);
+//   DOWN:   D = W_down[rows] . h^T, epilogue y_acc[token][n] += coef * D with
+//           coef = w * a for routed slots and (1 + sum w (1-a)) / S_h for
+//           shared slots — the availability blend and the weighted combine of
+//           moe_chronos.py:255-268 fused into the GEMM.
+//
+// Orientation: weights are the M = 128 operand (A), tokens the N = BN operand
+// (B), so decode batches of 1..64 tokens use narrow N tiles instead of padding
+// M.  Both operands are K-major bf16/fp16 tiles of 64 elements (128 B, one
+// 128-byte swizzle atom) staged by TMA into an STAGES-deep shared-memory ring.
+//
+// Warp roles (192 threads, one CTA per SM, persistent over the work units):
+//   warp 0      TMA producer (one thread)
+//   warp 1      TMEM allocator + MMA issuer (one thread)
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator rows, math, stores
+// The accumulator is double-buffered in TMEM so the epilogue of one unit
+// overlaps the MMAs of the next.  Every wait is bounded (globaltimer) and
+// reports CHRONOS_ERR_PIPELINE_TIMEOUT instead of hanging.
+#pragma once
+
+#include "common.cuh"
+#include "plan.cuh"
+
+namespace chronos {
+
+constexpr int kTcThreads = 192;
+constexpr int kTcBM = 128;  // weight rows per tile (MMA M)
+constexpr int kTcBK = 64;   // K per pipeline stage (one 128-byte swizzle atom)
+constexpr uint64_t kPipelineLimitNs = 4000000000ull;
+
+struct TcGemmParams {
+    const PlanHeader* hdr;
+    const int32_t* act_rows;
+    const int32_t* act_xrow;
+    const int32_t* act_hrow;
+    const int32_t* act_wslot;
+    const int32_t* act_eid;
+    const int32_t* ustart;
+    int k_tiles;       // K / 64
+    int kt_per_split;  // k tiles per split
+    int m_tiles;       // weight-row tiles per group
+    int w_rows;        // weight rows per slot (F for gate/up, H for down)
+    int out_cols;      // F (gate/up) or H (down)
+    int f, h;
+    void* hid;               // GATEUP: [slots, F]
+    float* gu;               // GATEUP + SPLIT: [slots, 2F]
+    float* y_acc;            // DOWN: [N, H]
+    const int32_t* slot_tok;
+    const float* slot_coef;
+    const int32_t* ready_flags;
+    int32_t ready_epoch;
+    uint64_t ready_limit_ns;
+    int32_t* status;
+};
+
+__host__ __device__ constexpr int tc_stage_bytes(int bn, bool gateup) {
+    return kTcBM * kTcBK * 2 * (gateup ? 2 : 1) + bn * kTcBK * 2;
+}
+__host__ __device__ constexpr int tc_stages(int bn, bool gateup) {
+    return (200 * 1024) / tc_stage_bytes(bn, gateup) > 8 ? 8
+                                                          : (200 * 1024) / tc_stage_bytes(bn, gateup);
+}
+__host__ __device__ constexpr int tc_tmem_cols(int bn, bool gateup) {
+    // two accumulator buffers of (gateup ? 2 : 1) * bn fp32 columns, power of two >= 32
+    return (2 * bn * (gateup ? 2 : 1)) <= 32    ? 32
+           : (2 * bn * (gateup ? 2 : 1)) <= 64  ? 64
+           : (2 * bn * (gateup ? 2 : 1)) <= 128 ? 128
+           : (2 * bn * (gateup ? 2 : 1)) <= 256 ? 256
+                                                 : 512;
+}
+__host__ __device__ constexpr int tc_smem_bytes(int bn, bool gateup) {
+    return 1024 /* alignment slack */ + tc_stages(bn, gateup) * tc_stage_bytes(bn, gateup) + 256;
+}
+
+struct TcUnit {
+    int a, tok_tile, mtile, split;
+};
+
+__device__ __forceinline__ TcUnit tc_decode(const TcGemmParams& p, int num_active, int u, int bn,
+                                           int splits) {
+    int lo = 0, hi = num_active - 1;
+    while (lo < hi) {  // largest a with ustart[a] <= u
+        const int mid = (lo + hi + 1) >> 1;
+        if (p.ustart[mid] <= u) lo = mid; else hi = mid - 1;
+    }
+    TcUnit r;
+    r.a = lo;
+    int rem = u - p.ustart[lo];
+    const int tt = (p.act_rows[lo] + bn - 1) / bn;
+    r.tok_tile = rem % tt;
+    rem /= tt;
+    r.mtile = rem % p.m_tiles;
+    r.split = rem / p.m_tiles;
+    (void)splits;
+    return r;
+}
+
+template <typename T, int BN, bool GATEUP, bool SPLIT>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_grouped_gemm(const __grid_constant__ CUtensorMap tm_a0r,  // routed gate (or down)
+                    const __grid_constant__ CUtensorMap tm_a1r,  // routed up
+                    const __grid_constant__ CUtensorMap tm_a0s,  // shared gate (or down)
+                    const __grid_constant__ CUtensorMap tm_a1s,  // shared up
+                    const __grid_constant__ CUtensorMap tm_br,   // routed token rows (Xp or h)
+                    const __grid_constant__ CUtensorMap tm_bs,   // shared token rows (x or h)
+                    TcGemmParams p) {
+    constexpr int A_BYTES = kTcBM * kTcBK * 2;
+    constexpr int B_BYTES = BN * kTcBK * 2;
+    constexpr int STAGE_BYTES = tc_stage_bytes(BN, GATEUP);
+    constexpr int STAGES = tc_stages(BN, GATEUP);
+    constexpr int ACC_COLS = GATEUP ? 2 * BN : BN;
+    constexpr int TMEM_COLS = tc_tmem_cols(BN, GATEUP);
+    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N must be a multiple of 16");
+    static_assert(B_BYTES % 1024 == 0 && A_BYTES % 1024 == 0,
+                  "operand tiles must keep the 1024-byte alignment of the 128-B swizzle atoms");
+    static_assert(2 * ACC_COLS <= 512, "two accumulator buffers must fit in TMEM");
+
+    extern __shared__ uint8_t tc_smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 128);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tm_a0r);
+        prefetch_tmap(&tm_br);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_holder, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    const int num_active = p.hdr->num_active;
+    const int total = GATEUP ? p.hdr->units_gu : p.hdr->units_dn;
+    const int splits_unused = 0;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------ TMA producer ------------------------------
+            int stage = 0;
+            uint32_t phase = 0;
+            int polled_eid = -1;
+            for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
+                const TcUnit w = tc_decode(p, num_active, u, BN, splits_unused);
+                const int eid = p.act_eid[w.a];
+                const bool shared = eid < 0;
+                if (!shared && p.ready_flags != nullptr && eid != polled_eid) {
+                    // wait (bounded) for this selected expert's weights to be resident
+                    const uint64_t t0 = globaltimer_ns();
+                    bool ok = true;
+                    while (ld_acquire_gpu(p.ready_flags + eid) < p.ready_epoch) {
+                        if (globaltimer_ns() - t0 > p.ready_limit_ns) { ok = false; break; }
+                        __nanosleep(256);
+                    }
+                    if (!ok) report_status(p.status, CHRONOS_ERR_EXPERT_NOT_READY);
+                    fence_proxy_async_global();
+                    polled_eid = eid;
+                }
+                const int a_row = p.act_wslot[w.a] * p.w_rows + w.mtile * kTcBM;
+                const int b_row = (GATEUP ? p.act_xrow[w.a] : p.act_hrow[w.a]) + w.tok_tile * BN;
+                const int kt0 = w.split * p.kt_per_split;
+                const int kt1 = min(p.k_tiles, kt0 + p.kt_per_split);
+                const CUtensorMap* ma0 = shared ? &tm_a0s : &tm_a0r;
+                const CUtensorMap* ma1 = shared ? &tm_a1s : &tm_a1r;
+                const CUtensorMap* mb = (GATEUP && shared) ? &tm_bs : &tm_br;
+                for (int kt = kt0; kt < kt1; ++kt) {
+                    if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, kPipelineLimitNs, abort_flag)) {
+                        *abort_flag = 1;
+                        report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                        break;
+                    }
+                    uint8_t* sb = smem + stage * STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+                    tma_load_2d(sb, ma0, &full[stage], kt * kTcBK, a_row);
+                    if (GATEUP) tma_load_2d(sb + A_BYTES, ma1, &full[stage], kt * kTcBK, a_row);
+                    tma_load_2d(sb + (GATEUP ? 2 : 1) * A_BYTES, mb, &full[stage], kt * kTcBK, b_row);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------ MMA issuer ------------------------------
+            constexpr uint32_t IDESC = idesc_f16(kTcBM, BN, AbFormat<T>::value);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
+                const TcUnit w = tc_decode(p, num_active, u, BN, splits_unused);
+                const int kt0 = w.split * p.kt_per_split;
+                const int kt1 = min(p.k_tiles, kt0 + p.kt_per_split);
+                if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, kPipelineLimitNs, abort_flag)) {
+                    *abort_flag = 1;
+                    report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d0 = tmem_base + static_cast<uint32_t>(acc * ACC_COLS);
+                const uint32_t d1 = d0 + BN;
+                bool failed = false;
+                for (int kt = kt0; kt < kt1; ++kt) {
+                    if (!mbar_wait_bounded(&full[stage], phase, kPipelineLimitNs, abort_flag)) {
+                        *abort_flag = 1;
+                        report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                        failed = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa0 = smem_u32(smem + stage * STAGE_BYTES);
+                    const uint32_t sa1 = sa0 + A_BYTES;
+                    const uint32_t sbb = sa0 + (GATEUP ? 2 : 1) * A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < kTcBK / 16; ++kk) {
+                        const uint32_t accum = (kt > kt0 || kk > 0) ? 1u : 0u;
+                        const uint64_t db = sdesc_k_sw128(sbb + kk * 32);
+                        umma_f16(d0, sdesc_k_sw128(sa0 + kk * 32), db, IDESC, accum);
+                        if (GATEUP) umma_f16(d1, sdesc_k_sw128(sa1 + kk * 32), db, IDESC, accum);
+                    }
+                    umma_commit(&empty[stage]);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+                if (failed) break;
+                umma_commit(&tfull[acc]);
+                if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+            }
+        }
+    } else {
+        // ------------------------------ epilogue ------------------------------
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int row_in_tile = q * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int u = blockIdx.x; u < total; u += gridDim.x) {
+            const TcUnit w = tc_decode(p, num_active, u, BN, splits_unused);
+            if (!mbar_wait_bounded(&tfull[acc], acc_phase, kPipelineLimitNs, abort_flag)) {
+                *abort_flag = 1;
+                report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(acc * ACC_COLS);
+            const int wrow = w.mtile * kTcBM + row_in_tile;
+            const bool row_ok = wrow < p.out_cols;
+            const int rows = p.act_rows[w.a];
+            const int tok0 = w.tok_tile * BN;
+            const int64_t hrow0 = p.act_hrow[w.a];
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 16) {
+                float g[16];
+                tmem_ld16(taddr + c, g);
+                if constexpr (GATEUP) {
+                    float uu[16];
+                    tmem_ld16(taddr + BN + c, uu);
+                    tmem_wait_ld();
+                    if (row_ok) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int tok = tok0 + c + j;
+                            if (tok < rows) {
+                                const int64_t slot = hrow0 + tok;
+                                if constexpr (SPLIT) {
+                                    red_add_f32(p.gu + slot * 2 * p.f + wrow, g[j]);
+                                    red_add_f32(p.gu + slot * 2 * p.f + p.f + wrow, uu[j]);
+                                } else {
+                                    static_cast<T*>(p.hid)[slot * p.f + wrow] =
+                                        from_f32<T>(silu_f32(g[j]) * uu[j]);
+                                }
+                            }
+                        }
+                    }
+                } else {
+                    tmem_wait_ld();
+                    if (row_ok) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int tok = tok0 + c + j;
+                            if (tok < rows) {
+                                const int64_t slot = hrow0 + tok;
+                                const int64_t t = p.slot_tok[slot];
+                                red_add_f32(p.y_acc + t * p.h + wrow, p.slot_coef[slot] * g[j]);
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+            if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+}  // namespace chronos

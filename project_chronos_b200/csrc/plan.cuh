@@ -1,0 +1,213 @@
+// plan.cuh — token-to-expert permutation and the small elementwise kernels.
+//
+// Replaces the reference's per-expert host loop (moe_chronos.py:149-154 and
+// :207-262: `(topk_idx == i)`, `.nonzero()`, `x_flat[token_idx]`, with one or
+// two host syncs per expert) by three device steps:
+//   plan    one block: exclusive scan of the expert-group sizes into slot
+//           offsets, the list of active groups (routed experts with at least
+//           one available selection, then the shared experts) and the
+//           per-group tile counts the persistent GEMMs walk;
+//   scatter one warp per (token, choice): slot = offset[e] + position,
+//           slot -> (token, w*a), and the x row copied into the expert-sorted
+//           buffer with 16-byte loads/stores;
+//   finalize fp32 accumulator -> output dtype.
+#pragma once
+
+#include "common.cuh"
+
+namespace chronos {
+
+// Written by plan_kernel, read by every later kernel of the call.
+struct PlanHeader {
+    int32_t num_active;      // active groups
+    int32_t routed_rows;     // routed slots in use (<= N*k)
+    int32_t units_gu;        // work units of the gate/up GEMM
+    int32_t units_dn;        // work units of the down GEMM
+    int32_t max_rows;        // largest group
+    int32_t pad[3];
+};
+
+struct PlanParams {
+    int64_t n;
+    int e, k, num_shared;
+    int tok_tile;                 // token rows per GEMM tile
+    int mt_gu, mt_dn;             // weight-row tiles per group (gate/up, down)
+    int splits_gu, splits_dn;     // K splits per tile
+    const int32_t* grp_count;     // [E]
+    const int32_t* slot_of_expert;  // [E] or null
+    PlanHeader* hdr;
+    int32_t* grp_off;             // [E] first slot of routed group e
+    // active groups, [E + S_h] each (+1 for the unit prefix arrays)
+    int32_t* act_rows;
+    int32_t* act_xrow;   // first row of the group's token rows in its B source
+    int32_t* act_hrow;   // first row of the group in the hidden buffer
+    int32_t* act_wslot;  // weight slot (routed pool slot, or shared index)
+    int32_t* act_eid;    // routed expert id, or -1 for a shared group
+    int32_t* ustart_gu;  // [A + 1]
+    int32_t* ustart_dn;  // [A + 1]
+};
+
+constexpr int kPlanThreads = 1024;
+
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
+    __shared__ int32_t s_scan[kPlanThreads];
+    __shared__ int32_t s_act[kPlanThreads];
+    const int tid = threadIdx.x;
+    const int E = p.e;
+    // E <= 256 (validated on the host), so one element per thread
+    const int cnt = tid < E ? p.grp_count[tid] : 0;
+    const int is_act = (tid < E && cnt > 0) ? 1 : 0;
+    s_scan[tid] = cnt;
+    s_act[tid] = is_act;
+    __syncthreads();
+    // Hillis-Steele inclusive scans (E <= 256 -> 8 steps)
+    for (int o = 1; o < kPlanThreads; o <<= 1) {
+        const int a = tid >= o ? s_scan[tid - o] : 0;
+        const int b = tid >= o ? s_act[tid - o] : 0;
+        __syncthreads();
+        s_scan[tid] += a;
+        s_act[tid] += b;
+        __syncthreads();
+    }
+    const int total_routed = s_scan[kPlanThreads - 1];
+    const int n_routed_act = s_act[kPlanThreads - 1];
+    const int S = p.num_shared;
+    const int N = static_cast<int>(p.n);
+    // shared groups first (largest), then routed groups in expert order
+    if (tid < E) {
+        const int off = s_scan[tid] - cnt;
+        p.grp_off[tid] = off;
+        if (is_act) {
+            const int a = S + s_act[tid] - 1;
+            p.act_rows[a] = cnt;
+            p.act_xrow[a] = off;
+            p.act_hrow[a] = off;
+            p.act_wslot[a] = p.slot_of_expert ? p.slot_of_expert[tid] : tid;
+            p.act_eid[a] = tid;
+        }
+    }
+    if (tid < S) {
+        p.act_rows[tid] = N;
+        p.act_xrow[tid] = 0;
+        p.act_hrow[tid] = N * p.k + tid * N;
+        p.act_wslot[tid] = tid;
+        p.act_eid[tid] = -1;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const int A = S + n_routed_act;
+        int ugu = 0, udn = 0, mx = 0;
+        for (int a = 0; a < A; ++a) {
+            const int rows = p.act_rows[a];
+            const int tt = (rows + p.tok_tile - 1) / p.tok_tile;
+            p.ustart_gu[a] = ugu;
+            p.ustart_dn[a] = udn;
+            ugu += tt * p.mt_gu * p.splits_gu;
+            udn += tt * p.mt_dn * p.splits_dn;
+            mx = max(mx, rows);
+        }
+        p.ustart_gu[A] = ugu;
+        p.ustart_dn[A] = udn;
+        p.hdr->num_active = A;
+        p.hdr->routed_rows = total_routed;
+        p.hdr->units_gu = ugu;
+        p.hdr->units_dn = udn;
+        p.hdr->max_rows = mx;
+    }
+}
+
+struct ScatterParams {
+    const void* x;
+    int64_t n;
+    int h, k, num_shared;
+    const int32_t* topk_idx;
+    const int32_t* pos;
+    const float* sel_coef;
+    const float* shared_coef;
+    const int32_t* grp_off;
+    void* xp;             // [N*k, H] expert-sorted copies of x rows
+    int32_t* slot_tok;    // [N*k + S*N]
+    float* slot_coef;     // [N*k + S*N]
+    int copy_rows;        // 0: only the slot tables (B operand read from x by row index)
+};
+
+constexpr int kScatterThreads = 256;
+
+// One warp per (token, choice); the shared-slot tables are filled by the
+// warps with choice index 0.
+template <typename T>
+__global__ void __launch_bounds__(kScatterThreads) scatter_kernel(ScatterParams p) {
+    const int64_t gw = (static_cast<int64_t>(blockIdx.x) * kScatterThreads + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t total = p.n * p.k;
+    if (gw >= total) return;
+    const int64_t t = gw / p.k;
+    const int j = static_cast<int>(gw % p.k);
+    if (j == 0 && lane < p.num_shared) {
+        const int64_t s = p.n * p.k + lane * p.n + t;
+        p.slot_tok[s] = static_cast<int32_t>(t);
+        p.slot_coef[s] = p.shared_coef[t];
+    }
+    const int ps = p.pos[gw];
+    if (ps < 0) return;
+    const int e = p.topk_idx[gw];
+    const int64_t slot = static_cast<int64_t>(p.grp_off[e]) + ps;
+    if (lane == 0) {
+        p.slot_tok[slot] = static_cast<int32_t>(t);
+        p.slot_coef[slot] = p.sel_coef[gw];
+    }
+    if (!p.copy_rows) return;
+    const T* src = static_cast<const T*>(p.x) + t * p.h;
+    T* dst = static_cast<T*>(p.xp) + slot * p.h;
+    const int bytes = p.h * static_cast<int>(sizeof(T));
+    if ((bytes & 15) == 0) {
+        const uint4* s4 = reinterpret_cast<const uint4*>(src);
+        uint4* d4 = reinterpret_cast<uint4*>(dst);
+        for (int i = lane; i < bytes / 16; i += 32) d4[i] = s4[i];
+    } else {
+        for (int i = lane; i < p.h; i += 32) dst[i] = src[i];
+    }
+}
+
+struct ActParams {
+    const float* gu;   // [rows, 2F] fp32 split-K partial sums (gate | up)
+    void* hid;         // [rows, F]
+    const PlanHeader* hdr;
+    int64_t n;
+    int f, k, num_shared;
+};
+
+// h = silu(g) * u for every slot row in use (routed rows < routed_rows, then
+// the shared rows).
+template <typename T>
+__global__ void act_kernel(ActParams p) {
+    const int64_t routed_cap = p.n * p.k;
+    const int64_t rows_total = routed_cap + p.n * p.num_shared;
+    const int routed_rows = p.hdr->routed_rows;
+    const int64_t per_row = p.f;
+    const int64_t total = rows_total * per_row;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / per_row;
+        const int c = static_cast<int>(i % per_row);
+        if (r < routed_cap && r >= routed_rows) continue;
+        const float g = p.gu[r * 2 * p.f + c];
+        const float u = p.gu[r * 2 * p.f + p.f + c];
+        static_cast<T*>(p.hid)[r * p.f + c] = from_f32<T>(silu_f32(g) * u);
+    }
+}
+
+template <typename T>
+__global__ void finalize_kernel(const float* __restrict__ y_acc, T* __restrict__ y, int64_t count4) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float4 v = reinterpret_cast<const float4*>(y_acc)[i];
+        T* d = y + 4 * i;
+        d[0] = from_f32<T>(v.x);
+        d[1] = from_f32<T>(v.y);
+        d[2] = from_f32<T>(v.z);
+        d[3] = from_f32<T>(v.w);
+    }
+}
+
+}  // namespace chronos

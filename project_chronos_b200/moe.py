@@ -1,0 +1,450 @@
+"""Drop-in ``ChronosMOEFeedForward`` whose arithmetic runs in the sm_100a kernels.
+
+Mirrors ``chronos/model/moe_chronos.py`` of FonaTech/Project_Chronos:
+
+* same constructor argument (a Chronos/MiniMind config), same submodules and
+  parameter shapes (``gate``, ``experts[e].{gate,up,down}_proj``,
+  ``shared_experts[j].*``), so ``state_dict`` keys load unchanged
+  (``chronos/io/expert_store.py:233-243``);
+* ``forward(x [B,S,H], available_expert_mask=None) -> [B,S,H]`` with the
+  reference's semantics for both branches (``moe_chronos.py:146-188`` and
+  ``:190-279``): placeholder (``LazyExpertPlaceholder``) experts and, in
+  training, mask-off experts are served by the shared-expert fallback; in eval
+  a live expert runs even when the mask calls it unavailable
+  (``moe_chronos.py:222-227``);
+* side effects kept: ``last_router_probs``, ``last_router_probs_grad``,
+  ``aux_loss``, ``aux_loss_raw``, ``last_on_demand_experts``,
+  ``last_fallback_experts``, ``last_on_demand_weight_mass``,
+  ``last_fallback_weight_mass``; runtime hooks ``runtime_miss_policy``,
+  ``runtime_on_demand_loader``, ``runtime_touch_expert`` (set by the
+  reference's inference engine, ``inference_engine.py:118-173``) are called in
+  ascending expert order for the selected experts, as the reference does.
+
+Fast path (no hooks installed): one C-ABI call, no host synchronisation; the
+bookkeeping lists are computed lazily from device tensors the first time they
+are read.  Hook path: routing runs first, the selected experts are read back
+once (one sync instead of the reference's two per expert), the hooks run, and
+the expert GEMMs run with the resulting availability.
+
+Expert weights live in stacked per-layer pools (``[E, F, H]``, ``[E, F, H]``,
+``[E, H, F]``); each expert's ``nn.Linear.weight`` is re-bound as a view into
+its pool slot, so ``load_state_dict`` writes straight into the layout the
+kernels read with TMA.  Modules swapped in later (``ExpertStore`` promoting a
+placeholder) are adopted into the pool on the next forward.
+
+There is no CPU implementation: CPU inputs raise.  Backward is not
+implemented (training-mode forward with autograd enabled raises).
+"""
+from __future__ import annotations
+
+from typing import List, Optional
+
+import numpy as np
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+
+
+def _act_fn(name: str):
+    if name in ("silu", "swish"):
+        return F.silu
+    raise ValueError(f"hidden_act={name!r}: the fused kernels implement SwiGLU with silu only")
+
+
+class FeedForward(nn.Module):
+    """Bias-free SwiGLU expert with minimind's parameter names
+    (``gate_proj``, ``up_proj``, ``down_proj``), restated at
+    ``chronos/mlx/moe.py:13-23``.  Its own ``forward`` (used only when called
+    directly, never by ``ChronosMOEFeedForward``) is the plain torch math."""
+
+    def __init__(self, config, intermediate_size: Optional[int] = None):
+        super().__init__()
+        inter = intermediate_size if intermediate_size is not None else config.intermediate_size
+        self.gate_proj = nn.Linear(config.hidden_size, inter, bias=False)
+        self.down_proj = nn.Linear(inter, config.hidden_size, bias=False)
+        self.up_proj = nn.Linear(config.hidden_size, inter, bias=False)
+        self.dropout = nn.Dropout(getattr(config, "dropout", 0.0))
+        self.act_fn = _act_fn(getattr(config, "hidden_act", "silu"))
+
+    def forward(self, x):
+        return self.dropout(self.down_proj(self.act_fn(self.gate_proj(x)) * self.up_proj(x)))
+
+
+class LazyExpertPlaceholder(nn.Module):
+    """Parameter-free stand-in for an expert that is not resident
+    (``moe_chronos.py:13-29``); raises if executed."""
+
+    def __init__(self, hidden_size: int, intermediate_size: int, dtype: torch.dtype):
+        super().__init__()
+        self.hidden_size = hidden_size
+        self.intermediate_size = intermediate_size
+        self.dtype = dtype
+        self.loaded = False
+
+    def forward(self, _x):
+        raise RuntimeError("lazy expert placeholder executed before materialization")
+
+
+def _is_placeholder(m: nn.Module) -> bool:
+    # any parameter-free module is a placeholder, including the reference's own class
+    if isinstance(m, LazyExpertPlaceholder):
+        return True
+    if type(m).__name__ == "LazyExpertPlaceholder":
+        return True
+    return next(m.parameters(recurse=True), None) is None
+
+
+class _ExpertList(nn.ModuleList):
+    """ModuleList that tells its owner when an expert module is swapped."""
+
+    def __init__(self, modules, owner_ref):
+        super().__init__(modules)
+        object.__setattr__(self, "_owner_ref", owner_ref)
+
+    def __setitem__(self, idx, module):
+        super().__setitem__(idx, module)
+        owner = self._owner_ref()
+        if owner is not None:
+            owner._pool_dirty = True
+
+
+class ChronosMOEFeedForward(nn.Module):
+    def __init__(self, config):
+        super().__init__()
+        import weakref
+
+        self.config = config
+        self.num_experts = config.num_experts
+        self.num_experts_per_tok = config.num_experts_per_tok
+        self.norm_topk_prob = config.norm_topk_prob
+        self.router_aux_loss_coef = config.router_aux_loss_coef
+        _act_fn(getattr(config, "hidden_act", "silu"))
+
+        self.gate = nn.Linear(config.hidden_size, config.num_experts, bias=False)
+        self.experts = _ExpertList([
+            FeedForward(config, intermediate_size=config.moe_intermediate_size)
+            for _ in range(config.num_experts)
+        ], weakref.ref(self))
+        self.shared_experts = nn.ModuleList([
+            FeedForward(config, intermediate_size=config.moe_intermediate_size)
+            for _ in range(getattr(config, "num_shared_experts", 1))
+        ])
+        self.aux_loss = torch.zeros(1)
+        self.aux_loss_raw: Optional[torch.Tensor] = None
+        self.last_router_probs: Optional[torch.Tensor] = None
+        self.last_router_probs_grad: Optional[torch.Tensor] = None
+        self.fallback_mask_prob = float(getattr(config, "fallback_mask_prob", 0.0))
+        self.runtime_miss_policy = "fallback_diagnostic"
+        self.runtime_on_demand_loader = None
+        self.runtime_touch_expert = None
+        self._stats_pending = None
+        self._last_on_demand_experts: List[int] = []
+        self._last_fallback_experts: List[int] = []
+        self._last_on_demand_weight_mass = 0.0
+        self._last_fallback_weight_mass = 0.0
+        # Benchmark knob: fp32 [E] offset added to the router logits (None in models).
+        self.router_logit_bias: Optional[torch.Tensor] = None
+        # Expert residency (set by a pooled ExpertStore): per-expert device ready
+        # flags the GEMMs wait on for selected experts only.
+        self.expert_ready_flags: Optional[torch.Tensor] = None
+        self.expert_ready_epoch: int = 0
+        self.expert_ready_timeout_ns: int = 0
+        self._pool = None
+        self._pool_dirty = True
+        self._live_np = None
+        self._avail_cache = {}
+
+    # ------------------------------------------------------------------
+    # bookkeeping attributes (lazy: resolved from device tensors on read)
+    # ------------------------------------------------------------------
+    def _resolve_stats(self):
+        pend = self._stats_pending
+        if pend is None:
+            return
+        self._stats_pending = None
+        counts = pend["counts"].cpu().numpy()
+        mass = pend["mass"].cpu().numpy().astype(np.float64)
+        od, fb = [], []
+        odm = fbm = 0.0
+        for e in range(self.num_experts):
+            if counts[e] <= 0:
+                continue
+            if pend["a"][e] > 0.0:
+                if pend["on_demand"][e]:
+                    od.append(e)
+                    odm += float(mass[e])
+            else:
+                fb.append(e)
+                fbm += float(mass[e])
+        self._last_on_demand_experts = od
+        self._last_fallback_experts = fb
+        self._last_on_demand_weight_mass = odm
+        self._last_fallback_weight_mass = fbm
+
+    def _stat_prop(name):  # noqa: N805 - property factory
+        def getter(self):
+            self._resolve_stats()
+            return getattr(self, "_" + name)
+
+        def setter(self, v):
+            self._stats_pending = None
+            setattr(self, "_" + name, v)
+
+        return property(getter, setter)
+
+    last_on_demand_experts = _stat_prop("last_on_demand_experts")
+    last_fallback_experts = _stat_prop("last_fallback_experts")
+    last_on_demand_weight_mass = _stat_prop("last_on_demand_weight_mass")
+    last_fallback_weight_mass = _stat_prop("last_fallback_weight_mass")
+    del _stat_prop
+
+    # ------------------------------------------------------------------
+    def _apply(self, fn, *args, **kwargs):
+        self._pool_dirty = True
+        return super()._apply(fn, *args, **kwargs)
+
+    def _shared_expert_output(self, x_flat: torch.Tensor) -> torch.Tensor:
+        """Average output of all shared experts (``moe_chronos.py:90-93``)."""
+        out = sum(e(x_flat) for e in self.shared_experts)
+        return out / len(self.shared_experts)
+
+    def _sync_pool(self, device: torch.device, dtype: torch.dtype) -> None:
+        """Adopt every live expert's weights into the stacked pools (views)."""
+        E = self.num_experts
+        H = self.config.hidden_size
+        Fd = self.config.moe_intermediate_size
+        S = len(self.shared_experts)
+        pool = self._pool
+        if pool is None or pool["gate"].device != device or pool["gate"].dtype != dtype:
+            pool = dict(
+                gate=torch.empty(E, Fd, H, device=device, dtype=dtype),
+                up=torch.empty(E, Fd, H, device=device, dtype=dtype),
+                down=torch.empty(E, H, Fd, device=device, dtype=dtype),
+                sh_gate=torch.empty(S, Fd, H, device=device, dtype=dtype) if S else None,
+                sh_up=torch.empty(S, Fd, H, device=device, dtype=dtype) if S else None,
+                sh_down=torch.empty(S, H, Fd, device=device, dtype=dtype) if S else None,
+            )
+            self._pool = pool
+        live = np.zeros(E, dtype=np.float32)
+
+        def adopt(mod, names_pools, idx):
+            for name, pt in names_pools:
+                lin = getattr(mod, name)
+                wt = lin.weight
+                dst = pt[idx]
+                if wt.data_ptr() != dst.data_ptr() or wt.shape != dst.shape:
+                    if tuple(wt.shape) != tuple(dst.shape):
+                        raise RuntimeError(f"expert weight {name} has shape {tuple(wt.shape)}, "
+                                           f"expected {tuple(dst.shape)}")
+                    with torch.no_grad():
+                        dst.copy_(wt.detach())
+                    lin.weight = nn.Parameter(dst, requires_grad=wt.requires_grad)
+
+        for e, ex in enumerate(self.experts):
+            if _is_placeholder(ex):
+                continue
+            live[e] = 1.0
+            adopt(ex, (("gate_proj", pool["gate"]), ("up_proj", pool["up"]),
+                       ("down_proj", pool["down"])), e)
+        for j, ex in enumerate(self.shared_experts):
+            adopt(ex, (("gate_proj", pool["sh_gate"]), ("up_proj", pool["sh_up"]),
+                       ("down_proj", pool["sh_down"])), j)
+        self._live_np = live
+        self._avail_cache = {}
+        self._pool_dirty = False
+
+    def _avail_tensor(self, a: np.ndarray, device) -> torch.Tensor:
+        key = (a.tobytes(), str(device))
+        t = self._avail_cache.get(key)
+        if t is None:
+            t = torch.from_numpy(a.astype(np.float32)).to(device, non_blocking=False)
+            if len(self._avail_cache) > 64:
+                self._avail_cache = {}
+            self._avail_cache[key] = t
+        return t
+
+    # ------------------------------------------------------------------
+    def forward(self, x: torch.Tensor, available_expert_mask: Optional[torch.Tensor] = None
+                ) -> torch.Tensor:
+        if not x.is_cuda:
+            raise RuntimeError("ChronosMOEFeedForward (sm_100a kernels) needs CUDA tensors; "
+                               f"got x on {x.device}")
+        if self.training and torch.is_grad_enabled():
+            raise NotImplementedError(
+                "ChronosMOEFeedForward runs forward-only kernels; backward is not implemented "
+                "(call it under torch.no_grad() or in eval mode)")
+        B, S, H = x.shape
+        E = self.num_experts
+        k = self.num_experts_per_tok
+        x_flat = x.reshape(-1, H)
+        dev, dt = x.device, x.dtype
+        if self._pool_dirty or self._pool is None or self._pool["gate"].device != dev:
+            self._sync_pool(dev, dt)
+        pool = self._pool
+        live = self._live_np
+        self._stats_pending = None
+        self._last_on_demand_experts = []
+        self._last_fallback_experts = []
+        self._last_on_demand_weight_mass = 0.0
+        self._last_fallback_weight_mass = 0.0
+
+        training_fallback_mask = None
+        if (available_expert_mask is None and self.training and self.fallback_mask_prob > 0.0
+                and len(self.shared_experts) > 0):
+            keep = torch.rand(self.num_experts, device=dev) >= self.fallback_mask_prob
+            if not torch.any(keep):
+                keep[torch.randint(0, self.num_experts, (1,), device=dev)] = True
+            training_fallback_mask = keep
+
+        masked = available_expert_mask is not None or training_fallback_mask is not None
+        mask_t = available_expert_mask if available_expert_mask is not None else training_fallback_mask
+        eval_with_mask = available_expert_mask is not None and not self.training
+        has_placeholder = bool((live == 0).any())
+        touch = getattr(self, "runtime_touch_expert", None)
+        loader = getattr(self, "runtime_on_demand_loader", None)
+        policy = getattr(self, "runtime_miss_policy", "fallback_diagnostic")
+        loader_active = (eval_with_mask and loader is not None
+                         and policy in {"on_demand", "sync_on_demand"} and has_placeholder)
+        touch_active = eval_with_mask and touch is not None
+        standard_with_placeholder = (not masked) and has_placeholder
+
+        mask_np = None
+        if masked and not eval_with_mask:
+            # training with a mask: a_e = live and mask > 0 (moe_chronos.py:221, 227)
+            if mask_t.is_cuda:
+                avail_dev = (mask_t.to(torch.float32) > 0).to(torch.float32) * \
+                    torch.from_numpy(live).to(dev)
+            else:
+                mask_np = mask_t.detach().to(torch.float32).numpy()
+                avail_dev = None
+        if masked and available_expert_mask is not None and not available_expert_mask.is_cuda:
+            mask_np = available_expert_mask.detach().to(torch.float32).numpy()
+
+        bias = self.router_logit_bias
+        probs = None
+        if touch_active or loader_active or standard_with_placeholder:
+            # ---- hook path: route, read back the selected experts once ----
+            r = ops.moe_route(x_flat, self.gate.weight, k, bool(self.norm_topk_prob),
+                              num_shared=len(self.shared_experts),
+                              ffn=self.config.moe_intermediate_size, router_bias=bias)
+            probs = r["probs"]
+            counts = r["counts"].cpu().numpy()
+            mass = r["mass"].cpu().numpy().astype(np.float64)
+            if mask_np is None and mask_t is not None:
+                mask_np = mask_t.detach().to(torch.float32).cpu().numpy()
+            a = np.ones(E, dtype=np.float32)
+            od, fb = [], []
+            odm = fbm = 0.0
+            for i in range(E):
+                if counts[i] <= 0:
+                    continue
+                if not masked:
+                    if live[i] == 0:
+                        raise RuntimeError("lazy expert placeholder executed before materialization")
+                    continue
+                expert_live = not _is_placeholder(self.experts[i])
+                expert_available = float(mask_np[i]) > 0.0
+                stale = eval_with_mask and expert_live
+                if expert_live and (expert_available or stale):
+                    if touch is not None and not self.training:
+                        touch(int(i))
+                    if not expert_available and eval_with_mask:
+                        od.append(i)
+                        odm += float(mass[i])
+                    a[i] = 1.0
+                else:
+                    loaded = False
+                    if eval_with_mask and policy in {"on_demand", "sync_on_demand"} and loader is not None:
+                        res = loader(int(i))
+                        loaded = bool(res.get("ok", False)) if isinstance(res, dict) else bool(res)
+                    if loaded and not _is_placeholder(self.experts[i]):
+                        od.append(i)
+                        odm += float(mass[i])
+                        a[i] = 1.0
+                    else:
+                        fb.append(i)
+                        fbm += float(mass[i])
+                        a[i] = 0.0
+            if self._pool_dirty:
+                # the loader promoted experts: adopt the new modules into the pool
+                self._sync_pool(dev, dt)
+                pool = self._pool
+            out = ops.moe_forward(
+                x_flat, self.gate.weight, pool["gate"], pool["up"], pool["down"],
+                pool["sh_gate"], pool["sh_up"], pool["sh_down"], k, bool(self.norm_topk_prob),
+                avail=self._avail_tensor(a, dev), router_bias=bias,
+                ready_flags=self.expert_ready_flags, ready_epoch=self.expert_ready_epoch,
+                spin_limit_ns=self.expert_ready_timeout_ns, want_probs=False,
+                topk=[r["topk_idx"], r["topk_weight"]])
+            self._last_on_demand_experts = od
+            self._last_fallback_experts = fb
+            self._last_on_demand_weight_mass = odm
+            self._last_fallback_weight_mass = fbm
+        else:
+            # ---- fast path: one call, no host synchronisation ----
+            on_demand = np.zeros(E, dtype=bool)
+            if not masked:
+                a_np = np.ones(E, dtype=np.float32)
+                avail_t = None
+            elif eval_with_mask:
+                a_np = live.copy()  # live experts run even when marked unavailable
+                if mask_np is not None:
+                    on_demand = (mask_np <= 0.0) & (live > 0)
+                avail_t = self._avail_tensor(a_np, dev)
+            else:
+                if mask_np is not None:
+                    a_np = ((mask_np > 0.0) & (live > 0)).astype(np.float32)
+                    avail_t = self._avail_tensor(a_np, dev)
+                else:
+                    a_np = None
+                    avail_t = avail_dev
+            out = ops.moe_forward(
+                x_flat, self.gate.weight, pool["gate"], pool["up"], pool["down"],
+                pool["sh_gate"], pool["sh_up"], pool["sh_down"], k, bool(self.norm_topk_prob),
+                avail=avail_t, router_bias=bias, ready_flags=self.expert_ready_flags,
+                ready_epoch=self.expert_ready_epoch, spin_limit_ns=self.expert_ready_timeout_ns,
+                want_probs=True, want_stats=masked)
+            probs = out["probs"]
+            if masked:
+                if a_np is None:
+                    a_np = avail_t.cpu().numpy()
+                if eval_with_mask and mask_np is None:
+                    # CUDA mask in eval: read lazily together with the counts
+                    self._stats_pending = dict(counts=out["counts"], mass=out["mass"], a=a_np,
+                                               on_demand=_LazyOnDemand(available_expert_mask, live))
+                else:
+                    self._stats_pending = dict(counts=out["counts"], mass=out["mass"], a=a_np,
+                                               on_demand=on_demand)
+
+        y = out["y"]
+        scores_bse = probs.view(B, S, E)
+        self.last_router_probs_grad = scores_bse
+        self.last_router_probs = scores_bse.detach()
+        if self.training:
+            topk_idx = out["topk_idx"].long()
+            load = torch.bincount(topk_idx.reshape(-1), minlength=E).float() / max(1, x_flat.shape[0])
+            aux_raw = (load * probs.float().mean(0)).sum() * E
+            self.aux_loss_raw = aux_raw
+            self.aux_loss = aux_raw * self.router_aux_loss_coef
+        else:
+            self.aux_loss_raw = probs.new_zeros(())
+            self.aux_loss = probs.new_zeros(())
+        return y.view(B, S, H)
+
+
+class _LazyOnDemand:
+    """on_demand[e] = mask[e] <= 0 and live[e], read from a CUDA mask on first use."""
+
+    def __init__(self, mask: torch.Tensor, live: np.ndarray):
+        self.mask = mask
+        self.live = live
+        self._v = None
+
+    def __getitem__(self, e):
+        if self._v is None:
+            m = self.mask.detach().to(torch.float32).cpu().numpy()
+            self._v = (m <= 0.0) & (self.live > 0)
+        return self._v[e]
+

@@ -1,0 +1,210 @@
+"""Torch-facing calls of the sm_100a MoE extension.
+
+``moe_forward`` / ``moe_route`` take CUDA tensors, allocate the outputs and
+the workspace through torch's caching allocator, and call the C ABI on the
+current CUDA stream.  They never fall back to another implementation: a CPU
+tensor, a missing library or a failing call raises.
+
+``moe_forward`` is also registered as the custom op ``chronos::moe_forward``
+(with a fake implementation) so ``torch.compile`` traces the whole layer as
+one node.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, List, Optional
+
+import torch
+
+from . import _native as N
+
+_DTYPES = {torch.bfloat16: N.DTYPE_BF16, torch.float16: N.DTYPE_FP16, torch.float32: N.DTYPE_FP32}
+
+_status_words: Dict[int, torch.Tensor] = {}
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """Persistent per-device int32 word the kernels report device-side failures in."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    w = _status_words.get(idx)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status_words[idx] = w
+    return w
+
+
+def check_status(device: Optional[torch.device] = None, reset: bool = True) -> int:
+    """Synchronise, read the device status word, raise on a recorded failure."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    w = status_word(device)
+    code = int(w.item())
+    if reset and code:
+        w.zero_()
+    if code:
+        raise N.ChronosMoeError(code, "device-side failure recorded by a MoE kernel")
+    return code
+
+
+def _check_cuda(*ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("chronos MoE kernels need CUDA tensors (no CPU path exists); "
+                               f"got a tensor on {t.device}")
+
+
+def _contig(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    return None if t is None else t.contiguous()
+
+
+def _shape(n: int, h: int, e: int, k: int, f: int, s: int, dtype: torch.dtype) -> N.ChronosMoeShape:
+    if dtype not in _DTYPES:
+        raise TypeError(f"unsupported dtype {dtype}")
+    return N.ChronosMoeShape(n, h, e, k, f, s, _DTYPES[dtype])
+
+
+def workspace_bytes(n: int, h: int, e: int, k: int, f: int, s: int, dtype: torch.dtype) -> int:
+    lib = N.load_library()
+    shp = _shape(n, h, e, k, f, s, dtype)
+    size = lib.chronos_moe_workspace_size(ctypes.byref(shp))
+    if size == 0 and n >= 0:
+        N.check(N.CHRONOS_ERR_INVALID_ARG)
+    return int(size)
+
+
+def moe_forward(x: torch.Tensor, router_w: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
+                w_down: torch.Tensor, sh_gate: Optional[torch.Tensor], sh_up: Optional[torch.Tensor],
+                sh_down: Optional[torch.Tensor], top_k: int, norm_topk: bool,
+                avail: Optional[torch.Tensor] = None, router_bias: Optional[torch.Tensor] = None,
+                slot_of_expert: Optional[torch.Tensor] = None,
+                ready_flags: Optional[torch.Tensor] = None, ready_epoch: int = 0,
+                spin_limit_ns: int = 0, want_probs: bool = True, want_stats: bool = False,
+                topk: Optional[List[torch.Tensor]] = None, status: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None):
+    """One MoE layer.  x [N, H]; router_w [E, H]; w_gate/w_up [P, F, H]; w_down [P, H, F];
+    sh_* [S, F, H] / [S, H, F] (or None when S = 0); avail [E] fp32 in [0, 1].
+
+    ``topk`` = [topk_idx int32 [N,k], topk_weight fp32 [N,k]] from an earlier
+    ``moe_route`` call skips routing (the host-hook slow path).
+
+    Returns dict(y, probs, topk_idx, topk_weight, counts, mass); probs/counts/mass
+    are None unless requested.
+    """
+    _check_cuda(x, router_w, w_gate, w_up, w_down, sh_gate, sh_up, sh_down, avail, router_bias,
+                slot_of_expert, ready_flags)
+    x = x.contiguous()
+    n, h = x.shape
+    e = router_w.shape[0]
+    p_slots, f, _ = w_gate.shape
+    s = 0 if sh_gate is None else sh_gate.shape[0]
+    dt = x.dtype
+    for name, t in (("router_w", router_w), ("w_gate", w_gate), ("w_up", w_up), ("w_down", w_down),
+                    ("sh_gate", sh_gate), ("sh_up", sh_up), ("sh_down", sh_down)):
+        if t is not None and t.dtype != dt:
+            raise TypeError(f"{name} dtype {t.dtype} != x dtype {dt}")
+    dev = x.device
+    lib = N.load_library()
+    shp = _shape(n, h, e, top_k, f, s, dt)
+    ws_bytes = int(lib.chronos_moe_workspace_size(ctypes.byref(shp)))
+    if ws_bytes == 0 and n > 0:
+        N.check(N.CHRONOS_ERR_INVALID_ARG)
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    y = out if out is not None else torch.empty(n, h, dtype=dt, device=dev)
+    probs = torch.empty(n, e, dtype=dt, device=dev) if want_probs else None
+    if topk is not None:
+        topk_idx, topk_w = topk
+        flags = N.FLAG_PREROUTED
+    else:
+        topk_idx = torch.empty(n, top_k, dtype=torch.int32, device=dev)
+        topk_w = torch.empty(n, top_k, dtype=torch.float32, device=dev)
+        flags = 0
+    counts = torch.empty(e, dtype=torch.int32, device=dev) if want_stats else None
+    mass = torch.empty(e, dtype=torch.float32, device=dev) if want_stats else None
+    if status is None:
+        status = status_word(dev)
+    w_gate, w_up, w_down = w_gate.contiguous(), w_up.contiguous(), w_down.contiguous()
+    sh_gate, sh_up, sh_down = _contig(sh_gate), _contig(sh_up), _contig(sh_down)
+    router_w = router_w.contiguous()
+    avail = None if avail is None else avail.to(device=dev, dtype=torch.float32).contiguous()
+    rb = None if router_bias is None else router_bias.to(device=dev, dtype=torch.float32).contiguous()
+    args = N.ChronosMoeArgs(
+        shape=shp, norm_topk=int(bool(norm_topk)), flags=flags,
+        x=_ptr(x), router_w=_ptr(router_w), router_bias=_ptr(rb),
+        w_gate=_ptr(w_gate), w_up=_ptr(w_up), w_down=_ptr(w_down), pool_slots=int(p_slots),
+        slot_of_expert=_ptr(slot_of_expert), w_shared_gate=_ptr(sh_gate),
+        w_shared_up=_ptr(sh_up), w_shared_down=_ptr(sh_down), avail=_ptr(avail),
+        ready_flags=_ptr(ready_flags), ready_epoch=int(ready_epoch),
+        spin_limit_ns=int(spin_limit_ns), y=_ptr(y), router_probs=_ptr(probs),
+        topk_idx=_ptr(topk_idx), topk_weight=_ptr(topk_w), expert_counts=_ptr(counts),
+        expert_mass=_ptr(mass), workspace=_ptr(workspace), workspace_bytes=int(workspace.numel()),
+        status=_ptr(status))
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        N.check(lib.chronos_moe_forward(ctypes.byref(args), ctypes.c_void_p(stream)))
+    return dict(y=y, probs=probs, topk_idx=topk_idx, topk_weight=topk_w, counts=counts, mass=mass)
+
+
+def moe_route(x: torch.Tensor, router_w: torch.Tensor, top_k: int, norm_topk: bool,
+              num_shared: int = 0, ffn: int = 64, router_bias: Optional[torch.Tensor] = None,
+              want_probs: bool = True, workspace: Optional[torch.Tensor] = None):
+    """Routing only: dict(probs, topk_idx, topk_weight, counts, mass) on the device."""
+    _check_cuda(x, router_w, router_bias)
+    x = x.contiguous()
+    n, h = x.shape
+    e = router_w.shape[0]
+    dt = x.dtype
+    if router_w.dtype != dt:
+        raise TypeError(f"router_w dtype {router_w.dtype} != x dtype {dt}")
+    dev = x.device
+    lib = N.load_library()
+    shp = _shape(n, h, e, top_k, ffn, num_shared, dt)
+    ws_bytes = int(lib.chronos_moe_workspace_size(ctypes.byref(shp)))
+    if ws_bytes == 0 and n > 0:
+        N.check(N.CHRONOS_ERR_INVALID_ARG)
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    probs = torch.empty(n, e, dtype=dt, device=dev) if want_probs else None
+    topk_idx = torch.empty(n, top_k, dtype=torch.int32, device=dev)
+    topk_w = torch.empty(n, top_k, dtype=torch.float32, device=dev)
+    counts = torch.empty(e, dtype=torch.int32, device=dev)
+    mass = torch.empty(e, dtype=torch.float32, device=dev)
+    router_w = router_w.contiguous()
+    rb = None if router_bias is None else router_bias.to(device=dev, dtype=torch.float32).contiguous()
+    args = N.ChronosMoeArgs(
+        shape=shp, norm_topk=int(bool(norm_topk)), flags=0, x=_ptr(x), router_w=_ptr(router_w),
+        router_bias=_ptr(rb), router_probs=_ptr(probs), topk_idx=_ptr(topk_idx),
+        topk_weight=_ptr(topk_w), expert_counts=_ptr(counts), expert_mass=_ptr(mass),
+        workspace=_ptr(workspace), workspace_bytes=int(workspace.numel()),
+        status=_ptr(status_word(dev)))
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        N.check(lib.chronos_moe_route(ctypes.byref(args), ctypes.c_void_p(stream)))
+    return dict(probs=probs, topk_idx=topk_idx, topk_weight=topk_w, counts=counts, mass=mass)
+
+
+# ---------------------------------------------------------------------------
+# torch.library registration (one graph node for torch.compile)
+# ---------------------------------------------------------------------------
+
+@torch.library.custom_op("chronos::moe_forward", mutates_args=())
+def moe_forward_op(x: torch.Tensor, router_w: torch.Tensor, w_gate: torch.Tensor,
+                   w_up: torch.Tensor, w_down: torch.Tensor, sh_gate: Optional[torch.Tensor],
+                   sh_up: Optional[torch.Tensor], sh_down: Optional[torch.Tensor],
+                   avail: Optional[torch.Tensor], top_k: int,
+                   norm_topk: bool) -> List[torch.Tensor]:
+    r = moe_forward(x, router_w, w_gate, w_up, w_down, sh_gate, sh_up, sh_down, top_k, norm_topk,
+                    avail=avail, want_probs=True)
+    return [r["y"], r["probs"], r["topk_idx"], r["topk_weight"]]
+
+
+@moe_forward_op.register_fake
+def _moe_forward_fake(x, router_w, w_gate, w_up, w_down, sh_gate, sh_up, sh_down, avail, top_k,
+                      norm_topk):
+    n, h = x.shape
+    e = router_w.shape[0]
+    return [x.new_empty(n, h), x.new_empty(n, e),
+            x.new_empty(n, top_k, dtype=torch.int32), x.new_empty(n, top_k, dtype=torch.float32)]

@@ -1,0 +1,182 @@
+"""The drop-in ChronosMOEFeedForward on the GPU vs the reference's golden outputs.
+
+Mirrors the reference's own MoE tests (tests/test_smoke.py of
+FonaTech/Project_Chronos): placeholder fallback (:147-167), all-available ==
+no-mask (:1099-1115), lazy on-demand == full (:429-488), plus the bookkeeping
+lists the reference fills (moe_chronos.py:114-117, 231-256).
+"""
+import types
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as O
+from tests import _golden as G
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _cfg(c, dropout=0.0):
+    return types.SimpleNamespace(hidden_size=c["H"], num_experts=c["E"], num_experts_per_tok=c["k"],
+                                 moe_intermediate_size=c["F"], num_shared_experts=c["S"],
+                                 norm_topk_prob=c["norm"], router_aux_loss_coef=5e-4,
+                                 hidden_act="silu", dropout=dropout, fallback_mask_prob=0.0,
+                                 intermediate_size=c["F"])
+
+
+def _module(c, wl):
+    from project_chronos_b200 import ChronosMOEFeedForward
+    m = ChronosMOEFeedForward(_cfg(c))
+    w = wl.weights
+    sd = {"gate.weight": w.router}
+    for e in range(c["E"]):
+        sd[f"experts.{e}.gate_proj.weight"] = w.gate[e]
+        sd[f"experts.{e}.up_proj.weight"] = w.up[e]
+        sd[f"experts.{e}.down_proj.weight"] = w.down[e]
+    for j in range(c["S"]):
+        sd[f"shared_experts.{j}.gate_proj.weight"] = w.sh_gate[j]
+        sd[f"shared_experts.{j}.up_proj.weight"] = w.sh_up[j]
+        sd[f"shared_experts.{j}.down_proj.weight"] = w.sh_down[j]
+    m.load_state_dict(sd, strict=True)
+    return m.to(device=DEV, dtype=wl.x.dtype)
+
+
+def _placeholders(m, c, mask):
+    from project_chronos_b200 import LazyExpertPlaceholder
+    for e in range(c["E"]):
+        if not mask[e]:
+            m.experts[e] = LazyExpertPlaceholder(c["H"], c["F"], torch.float32)
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in G.cases()])
+def test_module_matches_reference_golden(name):
+    c = G.case(name)
+    d = G.load(c)
+    wl = G.inputs(c)
+    m = _module(c, wl)
+    x = wl.x.to(DEV).view(c["B"], c["T"], c["H"])
+    mask = None
+    if c["mode"] == "eval":
+        m.eval()
+        _placeholders(m, c, c["mask"])
+        mask = torch.tensor(c["mask"])
+    elif c["mode"] == "eval_stale":
+        m.eval()
+        mask = torch.tensor(c["mask"])
+    elif c["mode"] == "train_mask":
+        m.train()
+        mask = torch.tensor(c["float_mask"], dtype=torch.float32)
+    else:
+        m.eval()
+    with torch.no_grad():
+        y = m(x, available_expert_mask=mask)
+    torch.cuda.synchronize()
+    assert y.shape == x.shape and y.dtype == x.dtype
+    ref = G.reference_y(c, d)
+    tol = 1e-5 if c["dtype"] == "fp32" else 1e-2
+    assert O.rel_l2(y.float().cpu().numpy().reshape(-1, c["H"]), ref) <= tol
+    probs = m.last_router_probs.float().cpu().numpy().reshape(-1, c["E"])
+    np.testing.assert_allclose(probs, d["probs_ref"], rtol=2e-2 if c["dtype"] != "fp32" else 1e-5,
+                               atol=2e-3 if c["dtype"] != "fp32" else 1e-6)
+    assert m.last_fallback_experts == c["fallback"]
+    assert m.last_on_demand_experts == c["on_demand"]
+    assert abs(m.last_fallback_weight_mass - c["fallback_mass"]) < 1e-4
+    assert abs(m.last_on_demand_weight_mass - c["on_demand_mass"]) < 1e-4
+    assert float(m.aux_loss) == 0.0 or c["mode"] == "train_mask"
+
+
+def test_all_available_matches_no_mask():
+    c = G.case("tiny_nomask")
+    wl = G.inputs(c)
+    m = _module(c, wl).eval()
+    x = wl.x.to(DEV).view(1, -1, c["H"])
+    with torch.no_grad():
+        a = m(x)
+        b = m(x, available_expert_mask=torch.ones(c["E"], dtype=torch.bool))
+    torch.cuda.synchronize()
+    assert (a.float() - b.float()).abs().max().item() < 1e-6
+
+
+def test_hooks_touch_and_sync_on_demand_loader():
+    """Runtime hooks are called for selected experts, in ascending order; a loader
+    that materialises a placeholder makes the output equal the all-live output."""
+    c = G.case("tiny_sh2_norm")
+    wl = G.inputs(c)
+    full = _module(c, wl).eval()
+    x = wl.x.to(DEV).view(c["B"], c["T"], c["H"])
+    with torch.no_grad():
+        y_full = full(x)
+    lazy = _module(c, wl).eval()
+    saved = {e: lazy.experts[e] for e in range(c["E"])}
+    mask = torch.tensor(c["mask"])
+    _placeholders(lazy, c, c["mask"])
+    touched, loaded = [], []
+
+    def loader(e):
+        loaded.append(e)
+        lazy.experts[e] = saved[e]
+        return {"ok": True}
+
+    lazy.runtime_touch_expert = touched.append
+    lazy.runtime_on_demand_loader = loader
+    lazy.runtime_miss_policy = "sync_on_demand"
+    with torch.no_grad():
+        y_lazy = lazy(x, available_expert_mask=mask)
+    torch.cuda.synchronize()
+    assert loaded == sorted(loaded) and set(loaded) == set(c["fallback"])
+    assert touched == sorted(touched)
+    assert lazy.last_fallback_experts == []
+    assert lazy.last_on_demand_experts == c["fallback"]
+    assert O.rel_l2(y_lazy.float().cpu().numpy(), y_full.float().cpu().numpy()) < 1e-5
+
+
+def test_placeholder_in_standard_path_raises_only_when_selected():
+    c = G.case("tiny_k1_placeholder")
+    wl = G.inputs(c)
+    m = _module(c, wl).eval()
+    _placeholders(m, c, c["mask"])
+    x = wl.x.to(DEV).view(1, -1, c["H"])
+    d = G.load(c)
+    selected = set(np.unique(d["idx_ref"]).tolist())
+    with torch.no_grad():
+        if 0 in selected:
+            with pytest.raises(RuntimeError, match="placeholder"):
+                m(x)
+        else:
+            m(x)
+
+
+def test_cpu_input_raises():
+    c = G.case("tiny_nomask")
+    wl = G.inputs(c)
+    from project_chronos_b200 import ChronosMOEFeedForward
+    m = ChronosMOEFeedForward(_cfg(c)).eval()
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m(wl.x.view(1, -1, c["H"]))
+
+
+def test_state_dict_keys_and_reload_into_pool():
+    c = G.case("bf16_small")
+    wl = G.inputs(c)
+    m = _module(c, wl).eval()
+    keys = set(m.state_dict().keys())
+    assert "experts.0.gate_proj.weight" in keys and "shared_experts.0.down_proj.weight" in keys
+    assert not any("pool" in k for k in keys)
+    x = wl.x.to(DEV).view(c["B"], c["T"], c["H"])
+    with torch.no_grad():
+        y1 = m(x)
+        # reload the same weights after the pool exists: writes go into the pool views
+        m.load_state_dict({k: v.clone() for k, v in m.state_dict().items()})
+        y2 = m(x)
+        # perturb one expert via load_state_dict; the output must change
+        sd = m.state_dict()
+        sd["experts.1.down_proj.weight"] = sd["experts.1.down_proj.weight"] * 2
+        m.load_state_dict(sd)
+        y3 = m(x)
+    torch.cuda.synchronize()
+    assert O.rel_l2(y2.float().cpu().numpy(), y1.float().cpu().numpy()) < 1e-5
+    d = G.load(c)
+    if (d["idx_ref"] == 1).any():
+        assert O.rel_l2(y3.float().cpu().numpy(), y1.float().cpu().numpy()) > 1e-4

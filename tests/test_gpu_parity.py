@@ -1,0 +1,208 @@
+"""CUDA path vs the oracle and the reference's golden vectors (GPU; calls the C ABI).
+
+Tolerances (written here, from the parity contract of the layer):
+  * top-k indices: bit-exact against the oracle's routing (fp32 fmaf chain,
+    ties -> lower index) and, as sets, against the reference's golden indices;
+  * outputs: rel-L2 <= 1e-5 for fp32 layers, <= 1e-2 for bf16 layers, against
+    the reference run in fp32 on the same (bf16-valued) inputs; bf16 results
+    are also held to 3e-3 against the oracle's bf16-emulating mode, which
+    rounds where the kernels round.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as O
+from tests import _golden as G
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _ops():
+    from project_chronos_b200 import ops
+    return ops
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _run(wl, k, norm, avail=None, bias=None, **kw):
+    ops = _ops()
+    w = wl.weights
+    return ops.moe_forward(wl.x, w.router, w.gate, w.up, w.down,
+                           w.sh_gate if w.sh_gate.shape[0] else None,
+                           w.sh_up if w.sh_up.shape[0] else None,
+                           w.sh_down if w.sh_down.shape[0] else None, k, norm,
+                           avail=avail, router_bias=bias, **kw)
+
+
+def _oracle(wl, k, norm, avail=None, bias=None, rows=None, emulate=False):
+    w = wl.weights
+    x = _np(wl.x)
+    if rows is not None:
+        x = x[rows]
+    dt = "bf16" if wl.x.dtype == torch.bfloat16 else ("fp16" if wl.x.dtype == torch.float16 else "fp32")
+    return O.moe_forward(x, _np(w.router), _np(w.gate), _np(w.up), _np(w.down), _np(w.sh_gate),
+                         _np(w.sh_up), _np(w.sh_down), k, norm,
+                         avail=None if avail is None else _np(avail),
+                         bias=None if bias is None else _np(bias), dtype=dt,
+                         emulate_device=emulate)
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in G.cases()])
+def test_golden_case(name):
+    c = G.case(name)
+    d = G.load(c)
+    wl = G.inputs(c, device=DEV)
+    a = G.effective_avail(c)
+    avail = None if a is None else torch.tensor(a, device=DEV)
+    out = _run(wl, c["k"], c["norm"], avail=avail)
+    torch.cuda.synchronize()
+    _ops().check_status()
+    idx = out["topk_idx"].cpu().numpy()
+    # reference's expert set per token (bit-exact routing)
+    assert np.array_equal(np.sort(idx, axis=1), d["idx_ref"])
+    # oracle's rank order
+    o_idx, o_w, o_probs, _ = O.route(_np(wl.x), _np(wl.weights.router), c["k"], c["norm"])
+    assert np.array_equal(idx, o_idx)
+    np.testing.assert_allclose(out["topk_weight"].cpu().numpy(), o_w, rtol=1e-5, atol=1e-6)
+    y = _np(out["y"])
+    ref = G.reference_y(c, d)
+    tol = 1e-5 if c["dtype"] == "fp32" else 1e-2
+    assert O.rel_l2(y, ref) <= tol, O.rel_l2(y, ref)
+    if c["dtype"] != "fp32":
+        emu, *_ = _oracle(wl, c["k"], c["norm"], avail=avail, emulate=True)
+        assert O.rel_l2(y, emu) <= 3e-3
+
+
+def _workload(h, e, k, f, s, n, dtype=torch.bfloat16, seed=0, avail_p=None, zipf=None):
+    from project_chronos_b200 import synthetic as syn
+    shape = syn.MoEShape(h, e, k, f, s)
+    return syn.make_workload(shape, n, seed=seed, dtype=dtype, device=DEV, avail_p=avail_p,
+                             zipf_s=zipf)
+
+
+@pytest.mark.parametrize("n", [1, 2, 7, 16, 33, 64, 65, 200])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tensor_core_path_token_counts(n, dtype):
+    # covers every token-tile width (16/32/64/128), split-K decode and ragged tails
+    wl = _workload(256, 16, 4, 192, 2, n, dtype=dtype, seed=n, avail_p=0.7)
+    avail = wl.mask.to(torch.float32)
+    out = _run(wl, 4, True, avail=avail)
+    torch.cuda.synchronize()
+    _ops().check_status()
+    y = _np(out["y"])
+    ref, o_idx, _, _ = _oracle(wl, 4, True, avail=avail)
+    assert np.array_equal(out["topk_idx"].cpu().numpy(), o_idx)
+    assert O.rel_l2(y, ref) <= 1e-2
+    emu, *_ = _oracle(wl, 4, True, avail=avail, emulate=True)
+    assert O.rel_l2(y, emu) <= 3e-3
+
+
+@pytest.mark.parametrize("h,e,k,f,s", [(32, 4, 2, 48, 1), (96, 6, 3, 80, 0), (64, 9, 1, 64, 2),
+                                       (128, 256, 8, 64, 1)])
+def test_simt_and_odd_shapes(h, e, k, f, s):
+    for dtype in (torch.float32, torch.bfloat16):
+        wl = _workload(h, e, k, f, s, 37, dtype=dtype, seed=h + e, avail_p=0.6)
+        avail = wl.mask.to(torch.float32)
+        out = _run(wl, k, False, avail=avail)
+        torch.cuda.synchronize()
+        y = _np(out["y"])
+        ref, o_idx, _, _ = _oracle(wl, k, False, avail=avail)
+        assert np.array_equal(out["topk_idx"].cpu().numpy(), o_idx)
+        tol = 1e-5 if dtype == torch.float32 else 1e-2
+        assert O.rel_l2(y, ref) <= tol
+
+
+def test_empty_input():
+    wl = _workload(128, 8, 2, 128, 1, 0)
+    out = _run(wl, 2, True)
+    torch.cuda.synchronize()
+    assert out["y"].shape == (0, 128)
+
+
+def test_all_unavailable_is_shared_only():
+    wl = _workload(128, 8, 2, 128, 2, 40, seed=3)
+    avail = torch.zeros(8, device=DEV)
+    out = _run(wl, 2, False, avail=avail)
+    torch.cuda.synchronize()
+    ref, *_ = _oracle(wl, 2, False, avail=avail)
+    assert O.rel_l2(_np(out["y"]), ref) <= 1e-2
+
+
+def test_fractional_availability_blend():
+    # a_e in (0,1): y = sum w (a E + (1-a) S) + S  (chronos/mlx/moe.py:162)
+    wl = _workload(128, 8, 2, 128, 1, 24, seed=5)
+    avail = torch.linspace(0.0, 1.0, 8, device=DEV)
+    out = _run(wl, 2, True, avail=avail)
+    torch.cuda.synchronize()
+    ref, *_ = _oracle(wl, 2, True, avail=avail)
+    assert O.rel_l2(_np(out["y"]), ref) <= 1e-2
+
+
+def test_routing_is_deterministic_and_prerouted_matches():
+    wl = _workload(256, 64, 6, 128, 2, 300, seed=11)
+    a = _run(wl, 6, True)
+    b = _run(wl, 6, True)
+    torch.cuda.synchronize()
+    assert torch.equal(a["topk_idx"], b["topk_idx"])
+    assert torch.equal(a["topk_weight"], b["topk_weight"])
+    c = _run(wl, 6, True, topk=[a["topk_idx"], a["topk_weight"]])
+    torch.cuda.synchronize()
+    assert O.rel_l2(_np(c["y"]), _np(a["y"])) < 1e-5
+
+
+def test_ready_flags_gate_selected_experts():
+    ops = _ops()
+    wl = _workload(128, 8, 2, 128, 1, 16, seed=2)
+    flags = torch.ones(8, dtype=torch.int32, device=DEV)
+    ok = _run(wl, 2, True, ready_flags=flags, ready_epoch=1)
+    torch.cuda.synchronize()
+    ops.check_status()
+    ref, *_ = _oracle(wl, 2, True)
+    assert O.rel_l2(_np(ok["y"]), ref) <= 1e-2
+    # a flag nothing sets: the bounded wait runs out and the status word says so
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    flags[int(ok["topk_idx"][0, 0])] = 0
+    _run(wl, 2, True, ready_flags=flags, ready_epoch=1, spin_limit_ns=2_000_000, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 4  # CHRONOS_ERR_EXPERT_NOT_READY
+    # the context is still usable
+    again = _run(wl, 2, True)
+    torch.cuda.synchronize()
+    assert O.rel_l2(_np(again["y"]), ref) <= 1e-2
+
+
+def test_prefill_full_size_routing_bit_exact_and_sampled_output():
+    from project_chronos_b200 import synthetic as syn
+    wl = syn.named_workload("prefill", device=DEV)
+    sh = wl.shape
+    out = _run(wl, sh.top_k, sh.norm_topk, bias=wl.bias, want_stats=True)
+    torch.cuda.synchronize()
+    _ops().check_status()
+    idx = out["topk_idx"].cpu().numpy()
+    o_idx, o_w, _, _ = O.route(_np(wl.x), _np(wl.weights.router), sh.top_k, sh.norm_topk,
+                               bias=_np(wl.bias))
+    assert np.array_equal(idx, o_idx)
+    counts = out["counts"].cpu().numpy()
+    assert counts.sum() == wl.x.shape[0] * sh.top_k
+    assert np.array_equal(counts, np.bincount(o_idx.ravel(), minlength=sh.num_experts))
+    rows = np.random.default_rng(0).choice(wl.x.shape[0], 48, replace=False)
+    ref, *_ = _oracle(wl, sh.top_k, sh.norm_topk, bias=wl.bias, rows=rows)
+    assert O.rel_l2(_np(out["y"])[rows], ref) <= 1e-2
+
+
+def test_custom_op_registration():
+    ops = _ops()
+    wl = _workload(128, 8, 2, 128, 1, 10, seed=9)
+    w = wl.weights
+    y, probs, idx, wt = torch.ops.chronos.moe_forward(wl.x, w.router, w.gate, w.up, w.down,
+                                                      w.sh_gate, w.sh_up, w.sh_down, None, 2, True)
+    torch.cuda.synchronize()
+    ref = ops.moe_forward(wl.x, w.router, w.gate, w.up, w.down, w.sh_gate, w.sh_up, w.sh_down, 2,
+                          True)
+    assert torch.equal(idx, ref["topk_idx"])
+    assert O.rel_l2(_np(y), _np(ref["y"])) < 1e-5

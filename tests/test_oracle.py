@@ -7,8 +7,7 @@ import pytest
 
 from tests import _golden as G
 
-sys.path.insert(0, os.path.join(G.GOLDEN, "..", "..", "oracle"))
-import oracle as O  # noqa: E402
+from oracle import moe_oracle as O  # noqa: E402
 
 
 def _np(t):
