@@ -1,0 +1,585 @@
+#!/usr/bin/env python
+"""Benchmark of the sm_100a Chronos MoE feed-forward layer.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload decode|prefill]
+
+Prints ONE JSON line (rank 0).  Workloads (synthetic data, seeded; weights
+N(0, 0.02), hidden states N(0, 1)):
+
+* ``decode`` (default): the DeepSeek-MoE-16B-shaped layer (d_model 2048, 64
+  routed experts top-6 + 2 shared, d_ff 1408, bf16) with availability mask
+  Bernoulli(0.9) (unavailable experts are placeholders served by the shared
+  fallback).  One step = one layer call at each decode batch 1, 8, 32 and 64
+  tokens (105 tokens).  ``value`` = tokens/s of the layer with inputs resident
+  in HBM (each call a CUDA-graph replay, L2 flushed before every call).
+* ``prefill``: the same layer on 8192 tokens, router logits offset by a
+  Zipf(s=1.1) per-expert bias, all experts available.  One step = one call.
+
+Both workloads are measured in every run; ``--workload`` picks the one the
+headline ``value`` reports, the other appears as a sub-object.  ``e2e``
+drives the public module (``ChronosMOEFeedForward``) with pinned host inputs:
+H2D copy, layer, D2H copy inside the timed region.  ``roofline`` is the
+dominant kernel of the headline workload, timed per launch with CUDA events
+around that kernel (stage events inside the extension).  ``cpu_baseline``
+(rank 0, N=1) is the CPU oracle port of the layer on a bounded sample.
+
+``--impl reference`` times the CPU implementation of the path (the oracle
+port: router restated in C, experts in numpy/BLAS with every host thread) on
+the same workload and prints the same metric with "impl": "reference".
+
+Multi-GPU (torchrun, one process per GPU): every rank runs an independent
+replica of the workload (the layer does not shard without expert
+parallelism); ``value`` = tokens of all ranks / max-over-ranks device time.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+DECODE_BATCHES = (1, 8, 32, 64)
+PREFILL_TOKENS = 8192
+FLUSH_BYTES = 256 << 20  # > 126 MB L2
+METRIC_DECODE = "MoE-layer tokens/s (decode, batches 1/8/32/64)"
+METRIC_PREFILL = "MoE-layer tokens/s (prefill, 8192 tokens)"
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+def measured_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return dict(hbm_gbs=float(d["hbm_gbs"]), bf16_tflops=float(d["bf16_tflops"]),
+                    bf16_tflops_sustained=float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                    source="measured")
+    return dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0,
+                source="fallback")
+
+
+def committed_traffic():
+    p = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,"
+              "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 10:
+                    continue
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+
+        busy = [r for r in rows if (num(r[4]) or 0.0) >= 50.0] or rows
+        sm = [num(r[1]) for r in busy if num(r[1]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in busy for i in range(4) if r[6 + i] == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": num(rows[0][2]), "reasons": reasons, "samples": len(rows),
+                "busy_samples": len(busy)}
+
+
+class Dist:
+    def __init__(self):
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = False
+
+    def init(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local_rank)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local_rank))
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+def decode_config(shape):
+    return dict(hidden_size=shape.hidden, num_experts=shape.num_experts,
+                num_experts_per_tok=shape.top_k, moe_intermediate_size=shape.ffn,
+                num_shared_experts=shape.num_shared, norm_topk_prob=shape.norm_topk,
+                router_aux_loss_coef=5e-4, hidden_act="silu", dropout=0.0,
+                fallback_mask_prob=0.0, intermediate_size=shape.ffn)
+
+
+def algorithmic_bytes(stage: str, shape, n_tokens: int, experts_applied: int, slots: int,
+                      elem: int = 2) -> float:
+    """HBM bytes one launch of a stage must move at minimum:
+    gate/up: gate+up weights of every expert applied (routed + shared), the
+    token rows read and the hidden rows written; down: down weights of every
+    expert applied, hidden rows read, fp32 output accumulator written."""
+    H, F = shape.hidden, shape.ffn
+    if stage == "gateup":
+        return experts_applied * 2 * F * H * elem + slots * H * elem + slots * F * elem
+    if stage == "down":
+        return experts_applied * F * H * elem + slots * F * elem + n_tokens * H * 4
+    raise ValueError(stage)
+
+
+# ---------------------------------------------------------------------------
+# our implementation
+# ---------------------------------------------------------------------------
+
+def run_ours(args, dist: Dist):
+    from project_chronos_b200 import LazyExpertPlaceholder, ops, synthetic as syn
+    from project_chronos_b200.moe import ChronosMOEFeedForward
+    import types
+
+    dev = torch.device("cuda", dist.local_rank)
+    torch.cuda.set_device(dev)
+    peaks = measured_peaks()
+    sampler = ClockSampler(dist.local_rank)
+    sampler.start()
+
+    spec = syn.WORKLOADS["decode"]
+    shape = spec["shape"]
+    wl = syn.make_workload(shape, max(DECODE_BATCHES), seed=1234 + dist.rank,
+                           dtype=torch.bfloat16, device=dev, avail_p=spec["avail_p"])
+    w = wl.weights
+    mask_host = wl.mask.cpu()
+    cfg = types.SimpleNamespace(**decode_config(shape))
+    module = ChronosMOEFeedForward.from_stacked(cfg, w.router, w.gate, w.up, w.down, w.sh_gate,
+                                                w.sh_up, w.sh_down).eval()
+    for e in range(shape.num_experts):
+        if not bool(mask_host[e]):
+            module.experts[e] = LazyExpertPlaceholder(shape.hidden, shape.ffn, torch.bfloat16)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    xs = {b: wl.x[:b].contiguous().view(1, b, shape.hidden) for b in DECODE_BATCHES}
+
+    # ---------------- decode: warm-up, graphs, timed region ----------------
+    with torch.no_grad():
+        for _ in range(max(1, args.warmup)):
+            for b in DECODE_BATCHES:
+                module(xs[b], mask_host)
+        torch.cuda.synchronize()
+        graphs, gouts, launches_per_graph = {}, {}, {}
+        for b in DECODE_BATCHES:
+            g = torch.cuda.CUDAGraph()
+            before = ops.kernel_launches()
+            with torch.cuda.graph(g):
+                gouts[b] = module(xs[b], mask_host)
+            launches_per_graph[b] = ops.kernel_launches() - before
+            graphs[b] = g
+        for _ in range(2):
+            for b in DECODE_BATCHES:
+                graphs[b].replay()
+        torch.cuda.synchronize()
+        # graph output equals the eager output
+        for b in DECODE_BATCHES:
+            ref = module(xs[b], mask_host)
+            graphs[b].replay()
+            torch.cuda.synchronize()
+            if not torch.allclose(ref.float(), gouts[b].float(), rtol=1e-2, atol=1e-2):
+                raise RuntimeError("graph replay disagrees with the eager layer call")
+
+        K = args.steps
+        ev = {b: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(K)] for b in DECODE_BATCHES}
+        dist.barrier()
+        torch.cuda.synchronize()
+        for i in range(K):
+            for b in DECODE_BATCHES:
+                flush.zero_()
+                ev[b][i][0].record()
+                graphs[b].replay()
+                ev[b][i][1].record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        dec_ms = {b: sum(s.elapsed_time(e) for s, e in ev[b]) for b in DECODE_BATCHES}
+        dec_total_ms = dist.max(sum(dec_ms.values()))
+        dec_launches = K * sum(launches_per_graph.values())
+
+        # per-stage kernel times (queue backed up behind a sleep so events
+        # bracket kernels, not host launch gaps)
+        ops.profile_begin(K * len(DECODE_BATCHES))
+        dec_apps = {}
+        for i in range(K):
+            for b in DECODE_BATCHES:
+                flush.zero_()
+                torch.cuda._sleep(1_000_000)
+                module(xs[b], mask_host)
+        prof_dec = ops.profile_end()
+        for b in DECODE_BATCHES:
+            r = ops.moe_route(xs[b].view(b, -1), w.router, shape.top_k, shape.norm_topk)
+            sel = set(r["topk_idx"].cpu().numpy().ravel().tolist())
+            avail_sel = [e for e in sel if bool(mask_host[e])]
+            slots_routed = int(sum(int((r["topk_idx"] == e).sum()) for e in avail_sel))
+            dec_apps[b] = dict(experts=len(avail_sel) + shape.num_shared,
+                               slots=slots_routed + b * shape.num_shared)
+        ops.check_status(dev)
+
+        # ---------------- prefill ----------------
+        pwl_g = syn.make_generator(99 + dist.rank, dev)
+        xp = syn.make_hidden(PREFILL_TOKENS, shape.hidden, pwl_g, dtype=torch.bfloat16, device=dev)
+        bias = syn.make_zipf_bias(shape.num_experts, 1.1, pwl_g, dev)
+
+        def prefill_call():
+            return ops.moe_forward(xp, w.router, w.gate, w.up, w.down, w.sh_gate, w.sh_up,
+                                   w.sh_down, shape.top_k, shape.norm_topk, router_bias=bias,
+                                   want_probs=True)
+
+        for _ in range(max(1, args.warmup)):
+            prefill_call()
+        torch.cuda.synchronize()
+        KP = max(3, min(args.steps, 20))
+        pev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(KP)]
+        launches0 = ops.kernel_launches()
+        dist.barrier()
+        torch.cuda.synchronize()
+        for i in range(KP):
+            flush.zero_()
+            pev[i][0].record()
+            prefill_call()
+            pev[i][1].record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        pre_launches = ops.kernel_launches() - launches0
+        pre_ms = dist.max(sum(s.elapsed_time(e) for s, e in pev)) / KP
+        ops.profile_begin(KP)
+        for i in range(KP):
+            flush.zero_()
+            torch.cuda._sleep(1_000_000)
+            out = prefill_call()
+        prof_pre = ops.profile_end()
+        ops.check_status(dev)
+        pre_slots_routed = PREFILL_TOKENS * shape.top_k
+        pre_flops = syn.layer_flops(shape, PREFILL_TOKENS)
+        counts = torch.bincount(out["topk_idx"].reshape(-1).long(), minlength=shape.num_experts)
+        imbalance = float(counts.max()) / float(counts.float().mean())
+
+        # ---------------- e2e through the public module ----------------
+        x_host = {b: xs[b].cpu().pin_memory() for b in DECODE_BATCHES}
+        y_host = {b: torch.empty_like(x_host[b]).pin_memory() for b in DECODE_BATCHES}
+        x_dev = {b: torch.empty_like(xs[b]) for b in DECODE_BATCHES}
+        for _ in range(max(1, args.warmup)):
+            for b in DECODE_BATCHES:
+                x_dev[b].copy_(x_host[b], non_blocking=True)
+                y = module(x_dev[b], mask_host)
+                y_host[b].copy_(y, non_blocking=True)
+        torch.cuda.synchronize()
+        eev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(K)]
+        dist.barrier()
+        torch.cuda.synchronize()
+        for i in range(K):
+            flush.zero_()
+            eev[i][0].record()
+            for b in DECODE_BATCHES:
+                x_dev[b].copy_(x_host[b], non_blocking=True)
+                y = module(x_dev[b], mask_host)
+                y_host[b].copy_(y, non_blocking=True)
+            eev[i][1].record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e2e_ms = dist.max(sum(s.elapsed_time(e) for s, e in eev)) / K
+        h2d = sum(x_host[b].numel() * x_host[b].element_size() for b in DECODE_BATCHES)
+        d2h = sum(y_host[b].numel() * y_host[b].element_size() for b in DECODE_BATCHES)
+
+    clocks = sampler.stop()
+
+    # ---------------- assemble ----------------
+    tokens_step = sum(DECODE_BATCHES)
+    dec_ms_step = dec_total_ms / K
+    dec_value = tokens_step * dist.world / (dec_ms_step / 1e3)
+    per_batch = {}
+    for b in DECODE_BATCHES:
+        t_ms = dec_ms[b] / K
+        lb = syn.decode_bytes(shape, b, dec_apps[b]["experts"] - shape.num_shared)
+        per_batch[str(b)] = dict(us_per_call=round(t_ms * 1e3, 2),
+                                 us_per_token=round(t_ms * 1e3 / b, 3),
+                                 layer_bytes=int(lb),
+                                 layer_gbs=round(lb / (t_ms / 1e3) / 1e9, 1),
+                                 layer_hbm_frac=round(lb / (t_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+                                 experts_read=dec_apps[b]["experts"])
+    # dominant decode kernel and its roofline
+    stage_ms = {s: prof_dec[s][0] for s in ("gateup", "down")}
+    dom = max(stage_ms, key=stage_ms.get)
+    dom_bytes = sum(algorithmic_bytes(dom, shape, b, dec_apps[b]["experts"], dec_apps[b]["slots"])
+                    for b in DECODE_BATCHES) * K
+    dom_launches = prof_dec[dom][1]
+    dom_avg_ms = prof_dec[dom][0] / max(1, dom_launches)
+    dec_achieved = dom_bytes / (prof_dec[dom][0] / 1e3) / 1e9
+    traffic = committed_traffic()
+    dec_roof = dict(kernel=f"tc_grouped_gemm ({dom}) decode", bound="hbm",
+                    achieved=round(dec_achieved, 1), peak=peaks["hbm_gbs"], unit="GB/s",
+                    frac=round(dec_achieved / peaks["hbm_gbs"], 4),
+                    traffic=traffic.get(f"decode_{dom}_bytes_per_launch"),
+                    algorithmic_bytes_per_launch=round(dom_bytes / max(1, dom_launches)),
+                    avg_launch_us=round(dom_avg_ms * 1e3, 2), launches=dom_launches,
+                    peak_source=peaks["source"])
+    # prefill
+    pre_gateup_ms = prof_pre["gateup"][0] / max(1, prof_pre["gateup"][1])
+    pre_gateup_flops = 2.0 * 2 * shape.ffn * shape.hidden * (pre_slots_routed
+                                                              + PREFILL_TOKENS * shape.num_shared)
+    pre_gu_tflops = pre_gateup_flops / (pre_gateup_ms / 1e3) / 1e12
+    pre_roof = dict(kernel="tc_grouped_gemm (gateup) prefill", bound="tensor",
+                    achieved=round(pre_gu_tflops, 1), peak=peaks["bf16_tflops"], unit="TFLOP/s",
+                    frac=round(pre_gu_tflops / peaks["bf16_tflops"], 4),
+                    traffic=traffic.get("prefill_gateup_bytes_per_launch"),
+                    algorithmic_flops_per_launch=pre_gateup_flops,
+                    avg_launch_us=round(pre_gateup_ms * 1e3, 1), launches=prof_pre["gateup"][1],
+                    peak_source=peaks["source"])
+    pre_layer_tflops = pre_flops / (pre_ms / 1e3) / 1e12
+    prefill = dict(metric=METRIC_PREFILL, value=round(PREFILL_TOKENS * dist.world / (pre_ms / 1e3), 1),
+                   unit="tokens/s", ms_per_step=round(pre_ms, 4), steps=KP,
+                   layer_tflops=round(pre_layer_tflops, 1),
+                   layer_tc_frac=round(pre_layer_tflops / peaks["bf16_tflops"], 4),
+                   flops_per_call=pre_flops, expert_load_max_over_mean=round(imbalance, 2),
+                   gpu_launches=pre_launches, roofline=pre_roof,
+                   stages_ms_per_call={s: round(prof_pre[s][0] / KP, 4) for s in prof_pre
+                                       if s != "calls"})
+    decode = dict(metric=METRIC_DECODE, value=round(dec_value, 1), unit="tokens/s",
+                  ms_per_step=round(dec_ms_step, 4), per_batch=per_batch, roofline=dec_roof,
+                  gpu_launches=dec_launches,
+                  stages_ms_per_step={s: round(prof_dec[s][0] / K, 4) for s in prof_dec
+                                      if s != "calls"})
+    e2e = dict(value=round(tokens_step * dist.world / (e2e_ms / 1e3), 1), unit="tokens/s",
+               h2d_bytes_per_step=int(h2d), d2h_bytes_per_step=int(d2h),
+               ms_per_step=round(e2e_ms, 4),
+               path="ChronosMOEFeedForward.forward (eager), pinned host x -> device -> host y")
+
+    head = decode if args.workload == "decode" else prefill
+    line = {
+        "metric": head["metric"], "value": head["value"], "unit": head["unit"],
+        "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, N(0,0.02) weights)",
+        "config": {
+            "workload": ("decode: MoE layer d_model 2048, 64 experts top-6 + 2 shared, d_ff 1408 "
+                         "(DeepSeek-MoE-16B shape), batches 1/8/32/64, availability "
+                         "Bernoulli(0.9)" if args.workload == "decode" else
+                         "prefill: same layer, 8192 tokens, Zipf(1.1) router bias, all available"),
+            "l2": "flushed before every timed call (256 MB write)",
+            "graphs": "decode calls replayed as CUDA graphs" if args.workload == "decode" else "eager",
+            "parallelism": f"replicas x{dist.world}",
+        },
+        "roofline": dec_roof if args.workload == "decode" else pre_roof,
+        "e2e": e2e,
+        "clocks": clocks,
+        "gpu_launches": decode["gpu_launches"] if args.workload == "decode" else pre_launches,
+        "decode": decode if args.workload != "decode" else {k: v for k, v in decode.items()
+                                                            if k not in ("metric", "value", "unit")},
+        "prefill": prefill,
+    }
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(w, wl.x, mask_host, shape, args.workload,
+                                            xp_dev=xp, bias=bias)
+    return line
+
+
+# ---------------------------------------------------------------------------
+# CPU: the oracle port (reference arm and cpu_baseline)
+# ---------------------------------------------------------------------------
+
+def _cpu_weights(w):
+    f = lambda t: t.detach().float().cpu().numpy()  # noqa: E731
+    return dict(router=f(w.router), gate=f(w.gate), up=f(w.up), down=f(w.down),
+                sh_gate=f(w.sh_gate), sh_up=f(w.sh_up), sh_down=f(w.sh_down))
+
+
+def _threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return int(max(n)) if n else 1
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def _oracle_call(cw, x, avail, shape, bias=None):
+    from oracle import moe_oracle as O
+    return O.moe_forward(x, cw["router"], cw["gate"], cw["up"], cw["down"], cw["sh_gate"],
+                         cw["sh_up"], cw["sh_down"], shape.top_k, shape.norm_topk, avail=avail,
+                         bias=bias)
+
+
+def cpu_baseline(w, x_dev, mask_host, shape, workload, xp_dev=None, bias=None, budget_s=15.0):
+    cw = _cpu_weights(w)
+    avail = mask_host.numpy().astype(np.float32)
+    if workload == "decode":
+        x = x_dev.float().cpu().numpy()
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            for b in DECODE_BATCHES:
+                _oracle_call(cw, x[:b], avail, shape)
+            reps += 1
+            if time.perf_counter() - t0 > budget_s or reps >= 5:
+                break
+        dt = time.perf_counter() - t0
+        return dict(value=round(reps * sum(DECODE_BATCHES) / dt, 2), unit="tokens/s",
+                    cores=_threads(), kind="port",
+                    sample=f"{reps} decode step(s) (batches 1/8/32/64) of the oracle port "
+                           "(C router + numpy/BLAS fp32 experts)")
+    x = xp_dev[:512].float().cpu().numpy()
+    b = bias.float().cpu().numpy()
+    t0 = time.perf_counter()
+    _oracle_call(cw, x, None, shape, bias=b)
+    dt = time.perf_counter() - t0
+    return dict(value=round(512 / dt, 2), unit="tokens/s", cores=_threads(), kind="port",
+                sample="512 of the 8192 prefill tokens through the oracle port")
+
+
+def run_reference(args, dist: Dist):
+    from project_chronos_b200 import synthetic as syn
+    spec = syn.WORKLOADS["decode"]
+    shape = spec["shape"]
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    wl = syn.make_workload(shape, max(DECODE_BATCHES), seed=1234, dtype=torch.bfloat16,
+                           device=dev, avail_p=spec["avail_p"])
+    cw = _cpu_weights(wl.weights)
+    mask = wl.mask.cpu().numpy().astype(np.float32)
+    x = wl.x.float().cpu().numpy()
+    if args.workload == "prefill":
+        g = syn.make_generator(99, dev)
+        xp = syn.make_hidden(PREFILL_TOKENS, shape.hidden, g, dtype=torch.bfloat16, device=dev)
+        bias = syn.make_zipf_bias(shape.num_experts, 1.1, g, dev).float().cpu().numpy()
+        sample_tokens = 256
+        xs = xp[:sample_tokens].float().cpu().numpy()
+
+        def step():
+            _oracle_call(cw, xs, None, shape, bias=bias)
+        tokens = sample_tokens
+        metric = METRIC_PREFILL
+        sample = f"{sample_tokens} of the 8192 prefill tokens per step"
+    else:
+        def step():
+            for b in DECODE_BATCHES:
+                _oracle_call(cw, x[:b], mask, shape)
+        tokens = sum(DECODE_BATCHES)
+        metric = METRIC_DECODE
+        sample = "one decode step (batches 1/8/32/64) per step"
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    value = tokens * args.steps / dt
+    cores = _threads()
+    return {
+        "impl": "reference", "metric": metric, "value": round(value, 2), "unit": "tokens/s",
+        "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": metric, "parallelism": "cpu (rank 0 only)"},
+        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": cores,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=("decode", "prefill"), default="decode")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    dist = Dist()
+    if args.impl == "reference":
+        if dist.rank != 0:
+            return 0
+        print(json.dumps(run_reference(args, dist)), flush=True)
+        return 0
+    if not torch.cuda.is_available():
+        print(json.dumps({"error": "no CUDA device"}))
+        return 1
+    dist.init()
+    try:
+        line = run_ours(args, dist)
+    finally:
+        torch.cuda.synchronize()
+        dist.close()
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

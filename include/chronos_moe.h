@@ -153,6 +153,31 @@ CHRONOS_API int chronos_moe_abi_version(void);
  * check its mirror of the struct. */
 CHRONOS_API size_t chronos_moe_args_size(void);
 
+/* ---- measurement aids (no counterpart in the reference, which has no
+ * profiling of this path) ---- */
+
+/* Stages of one chronos_moe_forward call, in launch order. */
+#define CHRONOS_STAGE_ROUTE 0
+#define CHRONOS_STAGE_PLAN 1
+#define CHRONOS_STAGE_SCATTER 2
+#define CHRONOS_STAGE_GATEUP 3
+#define CHRONOS_STAGE_ACT 4
+#define CHRONOS_STAGE_DOWN 5
+#define CHRONOS_STAGE_FINALIZE 6
+#define CHRONOS_NUM_STAGES 7
+
+/* After chronos_moe_profile_begin(max_calls), the next max_calls forward
+ * calls made on this host thread record CUDA events on their stream around
+ * each stage's kernel.  chronos_moe_profile_end synchronises on those events
+ * and writes, per stage, the summed device milliseconds and the number of
+ * kernel launches; it returns the number of calls recorded (or a negative
+ * CHRONOS_ERR_* code) and ends profiling. */
+CHRONOS_API int chronos_moe_profile_begin(int max_calls);
+CHRONOS_API int chronos_moe_profile_end(float* stage_ms, int32_t* stage_launches, int max_stages);
+
+/* Kernels launched by this library since it was loaded (all threads). */
+CHRONOS_API uint64_t chronos_moe_kernel_launches(void);
+
 #ifdef __cplusplus
 }
 #endif

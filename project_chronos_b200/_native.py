@@ -40,7 +40,11 @@ ABI_VERSION = 1
 
 # Functions declared in include/chronos_moe.h (checked against the header by the tests).
 EXPORTS = ("chronos_moe_workspace_size", "chronos_moe_forward", "chronos_moe_route",
-           "chronos_moe_last_error", "chronos_moe_abi_version", "chronos_moe_args_size")
+           "chronos_moe_last_error", "chronos_moe_abi_version", "chronos_moe_args_size",
+           "chronos_moe_profile_begin", "chronos_moe_profile_end",
+           "chronos_moe_kernel_launches")
+
+STAGES = ("route", "plan", "scatter", "gateup", "act", "down", "finalize")
 
 
 class ChronosMoeShape(ctypes.Structure):
@@ -120,6 +124,13 @@ def load_library(path: str = LIB_PATH):
         lib.chronos_moe_abi_version.restype = ctypes.c_int
         lib.chronos_moe_args_size.argtypes = []
         lib.chronos_moe_args_size.restype = ctypes.c_size_t
+        lib.chronos_moe_profile_begin.argtypes = [ctypes.c_int]
+        lib.chronos_moe_profile_begin.restype = ctypes.c_int
+        lib.chronos_moe_profile_end.argtypes = [ctypes.POINTER(ctypes.c_float),
+                                                ctypes.POINTER(ctypes.c_int32), ctypes.c_int]
+        lib.chronos_moe_profile_end.restype = ctypes.c_int
+        lib.chronos_moe_kernel_launches.argtypes = []
+        lib.chronos_moe_kernel_launches.restype = ctypes.c_uint64
         if lib.chronos_moe_abi_version() != ABI_VERSION:
             raise RuntimeError("chronos MoE extension ABI version mismatch; rebuild it")
         if lib.chronos_moe_args_size() != ctypes.sizeof(ChronosMoeArgs):

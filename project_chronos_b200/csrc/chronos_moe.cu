@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -15,6 +16,7 @@
 #include <type_traits>
 #include <string>
 #include <unordered_map>
+#include <vector>
 
 #include "chronos_moe.h"
 #include "common.cuh"
@@ -48,6 +50,37 @@ int fail(int code, const char* fmt, ...) {
     } while (0)
 
 constexpr int kSplitMaxTokens = 64;  // decode batches up to this size may split K
+
+std::atomic<uint64_t> g_kernel_launches{0};
+
+inline void count_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
+
+// ---------------------------------------------------------------------------
+// stage profiling: CUDA events at the stage boundaries of profiled calls
+// ---------------------------------------------------------------------------
+constexpr int kBoundaries = CHRONOS_NUM_STAGES + 1;
+
+struct ProfileState {
+    int max_calls = 0;
+    int calls = 0;
+    std::vector<cudaEvent_t> events;           // [max_calls * kBoundaries]
+    std::vector<uint8_t> ran;                  // [max_calls * CHRONOS_NUM_STAGES]
+};
+thread_local ProfileState g_prof;
+
+// Slot of the current call in the profile, or -1.
+int prof_begin_call() {
+    if (g_prof.calls >= g_prof.max_calls) return -1;
+    return g_prof.calls++;
+}
+
+void prof_mark(int slot, int boundary, cudaStream_t st) {
+    if (slot >= 0) cudaEventRecord(g_prof.events[static_cast<size_t>(slot) * kBoundaries + boundary], st);
+}
+
+void prof_ran(int slot, int stage) {
+    if (slot >= 0) g_prof.ran[static_cast<size_t>(slot) * CHRONOS_NUM_STAGES + stage] = 1;
+}
 
 size_t elem_size(int dtype) { return dtype == CHRONOS_DTYPE_FP32 ? 4 : 2; }
 
@@ -270,6 +303,7 @@ int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool p
     if (int rc = set_smem(route_kernel<T>, static_cast<int>(smem))) return rc;
     const unsigned grid = static_cast<unsigned>((s.num_tokens + kRouteTokens - 1) / kRouteTokens);
     route_kernel<T><<<grid, kRouteThreads, smem, st>>>(rp);
+    count_launch();
     CHRONOS_CUDA_CHECK(cudaGetLastError());
     return CHRONOS_OK;
 }
@@ -282,13 +316,14 @@ int launch_tc(const CUtensorMap& a0r, const CUtensorMap& a1r, const CUtensorMap&
     auto kern = tc_grouped_gemm<T, BN, GATEUP, SPLIT>;
     if (int rc = set_smem(kern, smem)) return rc;
     kern<<<grid, kTcThreads, smem, st>>>(a0r, a1r, a0s, a1s, br, bs, p);
+    count_launch();
     CHRONOS_CUDA_CHECK(cudaGetLastError());
     return CHRONOS_OK;
 }
 
 template <typename T, int BN>
 int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int splits_gu,
-                   int splits_dn, int kt_per_split_gu, int kt_per_split_dn) {
+                   int splits_dn, int kt_per_split_gu, int kt_per_split_dn, int slot) {
     const ChronosMoeShape& s = a->shape;
     const int dt = s.dtype;
     const uint64_t N = static_cast<uint64_t>(s.num_tokens), H = s.hidden, F = s.ffn;
@@ -344,8 +379,11 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     const bool split = splits_gu > 1;
     if (split) {
         CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + w.L->gu, 0, 4 * slots * 2 * F, st));
+        prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
         if ((rc = launch_tc<T, BN, true, true>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st)))
             return rc;
+        prof_ran(slot, CHRONOS_STAGE_GATEUP);
+        prof_mark(slot, CHRONOS_STAGE_ACT, st);
         ActParams ap{};
         ap.gu = w.at<float>(w.L->gu);
         ap.hid = w.ws + w.L->hid;
@@ -357,12 +395,18 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
         const int64_t total = static_cast<int64_t>(slots * F);
         const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4 * grid));
         act_kernel<T><<<blocks, 256, 0, st>>>(ap);
+        count_launch();
         CHRONOS_CUDA_CHECK(cudaGetLastError());
+        prof_ran(slot, CHRONOS_STAGE_ACT);
     } else {
+        prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
         if ((rc = launch_tc<T, BN, true, false>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st)))
             return rc;
+        prof_ran(slot, CHRONOS_STAGE_GATEUP);
+        prof_mark(slot, CHRONOS_STAGE_ACT, st);
     }
     (void)splits_dn;
+    prof_mark(slot, CHRONOS_STAGE_DOWN, st);
     // down
     TcGemmParams pd = p;
     pd.ustart = w.at<int32_t>(w.L->ustart_dn);
@@ -372,11 +416,12 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     pd.w_rows = static_cast<int>(H);
     pd.out_cols = static_cast<int>(H);
     if ((rc = launch_tc<T, BN, false, false>(d_r, d_r, d_s, d_s, h_m, h_m, pd, grid, st))) return rc;
+    prof_ran(slot, CHRONOS_STAGE_DOWN);
     return CHRONOS_OK;
 }
 
 template <typename T>
-int launch_simt(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st) {
+int launch_simt(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int slot) {
     const ChronosMoeShape& s = a->shape;
     SimtGemmParams p{};
     p.hdr = w.at<PlanHeader>(w.L->hdr);
@@ -403,8 +448,13 @@ int launch_simt(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st) {
     pg.w1r = a->w_up;
     pg.w0s = a->w_shared_gate;
     pg.w1s = a->w_shared_up;
+    prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
     simt_grouped_gemm<T, true><<<grid, kSimtThreads, 0, st>>>(pg);
+    count_launch();
     CHRONOS_CUDA_CHECK(cudaGetLastError());
+    prof_ran(slot, CHRONOS_STAGE_GATEUP);
+    prof_mark(slot, CHRONOS_STAGE_ACT, st);
+    prof_mark(slot, CHRONOS_STAGE_DOWN, st);
 
     SimtGemmParams pd = p;
     pd.ustart = w.at<int32_t>(w.L->ustart_dn);
@@ -414,7 +464,9 @@ int launch_simt(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st) {
     pd.w0r = a->w_down;
     pd.w0s = a->w_shared_down;
     simt_grouped_gemm<T, false><<<grid, kSimtThreads, 0, st>>>(pd);
+    count_launch();
     CHRONOS_CUDA_CHECK(cudaGetLastError());
+    prof_ran(slot, CHRONOS_STAGE_DOWN);
     return CHRONOS_OK;
 }
 
@@ -504,7 +556,11 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
         if (a->expert_mass)
             CHRONOS_CUDA_CHECK(cudaMemsetAsync(a->expert_mass, 0, 4 * s.num_experts, st));
     }
+    const int slot = prof_begin_call();
+    prof_mark(slot, CHRONOS_STAGE_ROUTE, st);
     if ((rc = launch_route<T>(a, w, st, prerouted, topk_idx, topk_w, true))) return rc;
+    prof_ran(slot, CHRONOS_STAGE_ROUTE);
+    prof_mark(slot, CHRONOS_STAGE_PLAN, st);
 
     PlanParams pp{};
     pp.n = N;
@@ -528,7 +584,10 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     pp.ustart_gu = w.at<int32_t>(L.ustart_gu);
     pp.ustart_dn = w.at<int32_t>(L.ustart_dn);
     plan_kernel<<<1, kPlanThreads, 0, st>>>(pp);
+    count_launch();
     CHRONOS_CUDA_CHECK(cudaGetLastError());
+    prof_ran(slot, CHRONOS_STAGE_PLAN);
+    prof_mark(slot, CHRONOS_STAGE_SCATTER, st);
 
     ScatterParams sp{};
     sp.x = a->x;
@@ -549,29 +608,35 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
         const int64_t warps = N * s.top_k;
         const unsigned blocks = static_cast<unsigned>((warps * 32 + kScatterThreads - 1) / kScatterThreads);
         scatter_kernel<T><<<blocks, kScatterThreads, 0, st>>>(sp);
+        count_launch();
         CHRONOS_CUDA_CHECK(cudaGetLastError());
     }
+    prof_ran(slot, CHRONOS_STAGE_SCATTER);
 
     if (tc) {
         if constexpr (std::is_same<T, float>::value) {
             return fail(CHRONOS_ERR_INVALID_ARG, "internal: fp32 on the tensor-core path");
         } else {
             switch (bn) {
-                case 16: rc = launch_tc_pair<T, 16>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn); break;
-                case 32: rc = launch_tc_pair<T, 32>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn); break;
-                case 64: rc = launch_tc_pair<T, 64>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn); break;
-                default: rc = launch_tc_pair<T, 128>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn); break;
+                case 16: rc = launch_tc_pair<T, 16>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot); break;
+                case 32: rc = launch_tc_pair<T, 32>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot); break;
+                case 64: rc = launch_tc_pair<T, 64>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot); break;
+                default: rc = launch_tc_pair<T, 128>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot); break;
             }
         }
     } else {
-        rc = launch_simt<T>(a, w, st);
+        rc = launch_simt<T>(a, w, st, slot);
     }
     if (rc) return rc;
 
+    prof_mark(slot, CHRONOS_STAGE_FINALIZE, st);
     const int64_t count4 = N * s.hidden / 4;
     const int blocks = static_cast<int>(std::min<int64_t>((count4 + 255) / 256, 8 * sm_count()));
     finalize_kernel<T><<<blocks, 256, 0, st>>>(w.at<float>(L.y_acc), static_cast<T*>(a->y), count4);
+    count_launch();
     CHRONOS_CUDA_CHECK(cudaGetLastError());
+    prof_ran(slot, CHRONOS_STAGE_FINALIZE);
+    prof_mark(slot, kBoundaries - 1, st);
     return CHRONOS_OK;
 }
 
@@ -628,3 +693,51 @@ extern "C" const char* chronos_moe_last_error(void) { return g_last_error.c_str(
 extern "C" int chronos_moe_abi_version(void) { return CHRONOS_MOE_ABI_VERSION; }
 
 extern "C" size_t chronos_moe_args_size(void) { return sizeof(ChronosMoeArgs); }
+
+extern "C" int chronos_moe_profile_begin(int max_calls) {
+    g_last_error.clear();
+    if (max_calls < 1 || max_calls > 100000)
+        return fail(CHRONOS_ERR_INVALID_ARG, "max_calls %d out of range [1, 100000]", max_calls);
+    const size_t need = static_cast<size_t>(max_calls) * kBoundaries;
+    while (g_prof.events.size() < need) {
+        cudaEvent_t ev;
+        CHRONOS_CUDA_CHECK(cudaEventCreate(&ev));
+        g_prof.events.push_back(ev);
+    }
+    g_prof.ran.assign(static_cast<size_t>(max_calls) * CHRONOS_NUM_STAGES, 0);
+    g_prof.max_calls = max_calls;
+    g_prof.calls = 0;
+    return CHRONOS_OK;
+}
+
+extern "C" int chronos_moe_profile_end(float* stage_ms, int32_t* stage_launches, int max_stages) {
+    g_last_error.clear();
+    const int calls = g_prof.calls;
+    g_prof.max_calls = 0;
+    g_prof.calls = 0;
+    const int ns = std::min(max_stages, CHRONOS_NUM_STAGES);
+    for (int i = 0; i < ns; ++i) {
+        if (stage_ms) stage_ms[i] = 0.0f;
+        if (stage_launches) stage_launches[i] = 0;
+    }
+    for (int c = 0; c < calls; ++c) {
+        cudaEvent_t* ev = g_prof.events.data() + static_cast<size_t>(c) * kBoundaries;
+        cudaError_t e = cudaEventSynchronize(ev[kBoundaries - 1]);
+        if (e != cudaSuccess)
+            return -fail(CHRONOS_ERR_CUDA, "cudaEventSynchronize: %s", cudaGetErrorString(e));
+        for (int i = 0; i < ns; ++i) {
+            float ms = 0.0f;
+            e = cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
+            if (e != cudaSuccess)
+                return -fail(CHRONOS_ERR_CUDA, "cudaEventElapsedTime: %s", cudaGetErrorString(e));
+            if (stage_ms) stage_ms[i] += ms;
+            if (stage_launches)
+                stage_launches[i] += g_prof.ran[static_cast<size_t>(c) * CHRONOS_NUM_STAGES + i];
+        }
+    }
+    return calls;
+}
+
+extern "C" uint64_t chronos_moe_kernel_launches(void) {
+    return g_kernel_launches.load(std::memory_order_relaxed);
+}

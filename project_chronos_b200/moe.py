@@ -200,6 +200,34 @@ class ChronosMOEFeedForward(nn.Module):
     last_fallback_weight_mass = _stat_prop("last_fallback_weight_mass")
     del _stat_prop
 
+    @classmethod
+    def from_stacked(cls, config, router: torch.Tensor, gate: torch.Tensor, up: torch.Tensor,
+                     down: torch.Tensor, sh_gate: Optional[torch.Tensor] = None,
+                     sh_up: Optional[torch.Tensor] = None,
+                     sh_down: Optional[torch.Tensor] = None) -> "ChronosMOEFeedForward":
+        """Build a layer around already-stacked weights (no copy): gate/up
+        ``[E, F, H]``, down ``[E, H, F]``, shared ``[S, ...]``; the per-expert
+        parameters become views of these tensors."""
+        with torch.device("meta"):
+            m = cls(config)
+        dev, dt = gate.device, gate.dtype
+        S = len(m.shared_experts)
+        pool = dict(gate=gate, up=up, down=down,
+                    sh_gate=sh_gate if S else None, sh_up=sh_up if S else None,
+                    sh_down=sh_down if S else None)
+        m.gate.weight = nn.Parameter(router, requires_grad=False)
+        for e, ex in enumerate(m.experts):
+            ex.gate_proj.weight = nn.Parameter(gate[e], requires_grad=False)
+            ex.up_proj.weight = nn.Parameter(up[e], requires_grad=False)
+            ex.down_proj.weight = nn.Parameter(down[e], requires_grad=False)
+        for j, ex in enumerate(m.shared_experts):
+            ex.gate_proj.weight = nn.Parameter(sh_gate[j], requires_grad=False)
+            ex.up_proj.weight = nn.Parameter(sh_up[j], requires_grad=False)
+            ex.down_proj.weight = nn.Parameter(sh_down[j], requires_grad=False)
+        m._pool = pool
+        m._sync_pool(dev, dt)
+        return m
+
     # ------------------------------------------------------------------
     def _apply(self, fn, *args, **kwargs):
         self._pool_dirty = True

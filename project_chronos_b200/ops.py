@@ -186,6 +186,31 @@ def moe_route(x: torch.Tensor, router_w: torch.Tensor, top_k: int, norm_topk: bo
     return dict(probs=probs, topk_idx=topk_idx, topk_weight=topk_w, counts=counts, mass=mass)
 
 
+def profile_begin(max_calls: int) -> None:
+    """Record per-stage CUDA events for the next ``max_calls`` layer calls (this thread)."""
+    lib = N.load_library()
+    N.check(lib.chronos_moe_profile_begin(int(max_calls)))
+
+
+def profile_end() -> dict:
+    """Synchronise and return {"calls": c, stage: (total_ms, launches), ...}."""
+    lib = N.load_library()
+    ms = (ctypes.c_float * len(N.STAGES))()
+    cnt = (ctypes.c_int32 * len(N.STAGES))()
+    calls = lib.chronos_moe_profile_end(ms, cnt, len(N.STAGES))
+    if calls < 0:
+        N.check(-calls)
+    out = {"calls": int(calls)}
+    for i, name in enumerate(N.STAGES):
+        out[name] = (float(ms[i]), int(cnt[i]))
+    return out
+
+
+def kernel_launches() -> int:
+    """Kernels launched by the extension since it was loaded."""
+    return int(N.load_library().chronos_moe_kernel_launches())
+
+
 # ---------------------------------------------------------------------------
 # torch.library registration (one graph node for torch.compile)
 # ---------------------------------------------------------------------------
