@@ -143,6 +143,37 @@ CHRONOS_API int chronos_moe_forward(const ChronosMoeArgs* args, void* cuda_strea
  * moe_chronos.py:228-248).  topk_idx and topk_weight are required. */
 CHRONOS_API int chronos_moe_route(const ChronosMoeArgs* args, void* cuda_stream);
 
+/* Largest workspace chronos_moe_forward_noalloc can serve: 16 MiB, enough
+ * for decode batches (e.g. up to 64 tokens of a d_model 2048, 64-expert top-6
+ * layer with d_ff 1408 and 2 shared experts). */
+#define CHRONOS_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* chronos_moe_forward for callers that cannot allocate device memory.
+ *
+ * No counterpart in the reference (its layer allocates through PyTorch).
+ * Some hosts cannot hand this library a workspace: an engine embedding the
+ * layer through FFI with no handle on the GPU allocator, a decode loop
+ * running inside a CUDA graph whose memory was fixed at capture time, or a
+ * real-time server that forbids cudaMalloc after start-up because it
+ * synchronises the device and can fail under fragmentation.  This entry point
+ * computes exactly what chronos_moe_forward computes, but ignores
+ * args->workspace / args->workspace_bytes and uses one scratch array built
+ * into the library (CHRONOS_NOALLOC_SCRATCH_BYTES of device memory, reserved
+ * on every GPU that loads the library and held until the process exits).  It
+ * calls no cudaMalloc, cudaFree or other allocating routine; the caller
+ * still passes x, the weights and every output buffer.
+ *
+ * - Shapes whose chronos_moe_workspace_size exceeds the limit are rejected
+ *   with CHRONOS_ERR_INVALID_ARG before anything is launched.
+ * - The first call on a device looks up the scratch array's device address
+ *   (with that device current); make that first call before any stream
+ *   capture on the device.
+ * - Every call shares the one array: calls that can overlap on the GPU (on
+ *   different streams, or from different host threads without ordering)
+ *   race on it and give undefined results.  Calls ordered on one stream are
+ *   safe; each call re-initialises the scratch state it relies on. */
+CHRONOS_API int chronos_moe_forward_noalloc(const ChronosMoeArgs* args, void* cuda_stream);
+
 /* Message of the last failing call on this host thread ("" if none). */
 CHRONOS_API const char* chronos_moe_last_error(void);
 

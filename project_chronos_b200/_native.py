@@ -42,7 +42,9 @@ ABI_VERSION = 1
 EXPORTS = ("chronos_moe_workspace_size", "chronos_moe_forward", "chronos_moe_route",
            "chronos_moe_last_error", "chronos_moe_abi_version", "chronos_moe_args_size",
            "chronos_moe_profile_begin", "chronos_moe_profile_end",
-           "chronos_moe_kernel_launches")
+           "chronos_moe_kernel_launches", "chronos_moe_forward_noalloc")
+
+NOALLOC_SCRATCH_BYTES = 16 << 20  # CHRONOS_NOALLOC_SCRATCH_BYTES
 
 STAGES = ("route", "plan", "scatter", "gateup", "act", "down", "finalize")
 
@@ -131,6 +133,9 @@ def load_library(path: str = LIB_PATH):
         lib.chronos_moe_profile_end.restype = ctypes.c_int
         lib.chronos_moe_kernel_launches.argtypes = []
         lib.chronos_moe_kernel_launches.restype = ctypes.c_uint64
+        lib.chronos_moe_forward_noalloc.argtypes = [ctypes.POINTER(ChronosMoeArgs),
+                                                    ctypes.c_void_p]
+        lib.chronos_moe_forward_noalloc.restype = ctypes.c_int
         if lib.chronos_moe_abi_version() != ABI_VERSION:
             raise RuntimeError("chronos MoE extension ABI version mismatch; rebuild it")
         if lib.chronos_moe_args_size() != ctypes.sizeof(ChronosMoeArgs):

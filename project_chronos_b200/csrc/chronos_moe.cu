@@ -688,6 +688,60 @@ extern "C" int chronos_moe_route(const ChronosMoeArgs* args, void* cuda_stream) 
     }
 }
 
+// ---------------------------------------------------------------------------
+// No-allocation variant: the workspace is a scratch array compiled into the
+// library instead of caller memory.  Host code must not use the array's name
+// as a device address (on the host it names a shadow object), so its device
+// address is looked up per device with cudaGetSymbolAddress and cached.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) uint8_t g_noalloc_scratch[CHRONOS_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {nullptr};
+
+int noalloc_scratch(void** out) {
+    int dev = -1;
+    CHRONOS_CUDA_CHECK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices)
+        return fail(CHRONOS_ERR_INVALID_ARG, "device %d out of range for the scratch table", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        CHRONOS_CUDA_CHECK(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        if (p == nullptr || (reinterpret_cast<uintptr_t>(p) & 255) != 0)
+            return fail(CHRONOS_ERR_CUDA, "scratch array address %p is unusable", p);
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return CHRONOS_OK;
+}
+}  // namespace
+
+extern "C" int chronos_moe_forward_noalloc(const ChronosMoeArgs* args, void* cuda_stream) {
+    g_last_error.clear();
+    if (args == nullptr) return fail(CHRONOS_ERR_INVALID_ARG, "args is NULL");
+    if (int rc = validate_shape(&args->shape)) return rc;
+    const size_t need = make_layout(args->shape).total;
+    if (need > CHRONOS_NOALLOC_SCRATCH_BYTES)
+        return fail(CHRONOS_ERR_INVALID_ARG,
+                    "this shape needs %zu bytes of scratch; chronos_moe_forward_noalloc serves at "
+                    "most %u (use chronos_moe_forward with a caller workspace)",
+                    need, CHRONOS_NOALLOC_SCRATCH_BYTES);
+    if (args->shape.num_tokens == 0) return CHRONOS_OK;
+    ChronosMoeArgs a = *args;
+    if (int rc = noalloc_scratch(&a.workspace)) return rc;
+    a.workspace_bytes = CHRONOS_NOALLOC_SCRATCH_BYTES;
+    if (int rc = validate_args(&a, true)) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    switch (a.shape.dtype) {
+        case CHRONOS_DTYPE_BF16: return forward_impl<__nv_bfloat16>(&a, st);
+        case CHRONOS_DTYPE_FP16: return forward_impl<__half>(&a, st);
+        default: return forward_impl<float>(&a, st);
+    }
+}
+
 extern "C" const char* chronos_moe_last_error(void) { return g_last_error.c_str(); }
 
 extern "C" int chronos_moe_abi_version(void) { return CHRONOS_MOE_ABI_VERSION; }
