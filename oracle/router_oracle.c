@@ -1,20 +1,21 @@
 /*
  * router_oracle.c — CPU restatement of the Chronos MoE router, TEST
  * INFRASTRUCTURE ONLY.  Only tests/, __graft_entry__.smoke() and bench.py's
- * CPU-baseline leg may load this file's library; it is the checker, never
- * the product.
+ * CPU legs may load this file's library; it is the checker, never the
+ * product.
  *
  * Restates chronos/model/moe_chronos.py:112 (gate GEMM + softmax) and
- * :124-128 (top-k + optional renormalisation) under the routing contract of
- * include/chronos_moe.h:
- *   logit[t][e] = fmaf-chain over h = 0..H-1 of x[t][h] * w[e][h]  (+ bias[e])
+ * :124-128 (top-k + optional renormalisation) under the bit-exact routing
+ * contract of include/chronos_moe.h:
+ *   partial[c] = fmaf chain over h in [128c, min(128c + 128, H)), from 0.0f
+ *   logit      = ((0.0f + partial[0]) + partial[1]) + ... (+ bias[e])
  *   rank experts by (logit desc, index asc), keep k
  *   prob = softmax(logit) in fp32; weight = prob of the chosen experts,
  *   divided by (sum + 1e-20) when norm_topk (moe_chronos.py:127-128).
- * The fmaf chain is the exact operation sequence every CUDA thread of the
- * router kernel performs, so top-k indices match bit for bit.  Softmax
- * uses libm expf, so probabilities/weights match the device within a few
- * ulp (compared with a tolerance, never bitwise).
+ * The chunk chains and their in-order sum are exactly the operations the CUDA
+ * router performs, so top-k indices match bit for bit.  Softmax uses libm
+ * expf, so probabilities/weights match the device within a few ulp (compared
+ * with a tolerance, never bitwise).
  *
  * Inputs are fp32 arrays holding the operand values (bf16/fp16 inputs are
  * widened exactly before the call).
@@ -24,15 +25,26 @@
 #include <stdlib.h>
 #include <string.h>
 
+#define ROUTER_CHUNK 128
+
+static float logit_of(const float* xr, const float* wr, int h) {
+    float total = 0.0f;
+    for (int c0 = 0; c0 < h; c0 += ROUTER_CHUNK) {
+        const int c1 = c0 + ROUTER_CHUNK < h ? c0 + ROUTER_CHUNK : h;
+        float acc = 0.0f;
+        for (int i = c0; i < c1; ++i) acc = fmaf(xr[i], wr[i], acc);
+        total = total + acc;
+    }
+    return total;
+}
+
 /* logits [N, E] only: the bit-exact part of the contract. */
 void oracle_router_logits(const float* x, const float* w, const float* bias,
                           int64_t n, int h, int e, float* logits) {
     for (int64_t t = 0; t < n; ++t) {
         const float* xr = x + t * (int64_t)h;
         for (int j = 0; j < e; ++j) {
-            const float* wr = w + (int64_t)j * h;
-            float acc = 0.0f;
-            for (int i = 0; i < h; ++i) acc = fmaf(xr[i], wr[i], acc);
+            float acc = logit_of(xr, w + (int64_t)j * h, h);
             if (bias) acc = acc + bias[j];
             logits[t * e + j] = acc;
         }

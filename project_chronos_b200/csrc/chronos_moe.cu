@@ -88,7 +88,7 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Workspace regions, a function of the shape only.
 struct Layout {
-    size_t grp_count, grp_off, act_rows, act_xrow, act_hrow, act_wslot, act_eid, ustart_gu,
+    size_t grp_count, grp_off, act_rows, act_xrow, act_hrow, act_wslot, act_eid, ustart_gu, partials,
         ustart_dn, hdr, pos, sel_coef, shared_coef, topk_idx, topk_w, slot_tok, slot_coef, xp,
         hid, gu, y_acc, total;
     bool split_capable;
@@ -121,6 +121,8 @@ Layout make_layout(const ChronosMoeShape& s) {
     L.shared_coef = take(4 * N);
     L.topk_idx = take(4 * N * K);
     L.topk_w = take(4 * N * K);
+    L.partials = take(4 * N * E *
+                      (N <= static_cast<size_t>(kRouteSmallMax) ? route_chunks(s.hidden) : 1));
     L.slot_tok = take(4 * (N * K + S * N));
     L.slot_coef = take(4 * (N * K + S * N));
     L.xp = take(es * N * K * H);
@@ -299,10 +301,25 @@ int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool p
     rp.sel_coef = w.at<float>(w.L->sel_coef);
     rp.shared_coef = w.at<float>(w.L->shared_coef);
     rp.y_acc = zero_acc ? w.at<float>(w.L->y_acc) : nullptr;
-    const size_t smem = route_smem_bytes(s.num_experts);
-    if (int rc = set_smem(route_kernel<T>, static_cast<int>(smem))) return rc;
-    const unsigned grid = static_cast<unsigned>((s.num_tokens + kRouteTokens - 1) / kRouteTokens);
-    route_kernel<T><<<grid, kRouteThreads, smem, st>>>(rp);
+    rp.partials = w.at<float>(w.L->partials);
+    const int64_t N = s.num_tokens;
+    const bool small = N <= kRouteSmallMax;
+    rp.nchunks = small ? route_chunks(s.hidden) : 1;
+    if (!prerouted) {
+        if (small) {
+            const int64_t threads = (N + kRouteGroup - 1) / kRouteGroup * s.num_experts * rp.nchunks;
+            const unsigned grid = static_cast<unsigned>((threads + kPartialThreads - 1) / kPartialThreads);
+            route_partials_kernel<T><<<grid, kPartialThreads, 0, st>>>(rp);
+        } else {
+            const dim3 grid(static_cast<unsigned>((N + kRouteTile - 1) / kRouteTile),
+                            static_cast<unsigned>((s.num_experts + kRouteTile - 1) / kRouteTile));
+            route_tiled_kernel<T><<<grid, kTiledThreads, 0, st>>>(rp);
+        }
+        count_launch();
+        CHRONOS_CUDA_CHECK(cudaGetLastError());
+    }
+    const unsigned sgrid = static_cast<unsigned>((N + kSelectThreads / 32 - 1) / (kSelectThreads / 32));
+    route_select_kernel<T><<<sgrid, kSelectThreads, 0, st>>>(rp);
     count_launch();
     CHRONOS_CUDA_CHECK(cudaGetLastError());
     return CHRONOS_OK;
@@ -312,7 +329,7 @@ template <typename T, int BN, bool GATEUP, bool SPLIT>
 int launch_tc(const CUtensorMap& a0r, const CUtensorMap& a1r, const CUtensorMap& a0s,
               const CUtensorMap& a1s, const CUtensorMap& br, const CUtensorMap& bs,
               const TcGemmParams& p, int grid, cudaStream_t st) {
-    constexpr int smem = tc_smem_bytes(BN, GATEUP);
+    constexpr int smem = tc_smem_bytes(BN, GATEUP, SPLIT);
     auto kern = tc_grouped_gemm<T, BN, GATEUP, SPLIT>;
     if (int rc = set_smem(kern, smem)) return rc;
     kern<<<grid, kTcThreads, smem, st>>>(a0r, a1r, a0s, a1s, br, bs, p);
@@ -377,7 +394,11 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     pg.w_rows = static_cast<int>(F);
     pg.out_cols = static_cast<int>(F);
     const bool split = splits_gu > 1;
+    if constexpr (BN > kSplitMaxTokens) {
+        if (split) return fail(CHRONOS_ERR_INVALID_ARG, "internal: split-K with a %d-token tile", BN);
+    }
     if (split) {
+        if constexpr (BN <= kSplitMaxTokens) {
         CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + w.L->gu, 0, 4 * slots * 2 * F, st));
         prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
         if ((rc = launch_tc<T, BN, true, true>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st)))
@@ -398,6 +419,7 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
         count_launch();
         CHRONOS_CUDA_CHECK(cudaGetLastError());
         prof_ran(slot, CHRONOS_STAGE_ACT);
+        }
     } else {
         prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
         if ((rc = launch_tc<T, BN, true, false>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st)))

@@ -216,6 +216,39 @@ struct AbFormat<__nv_bfloat16> {
     static constexpr int value = 1;
 };
 
+// ---------------------------------------------------------------------------
+// bulk (non-tensor) async copies between shared and global memory
+// ---------------------------------------------------------------------------
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (a following bulk copy that reads them).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// global[dst .. dst+bytes) += shared[src ..] element-wise in fp32 (performed at L2).
+__device__ __forceinline__ void bulk_reduce_add_f32(float* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(
+                     dst),
+                 "r"(smem_u32(src)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+                 "r"(smem_u32(src)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until this thread's committed bulk copies finished READING shared memory.
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until this thread's committed bulk copies completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Barrier among the `count` threads of the epilogue warps (id 1; id 0 is __syncthreads).
+__device__ __forceinline__ void epilogue_bar_sync(int count) {
+    asm volatile("bar.sync 1, %0;" ::"r"(count) : "memory");
+}
+
 __device__ __forceinline__ void red_add_f32(float* addr, float v) {
     asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
 }

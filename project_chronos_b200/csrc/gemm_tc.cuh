@@ -66,9 +66,19 @@ struct TcGemmParams {
 __host__ __device__ constexpr int tc_stage_bytes(int bn, bool gateup) {
     return kTcBM * kTcBK * 2 * (gateup ? 2 : 1) + bn * kTcBK * 2;
 }
-__host__ __device__ constexpr int tc_stages(int bn, bool gateup) {
-    return (200 * 1024) / tc_stage_bytes(bn, gateup) > 8 ? 8
-                                                          : (200 * 1024) / tc_stage_bytes(bn, gateup);
+// Epilogue staging: one output row per token of the tile, written to global
+// memory by per-token bulk copies (h rows: 128 bf16; split partials: 128 fp32
+// gate + 128 fp32 up; down: 128 fp32 to reduce into the accumulator).
+__host__ __device__ constexpr int tc_stage_row_bytes(bool gateup, bool split) {
+    return gateup ? (split ? 2 * kTcBM * 4 : kTcBM * 2) : kTcBM * 4;
+}
+__host__ __device__ constexpr int tc_staging_bytes(int bn, bool gateup, bool split) {
+    return bn * tc_stage_row_bytes(gateup, split);
+}
+__host__ __device__ constexpr int tc_stages(int bn, bool gateup, bool split) {
+    return (220 * 1024 - tc_staging_bytes(bn, gateup, split)) / tc_stage_bytes(bn, gateup) > 8
+               ? 8
+               : (220 * 1024 - tc_staging_bytes(bn, gateup, split)) / tc_stage_bytes(bn, gateup);
 }
 __host__ __device__ constexpr int tc_tmem_cols(int bn, bool gateup) {
     // two accumulator buffers of (gateup ? 2 : 1) * bn fp32 columns, power of two >= 32
@@ -78,8 +88,9 @@ __host__ __device__ constexpr int tc_tmem_cols(int bn, bool gateup) {
            : (2 * bn * (gateup ? 2 : 1)) <= 256 ? 256
                                                  : 512;
 }
-__host__ __device__ constexpr int tc_smem_bytes(int bn, bool gateup) {
-    return 1024 /* alignment slack */ + tc_stages(bn, gateup) * tc_stage_bytes(bn, gateup) + 256;
+__host__ __device__ constexpr int tc_smem_bytes(int bn, bool gateup, bool split) {
+    return 1024 /* alignment slack */ + tc_stages(bn, gateup, split) * tc_stage_bytes(bn, gateup) +
+           tc_staging_bytes(bn, gateup, split) + 256;
 }
 
 struct TcUnit {
@@ -117,18 +128,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     constexpr int A_BYTES = kTcBM * kTcBK * 2;
     constexpr int B_BYTES = BN * kTcBK * 2;
     constexpr int STAGE_BYTES = tc_stage_bytes(BN, GATEUP);
-    constexpr int STAGES = tc_stages(BN, GATEUP);
+    constexpr int STAGES = tc_stages(BN, GATEUP, SPLIT);
+    constexpr int ROW_BYTES = tc_stage_row_bytes(GATEUP, SPLIT);
     constexpr int ACC_COLS = GATEUP ? 2 * BN : BN;
     constexpr int TMEM_COLS = tc_tmem_cols(BN, GATEUP);
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N must be a multiple of 16");
     static_assert(B_BYTES % 1024 == 0 && A_BYTES % 1024 == 0,
                   "operand tiles must keep the 1024-byte alignment of the 128-B swizzle atoms");
     static_assert(2 * ACC_COLS <= 512, "two accumulator buffers must fit in TMEM");
+    static_assert(STAGES >= 2, "shared memory holds fewer than two pipeline stages");
+    static_assert(tc_smem_bytes(BN, GATEUP, SPLIT) <= 232448, "shared memory over the per-CTA limit");
 
     extern __shared__ uint8_t tc_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint8_t* staging = smem + STAGES * STAGE_BYTES;  // [BN][ROW_BYTES]
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + BN * ROW_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -258,22 +273,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else {
         // ------------------------------ epilogue ------------------------------
+        // Each unit: TMEM -> registers -> staging rows in shared memory (one row
+        // per token, 128 output columns), then one bulk copy per valid token
+        // row: a TMA reduce-add into the fp32 accumulator (down, split
+        // partials) or a plain bulk store of the hidden row (gate/up).
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         const int row_in_tile = q * 32 + lane;
+        const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
+        volatile int* ep_ok = abort_flag + 1;  // verdict of the accumulator wait, shared
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int u = blockIdx.x; u < total; u += gridDim.x) {
             const TcUnit w = tc_decode(p, num_active, u, BN, splits_unused);
-            if (!mbar_wait_bounded(&tfull[acc], acc_phase, kPipelineLimitNs, abort_flag)) {
-                *abort_flag = 1;
-                report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
-                break;
+            // one thread waits (bounded) for the accumulator; the barrier hands its
+            // verdict to the other 127, so they all leave together on a timeout
+            if (et == 0) {
+                const bool ok = mbar_wait_bounded(&tfull[acc], acc_phase, kPipelineLimitNs, abort_flag);
+                if (!ok) {
+                    *abort_flag = 1;
+                    report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                }
+                *ep_ok = ok ? 1 : 0;
             }
+            // the previous unit's bulk copies must also be done reading the staging rows
+            bulk_wait_read();
+            epilogue_bar_sync(128);
+            if (!*ep_ok) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * ACC_COLS);
-            const int wrow = w.mtile * kTcBM + row_in_tile;
-            const bool row_ok = wrow < p.out_cols;
+            const int m0 = w.mtile * kTcBM;
             const int rows = p.act_rows[w.a];
             const int tok0 = w.tok_tile * BN;
             const int64_t hrow0 = p.act_hrow[w.a];
@@ -285,41 +314,56 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     float uu[16];
                     tmem_ld16(taddr + BN + c, uu);
                     tmem_wait_ld();
-                    if (row_ok) {
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const int tok = tok0 + c + j;
-                            if (tok < rows) {
-                                const int64_t slot = hrow0 + tok;
-                                if constexpr (SPLIT) {
-                                    red_add_f32(p.gu + slot * 2 * p.f + wrow, g[j]);
-                                    red_add_f32(p.gu + slot * 2 * p.f + p.f + wrow, uu[j]);
-                                } else {
-                                    static_cast<T*>(p.hid)[slot * p.f + wrow] =
-                                        from_f32<T>(silu_f32(g[j]) * uu[j]);
-                                }
-                            }
+                    for (int j = 0; j < 16; ++j) {
+                        uint8_t* row = staging + (c + j) * ROW_BYTES;
+                        if constexpr (SPLIT) {
+                            reinterpret_cast<float*>(row)[row_in_tile] = g[j];
+                            reinterpret_cast<float*>(row)[kTcBM + row_in_tile] = uu[j];
+                        } else {
+                            reinterpret_cast<T*>(row)[row_in_tile] = from_f32<T>(silu_f32(g[j]) * uu[j]);
                         }
                     }
                 } else {
                     tmem_wait_ld();
-                    if (row_ok) {
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const int tok = tok0 + c + j;
-                            if (tok < rows) {
-                                const int64_t slot = hrow0 + tok;
-                                const int64_t t = p.slot_tok[slot];
-                                red_add_f32(p.y_acc + t * p.h + wrow, p.slot_coef[slot] * g[j]);
-                            }
-                        }
+                    for (int j = 0; j < 16; ++j) {
+                        const int tok = tok0 + c + j;
+                        const float coef = tok < rows ? p.slot_coef[hrow0 + tok] : 0.0f;
+                        reinterpret_cast<float*>(staging + (c + j) * ROW_BYTES)[row_in_tile] = coef * g[j];
                     }
                 }
             }
+            // accumulator drained: hand the TMEM buffer back to the MMA warp
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+            // staging rows complete -> per-token bulk copies
+            fence_proxy_async_smem();
+            epilogue_bar_sync(128);
+            const int ncols = min(kTcBM, p.out_cols - m0);
+            for (int r = et; r < BN; r += 128) {
+                const int tok = tok0 + r;
+                if (tok >= rows) continue;
+                const int64_t slot = hrow0 + tok;
+                const uint8_t* row = staging + r * ROW_BYTES;
+                if constexpr (GATEUP) {
+                    if constexpr (SPLIT) {
+                        float* dst = p.gu + slot * 2 * p.f + m0;
+                        bulk_reduce_add_f32(dst, row, static_cast<uint32_t>(ncols * 4));
+                        bulk_reduce_add_f32(dst + p.f, row + kTcBM * 4, static_cast<uint32_t>(ncols * 4));
+                    } else {
+                        bulk_store(static_cast<T*>(p.hid) + slot * p.f + m0, row,
+                                   static_cast<uint32_t>(ncols * sizeof(T)));
+                    }
+                } else {
+                    const int64_t t = p.slot_tok[slot];
+                    bulk_reduce_add_f32(p.y_acc + t * p.h + m0, row, static_cast<uint32_t>(ncols * 4));
+                }
+            }
+            bulk_commit();
         }
+        bulk_wait_all();
     }
 
     tc_fence_before();

@@ -47,43 +47,73 @@ struct PlanParams {
     int32_t* ustart_dn;  // [A + 1]
 };
 
-constexpr int kPlanThreads = 1024;
+constexpr int kPlanThreads = 256;  // >= the 256 experts the ABI accepts: one expert per thread
+
+// Inclusive scan over the block (kPlanThreads values), warp shuffles + one
+// pass over the warp totals.  `scratch` holds kPlanThreads / 32 ints.
+__device__ __forceinline__ int block_inclusive_scan(int v, int* scratch) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+    }
+    if (lane == 31) scratch[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        int s = lane < kPlanThreads / 32 ? scratch[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += n;
+        }
+        if (lane < kPlanThreads / 32) scratch[lane] = s;
+    }
+    __syncthreads();
+    if (warp > 0) v += scratch[warp - 1];
+    __syncthreads();
+    return v;
+}
 
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
-    __shared__ int32_t s_scan[kPlanThreads];
-    __shared__ int32_t s_act[kPlanThreads];
+    __shared__ int s_scratch[kPlanThreads / 32];
+    __shared__ int s_tot[4];
     const int tid = threadIdx.x;
     const int E = p.e;
-    // E <= 256 (validated on the host), so one element per thread
-    const int cnt = tid < E ? p.grp_count[tid] : 0;
-    const int is_act = (tid < E && cnt > 0) ? 1 : 0;
-    s_scan[tid] = cnt;
-    s_act[tid] = is_act;
-    __syncthreads();
-    // Hillis-Steele inclusive scans (E <= 256 -> 8 steps)
-    for (int o = 1; o < kPlanThreads; o <<= 1) {
-        const int a = tid >= o ? s_scan[tid - o] : 0;
-        const int b = tid >= o ? s_act[tid - o] : 0;
-        __syncthreads();
-        s_scan[tid] += a;
-        s_act[tid] += b;
-        __syncthreads();
-    }
-    const int total_routed = s_scan[kPlanThreads - 1];
-    const int n_routed_act = s_act[kPlanThreads - 1];
     const int S = p.num_shared;
     const int N = static_cast<int>(p.n);
-    // shared groups first (largest), then routed groups in expert order
+    const int cnt = tid < E ? p.grp_count[tid] : 0;
+    const int is_act = (tid < E && cnt > 0) ? 1 : 0;
+    const int tt = (cnt + p.tok_tile - 1) / p.tok_tile;
+    const int ugu = is_act ? tt * p.mt_gu * p.splits_gu : 0;
+    const int udn = is_act ? tt * p.mt_dn * p.splits_dn : 0;
+    const int inc_cnt = block_inclusive_scan(cnt, s_scratch);
+    const int inc_act = block_inclusive_scan(is_act, s_scratch);
+    const int inc_gu = block_inclusive_scan(ugu, s_scratch);
+    const int inc_dn = block_inclusive_scan(udn, s_scratch);
+    if (tid == kPlanThreads - 1) {
+        s_tot[0] = inc_cnt;
+        s_tot[1] = inc_act;
+        s_tot[2] = inc_gu;
+        s_tot[3] = inc_dn;
+    }
+    __syncthreads();
+    // shared groups first (the largest: N rows each), then routed groups in expert order
+    const int tt_sh = (N + p.tok_tile - 1) / p.tok_tile;
+    const int sh_gu = tt_sh * p.mt_gu * p.splits_gu;
+    const int sh_dn = tt_sh * p.mt_dn * p.splits_dn;
     if (tid < E) {
-        const int off = s_scan[tid] - cnt;
+        const int off = inc_cnt - cnt;
         p.grp_off[tid] = off;
         if (is_act) {
-            const int a = S + s_act[tid] - 1;
+            const int a = S + inc_act - 1;
             p.act_rows[a] = cnt;
             p.act_xrow[a] = off;
             p.act_hrow[a] = off;
             p.act_wslot[a] = p.slot_of_expert ? p.slot_of_expert[tid] : tid;
             p.act_eid[a] = tid;
+            p.ustart_gu[a] = S * sh_gu + inc_gu - ugu;
+            p.ustart_dn[a] = S * sh_dn + inc_dn - udn;
         }
     }
     if (tid < S) {
@@ -92,27 +122,20 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
         p.act_hrow[tid] = N * p.k + tid * N;
         p.act_wslot[tid] = tid;
         p.act_eid[tid] = -1;
+        p.ustart_gu[tid] = tid * sh_gu;
+        p.ustart_dn[tid] = tid * sh_dn;
     }
-    __syncthreads();
     if (tid == 0) {
-        const int A = S + n_routed_act;
-        int ugu = 0, udn = 0, mx = 0;
-        for (int a = 0; a < A; ++a) {
-            const int rows = p.act_rows[a];
-            const int tt = (rows + p.tok_tile - 1) / p.tok_tile;
-            p.ustart_gu[a] = ugu;
-            p.ustart_dn[a] = udn;
-            ugu += tt * p.mt_gu * p.splits_gu;
-            udn += tt * p.mt_dn * p.splits_dn;
-            mx = max(mx, rows);
-        }
-        p.ustart_gu[A] = ugu;
-        p.ustart_dn[A] = udn;
+        const int A = S + s_tot[1];
+        const int tot_gu = S * sh_gu + s_tot[2];
+        const int tot_dn = S * sh_dn + s_tot[3];
+        p.ustart_gu[A] = tot_gu;
+        p.ustart_dn[A] = tot_dn;
         p.hdr->num_active = A;
-        p.hdr->routed_rows = total_routed;
-        p.hdr->units_gu = ugu;
-        p.hdr->units_dn = udn;
-        p.hdr->max_rows = mx;
+        p.hdr->routed_rows = s_tot[0];
+        p.hdr->units_gu = tot_gu;
+        p.hdr->units_dn = tot_dn;
+        p.hdr->max_rows = S > 0 ? N : 0;
     }
 }
 

@@ -1,24 +1,35 @@
-// router.cuh — fused router GEMM + softmax + top-k + blend coefficients.
+// router.cuh — router GEMM + softmax + top-k + blend coefficients.
 //
 // Restates chronos/model/moe_chronos.py:112-128 (gate Linear, softmax, topk,
 // norm_topk_prob renormalisation) under the bit-exact routing contract of
-// include/chronos_moe.h: every logit is one thread's fmaf chain over
-// h = 0..H-1 in increasing order, so the ranking is identical on every run and
-// equal to the CPU oracle's.  Also produces, per token, the coefficient of the
-// shared-expert term (1 + sum_k w*(1-a)) / S_h (moe_chronos.py:255-268) and,
-// per selection with a > 0, the within-expert position used by the
-// permutation; zeroes the fp32 output accumulator rows of its tokens.
+// include/chronos_moe.h: a logit is the in-order fp32 sum of 128-element chunk
+// partials, each partial one thread's fmaf chain over its chunk in increasing
+// h, so the ranking is identical on every run and equal to the CPU oracle's.
+//
+// Two logit kernels produce the same bits:
+//   route_partials_kernel  small batches: one thread per (expert, chunk, group
+//                          of 8 tokens) writes chunk partials [N, E, C]
+//                          (parallel over chunks, so a decode token's 64
+//                          logits are not 2048-long serial chains);
+//   route_tiled_kernel     large batches: 64-token x 64-expert register-tiled
+//                          SIMT GEMM over the whole K, chunk partials folded in
+//                          order in registers, writes logits [N, E].
+// route_select_kernel (one warp per token) then sums the partials in chunk
+// order, applies the bias, softmax and top-k, and writes the per-token blend
+// coefficient of the shared experts (1 + sum_k w*(1-a)) / S_h
+// (moe_chronos.py:255-268), the within-expert position of every available
+// selection (for the permutation) and zeroes the token's fp32 accumulator row.
 #pragma once
 
 #include "common.cuh"
 
 namespace chronos {
 
-constexpr int kRouteTokens = 32;   // tokens per block
-constexpr int kRouteExperts = 64;  // experts per smem chunk
-constexpr int kRouteK = 64;        // h per smem chunk
-constexpr int kRouteThreads = 256;
-constexpr int kRoutePad = kRouteK + 4;  // row pitch (floats) of the smem tiles
+constexpr int kRouteChunk = 128;       // h per partial (the contract's chunk)
+constexpr int kRouteGroup = 8;         // tokens per thread in the partials kernel
+constexpr int kRouteSmallMax = 256;    // largest batch routed by the partials kernel
+constexpr int kRouteTile = 64;         // tokens and experts per tiled block
+constexpr int kRouteTileK = 32;        // h per smem stage of the tiled kernel
 constexpr int kMaxTopK = 16;
 constexpr int kMaxExperts = 256;
 
@@ -30,6 +41,8 @@ struct RouteParams {
     const int32_t* slot_of_expert;
     int64_t n;
     int h, e, k, num_shared, norm_topk, prerouted;
+    int nchunks;          // partials per logit in `partials` (1 = finished logits)
+    float* partials;      // [N, E, nchunks]
     void* probs;          // [N, E] T or null
     int32_t* topk_idx;    // [N, k]
     float* topk_w;        // [N, k]
@@ -39,10 +52,175 @@ struct RouteParams {
     int32_t* pos;         // [N, k] position within the expert group, -1 when a == 0
     float* sel_coef;      // [N, k] w * a
     float* shared_coef;   // [N] (1 + sum w (1 - a)) / S_h
-    float* y_acc;         // [N, H] fp32, zeroed here
+    float* y_acc;         // [N, H] fp32, zeroed here (or null)
 };
 
+inline int route_chunks(int h) { return (h + kRouteChunk - 1) / kRouteChunk; }
+
+// 4 consecutive elements as fp32 (8-byte loads for 16-bit types, 16 bytes for fp32).
 template <typename T>
+__device__ __forceinline__ float4 load4(const T* p);
+template <>
+__device__ __forceinline__ float4 load4<float>(const float* p) {
+    return *reinterpret_cast<const float4*>(p);
+}
+template <>
+__device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bfloat16* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+}
+template <>
+__device__ __forceinline__ float4 load4<__half>(const __half* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __half2 a = *reinterpret_cast<const __half2*>(&u.x);
+    const __half2 b = *reinterpret_cast<const __half2*>(&u.y);
+    const float2 fa = __half22float2(a), fb = __half22float2(b);
+    return make_float4(fa.x, fa.y, fb.x, fb.y);
+}
+
+// ---------------------------------------------------------------------------
+// small batches: chunk partials
+// ---------------------------------------------------------------------------
+constexpr int kPartialThreads = 128;
+
+template <typename T>
+__global__ void __launch_bounds__(kPartialThreads) route_partials_kernel(RouteParams p) {
+    const int E = p.e, C = p.nchunks, H = p.h;
+    const int64_t groups = (p.n + kRouteGroup - 1) / kRouteGroup;
+    const int64_t gid = static_cast<int64_t>(blockIdx.x) * kPartialThreads + threadIdx.x;
+    if (gid >= groups * E * C) return;
+    // consecutive threads: consecutive experts of one (token group, chunk), so
+    // the token chunks they read are the same addresses (L1 broadcast)
+    const int e = static_cast<int>(gid % E);
+    const int c = static_cast<int>((gid / E) % C);
+    const int64_t tgp = gid / (static_cast<int64_t>(E) * C);
+    const int64_t t0 = tgp * kRouteGroup;
+    const int64_t left = p.n - t0;
+    const int nt = left < kRouteGroup ? static_cast<int>(left) : kRouteGroup;
+    const int h0 = c * kRouteChunk;
+    const int h1 = min(H, h0 + kRouteChunk);
+    const T* x = static_cast<const T*>(p.x);
+    const T* wr = static_cast<const T*>(p.w) + static_cast<int64_t>(e) * H;
+    float acc[kRouteGroup];
+#pragma unroll
+    for (int i = 0; i < kRouteGroup; ++i) acc[i] = 0.0f;
+    for (int h = h0; h < h1; h += 4) {
+        const float4 b = load4<T>(wr + h);
+#pragma unroll
+        for (int i = 0; i < kRouteGroup; ++i) {
+            if (i < nt) {
+                const float4 a = load4<T>(x + (t0 + i) * H + h);
+                acc[i] = fmaf(a.x, b.x, acc[i]);
+                acc[i] = fmaf(a.y, b.y, acc[i]);
+                acc[i] = fmaf(a.z, b.z, acc[i]);
+                acc[i] = fmaf(a.w, b.w, acc[i]);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kRouteGroup; ++i)
+        if (i < nt) p.partials[((t0 + i) * E + e) * C + c] = acc[i];
+}
+
+// ---------------------------------------------------------------------------
+// large batches: register-tiled SIMT GEMM, chunk partials folded in order
+// ---------------------------------------------------------------------------
+constexpr int kTiledThreads = 256;
+constexpr int kTilePad = kRouteTileK + 4;
+
+template <typename T>
+__global__ void __launch_bounds__(kTiledThreads) route_tiled_kernel(RouteParams p) {
+    __shared__ __align__(16) float xs[2][kRouteTile][kTilePad];
+    __shared__ __align__(16) float ws[2][kRouteTile][kTilePad];
+    const int tid = threadIdx.x;
+    const int tg = tid >> 4;  // tokens tg*4 .. tg*4+3
+    const int eg = tid & 15;  // experts eg + 16 j
+    const int H = p.h, E = p.e;
+    const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kRouteTile;
+    const int e0 = blockIdx.y * kRouteTile;
+    const T* x = static_cast<const T*>(p.x);
+    const T* w = static_cast<const T*>(p.w);
+    // loader: row lr, 8 consecutive k at lk
+    const int lr = tid >> 2, lk = (tid & 3) * 8;
+    const bool xrow_ok = t0 + lr < p.n;
+    const bool wrow_ok = e0 + lr < E;
+    const T* xrow = x + (t0 + lr) * H;
+    const T* wrow = w + static_cast<int64_t>(e0 + lr) * H;
+    float4 xa, xb, wa, wb;
+    auto gload = [&](int kt) {
+        const int h = kt * kRouteTileK + lk;
+        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+        xa = (xrow_ok && h < H) ? load4<T>(xrow + h) : z;
+        xb = (xrow_ok && h + 4 < H) ? load4<T>(xrow + h + 4) : z;
+        wa = (wrow_ok && h < H) ? load4<T>(wrow + h) : z;
+        wb = (wrow_ok && h + 4 < H) ? load4<T>(wrow + h + 4) : z;
+    };
+    auto sstore = [&](int buf) {
+        *reinterpret_cast<float4*>(&xs[buf][lr][lk]) = xa;
+        *reinterpret_cast<float4*>(&xs[buf][lr][lk + 4]) = xb;
+        *reinterpret_cast<float4*>(&ws[buf][lr][lk]) = wa;
+        *reinterpret_cast<float4*>(&ws[buf][lr][lk + 4]) = wb;
+    };
+    float total[4][4], acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) { total[i][j] = 0.0f; acc[i][j] = 0.0f; }
+    const int KT = (H + kRouteTileK - 1) / kRouteTileK;
+    constexpr int kTilesPerChunk = kRouteChunk / kRouteTileK;
+    gload(0);
+    sstore(0);
+    __syncthreads();
+    for (int kt = 0; kt < KT; ++kt) {
+        const int buf = kt & 1;
+        if (kt + 1 < KT) gload(kt + 1);
+#pragma unroll
+        for (int kk = 0; kk < kRouteTileK; kk += 4) {
+            float4 a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = *reinterpret_cast<const float4*>(&xs[buf][tg * 4 + i][kk]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(&ws[buf][eg + 16 * j][kk]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    acc[i][j] = fmaf(a[i].x, b[j].x, acc[i][j]);
+                    acc[i][j] = fmaf(a[i].y, b[j].y, acc[i][j]);
+                    acc[i][j] = fmaf(a[i].z, b[j].z, acc[i][j]);
+                    acc[i][j] = fmaf(a[i].w, b[j].w, acc[i][j]);
+                }
+        }
+        if ((kt + 1) % kTilesPerChunk == 0 || kt + 1 == KT) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    total[i][j] = total[i][j] + acc[i][j];
+                    acc[i][j] = 0.0f;
+                }
+        }
+        if (kt + 1 < KT) sstore(buf ^ 1);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t t = t0 + tg * 4 + i;
+        if (t >= p.n) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int e = e0 + eg + 16 * j;
+            if (e < E) p.partials[t * E + e] = total[i][j];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// per token: finish logits, softmax, top-k, blend coefficients
+// ---------------------------------------------------------------------------
+constexpr int kSelectThreads = 256;
+
 __device__ __forceinline__ float expert_avail(const RouteParams& p, int e) {
     float a = p.avail ? p.avail[e] : 1.0f;
     if (p.slot_of_expert && p.slot_of_expert[e] < 0) a = 0.0f;
@@ -50,217 +228,145 @@ __device__ __forceinline__ float expert_avail(const RouteParams& p, int e) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteParams p) {
-    extern __shared__ float4 route_smem_f4[];
-    float* smem = reinterpret_cast<float*>(route_smem_f4);
-    float* xs = smem;                                  // [32][kRoutePad]
-    float* ws = xs + kRouteTokens * kRoutePad;         // [64][kRoutePad]
-    float* lg = ws + kRouteExperts * kRoutePad;        // [32][E]
-    const int tid = threadIdx.x;
-    const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kRouteTokens;
-    const int64_t left = p.n - t0;
-    const int nt = left < kRouteTokens ? static_cast<int>(left) : kRouteTokens;
-    const T* x = static_cast<const T*>(p.x);
-    const T* w = static_cast<const T*>(p.w);
-    const int H = p.h, E = p.e;
+__global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParams p) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * (kSelectThreads / 32) + warp;
+    if (t >= p.n) return;
+    const int E = p.e, H = p.h;
 
-    // zero this block's rows of the fp32 accumulator
     if (p.y_acc != nullptr) {
-        float4* yv = reinterpret_cast<float4*>(p.y_acc + t0 * H);
-        const int nv = nt * H / 4;
-        for (int i = tid; i < nv; i += kRouteThreads) yv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        float4* yv = reinterpret_cast<float4*>(p.y_acc + t * H);
+        for (int i = lane; i < H / 4; i += 32) yv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
 
-    if (!p.prerouted) {
-        // ---- logits: thread (tg, eg) owns tokens {2tg, 2tg+1} x experts {eg + 16j} ----
-        const int eg = tid & 15;
-        const int tg = tid >> 4;
-        for (int ec = 0; ec < E; ec += kRouteExperts) {
-            float acc[2][4];
-#pragma unroll
-            for (int i = 0; i < 2; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-            for (int kc = 0; kc < H; kc += kRouteK) {
-                const int kw = min(kRouteK, H - kc);
-                __syncthreads();
-                for (int i = tid; i < kRouteTokens * kRouteK; i += kRouteThreads) {
-                    const int r = i / kRouteK, c = i % kRouteK;
-                    float v = 0.0f;
-                    if (r < nt && c < kw) v = to_f32<T>(x[(t0 + r) * H + kc + c]);
-                    xs[r * kRoutePad + c] = v;
-                }
-                for (int i = tid; i < kRouteExperts * kRouteK; i += kRouteThreads) {
-                    const int r = i / kRouteK, c = i % kRouteK;
-                    float v = 0.0f;
-                    if (ec + r < E && c < kw) v = to_f32<T>(w[static_cast<int64_t>(ec + r) * H + kc + c]);
-                    ws[r * kRoutePad + c] = v;
-                }
-                __syncthreads();
-                const float* x0 = xs + (2 * tg) * kRoutePad;
-                const float* x1 = x0 + kRoutePad;
-                for (int c = 0; c < kw; c += 4) {
-                    const float4 a0 = *reinterpret_cast<const float4*>(x0 + c);
-                    const float4 a1 = *reinterpret_cast<const float4*>(x1 + c);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float4 b = *reinterpret_cast<const float4*>(ws + (eg + 16 * j) * kRoutePad + c);
-                        // sequential in h: c, c+1, c+2, c+3 (zero padding past kw adds exact zeros)
-                        acc[0][j] = fmaf(a0.x, b.x, acc[0][j]);
-                        acc[0][j] = fmaf(a0.y, b.y, acc[0][j]);
-                        acc[0][j] = fmaf(a0.z, b.z, acc[0][j]);
-                        acc[0][j] = fmaf(a0.w, b.w, acc[0][j]);
-                        acc[1][j] = fmaf(a1.x, b.x, acc[1][j]);
-                        acc[1][j] = fmaf(a1.y, b.y, acc[1][j]);
-                        acc[1][j] = fmaf(a1.z, b.z, acc[1][j]);
-                        acc[1][j] = fmaf(a1.w, b.w, acc[1][j]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < 2; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int e = ec + eg + 16 * j;
-                    if (e < E) {
-                        float v = acc[i][j];
-                        if (p.bias) v = v + p.bias[e];
-                        lg[(2 * tg + i) * E + e] = v;
-                    }
-                }
-        }
-    }
-    __syncthreads();
-
-    // ---- per token: softmax, top-k, blend coefficients (one warp per token) ----
-    const int warp = tid >> 5, lane = tid & 31;
-    const int per_lane = (E + 31) / 32;
-    for (int r = warp; r < nt; r += kRouteThreads / 32) {
-        const int64_t t = t0 + r;
-        if (p.prerouted) {
-            // weights and indices come from an earlier routing call
-            float shared_extra = 0.0f;
-            for (int j = 0; j < p.k; ++j) {
-                const int e = p.topk_idx[t * p.k + j];
-                const float wt = p.topk_w[t * p.k + j];
-                const float a = expert_avail<T>(p, e);
-                shared_extra += wt * (1.0f - a);
-                if (lane == 0) {
-                    p.sel_coef[t * p.k + j] = wt * a;
-                    p.pos[t * p.k + j] = a > 0.0f ? atomicAdd(&p.grp_count[e], 1) : -1;
-                }
-            }
-            if (lane == 0 && p.num_shared > 0)
-                p.shared_coef[t] = (1.0f + shared_extra) / static_cast<float>(p.num_shared);
-            continue;
-        }
-        float v[kMaxExperts / 32];
-        float m = -INFINITY;
-#pragma unroll
-        for (int q = 0; q < kMaxExperts / 32; ++q) {
-            const int e = lane + 32 * q;
-            v[q] = (q < per_lane && e < E) ? lg[r * E + e] : -INFINITY;
-            m = fmaxf(m, v[q]);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float s = 0.0f;
-        float ex[kMaxExperts / 32];
-#pragma unroll
-        for (int q = 0; q < kMaxExperts / 32; ++q) {
-            const int e = lane + 32 * q;
-            ex[q] = (q < per_lane && e < E) ? __expf(v[q] - m) : 0.0f;
-            s += ex[q];
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        const float inv = 1.0f / s;
-        if (p.probs) {
-            T* pr = static_cast<T*>(p.probs);
-#pragma unroll
-            for (int q = 0; q < kMaxExperts / 32; ++q) {
-                const int e = lane + 32 * q;
-                if (q < per_lane && e < E) pr[t * E + e] = from_f32<T>(ex[q] * inv);
-            }
-        }
-        // top-k by (logit desc, index asc)
-        unsigned taken = 0u;  // bit q: v[q] already chosen
-        float wsel[kMaxTopK];
-        int isel[kMaxTopK];
-        float wsum = 0.0f;
-        for (int j = 0; j < p.k; ++j) {
-            float bv = -INFINITY;
-            int bi = 0x7fffffff;
-#pragma unroll
-            for (int q = 0; q < kMaxExperts / 32; ++q) {
-                const int e = lane + 32 * q;
-                if (q < per_lane && e < E && !((taken >> q) & 1u)) {
-                    if (v[q] > bv || (v[q] == bv && e < bi)) {
-                        bv = v[q];
-                        bi = e;
-                    }
-                }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) {
-                    bv = ov;
-                    bi = oi;
-                }
-            }
-            if (bi >= E) {
-                // no finite candidate (NaN logits): take the lowest unchosen index so
-                // every access stays in bounds; routing of NaN rows is unspecified
-                int lo = 0x7fffffff;
-#pragma unroll
-                for (int q = 0; q < kMaxExperts / 32; ++q) {
-                    const int e = lane + 32 * q;
-                    if (q < per_lane && e < E && !((taken >> q) & 1u)) lo = min(lo, e);
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-                bi = lo;
-            }
-            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-            // probability of the chosen expert, broadcast from its owner lane
-            float pe = 0.0f;
-#pragma unroll
-            for (int q = 0; q < kMaxExperts / 32; ++q)
-                if ((bi >> 5) == q) pe = ex[q] * inv;
-            pe = __shfl_sync(0xffffffffu, pe, bi & 31);
-            wsel[j] = pe;
-            isel[j] = bi;
-            wsum += pe;
-        }
-        if (p.norm_topk) {
-            const float d = wsum + 1e-20f;
-            for (int j = 0; j < p.k; ++j) wsel[j] = wsel[j] / d;
-        }
+    if (p.prerouted) {
+        // weights and indices come from an earlier routing call
         float shared_extra = 0.0f;
         for (int j = 0; j < p.k; ++j) {
-            const int e = isel[j];
-            const float a = expert_avail<T>(p, e);
-            shared_extra += wsel[j] * (1.0f - a);
-            if (lane == j % 32) {
-                p.topk_idx[t * p.k + j] = e;
-                p.topk_w[t * p.k + j] = wsel[j];
-                p.sel_coef[t * p.k + j] = wsel[j] * a;
+            const int e = p.topk_idx[t * p.k + j];
+            const float wt = p.topk_w[t * p.k + j];
+            const float a = expert_avail(p, e);
+            shared_extra += wt * (1.0f - a);
+            if (lane == 0) {
+                p.sel_coef[t * p.k + j] = wt * a;
                 p.pos[t * p.k + j] = a > 0.0f ? atomicAdd(&p.grp_count[e], 1) : -1;
-                if (p.counts_all) atomicAdd(&p.counts_all[e], 1);
-                if (p.mass_all) atomicAdd(&p.mass_all[e], wsel[j]);
             }
         }
         if (lane == 0 && p.num_shared > 0)
             p.shared_coef[t] = (1.0f + shared_extra) / static_cast<float>(p.num_shared);
+        return;
     }
-}
 
-inline size_t route_smem_bytes(int num_experts) {
-    return sizeof(float) * (static_cast<size_t>(kRouteTokens) * kRoutePad +
-                            static_cast<size_t>(kRouteExperts) * kRoutePad +
-                            static_cast<size_t>(kRouteTokens) * num_experts);
+    const int per_lane = (E + 31) / 32;
+    const int C = p.nchunks;
+    float v[kMaxExperts / 32];
+    float m = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < kMaxExperts / 32; ++q) {
+        const int e = lane + 32 * q;
+        float lg = -INFINITY;
+        if (q < per_lane && e < E) {
+            const float* pp = p.partials + (t * E + e) * C;
+            float s = 0.0f;
+            for (int c = 0; c < C; ++c) s = s + pp[c];
+            if (p.bias) s = s + p.bias[e];
+            lg = s;
+        }
+        v[q] = lg;
+        m = fmaxf(m, lg);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.0f;
+    float ex[kMaxExperts / 32];
+#pragma unroll
+    for (int q = 0; q < kMaxExperts / 32; ++q) {
+        const int e = lane + 32 * q;
+        ex[q] = (q < per_lane && e < E) ? __expf(v[q] - m) : 0.0f;
+        s += ex[q];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float inv = 1.0f / s;
+    if (p.probs) {
+        T* pr = static_cast<T*>(p.probs);
+#pragma unroll
+        for (int q = 0; q < kMaxExperts / 32; ++q) {
+            const int e = lane + 32 * q;
+            if (q < per_lane && e < E) pr[t * E + e] = from_f32<T>(ex[q] * inv);
+        }
+    }
+    // top-k by (logit desc, index asc)
+    unsigned taken = 0u;  // bit q: v[q] already chosen
+    float wsel[kMaxTopK];
+    int isel[kMaxTopK];
+    float wsum = 0.0f;
+    for (int j = 0; j < p.k; ++j) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int q = 0; q < kMaxExperts / 32; ++q) {
+            const int e = lane + 32 * q;
+            if (q < per_lane && e < E && !((taken >> q) & 1u)) {
+                if (v[q] > bv || (v[q] == bv && e < bi)) {
+                    bv = v[q];
+                    bi = e;
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (bi >= E) {
+            // no finite candidate (NaN logits): take the lowest unchosen index so
+            // every access stays in bounds; routing of NaN rows is unspecified
+            int lo = 0x7fffffff;
+#pragma unroll
+            for (int q = 0; q < kMaxExperts / 32; ++q) {
+                const int e = lane + 32 * q;
+                if (q < per_lane && e < E && !((taken >> q) & 1u)) lo = min(lo, e);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+            bi = lo;
+        }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        // probability of the chosen expert, broadcast from its owner lane
+        float pe = 0.0f;
+#pragma unroll
+        for (int q = 0; q < kMaxExperts / 32; ++q)
+            if ((bi >> 5) == q) pe = ex[q] * inv;
+        pe = __shfl_sync(0xffffffffu, pe, bi & 31);
+        wsel[j] = pe;
+        isel[j] = bi;
+        wsum += pe;
+    }
+    if (p.norm_topk) {
+        const float d = wsum + 1e-20f;
+        for (int j = 0; j < p.k; ++j) wsel[j] = wsel[j] / d;
+    }
+    float shared_extra = 0.0f;
+    for (int j = 0; j < p.k; ++j) {
+        const int e = isel[j];
+        const float a = expert_avail(p, e);
+        shared_extra += wsel[j] * (1.0f - a);
+        if (lane == j % 32) {
+            p.topk_idx[t * p.k + j] = e;
+            p.topk_w[t * p.k + j] = wsel[j];
+            p.sel_coef[t * p.k + j] = wsel[j] * a;
+            p.pos[t * p.k + j] = a > 0.0f ? atomicAdd(&p.grp_count[e], 1) : -1;
+            if (p.counts_all) atomicAdd(&p.counts_all[e], 1);
+            if (p.mass_all) atomicAdd(&p.mass_all[e], wsel[j]);
+        }
+    }
+    if (lane == 0 && p.num_shared > 0)
+        p.shared_coef[t] = (1.0f + shared_extra) / static_cast<float>(p.num_shared);
 }
 
 }  // namespace chronos

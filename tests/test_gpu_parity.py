@@ -117,6 +117,27 @@ def test_simt_and_odd_shapes(h, e, k, f, s):
         assert O.rel_l2(y, ref) <= tol
 
 
+@pytest.mark.parametrize("n,h,e", [(256, 2048, 64), (257, 2048, 64), (300, 100, 256),
+                                   (1000, 260, 40), (5, 100, 256)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_router_both_logit_kernels_bit_exact(n, h, e, dtype):
+    # <= 256 tokens: chunk-partials kernel; larger: register-tiled kernel; odd H
+    # and E exercise the ragged chunk / tile edges
+    ops = _ops()
+    g = torch.Generator(device=DEV)
+    g.manual_seed(n + h + e)
+    x = torch.randn(n, h, generator=g, device=DEV).to(dtype)
+    w = (torch.randn(e, h, generator=g, device=DEV) * 0.02).to(dtype)
+    k = min(8, e)
+    r = ops.moe_route(x, w, k, True)
+    torch.cuda.synchronize()
+    o_idx, o_w, o_probs, _ = O.route(_np(x), _np(w), k, True)
+    assert np.array_equal(r["topk_idx"].cpu().numpy(), o_idx)
+    np.testing.assert_allclose(r["topk_weight"].cpu().numpy(), o_w, rtol=1e-5, atol=1e-6)
+    counts = r["counts"].cpu().numpy()
+    assert np.array_equal(counts, np.bincount(o_idx.ravel(), minlength=e))
+
+
 def test_empty_input():
     wl = _workload(128, 8, 2, 128, 1, 0)
     out = _run(wl, 2, True)

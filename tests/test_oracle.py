@@ -47,17 +47,30 @@ def test_oracle_rank_order_and_ties():
     np.testing.assert_allclose(wt.sum(1), 1.0, rtol=1e-6)
 
 
-def test_oracle_logits_are_a_sequential_fma_chain():
+def test_oracle_logits_are_in_order_sums_of_chunk_fma_chains():
+    # routing contract: partial = fmaf chain over each 128-wide chunk of h,
+    # logit = in-order fp32 sum of the partials starting from 0
+    import math
     rng = np.random.default_rng(0)
-    x = rng.standard_normal((4, 33)).astype(np.float32)
-    w = rng.standard_normal((3, 33)).astype(np.float32)
+    h = 300
+    x = rng.standard_normal((4, h)).astype(np.float32)
+    w = rng.standard_normal((3, h)).astype(np.float32)
     _, _, _, logits = O.route(x, w, 1, norm_topk=False)
+
+    def fma32(a, b, c):
+        # exact fp32 product in double, correctly rounded sum, then fp32; this
+        # double rounding differs from fmaf only on rare halfway cases (none here)
+        return np.float32(math.fsum([float(a) * float(b), float(c)]))
+
     for t in range(4):
         for e in range(3):
-            acc = np.float32(0.0)
-            for h in range(33):
-                acc = np.float32(np.float64(x[t, h]) * np.float64(w[e, h]) + np.float64(acc))
-            assert logits[t, e] == acc
+            total = np.float32(0.0)
+            for c0 in range(0, h, 128):
+                acc = np.float32(0.0)
+                for i in range(c0, min(h, c0 + 128)):
+                    acc = fma32(x[t, i], w[e, i], acc)
+                total = np.float32(total + acc)
+            assert logits[t, e] == total
 
 
 def test_bf16_rounding_helper():
