@@ -50,6 +50,7 @@ int fail(int code, const char* fmt, ...) {
     } while (0)
 
 constexpr int kSplitMaxTokens = 64;  // decode batches up to this size may split K
+constexpr int kDownWideMinTokens = 1024;  // batches from this size use 256-token down tiles
 
 std::atomic<uint64_t> g_kernel_launches{0};
 
@@ -307,8 +308,9 @@ int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool p
     rp.nchunks = small ? route_chunks(s.hidden) : 1;
     if (!prerouted) {
         if (small) {
-            const int64_t threads = (N + kRouteGroup - 1) / kRouteGroup * s.num_experts * rp.nchunks;
-            const unsigned grid = static_cast<unsigned>((threads + kPartialThreads - 1) / kPartialThreads);
+            const dim3 grid(static_cast<unsigned>((N + kRouteGroup - 1) / kRouteGroup),
+                            static_cast<unsigned>(rp.nchunks),
+                            static_cast<unsigned>((s.num_experts + kPartialThreads - 1) / kPartialThreads));
             route_partials_kernel<T><<<grid, kPartialThreads, 0, st>>>(rp);
         } else {
             const dim3 grid(static_cast<unsigned>((N + kRouteTile - 1) / kRouteTile),
@@ -338,7 +340,7 @@ int launch_tc(const CUtensorMap& a0r, const CUtensorMap& a1r, const CUtensorMap&
     return CHRONOS_OK;
 }
 
-template <typename T, int BN>
+template <typename T, int BN, int BN_DN>
 int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int splits_gu,
                    int splits_dn, int kt_per_split_gu, int kt_per_split_dn, int slot) {
     const ChronosMoeShape& s = a->shape;
@@ -362,7 +364,7 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     }
     if ((rc = make_map(&xp_m, w.ws + w.L->xp, N * K, H, BN, dt))) return rc;
     if ((rc = make_map(&x_m, a->x, N, H, BN, dt))) return rc;
-    if ((rc = make_map(&h_m, w.ws + w.L->hid, slots, F, BN, dt))) return rc;
+    if ((rc = make_map(&h_m, w.ws + w.L->hid, slots, F, BN_DN, dt))) return rc;
 
     TcGemmParams p{};
     p.hdr = w.at<PlanHeader>(w.L->hdr);
@@ -437,7 +439,8 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     pd.m_tiles = static_cast<int>((H + kTcBM - 1) / kTcBM);
     pd.w_rows = static_cast<int>(H);
     pd.out_cols = static_cast<int>(H);
-    if ((rc = launch_tc<T, BN, false, false>(d_r, d_r, d_s, d_s, h_m, h_m, pd, grid, st))) return rc;
+    if ((rc = launch_tc<T, BN_DN, false, false>(d_r, d_r, d_s, d_s, h_m, h_m, pd, grid, st)))
+        return rc;
     prof_ran(slot, CHRONOS_STAGE_DOWN);
     return CHRONOS_OK;
 }
@@ -543,7 +546,10 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
                                            aligned16(a->w_shared_down)));
     int bn = 128;
     if (tc) bn = N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128;
+    // large batches: 256-token tiles for the down GEMM (half the operand traffic per FLOP)
+    const int bn_dn = (tc && N >= kDownWideMinTokens) ? 256 : bn;
     const int tok_tile = tc ? bn : kSimtTile;
+    const int tok_tile_dn = tc ? bn_dn : kSimtTile;
     const int mt_gu = tc ? (s.ffn + kTcBM - 1) / kTcBM : (s.ffn + kSimtTile - 1) / kSimtTile;
     const int mt_dn = tc ? (s.hidden + kTcBM - 1) / kTcBM : (s.hidden + kSimtTile - 1) / kSimtTile;
 
@@ -562,7 +568,7 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     if (tc) {
         const int kt_total = s.ffn / kTcBK;
         const int64_t groups_est = std::min<int64_t>(s.num_experts, N * s.top_k) + s.num_shared;
-        const int64_t tiles_est = groups_est * ((N + bn - 1) / bn);
+        const int64_t tiles_est = groups_est * ((N + bn_dn - 1) / bn_dn);
         const int target = 2 * sm_count();
         while (tiles_est * mt_dn * splits_dn < target && splits_dn * 2 * 4 <= kt_total)
             splits_dn *= 2;
@@ -590,6 +596,7 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     pp.k = s.top_k;
     pp.num_shared = s.num_shared;
     pp.tok_tile = tok_tile;
+    pp.tok_tile_dn = tok_tile_dn;
     pp.mt_gu = mt_gu;
     pp.mt_dn = mt_dn;
     pp.splits_gu = splits_gu;
@@ -605,10 +612,7 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     pp.act_eid = w.at<int32_t>(L.act_eid);
     pp.ustart_gu = w.at<int32_t>(L.ustart_gu);
     pp.ustart_dn = w.at<int32_t>(L.ustart_dn);
-    plan_kernel<<<1, kPlanThreads, 0, st>>>(pp);
-    count_launch();
-    CHRONOS_CUDA_CHECK(cudaGetLastError());
-    prof_ran(slot, CHRONOS_STAGE_PLAN);
+    // the plan is computed inside the scatter launch (stage "plan" stays empty)
     prof_mark(slot, CHRONOS_STAGE_SCATTER, st);
 
     ScatterParams sp{};
@@ -628,8 +632,9 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     sp.copy_rows = tc ? 1 : 0;
     {
         const int64_t warps = N * s.top_k;
-        const unsigned blocks = static_cast<unsigned>((warps * 32 + kScatterThreads - 1) / kScatterThreads);
-        scatter_kernel<T><<<blocks, kScatterThreads, 0, st>>>(sp);
+        const unsigned blocks =
+            static_cast<unsigned>(std::max<int64_t>(1, (warps + kScatterWarps - 1) / kScatterWarps));
+        plan_scatter_kernel<T><<<blocks, kScatterThreads, 0, st>>>(pp, sp);
         count_launch();
         CHRONOS_CUDA_CHECK(cudaGetLastError());
     }
@@ -640,10 +645,14 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
             return fail(CHRONOS_ERR_INVALID_ARG, "internal: fp32 on the tensor-core path");
         } else {
             switch (bn) {
-                case 16: rc = launch_tc_pair<T, 16>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot); break;
-                case 32: rc = launch_tc_pair<T, 32>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot); break;
-                case 64: rc = launch_tc_pair<T, 64>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot); break;
-                default: rc = launch_tc_pair<T, 128>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot); break;
+                case 16: rc = launch_tc_pair<T, 16, 16>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot); break;
+                case 32: rc = launch_tc_pair<T, 32, 32>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot); break;
+                case 64: rc = launch_tc_pair<T, 64, 64>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot); break;
+                default:
+                    rc = bn_dn == 256
+                             ? launch_tc_pair<T, 128, 256>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot)
+                             : launch_tc_pair<T, 128, 128>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot);
+                    break;
             }
         }
     } else {

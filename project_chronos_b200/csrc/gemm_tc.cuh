@@ -72,8 +72,10 @@ __host__ __device__ constexpr int tc_stage_bytes(int bn, bool gateup) {
 __host__ __device__ constexpr int tc_stage_row_bytes(bool gateup, bool split) {
     return gateup ? (split ? 2 * kTcBM * 4 : kTcBM * 2) : kTcBM * 4;
 }
+// Rows staged at a time (a 256-token tile is drained in two halves).
+__host__ __device__ constexpr int tc_staging_rows(int bn) { return bn < 128 ? bn : 128; }
 __host__ __device__ constexpr int tc_staging_bytes(int bn, bool gateup, bool split) {
-    return bn * tc_stage_row_bytes(gateup, split);
+    return tc_staging_rows(bn) * tc_stage_row_bytes(gateup, split);
 }
 __host__ __device__ constexpr int tc_stages(int bn, bool gateup, bool split) {
     return (220 * 1024 - tc_staging_bytes(bn, gateup, split)) / tc_stage_bytes(bn, gateup) > 8
@@ -142,8 +144,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ uint8_t tc_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint8_t* staging = smem + STAGES * STAGE_BYTES;  // [BN][ROW_BYTES]
-    uint64_t* full = reinterpret_cast<uint64_t*>(staging + BN * ROW_BYTES);
+    uint8_t* staging = smem + STAGES * STAGE_BYTES;  // [tc_staging_rows(BN)][ROW_BYTES]
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + tc_staging_rows(BN) * ROW_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -306,62 +308,77 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int rows = p.act_rows[w.a];
             const int tok0 = w.tok_tile * BN;
             const int64_t hrow0 = p.act_hrow[w.a];
+            const int ncols = min(kTcBM, p.out_cols - m0);
+            constexpr int SUB = tc_staging_rows(BN);
 #pragma unroll 1
-            for (int c = 0; c < BN; c += 16) {
-                float g[16];
-                tmem_ld16(taddr + c, g);
-                if constexpr (GATEUP) {
-                    float uu[16];
-                    tmem_ld16(taddr + BN + c, uu);
-                    tmem_wait_ld();
+            for (int c0 = 0; c0 < BN; c0 += SUB) {
+                if (c0 > 0) {
+                    // the staging rows are reused for the next SUB tokens of the tile
+                    bulk_wait_read();
+                    epilogue_bar_sync(128);
+                }
+#pragma unroll 1
+                for (int c = c0; c < c0 + SUB; c += 16) {
+                    float g[16];
+                    tmem_ld16(taddr + c, g);
+                    if constexpr (GATEUP) {
+                        float uu[16];
+                        tmem_ld16(taddr + BN + c, uu);
+                        tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        uint8_t* row = staging + (c + j) * ROW_BYTES;
-                        if constexpr (SPLIT) {
-                            reinterpret_cast<float*>(row)[row_in_tile] = g[j];
-                            reinterpret_cast<float*>(row)[kTcBM + row_in_tile] = uu[j];
-                        } else {
-                            reinterpret_cast<T*>(row)[row_in_tile] = from_f32<T>(silu_f32(g[j]) * uu[j]);
+                        for (int j = 0; j < 16; ++j) {
+                            uint8_t* row = staging + (c - c0 + j) * ROW_BYTES;
+                            if constexpr (SPLIT) {
+                                reinterpret_cast<float*>(row)[row_in_tile] = g[j];
+                                reinterpret_cast<float*>(row)[kTcBM + row_in_tile] = uu[j];
+                            } else {
+                                reinterpret_cast<T*>(row)[row_in_tile] =
+                                    from_f32<T>(silu_f32(g[j]) * uu[j]);
+                            }
+                        }
+                    } else {
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int tok = tok0 + c + j;
+                            const float coef = tok < rows ? p.slot_coef[hrow0 + tok] : 0.0f;
+                            reinterpret_cast<float*>(staging + (c - c0 + j) * ROW_BYTES)[row_in_tile] =
+                                coef * g[j];
                         }
                     }
-                } else {
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int tok = tok0 + c + j;
-                        const float coef = tok < rows ? p.slot_coef[hrow0 + tok] : 0.0f;
-                        reinterpret_cast<float*>(staging + (c + j) * ROW_BYTES)[row_in_tile] = coef * g[j];
-                    }
                 }
-            }
-            // accumulator drained: hand the TMEM buffer back to the MMA warp
-            tc_fence_before();
-            mbar_arrive(&tempty[acc]);
-            if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
-            // staging rows complete -> per-token bulk copies
-            fence_proxy_async_smem();
-            epilogue_bar_sync(128);
-            const int ncols = min(kTcBM, p.out_cols - m0);
-            for (int r = et; r < BN; r += 128) {
-                const int tok = tok0 + r;
-                if (tok >= rows) continue;
-                const int64_t slot = hrow0 + tok;
-                const uint8_t* row = staging + r * ROW_BYTES;
-                if constexpr (GATEUP) {
-                    if constexpr (SPLIT) {
-                        float* dst = p.gu + slot * 2 * p.f + m0;
-                        bulk_reduce_add_f32(dst, row, static_cast<uint32_t>(ncols * 4));
-                        bulk_reduce_add_f32(dst + p.f, row + kTcBM * 4, static_cast<uint32_t>(ncols * 4));
+                if (c0 + SUB >= BN) {
+                    // accumulator drained: hand the TMEM buffer back to the MMA warp
+                    tc_fence_before();
+                    mbar_arrive(&tempty[acc]);
+                }
+                // staging rows complete -> per-token bulk copies
+                fence_proxy_async_smem();
+                epilogue_bar_sync(128);
+                for (int r = et; r < SUB; r += 128) {
+                    const int tok = tok0 + c0 + r;
+                    if (tok >= rows) continue;
+                    const int64_t slot = hrow0 + tok;
+                    const uint8_t* row = staging + r * ROW_BYTES;
+                    if constexpr (GATEUP) {
+                        if constexpr (SPLIT) {
+                            float* dst = p.gu + slot * 2 * p.f + m0;
+                            bulk_reduce_add_f32(dst, row, static_cast<uint32_t>(ncols * 4));
+                            bulk_reduce_add_f32(dst + p.f, row + kTcBM * 4,
+                                                static_cast<uint32_t>(ncols * 4));
+                        } else {
+                            bulk_store(static_cast<T*>(p.hid) + slot * p.f + m0, row,
+                                       static_cast<uint32_t>(ncols * sizeof(T)));
+                        }
                     } else {
-                        bulk_store(static_cast<T*>(p.hid) + slot * p.f + m0, row,
-                                   static_cast<uint32_t>(ncols * sizeof(T)));
+                        const int64_t t = p.slot_tok[slot];
+                        bulk_reduce_add_f32(p.y_acc + t * p.h + m0, row,
+                                            static_cast<uint32_t>(ncols * 4));
                     }
-                } else {
-                    const int64_t t = p.slot_tok[slot];
-                    bulk_reduce_add_f32(p.y_acc + t * p.h + m0, row, static_cast<uint32_t>(ncols * 4));
                 }
+                bulk_commit();
             }
-            bulk_commit();
+            if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         }
         bulk_wait_all();
     }

@@ -30,7 +30,8 @@ struct PlanHeader {
 struct PlanParams {
     int64_t n;
     int e, k, num_shared;
-    int tok_tile;                 // token rows per GEMM tile
+    int tok_tile;                 // token rows per gate/up GEMM tile
+    int tok_tile_dn;              // token rows per down GEMM tile
     int mt_gu, mt_dn;             // weight-row tiles per group (gate/up, down)
     int splits_gu, splits_dn;     // K splits per tile
     const int32_t* grp_count;     // [E]
@@ -75,19 +76,19 @@ __device__ __forceinline__ int block_inclusive_scan(int v, int* scratch) {
     return v;
 }
 
-__global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
-    __shared__ int s_scratch[kPlanThreads / 32];
-    __shared__ int s_tot[4];
+// The plan tables (active groups, unit prefixes, header); called by one block.
+// `cnt` / `inc_cnt`: this thread's expert group size and its inclusive scan.
+__device__ __forceinline__ void plan_tables(const PlanParams& p, int cnt, int inc_cnt, int* s_scratch,
+                                            int* s_tot) {
     const int tid = threadIdx.x;
     const int E = p.e;
     const int S = p.num_shared;
     const int N = static_cast<int>(p.n);
-    const int cnt = tid < E ? p.grp_count[tid] : 0;
     const int is_act = (tid < E && cnt > 0) ? 1 : 0;
     const int tt = (cnt + p.tok_tile - 1) / p.tok_tile;
+    const int tt_dn = (cnt + p.tok_tile_dn - 1) / p.tok_tile_dn;
     const int ugu = is_act ? tt * p.mt_gu * p.splits_gu : 0;
-    const int udn = is_act ? tt * p.mt_dn * p.splits_dn : 0;
-    const int inc_cnt = block_inclusive_scan(cnt, s_scratch);
+    const int udn = is_act ? tt_dn * p.mt_dn * p.splits_dn : 0;
     const int inc_act = block_inclusive_scan(is_act, s_scratch);
     const int inc_gu = block_inclusive_scan(ugu, s_scratch);
     const int inc_dn = block_inclusive_scan(udn, s_scratch);
@@ -100,8 +101,9 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
     __syncthreads();
     // shared groups first (the largest: N rows each), then routed groups in expert order
     const int tt_sh = (N + p.tok_tile - 1) / p.tok_tile;
+    const int tt_sh_dn = (N + p.tok_tile_dn - 1) / p.tok_tile_dn;
     const int sh_gu = tt_sh * p.mt_gu * p.splits_gu;
-    const int sh_dn = tt_sh * p.mt_dn * p.splits_dn;
+    const int sh_dn = tt_sh_dn * p.mt_dn * p.splits_dn;
     if (tid < E) {
         const int off = inc_cnt - cnt;
         p.grp_off[tid] = off;
@@ -154,14 +156,29 @@ struct ScatterParams {
     int copy_rows;        // 0: only the slot tables (B operand read from x by row index)
 };
 
-constexpr int kScatterThreads = 256;
+constexpr int kScatterThreads = kPlanThreads;
+constexpr int kScatterWarps = kScatterThreads / 32;
 
-// One warp per (token, choice); the shared-slot tables are filled by the
-// warps with choice index 0.
+// Plan + permutation in one launch.  Every block scans the E group sizes
+// itself (E <= 256 values) to get the group offsets; block 0 also writes the
+// plan tables the GEMMs walk.  Then one warp per (token, choice) writes the
+// slot tables and copies the x row into expert order (all of a lane's 16-byte
+// loads issued before its stores).  Warps with choice index 0 also fill the
+// shared experts' slot tables.
 template <typename T>
-__global__ void __launch_bounds__(kScatterThreads) scatter_kernel(ScatterParams p) {
-    const int64_t gw = (static_cast<int64_t>(blockIdx.x) * kScatterThreads + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(kScatterThreads) plan_scatter_kernel(PlanParams pp, ScatterParams p) {
+    __shared__ int s_scratch[kPlanThreads / 32];
+    __shared__ int s_tot[4];
+    __shared__ int s_off[kPlanThreads];
+    const int tid = threadIdx.x;
+    const int cnt = tid < pp.e ? pp.grp_count[tid] : 0;
+    const int inc_cnt = block_inclusive_scan(cnt, s_scratch);
+    s_off[tid] = inc_cnt - cnt;
+    if (blockIdx.x == 0) plan_tables(pp, cnt, inc_cnt, s_scratch, s_tot);
+    __syncthreads();
+
+    const int64_t gw = static_cast<int64_t>(blockIdx.x) * kScatterWarps + (tid >> 5);
+    const int lane = tid & 31;
     const int64_t total = p.n * p.k;
     if (gw >= total) return;
     const int64_t t = gw / p.k;
@@ -174,7 +191,7 @@ __global__ void __launch_bounds__(kScatterThreads) scatter_kernel(ScatterParams 
     const int ps = p.pos[gw];
     if (ps < 0) return;
     const int e = p.topk_idx[gw];
-    const int64_t slot = static_cast<int64_t>(p.grp_off[e]) + ps;
+    const int64_t slot = static_cast<int64_t>(s_off[e]) + ps;
     if (lane == 0) {
         p.slot_tok[slot] = static_cast<int32_t>(t);
         p.slot_coef[slot] = p.sel_coef[gw];
@@ -186,7 +203,16 @@ __global__ void __launch_bounds__(kScatterThreads) scatter_kernel(ScatterParams 
     if ((bytes & 15) == 0) {
         const uint4* s4 = reinterpret_cast<const uint4*>(src);
         uint4* d4 = reinterpret_cast<uint4*>(dst);
-        for (int i = lane; i < bytes / 16; i += 32) d4[i] = s4[i];
+        const int n16 = bytes / 16;
+        int i = lane;
+        for (; i + 32 * 7 < n16; i += 32 * 8) {
+            uint4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = s4[i + 32 * u];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) d4[i + 32 * u] = v[u];
+        }
+        for (; i < n16; i += 32) d4[i] = s4[i];
     } else {
         for (int i = lane; i < p.h; i += 32) dst[i] = src[i];
     }

@@ -82,40 +82,59 @@ __device__ __forceinline__ float4 load4<__half>(const __half* p) {
 // ---------------------------------------------------------------------------
 // small batches: chunk partials
 // ---------------------------------------------------------------------------
-constexpr int kPartialThreads = 128;
+constexpr int kPartialThreads = 128;  // experts per block (one thread each)
 
+// Block (token group g, chunk c, expert block eb): the group's x chunk
+// [8 tokens x 128 h] is staged in shared memory as fp32; every thread keeps
+// its expert's 128-element weight chunk in registers (all loads issued up
+// front, one memory latency), then runs the 8 chunk chains.
 template <typename T>
 __global__ void __launch_bounds__(kPartialThreads) route_partials_kernel(RouteParams p) {
+    __shared__ __align__(16) float xs[kRouteGroup][kRouteChunk];
     const int E = p.e, C = p.nchunks, H = p.h;
-    const int64_t groups = (p.n + kRouteGroup - 1) / kRouteGroup;
-    const int64_t gid = static_cast<int64_t>(blockIdx.x) * kPartialThreads + threadIdx.x;
-    if (gid >= groups * E * C) return;
-    // consecutive threads: consecutive experts of one (token group, chunk), so
-    // the token chunks they read are the same addresses (L1 broadcast)
-    const int e = static_cast<int>(gid % E);
-    const int c = static_cast<int>((gid / E) % C);
-    const int64_t tgp = gid / (static_cast<int64_t>(E) * C);
-    const int64_t t0 = tgp * kRouteGroup;
+    const int c = blockIdx.y;
+    const int e = blockIdx.z * kPartialThreads + threadIdx.x;
+    const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kRouteGroup;
     const int64_t left = p.n - t0;
     const int nt = left < kRouteGroup ? static_cast<int>(left) : kRouteGroup;
     const int h0 = c * kRouteChunk;
-    const int h1 = min(H, h0 + kRouteChunk);
+    const int len = min(kRouteChunk, H - h0);  // multiple of 4
     const T* x = static_cast<const T*>(p.x);
-    const T* wr = static_cast<const T*>(p.w) + static_cast<int64_t>(e) * H;
+    // stage x: 8 x 128 values, 4 per thread-iteration
+    for (int i = threadIdx.x; i < kRouteGroup * (kRouteChunk / 4); i += kPartialThreads) {
+        const int r = i / (kRouteChunk / 4), q4 = (i % (kRouteChunk / 4)) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < nt && q4 < len) v = load4<T>(x + (t0 + r) * H + h0 + q4);
+        *reinterpret_cast<float4*>(&xs[r][q4]) = v;
+    }
+    // this thread's weight chunk, all loads in flight together
+    float wv[kRouteChunk];
+    const bool e_ok = e < E;
+    const T* wr = static_cast<const T*>(p.w) + static_cast<int64_t>(e_ok ? e : 0) * H + h0;
+#pragma unroll
+    for (int q = 0; q < kRouteChunk; q += 4) {
+        const float4 b = (e_ok && q < len) ? load4<T>(wr + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        wv[q] = b.x;
+        wv[q + 1] = b.y;
+        wv[q + 2] = b.z;
+        wv[q + 3] = b.w;
+    }
+    __syncthreads();
+    if (!e_ok) return;
     float acc[kRouteGroup];
 #pragma unroll
     for (int i = 0; i < kRouteGroup; ++i) acc[i] = 0.0f;
-    for (int h = h0; h < h1; h += 4) {
-        const float4 b = load4<T>(wr + h);
+    // chains over h in increasing order; elements past `len` are zero pairs and
+    // leave the sums unchanged
+#pragma unroll
+    for (int q = 0; q < kRouteChunk; q += 4) {
 #pragma unroll
         for (int i = 0; i < kRouteGroup; ++i) {
-            if (i < nt) {
-                const float4 a = load4<T>(x + (t0 + i) * H + h);
-                acc[i] = fmaf(a.x, b.x, acc[i]);
-                acc[i] = fmaf(a.y, b.y, acc[i]);
-                acc[i] = fmaf(a.z, b.z, acc[i]);
-                acc[i] = fmaf(a.w, b.w, acc[i]);
-            }
+            const float4 a = *reinterpret_cast<const float4*>(&xs[i][q]);
+            acc[i] = fmaf(a.x, wv[q], acc[i]);
+            acc[i] = fmaf(a.y, wv[q + 1], acc[i]);
+            acc[i] = fmaf(a.z, wv[q + 2], acc[i]);
+            acc[i] = fmaf(a.w, wv[q + 3], acc[i]);
         }
     }
 #pragma unroll

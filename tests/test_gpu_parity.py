@@ -85,7 +85,7 @@ def _workload(h, e, k, f, s, n, dtype=torch.bfloat16, seed=0, avail_p=None, zipf
                              zipf_s=zipf)
 
 
-@pytest.mark.parametrize("n", [1, 2, 7, 16, 33, 64, 65, 200])
+@pytest.mark.parametrize("n", [1, 2, 7, 16, 33, 64, 65, 200, 1100])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_tensor_core_path_token_counts(n, dtype):
     # covers every token-tile width (16/32/64/128), split-K decode and ragged tails
