@@ -173,7 +173,10 @@ def test_routing_is_deterministic_and_prerouted_matches():
     assert torch.equal(a["topk_weight"], b["topk_weight"])
     c = _run(wl, 6, True, topk=[a["topk_idx"], a["topk_weight"]])
     torch.cuda.synchronize()
-    assert O.rel_l2(_np(c["y"]), _np(a["y"])) < 1e-5
+    # the fp32 combine is summed in a run-dependent order (TMA reduce-adds), so
+    # a few bf16 outputs may differ by one ulp between runs: bf16-level bound
+    assert O.rel_l2(_np(c["y"]), _np(a["y"])) < 1e-3
+    assert O.rel_l2(_np(b["y"]), _np(a["y"])) < 1e-3
 
 
 def test_ready_flags_gate_selected_experts():
@@ -226,4 +229,4 @@ def test_custom_op_registration():
     ref = ops.moe_forward(wl.x, w.router, w.gate, w.up, w.down, w.sh_gate, w.sh_up, w.sh_down, 2,
                           True)
     assert torch.equal(idx, ref["topk_idx"])
-    assert O.rel_l2(_np(y), _np(ref["y"])) < 1e-5
+    assert O.rel_l2(_np(y), _np(ref["y"])) < 1e-3  # bf16, run-order-dependent combine
