@@ -1,0 +1,56 @@
+"""Run one MoE-layer workload a few times (for profilers such as ncu).
+
+    python -m project_chronos_b200.profile_case --workload prefill --calls 3
+    python -m project_chronos_b200.profile_case --workload decode --tokens 1 --calls 3
+
+Builds the named synthetic workload on cuda:0 (``synthetic.WORKLOADS``),
+calls ``ops.moe_forward`` ``--calls`` times with an L2 flush (256 MB write)
+before each call, synchronises, checks the device status word and prints the
+average device time per call.  Nothing else runs, so a kernel filter with a
+launch skip count selects a steady-state call.
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+
+import torch
+
+from . import ops, synthetic as syn
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--workload", default="prefill", choices=sorted(syn.WORKLOADS))
+    ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--calls", type=int, default=3)
+    ap.add_argument("--seed", type=int, default=0)
+    args = ap.parse_args(argv)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    wl = syn.named_workload(args.workload, tokens=args.tokens, seed=args.seed, device=dev)
+    w = wl.weights
+    s = wl.shape
+    avail = None if wl.mask is None else wl.mask.to(torch.float32)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    total_ms = 0.0
+    for _ in range(args.calls):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        ops.moe_forward(wl.x, w.router, w.gate, w.up, w.down,
+                        w.sh_gate if s.num_shared else None, w.sh_up if s.num_shared else None,
+                        w.sh_down if s.num_shared else None, s.top_k, s.norm_topk, avail=avail,
+                        router_bias=wl.bias)
+        b.record()
+        torch.cuda.synchronize()
+        total_ms += a.elapsed_time(b)
+    ops.check_status(dev)
+    print(f"{args.workload} tokens={wl.x.shape[0]} calls={args.calls} "
+          f"avg_ms={total_ms / args.calls:.4f}")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
