@@ -33,7 +33,7 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { retu
 template <>
 __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
 
-__device__ __forceinline__ float silu_f32(float v) { return v / (1.0f + __expf(-v)); }
+__device__ __forceinline__ float silu_f32(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
 // Record the first device-side failure of a call in the caller's status word.
 __device__ __forceinline__ void report_status(int32_t* status, int32_t code) {

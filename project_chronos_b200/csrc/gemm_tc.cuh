@@ -92,7 +92,7 @@ __host__ __device__ constexpr int tc_tmem_cols(int bn, bool gateup) {
 }
 __host__ __device__ constexpr int tc_smem_bytes(int bn, bool gateup, bool split) {
     return 1024 /* alignment slack */ + tc_stages(bn, gateup, split) * tc_stage_bytes(bn, gateup) +
-           tc_staging_bytes(bn, gateup, split) + 256;
+           tc_staging_bytes(bn, gateup, split) + 4 * bn * 4 /* per-unit slot tables x2 */ + 256;
 }
 
 struct TcUnit {
@@ -145,7 +145,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* staging = smem + STAGES * STAGE_BYTES;  // [tc_staging_rows(BN)][ROW_BYTES]
-    uint64_t* full = reinterpret_cast<uint64_t*>(staging + tc_staging_rows(BN) * ROW_BYTES);
+    // per-unit slot tables of the tile (coefficient, token), double-buffered by accumulator
+    float* s_coef = reinterpret_cast<float*>(staging + tc_staging_rows(BN) * ROW_BYTES);  // [2][BN]
+    int32_t* s_tok = reinterpret_cast<int32_t*>(s_coef + 2 * BN);                          // [2][BN]
+    uint64_t* full = reinterpret_cast<uint64_t*>(s_tok + 2 * BN);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -287,6 +290,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         uint32_t acc_phase = 0;
         for (int u = blockIdx.x; u < total; u += gridDim.x) {
             const TcUnit w = tc_decode(p, num_active, u, BN, splits_unused);
+            const int rows = p.act_rows[w.a];
+            const int tok0 = w.tok_tile * BN;
+            const int64_t hrow0 = p.act_hrow[w.a];
+            float* cf = s_coef + acc * BN;
+            int32_t* tk = s_tok + acc * BN;
+            if constexpr (!GATEUP) {
+                // this tile's slot coefficients and tokens, read once (the other
+                // buffer may still be read by threads finishing the previous unit)
+                for (int r = et; r < BN; r += 128) {
+                    const int tok = tok0 + r;
+                    const bool ok = tok < rows;
+                    cf[r] = ok ? p.slot_coef[hrow0 + tok] : 0.0f;
+                    tk[r] = ok ? p.slot_tok[hrow0 + tok] : 0;
+                }
+            }
             // one thread waits (bounded) for the accumulator; the barrier hands its
             // verdict to the other 127, so they all leave together on a timeout
             if (et == 0) {
@@ -305,9 +323,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * ACC_COLS);
             const int m0 = w.mtile * kTcBM;
-            const int rows = p.act_rows[w.a];
-            const int tok0 = w.tok_tile * BN;
-            const int64_t hrow0 = p.act_hrow[w.a];
             const int ncols = min(kTcBM, p.out_cols - m0);
             constexpr int SUB = tc_staging_rows(BN);
 #pragma unroll 1
@@ -340,10 +355,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         tmem_wait_ld();
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
-                            const int tok = tok0 + c + j;
-                            const float coef = tok < rows ? p.slot_coef[hrow0 + tok] : 0.0f;
                             reinterpret_cast<float*>(staging + (c - c0 + j) * ROW_BYTES)[row_in_tile] =
-                                coef * g[j];
+                                cf[c + j] * g[j];
                         }
                     }
                 }
@@ -371,7 +384,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                        static_cast<uint32_t>(ncols * sizeof(T)));
                         }
                     } else {
-                        const int64_t t = p.slot_tok[slot];
+                        const int64_t t = tk[c0 + r];
                         bulk_reduce_add_f32(p.y_acc + t * p.h + m0, row,
                                             static_cast<uint32_t>(ncols * 4));
                     }

@@ -82,59 +82,75 @@ __device__ __forceinline__ float4 load4<__half>(const __half* p) {
 // ---------------------------------------------------------------------------
 // small batches: chunk partials
 // ---------------------------------------------------------------------------
-constexpr int kPartialThreads = 128;  // experts per block (one thread each)
+constexpr int kPartialThreads = 64;  // experts per block (one thread each)
 
 // Block (token group g, chunk c, expert block eb): the group's x chunk
-// [8 tokens x 128 h] is staged in shared memory as fp32; every thread keeps
-// its expert's 128-element weight chunk in registers (all loads issued up
-// front, one memory latency), then runs the 8 chunk chains.
+// [8 tokens x 128 h] is staged in shared memory as fp32, and the block's
+// weight chunk [64 experts x 128 h] is copied in with coalesced 16-byte loads
+// (rows padded by 16 bytes so each thread's row reads are conflict-free).
+// Then every thread runs its expert's 8 chunk chains.
 template <typename T>
 __global__ void __launch_bounds__(kPartialThreads) route_partials_kernel(RouteParams p) {
+    constexpr int ROW = kRouteChunk * static_cast<int>(sizeof(T)) + 16;  // padded row bytes
+    constexpr int V16 = kRouteChunk * static_cast<int>(sizeof(T)) / 16;  // 16-byte vectors per row
+    constexpr int EPV = 16 / static_cast<int>(sizeof(T));                // elements per vector
     __shared__ __align__(16) float xs[kRouteGroup][kRouteChunk];
+    __shared__ __align__(16) uint8_t ws[kPartialThreads * ROW];
     const int E = p.e, C = p.nchunks, H = p.h;
     const int c = blockIdx.y;
-    const int e = blockIdx.z * kPartialThreads + threadIdx.x;
+    const int e0 = blockIdx.z * kPartialThreads;
+    const int e = e0 + threadIdx.x;
     const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kRouteGroup;
     const int64_t left = p.n - t0;
     const int nt = left < kRouteGroup ? static_cast<int>(left) : kRouteGroup;
     const int h0 = c * kRouteChunk;
     const int len = min(kRouteChunk, H - h0);  // multiple of 4
     const T* x = static_cast<const T*>(p.x);
-    // stage x: 8 x 128 values, 4 per thread-iteration
+    const T* w = static_cast<const T*>(p.w);
+    // weights: row r = expert e0 + r, vector v = elements [v*EPV, v*EPV + EPV) of the chunk
+    const bool vec_ok = (H % EPV) == 0;  // 16-byte aligned rows
+    for (int i = threadIdx.x; i < kPartialThreads * V16; i += kPartialThreads) {
+        const int r = i / V16, v = i % V16;
+        const int er = e0 + r;
+        uint4 val = make_uint4(0u, 0u, 0u, 0u);
+        if (er < E) {
+            const T* src = w + static_cast<int64_t>(er) * H + h0 + v * EPV;
+            if (vec_ok && v * EPV + EPV <= len) {
+                val = *reinterpret_cast<const uint4*>(src);
+            } else {
+                T tmp[EPV];
+#pragma unroll
+                for (int u = 0; u < EPV; ++u) tmp[u] = (v * EPV + u < len) ? src[u] : from_f32<T>(0.0f);
+                val = *reinterpret_cast<const uint4*>(tmp);
+            }
+        }
+        *reinterpret_cast<uint4*>(ws + r * ROW + v * 16) = val;
+    }
+    // x chunk of the token group, as fp32
     for (int i = threadIdx.x; i < kRouteGroup * (kRouteChunk / 4); i += kPartialThreads) {
         const int r = i / (kRouteChunk / 4), q4 = (i % (kRouteChunk / 4)) * 4;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (r < nt && q4 < len) v = load4<T>(x + (t0 + r) * H + h0 + q4);
         *reinterpret_cast<float4*>(&xs[r][q4]) = v;
     }
-    // this thread's weight chunk, all loads in flight together
-    float wv[kRouteChunk];
-    const bool e_ok = e < E;
-    const T* wr = static_cast<const T*>(p.w) + static_cast<int64_t>(e_ok ? e : 0) * H + h0;
-#pragma unroll
-    for (int q = 0; q < kRouteChunk; q += 4) {
-        const float4 b = (e_ok && q < len) ? load4<T>(wr + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-        wv[q] = b.x;
-        wv[q + 1] = b.y;
-        wv[q + 2] = b.z;
-        wv[q + 3] = b.w;
-    }
     __syncthreads();
-    if (!e_ok) return;
+    if (e >= E) return;
     float acc[kRouteGroup];
 #pragma unroll
     for (int i = 0; i < kRouteGroup; ++i) acc[i] = 0.0f;
     // chains over h in increasing order; elements past `len` are zero pairs and
     // leave the sums unchanged
-#pragma unroll
+    const uint8_t* wrow = ws + threadIdx.x * ROW;
+#pragma unroll 4
     for (int q = 0; q < kRouteChunk; q += 4) {
+        const float4 b = load4<T>(reinterpret_cast<const T*>(wrow) + q);
 #pragma unroll
         for (int i = 0; i < kRouteGroup; ++i) {
             const float4 a = *reinterpret_cast<const float4*>(&xs[i][q]);
-            acc[i] = fmaf(a.x, wv[q], acc[i]);
-            acc[i] = fmaf(a.y, wv[q + 1], acc[i]);
-            acc[i] = fmaf(a.z, wv[q + 2], acc[i]);
-            acc[i] = fmaf(a.w, wv[q + 3], acc[i]);
+            acc[i] = fmaf(a.x, b.x, acc[i]);
+            acc[i] = fmaf(a.y, b.y, acc[i]);
+            acc[i] = fmaf(a.z, b.z, acc[i]);
+            acc[i] = fmaf(a.w, b.w, acc[i]);
         }
     }
 #pragma unroll
@@ -259,17 +275,24 @@ __global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParam
     }
 
     if (p.prerouted) {
-        // weights and indices come from an earlier routing call
+        // weights and indices come from an earlier routing call; lane j owns choice j
         float shared_extra = 0.0f;
+        float mine_w = 0.0f, mine_a = 0.0f;
+        int mine_e = 0;
         for (int j = 0; j < p.k; ++j) {
             const int e = p.topk_idx[t * p.k + j];
             const float wt = p.topk_w[t * p.k + j];
             const float a = expert_avail(p, e);
             shared_extra += wt * (1.0f - a);
-            if (lane == 0) {
-                p.sel_coef[t * p.k + j] = wt * a;
-                p.pos[t * p.k + j] = a > 0.0f ? atomicAdd(&p.grp_count[e], 1) : -1;
+            if (lane == j) {
+                mine_e = e;
+                mine_w = wt;
+                mine_a = a;
             }
+        }
+        if (lane < p.k) {
+            p.sel_coef[t * p.k + lane] = mine_w * mine_a;
+            p.pos[t * p.k + lane] = mine_a > 0.0f ? atomicAdd(&p.grp_count[mine_e], 1) : -1;
         }
         if (lane == 0 && p.num_shared > 0)
             p.shared_coef[t] = (1.0f + shared_extra) / static_cast<float>(p.num_shared);
@@ -287,7 +310,16 @@ __global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParam
         if (q < per_lane && e < E) {
             const float* pp = p.partials + (t * E + e) * C;
             float s = 0.0f;
-            for (int c = 0; c < C; ++c) s = s + pp[c];
+            int c = 0;
+            // loads in groups of 8 ahead of the in-order adds
+            for (; c + 8 <= C; c += 8) {
+                float r[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) r[u] = pp[c + u];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) s = s + r[u];
+            }
+            for (; c < C; ++c) s = s + pp[c];
             if (p.bias) s = s + p.bias[e];
             lg = s;
         }
@@ -370,19 +402,28 @@ __global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParam
         const float d = wsum + 1e-20f;
         for (int j = 0; j < p.k; ++j) wsel[j] = wsel[j] / d;
     }
+    // lane j < k owns choice j: its stores and returning atomic run in parallel
+    float mine_w = 0.0f, mine_a = 0.0f;
+    int mine_e = 0;
     float shared_extra = 0.0f;
     for (int j = 0; j < p.k; ++j) {
         const int e = isel[j];
         const float a = expert_avail(p, e);
         shared_extra += wsel[j] * (1.0f - a);
-        if (lane == j % 32) {
-            p.topk_idx[t * p.k + j] = e;
-            p.topk_w[t * p.k + j] = wsel[j];
-            p.sel_coef[t * p.k + j] = wsel[j] * a;
-            p.pos[t * p.k + j] = a > 0.0f ? atomicAdd(&p.grp_count[e], 1) : -1;
-            if (p.counts_all) atomicAdd(&p.counts_all[e], 1);
-            if (p.mass_all) atomicAdd(&p.mass_all[e], wsel[j]);
+        if (lane == j) {
+            mine_e = e;
+            mine_w = wsel[j];
+            mine_a = a;
         }
+    }
+    if (lane < p.k) {
+        const int64_t o = t * p.k + lane;
+        p.topk_idx[o] = mine_e;
+        p.topk_w[o] = mine_w;
+        p.sel_coef[o] = mine_w * mine_a;
+        p.pos[o] = mine_a > 0.0f ? atomicAdd(&p.grp_count[mine_e], 1) : -1;
+        if (p.counts_all) atomicAdd(&p.counts_all[mine_e], 1);
+        if (p.mass_all) atomicAdd(&p.mass_all[mine_e], mine_w);
     }
     if (lane == 0 && p.num_shared > 0)
         p.shared_coef[t] = (1.0f + shared_extra) / static_cast<float>(p.num_shared);
