@@ -61,6 +61,16 @@ struct TcGemmParams {
     int32_t ready_epoch;
     uint64_t ready_limit_ns;
     int32_t* status;
+    // Fused tails (decode batches; zeroed counters, null to disable):
+    //   tile_done  GATEUP+SPLIT: arrivals per (group, token tile, weight tile); the
+    //              last of the `splits` K-slices computes h = silu(G) * U for the tile
+    //   ntile_done DOWN: arrivals per output-column tile; the last unit converts that
+    //              column block of y_acc into y for all n_tokens rows
+    int splits;
+    int32_t* tile_done;
+    int32_t* ntile_done;
+    void* y;
+    int64_t n_tokens;
 };
 
 __host__ __device__ constexpr int tc_stage_bytes(int bn, bool gateup) {
@@ -288,6 +298,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         volatile int* ep_ok = abort_flag + 1;  // verdict of the accumulator wait, shared
         int acc = 0;
         uint32_t acc_phase = 0;
+        if constexpr (!GATEUP) {
+            if (p.ntile_done != nullptr && total == 0 && blockIdx.x == 0) {
+                // nothing to reduce (no shared experts, no available selection): y = 0
+                for (int64_t i = et; i < p.n_tokens * p.h; i += 128)
+                    static_cast<T*>(p.y)[i] = from_f32<T>(__ldcg(p.y_acc + i));
+            }
+        }
         for (int u = blockIdx.x; u < total; u += gridDim.x) {
             const TcUnit w = tc_decode(p, num_active, u, BN, splits_unused);
             const int rows = p.act_rows[w.a];
@@ -392,6 +409,56 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 bulk_commit();
             }
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+
+            // ---- fused tails: the last arrival on a tile finishes it (no waiting) ----
+            int32_t* counter = nullptr;
+            int expected = 0;
+            if constexpr (GATEUP && SPLIT) {
+                if (p.tile_done != nullptr) {
+                    const int tt = (rows + BN - 1) / BN;
+                    const int rem = u - p.ustart[w.a];
+                    counter = p.tile_done + p.ustart[w.a] / p.splits + rem % (tt * p.m_tiles);
+                    expected = p.splits;
+                }
+            } else if constexpr (!GATEUP) {
+                if (p.ntile_done != nullptr) {
+                    counter = p.ntile_done + w.mtile;
+                    expected = total / p.m_tiles;  // units per output-column tile
+                }
+            }
+            if (counter != nullptr) {
+                // this unit's reduce-adds must be complete and visible before it counts
+                bulk_wait_all();
+                fence_proxy_async_global();
+                __threadfence();
+                epilogue_bar_sync(128);
+                if (et == 0) ep_ok[1] = (atomicAdd(counter, 1) == expected - 1) ? 1 : 0;
+                epilogue_bar_sync(128);
+                if (ep_ok[1]) {
+                    __threadfence();
+                    if constexpr (GATEUP) {
+                        // h rows of this tile = silu(G) * U from the summed fp32 partials
+                        if (et < ncols) {
+                            const int f = m0 + et;
+                            const int last = min(rows, tok0 + BN);
+                            for (int tok = tok0; tok < last; ++tok) {
+                                const int64_t slot = hrow0 + tok;
+                                const float gv = __ldcg(p.gu + slot * 2 * p.f + f);
+                                const float uv = __ldcg(p.gu + slot * 2 * p.f + p.f + f);
+                                static_cast<T*>(p.hid)[slot * p.f + f] = from_f32<T>(silu_f32(gv) * uv);
+                            }
+                        }
+                    } else {
+                        // every contribution to this column block has landed: convert it
+                        if (et < ncols) {
+                            const int col = m0 + et;
+                            for (int64_t t = 0; t < p.n_tokens; ++t)
+                                static_cast<T*>(p.y)[t * p.h + col] =
+                                    from_f32<T>(__ldcg(p.y_acc + t * p.h + col));
+                        }
+                    }
+                }
+            }
         }
         bulk_wait_all();
     }

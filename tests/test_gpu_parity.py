@@ -154,6 +154,15 @@ def test_all_unavailable_is_shared_only():
     assert O.rel_l2(_np(out["y"]), ref) <= 1e-2
 
 
+@pytest.mark.parametrize("n", [3, 40, 300])
+def test_no_shared_experts_and_nothing_available_gives_zero(n):
+    # S_h = 0 and every expert unavailable: the layer output is exactly zero
+    wl = _workload(128, 8, 2, 128, 0, n, seed=n)
+    out = _run(wl, 2, True, avail=torch.zeros(8, device=DEV))
+    torch.cuda.synchronize()
+    assert float(out["y"].float().abs().max()) == 0.0
+
+
 def test_fractional_availability_blend():
     # a_e in (0,1): y = sum w (a E + (1-a) S) + S  (chronos/mlx/moe.py:162)
     wl = _workload(128, 8, 2, 128, 1, 24, seed=5)
