@@ -305,6 +305,70 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     static_cast<T*>(p.y)[i] = from_f32<T>(__ldcg(p.y_acc + i));
             }
         }
+
+        // ---- fused tails (decode batches): the last arrival on a tile finishes it ----
+        // Finished units are recorded and counted in batches: one wait for this CTA's
+        // reduce-adds, then one counter increment per unit; whoever completes a tile
+        // writes h (split gate/up) or converts the tile's column block of y (down).
+        constexpr int kMaxPending = 16;
+        bool fused = false;
+        if constexpr (GATEUP && SPLIT) {
+            fused = p.tile_done != nullptr;
+        } else if constexpr (!GATEUP) {
+            fused = p.ntile_done != nullptr;
+        }
+        int pend_u[kMaxPending] = {};
+        int npend = 0;
+        volatile int* ep_last = abort_flag + 4;  // [kMaxPending] verdicts, shared
+        auto flush_pending = [&]() {
+            bulk_wait_all();
+            fence_proxy_async_global();
+            __threadfence();
+            epilogue_bar_sync(128);
+            if (et < npend) {
+                const int uu = pend_u[et];
+                const TcUnit v = tc_decode(p, num_active, uu, BN, 0);
+                int32_t* counter;
+                int expected;
+                if constexpr (GATEUP) {
+                    const int tt = (p.act_rows[v.a] + BN - 1) / BN;
+                    const int rem = uu - p.ustart[v.a];
+                    counter = p.tile_done + p.ustart[v.a] / p.splits + rem % (tt * p.m_tiles);
+                    expected = p.splits;
+                } else {
+                    counter = p.ntile_done + v.mtile;
+                    expected = total / p.m_tiles;  // units per output-column tile
+                }
+                ep_last[et] = (atomicAdd(counter, 1) == expected - 1) ? 1 : 0;
+            }
+            epilogue_bar_sync(128);
+            __threadfence();
+            for (int i = 0; i < npend; ++i) {
+                if (!ep_last[i]) continue;
+                const TcUnit v = tc_decode(p, num_active, pend_u[i], BN, 0);
+                const int m0 = v.mtile * kTcBM;
+                if (et >= min(kTcBM, p.out_cols - m0)) continue;
+                if constexpr (GATEUP) {
+                    // h rows of this tile = silu(G) * U from the summed fp32 partials
+                    const int f = m0 + et;
+                    const int rows = p.act_rows[v.a];
+                    const int64_t hrow0 = p.act_hrow[v.a];
+                    const int last = min(rows, v.tok_tile * BN + BN);
+                    for (int tok = v.tok_tile * BN; tok < last; ++tok) {
+                        const int64_t slot = hrow0 + tok;
+                        const float gv = __ldcg(p.gu + slot * 2 * p.f + f);
+                        const float uv = __ldcg(p.gu + slot * 2 * p.f + p.f + f);
+                        static_cast<T*>(p.hid)[slot * p.f + f] = from_f32<T>(silu_f32(gv) * uv);
+                    }
+                } else {
+                    // every contribution to this column block has landed: convert it
+                    const int col = m0 + et;
+                    for (int64_t t = 0; t < p.n_tokens; ++t)
+                        static_cast<T*>(p.y)[t * p.h + col] = from_f32<T>(__ldcg(p.y_acc + t * p.h + col));
+                }
+            }
+        };
+
         for (int u = blockIdx.x; u < total; u += gridDim.x) {
             const TcUnit w = tc_decode(p, num_active, u, BN, splits_unused);
             const int rows = p.act_rows[w.a];
@@ -410,56 +474,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
 
-            // ---- fused tails: the last arrival on a tile finishes it (no waiting) ----
-            int32_t* counter = nullptr;
-            int expected = 0;
-            if constexpr (GATEUP && SPLIT) {
-                if (p.tile_done != nullptr) {
-                    const int tt = (rows + BN - 1) / BN;
-                    const int rem = u - p.ustart[w.a];
-                    counter = p.tile_done + p.ustart[w.a] / p.splits + rem % (tt * p.m_tiles);
-                    expected = p.splits;
-                }
-            } else if constexpr (!GATEUP) {
-                if (p.ntile_done != nullptr) {
-                    counter = p.ntile_done + w.mtile;
-                    expected = total / p.m_tiles;  // units per output-column tile
-                }
-            }
-            if (counter != nullptr) {
-                // this unit's reduce-adds must be complete and visible before it counts
-                bulk_wait_all();
-                fence_proxy_async_global();
-                __threadfence();
-                epilogue_bar_sync(128);
-                if (et == 0) ep_ok[1] = (atomicAdd(counter, 1) == expected - 1) ? 1 : 0;
-                epilogue_bar_sync(128);
-                if (ep_ok[1]) {
-                    __threadfence();
-                    if constexpr (GATEUP) {
-                        // h rows of this tile = silu(G) * U from the summed fp32 partials
-                        if (et < ncols) {
-                            const int f = m0 + et;
-                            const int last = min(rows, tok0 + BN);
-                            for (int tok = tok0; tok < last; ++tok) {
-                                const int64_t slot = hrow0 + tok;
-                                const float gv = __ldcg(p.gu + slot * 2 * p.f + f);
-                                const float uv = __ldcg(p.gu + slot * 2 * p.f + p.f + f);
-                                static_cast<T*>(p.hid)[slot * p.f + f] = from_f32<T>(silu_f32(gv) * uv);
-                            }
-                        }
-                    } else {
-                        // every contribution to this column block has landed: convert it
-                        if (et < ncols) {
-                            const int col = m0 + et;
-                            for (int64_t t = 0; t < p.n_tokens; ++t)
-                                static_cast<T*>(p.y)[t * p.h + col] =
-                                    from_f32<T>(__ldcg(p.y_acc + t * p.h + col));
-                        }
-                    }
+            // fused tails: remember the finished tile; counting happens in batches
+            if (fused) {
+                pend_u[npend++] = u;
+                if (npend == kMaxPending) {
+                    flush_pending();
+                    npend = 0;
                 }
             }
         }
+        if (fused && npend > 0) flush_pending();
         bulk_wait_all();
     }
 
