@@ -348,23 +348,41 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const TcUnit v = tc_decode(p, num_active, pend_u[i], BN, 0);
                 const int m0 = v.mtile * kTcBM;
                 if (et >= min(kTcBM, p.out_cols - m0)) continue;
+                constexpr int kBatch = 16;  // rows whose loads are in flight together
                 if constexpr (GATEUP) {
                     // h rows of this tile = silu(G) * U from the summed fp32 partials
                     const int f = m0 + et;
                     const int rows = p.act_rows[v.a];
                     const int64_t hrow0 = p.act_hrow[v.a];
-                    const int last = min(rows, v.tok_tile * BN + BN);
-                    for (int tok = v.tok_tile * BN; tok < last; ++tok) {
-                        const int64_t slot = hrow0 + tok;
-                        const float gv = __ldcg(p.gu + slot * 2 * p.f + f);
-                        const float uv = __ldcg(p.gu + slot * 2 * p.f + p.f + f);
-                        static_cast<T*>(p.hid)[slot * p.f + f] = from_f32<T>(silu_f32(gv) * uv);
+                    const int first = v.tok_tile * BN;
+                    const int last = min(rows, first + BN);
+                    for (int t0 = first; t0 < last; t0 += kBatch) {
+                        float gv[kBatch], uv[kBatch];
+#pragma unroll
+                        for (int j = 0; j < kBatch; ++j) {
+                            const int64_t slot = hrow0 + min(t0 + j, last - 1);
+                            gv[j] = __ldcg(p.gu + slot * 2 * p.f + f);
+                            uv[j] = __ldcg(p.gu + slot * 2 * p.f + p.f + f);
+                        }
+#pragma unroll
+                        for (int j = 0; j < kBatch; ++j)
+                            if (t0 + j < last)
+                                static_cast<T*>(p.hid)[(hrow0 + t0 + j) * p.f + f] =
+                                    from_f32<T>(silu_f32(gv[j]) * uv[j]);
                     }
                 } else {
                     // every contribution to this column block has landed: convert it
                     const int col = m0 + et;
-                    for (int64_t t = 0; t < p.n_tokens; ++t)
-                        static_cast<T*>(p.y)[t * p.h + col] = from_f32<T>(__ldcg(p.y_acc + t * p.h + col));
+                    const int64_t n = p.n_tokens;
+                    for (int64_t t0 = 0; t0 < n; t0 += kBatch) {
+                        float yv[kBatch];
+#pragma unroll
+                        for (int j = 0; j < kBatch; ++j)
+                            yv[j] = __ldcg(p.y_acc + min<int64_t>(t0 + j, n - 1) * p.h + col);
+#pragma unroll
+                        for (int j = 0; j < kBatch; ++j)
+                            if (t0 + j < n) static_cast<T*>(p.y)[(t0 + j) * p.h + col] = from_f32<T>(yv[j]);
+                    }
                 }
             }
         };
