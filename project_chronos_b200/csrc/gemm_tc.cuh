@@ -378,7 +378,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         float yv[kBatch];
 #pragma unroll
                         for (int j = 0; j < kBatch; ++j)
-                            yv[j] = __ldcg(p.y_acc + min<int64_t>(t0 + j, n - 1) * p.h + col);
+                            yv[j] = __ldcg(p.y_acc + (t0 + j < n ? t0 + j : n - 1) * p.h + col);
 #pragma unroll
                         for (int j = 0; j < kBatch; ++j)
                             if (t0 + j < n) static_cast<T*>(p.y)[(t0 + j) * p.h + col] = from_f32<T>(yv[j]);
