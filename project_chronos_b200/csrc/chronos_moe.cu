@@ -91,7 +91,7 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 struct Layout {
     size_t grp_count, grp_off, act_rows, act_xrow, act_hrow, act_wslot, act_eid, ustart_gu, partials,
         ustart_dn, hdr, pos, sel_coef, shared_coef, topk_idx, topk_w, slot_tok, slot_coef, xp,
-        hid, gu, y_acc, total, tile_done, ntile_done, n_tile_done, n_ntile_done;
+        hid, gu, y_acc, total;
     bool split_capable;
 };
 
@@ -107,15 +107,7 @@ Layout make_layout(const ChronosMoeShape& s) {
         off = align_up(off + bytes, 256);
         return o;
     };
-    // counters zeroed by one memset per call: group sizes, then (decode batches)
-    // the fused-tail arrival counters of the two GEMMs
-    const size_t mt_gu = (F + 127) / 128, mt_dn = (H + 127) / 128;
-    L.split_capable = N <= static_cast<size_t>(kSplitMaxTokens);
-    L.n_tile_done = L.split_capable ? ((N * K + S * N) / 16 + G + 1) * mt_gu : 0;
-    L.n_ntile_done = L.split_capable ? mt_dn : 0;
-    L.grp_count = take(4 * (E + L.n_tile_done + L.n_ntile_done));
-    L.tile_done = L.grp_count + 4 * E;
-    L.ntile_done = L.tile_done + 4 * L.n_tile_done;
+    L.grp_count = take(4 * E);
     L.grp_off = take(4 * E);
     L.act_rows = take(4 * G);
     L.act_xrow = take(4 * G);
@@ -136,6 +128,7 @@ Layout make_layout(const ChronosMoeShape& s) {
     L.slot_coef = take(4 * (N * K + S * N));
     L.xp = take(es * N * K * H);
     L.hid = take(es * (N * K + S * N) * F);
+    L.split_capable = N <= static_cast<size_t>(kSplitMaxTokens);
     L.gu = L.split_capable ? take(4 * (N * K + S * N) * 2 * F) : off;
     L.y_acc = take(4 * N * H);
     L.total = off;
@@ -408,16 +401,26 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     }
     if (split) {
         if constexpr (BN <= kSplitMaxTokens) {
-        // fp32 partials are reduced into `gu`; the last K-slice of each tile writes h
-        // (the activation is fused into the GEMM, the act stage stays empty)
         CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + w.L->gu, 0, 4 * slots * 2 * F, st));
-        pg.splits = splits_gu;
-        pg.tile_done = w.at<int32_t>(w.L->tile_done);
         prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
         if ((rc = launch_tc<T, BN, true, true>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st)))
             return rc;
         prof_ran(slot, CHRONOS_STAGE_GATEUP);
         prof_mark(slot, CHRONOS_STAGE_ACT, st);
+        ActParams ap{};
+        ap.gu = w.at<float>(w.L->gu);
+        ap.hid = w.ws + w.L->hid;
+        ap.hdr = p.hdr;
+        ap.n = s.num_tokens;
+        ap.f = s.ffn;
+        ap.k = s.top_k;
+        ap.num_shared = s.num_shared;
+        const int64_t total = static_cast<int64_t>(slots * F);
+        const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4 * grid));
+        act_kernel<T><<<blocks, 256, 0, st>>>(ap);
+        count_launch();
+        CHRONOS_CUDA_CHECK(cudaGetLastError());
+        prof_ran(slot, CHRONOS_STAGE_ACT);
         }
     } else {
         prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
@@ -436,12 +439,6 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     pd.m_tiles = static_cast<int>((H + kTcBM - 1) / kTcBM);
     pd.w_rows = static_cast<int>(H);
     pd.out_cols = static_cast<int>(H);
-    if (w.L->split_capable) {
-        // decode batches: the last unit of each output-column tile writes y
-        pd.ntile_done = w.at<int32_t>(w.L->ntile_done);
-        pd.y = a->y;
-        pd.n_tokens = s.num_tokens;
-    }
     if ((rc = launch_tc<T, BN_DN, false, false>(d_r, d_r, d_s, d_s, h_m, h_m, pd, grid, st)))
         return rc;
     prof_ran(slot, CHRONOS_STAGE_DOWN);
@@ -580,8 +577,7 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     }
 
     int rc;
-    CHRONOS_CUDA_CHECK(cudaMemsetAsync(
-        w.ws + L.grp_count, 0, 4 * (s.num_experts + L.n_tile_done + L.n_ntile_done), st));
+    CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + L.grp_count, 0, 4 * s.num_experts, st));
     if (!prerouted) {
         if (a->expert_counts)
             CHRONOS_CUDA_CHECK(cudaMemsetAsync(a->expert_counts, 0, 4 * s.num_experts, st));
@@ -665,14 +661,12 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     if (rc) return rc;
 
     prof_mark(slot, CHRONOS_STAGE_FINALIZE, st);
-    if (!(tc && L.split_capable)) {  // decode batches on the tensor-core path convert in the down GEMM
-        const int64_t count4 = N * s.hidden / 4;
-        const int blocks = static_cast<int>(std::min<int64_t>((count4 + 255) / 256, 8 * sm_count()));
-        finalize_kernel<T><<<blocks, 256, 0, st>>>(w.at<float>(L.y_acc), static_cast<T*>(a->y), count4);
-        count_launch();
-        CHRONOS_CUDA_CHECK(cudaGetLastError());
-        prof_ran(slot, CHRONOS_STAGE_FINALIZE);
-    }
+    const int64_t count4 = N * s.hidden / 4;
+    const int blocks = static_cast<int>(std::min<int64_t>((count4 + 255) / 256, 8 * sm_count()));
+    finalize_kernel<T><<<blocks, 256, 0, st>>>(w.at<float>(L.y_acc), static_cast<T*>(a->y), count4);
+    count_launch();
+    CHRONOS_CUDA_CHECK(cudaGetLastError());
+    prof_ran(slot, CHRONOS_STAGE_FINALIZE);
     prof_mark(slot, kBoundaries - 1, st);
     return CHRONOS_OK;
 }

@@ -61,16 +61,6 @@ struct TcGemmParams {
     int32_t ready_epoch;
     uint64_t ready_limit_ns;
     int32_t* status;
-    // Fused tails (decode batches; zeroed counters, null to disable):
-    //   tile_done  GATEUP+SPLIT: arrivals per (group, token tile, weight tile); the
-    //              last of the `splits` K-slices computes h = silu(G) * U for the tile
-    //   ntile_done DOWN: arrivals per output-column tile; the last unit converts that
-    //              column block of y_acc into y for all n_tokens rows
-    int splits;
-    int32_t* tile_done;
-    int32_t* ntile_done;
-    void* y;
-    int64_t n_tokens;
 };
 
 __host__ __device__ constexpr int tc_stage_bytes(int bn, bool gateup) {
@@ -298,95 +288,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         volatile int* ep_ok = abort_flag + 1;  // verdict of the accumulator wait, shared
         int acc = 0;
         uint32_t acc_phase = 0;
-        if constexpr (!GATEUP) {
-            if (p.ntile_done != nullptr && total == 0 && blockIdx.x == 0) {
-                // nothing to reduce (no shared experts, no available selection): y = 0
-                for (int64_t i = et; i < p.n_tokens * p.h; i += 128)
-                    static_cast<T*>(p.y)[i] = from_f32<T>(__ldcg(p.y_acc + i));
-            }
-        }
-
-        // ---- fused tails (decode batches): the last arrival on a tile finishes it ----
-        // Finished units are recorded and counted in batches: one wait for this CTA's
-        // reduce-adds, then one counter increment per unit; whoever completes a tile
-        // writes h (split gate/up) or converts the tile's column block of y (down).
-        constexpr int kMaxPending = 16;
-        bool fused = false;
-        if constexpr (GATEUP && SPLIT) {
-            fused = p.tile_done != nullptr;
-        } else if constexpr (!GATEUP) {
-            fused = p.ntile_done != nullptr;
-        }
-        int pend_u[kMaxPending] = {};
-        int npend = 0;
-        volatile int* ep_last = abort_flag + 4;  // [kMaxPending] verdicts, shared
-        auto flush_pending = [&]() {
-            bulk_wait_all();
-            fence_proxy_async_global();
-            __threadfence();
-            epilogue_bar_sync(128);
-            if (et < npend) {
-                const int uu = pend_u[et];
-                const TcUnit v = tc_decode(p, num_active, uu, BN, 0);
-                int32_t* counter;
-                int expected;
-                if constexpr (GATEUP) {
-                    const int tt = (p.act_rows[v.a] + BN - 1) / BN;
-                    const int rem = uu - p.ustart[v.a];
-                    counter = p.tile_done + p.ustart[v.a] / p.splits + rem % (tt * p.m_tiles);
-                    expected = p.splits;
-                } else {
-                    counter = p.ntile_done + v.mtile;
-                    expected = total / p.m_tiles;  // units per output-column tile
-                }
-                ep_last[et] = (atomicAdd(counter, 1) == expected - 1) ? 1 : 0;
-            }
-            epilogue_bar_sync(128);
-            __threadfence();
-            for (int i = 0; i < npend; ++i) {
-                if (!ep_last[i]) continue;
-                const TcUnit v = tc_decode(p, num_active, pend_u[i], BN, 0);
-                const int m0 = v.mtile * kTcBM;
-                if (et >= min(kTcBM, p.out_cols - m0)) continue;
-                constexpr int kBatch = 16;  // rows whose loads are in flight together
-                if constexpr (GATEUP) {
-                    // h rows of this tile = silu(G) * U from the summed fp32 partials
-                    const int f = m0 + et;
-                    const int rows = p.act_rows[v.a];
-                    const int64_t hrow0 = p.act_hrow[v.a];
-                    const int first = v.tok_tile * BN;
-                    const int last = min(rows, first + BN);
-                    for (int t0 = first; t0 < last; t0 += kBatch) {
-                        float gv[kBatch], uv[kBatch];
-#pragma unroll
-                        for (int j = 0; j < kBatch; ++j) {
-                            const int64_t slot = hrow0 + min(t0 + j, last - 1);
-                            gv[j] = __ldcg(p.gu + slot * 2 * p.f + f);
-                            uv[j] = __ldcg(p.gu + slot * 2 * p.f + p.f + f);
-                        }
-#pragma unroll
-                        for (int j = 0; j < kBatch; ++j)
-                            if (t0 + j < last)
-                                static_cast<T*>(p.hid)[(hrow0 + t0 + j) * p.f + f] =
-                                    from_f32<T>(silu_f32(gv[j]) * uv[j]);
-                    }
-                } else {
-                    // every contribution to this column block has landed: convert it
-                    const int col = m0 + et;
-                    const int64_t n = p.n_tokens;
-                    for (int64_t t0 = 0; t0 < n; t0 += kBatch) {
-                        float yv[kBatch];
-#pragma unroll
-                        for (int j = 0; j < kBatch; ++j)
-                            yv[j] = __ldcg(p.y_acc + (t0 + j < n ? t0 + j : n - 1) * p.h + col);
-#pragma unroll
-                        for (int j = 0; j < kBatch; ++j)
-                            if (t0 + j < n) static_cast<T*>(p.y)[(t0 + j) * p.h + col] = from_f32<T>(yv[j]);
-                    }
-                }
-            }
-        };
-
         for (int u = blockIdx.x; u < total; u += gridDim.x) {
             const TcUnit w = tc_decode(p, num_active, u, BN, splits_unused);
             const int rows = p.act_rows[w.a];
@@ -491,17 +392,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 bulk_commit();
             }
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
-
-            // fused tails: remember the finished tile; counting happens in batches
-            if (fused) {
-                pend_u[npend++] = u;
-                if (npend == kMaxPending) {
-                    flush_pending();
-                    npend = 0;
-                }
-            }
         }
-        if (fused && npend > 0) flush_pending();
         bulk_wait_all();
     }
 
