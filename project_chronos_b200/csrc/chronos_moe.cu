@@ -569,7 +569,9 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
         const int kt_total = s.ffn / kTcBK;
         const int64_t groups_est = std::min<int64_t>(s.num_experts, N * s.top_k) + s.num_shared;
         const int64_t tiles_est = groups_est * ((N + bn_dn - 1) / bn_dn);
-        const int target = 2 * sm_count();
+        // the down epilogue reduces anyway, so K splits only cost reduce traffic:
+        // aim at >= 8 units per SM for an even finish
+        const int target = 8 * sm_count();
         while (tiles_est * mt_dn * splits_dn < target && splits_dn * 2 * 4 <= kt_total)
             splits_dn *= 2;
         kt_dn = (kt_total + splits_dn - 1) / splits_dn;

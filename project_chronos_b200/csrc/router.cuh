@@ -107,31 +107,51 @@ __global__ void __launch_bounds__(kPartialThreads) route_partials_kernel(RoutePa
     const int len = min(kRouteChunk, H - h0);  // multiple of 4
     const T* x = static_cast<const T*>(p.x);
     const T* w = static_cast<const T*>(p.w);
-    // weights: row r = expert e0 + r, vector v = elements [v*EPV, v*EPV + EPV) of the chunk
+    // weights: row r = expert e0 + r, vector v = elements [v*EPV, v*EPV + EPV) of the
+    // chunk; every thread issues all of its V16 loads before any store (one latency)
     const bool vec_ok = (H % EPV) == 0;  // 16-byte aligned rows
-    for (int i = threadIdx.x; i < kPartialThreads * V16; i += kPartialThreads) {
-        const int r = i / V16, v = i % V16;
-        const int er = e0 + r;
-        uint4 val = make_uint4(0u, 0u, 0u, 0u);
-        if (er < E) {
-            const T* src = w + static_cast<int64_t>(er) * H + h0 + v * EPV;
-            if (vec_ok && v * EPV + EPV <= len) {
-                val = *reinterpret_cast<const uint4*>(src);
-            } else {
-                T tmp[EPV];
+    {
+        uint4 val[V16];
 #pragma unroll
-                for (int u = 0; u < EPV; ++u) tmp[u] = (v * EPV + u < len) ? src[u] : from_f32<T>(0.0f);
-                val = *reinterpret_cast<const uint4*>(tmp);
+        for (int it = 0; it < V16; ++it) {
+            const int i = it * kPartialThreads + threadIdx.x;
+            const int r = i / V16, v = i % V16;
+            const int er = e0 + r;
+            val[it] = make_uint4(0u, 0u, 0u, 0u);
+            if (er < E) {
+                const T* src = w + static_cast<int64_t>(er) * H + h0 + v * EPV;
+                if (vec_ok && v * EPV + EPV <= len) {
+                    val[it] = *reinterpret_cast<const uint4*>(src);
+                } else {
+                    T tmp[EPV];
+#pragma unroll
+                    for (int u = 0; u < EPV; ++u) tmp[u] = (v * EPV + u < len) ? src[u] : from_f32<T>(0.0f);
+                    val[it] = *reinterpret_cast<const uint4*>(tmp);
+                }
             }
         }
-        *reinterpret_cast<uint4*>(ws + r * ROW + v * 16) = val;
+#pragma unroll
+        for (int it = 0; it < V16; ++it) {
+            const int i = it * kPartialThreads + threadIdx.x;
+            *reinterpret_cast<uint4*>(ws + (i / V16) * ROW + (i % V16) * 16) = val[it];
+        }
     }
-    // x chunk of the token group, as fp32
-    for (int i = threadIdx.x; i < kRouteGroup * (kRouteChunk / 4); i += kPartialThreads) {
-        const int r = i / (kRouteChunk / 4), q4 = (i % (kRouteChunk / 4)) * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (r < nt && q4 < len) v = load4<T>(x + (t0 + r) * H + h0 + q4);
-        *reinterpret_cast<float4*>(&xs[r][q4]) = v;
+    // x chunk of the token group, as fp32 (loads first, then stores)
+    {
+        constexpr int XV = kRouteGroup * (kRouteChunk / 4) / kPartialThreads;
+        float4 xv[XV];
+#pragma unroll
+        for (int it = 0; it < XV; ++it) {
+            const int i = it * kPartialThreads + threadIdx.x;
+            const int r = i / (kRouteChunk / 4), q4 = (i % (kRouteChunk / 4)) * 4;
+            xv[it] = (r < nt && q4 < len) ? load4<T>(x + (t0 + r) * H + h0 + q4)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int it = 0; it < XV; ++it) {
+            const int i = it * kPartialThreads + threadIdx.x;
+            *reinterpret_cast<float4*>(&xs[i / (kRouteChunk / 4)][(i % (kRouteChunk / 4)) * 4]) = xv[it];
+        }
     }
     __syncthreads();
     if (e >= E) return;
@@ -311,13 +331,15 @@ __global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParam
             const float* pp = p.partials + (t * E + e) * C;
             float s = 0.0f;
             int c = 0;
-            // loads in groups of 8 ahead of the in-order adds
-            for (; c + 8 <= C; c += 8) {
-                float r[8];
+            // loads in groups of 16 ahead of the in-order adds
+            for (; c + 16 <= C; c += 16) {
+                float4 r[4];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) r[u] = pp[c + u];
+                for (int u = 0; u < 4; ++u) r[u] = (C % 4 == 0) ? reinterpret_cast<const float4*>(pp + c)[u]
+                                                               : make_float4(pp[c + 4 * u], pp[c + 4 * u + 1],
+                                                                             pp[c + 4 * u + 2], pp[c + 4 * u + 3]);
 #pragma unroll
-                for (int u = 0; u < 8; ++u) s = s + r[u];
+                for (int u = 0; u < 4; ++u) s = ((s + r[u].x) + r[u].y + r[u].z) + r[u].w;
             }
             for (; c < C; ++c) s = s + pp[c];
             if (p.bias) s = s + p.bias[e];
