@@ -56,6 +56,27 @@ std::atomic<uint64_t> g_kernel_launches{0};
 
 inline void count_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
 
+// Launch with programmatic stream serialisation (`pdl`): the kernel may start
+// while its predecessor in the stream runs and waits for it with pdl_wait().
+// The first kernel of a call is launched without it, so a call never overlaps
+// the previous call's kernels.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t st, bool pdl, Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl ? attr : nullptr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    count_launch();
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // ---------------------------------------------------------------------------
 // stage profiling: CUDA events at the stage boundaries of profiled calls
 // ---------------------------------------------------------------------------
@@ -306,24 +327,25 @@ int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool p
     const int64_t N = s.num_tokens;
     const bool small = N <= kRouteSmallMax;
     rp.nchunks = small ? route_chunks(s.hidden) : 1;
+    // the logit kernel is the call's first launch (no PDL) and zeroes the counters;
+    // with pre-routed inputs the caller zeroed them and the select kernel comes first
     if (!prerouted) {
         if (small) {
             const dim3 grid(static_cast<unsigned>((N + kRouteGroup - 1) / kRouteGroup),
                             static_cast<unsigned>(rp.nchunks),
                             static_cast<unsigned>((s.num_experts + kPartialThreads - 1) / kPartialThreads));
-            route_partials_kernel<T><<<grid, kPartialThreads, 0, st>>>(rp);
+            CHRONOS_CUDA_CHECK(launch_kernel(route_partials_kernel<T>, grid, dim3(kPartialThreads), 0, st,
+                                             false, rp));
         } else {
             const dim3 grid(static_cast<unsigned>((N + kRouteTile - 1) / kRouteTile),
                             static_cast<unsigned>((s.num_experts + kRouteTile - 1) / kRouteTile));
-            route_tiled_kernel<T><<<grid, kTiledThreads, 0, st>>>(rp);
+            CHRONOS_CUDA_CHECK(launch_kernel(route_tiled_kernel<T>, grid, dim3(kTiledThreads), 0, st,
+                                             false, rp));
         }
-        count_launch();
-        CHRONOS_CUDA_CHECK(cudaGetLastError());
     }
     const unsigned sgrid = static_cast<unsigned>((N + kSelectThreads / 32 - 1) / (kSelectThreads / 32));
-    route_select_kernel<T><<<sgrid, kSelectThreads, 0, st>>>(rp);
-    count_launch();
-    CHRONOS_CUDA_CHECK(cudaGetLastError());
+    CHRONOS_CUDA_CHECK(launch_kernel(route_select_kernel<T>, dim3(sgrid), dim3(kSelectThreads), 0, st,
+                                     !prerouted, rp));
     return CHRONOS_OK;
 }
 
@@ -334,9 +356,8 @@ int launch_tc(const CUtensorMap& a0r, const CUtensorMap& a1r, const CUtensorMap&
     constexpr int smem = tc_smem_bytes(BN, GATEUP, SPLIT);
     auto kern = tc_grouped_gemm<T, BN, GATEUP, SPLIT>;
     if (int rc = set_smem(kern, smem)) return rc;
-    kern<<<grid, kTcThreads, smem, st>>>(a0r, a1r, a0s, a1s, br, bs, p);
-    count_launch();
-    CHRONOS_CUDA_CHECK(cudaGetLastError());
+    CHRONOS_CUDA_CHECK(launch_kernel(kern, dim3(grid), dim3(kTcThreads), smem, st, true, a0r, a1r, a0s,
+                                     a1s, br, bs, p));
     return CHRONOS_OK;
 }
 
@@ -401,7 +422,7 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     }
     if (split) {
         if constexpr (BN <= kSplitMaxTokens) {
-        CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + w.L->gu, 0, 4 * slots * 2 * F, st));
+        // (the plan/scatter kernel zeroed the fp32 partial buffer `gu`)
         prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
         if ((rc = launch_tc<T, BN, true, true>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st)))
             return rc;
@@ -417,9 +438,7 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
         ap.num_shared = s.num_shared;
         const int64_t total = static_cast<int64_t>(slots * F);
         const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4 * grid));
-        act_kernel<T><<<blocks, 256, 0, st>>>(ap);
-        count_launch();
-        CHRONOS_CUDA_CHECK(cudaGetLastError());
+        CHRONOS_CUDA_CHECK(launch_kernel(act_kernel<T>, dim3(blocks), dim3(256), 0, st, true, ap));
         prof_ran(slot, CHRONOS_STAGE_ACT);
         }
     } else {
@@ -474,9 +493,8 @@ int launch_simt(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int slo
     pg.w0s = a->w_shared_gate;
     pg.w1s = a->w_shared_up;
     prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
-    simt_grouped_gemm<T, true><<<grid, kSimtThreads, 0, st>>>(pg);
-    count_launch();
-    CHRONOS_CUDA_CHECK(cudaGetLastError());
+    CHRONOS_CUDA_CHECK(launch_kernel(simt_grouped_gemm<T, true>, dim3(grid), dim3(kSimtThreads), 0, st,
+                                     true, pg));
     prof_ran(slot, CHRONOS_STAGE_GATEUP);
     prof_mark(slot, CHRONOS_STAGE_ACT, st);
     prof_mark(slot, CHRONOS_STAGE_DOWN, st);
@@ -488,9 +506,8 @@ int launch_simt(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int slo
     pd.out_cols = s.hidden;
     pd.w0r = a->w_down;
     pd.w0s = a->w_shared_down;
-    simt_grouped_gemm<T, false><<<grid, kSimtThreads, 0, st>>>(pd);
-    count_launch();
-    CHRONOS_CUDA_CHECK(cudaGetLastError());
+    CHRONOS_CUDA_CHECK(launch_kernel(simt_grouped_gemm<T, false>, dim3(grid), dim3(kSimtThreads), 0, st,
+                                     true, pd));
     prof_ran(slot, CHRONOS_STAGE_DOWN);
     return CHRONOS_OK;
 }
@@ -579,13 +596,9 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     }
 
     int rc;
-    CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + L.grp_count, 0, 4 * s.num_experts, st));
-    if (!prerouted) {
-        if (a->expert_counts)
-            CHRONOS_CUDA_CHECK(cudaMemsetAsync(a->expert_counts, 0, 4 * s.num_experts, st));
-        if (a->expert_mass)
-            CHRONOS_CUDA_CHECK(cudaMemsetAsync(a->expert_mass, 0, 4 * s.num_experts, st));
-    }
+    // counters: zeroed by the logit kernel, or here when routing is skipped
+    if (prerouted)
+        CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + L.grp_count, 0, 4 * s.num_experts, st));
     const int slot = prof_begin_call();
     prof_mark(slot, CHRONOS_STAGE_ROUTE, st);
     if ((rc = launch_route<T>(a, w, st, prerouted, topk_idx, topk_w, true))) return rc;
@@ -632,13 +645,16 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     sp.slot_tok = w.at<int32_t>(L.slot_tok);
     sp.slot_coef = w.at<float>(L.slot_coef);
     sp.copy_rows = tc ? 1 : 0;
+    if (tc && splits_gu > 1) {  // split-K partials accumulate into `gu`
+        sp.zero = reinterpret_cast<float4*>(w.ws + L.gu);
+        sp.zero_count4 = static_cast<int64_t>((N * s.top_k + s.num_shared * N) * 2 * s.ffn / 4);
+    }
     {
         const int64_t warps = N * s.top_k;
         const unsigned blocks =
             static_cast<unsigned>(std::max<int64_t>(1, (warps + kScatterWarps - 1) / kScatterWarps));
-        plan_scatter_kernel<T><<<blocks, kScatterThreads, 0, st>>>(pp, sp);
-        count_launch();
-        CHRONOS_CUDA_CHECK(cudaGetLastError());
+        CHRONOS_CUDA_CHECK(launch_kernel(plan_scatter_kernel<T>, dim3(blocks), dim3(kScatterThreads), 0,
+                                         st, true, pp, sp));
     }
     prof_ran(slot, CHRONOS_STAGE_SCATTER);
 
@@ -665,9 +681,9 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     prof_mark(slot, CHRONOS_STAGE_FINALIZE, st);
     const int64_t count4 = N * s.hidden / 4;
     const int blocks = static_cast<int>(std::min<int64_t>((count4 + 255) / 256, 8 * sm_count()));
-    finalize_kernel<T><<<blocks, 256, 0, st>>>(w.at<float>(L.y_acc), static_cast<T*>(a->y), count4);
-    count_launch();
-    CHRONOS_CUDA_CHECK(cudaGetLastError());
+    CHRONOS_CUDA_CHECK(launch_kernel(finalize_kernel<T>, dim3(blocks), dim3(256), 0, st, true,
+                                     static_cast<const float*>(w.at<float>(L.y_acc)),
+                                     static_cast<T*>(a->y), count4));
     prof_ran(slot, CHRONOS_STAGE_FINALIZE);
     prof_mark(slot, kBoundaries - 1, st);
     return CHRONOS_OK;
@@ -678,10 +694,7 @@ int route_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     const ChronosMoeShape& s = a->shape;
     const Layout L = make_layout(s);
     Ptrs w{static_cast<uint8_t*>(a->workspace), &L};
-    CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + L.grp_count, 0, 4 * s.num_experts, st));
-    if (a->expert_counts)
-        CHRONOS_CUDA_CHECK(cudaMemsetAsync(a->expert_counts, 0, 4 * s.num_experts, st));
-    if (a->expert_mass) CHRONOS_CUDA_CHECK(cudaMemsetAsync(a->expert_mass, 0, 4 * s.num_experts, st));
+    // the logit kernel zeroes the group counters and the per-expert statistics
     return launch_route<T>(a, w, st, false, a->topk_idx, a->topk_weight, false);
 }
 

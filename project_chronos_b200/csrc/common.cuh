@@ -35,6 +35,13 @@ __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2hal
 
 __device__ __forceinline__ float silu_f32(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start while its predecessor is still running; it must
+// call pdl_wait() before reading anything the predecessor writes (a no-op when
+// launched without the attribute).  pdl_trigger() lets the successor launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Record the first device-side failure of a call in the caller's status word.
 __device__ __forceinline__ void report_status(int32_t* status, int32_t code) {
     if (status != nullptr) atomicCAS(status, 0, code);

@@ -49,6 +49,8 @@ __global__ void __launch_bounds__(kSimtThreads) simt_grouped_gemm(SimtGemmParams
 
     const int tid = threadIdx.x;
     const int tx = tid & 15, ty = tid >> 4;
+    pdl_trigger();
+    pdl_wait();
     const int num_active = p.hdr->num_active;
     const int total = GATEUP ? p.hdr->units_gu : p.hdr->units_dn;
     const int K = p.kdim;

@@ -157,6 +157,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    pdl_trigger();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -181,6 +182,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
 
+    pdl_wait();  // everything below reads what earlier kernels of the call wrote
     const int num_active = p.hdr->num_active;
     const int total = GATEUP ? p.hdr->units_gu : p.hdr->units_dn;
     const int splits_unused = 0;

@@ -154,6 +154,8 @@ struct ScatterParams {
     int32_t* slot_tok;    // [N*k + S*N]
     float* slot_coef;     // [N*k + S*N]
     int copy_rows;        // 0: only the slot tables (B operand read from x by row index)
+    float4* zero;         // buffer the next kernel accumulates into (split-K partials), or null
+    int64_t zero_count4;  // its size in float4
 };
 
 constexpr int kScatterThreads = kPlanThreads;
@@ -171,6 +173,13 @@ __global__ void __launch_bounds__(kScatterThreads) plan_scatter_kernel(PlanParam
     __shared__ int s_tot[4];
     __shared__ int s_off[kPlanThreads];
     const int tid = threadIdx.x;
+    pdl_trigger();
+    if (p.zero != nullptr) {  // independent of the routing: before the dependency wait
+        for (int64_t i = static_cast<int64_t>(blockIdx.x) * kScatterThreads + tid; i < p.zero_count4;
+             i += static_cast<int64_t>(gridDim.x) * kScatterThreads)
+            p.zero[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    pdl_wait();  // routing results
     const int cnt = tid < pp.e ? pp.grp_count[tid] : 0;
     const int inc_cnt = block_inclusive_scan(cnt, s_scratch);
     s_off[tid] = inc_cnt - cnt;
@@ -230,6 +239,8 @@ struct ActParams {
 // the shared rows).
 template <typename T>
 __global__ void act_kernel(ActParams p) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t routed_cap = p.n * p.k;
     const int64_t rows_total = routed_cap + p.n * p.num_shared;
     const int routed_rows = p.hdr->routed_rows;
@@ -248,6 +259,8 @@ __global__ void act_kernel(ActParams p) {
 
 template <typename T>
 __global__ void finalize_kernel(const float* __restrict__ y_acc, T* __restrict__ y, int64_t count4) {
+    pdl_trigger();
+    pdl_wait();
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count4;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const float4 v = reinterpret_cast<const float4*>(y_acc)[i];

@@ -55,6 +55,17 @@ struct RouteParams {
     float* y_acc;         // [N, H] fp32, zeroed here (or null)
 };
 
+// The logit kernels run first in a call: their first block zeroes the
+// per-call counters (group sizes and the optional per-expert statistics) that
+// the select kernel, launched after them, accumulates into.
+__device__ __forceinline__ void zero_route_counters(const RouteParams& p) {
+    for (int i = threadIdx.x; i < p.e; i += blockDim.x) {
+        p.grp_count[i] = 0;
+        if (p.counts_all) p.counts_all[i] = 0;
+        if (p.mass_all) p.mass_all[i] = 0.0f;
+    }
+}
+
 inline int route_chunks(int h) { return (h + kRouteChunk - 1) / kRouteChunk; }
 
 // 4 consecutive elements as fp32 (8-byte loads for 16-bit types, 16 bytes for fp32).
@@ -96,6 +107,8 @@ __global__ void __launch_bounds__(kPartialThreads) route_partials_kernel(RoutePa
     constexpr int EPV = 16 / static_cast<int>(sizeof(T));                // elements per vector
     __shared__ __align__(16) float xs[kRouteGroup][kRouteChunk];
     __shared__ __align__(16) uint8_t ws[kPartialThreads * ROW];
+    pdl_trigger();
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) zero_route_counters(p);
     const int E = p.e, C = p.nchunks, H = p.h;
     const int c = blockIdx.y;
     const int e0 = blockIdx.z * kPartialThreads;
@@ -188,6 +201,8 @@ template <typename T>
 __global__ void __launch_bounds__(kTiledThreads) route_tiled_kernel(RouteParams p) {
     __shared__ __align__(16) float xs[2][kRouteTile][kTilePad];
     __shared__ __align__(16) float ws[2][kRouteTile][kTilePad];
+    pdl_trigger();
+    if (blockIdx.x == 0 && blockIdx.y == 0) zero_route_counters(p);
     const int tid = threadIdx.x;
     const int tg = tid >> 4;  // tokens tg*4 .. tg*4+3
     const int eg = tid & 15;  // experts eg + 16 j
@@ -284,6 +299,8 @@ __device__ __forceinline__ float expert_avail(const RouteParams& p, int e) {
 
 template <typename T>
 __global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParams p) {
+    pdl_trigger();
+    pdl_wait();  // partials and zeroed counters from the logit kernel
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t t = static_cast<int64_t>(blockIdx.x) * (kSelectThreads / 32) + warp;
     if (t >= p.n) return;
