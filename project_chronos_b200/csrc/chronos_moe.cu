@@ -111,7 +111,7 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // Workspace regions, a function of the shape only.
 struct Layout {
     size_t grp_count, grp_off, act_rows, act_xrow, act_hrow, act_wslot, act_eid, ustart_gu, partials,
-        ustart_dn, hdr, pos, sel_coef, shared_coef, topk_idx, topk_w, slot_tok, slot_coef, xp,
+        ustart_dn, hdr, pos, sel_coef, shared_coef, topk_idx, topk_w, slot_tok, slot_coef, slot_map, xp,
         hid, gu, y_acc, total;
     bool split_capable;
 };
@@ -147,6 +147,7 @@ Layout make_layout(const ChronosMoeShape& s) {
                       (N <= static_cast<size_t>(kRouteSmallMax) ? route_chunks(s.hidden) : 1));
     L.slot_tok = take(4 * (N * K + S * N));
     L.slot_coef = take(4 * (N * K + S * N));
+    L.slot_map = N <= static_cast<size_t>(kSelectPlanMaxTokens) ? take(4 * E * N) : off;
     L.xp = take(es * N * K * H);
     L.hid = take(es * (N * K + S * N) * F);
     L.split_capable = N <= static_cast<size_t>(kSplitMaxTokens);
@@ -296,9 +297,15 @@ struct Ptrs {
 // ---------------------------------------------------------------------------
 // launch helpers
 // ---------------------------------------------------------------------------
+int experts_per_lane(int num_experts) {
+    return num_experts <= 32 ? 1 : num_experts <= 64 ? 2 : num_experts <= 128 ? 4 : 8;
+}
+
+// Launches the logit kernel and (unless `out_params` is given, in which case
+// the parameters are returned for the fused select + plan kernel) the select kernel.
 template <typename T>
 int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool prerouted,
-                 int32_t* topk_idx, float* topk_w, bool zero_acc) {
+                 int32_t* topk_idx, float* topk_w, bool zero_acc, RouteParams* out_params = nullptr) {
     const ChronosMoeShape& s = a->shape;
     RouteParams rp{};
     rp.x = a->x;
@@ -343,18 +350,45 @@ int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool p
                                              false, rp));
         }
     }
+    if (out_params != nullptr) {  // the caller launches the fused select + plan kernel
+        *out_params = rp;
+        return CHRONOS_OK;
+    }
     const unsigned sgrid = static_cast<unsigned>((N + kSelectThreads / 32 - 1) / (kSelectThreads / 32));
-    CHRONOS_CUDA_CHECK(launch_kernel(route_select_kernel<T>, dim3(sgrid), dim3(kSelectThreads), 0, st,
-                                     !prerouted, rp));
+    const dim3 g(sgrid), b(kSelectThreads);
+    const int epl = experts_per_lane(s.num_experts);
+    cudaError_t err;
+    switch (epl) {
+        case 1: err = launch_kernel(route_select_kernel<T, 1>, g, b, 0, st, !prerouted, rp); break;
+        case 2: err = launch_kernel(route_select_kernel<T, 2>, g, b, 0, st, !prerouted, rp); break;
+        case 4: err = launch_kernel(route_select_kernel<T, 4>, g, b, 0, st, !prerouted, rp); break;
+        default: err = launch_kernel(route_select_kernel<T, 8>, g, b, 0, st, !prerouted, rp); break;
+    }
+    CHRONOS_CUDA_CHECK(err);
     return CHRONOS_OK;
 }
 
-template <typename T, int BN, bool GATEUP, bool SPLIT>
+template <typename T>
+int launch_select_plan(const RouteParams& rp, const PlanParams& pp, const ScatterParams& sp, int num_experts,
+                       bool pdl, cudaStream_t st) {
+    const dim3 g(1), b(kSelectPlanThreads);
+    cudaError_t err;
+    switch (experts_per_lane(num_experts)) {
+        case 1: err = launch_kernel(route_select_plan_kernel<T, 1>, g, b, 0, st, pdl, rp, pp, sp); break;
+        case 2: err = launch_kernel(route_select_plan_kernel<T, 2>, g, b, 0, st, pdl, rp, pp, sp); break;
+        case 4: err = launch_kernel(route_select_plan_kernel<T, 4>, g, b, 0, st, pdl, rp, pp, sp); break;
+        default: err = launch_kernel(route_select_plan_kernel<T, 8>, g, b, 0, st, pdl, rp, pp, sp); break;
+    }
+    CHRONOS_CUDA_CHECK(err);
+    return CHRONOS_OK;
+}
+
+template <typename T, int BN, bool GATEUP, bool SPLIT, bool DENSE = false>
 int launch_tc(const CUtensorMap& a0r, const CUtensorMap& a1r, const CUtensorMap& a0s,
               const CUtensorMap& a1s, const CUtensorMap& br, const CUtensorMap& bs,
               const TcGemmParams& p, int grid, cudaStream_t st) {
     constexpr int smem = tc_smem_bytes(BN, GATEUP, SPLIT);
-    auto kern = tc_grouped_gemm<T, BN, GATEUP, SPLIT>;
+    auto kern = tc_grouped_gemm<T, BN, GATEUP, SPLIT, DENSE>;
     if (int rc = set_smem(kern, smem)) return rc;
     CHRONOS_CUDA_CHECK(launch_kernel(kern, dim3(grid), dim3(kTcThreads), smem, st, true, a0r, a1r, a0s,
                                      a1s, br, bs, p));
@@ -383,8 +417,15 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
         u_s = u_r;
         d_s = d_r;
     }
-    if ((rc = make_map(&xp_m, w.ws + w.L->xp, N * K, H, BN, dt))) return rc;
+    // decode tiles (BN >= N): every group's B operand is x itself (DENSE), no
+    // expert-ordered copy of x exists
+    constexpr bool kDense = BN <= kSelectPlanMaxTokens;
     if ((rc = make_map(&x_m, a->x, N, H, BN, dt))) return rc;
+    if (kDense) {
+        xp_m = x_m;
+    } else if ((rc = make_map(&xp_m, w.ws + w.L->xp, N * K, H, BN, dt))) {
+        return rc;
+    }
     if ((rc = make_map(&h_m, w.ws + w.L->hid, slots, F, BN_DN, dt))) return rc;
 
     TcGemmParams p{};
@@ -406,6 +447,8 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     p.ready_limit_ns = a->spin_limit_ns > 0 ? static_cast<uint64_t>(a->spin_limit_ns)
                                             : 2000000000ull;
     p.status = a->status;
+    p.slot_map = w.at<int32_t>(w.L->slot_map);
+    p.n_tokens = s.num_tokens;
     const int grid = sm_count();
 
     // gate/up
@@ -424,7 +467,7 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
         if constexpr (BN <= kSplitMaxTokens) {
         // (the plan/scatter kernel zeroed the fp32 partial buffer `gu`)
         prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
-        if ((rc = launch_tc<T, BN, true, true>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st)))
+        if ((rc = launch_tc<T, BN, true, true, kDense>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st)))
             return rc;
         prof_ran(slot, CHRONOS_STAGE_GATEUP);
         prof_mark(slot, CHRONOS_STAGE_ACT, st);
@@ -443,7 +486,7 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
         }
     } else {
         prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
-        if ((rc = launch_tc<T, BN, true, false>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st)))
+        if ((rc = launch_tc<T, BN, true, false, kDense>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st)))
             return rc;
         prof_ran(slot, CHRONOS_STAGE_GATEUP);
         prof_mark(slot, CHRONOS_STAGE_ACT, st);
@@ -600,8 +643,12 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     if (prerouted)
         CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + L.grp_count, 0, 4 * s.num_experts, st));
     const int slot = prof_begin_call();
+    // decode batches: the routing selection, plan and slot tables run in one block
+    const bool fused_plan = N <= kSelectPlanMaxTokens;
+    RouteParams rp{};
     prof_mark(slot, CHRONOS_STAGE_ROUTE, st);
-    if ((rc = launch_route<T>(a, w, st, prerouted, topk_idx, topk_w, true))) return rc;
+    if ((rc = launch_route<T>(a, w, st, prerouted, topk_idx, topk_w, true, fused_plan ? &rp : nullptr)))
+        return rc;
     prof_ran(slot, CHRONOS_STAGE_ROUTE);
     prof_mark(slot, CHRONOS_STAGE_PLAN, st);
 
@@ -649,7 +696,13 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
         sp.zero = reinterpret_cast<float4*>(w.ws + L.gu);
         sp.zero_count4 = static_cast<int64_t>((N * s.top_k + s.num_shared * N) * 2 * s.ffn / 4);
     }
-    {
+    if (fused_plan) {
+        sp.copy_rows = 0;
+        sp.slot_map = tc ? w.at<int32_t>(L.slot_map) : nullptr;
+        sp.e = s.num_experts;
+        // first launch of the call when routing was skipped (pre-routed inputs)
+        if ((rc = launch_select_plan<T>(rp, pp, sp, s.num_experts, !prerouted, st))) return rc;
+    } else {
         const int64_t warps = N * s.top_k;
         const unsigned blocks =
             static_cast<unsigned>(std::max<int64_t>(1, (warps + kScatterWarps - 1) / kScatterWarps));

@@ -61,6 +61,10 @@ struct TcGemmParams {
     int32_t ready_epoch;
     uint64_t ready_limit_ns;
     int32_t* status;
+    // DENSE gate/up (decode batches, N <= BN): slot of (expert, token), -1 if
+    // the token did not choose the expert (or it is unavailable); [E, n_tokens]
+    const int32_t* slot_map;
+    int64_t n_tokens;
 };
 
 __host__ __device__ constexpr int tc_stage_bytes(int bn, bool gateup) {
@@ -118,7 +122,7 @@ __device__ __forceinline__ TcUnit tc_decode(const TcGemmParams& p, int num_activ
     return r;
 }
 
-template <typename T, int BN, bool GATEUP, bool SPLIT>
+template <typename T, int BN, bool GATEUP, bool SPLIT, bool DENSE = false>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_grouped_gemm(const __grid_constant__ CUtensorMap tm_a0r,  // routed gate (or down)
                     const __grid_constant__ CUtensorMap tm_a1r,  // routed up
@@ -215,7 +219,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int kt1 = min(p.k_tiles, kt0 + p.kt_per_split);
                 const CUtensorMap* ma0 = shared ? &tm_a0s : &tm_a0r;
                 const CUtensorMap* ma1 = shared ? &tm_a1s : &tm_a1r;
-                const CUtensorMap* mb = (GATEUP && shared) ? &tm_bs : &tm_br;
+                // DENSE: every group's B tile is x rows [0, BN) (all N <= BN tokens);
+                // the epilogue keeps the columns of the tokens routed to the group
+                const CUtensorMap* mb = ((GATEUP && shared) || DENSE) ? &tm_bs : &tm_br;
+                const int b_row_eff = DENSE ? 0 : b_row;
                 for (int kt = kt0; kt < kt1; ++kt) {
                     if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, kPipelineLimitNs, abort_flag)) {
                         *abort_flag = 1;
@@ -226,7 +233,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
                     tma_load_2d(sb, ma0, &full[stage], kt * kTcBK, a_row);
                     if (GATEUP) tma_load_2d(sb + A_BYTES, ma1, &full[stage], kt * kTcBK, a_row);
-                    tma_load_2d(sb + (GATEUP ? 2 : 1) * A_BYTES, mb, &full[stage], kt * kTcBK, b_row);
+                    tma_load_2d(sb + (GATEUP ? 2 : 1) * A_BYTES, mb, &full[stage], kt * kTcBK, b_row_eff);
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
             }
@@ -293,6 +300,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int u = blockIdx.x; u < total; u += gridDim.x) {
             const TcUnit w = tc_decode(p, num_active, u, BN, splits_unused);
             const int rows = p.act_rows[w.a];
+            const int eid = p.act_eid[w.a];
             const int tok0 = w.tok_tile * BN;
             const int64_t hrow0 = p.act_hrow[w.a];
             float* cf = s_coef + acc * BN;
@@ -372,8 +380,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 epilogue_bar_sync(128);
                 for (int r = et; r < SUB; r += 128) {
                     const int tok = tok0 + c0 + r;
-                    if (tok >= rows) continue;
-                    const int64_t slot = hrow0 + tok;
+                    int64_t slot;
+                    if constexpr (DENSE) {
+                        // column = token id; keep it only if the token chose this group
+                        if (tok >= p.n_tokens) continue;
+                        slot = eid < 0 ? hrow0 + tok : p.slot_map[static_cast<int64_t>(eid) * p.n_tokens + tok];
+                        if (slot < 0) continue;
+                    } else {
+                        if (tok >= rows) continue;
+                        slot = hrow0 + tok;
+                    }
                     const uint8_t* row = staging + r * ROW_BYTES;
                     if constexpr (GATEUP) {
                         if constexpr (SPLIT) {

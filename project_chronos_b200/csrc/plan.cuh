@@ -14,6 +14,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "router.cuh"
 
 namespace chronos {
 
@@ -50,8 +51,9 @@ struct PlanParams {
 
 constexpr int kPlanThreads = 256;  // >= the 256 experts the ABI accepts: one expert per thread
 
-// Inclusive scan over the block (kPlanThreads values), warp shuffles + one
-// pass over the warp totals.  `scratch` holds kPlanThreads / 32 ints.
+// Inclusive scan over the block (NT values, NT = blockDim.x), warp shuffles +
+// one pass over the warp totals.  `scratch` holds NT / 32 ints.
+template <int NT = kPlanThreads>
 __device__ __forceinline__ int block_inclusive_scan(int v, int* scratch) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -62,13 +64,13 @@ __device__ __forceinline__ int block_inclusive_scan(int v, int* scratch) {
     if (lane == 31) scratch[warp] = v;
     __syncthreads();
     if (warp == 0) {
-        int s = lane < kPlanThreads / 32 ? scratch[lane] : 0;
+        int s = lane < NT / 32 ? scratch[lane] : 0;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const int n = __shfl_up_sync(0xffffffffu, s, o);
             if (lane >= o) s += n;
         }
-        if (lane < kPlanThreads / 32) scratch[lane] = s;
+        if (lane < NT / 32) scratch[lane] = s;
     }
     __syncthreads();
     if (warp > 0) v += scratch[warp - 1];
@@ -76,8 +78,10 @@ __device__ __forceinline__ int block_inclusive_scan(int v, int* scratch) {
     return v;
 }
 
-// The plan tables (active groups, unit prefixes, header); called by one block.
-// `cnt` / `inc_cnt`: this thread's expert group size and its inclusive scan.
+// The plan tables (active groups, unit prefixes, header); called by one block
+// of NT threads.  `cnt` / `inc_cnt`: this thread's expert group size and its
+// inclusive scan.
+template <int NT = kPlanThreads>
 __device__ __forceinline__ void plan_tables(const PlanParams& p, int cnt, int inc_cnt, int* s_scratch,
                                             int* s_tot) {
     const int tid = threadIdx.x;
@@ -89,10 +93,10 @@ __device__ __forceinline__ void plan_tables(const PlanParams& p, int cnt, int in
     const int tt_dn = (cnt + p.tok_tile_dn - 1) / p.tok_tile_dn;
     const int ugu = is_act ? tt * p.mt_gu * p.splits_gu : 0;
     const int udn = is_act ? tt_dn * p.mt_dn * p.splits_dn : 0;
-    const int inc_act = block_inclusive_scan(is_act, s_scratch);
-    const int inc_gu = block_inclusive_scan(ugu, s_scratch);
-    const int inc_dn = block_inclusive_scan(udn, s_scratch);
-    if (tid == kPlanThreads - 1) {
+    const int inc_act = block_inclusive_scan<NT>(is_act, s_scratch);
+    const int inc_gu = block_inclusive_scan<NT>(ugu, s_scratch);
+    const int inc_dn = block_inclusive_scan<NT>(udn, s_scratch);
+    if (tid == NT - 1) {
         s_tot[0] = inc_cnt;
         s_tot[1] = inc_act;
         s_tot[2] = inc_gu;
@@ -156,6 +160,8 @@ struct ScatterParams {
     int copy_rows;        // 0: only the slot tables (B operand read from x by row index)
     float4* zero;         // buffer the next kernel accumulates into (split-K partials), or null
     int64_t zero_count4;  // its size in float4
+    int32_t* slot_map;    // decode batches: [E, N] slot of (expert, token) or -1
+    int e;                // experts (rows of slot_map)
 };
 
 constexpr int kScatterThreads = kPlanThreads;
@@ -224,6 +230,77 @@ __global__ void __launch_bounds__(kScatterThreads) plan_scatter_kernel(PlanParam
         for (; i < n16; i += 32) d4[i] = s4[i];
     } else {
         for (int i = lane; i < p.h; i += 32) dst[i] = src[i];
+    }
+}
+
+// Decode batches (<= kSelectPlanMaxTokens tokens): routing selection, plan and
+// slot tables in ONE block.  Positions inside the expert groups come from
+// shared-memory atomics, the group offsets from a block scan, and nothing is
+// copied: the gate/up GEMM gathers the token rows of x itself.  Replaces the
+// select + plan/scatter launches of larger batches.
+constexpr int kSelectPlanThreads = 1024;
+constexpr int kSelectPlanMaxTokens = 64;
+
+template <typename T, int EPL>
+__global__ void __launch_bounds__(kSelectPlanThreads)
+    route_select_plan_kernel(RouteParams rp, PlanParams pp, ScatterParams sp) {
+    __shared__ int s_count[kMaxExperts];
+    __shared__ int s_off[kMaxExperts];
+    __shared__ int s_scratch[kSelectPlanThreads / 32];
+    __shared__ int s_tot[4];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    pdl_trigger();
+    if (sp.zero != nullptr)  // split-K partial buffer: independent of the routing
+        for (int64_t i = tid; i < sp.zero_count4; i += kSelectPlanThreads)
+            sp.zero[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (sp.slot_map != nullptr)
+        for (int64_t i = tid; i < static_cast<int64_t>(sp.e) * sp.n; i += kSelectPlanThreads) sp.slot_map[i] = -1;
+    if (tid < kMaxExperts) s_count[tid] = 0;
+    __syncthreads();
+    pdl_wait();  // chunk partials from the logit kernel
+
+    // 1) one warp per token: select, position within the expert group
+    const int k = rp.k;
+    for (int64_t t = warp; t < rp.n; t += kSelectPlanThreads / 32) {
+        if (rp.y_acc != nullptr) {
+            float4* yv = reinterpret_cast<float4*>(rp.y_acc + t * rp.h);
+            for (int i = lane; i < rp.h / 4; i += 32) yv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        int mine_e;
+        float mine_w, mine_a, shared_extra;
+        select_token<T, EPL>(rp, t, lane, mine_e, mine_w, mine_a, shared_extra);
+        if (lane < k) rp.pos[t * k + lane] = mine_a > 0.0f ? atomicAdd(&s_count[mine_e], 1) : -1;
+        if (lane == 0 && rp.num_shared > 0)
+            rp.shared_coef[t] = (1.0f + shared_extra) / static_cast<float>(rp.num_shared);
+    }
+    __syncthreads();
+
+    // 2) plan: group offsets and the GEMM work tables
+    const int cnt = tid < pp.e ? s_count[tid] : 0;
+    const int inc = block_inclusive_scan<kSelectPlanThreads>(cnt, s_scratch);
+    if (tid < pp.e) s_off[tid] = inc - cnt;
+    plan_tables<kSelectPlanThreads>(pp, cnt, inc, s_scratch, s_tot);
+    __syncthreads();
+
+    // 3) slot tables, one thread per (token, choice)
+    const int64_t total = rp.n * k;
+    for (int64_t i = tid; i < total; i += kSelectPlanThreads) {
+        const int64_t t = i / k;
+        const int j = static_cast<int>(i % k);
+        if (j == 0) {
+            for (int s = 0; s < sp.num_shared; ++s) {
+                const int64_t slot = sp.n * k + s * sp.n + t;
+                sp.slot_tok[slot] = static_cast<int32_t>(t);
+                sp.slot_coef[slot] = rp.shared_coef[t];
+            }
+        }
+        const int ps = rp.pos[i];
+        if (ps < 0) continue;
+        const int e = rp.topk_idx[i];
+        const int64_t slot = static_cast<int64_t>(s_off[e]) + ps;
+        sp.slot_tok[slot] = static_cast<int32_t>(t);
+        sp.slot_coef[slot] = rp.sel_coef[i];
+        if (sp.slot_map != nullptr) sp.slot_map[static_cast<int64_t>(e) * sp.n + t] = static_cast<int32_t>(slot);
     }
 }
 

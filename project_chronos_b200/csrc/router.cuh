@@ -297,25 +297,21 @@ __device__ __forceinline__ float expert_avail(const RouteParams& p, int e) {
     return a;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParams p) {
-    pdl_trigger();
-    pdl_wait();  // partials and zeroed counters from the logit kernel
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t t = static_cast<int64_t>(blockIdx.x) * (kSelectThreads / 32) + warp;
-    if (t >= p.n) return;
-    const int E = p.e, H = p.h;
-
-    if (p.y_acc != nullptr) {
-        float4* yv = reinterpret_cast<float4*>(p.y_acc + t * H);
-        for (int i = lane; i < H / 4; i += 32) yv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-
+// Finish one token's routing (one warp): logits from the chunk partials in
+// chunk order (+ bias), softmax, top-k by (logit desc, index asc), optional
+// renormalisation; or, with pre-routed inputs, read the given top-k.  Lane
+// j < k returns choice j (expert, weight, availability) and has written its
+// top-k outputs; every lane returns the token's shared-expert extra weight
+// sum_k w (1 - a).  EPL = experts per lane (E <= 32 * EPL).
+template <typename T, int EPL>
+__device__ __forceinline__ void select_token(const RouteParams& p, int64_t t, int lane, int& mine_e,
+                                             float& mine_w, float& mine_a, float& shared_extra) {
+    const int E = p.e;
+    mine_e = 0;
+    mine_w = 0.0f;
+    mine_a = 0.0f;
+    shared_extra = 0.0f;
     if (p.prerouted) {
-        // weights and indices come from an earlier routing call; lane j owns choice j
-        float shared_extra = 0.0f;
-        float mine_w = 0.0f, mine_a = 0.0f;
-        int mine_e = 0;
         for (int j = 0; j < p.k; ++j) {
             const int e = p.topk_idx[t * p.k + j];
             const float wt = p.topk_w[t * p.k + j];
@@ -327,24 +323,17 @@ __global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParam
                 mine_a = a;
             }
         }
-        if (lane < p.k) {
-            p.sel_coef[t * p.k + lane] = mine_w * mine_a;
-            p.pos[t * p.k + lane] = mine_a > 0.0f ? atomicAdd(&p.grp_count[mine_e], 1) : -1;
-        }
-        if (lane == 0 && p.num_shared > 0)
-            p.shared_coef[t] = (1.0f + shared_extra) / static_cast<float>(p.num_shared);
+        if (lane < p.k) p.sel_coef[t * p.k + lane] = mine_w * mine_a;
         return;
     }
-
-    const int per_lane = (E + 31) / 32;
     const int C = p.nchunks;
-    float v[kMaxExperts / 32];
+    float v[EPL];
     float m = -INFINITY;
 #pragma unroll
-    for (int q = 0; q < kMaxExperts / 32; ++q) {
+    for (int q = 0; q < EPL; ++q) {
         const int e = lane + 32 * q;
         float lg = -INFINITY;
-        if (q < per_lane && e < E) {
+        if (e < E) {
             const float* pp = p.partials + (t * E + e) * C;
             float s = 0.0f;
             int c = 0;
@@ -352,9 +341,10 @@ __global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParam
             for (; c + 16 <= C; c += 16) {
                 float4 r[4];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) r[u] = (C % 4 == 0) ? reinterpret_cast<const float4*>(pp + c)[u]
-                                                               : make_float4(pp[c + 4 * u], pp[c + 4 * u + 1],
-                                                                             pp[c + 4 * u + 2], pp[c + 4 * u + 3]);
+                for (int u = 0; u < 4; ++u)
+                    r[u] = (C % 4 == 0) ? reinterpret_cast<const float4*>(pp + c)[u]
+                                        : make_float4(pp[c + 4 * u], pp[c + 4 * u + 1], pp[c + 4 * u + 2],
+                                                      pp[c + 4 * u + 3]);
 #pragma unroll
                 for (int u = 0; u < 4; ++u) s = ((s + r[u].x) + r[u].y + r[u].z) + r[u].w;
             }
@@ -368,11 +358,10 @@ __global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParam
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float s = 0.0f;
-    float ex[kMaxExperts / 32];
+    float ex[EPL];
 #pragma unroll
-    for (int q = 0; q < kMaxExperts / 32; ++q) {
-        const int e = lane + 32 * q;
-        ex[q] = (q < per_lane && e < E) ? __expf(v[q] - m) : 0.0f;
+    for (int q = 0; q < EPL; ++q) {
+        ex[q] = (lane + 32 * q < E) ? __expf(v[q] - m) : 0.0f;
         s += ex[q];
     }
 #pragma unroll
@@ -381,23 +370,21 @@ __global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParam
     if (p.probs) {
         T* pr = static_cast<T*>(p.probs);
 #pragma unroll
-        for (int q = 0; q < kMaxExperts / 32; ++q) {
+        for (int q = 0; q < EPL; ++q) {
             const int e = lane + 32 * q;
-            if (q < per_lane && e < E) pr[t * E + e] = from_f32<T>(ex[q] * inv);
+            if (e < E) pr[t * E + e] = from_f32<T>(ex[q] * inv);
         }
     }
-    // top-k by (logit desc, index asc)
+    // top-k by (logit desc, index asc); lane j keeps choice j
     unsigned taken = 0u;  // bit q: v[q] already chosen
-    float wsel[kMaxTopK];
-    int isel[kMaxTopK];
     float wsum = 0.0f;
     for (int j = 0; j < p.k; ++j) {
         float bv = -INFINITY;
         int bi = 0x7fffffff;
 #pragma unroll
-        for (int q = 0; q < kMaxExperts / 32; ++q) {
+        for (int q = 0; q < EPL; ++q) {
             const int e = lane + 32 * q;
-            if (q < per_lane && e < E && !((taken >> q) & 1u)) {
+            if (e < E && !((taken >> q) & 1u)) {
                 if (v[q] > bv || (v[q] == bv && e < bi)) {
                     bv = v[q];
                     bi = e;
@@ -418,9 +405,9 @@ __global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParam
             // every access stays in bounds; routing of NaN rows is unspecified
             int lo = 0x7fffffff;
 #pragma unroll
-            for (int q = 0; q < kMaxExperts / 32; ++q) {
+            for (int q = 0; q < EPL; ++q) {
                 const int e = lane + 32 * q;
-                if (q < per_lane && e < E && !((taken >> q) & 1u)) lo = min(lo, e);
+                if (e < E && !((taken >> q) & 1u)) lo = min(lo, e);
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
@@ -430,40 +417,48 @@ __global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParam
         // probability of the chosen expert, broadcast from its owner lane
         float pe = 0.0f;
 #pragma unroll
-        for (int q = 0; q < kMaxExperts / 32; ++q)
+        for (int q = 0; q < EPL; ++q)
             if ((bi >> 5) == q) pe = ex[q] * inv;
         pe = __shfl_sync(0xffffffffu, pe, bi & 31);
-        wsel[j] = pe;
-        isel[j] = bi;
+        if (lane == j) {
+            mine_e = bi;
+            mine_w = pe;
+        }
         wsum += pe;
     }
-    if (p.norm_topk) {
-        const float d = wsum + 1e-20f;
-        for (int j = 0; j < p.k; ++j) wsel[j] = wsel[j] / d;
-    }
-    // lane j < k owns choice j: its stores and returning atomic run in parallel
-    float mine_w = 0.0f, mine_a = 0.0f;
-    int mine_e = 0;
-    float shared_extra = 0.0f;
-    for (int j = 0; j < p.k; ++j) {
-        const int e = isel[j];
-        const float a = expert_avail(p, e);
-        shared_extra += wsel[j] * (1.0f - a);
-        if (lane == j) {
-            mine_e = e;
-            mine_w = wsel[j];
-            mine_a = a;
-        }
-    }
+    if (p.norm_topk) mine_w = mine_w / (wsum + 1e-20f);
+    if (lane < p.k) mine_a = expert_avail(p, mine_e);
+    float extra = lane < p.k ? mine_w * (1.0f - mine_a) : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) extra += __shfl_xor_sync(0xffffffffu, extra, o);
+    shared_extra = extra;
     if (lane < p.k) {
         const int64_t o = t * p.k + lane;
         p.topk_idx[o] = mine_e;
         p.topk_w[o] = mine_w;
         p.sel_coef[o] = mine_w * mine_a;
-        p.pos[o] = mine_a > 0.0f ? atomicAdd(&p.grp_count[mine_e], 1) : -1;
         if (p.counts_all) atomicAdd(&p.counts_all[mine_e], 1);
         if (p.mass_all) atomicAdd(&p.mass_all[mine_e], mine_w);
     }
+}
+
+// One warp per token: select, then a global atomic gives each available
+// selection its position in its expert group.
+template <typename T, int EPL>
+__global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParams p) {
+    pdl_trigger();
+    pdl_wait();  // partials and zeroed counters from the logit kernel
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * (kSelectThreads / 32) + warp;
+    if (t >= p.n) return;
+    if (p.y_acc != nullptr) {
+        float4* yv = reinterpret_cast<float4*>(p.y_acc + t * p.h);
+        for (int i = lane; i < p.h / 4; i += 32) yv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    int mine_e;
+    float mine_w, mine_a, shared_extra;
+    select_token<T, EPL>(p, t, lane, mine_e, mine_w, mine_a, shared_extra);
+    if (lane < p.k) p.pos[t * p.k + lane] = mine_a > 0.0f ? atomicAdd(&p.grp_count[mine_e], 1) : -1;
     if (lane == 0 && p.num_shared > 0)
         p.shared_coef[t] = (1.0f + shared_extra) / static_cast<float>(p.num_shared);
 }
