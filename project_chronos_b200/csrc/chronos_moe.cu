@@ -128,7 +128,7 @@ Layout make_layout(const ChronosMoeShape& s) {
         off = align_up(off + bytes, 256);
         return o;
     };
-    L.grp_count = take(4 * E);
+    L.grp_count = take(4 * (E + 1));  // + the ticket of the decode select + plan kernel
     L.grp_off = take(4 * E);
     L.act_rows = take(4 * G);
     L.act_xrow = take(4 * G);
@@ -371,13 +371,14 @@ int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool p
 template <typename T>
 int launch_select_plan(const RouteParams& rp, const PlanParams& pp, const ScatterParams& sp, int num_experts,
                        bool pdl, cudaStream_t st) {
-    const dim3 g(1), b(kSelectPlanThreads);
+    const dim3 g(static_cast<unsigned>((rp.n + kSelectPlanWarps - 1) / kSelectPlanWarps)), b(kSelectPlanThreads);
+    int32_t* ticket = rp.grp_count + num_experts;
     cudaError_t err;
     switch (experts_per_lane(num_experts)) {
-        case 1: err = launch_kernel(route_select_plan_kernel<T, 1>, g, b, 0, st, pdl, rp, pp, sp); break;
-        case 2: err = launch_kernel(route_select_plan_kernel<T, 2>, g, b, 0, st, pdl, rp, pp, sp); break;
-        case 4: err = launch_kernel(route_select_plan_kernel<T, 4>, g, b, 0, st, pdl, rp, pp, sp); break;
-        default: err = launch_kernel(route_select_plan_kernel<T, 8>, g, b, 0, st, pdl, rp, pp, sp); break;
+        case 1: err = launch_kernel(route_select_plan_kernel<T, 1>, g, b, 0, st, pdl, rp, pp, sp, ticket); break;
+        case 2: err = launch_kernel(route_select_plan_kernel<T, 2>, g, b, 0, st, pdl, rp, pp, sp, ticket); break;
+        case 4: err = launch_kernel(route_select_plan_kernel<T, 4>, g, b, 0, st, pdl, rp, pp, sp, ticket); break;
+        default: err = launch_kernel(route_select_plan_kernel<T, 8>, g, b, 0, st, pdl, rp, pp, sp, ticket); break;
     }
     CHRONOS_CUDA_CHECK(err);
     return CHRONOS_OK;
@@ -641,7 +642,7 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     int rc;
     // counters: zeroed by the logit kernel, or here when routing is skipped
     if (prerouted)
-        CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + L.grp_count, 0, 4 * s.num_experts, st));
+        CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + L.grp_count, 0, 4 * (s.num_experts + 1), st));
     const int slot = prof_begin_call();
     // decode batches: the routing selection, plan and slot tables run in one block
     const bool fused_plan = N <= kSelectPlanMaxTokens;

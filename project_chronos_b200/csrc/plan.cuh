@@ -234,34 +234,38 @@ __global__ void __launch_bounds__(kScatterThreads) plan_scatter_kernel(PlanParam
 }
 
 // Decode batches (<= kSelectPlanMaxTokens tokens): routing selection, plan and
-// slot tables in ONE block.  Positions inside the expert groups come from
-// shared-memory atomics, the group offsets from a block scan, and nothing is
-// copied: the gate/up GEMM gathers the token rows of x itself.  Replaces the
-// select + plan/scatter launches of larger batches.
-constexpr int kSelectPlanThreads = 1024;
+// slot tables in ONE launch.  One warp per token selects (blocks of 8 tokens,
+// so a 64-token batch selects on 8 SMs), a global atomic gives each available
+// selection its position in its expert group, and the last block to finish
+// (a ticket counter, zeroed with the group counters) scans the group sizes and
+// writes the plan and slot tables plus the (expert, token) -> slot map.
+// Nothing is copied: the gate/up GEMM reads the token rows of x itself.
+// Replaces the select + plan/scatter launches of larger batches.
+constexpr int kSelectPlanThreads = kPlanThreads;
+constexpr int kSelectPlanWarps = kSelectPlanThreads / 32;
 constexpr int kSelectPlanMaxTokens = 64;
 
 template <typename T, int EPL>
 __global__ void __launch_bounds__(kSelectPlanThreads)
-    route_select_plan_kernel(RouteParams rp, PlanParams pp, ScatterParams sp) {
-    __shared__ int s_count[kMaxExperts];
+    route_select_plan_kernel(RouteParams rp, PlanParams pp, ScatterParams sp, int32_t* ticket) {
     __shared__ int s_off[kMaxExperts];
-    __shared__ int s_scratch[kSelectPlanThreads / 32];
+    __shared__ int s_scratch[kSelectPlanWarps];
     __shared__ int s_tot[4];
+    __shared__ int s_last;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t gtid = static_cast<int64_t>(blockIdx.x) * kSelectPlanThreads + tid;
+    const int64_t gthreads = static_cast<int64_t>(gridDim.x) * kSelectPlanThreads;
     pdl_trigger();
     if (sp.zero != nullptr)  // split-K partial buffer: independent of the routing
-        for (int64_t i = tid; i < sp.zero_count4; i += kSelectPlanThreads)
-            sp.zero[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int64_t i = gtid; i < sp.zero_count4; i += gthreads) sp.zero[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (sp.slot_map != nullptr)
-        for (int64_t i = tid; i < static_cast<int64_t>(sp.e) * sp.n; i += kSelectPlanThreads) sp.slot_map[i] = -1;
-    if (tid < kMaxExperts) s_count[tid] = 0;
-    __syncthreads();
-    pdl_wait();  // chunk partials from the logit kernel
+        for (int64_t i = gtid; i < static_cast<int64_t>(sp.e) * sp.n; i += gthreads) sp.slot_map[i] = -1;
+    pdl_wait();  // chunk partials and zeroed counters from the logit kernel
 
     // 1) one warp per token: select, position within the expert group
     const int k = rp.k;
-    for (int64_t t = warp; t < rp.n; t += kSelectPlanThreads / 32) {
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * kSelectPlanWarps + warp;
+    if (t < rp.n) {
         if (rp.y_acc != nullptr) {
             float4* yv = reinterpret_cast<float4*>(rp.y_acc + t * rp.h);
             for (int i = lane; i < rp.h / 4; i += 32) yv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -269,38 +273,47 @@ __global__ void __launch_bounds__(kSelectPlanThreads)
         int mine_e;
         float mine_w, mine_a, shared_extra;
         select_token<T, EPL>(rp, t, lane, mine_e, mine_w, mine_a, shared_extra);
-        if (lane < k) rp.pos[t * k + lane] = mine_a > 0.0f ? atomicAdd(&s_count[mine_e], 1) : -1;
+        if (lane < k) rp.pos[t * k + lane] = mine_a > 0.0f ? atomicAdd(&rp.grp_count[mine_e], 1) : -1;
         if (lane == 0 && rp.num_shared > 0)
             rp.shared_coef[t] = (1.0f + shared_extra) / static_cast<float>(rp.num_shared);
     }
-    __syncthreads();
 
-    // 2) plan: group offsets and the GEMM work tables
-    const int cnt = tid < pp.e ? s_count[tid] : 0;
+    // 2) the last block to arrive sees every block's counts and tables
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(ticket, 1) == static_cast<int>(gridDim.x) - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+
+    // 3) plan: group offsets and the GEMM work tables
+    const int cnt = tid < pp.e ? __ldcg(rp.grp_count + tid) : 0;
     const int inc = block_inclusive_scan<kSelectPlanThreads>(cnt, s_scratch);
     if (tid < pp.e) s_off[tid] = inc - cnt;
     plan_tables<kSelectPlanThreads>(pp, cnt, inc, s_scratch, s_tot);
     __syncthreads();
 
-    // 3) slot tables, one thread per (token, choice)
+    // 4) slot tables, one thread per (token, choice)
     const int64_t total = rp.n * k;
     for (int64_t i = tid; i < total; i += kSelectPlanThreads) {
-        const int64_t t = i / k;
+        const int64_t tt = i / k;
         const int j = static_cast<int>(i % k);
-        if (j == 0) {
-            for (int s = 0; s < sp.num_shared; ++s) {
-                const int64_t slot = sp.n * k + s * sp.n + t;
-                sp.slot_tok[slot] = static_cast<int32_t>(t);
-                sp.slot_coef[slot] = rp.shared_coef[t];
+        const int ps = __ldcg(rp.pos + i);
+        const int e = __ldcg(rp.topk_idx + i);
+        const float c = __ldcg(rp.sel_coef + i);
+        if (j == 0 && sp.num_shared > 0) {
+            const float sc = __ldcg(rp.shared_coef + tt);
+            for (int q = 0; q < sp.num_shared; ++q) {
+                const int64_t slot = sp.n * k + q * sp.n + tt;
+                sp.slot_tok[slot] = static_cast<int32_t>(tt);
+                sp.slot_coef[slot] = sc;
             }
         }
-        const int ps = rp.pos[i];
         if (ps < 0) continue;
-        const int e = rp.topk_idx[i];
         const int64_t slot = static_cast<int64_t>(s_off[e]) + ps;
-        sp.slot_tok[slot] = static_cast<int32_t>(t);
-        sp.slot_coef[slot] = rp.sel_coef[i];
-        if (sp.slot_map != nullptr) sp.slot_map[static_cast<int64_t>(e) * sp.n + t] = static_cast<int32_t>(slot);
+        sp.slot_tok[slot] = static_cast<int32_t>(tt);
+        sp.slot_coef[slot] = c;
+        if (sp.slot_map != nullptr) sp.slot_map[static_cast<int64_t>(e) * sp.n + tt] = static_cast<int32_t>(slot);
     }
 }
 

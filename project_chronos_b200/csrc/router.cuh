@@ -48,7 +48,7 @@ struct RouteParams {
     float* topk_w;        // [N, k]
     int32_t* counts_all;  // [E] or null
     float* mass_all;      // [E] or null
-    int32_t* grp_count;   // [E] routed-group sizes (selections with a > 0); zeroed by the caller
+    int32_t* grp_count;   // [E + 1] routed-group sizes (selections with a > 0), then a ticket counter
     int32_t* pos;         // [N, k] position within the expert group, -1 when a == 0
     float* sel_coef;      // [N, k] w * a
     float* shared_coef;   // [N] (1 + sum w (1 - a)) / S_h
@@ -59,6 +59,7 @@ struct RouteParams {
 // per-call counters (group sizes and the optional per-expert statistics) that
 // the select kernel, launched after them, accumulates into.
 __device__ __forceinline__ void zero_route_counters(const RouteParams& p) {
+    if (threadIdx.x == 0) p.grp_count[p.e] = 0;  // ticket of the decode select + plan kernel
     for (int i = threadIdx.x; i < p.e; i += blockDim.x) {
         p.grp_count[i] = 0;
         if (p.counts_all) p.counts_all[i] = 0;
