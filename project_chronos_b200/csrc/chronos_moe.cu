@@ -525,6 +525,10 @@ int launch_simt(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int slo
     p.y_acc = w.at<float>(w.L->y_acc);
     p.slot_tok = w.at<int32_t>(w.L->slot_tok);
     p.slot_coef = w.at<float>(w.L->slot_coef);
+    p.ready_flags = a->ready_flags;
+    p.ready_epoch = a->ready_epoch;
+    p.ready_limit_ns = a->spin_limit_ns > 0 ? static_cast<uint64_t>(a->spin_limit_ns) : 2000000000ull;
+    p.status = a->status;
     const int grid = 4 * sm_count();
 
     SimtGemmParams pg = p;

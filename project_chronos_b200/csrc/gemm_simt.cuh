@@ -38,6 +38,11 @@ struct SimtGemmParams {
     float* y_acc;           // DOWN
     const int32_t* slot_tok;
     const float* slot_coef;
+    // expert readiness: wait (bounded) until ready_flags[e] >= ready_epoch
+    const int32_t* ready_flags;
+    int32_t ready_epoch;
+    uint64_t ready_limit_ns;
+    int32_t* status;
 };
 
 template <typename T, bool GATEUP>
@@ -46,6 +51,7 @@ __global__ void __launch_bounds__(kSimtThreads) simt_grouped_gemm(SimtGemmParams
     __shared__ float bs0[kSimtBK][kSimtTile + 4];
     __shared__ float bs1[GATEUP ? kSimtBK : 1][kSimtTile + 4];
     __shared__ int64_t s_arow[kSimtTile];
+    int polled_eid = -1;  // meaningful in thread 0 only
 
     const int tid = threadIdx.x;
     const int tx = tid & 15, ty = tid >> 4;
@@ -73,6 +79,19 @@ __global__ void __launch_bounds__(kSimtThreads) simt_grouped_gemm(SimtGemmParams
         const T* w0 = static_cast<const T*>(shared ? p.w0s : p.w0r) + wslot * p.out_cols * K;
         const T* w1 = GATEUP ? static_cast<const T*>(shared ? p.w1s : p.w1r) + wslot * p.out_cols * K
                              : nullptr;
+        if (tid == 0 && !shared && p.ready_flags != nullptr && p.act_eid[a] != polled_eid) {
+            // wait (bounded) for this selected expert's weights to be resident
+            const int eid = p.act_eid[a];
+            const uint64_t t0 = globaltimer_ns();
+            while (ld_acquire_gpu(p.ready_flags + eid) < p.ready_epoch) {
+                if (globaltimer_ns() - t0 > p.ready_limit_ns) {
+                    report_status(p.status, CHRONOS_ERR_EXPERT_NOT_READY);
+                    break;
+                }
+                __nanosleep(256);
+            }
+            polled_eid = eid;
+        }
         __syncthreads();
         if (tid < kSimtTile) {
             const int tok = tok_tile * kSimtTile + tid;

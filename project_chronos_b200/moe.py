@@ -155,6 +155,8 @@ class ChronosMOEFeedForward(nn.Module):
         self._pool_dirty = True
         self._live_np = None
         self._avail_cache = {}
+        # Slot pools owned by a pooled ExpertStore (attach_expert_pool), or None.
+        self._ext_pool = None
 
     # ------------------------------------------------------------------
     # bookkeeping attributes (lazy: resolved from device tensors on read)
@@ -228,6 +230,32 @@ class ChronosMOEFeedForward(nn.Module):
         m._sync_pool(dev, dt)
         return m
 
+    def attach_expert_pool(self, gate: torch.Tensor, up: torch.Tensor, down: torch.Tensor,
+                           slot_of_expert: torch.Tensor, slot_host: np.ndarray,
+                           ready_flags: Optional[torch.Tensor] = None,
+                           ready_timeout_ns: int = 0) -> None:
+        """Serve the routed experts from slot pools owned by an expert store.
+
+        gate/up ``[P, F, H]``, down ``[P, H, F]``: P resident slots.
+        ``slot_of_expert`` (device int32 ``[E]``) and ``slot_host`` (the store's
+        host copy) map expert -> slot, -1 = not resident.  ``ready_flags``
+        (device int32 ``[E]``, this layer's row) is 1 once the slot's copy of
+        the expert has landed; the GEMMs wait on it for selected experts only.
+        Expert modules stay ``experts[e]`` (live views of their slot, or
+        placeholders), so the reference's residency checks keep working."""
+        self._ext_pool = dict(gate=gate, up=up, down=down, slot=slot_of_expert, slot_host=slot_host)
+        self.expert_ready_flags = ready_flags
+        self.expert_ready_epoch = 1 if ready_flags is not None else 0
+        self.expert_ready_timeout_ns = int(ready_timeout_ns)
+        self._pool_dirty = True
+
+    def detach_expert_pool(self) -> None:
+        self._ext_pool = None
+        self._pool = None
+        self.expert_ready_flags = None
+        self.expert_ready_epoch = 0
+        self._pool_dirty = True
+
     # ------------------------------------------------------------------
     def _apply(self, fn, *args, **kwargs):
         self._pool_dirty = True
@@ -244,8 +272,13 @@ class ChronosMOEFeedForward(nn.Module):
         H = self.config.hidden_size
         Fd = self.config.moe_intermediate_size
         S = len(self.shared_experts)
+        ext = self._ext_pool
+        if ext is not None:
+            self._sync_ext_pool(ext, device, dtype)
+            return
         pool = self._pool
-        if pool is None or pool["gate"].device != device or pool["gate"].dtype != dtype:
+        if pool is None or pool.get("slot") is not None or pool["gate"].device != device \
+                or pool["gate"].dtype != dtype:
             pool = dict(
                 gate=torch.empty(E, Fd, H, device=device, dtype=dtype),
                 up=torch.empty(E, Fd, H, device=device, dtype=dtype),
@@ -279,6 +312,58 @@ class ChronosMOEFeedForward(nn.Module):
         for j, ex in enumerate(self.shared_experts):
             adopt(ex, (("gate_proj", pool["sh_gate"]), ("up_proj", pool["sh_up"]),
                        ("down_proj", pool["sh_down"])), j)
+        self._live_np = live
+        self._avail_cache = {}
+        self._pool_dirty = False
+
+    def _sync_ext_pool(self, ext, device: torch.device, dtype: torch.dtype) -> None:
+        """Pooled-store mode: routed experts live in the store's slots; shared
+        experts are adopted into this layer's own stacked pool."""
+        if ext["gate"].device != device or ext["gate"].dtype != dtype:
+            raise RuntimeError(f"expert slot pool is {ext['gate'].dtype} on {ext['gate'].device}, "
+                               f"input is {dtype} on {device}")
+        E = self.num_experts
+        H = self.config.hidden_size
+        Fd = self.config.moe_intermediate_size
+        S = len(self.shared_experts)
+        old = self._pool or {}
+        sh = old.get("sh_gate")
+        if S and (sh is None or sh.device != device or sh.dtype != dtype):
+            sh_pools = dict(sh_gate=torch.empty(S, Fd, H, device=device, dtype=dtype),
+                            sh_up=torch.empty(S, Fd, H, device=device, dtype=dtype),
+                            sh_down=torch.empty(S, H, Fd, device=device, dtype=dtype))
+        else:
+            sh_pools = dict(sh_gate=old.get("sh_gate"), sh_up=old.get("sh_up"),
+                            sh_down=old.get("sh_down"))
+        for j, ex in enumerate(self.shared_experts):
+            for name, key in (("gate_proj", "sh_gate"), ("up_proj", "sh_up"), ("down_proj", "sh_down")):
+                lin = getattr(ex, name)
+                dst = sh_pools[key][j]
+                if lin.weight.data_ptr() != dst.data_ptr():
+                    with torch.no_grad():
+                        dst.copy_(lin.weight.detach())
+                    lin.weight = nn.Parameter(dst, requires_grad=lin.weight.requires_grad)
+        slot_host = ext["slot_host"]
+        live = np.zeros(E, dtype=np.float32)
+        for e, ex in enumerate(self.experts):
+            if _is_placeholder(ex):
+                continue
+            s = int(slot_host[e])
+            if s < 0:
+                raise RuntimeError(f"expert {e} is live but has no slot in the store's pool")
+            for name, key in (("gate_proj", "gate"), ("up_proj", "up"), ("down_proj", "down")):
+                lin = getattr(ex, name)
+                dst = ext[key][s]
+                if lin.weight.data_ptr() != dst.data_ptr():
+                    if tuple(lin.weight.shape) != tuple(dst.shape):
+                        raise RuntimeError(f"expert weight {name} has shape {tuple(lin.weight.shape)}, "
+                                           f"expected {tuple(dst.shape)}")
+                    with torch.no_grad():
+                        dst.copy_(lin.weight.detach())
+                    lin.weight = nn.Parameter(dst, requires_grad=False)
+            live[e] = 1.0
+        self._pool = dict(gate=ext["gate"], up=ext["up"], down=ext["down"], slot=ext["slot"],
+                          **sh_pools)
         self._live_np = live
         self._avail_cache = {}
         self._pool_dirty = False
@@ -365,6 +450,41 @@ class ChronosMOEFeedForward(nn.Module):
             a = np.ones(E, dtype=np.float32)
             od, fb = [], []
             odm = fbm = 0.0
+            topk = [r["topk_idx"], r["topk_weight"]]
+            # A pooled store smaller than this call's set of experts: loading
+            # into a full pool evicts, possibly an expert this call already
+            # counts on.  Then the experts are computed in passes (routed only)
+            # before each such load, as the reference computes each expert
+            # before loading the next (moe_chronos.py:228-254), and the shared
+            # term is added once at the end with the fallback weights.
+            state = dict(chunk=[], y=None, pool=pool)
+
+            def pool_full() -> bool:
+                ext = self._ext_pool
+                return ext is not None and \
+                    int((ext["slot_host"] >= 0).sum()) >= int(ext["gate"].shape[0])
+
+            def routed_pass(experts) -> torch.Tensor:
+                if self._pool_dirty:
+                    self._sync_pool(dev, dt)
+                    state["pool"] = self._pool
+                pl = state["pool"]
+                a_c = np.zeros(E, dtype=np.float32)
+                a_c[experts] = 1.0
+                o = ops.moe_forward(
+                    x_flat, self.gate.weight, pl["gate"], pl["up"], pl["down"], None, None, None, k,
+                    bool(self.norm_topk_prob), avail=self._avail_tensor(a_c, dev), router_bias=bias,
+                    slot_of_expert=pl.get("slot"), ready_flags=self.expert_ready_flags,
+                    ready_epoch=self.expert_ready_epoch, spin_limit_ns=self.expert_ready_timeout_ns,
+                    want_probs=False, topk=topk)
+                return o["y"].float()
+
+            def flush() -> None:
+                if state["chunk"]:
+                    yc = routed_pass(state["chunk"])
+                    state["y"] = yc if state["y"] is None else state["y"] + yc
+                    state["chunk"] = []
+
             for i in range(E):
                 if counts[i] <= 0:
                     continue
@@ -382,15 +502,19 @@ class ChronosMOEFeedForward(nn.Module):
                         od.append(i)
                         odm += float(mass[i])
                     a[i] = 1.0
+                    state["chunk"].append(i)
                 else:
                     loaded = False
                     if eval_with_mask and policy in {"on_demand", "sync_on_demand"} and loader is not None:
+                        if state["chunk"] and pool_full():
+                            flush()
                         res = loader(int(i))
                         loaded = bool(res.get("ok", False)) if isinstance(res, dict) else bool(res)
                     if loaded and not _is_placeholder(self.experts[i]):
                         od.append(i)
                         odm += float(mass[i])
                         a[i] = 1.0
+                        state["chunk"].append(i)
                     else:
                         fb.append(i)
                         fbm += float(mass[i])
@@ -398,14 +522,32 @@ class ChronosMOEFeedForward(nn.Module):
             if self._pool_dirty:
                 # the loader promoted experts: adopt the new modules into the pool
                 self._sync_pool(dev, dt)
-                pool = self._pool
-            out = ops.moe_forward(
-                x_flat, self.gate.weight, pool["gate"], pool["up"], pool["down"],
-                pool["sh_gate"], pool["sh_up"], pool["sh_down"], k, bool(self.norm_topk_prob),
-                avail=self._avail_tensor(a, dev), router_bias=bias,
-                ready_flags=self.expert_ready_flags, ready_epoch=self.expert_ready_epoch,
-                spin_limit_ns=self.expert_ready_timeout_ns, want_probs=False,
-                topk=[r["topk_idx"], r["topk_weight"]])
+            pool = self._pool
+            if state["y"] is None:
+                out = ops.moe_forward(
+                    x_flat, self.gate.weight, pool["gate"], pool["up"], pool["down"],
+                    pool["sh_gate"], pool["sh_up"], pool["sh_down"], k, bool(self.norm_topk_prob),
+                    avail=self._avail_tensor(a, dev), router_bias=bias,
+                    slot_of_expert=pool.get("slot"),
+                    ready_flags=self.expert_ready_flags, ready_epoch=self.expert_ready_epoch,
+                    spin_limit_ns=self.expert_ready_timeout_ns, want_probs=False, topk=topk)
+            else:
+                flush()
+                y_acc = state["y"]
+                if len(self.shared_experts) > 0:
+                    # shared term once: (1 + sum of the fallback selections' weights) * S(x)
+                    fb_t = torch.zeros(E, dtype=torch.float32, device=dev)
+                    if fb:
+                        fb_t[torch.tensor(fb, device=dev)] = 1.0
+                    w_fb = (r["topk_weight"] * fb_t[r["topk_idx"].long()]).contiguous()
+                    o = ops.moe_forward(
+                        x_flat, self.gate.weight, pool["gate"], pool["up"], pool["down"],
+                        pool["sh_gate"], pool["sh_up"], pool["sh_down"], k,
+                        bool(self.norm_topk_prob), avail=self._avail_tensor(np.zeros(E, np.float32), dev),
+                        router_bias=bias, slot_of_expert=pool.get("slot"), want_probs=False,
+                        topk=[r["topk_idx"], w_fb])
+                    y_acc = y_acc + o["y"].float()
+                out = dict(y=y_acc.to(dt), topk_idx=r["topk_idx"])
             self._last_on_demand_experts = od
             self._last_fallback_experts = fb
             self._last_on_demand_weight_mass = odm
@@ -431,7 +573,8 @@ class ChronosMOEFeedForward(nn.Module):
             out = ops.moe_forward(
                 x_flat, self.gate.weight, pool["gate"], pool["up"], pool["down"],
                 pool["sh_gate"], pool["sh_up"], pool["sh_down"], k, bool(self.norm_topk_prob),
-                avail=avail_t, router_bias=bias, ready_flags=self.expert_ready_flags,
+                avail=avail_t, router_bias=bias, slot_of_expert=pool.get("slot"),
+                ready_flags=self.expert_ready_flags,
                 ready_epoch=self.expert_ready_epoch, spin_limit_ns=self.expert_ready_timeout_ns,
                 want_probs=True, want_stats=masked)
             probs = out["probs"]

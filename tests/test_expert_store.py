@@ -1,0 +1,187 @@
+"""Host logic of the pooled expert store and cache manager (CPU).
+
+Mirrors the reference's store tests (tests/test_smoke.py of
+FonaTech/Project_Chronos: ``test_lru_cache`` :127-134, ``test_expert_store_init``
+:137-145) and checks the slot bookkeeping the device path relies on: slot
+assignment and reuse under LRU eviction, the expert -> slot map, ready flags,
+placeholders swapped in and out, the warm tier and the availability mask.
+The copies run on CPU tensors here; the GPU tests cover the same flow with the
+H2D stream, events and the kernels' ready-flag waits.
+"""
+import types
+
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+
+def _cfg(E=4, H=32, F=64, S=1, k=1, budget_experts=2):
+    expert_fp16_bytes = 3 * H * F * 2
+    return types.SimpleNamespace(
+        hidden_size=H, num_experts=E, num_experts_per_tok=k, moe_intermediate_size=F,
+        num_shared_experts=S, norm_topk_prob=False, router_aux_loss_coef=5e-4, hidden_act="silu",
+        dropout=0.0, fallback_mask_prob=0.0, intermediate_size=F,
+        # vram_capacity = budget * 0.5 / expert bytes
+        vram_budget_gb=budget_experts * expert_fp16_bytes * 2 / (1024 ** 3),
+        pinned_memory_max_fraction=0.25)
+
+
+class _Block(nn.Module):
+    def __init__(self, cfg):
+        super().__init__()
+        from project_chronos_b200 import ChronosMOEFeedForward
+        self.mlp = ChronosMOEFeedForward(cfg)
+
+
+class _Model(nn.Module):
+    """Stand-in with the reference model's ``model.layers[i].mlp`` structure."""
+
+    def __init__(self, cfg, layers=2):
+        super().__init__()
+        self.model = nn.Module()
+        self.model.layers = nn.ModuleList([_Block(cfg) for _ in range(layers)])
+
+
+def _half_state(model):
+    return {f"model.{k}": v.detach().half().float() for k, v in model.model.state_dict().items()}
+
+
+def test_lru_cache():
+    from project_chronos_b200 import LRUCache
+    lru = LRUCache(capacity=3)
+    lru.put(0); lru.put(1); lru.put(2)
+    assert lru.put(3) == 0
+    assert lru.contains(3) and not lru.contains(0)
+    assert lru.put(3) is None
+    lru.touch(1)
+    assert lru.keys() == [2, 3, 1]
+    lru.reorder_by_score({1: 0.1, 2: 0.9, 3: 0.5})
+    assert lru.keys() == [1, 3, 2]
+    assert lru.put(7) == 1
+    lru.remove(3)
+    assert len(lru) == 2
+
+
+def test_expert_store_init(tmp_path):
+    from project_chronos_b200 import ExpertStore
+    cfg = _cfg()
+    model = _Model(cfg)
+    store = ExpertStore(model, cfg, ssd_dir=str(tmp_path / "cache"))
+    s = store.stats()
+    assert s["vram_capacity"] == 2
+    assert s["ram_capacity_dynamic"] >= 1
+    assert "available_ram_gb" in s
+    assert store.num_layers == 2 and store.num_experts == 4
+
+
+def test_offload_promote_evict_cycle(tmp_path):
+    from project_chronos_b200 import ExpertStore, LazyExpertPlaceholder
+    torch.manual_seed(0)
+    cfg = _cfg()
+    model = _Model(cfg)
+    state = _half_state(model)
+    store = ExpertStore(model, cfg, ssd_dir=str(tmp_path / "cache"))
+    store.offload_from_state_dict(state)
+    assert (tmp_path / "cache" / "expert_l1_e3.pt").exists()
+    moes = store.moe_layers
+    assert all(isinstance(m.experts[e], LazyExpertPlaceholder) for m in moes for e in range(4))
+    assert store.vram_availability_mask().tolist() == [False] * 4
+
+    assert store.promote_to_vram(2) is True
+    assert store.promote_to_vram(0) is True
+    slots = store.slot_of_expert()
+    assert sorted([slots[2], slots[0]]) == [0, 1] and slots[1] == -1 and slots[3] == -1
+    assert store.vram_availability_mask().tolist() == [True, False, True, False]
+    assert store._slot_dev.tolist() == slots.tolist()
+    assert store._ready[:, [0, 2]].eq(1).all() and store._ready[:, [1, 3]].eq(0).all()
+    for li, m in enumerate(moes):
+        ex = m.experts[2]
+        assert not isinstance(ex, LazyExpertPlaceholder)
+        want = state[f"model.layers.{li}.mlp.experts.2.up_proj.weight"]
+        assert torch.equal(ex.up_proj.weight, want)
+        # the live module's weight IS the slot of the pool (no separate copy)
+        assert ex.up_proj.weight.data_ptr() == store._pools[li]["up"][slots[2]].data_ptr()
+
+    # capacity 2: promoting a third expert evicts the least recent (2) and reuses its slot
+    slot2 = int(slots[2])
+    assert store.promote_to_vram(3) is True
+    slots = store.slot_of_expert()
+    assert slots[2] == -1 and slots[3] == slot2
+    assert store._ready[:, 2].eq(0).all() and store._ready[:, 3].eq(1).all()
+    assert all(isinstance(m.experts[2], LazyExpertPlaceholder) for m in moes)
+    for li, m in enumerate(moes):
+        want = state[f"model.layers.{li}.mlp.experts.3.down_proj.weight"]
+        assert torch.equal(m.experts[3].down_proj.weight, want)
+    assert store.ram_lru.contains(2)  # the evicted expert stays warm
+
+    # re-promoting a resident expert keeps its slot and copies nothing
+    before = store._pools[0]["gate"].clone()
+    assert store.promote_to_vram(3) is True
+    assert store.slot_of_expert()[3] == slot2
+    assert torch.equal(before, store._pools[0]["gate"])
+
+    # an id with no cold-tier file cannot be promoted
+    assert store.promote_to_vram(99) is False
+
+
+def test_eviction_without_warm_copy_writes_back(tmp_path):
+    from project_chronos_b200 import ExpertStore
+    torch.manual_seed(1)
+    cfg = _cfg()
+    model = _Model(cfg, layers=1)
+    state = _half_state(model)
+    store = ExpertStore(model, cfg, ssd_dir=str(tmp_path / "c"))
+    store.offload_from_state_dict(state)
+    store.promote_to_vram(1)
+    with store._ram_lock:
+        store._ram_buffers.pop(1)          # warm copy gone
+    store.ram_lru.remove(1)
+    for e in (2, 3):                        # evicts 1
+        store.promote_to_vram(e)
+    assert store.slot_of_expert()[1] == -1
+    got = store._ram_buffers[1][0]["gate_proj.weight"]
+    assert torch.equal(got, state["model.layers.0.mlp.experts.1.gate_proj.weight"])
+
+
+def test_cache_manager_ensure_resident_and_masks(tmp_path):
+    from project_chronos_b200 import CacheManager
+    torch.manual_seed(2)
+    cfg = _cfg(E=6, budget_experts=3)
+    model = _Model(cfg)
+    mgr = CacheManager(model, cfg, ssd_dir=str(tmp_path / "m"))
+    mgr.expert_store.offload_from_state_dict(_half_state(model))
+    mgr.warm_up([0, 1])
+    assert mgr.availability_mask().tolist() == [True, True, False, False, False, False]
+    newly = mgr.ensure_resident([1, 4, 5])
+    assert newly == [4, 5]
+    m = mgr.availability_mask().tolist()
+    assert sum(m) == 3 and m[4] and m[5] and m[1]
+    masks = mgr.availability_masks_all_layers()
+    assert len(masks) == 2 and all(torch.equal(x, masks[0]) for x in masks)
+    assert mgr.prefetch_experts_to_ram([3, 3, 2]) == [3, 2]
+    st = mgr.stats()
+    assert st["vram_experts"] == 3 and st["pool_slots"] == 3
+
+
+def test_module_attached_pool_bookkeeping(tmp_path):
+    """The layer adopts the store's pools: live experts = resident slots, the
+    shared experts in the layer's own pool, the device slot map passed along."""
+    from project_chronos_b200 import ExpertStore
+    torch.manual_seed(3)
+    cfg = _cfg()
+    model = _Model(cfg, layers=1)
+    store = ExpertStore(model, cfg, ssd_dir=str(tmp_path / "p"))
+    store.offload_from_state_dict(_half_state(model))
+    store.promote_to_vram(1)
+    moe = store.moe_layers[0]
+    moe._sync_pool(torch.device("cpu"), torch.float32)
+    assert moe._live_np.tolist() == [0.0, 1.0, 0.0, 0.0]
+    assert moe._pool["slot"] is store._slot_dev
+    assert moe._pool["gate"] is store._pools[0]["gate"]
+    assert moe.expert_ready_flags is None  # flags only on CUDA
+    sh = moe.shared_experts[0].gate_proj.weight
+    assert sh.data_ptr() == moe._pool["sh_gate"][0].data_ptr()
+    with pytest.raises(RuntimeError, match="CUDA"):
+        moe(torch.zeros(1, 1, cfg.hidden_size))
+    np.testing.assert_array_equal(store.slot_of_expert(), [-1, 0, -1, -1])

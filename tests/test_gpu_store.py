@@ -1,0 +1,185 @@
+"""Pooled expert store on the GPU: slots, H2D stream, device ready flags.
+
+Mirrors the reference's lazy-loading tests (tests/test_smoke.py of
+FonaTech/Project_Chronos: on-demand offload == full model, :429-488, with a
+pool of ONE resident expert; CUDA double-stream pipeline, tests/test_smoke_cuda.py)
+on the layer level, and checks what the device path adds: a forward issued
+while its experts' copies are still queued on the H2D stream waits on the
+per-(layer, expert) ready flags, not on the stream, and still matches.
+"""
+import types
+
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _cfg(E=8, H=128, F=256, S=1, k=2, budget_experts=4, flags=True):
+    return types.SimpleNamespace(
+        hidden_size=H, num_experts=E, num_experts_per_tok=k, moe_intermediate_size=F,
+        num_shared_experts=S, norm_topk_prob=True, router_aux_loss_coef=5e-4, hidden_act="silu",
+        dropout=0.0, fallback_mask_prob=0.0, intermediate_size=F,
+        vram_budget_gb=budget_experts * 3 * H * F * 2 * 2 / (1024 ** 3),
+        pinned_memory_max_fraction=0.25, device_ready_flags=flags)
+
+
+class _Block(nn.Module):
+    def __init__(self, cfg):
+        super().__init__()
+        from project_chronos_b200 import ChronosMOEFeedForward
+        self.mlp = ChronosMOEFeedForward(cfg)
+
+
+class _Model(nn.Module):
+    def __init__(self, cfg, layers):
+        super().__init__()
+        self.model = nn.Module()
+        self.model.layers = nn.ModuleList([_Block(cfg) for _ in range(layers)])
+
+
+def _pair(cfg, layers, dtype, seed=0):
+    """(full model, lazy model, half-representable state) on the GPU."""
+    torch.manual_seed(seed)
+    src = _Model(cfg, layers)
+    with torch.no_grad():
+        for p in src.parameters():
+            p.normal_(0.0, 0.05)
+    state = {f"model.{k}": v.detach().half().float() for k, v in src.model.state_dict().items()}
+    full = _Model(cfg, layers)
+    full.load_state_dict(state)
+    lazy = _Model(cfg, layers)
+    lazy.load_state_dict(state)
+    full = full.to(DEV, dtype).eval()
+    lazy = lazy.to(DEV, dtype).eval()
+    return full, lazy, state
+
+
+def _selected(moe, x):
+    from project_chronos_b200 import ops
+    r = ops.moe_route(x.reshape(-1, x.shape[-1]), moe.gate.weight, moe.num_experts_per_tok, True,
+                      num_shared=len(moe.shared_experts), ffn=moe.config.moe_intermediate_size)
+    return sorted(set(r["topk_idx"].reshape(-1).tolist()))
+
+
+def _tol(dtype):
+    return 1e-5 if dtype == torch.float32 else 1e-2
+
+
+def _rel(a, b):
+    return (torch.linalg.vector_norm((a.float() - b.float())) /
+            torch.linalg.vector_norm(b.float()).clamp_min(1e-30)).item()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_store_layers_match_full_model(tmp_path, dtype):
+    """Per layer: ensure_resident(the layer's experts) then the layer with the
+    store's mask == the full layer.  Four slots for eight experts, two layers:
+    slots are reused between layers (eviction events order the copies)."""
+    from project_chronos_b200 import CacheManager
+    cfg = _cfg()
+    full, lazy, state = _pair(cfg, 2, dtype)
+    mgr = CacheManager(lazy, cfg, ssd_dir=str(tmp_path / "c"))
+    mgr.expert_store.offload_from_state_dict(state)
+    x = torch.randn(2, 3, cfg.hidden_size, device=DEV, dtype=dtype)
+    with torch.no_grad():
+        for li in range(2):
+            f_moe = full.model.layers[li].mlp
+            l_moe = lazy.model.layers[li].mlp
+            need = _selected(f_moe, x)
+            assert len(need) <= 4
+            mgr.ensure_resident(need)
+            y_full = f_moe(x)
+            y_lazy = l_moe(x, available_expert_mask=mgr.availability_mask())
+            torch.cuda.synchronize()
+            assert l_moe.last_fallback_experts == []
+            assert _rel(y_lazy, y_full) <= _tol(dtype)
+    assert mgr.stats()["vram_experts"] <= 4
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_forward_waits_on_ready_flags_not_on_the_stream(tmp_path, dtype):
+    """The H2D stream is held back (a sleep kernel) so the copies land well
+    after the forward starts; the GEMMs must wait on the experts' flags."""
+    from project_chronos_b200 import CacheManager, ops
+    cfg = _cfg(budget_experts=8)
+    full, lazy, state = _pair(cfg, 1, dtype, seed=1)
+    mgr = CacheManager(lazy, cfg, ssd_dir=str(tmp_path / "d"))
+    store = mgr.expert_store
+    store.offload_from_state_dict(state)
+    x = torch.randn(1, 5, cfg.hidden_size, device=DEV, dtype=dtype)
+    f_moe, l_moe = full.model.layers[0].mlp, lazy.model.layers[0].mlp
+    need = _selected(f_moe, x)
+    store.prefetch_to_ram(need)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(store._h2d_stream):
+        torch.cuda._sleep(100_000_000)   # ~50 ms of the H2D stream
+    with torch.no_grad():
+        newly = mgr.ensure_resident(need)
+        assert newly == need
+        y_lazy = l_moe(x, available_expert_mask=mgr.availability_mask())
+        launched_before_copies = not store._h2d_stream.query()
+        y_full = f_moe(x)
+    torch.cuda.synchronize()
+    ops.check_status(torch.device(DEV))
+    assert launched_before_copies
+    assert (store._ready[0, need] == 1).all()
+    assert l_moe.last_fallback_experts == []
+    assert _rel(y_lazy, y_full) <= _tol(dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_sync_on_demand_with_one_slot_matches_full(tmp_path, dtype):
+    """Reference tests/test_smoke.py:429-488 on the layer: every expert cold,
+    a pool of ONE slot, the runtime loader promotes each selected expert; the
+    layer computes them in passes and matches the full model."""
+    from project_chronos_b200 import ExpertStore
+    cfg = _cfg(budget_experts=1)
+    full, lazy, state = _pair(cfg, 1, dtype, seed=2)
+    store = ExpertStore(lazy, cfg, ssd_dir=str(tmp_path / "e"))
+    assert store.vram_capacity == 1
+    store.offload_from_state_dict(state)
+    loaded = []
+
+    def loader(eid):
+        ok = store.promote_to_vram(eid)
+        loaded.append(eid)
+        return {"ok": ok}
+
+    l_moe = lazy.model.layers[0].mlp
+    l_moe.runtime_miss_policy = "sync_on_demand"
+    l_moe.runtime_on_demand_loader = loader
+    x = torch.randn(1, 6, cfg.hidden_size, device=DEV, dtype=dtype)
+    cold = torch.zeros(cfg.num_experts, dtype=torch.bool)
+    with torch.no_grad():
+        y_full = full.model.layers[0].mlp(x)
+        y_lazy = l_moe(x, available_expert_mask=cold)
+    torch.cuda.synchronize()
+    need = _selected(full.model.layers[0].mlp, x)
+    assert sorted(loaded) == need
+    assert l_moe.last_on_demand_experts == need
+    assert l_moe.last_fallback_experts == []
+    assert len(store.vram_lru) <= 1
+    assert _rel(y_lazy, y_full) <= _tol(dtype)
+
+
+def test_event_wait_mode_without_flags(tmp_path):
+    """device_ready_flags=False: ensure_resident makes the compute stream wait
+    on the promoted experts' events (the reference's M3 path)."""
+    from project_chronos_b200 import CacheManager
+    cfg = _cfg(flags=False)
+    full, lazy, state = _pair(cfg, 1, torch.bfloat16, seed=3)
+    mgr = CacheManager(lazy, cfg, ssd_dir=str(tmp_path / "f"))
+    mgr.expert_store.offload_from_state_dict(state)
+    assert lazy.model.layers[0].mlp.expert_ready_flags is None
+    x = torch.randn(1, 2, cfg.hidden_size, device=DEV, dtype=torch.bfloat16)
+    need = _selected(full.model.layers[0].mlp, x)
+    with torch.no_grad():
+        mgr.ensure_resident(need)
+        y_lazy = lazy.model.layers[0].mlp(x, available_expert_mask=mgr.availability_mask())
+        y_full = full.model.layers[0].mlp(x)
+    torch.cuda.synchronize()
+    assert _rel(y_lazy, y_full) <= 1e-2
