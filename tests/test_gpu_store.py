@@ -84,7 +84,7 @@ def test_store_layers_match_full_model(tmp_path, dtype):
     full, lazy, state = _pair(cfg, 2, dtype)
     mgr = CacheManager(lazy, cfg, ssd_dir=str(tmp_path / "c"))
     mgr.expert_store.offload_from_state_dict(state)
-    x = torch.randn(2, 3, cfg.hidden_size, device=DEV, dtype=dtype)
+    x = torch.randn(1, 2, cfg.hidden_size, device=DEV, dtype=dtype)
     with torch.no_grad():
         for li in range(2):
             f_moe = full.model.layers[li].mlp
