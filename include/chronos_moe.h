@@ -16,12 +16,13 @@
  * the effective availability of routed expert e (1 = resident, 0 = cache
  * miss served by the shared experts).
  *
- * Routing contract (bit-exact, identical on every run): logits are fp32
- * sums over h = 0..H-1 in increasing order with one fused multiply-add per
- * element (operands widened to fp32), plus router_bias[e] when given.
- * Experts are ranked by (logit descending, expert index ascending); the
- * top-k weights are the fp32 softmax probabilities of the chosen experts,
- * renormalised by (sum + 1e-20) when norm_topk is set.
+ * Routing contract (bit-exact, identical on every run): a logit is the
+ * in-order fp32 sum of chunk partials, partial c being one chain of fused
+ * multiply-adds over h in [128c, min(128c + 128, H)) starting from 0
+ * (operands widened to fp32), plus router_bias[e] when given.  Experts are
+ * ranked by (logit descending, expert index ascending); the top-k weights
+ * are the fp32 softmax probabilities of the chosen experts, renormalised by
+ * (sum + 1e-20) when norm_topk is set.
  *
  * Conventions: every pointer in ChronosMoeArgs is a DEVICE pointer unless
  * stated otherwise; all matrices are row-major and contiguous with the

@@ -42,7 +42,11 @@ ABI_VERSION = 1
 EXPORTS = ("chronos_moe_workspace_size", "chronos_moe_forward", "chronos_moe_route",
            "chronos_moe_last_error", "chronos_moe_abi_version", "chronos_moe_args_size",
            "chronos_moe_profile_begin", "chronos_moe_profile_end",
-           "chronos_moe_kernel_launches", "chronos_moe_forward_noalloc")
+           "chronos_moe_kernel_launches", "chronos_moe_forward_noalloc",
+           "chronos_ep_dispatch", "chronos_ep_combine", "chronos_ep_dispatch_args_size",
+           "chronos_ep_combine_args_size")
+
+EP_MAX_RANKS = 32  # CHRONOS_EP_MAX_RANKS
 
 NOALLOC_SCRATCH_BYTES = 16 << 20  # CHRONOS_NOALLOC_SCRATCH_BYTES
 
@@ -93,6 +97,42 @@ class ChronosMoeArgs(ctypes.Structure):
     ]
 
 
+class ChronosEpDispatchArgs(ctypes.Structure):
+    """Mirror of include/chronos_ep.h ChronosEpDispatchArgs."""
+    _fields_ = [
+        ("num_tokens", ctypes.c_int64),
+        ("hidden", ctypes.c_int32),
+        ("num_experts", ctypes.c_int32),
+        ("top_k", ctypes.c_int32),
+        ("world_size", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("x", ctypes.c_void_p),
+        ("topk_idx", ctypes.c_void_p),
+        ("topk_weight", ctypes.c_void_p),
+        ("avail", ctypes.c_void_p),
+        ("send_counts", ctypes.c_void_p),
+        ("send_x", ctypes.c_void_p),
+        ("send_meta", ctypes.c_void_p),
+        ("pair_slot", ctypes.c_void_p),
+        ("shared_weight", ctypes.c_void_p),
+        ("scratch", ctypes.c_void_p),
+    ]
+
+
+class ChronosEpCombineArgs(ctypes.Structure):
+    """Mirror of include/chronos_ep.h ChronosEpCombineArgs."""
+    _fields_ = [
+        ("num_tokens", ctypes.c_int64),
+        ("hidden", ctypes.c_int32),
+        ("top_k", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("y_shared", ctypes.c_void_p),
+        ("recv_y", ctypes.c_void_p),
+        ("pair_slot", ctypes.c_void_p),
+        ("y", ctypes.c_void_p),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -136,6 +176,17 @@ def load_library(path: str = LIB_PATH):
         lib.chronos_moe_forward_noalloc.argtypes = [ctypes.POINTER(ChronosMoeArgs),
                                                     ctypes.c_void_p]
         lib.chronos_moe_forward_noalloc.restype = ctypes.c_int
+        lib.chronos_ep_dispatch.argtypes = [ctypes.POINTER(ChronosEpDispatchArgs), ctypes.c_void_p]
+        lib.chronos_ep_dispatch.restype = ctypes.c_int
+        lib.chronos_ep_combine.argtypes = [ctypes.POINTER(ChronosEpCombineArgs), ctypes.c_void_p]
+        lib.chronos_ep_combine.restype = ctypes.c_int
+        lib.chronos_ep_dispatch_args_size.argtypes = []
+        lib.chronos_ep_dispatch_args_size.restype = ctypes.c_size_t
+        lib.chronos_ep_combine_args_size.argtypes = []
+        lib.chronos_ep_combine_args_size.restype = ctypes.c_size_t
+        if (lib.chronos_ep_dispatch_args_size() != ctypes.sizeof(ChronosEpDispatchArgs)
+                or lib.chronos_ep_combine_args_size() != ctypes.sizeof(ChronosEpCombineArgs)):
+            raise RuntimeError("expert-parallel args layout mismatch between the library and the binding")
         if lib.chronos_moe_abi_version() != ABI_VERSION:
             raise RuntimeError("chronos MoE extension ABI version mismatch; rebuild it")
         if lib.chronos_moe_args_size() != ctypes.sizeof(ChronosMoeArgs):

@@ -18,8 +18,10 @@
 #include <unordered_map>
 #include <vector>
 
+#include "chronos_ep.h"
 #include "chronos_moe.h"
 #include "common.cuh"
+#include "ep.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
 #include "plan.cuh"
@@ -899,3 +901,116 @@ extern "C" int chronos_moe_profile_end(float* stage_ms, int32_t* stage_launches,
 extern "C" uint64_t chronos_moe_kernel_launches(void) {
     return g_kernel_launches.load(std::memory_order_relaxed);
 }
+
+// ---------------------------------------------------------------------------
+// expert-parallel dispatch / combine (include/chronos_ep.h)
+// ---------------------------------------------------------------------------
+namespace chronos {
+namespace {
+
+int validate_ep_rows(int64_t n, int32_t h, int32_t k, int32_t dtype) {
+    if (n < 0 || n > (int64_t(1) << 24)) return fail(CHRONOS_ERR_INVALID_ARG, "num_tokens %lld out of range",
+                                                     static_cast<long long>(n));
+    if (dtype != CHRONOS_DTYPE_BF16 && dtype != CHRONOS_DTYPE_FP16 && dtype != CHRONOS_DTYPE_FP32)
+        return fail(CHRONOS_ERR_INVALID_ARG, "dtype %d unknown", dtype);
+    if (h <= 0 || (static_cast<size_t>(h) * elem_size(dtype)) % 16 != 0)
+        return fail(CHRONOS_ERR_INVALID_ARG, "hidden %d: rows must be a multiple of 16 bytes", h);
+    if (k < 1 || k > kMaxTopKEp) return fail(CHRONOS_ERR_INVALID_ARG, "top_k %d out of range [1, %d]", k,
+                                             kMaxTopKEp);
+    return CHRONOS_OK;
+}
+
+template <typename T>
+int ep_dispatch_impl(const ChronosEpDispatchArgs* a, cudaStream_t st) {
+    EpParams p{};
+    p.x = a->x;
+    p.n = a->num_tokens;
+    p.h = a->hidden;
+    p.e = a->num_experts;
+    p.k = a->top_k;
+    p.g = a->world_size;
+    p.epr = a->num_experts / a->world_size;
+    p.topk_idx = a->topk_idx;
+    p.topk_w = a->topk_weight;
+    p.avail = a->avail;
+    p.counts = a->send_counts;
+    p.pos = a->scratch;
+    p.send_x = a->send_x;
+    p.send_meta = a->send_meta;
+    p.pair_slot = a->pair_slot;
+    p.shared_w = a->shared_weight;
+    CHRONOS_CUDA_CHECK(cudaMemsetAsync(a->send_counts, 0, sizeof(int32_t) * a->world_size, st));
+    const int64_t pairs = p.n * p.k;
+    if (pairs == 0) return CHRONOS_OK;
+    const unsigned cb = static_cast<unsigned>((pairs + kEpPackThreads - 1) / kEpPackThreads);
+    CHRONOS_CUDA_CHECK(launch_kernel(ep_count_kernel, dim3(cb), dim3(kEpPackThreads), 0, st, false, p));
+    const int64_t wpb = kEpPackThreads / 32;
+    const unsigned pb = static_cast<unsigned>((pairs + wpb - 1) / wpb);
+    CHRONOS_CUDA_CHECK(launch_kernel(ep_pack_kernel<T>, dim3(pb), dim3(kEpPackThreads), 0, st, true, p));
+    return CHRONOS_OK;
+}
+
+template <typename T>
+int ep_combine_impl(const ChronosEpCombineArgs* a, cudaStream_t st) {
+    EpCombineParams p{};
+    p.y_shared = a->y_shared;
+    p.recv_y = a->recv_y;
+    p.pair_slot = a->pair_slot;
+    p.y = a->y;
+    p.n = a->num_tokens;
+    p.h = a->hidden;
+    p.k = a->top_k;
+    if (p.n == 0) return CHRONOS_OK;
+    CHRONOS_CUDA_CHECK(launch_kernel(ep_combine_kernel<T>, dim3(static_cast<unsigned>(p.n)),
+                                     dim3(kEpCombineThreads), 0, st, false, p));
+    return CHRONOS_OK;
+}
+
+}  // namespace
+}  // namespace chronos
+
+extern "C" int chronos_ep_dispatch(const ChronosEpDispatchArgs* a, void* stream) {
+    using namespace chronos;
+    if (a == nullptr) return fail(CHRONOS_ERR_INVALID_ARG, "args is NULL");
+    if (int rc = validate_ep_rows(a->num_tokens, a->hidden, a->top_k, a->dtype)) return rc;
+    if (a->world_size < 1 || a->world_size > CHRONOS_EP_MAX_RANKS)
+        return fail(CHRONOS_ERR_INVALID_ARG, "world_size %d out of range [1, %d]", a->world_size,
+                    CHRONOS_EP_MAX_RANKS);
+    if (a->num_experts < 1 || a->num_experts % a->world_size != 0 || a->num_experts < a->top_k)
+        return fail(CHRONOS_ERR_INVALID_ARG, "num_experts %d must be >= top_k and a multiple of world_size %d",
+                    a->num_experts, a->world_size);
+    if (a->send_counts == nullptr) return fail(CHRONOS_ERR_INVALID_ARG, "send_counts is required");
+    if (a->num_tokens > 0 &&
+        (a->x == nullptr || a->topk_idx == nullptr || a->topk_weight == nullptr || a->send_x == nullptr ||
+         a->send_meta == nullptr || a->pair_slot == nullptr ||
+         a->shared_weight == nullptr || a->scratch == nullptr))
+        return fail(CHRONOS_ERR_INVALID_ARG, "a required pointer is NULL");
+    if ((reinterpret_cast<uintptr_t>(a->x) | reinterpret_cast<uintptr_t>(a->send_x)) & 15)
+        return fail(CHRONOS_ERR_INVALID_ARG, "x and send_x must be 16-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (a->dtype) {
+        case CHRONOS_DTYPE_BF16: return ep_dispatch_impl<__nv_bfloat16>(a, st);
+        case CHRONOS_DTYPE_FP16: return ep_dispatch_impl<__half>(a, st);
+        default: return ep_dispatch_impl<float>(a, st);
+    }
+}
+
+extern "C" int chronos_ep_combine(const ChronosEpCombineArgs* a, void* stream) {
+    using namespace chronos;
+    if (a == nullptr) return fail(CHRONOS_ERR_INVALID_ARG, "args is NULL");
+    if (int rc = validate_ep_rows(a->num_tokens, a->hidden, a->top_k, a->dtype)) return rc;
+    if (a->num_tokens > 0 && (a->recv_y == nullptr || a->pair_slot == nullptr || a->y == nullptr))
+        return fail(CHRONOS_ERR_INVALID_ARG, "recv_y, pair_slot and y are required");
+    if ((reinterpret_cast<uintptr_t>(a->recv_y) | reinterpret_cast<uintptr_t>(a->y) |
+         reinterpret_cast<uintptr_t>(a->y_shared)) & 15)
+        return fail(CHRONOS_ERR_INVALID_ARG, "row buffers must be 16-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (a->dtype) {
+        case CHRONOS_DTYPE_BF16: return ep_combine_impl<__nv_bfloat16>(a, st);
+        case CHRONOS_DTYPE_FP16: return ep_combine_impl<__half>(a, st);
+        default: return ep_combine_impl<float>(a, st);
+    }
+}
+
+extern "C" size_t chronos_ep_dispatch_args_size(void) { return sizeof(ChronosEpDispatchArgs); }
+extern "C" size_t chronos_ep_combine_args_size(void) { return sizeof(ChronosEpCombineArgs); }

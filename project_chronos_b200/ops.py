@@ -186,6 +186,68 @@ def moe_route(x: torch.Tensor, router_w: torch.Tensor, top_k: int, norm_topk: bo
     return dict(probs=probs, topk_idx=topk_idx, topk_weight=topk_w, counts=counts, mass=mass)
 
 
+def ep_dispatch(x: torch.Tensor, topk_idx: torch.Tensor, topk_weight: torch.Tensor, num_experts: int,
+                world_size: int, avail: Optional[torch.Tensor] = None) -> dict:
+    """Send buffers of one rank for expert parallelism (include/chronos_ep.h).
+
+    Returns dict(send_counts [G] int32, send_x [N*k, H], send_meta [N*k, 2] int32
+    (local expert id, fp32 bits of w*a), pair_slot [N*k] int32, shared_weight [N, k]
+    fp32); the first ``send_counts.sum()`` rows of the send buffers are used."""
+    _check_cuda(x, topk_idx, topk_weight, avail)
+    x = x.contiguous()
+    n, h = x.shape
+    k = topk_idx.shape[1]
+    dev = x.device
+    if x.dtype not in _DTYPES:
+        raise TypeError(f"unsupported dtype {x.dtype}")
+    topk_idx = topk_idx.to(torch.int32).contiguous()
+    topk_weight = topk_weight.to(torch.float32).contiguous()
+    av = None if avail is None else avail.to(device=dev, dtype=torch.float32).contiguous()
+    out = dict(send_counts=torch.empty(world_size, dtype=torch.int32, device=dev),
+               send_x=torch.empty(n * k, h, dtype=x.dtype, device=dev),
+               send_meta=torch.empty(n * k, 2, dtype=torch.int32, device=dev),
+               pair_slot=torch.empty(n * k, dtype=torch.int32, device=dev),
+               shared_weight=torch.empty(n, k, dtype=torch.float32, device=dev))
+    scratch = torch.empty(max(n * k, 1), dtype=torch.int32, device=dev)
+    args = N.ChronosEpDispatchArgs(
+        num_tokens=n, hidden=h, num_experts=int(num_experts), top_k=k, world_size=int(world_size),
+        dtype=_DTYPES[x.dtype], x=_ptr(x), topk_idx=_ptr(topk_idx), topk_weight=_ptr(topk_weight),
+        avail=_ptr(av), send_counts=_ptr(out["send_counts"]), send_x=_ptr(out["send_x"]),
+        send_meta=_ptr(out["send_meta"]),
+        pair_slot=_ptr(out["pair_slot"]), shared_weight=_ptr(out["shared_weight"]),
+        scratch=_ptr(scratch))
+    lib = N.load_library()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        N.check(lib.chronos_ep_dispatch(ctypes.byref(args), ctypes.c_void_p(stream)))
+    return out
+
+
+def ep_combine(recv_y: torch.Tensor, pair_slot: torch.Tensor, top_k: int,
+               y_shared: Optional[torch.Tensor] = None, num_tokens: Optional[int] = None,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y_t = y_shared_t + sum_j recv_y[pair_slot[t, j]] (fp32, j ascending)."""
+    _check_cuda(recv_y, pair_slot, y_shared)
+    h = recv_y.shape[1]
+    n = int(num_tokens if num_tokens is not None else pair_slot.numel() // top_k)
+    dev = recv_y.device
+    dt = recv_y.dtype
+    if y_shared is not None and y_shared.dtype != dt:
+        raise TypeError(f"y_shared dtype {y_shared.dtype} != recv_y dtype {dt}")
+    recv_y = recv_y.contiguous()
+    y_shared = _contig(y_shared)
+    pair_slot = pair_slot.to(torch.int32).contiguous()
+    y = out if out is not None else torch.empty(n, h, dtype=dt, device=dev)
+    args = N.ChronosEpCombineArgs(num_tokens=n, hidden=h, top_k=int(top_k), dtype=_DTYPES[dt],
+                                  y_shared=_ptr(y_shared), recv_y=_ptr(recv_y),
+                                  pair_slot=_ptr(pair_slot), y=_ptr(y))
+    lib = N.load_library()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        N.check(lib.chronos_ep_combine(ctypes.byref(args), ctypes.c_void_p(stream)))
+    return y
+
+
 def profile_begin(max_calls: int) -> None:
     """Record per-stage CUDA events for the next ``max_calls`` layer calls (this thread)."""
     lib = N.load_library()

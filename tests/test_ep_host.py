@@ -1,0 +1,60 @@
+"""Expert-parallel host orchestration on gloo CPU ranks (world size 2).
+
+The extension's calls are replaced by the oracle's CPU stand-ins
+(oracle/ep_oracle.py), so what runs here is the layer's own logic: routing
+to ranks, split sizes, the three all-to-alls and the combine.  Checked against
+the single-device oracle on the same global weights; an injected rank failure
+(a rank raising before the exchange) must end the other rank's collective
+with an error, not a hang.
+"""
+import socket
+
+import pytest
+import torch.multiprocessing as mp
+
+from tests import _ep_worker
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(scenario, world=2, timeout=120):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_ep_worker.cpu_rank, args=(r, world, port, q, scenario))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    out = []
+    try:
+        for _ in range(world):
+            out.append(q.get(timeout=timeout))
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+                p.join()
+    return sorted(out, key=lambda r: r[1])
+
+
+@pytest.mark.parametrize("scenario", ["all", "mask"])
+def test_ep_two_ranks_match_single_device_oracle(scenario):
+    res = _run(scenario)
+    for status, rank, val, sc, rc in res:
+        assert status == "ok", (rank, val)
+        assert val < 1e-5, (rank, val)
+    # what rank 0 sends to rank 1 is what rank 1 receives from rank 0
+    assert res[0][3][1] == res[1][4][0]
+    assert res[1][3][0] == res[0][4][1]
+
+
+def test_injected_rank_failure_ends_the_collective_with_an_error():
+    res = _run("fail", timeout=90)
+    by_rank = {r[1]: r for r in res}
+    assert by_rank[1][0] == "error" and "injected" in by_rank[1][2]
+    assert by_rank[0][0] == "error"

@@ -1,0 +1,116 @@
+"""Expert-parallel kernels and layer on the GPU.
+
+* ``chronos_ep_dispatch`` / ``chronos_ep_combine`` against the oracle's
+  restatement (oracle/ep_oracle.py): counts, shared weights and the combine
+  exactly; send rows and metadata through ``pair_slot`` (the order inside a
+  rank is unspecified);
+* the layer on one rank (no exchange) == the single-device layer;
+* two NCCL ranks on two GPUs (skipped with fewer): each rank's output == the
+  single-device layer on its tokens.
+"""
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from tests import _ep_worker
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _route(x, router, k):
+    from project_chronos_b200 import ops
+    return ops.moe_route(x, router, k, True, num_shared=1, ffn=64, want_probs=False)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("world,n", [(1, 7), (2, 33), (4, 300), (8, 1)])
+def test_dispatch_and_combine_match_oracle(dtype, world, n):
+    from oracle.ep_oracle import CpuEpBackend
+    from project_chronos_b200 import ops
+    E, k, H = 16, 4, 256
+    g = torch.Generator().manual_seed(world * 1000 + n)
+    x = torch.randn(n, H, generator=g).to(DEV, dtype)
+    router = (torch.randn(E, H, generator=g) * 0.05).to(DEV, dtype)
+    avail = (torch.rand(E, generator=g) > 0.25).float()
+    avail[3] = 0.5
+    r = _route(x, router, k)
+    d = ops.ep_dispatch(x, r["topk_idx"], r["topk_weight"], E, world, avail=avail.to(DEV))
+    ref = CpuEpBackend.ep_dispatch(x.cpu(), r["topk_idx"].cpu(), r["topk_weight"].cpu(), E, world, avail)
+    assert d["send_counts"].cpu().tolist() == ref["send_counts"].tolist()
+    assert torch.equal(d["shared_weight"].cpu(), ref["shared_weight"])
+    ps = d["pair_slot"].cpu()
+    assert torch.equal(ps < 0, ref["pair_slot"] < 0)
+    n_send = int(ref["send_counts"].sum())
+    # rows and metadata, matched through pair_slot
+    sent = ps >= 0
+    got_rows = d["send_x"].cpu()[ps[sent].long()]
+    want_rows = ref["send_x"][ref["pair_slot"][sent].long()]
+    assert torch.equal(got_rows, want_rows)
+    assert torch.equal(d["send_meta"].cpu()[ps[sent].long()], ref["send_meta"][ref["pair_slot"][sent].long()])
+    assert sorted(ps[sent].tolist()) == list(range(n_send))
+    # rows of each destination rank are contiguous, in rank order
+    offs = np.concatenate([[0], np.cumsum(ref["send_counts"].numpy())])
+    dest = (r["topk_idx"].cpu().view(-1)[sent] // (E // world)).numpy()
+    slots = ps[sent].numpy()
+    assert np.all((slots >= offs[dest]) & (slots < offs[dest + 1]))
+
+    # combine: returned rows (any values), shared term
+    rows = torch.randn(max(n_send, 1), H, generator=g).to(DEV, dtype)[:n_send]
+    y_sh = torch.randn(n, H, generator=g).to(DEV, dtype)
+    y = ops.ep_combine(rows, d["pair_slot"], k, y_shared=y_sh, num_tokens=n)
+    want = CpuEpBackend.ep_combine(rows.cpu(), d["pair_slot"].cpu(), k, y_shared=y_sh.cpu(), num_tokens=n)
+    assert torch.equal(y.cpu(), want)
+
+
+@pytest.mark.parametrize("masked", [False, True])
+def test_single_rank_layer_matches_single_device(masked):
+    from project_chronos_b200 import ops
+    from project_chronos_b200.ep import ExpertParallelMoE
+    E, k, H, F, S, n = 16, 4, 256, 128, 1, 96
+    w = {key: v.to(DEV, torch.bfloat16) for key, v in _ep_worker._weights(E, H, F, S).items()}
+    x = torch.randn(n, H, generator=torch.Generator().manual_seed(5)).to(DEV, torch.bfloat16)
+    mask = None
+    if masked:
+        mask = (torch.rand(E, generator=torch.Generator().manual_seed(6)) > 0.3).float().to(DEV)
+    m = ExpertParallelMoE.from_stacked(_ep_worker._cfg(E, k, H, F, S), w["router"], w["gate"], w["up"],
+                                       w["down"], w["sh_gate"], w["sh_up"], w["sh_down"])
+    y = m(x.view(2, n // 2, H), available_expert_mask=mask).view(n, H)
+    full = ops.moe_forward(x, w["router"], w["gate"], w["up"], w["down"], w["sh_gate"], w["sh_up"],
+                           w["sh_down"], k, True, avail=mask, want_probs=False)["y"]
+    torch.cuda.synchronize()
+    ops.check_status(torch.device(DEV))
+    rel = (torch.linalg.vector_norm(y.float() - full.float()) / torch.linalg.vector_norm(full.float())).item()
+    assert rel <= 1e-2
+    assert m.last_send_counts == m.last_recv_counts
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_ranks_nccl_match_single_device():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    cfg = dict(E=16, k=4, H=512, F=256, S=1, n=200)
+    procs = [ctx.Process(target=_ep_worker.gpu_rank, args=(r, 2, port, q, cfg)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = []
+    try:
+        for _ in range(2):
+            res.append(q.get(timeout=240))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+                p.join()
+    res.sort(key=lambda r: r[1])
+    for status, rank, val, sc, rc in res:
+        assert status == "ok", val
+        assert val <= 1e-2, (rank, val)
+    assert res[0][3][1] == res[1][4][0] and res[1][3][0] == res[0][4][1]
