@@ -2,7 +2,7 @@
 """Benchmark of the sm_100a Chronos MoE feed-forward layer.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|prefill]
+                    [--workload decode|prefill|ep]
 
 Prints ONE JSON line (rank 0).  Workloads (synthetic data, seeded; weights
 N(0, 0.02), hidden states N(0, 1)):
@@ -16,8 +16,13 @@ N(0, 0.02), hidden states N(0, 1)):
 * ``prefill``: the same layer on 8192 tokens, router logits offset by a
   Zipf(s=1.1) per-expert bias, all experts available.  One step = one call.
 
-Both workloads are measured in every run; ``--workload`` picks the one the
-headline ``value`` reports, the other appears as a sub-object.  ``e2e``
+* ``ep``: the DeepSeek-V3-shaped layer (d_model 7168, 256 routed experts
+  top-8 + 1 shared, d_ff 2048, bf16), 4096 tokens per GPU, routed experts
+  sharded evenly over the GPUs with NCCL all-to-all dispatch/combine (one
+  GPU: all experts local, no exchange).  One step = one layer call per rank.
+
+All workloads are measured in every run; ``--workload`` picks the one the
+headline ``value`` reports, the others appear as sub-objects.  ``e2e``
 drives the public module (``ChronosMOEFeedForward``) with pinned host inputs:
 H2D copy, layer, D2H copy inside the timed region.  ``roofline`` is the
 dominant kernel of the headline workload, timed per launch with CUDA events
@@ -28,9 +33,10 @@ around that kernel (stage events inside the extension).  ``cpu_baseline``
 port: router restated in C, experts in numpy/BLAS with every host thread) on
 the same workload and prints the same metric with "impl": "reference".
 
-Multi-GPU (torchrun, one process per GPU): every rank runs an independent
-replica of the workload (the layer does not shard without expert
-parallelism); ``value`` = tokens of all ranks / max-over-ranks device time.
+Multi-GPU (torchrun, one process per GPU): decode and prefill run an
+independent replica per rank (those layers do not shard); ``ep`` shards the
+experts over the ranks.  ``value`` = tokens of all ranks / max-over-ranks
+device time.
 """
 from __future__ import annotations
 
@@ -355,6 +361,9 @@ def run_ours(args, dist: Dist):
         h2d = sum(x_host[b].numel() * x_host[b].element_size() for b in DECODE_BATCHES)
         d2h = sum(y_host[b].numel() * y_host[b].element_size() for b in DECODE_BATCHES)
 
+        # ---------------- expert parallel (DeepSeek-V3 shape) ----------------
+        ep = run_ep(args, dist, dev, peaks, flush)
+
     clocks = sampler.stop()
 
     # ---------------- assemble ----------------
@@ -418,33 +427,97 @@ def run_ours(args, dist: Dist):
                ms_per_step=round(e2e_ms, 4),
                path="ChronosMOEFeedForward.forward (eager), pinned host x -> device -> host y")
 
-    head = decode if args.workload == "decode" else prefill
+    head = {"decode": decode, "prefill": prefill, "ep": ep}[args.workload]
+    workload_desc = {
+        "decode": ("decode: MoE layer d_model 2048, 64 experts top-6 + 2 shared, d_ff 1408 "
+                   "(DeepSeek-MoE-16B shape), batches 1/8/32/64, availability Bernoulli(0.9)"),
+        "prefill": "prefill: same layer, 8192 tokens, Zipf(1.1) router bias, all available",
+        "ep": ("expert parallel: MoE layer d_model 7168, 256 experts top-8 + 1 shared, d_ff 2048 "
+               "(DeepSeek-V3 shape), 4096 tokens per GPU, experts sharded evenly over the GPUs, "
+               "NCCL all-to-all dispatch/combine"),
+    }[args.workload]
     line = {
         "metric": head["metric"], "value": head["value"], "unit": head["unit"],
         "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, N(0,0.02) weights)",
         "config": {
-            "workload": ("decode: MoE layer d_model 2048, 64 experts top-6 + 2 shared, d_ff 1408 "
-                         "(DeepSeek-MoE-16B shape), batches 1/8/32/64, availability "
-                         "Bernoulli(0.9)" if args.workload == "decode" else
-                         "prefill: same layer, 8192 tokens, Zipf(1.1) router bias, all available"),
+            "workload": workload_desc,
             "l2": "flushed before every timed call (256 MB write)",
             "graphs": "decode calls replayed as CUDA graphs" if args.workload == "decode" else "eager",
-            "parallelism": f"replicas x{dist.world}",
+            "parallelism": (f"ep{dist.world} (experts sharded)" if args.workload == "ep"
+                            else f"replicas x{dist.world} (decode/prefill), ep{dist.world} (ep)"),
         },
-        "roofline": dec_roof if args.workload == "decode" else pre_roof,
+        "roofline": {"decode": dec_roof, "prefill": pre_roof, "ep": ep["roofline"]}[args.workload],
         "e2e": e2e,
         "clocks": clocks,
-        "gpu_launches": decode["gpu_launches"] if args.workload == "decode" else pre_launches,
+        "gpu_launches": head["gpu_launches"],
         "decode": decode if args.workload != "decode" else {k: v for k, v in decode.items()
                                                             if k not in ("metric", "value", "unit")},
-        "prefill": prefill,
+        "prefill": prefill if args.workload != "prefill" else {k: v for k, v in prefill.items()
+                                                               if k not in ("metric", "value", "unit")},
+        "ep": ep if args.workload != "ep" else {k: v for k, v in ep.items()
+                                                 if k not in ("metric", "value", "unit")},
     }
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w, wl.x, mask_host, shape, args.workload,
                                             xp_dev=xp, bias=bias)
     return line
+
+
+def run_ep(args, dist: Dist, dev, peaks, flush) -> dict:
+    """Expert-parallel layer, DeepSeek-V3 shape, 4096 tokens per rank, experts
+    sharded over the ranks (one rank: all 256 experts local, no exchange)."""
+    import types
+    from project_chronos_b200 import ops, synthetic as syn
+    from project_chronos_b200.ep import ExpertParallelMoE
+
+    spec = syn.WORKLOADS["ep"]
+    shape = spec["shape"]
+    n = spec["tokens"]
+    w = syn.make_ep_weights(shape, dist.rank, dist.world, seed=4321, dtype=torch.bfloat16, device=dev)
+    x = syn.make_hidden(n, shape.hidden, syn.make_generator(777 + dist.rank, dev), dtype=torch.bfloat16,
+                        device=dev)
+    cfg = types.SimpleNamespace(hidden_size=shape.hidden, num_experts=shape.num_experts,
+                                num_experts_per_tok=shape.top_k, moe_intermediate_size=shape.ffn,
+                                num_shared_experts=shape.num_shared, norm_topk_prob=shape.norm_topk)
+    m = ExpertParallelMoE.from_stacked(cfg, w.router, w.gate, w.up, w.down, w.sh_gate, w.sh_up,
+                                       w.sh_down, local=True)
+    for _ in range(max(1, args.warmup)):
+        m(x)
+    torch.cuda.synchronize()
+    K = max(3, min(args.steps, 10))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    launches0 = ops.kernel_launches()
+    dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(K):
+        flush.zero_()
+        evs[i][0].record()
+        m(x)
+        evs[i][1].record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    launches = ops.kernel_launches() - launches0
+    ms = dist.max(sum(a.elapsed_time(b) for a, b in evs) / K)
+    ops.check_status(dev)
+    H, F, E, k, S = shape.hidden, shape.ffn, shape.num_experts, shape.top_k, shape.num_shared
+    flops = 2.0 * n * (H * E + 3 * H * F * (k + S))          # per rank
+    tflops = flops / (ms / 1e3) / 1e12
+    sc = m.last_send_counts
+    remote_rows = sum(c for g, c in enumerate(sc) if g != dist.rank)
+    a2a_bytes = remote_rows * H * 2
+    roof = dict(kernel="expert-parallel layer (all kernels + all-to-all), per GPU", bound="tensor",
+                achieved=round(tflops, 1), peak=peaks["bf16_tflops_sustained"], unit="TFLOP/s",
+                frac=round(tflops / peaks["bf16_tflops_sustained"], 4), traffic=None,
+                algorithmic_flops_per_step=flops, peak_source=peaks["source"] + " (sustained)")
+    return dict(metric="MoE-layer tokens/s (expert parallel, DeepSeek-V3 shape, 4096 tokens/GPU)",
+                value=round(n * dist.world / (ms / 1e3), 1), unit="tokens/s", ms_per_step=round(ms, 4),
+                steps=K, ranks=dist.world, experts_per_rank=E // dist.world,
+                layer_tflops_per_gpu=round(tflops, 1),
+                a2a_bytes_per_gpu_per_direction=int(a2a_bytes),
+                a2a_gbs_if_serial=round(a2a_bytes / (ms / 1e3) / 1e9, 1),
+                send_counts_rank0=sc, gpu_launches=launches, roofline=roof)
 
 
 # ---------------------------------------------------------------------------
@@ -556,7 +629,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "prefill"), default="decode")
+    ap.add_argument("--workload", choices=("decode", "prefill", "ep"), default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -107,6 +107,34 @@ def make_weights(shape: MoEShape, g: torch.Generator, dtype=torch.float32, devic
     return MoEWeights(router, gate, up, down, sh_gate, sh_up, sh_down)
 
 
+def make_ep_weights(shape: MoEShape, rank: int, world: int, seed: int = 0, dtype=torch.bfloat16,
+                    device="cpu", std: float = 0.02) -> MoEWeights:
+    """Weights of one expert-parallel rank: the router and shared experts
+    (replicated, from ``seed``) and ONLY this rank's routed experts
+    ``[rank*E/G, (rank+1)*E/G)``, expert e drawn from its own generator
+    (``seed * 1000003 + 1 + e``) so every rank agrees on every expert without
+    materialising the others."""
+    e, h, f, s = shape.num_experts, shape.hidden, shape.ffn, shape.num_shared
+    epr = e // world
+    g = make_generator(seed, device)
+    router = _randn(g, (e, h), std, device).to(dtype)
+    sh = [torch.empty(s, f, h, dtype=dtype, device=device), torch.empty(s, f, h, dtype=dtype, device=device),
+          torch.empty(s, h, f, dtype=dtype, device=device)]
+    for j in range(s):
+        sh[0][j].copy_(_randn(g, (f, h), std, device))
+        sh[1][j].copy_(_randn(g, (f, h), std, device))
+        sh[2][j].copy_(_randn(g, (h, f), std, device))
+    gate = torch.empty(epr, f, h, dtype=dtype, device=device)
+    up = torch.empty(epr, f, h, dtype=dtype, device=device)
+    down = torch.empty(epr, h, f, dtype=dtype, device=device)
+    for i in range(epr):
+        ge = make_generator(seed * 1000003 + 1 + rank * epr + i, device)
+        gate[i].copy_(_randn(ge, (f, h), std, device))
+        up[i].copy_(_randn(ge, (f, h), std, device))
+        down[i].copy_(_randn(ge, (h, f), std, device))
+    return MoEWeights(router, gate, up, down, sh[0], sh[1], sh[2])
+
+
 def make_hidden(n: int, hidden: int, g: torch.Generator, dtype=torch.float32,
                 device="cpu") -> torch.Tensor:
     """Step 4: hidden states N(0, 1), [N, H]."""
@@ -192,5 +220,5 @@ def decode_bytes(shape: MoEShape, tokens: int, experts_read: int, elem_bytes: in
 
 __all__ = ["MoEShape", "MoEWeights", "Workload", "WORKLOADS", "make_generator", "make_weights",
            "make_hidden", "make_mask", "make_zipf_bias", "make_workload", "named_workload",
-           "layer_flops", "decode_bytes", "expert_bytes", "flops_per_token_routed"]
+           "layer_flops", "decode_bytes", "expert_bytes", "flops_per_token_routed", "make_ep_weights"]
 
