@@ -2,6 +2,7 @@
 
     python -m project_chronos_b200.profile_case --workload prefill --calls 3
     python -m project_chronos_b200.profile_case --workload decode --tokens 1 --calls 3
+    python -m project_chronos_b200.profile_case --workload ep --calls 3
 
 Builds the named synthetic workload on cuda:0 (``synthetic.WORKLOADS``),
 calls ``ops.moe_forward`` ``--calls`` times with an L2 flush (256 MB write)
@@ -28,6 +29,8 @@ def main(argv=None) -> int:
     args = ap.parse_args(argv)
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if args.workload == "ep":
+        return _ep(args, dev)
     wl = syn.named_workload(args.workload, tokens=args.tokens, seed=args.seed, device=dev)
     w = wl.weights
     s = wl.shape
@@ -49,6 +52,37 @@ def main(argv=None) -> int:
     ops.check_status(dev)
     print(f"{args.workload} tokens={wl.x.shape[0]} calls={args.calls} "
           f"avg_ms={total_ms / args.calls:.4f}")
+    return 0
+
+
+def _ep(args, dev) -> int:
+    """The expert-parallel layer on one GPU (all experts local, no exchange)."""
+    import types
+    from .ep import ExpertParallelMoE
+    spec = syn.WORKLOADS["ep"]
+    shape = spec["shape"]
+    n = args.tokens or spec["tokens"]
+    w = syn.make_ep_weights(shape, 0, 1, seed=args.seed, dtype=torch.bfloat16, device=dev)
+    x = syn.make_hidden(n, shape.hidden, syn.make_generator(args.seed + 1, dev), dtype=torch.bfloat16,
+                        device=dev)
+    cfg = types.SimpleNamespace(hidden_size=shape.hidden, num_experts=shape.num_experts,
+                                num_experts_per_tok=shape.top_k, moe_intermediate_size=shape.ffn,
+                                num_shared_experts=shape.num_shared, norm_topk_prob=shape.norm_topk)
+    m = ExpertParallelMoE.from_stacked(cfg, w.router, w.gate, w.up, w.down, w.sh_gate, w.sh_up,
+                                       w.sh_down, local=True)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    total_ms = 0.0
+    for _ in range(args.calls):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        m(x)
+        b.record()
+        torch.cuda.synchronize()
+        total_ms += a.elapsed_time(b)
+    ops.check_status(dev)
+    print(f"ep tokens={n} calls={args.calls} avg_ms={total_ms / args.calls:.4f}")
     return 0
 
 
