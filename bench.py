@@ -504,7 +504,7 @@ def run_ep(args, dist: Dist, dev, peaks, flush) -> dict:
     H, F, E, k, S = shape.hidden, shape.ffn, shape.num_experts, shape.top_k, shape.num_shared
     flops = 2.0 * n * (H * E + 3 * H * F * (k + S))          # per rank
     tflops = flops / (ms / 1e3) / 1e12
-    sc = m.last_send_counts
+    sc = m.last_send_counts or [n * k]
     remote_rows = sum(c for g, c in enumerate(sc) if g != dist.rank)
     a2a_bytes = remote_rows * H * 2
     roof = dict(kernel="expert-parallel layer (all kernels + all-to-all), per GPU", bound="tensor",

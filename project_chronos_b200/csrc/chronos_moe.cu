@@ -307,7 +307,8 @@ int experts_per_lane(int num_experts) {
 // the parameters are returned for the fused select + plan kernel) the select kernel.
 template <typename T>
 int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool prerouted,
-                 int32_t* topk_idx, float* topk_w, bool zero_acc, RouteParams* out_params = nullptr) {
+                 int32_t* topk_idx, float* topk_w, bool zero_acc, RouteParams* out_params = nullptr,
+                 void* y_direct = nullptr) {
     const ChronosMoeShape& s = a->shape;
     RouteParams rp{};
     rp.x = a->x;
@@ -331,7 +332,8 @@ int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool p
     rp.pos = w.at<int32_t>(w.L->pos);
     rp.sel_coef = w.at<float>(w.L->sel_coef);
     rp.shared_coef = w.at<float>(w.L->shared_coef);
-    rp.y_acc = zero_acc ? w.at<float>(w.L->y_acc) : nullptr;
+    rp.y_acc = (zero_acc && y_direct == nullptr) ? w.at<float>(w.L->y_acc) : nullptr;
+    rp.y_direct = y_direct;
     rp.partials = w.at<float>(w.L->partials);
     const int64_t N = s.num_tokens;
     const bool small = N <= kRouteSmallMax;
@@ -400,7 +402,7 @@ int launch_tc(const CUtensorMap& a0r, const CUtensorMap& a1r, const CUtensorMap&
 
 template <typename T, int BN, int BN_DN>
 int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int splits_gu,
-                   int splits_dn, int kt_per_split_gu, int kt_per_split_dn, int slot) {
+                   int splits_dn, int kt_per_split_gu, int kt_per_split_dn, int slot, bool direct) {
     const ChronosMoeShape& s = a->shape;
     const int dt = s.dtype;
     const uint64_t N = static_cast<uint64_t>(s.num_tokens), H = s.hidden, F = s.ffn;
@@ -504,6 +506,7 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     pd.m_tiles = static_cast<int>((H + kTcBM - 1) / kTcBM);
     pd.w_rows = static_cast<int>(H);
     pd.out_cols = static_cast<int>(H);
+    pd.y_direct = direct ? a->y : nullptr;
     if ((rc = launch_tc<T, BN_DN, false, false>(d_r, d_r, d_s, d_s, h_m, h_m, pd, grid, st)))
         return rc;
     prof_ran(slot, CHRONOS_STAGE_DOWN);
@@ -645,6 +648,15 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
         splits_dn = (kt_total + kt_dn - 1) / kt_dn;
     }
 
+    // one contribution per token (k = 1, no shared experts, e.g. the rows an
+    // expert-parallel rank received): the down GEMM stores the output rows
+    // itself; no fp32 accumulator, no finalize pass
+    const bool direct = tc && s.top_k == 1 && s.num_shared == 0 && aligned16(a->y);
+    if (direct) {
+        splits_dn = 1;
+        kt_dn = s.ffn / kTcBK;
+    }
+
     int rc;
     // counters: zeroed by the logit kernel, or here when routing is skipped
     if (prerouted)
@@ -654,7 +666,8 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     const bool fused_plan = N <= kSelectPlanMaxTokens;
     RouteParams rp{};
     prof_mark(slot, CHRONOS_STAGE_ROUTE, st);
-    if ((rc = launch_route<T>(a, w, st, prerouted, topk_idx, topk_w, true, fused_plan ? &rp : nullptr)))
+    if ((rc = launch_route<T>(a, w, st, prerouted, topk_idx, topk_w, true, fused_plan ? &rp : nullptr,
+                              direct ? a->y : nullptr)))
         return rc;
     prof_ran(slot, CHRONOS_STAGE_ROUTE);
     prof_mark(slot, CHRONOS_STAGE_PLAN, st);
@@ -723,13 +736,15 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
             return fail(CHRONOS_ERR_INVALID_ARG, "internal: fp32 on the tensor-core path");
         } else {
             switch (bn) {
-                case 16: rc = launch_tc_pair<T, 16, 16>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot); break;
-                case 32: rc = launch_tc_pair<T, 32, 32>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot); break;
-                case 64: rc = launch_tc_pair<T, 64, 64>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot); break;
+                case 16: rc = launch_tc_pair<T, 16, 16>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot, direct); break;
+                case 32: rc = launch_tc_pair<T, 32, 32>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot, direct); break;
+                case 64: rc = launch_tc_pair<T, 64, 64>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot, direct); break;
                 default:
                     rc = bn_dn == 256
-                             ? launch_tc_pair<T, 128, 256>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot)
-                             : launch_tc_pair<T, 128, 128>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot);
+                             ? launch_tc_pair<T, 128, 256>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot,
+                                                           direct)
+                             : launch_tc_pair<T, 128, 128>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot,
+                                                           direct);
                     break;
             }
         }
@@ -739,6 +754,10 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     if (rc) return rc;
 
     prof_mark(slot, CHRONOS_STAGE_FINALIZE, st);
+    if (direct) {
+        prof_mark(slot, kBoundaries - 1, st);
+        return CHRONOS_OK;
+    }
     const int64_t count4 = N * s.hidden / 4;
     const int blocks = static_cast<int>(std::min<int64_t>((count4 + 255) / 256, 8 * sm_count()));
     CHRONOS_CUDA_CHECK(launch_kernel(finalize_kernel<T>, dim3(blocks), dim3(256), 0, st, true,

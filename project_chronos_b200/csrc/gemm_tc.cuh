@@ -65,6 +65,10 @@ struct TcGemmParams {
     // the token did not choose the expert (or it is unavailable); [E, n_tokens]
     const int32_t* slot_map;
     int64_t n_tokens;
+    // DOWN, one contribution per token (k = 1, no shared experts): rows of
+    // coef * D stored straight into the output [N, H] (x dtype) instead of
+    // reduce-added into y_acc; null otherwise
+    void* y_direct;
 };
 
 __host__ __device__ constexpr int tc_stage_bytes(int bn, bool gateup) {
@@ -363,10 +367,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         }
                     } else {
                         tmem_wait_ld();
+                        if (p.y_direct != nullptr) {
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            reinterpret_cast<float*>(staging + (c - c0 + j) * ROW_BYTES)[row_in_tile] =
-                                cf[c + j] * g[j];
+                            for (int j = 0; j < 16; ++j)
+                                reinterpret_cast<T*>(staging + (c - c0 + j) * ROW_BYTES)[row_in_tile] =
+                                    from_f32<T>(cf[c + j] * g[j]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                reinterpret_cast<float*>(staging + (c - c0 + j) * ROW_BYTES)[row_in_tile] =
+                                    cf[c + j] * g[j];
                         }
                     }
                 }
@@ -403,8 +413,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         }
                     } else {
                         const int64_t t = tk[c0 + r];
-                        bulk_reduce_add_f32(p.y_acc + t * p.h + m0, row,
-                                            static_cast<uint32_t>(ncols * 4));
+                        if (p.y_direct != nullptr)
+                            bulk_store(static_cast<T*>(p.y_direct) + t * p.h + m0, row,
+                                       static_cast<uint32_t>(ncols * sizeof(T)));
+                        else
+                            bulk_reduce_add_f32(p.y_acc + t * p.h + m0, row,
+                                                static_cast<uint32_t>(ncols * 4));
                     }
                 }
                 bulk_commit();

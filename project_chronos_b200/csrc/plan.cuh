@@ -276,6 +276,7 @@ __global__ void __launch_bounds__(kSelectPlanThreads)
         if (lane < k) rp.pos[t * k + lane] = mine_a > 0.0f ? atomicAdd(&rp.grp_count[mine_e], 1) : -1;
         if (lane == 0 && rp.num_shared > 0)
             rp.shared_coef[t] = (1.0f + shared_extra) / static_cast<float>(rp.num_shared);
+        zero_direct_row<T>(rp, t, lane, mine_a);
     }
 
     // 2) the last block to arrive sees every block's counts and tables

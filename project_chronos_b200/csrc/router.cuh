@@ -53,6 +53,8 @@ struct RouteParams {
     float* sel_coef;      // [N, k] w * a
     float* shared_coef;   // [N] (1 + sum w (1 - a)) / S_h
     float* y_acc;         // [N, H] fp32, zeroed here (or null)
+    void* y_direct;       // k = 1, no shared experts: the output [N, H]; rows of tokens
+                          // whose one selection is unavailable are zeroed here (or null)
 };
 
 // The logit kernels run first in a call: their first block zeroes the
@@ -443,6 +445,18 @@ __device__ __forceinline__ void select_token(const RouteParams& p, int64_t t, in
     }
 }
 
+// Direct-output calls (k = 1, no shared experts): a token whose selection is
+// unavailable gets no contribution, so its output row is zeroed here.
+template <typename T>
+__device__ __forceinline__ void zero_direct_row(const RouteParams& p, int64_t t, int lane, float mine_a) {
+    if (p.y_direct == nullptr) return;
+    const float a0 = __shfl_sync(0xffffffffu, mine_a, 0);
+    if (a0 > 0.0f) return;
+    uint4* yv = reinterpret_cast<uint4*>(static_cast<T*>(p.y_direct) + t * p.h);
+    const int n16 = p.h * static_cast<int>(sizeof(T)) / 16;
+    for (int i = lane; i < n16; i += 32) yv[i] = make_uint4(0u, 0u, 0u, 0u);
+}
+
 // One warp per token: select, then a global atomic gives each available
 // selection its position in its expert group.
 template <typename T, int EPL>
@@ -462,6 +476,7 @@ __global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParam
     if (lane < p.k) p.pos[t * p.k + lane] = mine_a > 0.0f ? atomicAdd(&p.grp_count[mine_e], 1) : -1;
     if (lane == 0 && p.num_shared > 0)
         p.shared_coef[t] = (1.0f + shared_extra) / static_cast<float>(p.num_shared);
+    zero_direct_row<T>(p, t, lane, mine_a);
 }
 
 }  // namespace chronos

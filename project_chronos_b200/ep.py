@@ -3,7 +3,9 @@
 The reference runs every expert of a layer on one device
 (``chronos/model/moe_chronos.py:146-173, 190-268``).  Here rank g of a group of
 G owns the routed experts ``[g*E/G, (g+1)*E/G)``; the router and the shared
-experts are replicated; tokens stay on their rank.  One forward:
+experts are replicated; tokens stay on their rank.  One forward (with one rank
+and ``dispatch_single_rank=False``, the default, it is the single-device layer
+call instead):
 
 1. route the rank's tokens (router kernels, bit-exact routing contract);
 2. ``chronos_ep_dispatch``: rows of x grouped by destination rank, with
@@ -36,8 +38,10 @@ from . import ops
 
 
 class ExpertParallelMoE(nn.Module):
-    def __init__(self, config, group: Optional["dist.ProcessGroup"] = None, backend=None):
+    def __init__(self, config, group: Optional["dist.ProcessGroup"] = None, backend=None,
+                 dispatch_single_rank: bool = False):
         super().__init__()
+        self.dispatch_single_rank = bool(dispatch_single_rank)
         self.config = config
         self.group = group
         if dist.is_available() and dist.is_initialized():
@@ -66,11 +70,12 @@ class ExpertParallelMoE(nn.Module):
     def from_stacked(cls, config, router: torch.Tensor, gate: torch.Tensor, up: torch.Tensor,
                      down: torch.Tensor, sh_gate: Optional[torch.Tensor] = None,
                      sh_up: Optional[torch.Tensor] = None, sh_down: Optional[torch.Tensor] = None,
-                     group=None, backend=None, local: bool = False) -> "ExpertParallelMoE":
+                     group=None, backend=None, local: bool = False,
+                     dispatch_single_rank: bool = False) -> "ExpertParallelMoE":
         """Build from stacked weights.  ``local=False``: gate/up/down hold all E
         experts and this rank keeps its slice (a view); ``local=True``: they
         already hold only this rank's E/G experts."""
-        m = cls(config, group=group, backend=backend)
+        m = cls(config, group=group, backend=backend, dispatch_single_rank=dispatch_single_rank)
         lo, n = m.first_expert, m.experts_per_rank
         if not local:
             gate, up, down = gate[lo:lo + n], up[lo:lo + n], down[lo:lo + n]
@@ -114,6 +119,14 @@ class ExpertParallelMoE(nn.Module):
         avail = None
         if available_expert_mask is not None:
             avail = available_expert_mask.to(device=dev, dtype=torch.float32)
+
+        if G == 1 and not self.dispatch_single_rank:
+            # one rank owns every expert: the single-device layer, no dispatch
+            y = be.moe_forward(xf, self.router, self.w_gate, self.w_up, self.w_down, self.sh_gate,
+                               self.sh_up, self.sh_down, k, self.norm_topk_prob, avail=avail,
+                               router_bias=self.router_logit_bias, want_probs=False)["y"]
+            self.last_send_counts = self.last_recv_counts = None
+            return y.view(shp)
 
         # 1-2: route, build the send buffers
         r = be.moe_route(xf, self.router, k, self.norm_topk_prob, num_shared=self.num_shared,

@@ -66,8 +66,9 @@ def test_dispatch_and_combine_match_oracle(dtype, world, n):
     assert torch.equal(y.cpu(), want)
 
 
+@pytest.mark.parametrize("dispatch", [False, True])
 @pytest.mark.parametrize("masked", [False, True])
-def test_single_rank_layer_matches_single_device(masked):
+def test_single_rank_layer_matches_single_device(masked, dispatch):
     from project_chronos_b200 import ops
     from project_chronos_b200.ep import ExpertParallelMoE
     E, k, H, F, S, n = 16, 4, 256, 128, 1, 96
@@ -77,7 +78,8 @@ def test_single_rank_layer_matches_single_device(masked):
     if masked:
         mask = (torch.rand(E, generator=torch.Generator().manual_seed(6)) > 0.3).float().to(DEV)
     m = ExpertParallelMoE.from_stacked(_ep_worker._cfg(E, k, H, F, S), w["router"], w["gate"], w["up"],
-                                       w["down"], w["sh_gate"], w["sh_up"], w["sh_down"])
+                                       w["down"], w["sh_gate"], w["sh_up"], w["sh_down"],
+                                       dispatch_single_rank=dispatch)
     y = m(x.view(2, n // 2, H), available_expert_mask=mask).view(n, H)
     full = ops.moe_forward(x, w["router"], w["gate"], w["up"], w["down"], w["sh_gate"], w["sh_up"],
                            w["sh_down"], k, True, avail=mask, want_probs=False)["y"]

@@ -163,6 +163,29 @@ def test_no_shared_experts_and_nothing_available_gives_zero(n):
     assert float(out["y"].float().abs().max()) == 0.0
 
 
+@pytest.mark.parametrize("n", [1, 5, 64, 65, 700])
+def test_one_choice_no_shared_direct_output(n):
+    """k = 1, S_h = 0: the down GEMM stores the output rows itself (no fp32
+    accumulator); tokens whose one expert is unavailable get exact zeros;
+    fractional availability scales the row.  The output buffer starts as
+    garbage (NaN-filled) so every row must be written."""
+    wl = _workload(256, 8, 1, 192, 0, n, seed=40 + n)
+    avail = torch.tensor([1.0, 0.0, 1.0, 0.5, 1.0, 0.0, 1.0, 1.0], device=DEV)
+    y0 = torch.full((n, 256), float("nan"), dtype=wl.x.dtype, device=DEV)
+    out = _run(wl, 1, False, avail=avail, out=y0)
+    torch.cuda.synchronize()
+    _ops().check_status()
+    y = _np(out["y"])
+    ref, o_idx, _, _ = _oracle(wl, 1, False, avail=avail)
+    assert np.array_equal(out["topk_idx"].cpu().numpy(), o_idx)
+    assert np.isfinite(y).all()
+    dead = np.isin(o_idx[:, 0], [1, 5])
+    assert (y[dead] == 0.0).all()
+    assert O.rel_l2(y, ref) <= 1e-2
+    emu, *_ = _oracle(wl, 1, False, avail=avail, emulate=True)
+    assert O.rel_l2(y, emu) <= 3e-3
+
+
 def test_fractional_availability_blend():
     # a_e in (0,1): y = sum w (a E + (1-a) S) + S  (chronos/mlx/moe.py:162)
     wl = _workload(128, 8, 2, 128, 1, 24, seed=5)
