@@ -16,6 +16,9 @@ N(0, 0.02), hidden states N(0, 1)):
 * ``prefill``: the same layer on 8192 tokens, router logits offset by a
   Zipf(s=1.1) per-expert bias, all experts available.  One step = one call.
 
+* ``e2e_decode`` (sub-object): the MoE FFNs of an 8-layer decode (d_model 1024,
+  16 experts top-2 + 1 shared, d_ff 2048, batch 32, 512-token prompt, 256
+  steps, availability Bernoulli(0.85) per step and layer, ready flags on).
 * ``ep``: the DeepSeek-V3-shaped layer (d_model 7168, 256 routed experts
   top-8 + 1 shared, d_ff 2048, bf16), 4096 tokens per GPU, routed experts
   sharded evenly over the GPUs with NCCL all-to-all dispatch/combine (one
@@ -363,6 +366,8 @@ def run_ours(args, dist: Dist):
 
         # ---------------- expert parallel (DeepSeek-V3 shape) ----------------
         ep = run_ep(args, dist, dev, peaks, flush)
+        # ---------------- 8-layer decode, MoE FFNs (e2e workload) ----------------
+        e2e_dec = run_e2e_decode(args, dist, dev, peaks)
 
     clocks = sampler.stop()
 
@@ -458,11 +463,128 @@ def run_ours(args, dist: Dist):
                                                                if k not in ("metric", "value", "unit")},
         "ep": ep if args.workload != "ep" else {k: v for k, v in ep.items()
                                                  if k not in ("metric", "value", "unit")},
+        "e2e_decode": e2e_dec,
     }
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w, wl.x, mask_host, shape, args.workload,
                                             xp_dev=xp, bias=bias)
     return line
+
+
+E2E_LAYERS = 8
+E2E_PROMPT = 512
+E2E_STEPS = 256
+
+
+def run_e2e_decode(args, dist: Dist, dev, peaks) -> dict:
+    """The MoE FFNs of an 8-layer decode: d_model 1024, 16 experts top-2 + 1 shared,
+    d_ff 2048, bf16, batch 32, a 512-token prompt then 256 decode steps; every
+    layer's availability mask is a fresh Bernoulli(0.85) draw per step (experts
+    drawn unavailable are served by the shared fallback, as a non-resident expert
+    is) and the per-expert device ready flags are on.  Only the MoE layers run
+    (h <- h + MoE_l(h)); attention, embeddings and the LM head are not part of
+    this build.  Each decode step (8 layer calls) is one CUDA-graph replay after
+    the step's masks are copied into the graph's mask buffers."""
+    from project_chronos_b200 import ops, synthetic as syn
+
+    spec = syn.WORKLOADS["e2e"]
+    shape = spec["shape"]
+    B = spec["tokens"]
+    E, L = shape.num_experts, E2E_LAYERS
+    layers = [syn.make_workload(shape, 1, seed=5000 + 17 * l, dtype=torch.bfloat16, device=dev).weights
+              for l in range(L)]
+    g = syn.make_generator(6000 + dist.rank, dev)
+    prompt = syn.make_hidden(B * E2E_PROMPT, shape.hidden, g, dtype=torch.bfloat16, device=dev)
+    h0 = syn.make_hidden(B, shape.hidden, g, dtype=torch.bfloat16, device=dev)
+    masks = (torch.rand(E2E_STEPS, L, E, generator=g, device=dev) < spec["avail_p"]).float()
+    flags = torch.ones(E, dtype=torch.int32, device=dev)
+    cur = torch.ones(L, E, dtype=torch.float32, device=dev)
+    ws = {}
+
+    def layer(l, x, avail):
+        w = layers[l]
+        key = x.shape[0]
+        if key not in ws:
+            ws[key] = torch.empty(ops.workspace_bytes(key, shape.hidden, E, shape.top_k, shape.ffn,
+                                                      shape.num_shared, torch.bfloat16),
+                                  dtype=torch.uint8, device=dev)
+        return ops.moe_forward(x, w.router, w.gate, w.up, w.down, w.sh_gate, w.sh_up, w.sh_down,
+                               shape.top_k, shape.norm_topk, avail=avail, ready_flags=flags,
+                               ready_epoch=1, want_probs=False, workspace=ws[key])["y"]
+
+    # prompt: the 8 layers on B*512 tokens (all experts available)
+    def prefill():
+        x = prompt
+        for l in range(L):
+            x = x + layer(l, x, None)
+        return x
+
+    for _ in range(2):
+        prefill()
+    torch.cuda.synchronize()
+    pa, pb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pa.record()
+    prefill()
+    pb.record()
+    torch.cuda.synchronize()
+    prompt_ms = pa.elapsed_time(pb)
+
+    # decode step graph
+    h = h0.clone()
+
+    def step():
+        x = h
+        for l in range(L):
+            x = x + layer(l, x, cur[l])
+        h.copy_(x)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    before = ops.kernel_launches()
+    with torch.cuda.graph(graph):
+        step()
+    launches_per_step = ops.kernel_launches() - before
+    h.copy_(h0)
+    for t in range(3):
+        cur.copy_(masks[t])
+        graph.replay()
+    torch.cuda.synchronize()
+    h.copy_(h0)
+    dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for t in range(E2E_STEPS):
+        cur.copy_(masks[t])
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ops.check_status(dev)
+    ms = dist.max(a.elapsed_time(b)) / E2E_STEPS
+    # algorithmic bytes of a step: per layer the router, the shared expert and every
+    # selected expert that is available, each read once (expected over the masks:
+    # the realised selection is counted on the last step's inputs, eagerly)
+    ebytes = syn.expert_bytes(shape)
+    x = h.clone()
+    tot = 0
+    for l in range(L):
+        w = layers[l]
+        r = ops.moe_route(x, w.router, shape.top_k, shape.norm_topk, want_probs=False)
+        sel = set(r["topk_idx"].view(-1).tolist())
+        avail_sel = [e for e in sel if masks[-1, l, e] > 0]
+        tot += ebytes * (len(avail_sel) + shape.num_shared) + E * shape.hidden * 2
+        x = x + layer(l, x, masks[-1, l])
+    hbm = tot / (ms / 1e3) / 1e9
+    return dict(metric="MoE FFN time per decode step, 8 layers (e2e decode workload)",
+                us_per_step=round(ms * 1e3, 2), tokens_per_s_moe_only=round(B * dist.world / (ms / 1e3), 1),
+                step_bytes=int(tot), step_gbs=round(hbm, 1), hbm_frac=round(hbm / peaks["hbm_gbs"], 4),
+                prompt_ms=round(prompt_ms, 3), prompt_tokens=B * E2E_PROMPT, steps=E2E_STEPS,
+                gpu_launches_per_step=launches_per_step,
+                note=("MoE layers only; attention/embedding/LM head not built; masks Bernoulli(0.85) per "
+                      "step and layer; device ready flags on; one CUDA graph replay per step"))
 
 
 def run_ep(args, dist: Dist, dev, peaks, flush) -> dict:
