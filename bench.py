@@ -481,10 +481,12 @@ def run_e2e_decode(args, dist: Dist, dev, peaks) -> dict:
     d_ff 2048, bf16, batch 32, a 512-token prompt then 256 decode steps; every
     layer's availability mask is a fresh Bernoulli(0.85) draw per step (experts
     drawn unavailable are served by the shared fallback, as a non-resident expert
-    is) and the per-expert device ready flags are on.  Only the MoE layers run
-    (h <- h + MoE_l(h)); attention, embeddings and the LM head are not part of
-    this build.  Each decode step (8 layer calls) is one CUDA-graph replay after
-    the step's masks are copied into the graph's mask buffers."""
+    is) and the per-expert device ready flags are on.  Only the MoE layers run;
+    attention, embeddings and the LM head are not part of this build, so each
+    layer call of a step gets its own fresh N(0, 1) hidden states (what attention
+    would hand it) instead of the previous layer's output.  Each decode step (8
+    layer calls) is one CUDA-graph replay after the step's masks and inputs are
+    copied into the graph's buffers."""
     from project_chronos_b200 import ops, synthetic as syn
 
     spec = syn.WORKLOADS["e2e"]
@@ -495,7 +497,8 @@ def run_e2e_decode(args, dist: Dist, dev, peaks) -> dict:
               for l in range(L)]
     g = syn.make_generator(6000 + dist.rank, dev)
     prompt = syn.make_hidden(B * E2E_PROMPT, shape.hidden, g, dtype=torch.bfloat16, device=dev)
-    h0 = syn.make_hidden(B, shape.hidden, g, dtype=torch.bfloat16, device=dev)
+    inputs = syn.make_hidden(E2E_STEPS * L * B, shape.hidden, g, dtype=torch.bfloat16,
+                             device=dev).view(E2E_STEPS, L, B, shape.hidden)
     masks = (torch.rand(E2E_STEPS, L, E, generator=g, device=dev) < spec["avail_p"]).float()
     flags = torch.ones(E, dtype=torch.int32, device=dev)
     cur = torch.ones(L, E, dtype=torch.float32, device=dev)
@@ -514,10 +517,8 @@ def run_e2e_decode(args, dist: Dist, dev, peaks) -> dict:
 
     # prompt: the 8 layers on B*512 tokens (all experts available)
     def prefill():
-        x = prompt
         for l in range(L):
-            x = x + layer(l, x, None)
-        return x
+            layer(l, prompt, None)
 
     for _ in range(2):
         prefill()
@@ -530,13 +531,11 @@ def run_e2e_decode(args, dist: Dist, dev, peaks) -> dict:
     prompt_ms = pa.elapsed_time(pb)
 
     # decode step graph
-    h = h0.clone()
+    xin = torch.empty(L, B, shape.hidden, dtype=torch.bfloat16, device=dev)
 
     def step():
-        x = h
         for l in range(L):
-            x = x + layer(l, x, cur[l])
-        h.copy_(x)
+            layer(l, xin[l], cur[l])
 
     for _ in range(3):
         step()
@@ -546,37 +545,37 @@ def run_e2e_decode(args, dist: Dist, dev, peaks) -> dict:
     with torch.cuda.graph(graph):
         step()
     launches_per_step = ops.kernel_launches() - before
-    h.copy_(h0)
     for t in range(3):
         cur.copy_(masks[t])
+        xin.copy_(inputs[t])
         graph.replay()
     torch.cuda.synchronize()
-    h.copy_(h0)
     dist.barrier()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for t in range(E2E_STEPS):
         cur.copy_(masks[t])
+        xin.copy_(inputs[t])
         graph.replay()
     b.record()
     torch.cuda.synchronize()
     dist.barrier()
     ops.check_status(dev)
     ms = dist.max(a.elapsed_time(b)) / E2E_STEPS
-    # algorithmic bytes of a step: per layer the router, the shared expert and every
-    # selected expert that is available, each read once (expected over the masks:
-    # the realised selection is counted on the last step's inputs, eagerly)
+    # algorithmic bytes per step: per layer the router weight, the shared expert and
+    # every selected expert that is available, each read once (mean over 16 steps)
     ebytes = syn.expert_bytes(shape)
-    x = h.clone()
     tot = 0
-    for l in range(L):
-        w = layers[l]
-        r = ops.moe_route(x, w.router, shape.top_k, shape.norm_topk, want_probs=False)
-        sel = set(r["topk_idx"].view(-1).tolist())
-        avail_sel = [e for e in sel if masks[-1, l, e] > 0]
-        tot += ebytes * (len(avail_sel) + shape.num_shared) + E * shape.hidden * 2
-        x = x + layer(l, x, masks[-1, l])
+    sample = range(0, E2E_STEPS, E2E_STEPS // 16)
+    for t in sample:
+        for l in range(L):
+            r = ops.moe_route(inputs[t, l], layers[l].router, shape.top_k, shape.norm_topk,
+                              want_probs=False)
+            sel = set(r["topk_idx"].view(-1).tolist())
+            avail_sel = [e for e in sel if masks[t, l, e] > 0]
+            tot += ebytes * (len(avail_sel) + shape.num_shared) + E * shape.hidden * 2
+    tot //= len(sample)
     hbm = tot / (ms / 1e3) / 1e9
     return dict(metric="MoE FFN time per decode step, 8 layers (e2e decode workload)",
                 us_per_step=round(ms * 1e3, 2), tokens_per_s_moe_only=round(B * dist.world / (ms / 1e3), 1),

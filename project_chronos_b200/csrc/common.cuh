@@ -118,6 +118,45 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         : "memory");
 }
 
+// Same load with an L2 cache policy (from l2_evict_first_policy): for operands
+// read exactly once, so they do not displace lines that will be read again.
+__device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                                 int32_t c0, int32_t c1, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// Asynchronous prefetch of [p, p + bytes) into L2 (a hint; no completion).
+// p 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// Prefetch the byte range [base, base + bytes) into L2 in 64 KB pieces, piece i
+// by thread i of `nthreads` cooperating threads (thread `tid`).
+__device__ __forceinline__ void prefetch_l2_range(const void* base, uint64_t bytes, uint64_t tid,
+                                                  uint64_t nthreads) {
+    constexpr uint64_t kPiece = 64 << 10;
+    const uint64_t pieces = (bytes + kPiece - 1) / kPiece;
+    const uint8_t* b = static_cast<const uint8_t*>(base);
+    for (uint64_t i = tid; i < pieces; i += nthreads) {
+        const uint64_t off = i * kPiece;
+        const uint64_t n = (bytes - off < kPiece ? bytes - off : kPiece) & ~uint64_t(15);
+        if (n > 0) prefetch_l2_bulk(b + off, static_cast<uint32_t>(n));
+    }
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -201,6 +201,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             int stage = 0;
             uint32_t phase = 0;
             int polled_eid = -1;
+            // decode tiles (one token tile per group): weights streamed once, evict first
+            constexpr bool kStreamA = BN <= 64;
+            const uint64_t pol_a = kStreamA ? l2_evict_first_policy() : 0ull;
             for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
                 const TcUnit w = tc_decode(p, num_active, u, BN, splits_unused);
                 const int eid = p.act_eid[w.a];
@@ -235,8 +238,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                     uint8_t* sb = smem + stage * STAGE_BYTES;
                     mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-                    tma_load_2d(sb, ma0, &full[stage], kt * kTcBK, a_row);
-                    if (GATEUP) tma_load_2d(sb + A_BYTES, ma1, &full[stage], kt * kTcBK, a_row);
+                    if constexpr (kStreamA) {
+                        // decode tiles: every weight tile is read once per call
+                        tma_load_2d_hint(sb, ma0, &full[stage], kt * kTcBK, a_row, pol_a);
+                        if (GATEUP) tma_load_2d_hint(sb + A_BYTES, ma1, &full[stage], kt * kTcBK, a_row, pol_a);
+                    } else {
+                        tma_load_2d(sb, ma0, &full[stage], kt * kTcBK, a_row);
+                        if (GATEUP) tma_load_2d(sb + A_BYTES, ma1, &full[stage], kt * kTcBK, a_row);
+                    }
                     tma_load_2d(sb + (GATEUP ? 2 : 1) * A_BYTES, mb, &full[stage], kt * kTcBK, b_row_eff);
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
