@@ -52,9 +52,6 @@ int fail(int code, const char* fmt, ...) {
     } while (0)
 
 constexpr int kSplitMaxTokens = 64;  // decode batches up to this size may split K
-// L2 bytes of routed gate/up weights a decode call prefetches while routing runs
-// (with the shared experts' weights this stays well inside the 126 MB L2)
-constexpr uint64_t kPrefetchBudgetBytes = 64ull << 20;
 constexpr int kDownWideMinTokens = 1024;  // batches from this size use 256-token down tiles
 
 std::atomic<uint64_t> g_kernel_launches{0};
@@ -133,7 +130,7 @@ Layout make_layout(const ChronosMoeShape& s) {
         off = align_up(off + bytes, 256);
         return o;
     };
-    L.grp_count = take(4 * (E + 2));  // + decode select/plan ticket, prefetch-claim counter
+    L.grp_count = take(4 * (E + 1));  // + the ticket of the decode select + plan kernel
     L.grp_off = take(4 * E);
     L.act_rows = take(4 * G);
     L.act_xrow = take(4 * G);
@@ -337,21 +334,6 @@ int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool p
     rp.shared_coef = w.at<float>(w.L->shared_coef);
     rp.y_acc = (zero_acc && y_direct == nullptr) ? w.at<float>(w.L->y_acc) : nullptr;
     rp.y_direct = y_direct;
-    if (out_params != nullptr && s.dtype != CHRONOS_DTYPE_FP32 && a->w_gate != nullptr) {
-        // decode batches: prefetch into L2, while routing runs, the shared experts'
-        // weights and the gate/up rows of the first routed experts selected
-        const uint64_t eb = static_cast<uint64_t>(s.ffn) * s.hidden * elem_size(s.dtype);
-        if (s.num_shared > 0 && a->w_shared_gate && a->w_shared_up && a->w_shared_down) {
-            rp.pf_shared[0] = a->w_shared_gate;
-            rp.pf_shared[1] = a->w_shared_up;
-            rp.pf_shared[2] = a->w_shared_down;
-            rp.pf_shared_bytes = eb * s.num_shared;
-        }
-        rp.pf_gate = a->w_gate;
-        rp.pf_up = a->w_up;
-        rp.pf_expert_bytes = eb;
-        rp.pf_max_experts = static_cast<int>(std::min<uint64_t>(s.num_experts, kPrefetchBudgetBytes / (2 * eb)));
-    }
     rp.partials = w.at<float>(w.L->partials);
     const int64_t N = s.num_tokens;
     const bool small = N <= kRouteSmallMax;
@@ -678,7 +660,7 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     int rc;
     // counters: zeroed by the logit kernel, or here when routing is skipped
     if (prerouted)
-        CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + L.grp_count, 0, 4 * (s.num_experts + 2), st));
+        CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + L.grp_count, 0, 4 * (s.num_experts + 1), st));
     const int slot = prof_begin_call();
     // decode batches: the routing selection, plan and slot tables run in one block
     const bool fused_plan = N <= kSelectPlanMaxTokens;

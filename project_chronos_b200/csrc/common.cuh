@@ -135,28 +135,6 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     return pol;
 }
 
-// Asynchronous prefetch of [p, p + bytes) into L2 (a hint; no completion).
-// p 16-byte aligned, bytes a multiple of 16.
-__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-// Prefetch the byte range [base, base + bytes) into L2 in 64 KB pieces, piece i
-// by thread i of `nthreads` cooperating threads (thread `tid`).
-__device__ __forceinline__ void prefetch_l2_range(const void* base, uint64_t bytes, uint64_t tid,
-                                                  uint64_t nthreads) {
-    constexpr uint64_t kPiece = 64 << 10;
-    const uint64_t pieces = (bytes + kPiece - 1) / kPiece;
-    const uint8_t* b = static_cast<const uint8_t*>(base);
-    for (uint64_t i = tid; i < pieces; i += nthreads) {
-        const uint64_t off = i * kPiece;
-        const uint64_t n = (bytes - off < kPiece ? bytes - off : kPiece) & ~uint64_t(15);
-        if (n > 0) prefetch_l2_bulk(b + off, static_cast<uint32_t>(n));
-    }
-}
-
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

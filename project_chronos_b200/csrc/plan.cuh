@@ -273,30 +273,10 @@ __global__ void __launch_bounds__(kSelectPlanThreads)
         int mine_e;
         float mine_w, mine_a, shared_extra;
         select_token<T, EPL>(rp, t, lane, mine_e, mine_w, mine_a, shared_extra);
-        int my_pos = -1;
-        if (lane < k) {
-            my_pos = mine_a > 0.0f ? atomicAdd(&rp.grp_count[mine_e], 1) : -1;
-            rp.pos[t * k + lane] = my_pos;
-        }
+        if (lane < k) rp.pos[t * k + lane] = mine_a > 0.0f ? atomicAdd(&rp.grp_count[mine_e], 1) : -1;
         if (lane == 0 && rp.num_shared > 0)
             rp.shared_coef[t] = (1.0f + shared_extra) / static_cast<float>(rp.num_shared);
         zero_direct_row<T>(rp, t, lane, mine_a);
-        if (rp.pf_max_experts > 0) {
-            // the first selection of an expert claims its L2 prefetch (gate + up
-            // rows), up to pf_max_experts per call; the warp shares the pieces
-            bool want = my_pos == 0;
-            if (want) want = atomicAdd(&rp.grp_count[rp.e + 1], 1) < rp.pf_max_experts;
-            unsigned m = __ballot_sync(0xffffffffu, want);
-            while (m != 0u) {
-                const int src = __ffs(m) - 1;
-                m &= m - 1u;
-                const int e = __shfl_sync(0xffffffffu, mine_e, src);
-                const int64_t slot = rp.slot_of_expert ? rp.slot_of_expert[e] : e;
-                const uint64_t off = static_cast<uint64_t>(slot) * rp.pf_expert_bytes;
-                prefetch_l2_range(static_cast<const uint8_t*>(rp.pf_gate) + off, rp.pf_expert_bytes, lane, 32);
-                prefetch_l2_range(static_cast<const uint8_t*>(rp.pf_up) + off, rp.pf_expert_bytes, lane, 32);
-            }
-        }
     }
 
     // 2) the last block to arrive sees every block's counts and tables

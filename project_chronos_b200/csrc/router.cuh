@@ -48,32 +48,20 @@ struct RouteParams {
     float* topk_w;        // [N, k]
     int32_t* counts_all;  // [E] or null
     float* mass_all;      // [E] or null
-    int32_t* grp_count;   // [E + 2] routed-group sizes (selections with a > 0), then a ticket
-                          // counter and the prefetch-claim counter
+    int32_t* grp_count;   // [E + 1] routed-group sizes (selections with a > 0), then a ticket counter
     int32_t* pos;         // [N, k] position within the expert group, -1 when a == 0
     float* sel_coef;      // [N, k] w * a
     float* shared_coef;   // [N] (1 + sum w (1 - a)) / S_h
     float* y_acc;         // [N, H] fp32, zeroed here (or null)
     void* y_direct;       // k = 1, no shared experts: the output [N, H]; rows of tokens
                           // whose one selection is unavailable are zeroed here (or null)
-    // Decode batches: L2 prefetch, while routing runs, of weights the GEMMs stream
-    // next (HBM is otherwise idle then).  pf_shared_bytes = 0 / pf_max_experts = 0: off.
-    const void* pf_shared[3];   // shared gate, up, down pools
-    uint64_t pf_shared_bytes;   // bytes of each of the three
-    const void* pf_gate;        // routed gate / up pools [P, F, H]
-    const void* pf_up;
-    uint64_t pf_expert_bytes;   // F * H * element size
-    int pf_max_experts;         // routed experts prefetched (first claimed), per call
 };
 
 // The logit kernels run first in a call: their first block zeroes the
 // per-call counters (group sizes and the optional per-expert statistics) that
 // the select kernel, launched after them, accumulates into.
 __device__ __forceinline__ void zero_route_counters(const RouteParams& p) {
-    if (threadIdx.x == 0) {
-        p.grp_count[p.e] = 0;      // ticket of the decode select + plan kernel
-        p.grp_count[p.e + 1] = 0;  // routed experts claimed for L2 prefetch
-    }
+    if (threadIdx.x == 0) p.grp_count[p.e] = 0;  // ticket of the decode select + plan kernel
     for (int i = threadIdx.x; i < p.e; i += blockDim.x) {
         p.grp_count[i] = 0;
         if (p.counts_all) p.counts_all[i] = 0;
@@ -124,13 +112,6 @@ __global__ void __launch_bounds__(kPartialThreads) route_partials_kernel(RoutePa
     __shared__ __align__(16) uint8_t ws[kPartialThreads * ROW];
     pdl_trigger();
     if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) zero_route_counters(p);
-    if (p.pf_shared_bytes > 0) {
-        // the shared experts' weights, streamed first by both GEMMs
-        const uint64_t bid = blockIdx.x + static_cast<uint64_t>(gridDim.x) * (blockIdx.y + gridDim.y * blockIdx.z);
-        const uint64_t nt = static_cast<uint64_t>(gridDim.x) * gridDim.y * gridDim.z * blockDim.x;
-        for (int m = 0; m < 3; ++m)
-            prefetch_l2_range(p.pf_shared[m], p.pf_shared_bytes, bid * blockDim.x + threadIdx.x, nt);
-    }
     const int E = p.e, C = p.nchunks, H = p.h;
     const int c = blockIdx.y;
     const int e0 = blockIdx.z * kPartialThreads;
