@@ -10,7 +10,7 @@ same arguments and results as ``project_chronos_b200.ops``:
 
 * ``moe_route``   — the routing contract of include/chronos_moe.h
   (``router_oracle.c``; reference ``chronos/model/moe_chronos.py:112-128``);
-* ``ep_dispatch`` — include/chronos_ep.h: rows grouped by destination rank,
+* ``ep_dispatch`` — include/chronos_ep.h: rows grouped by (token chunk, destination rank),
   metadata (local expert, w*a), ``pair_slot``, shared share w*(1-a); inside a
   rank this restatement orders rows by (token, choice), the kernel's order is
   unspecified and nothing downstream depends on it;
@@ -46,7 +46,7 @@ class CpuEpBackend:
                     probs=torch.from_numpy(probs) if want_probs else None, counts=None, mass=None)
 
     @staticmethod
-    def ep_dispatch(x, topk_idx, topk_weight, num_experts, world_size, avail=None):
+    def ep_dispatch(x, topk_idx, topk_weight, num_experts, world_size, avail=None, num_chunks=1):
         xn = x.detach()
         idx = topk_idx.to(torch.int64).numpy()
         wt = topk_weight.to(torch.float32).numpy()
@@ -56,9 +56,13 @@ class CpuEpBackend:
             np.clip(_np(avail), 0.0, 1.0).astype(np.float32)
         a = a_all[idx]
         shared_w = (wt * (np.float32(1.0) - a)).astype(np.float32)
+        num_chunks = max(1, int(num_chunks))
+        ct = max(1, -(-n // num_chunks))
+        chunk = (np.arange(n) // ct)[:, None] * np.ones((1, k), np.int64)
         dest = idx // epr
+        key = chunk * world_size + dest
         sent = a > 0
-        counts = np.array([int(np.sum(sent & (dest == g))) for g in range(world_size)], np.int32)
+        counts = np.array([int(np.sum(sent & (key == q))) for q in range(num_chunks * world_size)], np.int32)
         offs = np.concatenate([[0], np.cumsum(counts)[:-1]]).astype(np.int64)
         send_x = torch.zeros(n * k, xn.shape[1], dtype=xn.dtype)
         meta = np.zeros((n * k, 2), np.int32)
@@ -69,13 +73,14 @@ class CpuEpBackend:
             if not sent[t, j]:
                 continue
             g = dest[t, j]
-            s = int(fill[g])
-            fill[g] += 1
+            q = key[t, j]
+            s = int(fill[q])
+            fill[q] += 1
             pair_slot[i] = s
             send_x[s] = xn[t]
             meta[s, 0] = idx[t, j] - g * epr
             meta[s, 1] = np.float32(wt[t, j] * a[t, j]).view(np.int32)
-        return dict(send_counts=torch.from_numpy(counts), send_x=send_x,
+        return dict(send_counts=torch.from_numpy(counts).view(num_chunks, world_size), send_x=send_x,
                     send_meta=torch.from_numpy(meta), pair_slot=torch.from_numpy(pair_slot),
                     shared_weight=torch.from_numpy(shared_w))
 

@@ -949,6 +949,8 @@ int ep_dispatch_impl(const ChronosEpDispatchArgs* a, cudaStream_t st) {
     p.k = a->top_k;
     p.g = a->world_size;
     p.epr = a->num_experts / a->world_size;
+    const int chunks = a->num_chunks < 1 ? 1 : a->num_chunks;
+    p.chunk_tokens = p.n > 0 ? (p.n + chunks - 1) / chunks : 1;
     p.topk_idx = a->topk_idx;
     p.topk_w = a->topk_weight;
     p.avail = a->avail;
@@ -958,7 +960,7 @@ int ep_dispatch_impl(const ChronosEpDispatchArgs* a, cudaStream_t st) {
     p.send_meta = a->send_meta;
     p.pair_slot = a->pair_slot;
     p.shared_w = a->shared_weight;
-    CHRONOS_CUDA_CHECK(cudaMemsetAsync(a->send_counts, 0, sizeof(int32_t) * a->world_size, st));
+    CHRONOS_CUDA_CHECK(cudaMemsetAsync(a->send_counts, 0, sizeof(int32_t) * a->world_size * chunks, st));
     const int64_t pairs = p.n * p.k;
     if (pairs == 0) return CHRONOS_OK;
     const unsigned cb = static_cast<unsigned>((pairs + kEpPackThreads - 1) / kEpPackThreads);
@@ -995,6 +997,9 @@ extern "C" int chronos_ep_dispatch(const ChronosEpDispatchArgs* a, void* stream)
     if (a->world_size < 1 || a->world_size > CHRONOS_EP_MAX_RANKS)
         return fail(CHRONOS_ERR_INVALID_ARG, "world_size %d out of range [1, %d]", a->world_size,
                     CHRONOS_EP_MAX_RANKS);
+    if (static_cast<int64_t>(a->num_chunks < 1 ? 1 : a->num_chunks) * a->world_size > CHRONOS_EP_MAX_RANKS)
+        return fail(CHRONOS_ERR_INVALID_ARG, "num_chunks %d x world_size %d exceeds %d", a->num_chunks,
+                    a->world_size, CHRONOS_EP_MAX_RANKS);
     if (a->num_experts < 1 || a->num_experts % a->world_size != 0 || a->num_experts < a->top_k)
         return fail(CHRONOS_ERR_INVALID_ARG, "num_experts %d must be >= top_k and a multiple of world_size %d",
                     a->num_experts, a->world_size);

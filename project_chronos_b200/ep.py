@@ -13,11 +13,12 @@ call instead):
    are not sent, their weight moves to the shared term;
 3. all-to-all of the counts (the one host synchronisation: NCCL's variable
    all-to-all needs the split sizes), then of the rows and metadata (NCCL over
-   NVLink); the shared term (1 + sum w(1-a)) * mean_j Shared_j(x) is computed
-   while the rows travel;
-4. the received rows through the grouped expert kernels (pre-routed, k = 1):
-   w*a*SwiGLU_e(x) per row;
-5. all-to-all of the result rows back to their source ranks;
+   NVLink), in C token chunks, all issued at once; the shared term
+   (1 + sum w(1-a)) * mean_j Shared_j(x) is computed while the rows travel;
+4. as each chunk lands, its rows through the grouped expert kernels
+   (pre-routed, k = 1): w*a*SwiGLU_e(x) per row;
+5. all-to-all of each chunk's result rows back to their source ranks, in
+   flight while the next chunk's experts run;
 6. ``chronos_ep_combine``: y_t = shared term + sum_j returned row (t, j).
 
 Same arithmetic as the single-device layer (the blend of
@@ -35,6 +36,8 @@ import torch.distributed as dist
 import torch.nn as nn
 
 from . import ops
+
+_MAX_KEYS = 32  # chunks x ranks of one dispatch (CHRONOS_EP_MAX_RANKS)
 
 
 class ExpertParallelMoE(nn.Module):
@@ -65,6 +68,8 @@ class ExpertParallelMoE(nn.Module):
         self.sh_gate = self.sh_up = self.sh_down = None
         self.last_send_counts = None
         self.last_recv_counts = None
+        # token chunks of the exchange pipeline (chunk * ranks <= 32)
+        self.chunks = 4
 
     @classmethod
     def from_stacked(cls, config, router: torch.Tensor, gate: torch.Tensor, up: torch.Tensor,
@@ -128,28 +133,36 @@ class ExpertParallelMoE(nn.Module):
             self.last_send_counts = self.last_recv_counts = None
             return y.view(shp)
 
-        # 1-2: route, build the send buffers
+        # 1-2: route, build the send buffers (rows ordered by token chunk, then rank)
         r = be.moe_route(xf, self.router, k, self.norm_topk_prob, num_shared=self.num_shared,
                          ffn=F, router_bias=self.router_logit_bias, want_probs=False)
-        d = be.ep_dispatch(xf, r["topk_idx"], r["topk_weight"], E, G, avail=avail)
+        C = max(1, min(self.chunks, _MAX_KEYS // G))
+        d = be.ep_dispatch(xf, r["topk_idx"], r["topk_weight"], E, G, avail=avail, num_chunks=C)
 
-        # 3: counts, then rows + metadata (async) while the shared term runs
-        send_counts = d["send_counts"]
-        recv_counts = send_counts if G == 1 else torch.empty_like(send_counts)
-        if G > 1:
-            self._exchange(recv_counts, send_counts, None, None)
-        both = torch.cat([send_counts, recv_counts]).cpu().tolist()
-        sc, rc = both[:G], both[G:]
-        self.last_send_counts, self.last_recv_counts = sc, rc
-        n_send, n_recv = sum(sc), sum(rc)
-        if G == 1:  # nothing to exchange: the send buffers are the receive buffers
-            recv_x, recv_meta = d["send_x"][:n_send], d["send_meta"][:n_send]
-            w1 = w2 = None
-        else:
-            recv_x = torch.empty(n_recv, H, dtype=dt, device=dev)
-            recv_meta = torch.empty(n_recv, 2, dtype=torch.int32, device=dev)
-            w1 = self._exchange(recv_x, d["send_x"][:n_send], rc, sc, async_op=True)
-            w2 = self._exchange(recv_meta, d["send_meta"][:n_send], rc, sc, async_op=True)
+        # 3: counts [C, G] -> per destination [G, C]; one host sync for every split size
+        send_gc = d["send_counts"].reshape(C, G).t().contiguous()
+        recv_gc = torch.empty_like(send_gc)
+        self._exchange(recv_gc, send_gc, None, None)
+        both = torch.cat([send_gc.reshape(-1), recv_gc.reshape(-1)]).cpu().tolist()
+        sc = [[both[g * C + c] for g in range(G)] for c in range(C)]          # sent, [c][g]
+        rc = [[both[G * C + g * C + c] for g in range(G)] for c in range(C)]  # received, [c][g]
+        self.last_send_counts = [sum(sc[c][g] for c in range(C)) for g in range(G)]
+        self.last_recv_counts = [sum(rc[c][g] for c in range(C)) for g in range(G)]
+        send_off = [0]
+        for c in range(C):
+            send_off.append(send_off[-1] + sum(sc[c]))
+        n_send = send_off[-1]
+
+        # rows and metadata of every chunk, in flight while the shared term runs
+        recv_x, recv_meta, works = [], [], []
+        for c in range(C):
+            lo, hi = send_off[c], send_off[c + 1]
+            rx = torch.empty(sum(rc[c]), H, dtype=dt, device=dev)
+            rm = torch.empty(sum(rc[c]), 2, dtype=torch.int32, device=dev)
+            works.append((self._exchange(rx, d["send_x"][lo:hi], rc[c], sc[c], async_op=True),
+                          self._exchange(rm, d["send_meta"][lo:hi], rc[c], sc[c], async_op=True)))
+            recv_x.append(rx)
+            recv_meta.append(rm)
 
         y_shared = None
         if self.num_shared:
@@ -159,22 +172,25 @@ class ExpertParallelMoE(nn.Module):
                 self.sh_down, k, self.norm_topk_prob, avail=torch.zeros(E, dtype=torch.float32, device=dev),
                 slot_of_expert=no_slot, want_probs=False,
                 topk=[r["topk_idx"], d["shared_weight"]])["y"]
-        for w in (w1, w2):
-            if w is not None:
-                w.wait()
 
-        # 4: this rank's experts on the rows it received
-        eid = recv_meta[:, 0:1].contiguous()
-        wgt = recv_meta[:, 1:2].contiguous().view(torch.float32)
+        # 4-5: per chunk, as it lands: this rank's experts on its rows, rows sent back
+        # (the return of chunk c overlaps the experts of chunk c + 1)
         local_router = torch.empty(self.experts_per_rank, H, dtype=dt, device=dev)
-        y_loc = be.moe_forward(recv_x, local_router, self.w_gate, self.w_up, self.w_down, None, None,
-                               None, 1, False, want_probs=False, topk=[eid, wgt])["y"]
+        back = torch.empty(n_send, H, dtype=dt, device=dev)
+        back_works = []
+        for c in range(C):
+            for w in works[c]:
+                w.wait()
+            rm = recv_meta[c]
+            eid = rm[:, 0:1].contiguous()
+            wgt = rm[:, 1:2].contiguous().view(torch.float32)
+            y_loc = be.moe_forward(recv_x[c], local_router, self.w_gate, self.w_up, self.w_down, None,
+                                   None, None, 1, False, want_probs=False, topk=[eid, wgt])["y"]
+            back_works.append(self._exchange(back[send_off[c]:send_off[c + 1]], y_loc, sc[c], rc[c],
+                                             async_op=True))
+        for w in back_works:
+            w.wait()
 
-        # 5-6: rows back to their source ranks, combine
-        if G == 1:
-            back = y_loc
-        else:
-            back = torch.empty(n_send, H, dtype=dt, device=dev)
-            self._exchange(back, y_loc, sc, rc)
+        # 6: fold the returned rows and the shared term
         y = be.ep_combine(back, d["pair_slot"], k, y_shared=y_shared, num_tokens=xf.shape[0])
         return y.view(shp)

@@ -187,10 +187,12 @@ def moe_route(x: torch.Tensor, router_w: torch.Tensor, top_k: int, norm_topk: bo
 
 
 def ep_dispatch(x: torch.Tensor, topk_idx: torch.Tensor, topk_weight: torch.Tensor, num_experts: int,
-                world_size: int, avail: Optional[torch.Tensor] = None) -> dict:
+                world_size: int, avail: Optional[torch.Tensor] = None, num_chunks: int = 1) -> dict:
     """Send buffers of one rank for expert parallelism (include/chronos_ep.h).
 
-    Returns dict(send_counts [G] int32, send_x [N*k, H], send_meta [N*k, 2] int32
+    Rows are ordered by (token chunk, destination rank), ``num_chunks`` contiguous
+    chunks of ceil(N / num_chunks) tokens.
+    Returns dict(send_counts [C, G] int32, send_x [N*k, H], send_meta [N*k, 2] int32
     (local expert id, fp32 bits of w*a), pair_slot [N*k] int32, shared_weight [N, k]
     fp32); the first ``send_counts.sum()`` rows of the send buffers are used."""
     _check_cuda(x, topk_idx, topk_weight, avail)
@@ -203,7 +205,8 @@ def ep_dispatch(x: torch.Tensor, topk_idx: torch.Tensor, topk_weight: torch.Tens
     topk_idx = topk_idx.to(torch.int32).contiguous()
     topk_weight = topk_weight.to(torch.float32).contiguous()
     av = None if avail is None else avail.to(device=dev, dtype=torch.float32).contiguous()
-    out = dict(send_counts=torch.empty(world_size, dtype=torch.int32, device=dev),
+    num_chunks = max(1, int(num_chunks))
+    out = dict(send_counts=torch.empty(num_chunks, world_size, dtype=torch.int32, device=dev),
                send_x=torch.empty(n * k, h, dtype=x.dtype, device=dev),
                send_meta=torch.empty(n * k, 2, dtype=torch.int32, device=dev),
                pair_slot=torch.empty(n * k, dtype=torch.int32, device=dev),
@@ -211,7 +214,7 @@ def ep_dispatch(x: torch.Tensor, topk_idx: torch.Tensor, topk_weight: torch.Tens
     scratch = torch.empty(max(n * k, 1), dtype=torch.int32, device=dev)
     args = N.ChronosEpDispatchArgs(
         num_tokens=n, hidden=h, num_experts=int(num_experts), top_k=k, world_size=int(world_size),
-        dtype=_DTYPES[x.dtype], x=_ptr(x), topk_idx=_ptr(topk_idx), topk_weight=_ptr(topk_weight),
+        dtype=_DTYPES[x.dtype], num_chunks=num_chunks, x=_ptr(x), topk_idx=_ptr(topk_idx), topk_weight=_ptr(topk_weight),
         avail=_ptr(av), send_counts=_ptr(out["send_counts"]), send_x=_ptr(out["send_x"]),
         send_meta=_ptr(out["send_meta"]),
         pair_slot=_ptr(out["pair_slot"]), shared_weight=_ptr(out["shared_weight"]),

@@ -27,8 +27,9 @@ def _route(x, router, k):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("world,n", [(1, 7), (2, 33), (4, 300), (8, 1)])
-def test_dispatch_and_combine_match_oracle(dtype, world, n):
+@pytest.mark.parametrize("world,n,chunks", [(1, 7, 1), (2, 33, 1), (4, 300, 1), (8, 1, 1), (2, 33, 3),
+                                            (8, 300, 4), (4, 5, 8)])
+def test_dispatch_and_combine_match_oracle(dtype, world, n, chunks):
     from oracle.ep_oracle import CpuEpBackend
     from project_chronos_b200 import ops
     E, k, H = 16, 4, 256
@@ -38,8 +39,9 @@ def test_dispatch_and_combine_match_oracle(dtype, world, n):
     avail = (torch.rand(E, generator=g) > 0.25).float()
     avail[3] = 0.5
     r = _route(x, router, k)
-    d = ops.ep_dispatch(x, r["topk_idx"], r["topk_weight"], E, world, avail=avail.to(DEV))
-    ref = CpuEpBackend.ep_dispatch(x.cpu(), r["topk_idx"].cpu(), r["topk_weight"].cpu(), E, world, avail)
+    d = ops.ep_dispatch(x, r["topk_idx"], r["topk_weight"], E, world, avail=avail.to(DEV), num_chunks=chunks)
+    ref = CpuEpBackend.ep_dispatch(x.cpu(), r["topk_idx"].cpu(), r["topk_weight"].cpu(), E, world, avail,
+                                   num_chunks=chunks)
     assert d["send_counts"].cpu().tolist() == ref["send_counts"].tolist()
     assert torch.equal(d["shared_weight"].cpu(), ref["shared_weight"])
     ps = d["pair_slot"].cpu()
@@ -52,11 +54,13 @@ def test_dispatch_and_combine_match_oracle(dtype, world, n):
     assert torch.equal(got_rows, want_rows)
     assert torch.equal(d["send_meta"].cpu()[ps[sent].long()], ref["send_meta"][ref["pair_slot"][sent].long()])
     assert sorted(ps[sent].tolist()) == list(range(n_send))
-    # rows of each destination rank are contiguous, in rank order
-    offs = np.concatenate([[0], np.cumsum(ref["send_counts"].numpy())])
-    dest = (r["topk_idx"].cpu().view(-1)[sent] // (E // world)).numpy()
+    # rows of each (token chunk, destination rank) are contiguous, chunk-major
+    offs = np.concatenate([[0], np.cumsum(ref["send_counts"].numpy().ravel())])
+    ct = -(-n // chunks)
+    tok = np.repeat(np.arange(n), k)[sent.numpy()]
+    key = (tok // ct) * world + (r["topk_idx"].cpu().view(-1)[sent] // (E // world)).numpy()
     slots = ps[sent].numpy()
-    assert np.all((slots >= offs[dest]) & (slots < offs[dest + 1]))
+    assert np.all((slots >= offs[key]) & (slots < offs[key + 1]))
 
     # combine: returned rows (any values), shared term
     rows = torch.randn(max(n_send, 1), H, generator=g).to(DEV, dtype)[:n_send]
