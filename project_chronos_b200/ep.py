@@ -108,6 +108,9 @@ class ExpertParallelMoE(nn.Module):
 
     # ------------------------------------------------------------------
     def _exchange(self, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits, async_op=False):
+        if self.world == 1:  # a single rank sends everything to itself
+            out.copy_(inp)
+            return None
         return dist.all_to_all_single(out, inp, output_split_sizes=out_splits,
                                       input_split_sizes=in_splits, group=self.group,
                                       async_op=async_op)
@@ -180,7 +183,8 @@ class ExpertParallelMoE(nn.Module):
         back_works = []
         for c in range(C):
             for w in works[c]:
-                w.wait()
+                if w is not None:
+                    w.wait()
             rm = recv_meta[c]
             eid = rm[:, 0:1].contiguous()
             wgt = rm[:, 1:2].contiguous().view(torch.float32)
@@ -189,7 +193,8 @@ class ExpertParallelMoE(nn.Module):
             back_works.append(self._exchange(back[send_off[c]:send_off[c + 1]], y_loc, sc[c], rc[c],
                                              async_op=True))
         for w in back_works:
-            w.wait()
+            if w is not None:
+                w.wait()
 
         # 6: fold the returned rows and the shared term
         y = be.ep_combine(back, d["pair_slot"], k, y_shared=y_shared, num_tokens=xf.shape[0])

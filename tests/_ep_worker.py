@@ -51,6 +51,7 @@ def cpu_rank(rank, world, port, q, scenario):
         m = ExpertParallelMoE.from_stacked(_cfg(E, k, H, F, S), w["router"], w["gate"], w["up"],
                                            w["down"], w["sh_gate"], w["sh_up"], w["sh_down"],
                                            backend=CpuEpBackend())
+        m.chunks = 3 if scenario == "mask" else 1
         y = m(x, available_expert_mask=mask)
         ref, _, _, _ = O.moe_forward(x.numpy(), w["router"].numpy(), w["gate"].numpy(),
                                      w["up"].numpy(), w["down"].numpy(), w["sh_gate"].numpy(),

@@ -58,3 +58,27 @@ def test_injected_rank_failure_ends_the_collective_with_an_error():
     by_rank = {r[1]: r for r in res}
     assert by_rank[1][0] == "error" and "injected" in by_rank[1][2]
     assert by_rank[0][0] == "error"
+
+
+@pytest.mark.parametrize("chunks", [1, 3])
+def test_single_rank_dispatch_path_without_a_process_group(chunks):
+    """One rank, no process group, the dispatch path forced: the exchanges
+    degenerate to copies and the result equals the single-device oracle."""
+    import torch
+    from oracle import moe_oracle as O
+    from oracle.ep_oracle import CpuEpBackend
+    from project_chronos_b200.ep import ExpertParallelMoE
+    E, k, H, F, S = 8, 2, 32, 16, 1
+    w = _ep_worker._weights(E, H, F, S)
+    x = torch.randn(11, H, generator=torch.Generator().manual_seed(3))
+    m = ExpertParallelMoE.from_stacked(_ep_worker._cfg(E, k, H, F, S), w["router"], w["gate"], w["up"],
+                                       w["down"], w["sh_gate"], w["sh_up"], w["sh_down"],
+                                       backend=CpuEpBackend(), dispatch_single_rank=True)
+    m.chunks = chunks
+    mask = torch.tensor([1, 1, 0, 1, 1, 1, 0, 1], dtype=torch.float32)
+    y = m(x, available_expert_mask=mask)
+    ref, _, _, _ = O.moe_forward(x.numpy(), w["router"].numpy(), w["gate"].numpy(), w["up"].numpy(),
+                                 w["down"].numpy(), w["sh_gate"].numpy(), w["sh_up"].numpy(),
+                                 w["sh_down"].numpy(), k, True, avail=mask.numpy())
+    assert O.rel_l2(y.numpy(), ref) < 1e-5
+    assert m.last_send_counts == m.last_recv_counts
