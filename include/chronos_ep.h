@@ -39,14 +39,14 @@ typedef struct ChronosEpDispatchArgs {
     int32_t top_k;             /* k */
     int32_t world_size;        /* G, 1..CHRONOS_EP_MAX_RANKS */
     int32_t dtype;             /* CHRONOS_DTYPE_* of x and send_x */
-    int32_t num_chunks;        /* C >= 1: tokens split into C contiguous chunks of ceil(N/C)
-                                  tokens, send rows ordered by (chunk, destination rank);
-                                  C * G <= CHRONOS_EP_MAX_RANKS */
+    int32_t num_chunks;        /* C >= 1 dividing E/G: each rank's local experts split into C
+                                  chunks of E/(G*C); send rows ordered by (expert chunk,
+                                  destination rank); C * G <= CHRONOS_EP_MAX_RANKS */
     const void* x;             /* [N, H] */
     const int32_t* topk_idx;   /* [N, k] global expert ids (chronos_moe_route) */
     const float* topk_weight;  /* [N, k] */
     const float* avail;        /* [E] availability a_e in [0, 1], or NULL for all 1 */
-    int32_t* send_counts;      /* [C, G] out: selections of each chunk sent to each rank */
+    int32_t* send_counts;      /* [C, G] out: selections of each expert chunk sent to each rank */
     void* send_x;              /* [N*k, H] out: x rows grouped by destination rank */
     int32_t* send_meta;        /* [N*k, 2] out: (expert id local to the destination rank,
                                   fp32 bits of w * a) per send row */
@@ -55,10 +55,12 @@ typedef struct ChronosEpDispatchArgs {
     int32_t* scratch;          /* [N*k] int32 scratch */
 } ChronosEpDispatchArgs;
 
-/* Builds the send buffers of one rank: rows are grouped by (chunk, destination
- * rank), chunk-major (first send_counts[0][0] rows: chunk 0 to rank 0, ...), so
- * each chunk's rows form one contiguous all-to-all send buffer; within a group
- * their order is unspecified.  Selections with a_e = 0 are not sent. */
+/* Builds the send buffers of one rank: rows are grouped by (expert chunk,
+ * destination rank), chunk-major (first send_counts[0][0] rows: chunk 0 to
+ * rank 0, ...), so each chunk's rows form one contiguous all-to-all send
+ * buffer and a receiver can run each chunk's experts as soon as it lands
+ * (reading each expert's weights once); within a group the row order is
+ * unspecified.  Selections with a_e = 0 are not sent. */
 CHRONOS_API int chronos_ep_dispatch(const ChronosEpDispatchArgs* args, void* cuda_stream);
 
 typedef struct ChronosEpCombineArgs {

@@ -47,7 +47,7 @@
 extern "C" {
 #endif
 
-#define CHRONOS_MOE_ABI_VERSION 1
+#define CHRONOS_MOE_ABI_VERSION 2
 
 /* Return codes. */
 #define CHRONOS_OK 0
@@ -126,6 +126,9 @@ typedef struct ChronosMoeArgs {
     size_t workspace_bytes;
     int32_t* status;       /* [1] device word; kernels write a CHRONOS_ERR_* code on a
                               device-side failure.  The caller zeroes it.  May be NULL. */
+    int32_t max_ctas;      /* > 0: the persistent expert GEMMs use at most this many CTAs
+                              (one per SM), leaving SMs free for concurrent work such as an
+                              all-to-all on another stream; 0 = every SM */
 } ChronosMoeArgs;
 
 /* Bytes of workspace one chronos_moe_forward / chronos_moe_route call with

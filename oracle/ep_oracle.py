@@ -10,7 +10,7 @@ same arguments and results as ``project_chronos_b200.ops``:
 
 * ``moe_route``   — the routing contract of include/chronos_moe.h
   (``router_oracle.c``; reference ``chronos/model/moe_chronos.py:112-128``);
-* ``ep_dispatch`` — include/chronos_ep.h: rows grouped by (token chunk, destination rank),
+* ``ep_dispatch`` — include/chronos_ep.h: rows grouped by (expert chunk, destination rank),
   metadata (local expert, w*a), ``pair_slot``, shared share w*(1-a); inside a
   rank this restatement orders rows by (token, choice), the kernel's order is
   unspecified and nothing downstream depends on it;
@@ -57,10 +57,8 @@ class CpuEpBackend:
         a = a_all[idx]
         shared_w = (wt * (np.float32(1.0) - a)).astype(np.float32)
         num_chunks = max(1, int(num_chunks))
-        ct = max(1, -(-n // num_chunks))
-        chunk = (np.arange(n) // ct)[:, None] * np.ones((1, k), np.int64)
         dest = idx // epr
-        key = chunk * world_size + dest
+        key = ((idx % epr) // (epr // num_chunks)) * world_size + dest
         sent = a > 0
         counts = np.array([int(np.sum(sent & (key == q))) for q in range(num_chunks * world_size)], np.int32)
         offs = np.concatenate([[0], np.cumsum(counts)[:-1]]).astype(np.int64)

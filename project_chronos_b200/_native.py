@@ -36,7 +36,7 @@ DTYPE_FP32 = 2
 
 FLAG_PREROUTED = 0x1
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 # Functions declared in include/chronos_moe.h (checked against the header by the tests).
 EXPORTS = ("chronos_moe_workspace_size", "chronos_moe_forward", "chronos_moe_route",
@@ -94,6 +94,7 @@ class ChronosMoeArgs(ctypes.Structure):
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
         ("status", ctypes.c_void_p),
+        ("max_ctas", ctypes.c_int32),
     ]
 
 

@@ -454,7 +454,7 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     p.status = a->status;
     p.slot_map = w.at<int32_t>(w.L->slot_map);
     p.n_tokens = s.num_tokens;
-    const int grid = sm_count();
+    const int grid = (a->max_ctas > 0 && a->max_ctas < sm_count()) ? a->max_ctas : sm_count();
 
     // gate/up
     TcGemmParams pg = p;
@@ -950,7 +950,8 @@ int ep_dispatch_impl(const ChronosEpDispatchArgs* a, cudaStream_t st) {
     p.g = a->world_size;
     p.epr = a->num_experts / a->world_size;
     const int chunks = a->num_chunks < 1 ? 1 : a->num_chunks;
-    p.chunk_tokens = p.n > 0 ? (p.n + chunks - 1) / chunks : 1;
+    p.chunks = chunks;
+    p.chunk_experts = p.epr / chunks;
     p.topk_idx = a->topk_idx;
     p.topk_w = a->topk_weight;
     p.avail = a->avail;
@@ -1003,6 +1004,9 @@ extern "C" int chronos_ep_dispatch(const ChronosEpDispatchArgs* a, void* stream)
     if (a->num_experts < 1 || a->num_experts % a->world_size != 0 || a->num_experts < a->top_k)
         return fail(CHRONOS_ERR_INVALID_ARG, "num_experts %d must be >= top_k and a multiple of world_size %d",
                     a->num_experts, a->world_size);
+    if ((a->num_experts / a->world_size) % (a->num_chunks < 1 ? 1 : a->num_chunks) != 0)
+        return fail(CHRONOS_ERR_INVALID_ARG, "num_chunks %d does not divide the %d experts of a rank",
+                    a->num_chunks, a->num_experts / a->world_size);
     if (a->send_counts == nullptr) return fail(CHRONOS_ERR_INVALID_ARG, "send_counts is required");
     if (a->num_tokens > 0 &&
         (a->x == nullptr || a->topk_idx == nullptr || a->topk_weight == nullptr || a->send_x == nullptr ||

@@ -5,8 +5,8 @@
 // all-to-all send buffers:
 //   ep_count_kernel  one thread per (token, choice): a = avail[e], the shared
 //                    experts' share w*(1-a), and for a > 0 the selection's
-//                    position among those of its token chunk bound for rank
-//                    e/epr (global atomics on C*G counters, zeroed by the caller);
+//                    position among those bound for (expert chunk, rank e/epr)
+//                    (global atomics on C*G counters, zeroed by the caller);
 //   ep_pack_kernel   one warp per (token, choice): send row = prefix of the
 //                    counts + position; metadata (local expert, w*a) and the x
 //                    row copied with 16-byte vectors, every load of a lane
@@ -29,7 +29,8 @@ struct EpParams {
     const void* x;
     int64_t n;
     int h, e, k, g, epr;
-    int64_t chunk_tokens;   // tokens per chunk (N when unchunked)
+    int chunks;             // expert chunks per rank (1: unchunked)
+    int chunk_experts;      // local experts per chunk (epr / chunks)
     const int32_t* topk_idx;
     const float* topk_w;
     const float* avail;
@@ -56,7 +57,7 @@ __global__ void __launch_bounds__(kEpPackThreads) ep_count_kernel(EpParams p) {
     const float w = p.topk_w[i];
     const float a = ep_avail(p, e);
     p.shared_w[i] = w * (1.0f - a);
-    const int key = static_cast<int>((i / p.k) / p.chunk_tokens) * p.g + e / p.epr;
+    const int key = a > 0.0f ? ((e % p.epr) / p.chunk_experts) * p.g + e / p.epr : 0;
     p.pos[i] = a > 0.0f ? atomicAdd(&p.counts[key], 1) : -1;
 }
 
@@ -67,8 +68,7 @@ __global__ void __launch_bounds__(kEpPackThreads) ep_pack_kernel(EpParams p) {
     pdl_wait();  // counts and positions
     const int tid = threadIdx.x, lane = tid & 31;
     if (tid < 32) {
-        const int keys = static_cast<int>((p.n + p.chunk_tokens - 1) / p.chunk_tokens) * p.g;
-        const int c = lane < keys ? p.counts[lane] : 0;
+        const int c = lane < p.chunks * p.g ? p.counts[lane] : 0;
         int v = c;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(kEpPackThreads) ep_pack_kernel(EpParams p) {
     }
     const int e = p.topk_idx[gw];
     const int dest = e / p.epr;
-    const int key = static_cast<int>((gw / p.k) / p.chunk_tokens) * p.g + dest;
+    const int key = ((e % p.epr) / p.chunk_experts) * p.g + dest;
     const int64_t slot = static_cast<int64_t>(s_off[key]) + ps;
     if (lane == 0) {
         p.pair_slot[gw] = static_cast<int32_t>(slot);

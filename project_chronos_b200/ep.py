@@ -13,10 +13,11 @@ call instead):
    are not sent, their weight moves to the shared term;
 3. all-to-all of the counts (the one host synchronisation: NCCL's variable
    all-to-all needs the split sizes), then of the rows and metadata (NCCL over
-   NVLink), in C token chunks, all issued at once; the shared term
-   (1 + sum w(1-a)) * mean_j Shared_j(x) is computed while the rows travel;
+   NVLink), in C chunks of each rank's experts, all issued at once; the shared
+   term (1 + sum w(1-a)) * mean_j Shared_j(x) is computed while the rows travel;
 4. as each chunk lands, its rows through the grouped expert kernels
-   (pre-routed, k = 1): w*a*SwiGLU_e(x) per row;
+   (pre-routed, k = 1): w*a*SwiGLU_e(x) per row (with C > 1 on at most
+   ``gemm_ctas`` SMs, leaving the rest to the exchange);
 5. all-to-all of each chunk's result rows back to their source ranks, in
    flight while the next chunk's experts run;
 6. ``chronos_ep_combine``: y_t = shared term + sum_j returned row (t, j).
@@ -68,8 +69,10 @@ class ExpertParallelMoE(nn.Module):
         self.sh_gate = self.sh_up = self.sh_down = None
         self.last_send_counts = None
         self.last_recv_counts = None
-        # token chunks of the exchange pipeline (chunk * ranks <= 32)
-        self.chunks = 4
+        # expert chunks of the exchange pipeline (dividing E/G, chunks * ranks <= 32), and
+        # the CTAs the expert GEMMs may use while chunks are exchanged beside them
+        self.chunks = 1
+        self.gemm_ctas = 132
 
     @classmethod
     def from_stacked(cls, config, router: torch.Tensor, gate: torch.Tensor, up: torch.Tensor,
@@ -139,7 +142,10 @@ class ExpertParallelMoE(nn.Module):
         # 1-2: route, build the send buffers (rows ordered by token chunk, then rank)
         r = be.moe_route(xf, self.router, k, self.norm_topk_prob, num_shared=self.num_shared,
                          ffn=F, router_bias=self.router_logit_bias, want_probs=False)
-        C = max(1, min(self.chunks, _MAX_KEYS // G))
+        C = max(c for c in range(1, max(1, min(self.chunks, _MAX_KEYS // G)) + 1)
+                if self.experts_per_rank % c == 0)
+        # with chunks, the exchange runs beside the expert GEMMs: leave it SMs
+        max_ctas = 0 if C == 1 else self.gemm_ctas
         d = be.ep_dispatch(xf, r["topk_idx"], r["topk_weight"], E, G, avail=avail, num_chunks=C)
 
         # 3: counts [C, G] -> per destination [G, C]; one host sync for every split size
@@ -176,7 +182,7 @@ class ExpertParallelMoE(nn.Module):
                 slot_of_expert=no_slot, want_probs=False,
                 topk=[r["topk_idx"], d["shared_weight"]])["y"]
 
-        # 4-5: per chunk, as it lands: this rank's experts on its rows, rows sent back
+        # 4-5: per expert chunk, as it lands: its experts on its rows, rows sent back
         # (the return of chunk c overlaps the experts of chunk c + 1)
         local_router = torch.empty(self.experts_per_rank, H, dtype=dt, device=dev)
         back = torch.empty(n_send, H, dtype=dt, device=dev)
@@ -189,7 +195,8 @@ class ExpertParallelMoE(nn.Module):
             eid = rm[:, 0:1].contiguous()
             wgt = rm[:, 1:2].contiguous().view(torch.float32)
             y_loc = be.moe_forward(recv_x[c], local_router, self.w_gate, self.w_up, self.w_down, None,
-                                   None, None, 1, False, want_probs=False, topk=[eid, wgt])["y"]
+                                   None, None, 1, False, want_probs=False, topk=[eid, wgt],
+                                   max_ctas=max_ctas)["y"]
             back_works.append(self._exchange(back[send_off[c]:send_off[c + 1]], y_loc, sc[c], rc[c],
                                              async_op=True))
         for w in back_works:

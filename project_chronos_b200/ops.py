@@ -83,7 +83,8 @@ def moe_forward(x: torch.Tensor, router_w: torch.Tensor, w_gate: torch.Tensor, w
                 ready_flags: Optional[torch.Tensor] = None, ready_epoch: int = 0,
                 spin_limit_ns: int = 0, want_probs: bool = True, want_stats: bool = False,
                 topk: Optional[List[torch.Tensor]] = None, status: Optional[torch.Tensor] = None,
-                out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None):
+                out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
+                max_ctas: int = 0):
     """One MoE layer.  x [N, H]; router_w [E, H]; w_gate/w_up [P, F, H]; w_down [P, H, F];
     sh_* [S, F, H] / [S, H, F] (or None when S = 0); avail [E] fp32 in [0, 1].
 
@@ -141,7 +142,7 @@ def moe_forward(x: torch.Tensor, router_w: torch.Tensor, w_gate: torch.Tensor, w
         spin_limit_ns=int(spin_limit_ns), y=_ptr(y), router_probs=_ptr(probs),
         topk_idx=_ptr(topk_idx), topk_weight=_ptr(topk_w), expert_counts=_ptr(counts),
         expert_mass=_ptr(mass), workspace=_ptr(workspace), workspace_bytes=int(workspace.numel()),
-        status=_ptr(status))
+        status=_ptr(status), max_ctas=int(max_ctas))
     stream = torch.cuda.current_stream(dev).cuda_stream
     with torch.cuda.device(dev):
         N.check(lib.chronos_moe_forward(ctypes.byref(args), ctypes.c_void_p(stream)))
@@ -190,8 +191,8 @@ def ep_dispatch(x: torch.Tensor, topk_idx: torch.Tensor, topk_weight: torch.Tens
                 world_size: int, avail: Optional[torch.Tensor] = None, num_chunks: int = 1) -> dict:
     """Send buffers of one rank for expert parallelism (include/chronos_ep.h).
 
-    Rows are ordered by (token chunk, destination rank), ``num_chunks`` contiguous
-    chunks of ceil(N / num_chunks) tokens.
+    Rows are ordered by (expert chunk, destination rank): each rank's E/G local
+    experts split into ``num_chunks`` chunks (which must divide E/G).
     Returns dict(send_counts [C, G] int32, send_x [N*k, H], send_meta [N*k, 2] int32
     (local expert id, fp32 bits of w*a), pair_slot [N*k] int32, shared_weight [N, k]
     fp32); the first ``send_counts.sum()`` rows of the send buffers are used."""
