@@ -145,8 +145,7 @@ Layout make_layout(const ChronosMoeShape& s) {
     L.shared_coef = take(4 * N);
     L.topk_idx = take(4 * N * K);
     L.topk_w = take(4 * N * K);
-    L.partials = take(4 * N * E *
-                      (N <= static_cast<size_t>(kRouteSmallMax) ? route_chunks(s.hidden) : 1));
+    L.partials = take(4 * N * E * route_chunks(s.hidden));
     L.slot_tok = take(4 * (N * K + S * N));
     L.slot_coef = take(4 * (N * K + S * N));
     L.slot_map = N <= static_cast<size_t>(kSelectPlanMaxTokens) ? take(4 * E * N) : off;
@@ -337,7 +336,7 @@ int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool p
     rp.partials = w.at<float>(w.L->partials);
     const int64_t N = s.num_tokens;
     const bool small = N <= kRouteSmallMax;
-    rp.nchunks = small ? route_chunks(s.hidden) : 1;
+    rp.nchunks = route_chunks(s.hidden);
     // the logit kernel is the call's first launch (no PDL) and zeroes the counters;
     // with pre-routed inputs the caller zeroed them and the select kernel comes first
     if (!prerouted) {
@@ -349,7 +348,8 @@ int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool p
                                              false, rp));
         } else {
             const dim3 grid(static_cast<unsigned>((N + kRouteTile - 1) / kRouteTile),
-                            static_cast<unsigned>((s.num_experts + kRouteTile - 1) / kRouteTile));
+                            static_cast<unsigned>((s.num_experts + kRouteTile - 1) / kRouteTile),
+                            static_cast<unsigned>((rp.nchunks + kTiledChunks - 1) / kTiledChunks));
             CHRONOS_CUDA_CHECK(launch_kernel(route_tiled_kernel<T>, grid, dim3(kTiledThreads), 0, st,
                                              false, rp));
         }

@@ -6,14 +6,15 @@
 // partials, each partial one thread's fmaf chain over its chunk in increasing
 // h, so the ranking is identical on every run and equal to the CPU oracle's.
 //
-// Two logit kernels produce the same bits:
+// Two logit kernels produce the same bits, both writing the chunk partials
+// chunk-major, partials[c][t][e] ([C, N, E], coalesced along experts):
 //   route_partials_kernel  small batches: one thread per (expert, chunk, group
-//                          of 8 tokens) writes chunk partials [N, E, C]
-//                          (parallel over chunks, so a decode token's 64
-//                          logits are not 2048-long serial chains);
+//                          of 8 tokens) (parallel over chunks, so a decode
+//                          token's 64 logits are not 2048-long serial chains);
 //   route_tiled_kernel     large batches: 64-token x 64-expert register-tiled
-//                          SIMT GEMM over the whole K, chunk partials folded in
-//                          order in registers, writes logits [N, E].
+//                          SIMT GEMM, each block over 4 chunks (512 h) of K
+//                          (the K split gives the grid enough blocks to fill
+//                          every SM; the in-order fold stays in the select).
 // route_select_kernel (one warp per token) then sums the partials in chunk
 // order, applies the bias, softmax and top-k, and writes the per-token blend
 // coefficient of the shared experts (1 + sum_k w*(1-a)) / S_h
@@ -41,8 +42,8 @@ struct RouteParams {
     const int32_t* slot_of_expert;
     int64_t n;
     int h, e, k, num_shared, norm_topk, prerouted;
-    int nchunks;          // partials per logit in `partials` (1 = finished logits)
-    float* partials;      // [N, E, nchunks]
+    int nchunks;          // chunk partials per logit
+    float* partials;      // [nchunks, N, E]
     void* probs;          // [N, E] T or null
     int32_t* topk_idx;    // [N, k]
     float* topk_w;        // [N, k]
@@ -191,7 +192,7 @@ __global__ void __launch_bounds__(kPartialThreads) route_partials_kernel(RoutePa
     }
 #pragma unroll
     for (int i = 0; i < kRouteGroup; ++i)
-        if (i < nt) p.partials[((t0 + i) * E + e) * C + c] = acc[i];
+        if (i < nt) p.partials[(static_cast<int64_t>(c) * p.n + t0 + i) * E + e] = acc[i];
 }
 
 // ---------------------------------------------------------------------------
@@ -199,13 +200,14 @@ __global__ void __launch_bounds__(kPartialThreads) route_partials_kernel(RoutePa
 // ---------------------------------------------------------------------------
 constexpr int kTiledThreads = 256;
 constexpr int kTilePad = kRouteTileK + 4;
+constexpr int kTiledChunks = 4;  // chunks of K per block (blockIdx.z)
 
 template <typename T>
 __global__ void __launch_bounds__(kTiledThreads) route_tiled_kernel(RouteParams p) {
     __shared__ __align__(16) float xs[2][kRouteTile][kTilePad];
     __shared__ __align__(16) float ws[2][kRouteTile][kTilePad];
     pdl_trigger();
-    if (blockIdx.x == 0 && blockIdx.y == 0) zero_route_counters(p);
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) zero_route_counters(p);
     const int tid = threadIdx.x;
     const int tg = tid >> 4;  // tokens tg*4 .. tg*4+3
     const int eg = tid & 15;  // experts eg + 16 j
@@ -235,19 +237,21 @@ __global__ void __launch_bounds__(kTiledThreads) route_tiled_kernel(RouteParams 
         *reinterpret_cast<float4*>(&ws[buf][lr][lk]) = wa;
         *reinterpret_cast<float4*>(&ws[buf][lr][lk + 4]) = wb;
     };
-    float total[4][4], acc[4][4];
+    float acc[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) { total[i][j] = 0.0f; acc[i][j] = 0.0f; }
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
     const int KT = (H + kRouteTileK - 1) / kRouteTileK;
     constexpr int kTilesPerChunk = kRouteChunk / kRouteTileK;
-    gload(0);
+    const int kt_begin = blockIdx.z * kTiledChunks * kTilesPerChunk;
+    const int kt_end = min(KT, kt_begin + kTiledChunks * kTilesPerChunk);
+    gload(kt_begin);
     sstore(0);
     __syncthreads();
-    for (int kt = 0; kt < KT; ++kt) {
-        const int buf = kt & 1;
-        if (kt + 1 < KT) gload(kt + 1);
+    for (int kt = kt_begin; kt < kt_end; ++kt) {
+        const int buf = (kt - kt_begin) & 1;
+        if (kt + 1 < kt_end) gload(kt + 1);
 #pragma unroll
         for (int kk = 0; kk < kRouteTileK; kk += 4) {
             float4 a[4], b[4];
@@ -266,26 +270,21 @@ __global__ void __launch_bounds__(kTiledThreads) route_tiled_kernel(RouteParams 
                 }
         }
         if ((kt + 1) % kTilesPerChunk == 0 || kt + 1 == KT) {
+            // chunk finished: its partials, experts contiguous across the threads
+            float* out = p.partials + static_cast<int64_t>(kt / kTilesPerChunk) * p.n * E;
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < 4; ++i) {
+                const int64_t t = t0 + tg * 4 + i;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    total[i][j] = total[i][j] + acc[i][j];
+                    const int e = e0 + eg + 16 * j;
+                    if (t < p.n && e < E) out[t * E + e] = acc[i][j];
                     acc[i][j] = 0.0f;
                 }
+            }
         }
-        if (kt + 1 < KT) sstore(buf ^ 1);
+        if (kt + 1 < kt_end) sstore(buf ^ 1);
         __syncthreads();
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int64_t t = t0 + tg * 4 + i;
-        if (t >= p.n) continue;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int e = e0 + eg + 16 * j;
-            if (e < E) p.partials[t * E + e] = total[i][j];
-        }
     }
 }
 
@@ -337,21 +336,20 @@ __device__ __forceinline__ void select_token(const RouteParams& p, int64_t t, in
         const int e = lane + 32 * q;
         float lg = -INFINITY;
         if (e < E) {
-            const float* pp = p.partials + (t * E + e) * C;
+            // partials[c][t][e]: the warp's lanes read consecutive experts
+            const float* pp = p.partials + t * E + e;
+            const int64_t cs = p.n * E;
             float s = 0.0f;
             int c = 0;
             // loads in groups of 16 ahead of the in-order adds
             for (; c + 16 <= C; c += 16) {
-                float4 r[4];
+                float r[16];
 #pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    r[u] = (C % 4 == 0) ? reinterpret_cast<const float4*>(pp + c)[u]
-                                        : make_float4(pp[c + 4 * u], pp[c + 4 * u + 1], pp[c + 4 * u + 2],
-                                                      pp[c + 4 * u + 3]);
+                for (int u = 0; u < 16; ++u) r[u] = pp[(c + u) * cs];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) s = ((s + r[u].x) + r[u].y + r[u].z) + r[u].w;
+                for (int u = 0; u < 16; ++u) s = s + r[u];
             }
-            for (; c < C; ++c) s = s + pp[c];
+            for (; c < C; ++c) s = s + pp[c * cs];
             if (p.bias) s = s + p.bias[e];
             lg = s;
         }
