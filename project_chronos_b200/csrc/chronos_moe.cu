@@ -616,8 +616,11 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
                                            aligned16(a->w_shared_down)));
     int bn = 128;
     if (tc) bn = N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128;
-    // large batches: 256-token tiles for the down GEMM (half the operand traffic per FLOP)
-    const int bn_dn = (tc && N >= kDownWideMinTokens) ? 256 : bn;
+    // large batches whose experts get many rows each: 256-token tiles for the down GEMM
+    // (half the weight-operand traffic per FLOP); with ~128 rows per expert (e.g. 256
+    // experts, top-8, 4096 tokens) a 256-row tile would be half padding
+    const int64_t avg_rows = N * s.top_k / s.num_experts;
+    const int bn_dn = (tc && N >= kDownWideMinTokens && avg_rows >= 384) ? 256 : bn;
     const int tok_tile = tc ? bn : kSimtTile;
     const int tok_tile_dn = tc ? bn_dn : kSimtTile;
     const int mt_gu = tc ? (s.ffn + kTcBM - 1) / kTcBM : (s.ffn + kSimtTile - 1) / kSimtTile;
