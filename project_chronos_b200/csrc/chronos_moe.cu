@@ -51,7 +51,6 @@ int fail(int code, const char* fmt, ...) {
                         cudaGetErrorString(err_), __FILE__, __LINE__);                        \
     } while (0)
 
-constexpr int kSplitMaxTokens = 64;  // decode batches up to this size may split K
 constexpr int kDownWideMinTokens = 1024;  // batches from this size use 256-token down tiles
 
 std::atomic<uint64_t> g_kernel_launches{0};
@@ -114,8 +113,7 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 struct Layout {
     size_t grp_count, grp_off, act_rows, act_xrow, act_hrow, act_wslot, act_eid, ustart_gu, partials,
         ustart_dn, hdr, pos, sel_coef, shared_coef, topk_idx, topk_w, slot_tok, slot_coef, slot_map, xp,
-        hid, gu, y_acc, total;
-    bool split_capable;
+        hid, y_acc, total;
 };
 
 Layout make_layout(const ChronosMoeShape& s) {
@@ -151,8 +149,6 @@ Layout make_layout(const ChronosMoeShape& s) {
     L.slot_map = N <= static_cast<size_t>(kSelectPlanMaxTokens) ? take(4 * E * N) : off;
     L.xp = take(es * N * K * H);
     L.hid = take(es * (N * K + S * N) * F);
-    L.split_capable = N <= static_cast<size_t>(kSplitMaxTokens);
-    L.gu = L.split_capable ? take(4 * (N * K + S * N) * 2 * F) : off;
     L.y_acc = take(4 * N * H);
     L.total = off;
     return L;
@@ -388,12 +384,12 @@ int launch_select_plan(const RouteParams& rp, const PlanParams& pp, const Scatte
     return CHRONOS_OK;
 }
 
-template <typename T, int BN, bool GATEUP, bool SPLIT, bool DENSE = false>
+template <typename T, int BN, bool GATEUP, bool DENSE = false>
 int launch_tc(const CUtensorMap& a0r, const CUtensorMap& a1r, const CUtensorMap& a0s,
               const CUtensorMap& a1s, const CUtensorMap& br, const CUtensorMap& bs,
               const TcGemmParams& p, int grid, cudaStream_t st) {
-    constexpr int smem = tc_smem_bytes(BN, GATEUP, SPLIT);
-    auto kern = tc_grouped_gemm<T, BN, GATEUP, SPLIT, DENSE>;
+    constexpr int smem = tc_smem_bytes(BN, GATEUP);
+    auto kern = tc_grouped_gemm<T, BN, GATEUP, DENSE>;
     if (int rc = set_smem(kern, smem)) return rc;
     CHRONOS_CUDA_CHECK(launch_kernel(kern, dim3(grid), dim3(kTcThreads), smem, st, true, a0r, a1r, a0s,
                                      a1s, br, bs, p));
@@ -401,8 +397,8 @@ int launch_tc(const CUtensorMap& a0r, const CUtensorMap& a1r, const CUtensorMap&
 }
 
 template <typename T, int BN, int BN_DN>
-int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int splits_gu,
-                   int splits_dn, int kt_per_split_gu, int kt_per_split_dn, int slot, bool direct) {
+int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int kt_per_split_dn, int slot,
+                   bool direct) {
     const ChronosMoeShape& s = a->shape;
     const int dt = s.dtype;
     const uint64_t N = static_cast<uint64_t>(s.num_tokens), H = s.hidden, F = s.ffn;
@@ -443,7 +439,6 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     p.f = static_cast<int>(F);
     p.h = static_cast<int>(H);
     p.hid = w.ws + w.L->hid;
-    p.gu = w.at<float>(w.L->gu);
     p.y_acc = w.at<float>(w.L->y_acc);
     p.slot_tok = w.at<int32_t>(w.L->slot_tok);
     p.slot_coef = w.at<float>(w.L->slot_coef);
@@ -460,43 +455,14 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     TcGemmParams pg = p;
     pg.ustart = w.at<int32_t>(w.L->ustart_gu);
     pg.k_tiles = static_cast<int>(H / kTcBK);
-    pg.kt_per_split = kt_per_split_gu;
+    pg.kt_per_split = static_cast<int>(H / kTcBK);
     pg.m_tiles = static_cast<int>((F + kTcBM - 1) / kTcBM);
     pg.w_rows = static_cast<int>(F);
     pg.out_cols = static_cast<int>(F);
-    const bool split = splits_gu > 1;
-    if constexpr (BN > kSplitMaxTokens) {
-        if (split) return fail(CHRONOS_ERR_INVALID_ARG, "internal: split-K with a %d-token tile", BN);
-    }
-    if (split) {
-        if constexpr (BN <= kSplitMaxTokens) {
-        // (the plan/scatter kernel zeroed the fp32 partial buffer `gu`)
-        prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
-        if ((rc = launch_tc<T, BN, true, true, kDense>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st)))
-            return rc;
-        prof_ran(slot, CHRONOS_STAGE_GATEUP);
-        prof_mark(slot, CHRONOS_STAGE_ACT, st);
-        ActParams ap{};
-        ap.gu = w.at<float>(w.L->gu);
-        ap.hid = w.ws + w.L->hid;
-        ap.hdr = p.hdr;
-        ap.n = s.num_tokens;
-        ap.f = s.ffn;
-        ap.k = s.top_k;
-        ap.num_shared = s.num_shared;
-        const int64_t total = static_cast<int64_t>(slots * F);
-        const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4 * grid));
-        CHRONOS_CUDA_CHECK(launch_kernel(act_kernel<T>, dim3(blocks), dim3(256), 0, st, true, ap));
-        prof_ran(slot, CHRONOS_STAGE_ACT);
-        }
-    } else {
-        prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
-        if ((rc = launch_tc<T, BN, true, false, kDense>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st)))
-            return rc;
-        prof_ran(slot, CHRONOS_STAGE_GATEUP);
-        prof_mark(slot, CHRONOS_STAGE_ACT, st);
-    }
-    (void)splits_dn;
+    prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
+    if ((rc = launch_tc<T, BN, true, kDense>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st))) return rc;
+    prof_ran(slot, CHRONOS_STAGE_GATEUP);
+    prof_mark(slot, CHRONOS_STAGE_ACT, st);  // SiLU-mul is fused into the gate/up epilogue
     prof_mark(slot, CHRONOS_STAGE_DOWN, st);
     // down
     TcGemmParams pd = p;
@@ -507,7 +473,7 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     pd.w_rows = static_cast<int>(H);
     pd.out_cols = static_cast<int>(H);
     pd.y_direct = direct ? a->y : nullptr;
-    if ((rc = launch_tc<T, BN_DN, false, false>(d_r, d_r, d_s, d_s, h_m, h_m, pd, grid, st)))
+    if ((rc = launch_tc<T, BN_DN, false>(d_r, d_r, d_s, d_s, h_m, h_m, pd, grid, st)))
         return rc;
     prof_ran(slot, CHRONOS_STAGE_DOWN);
     return CHRONOS_OK;
@@ -626,17 +592,6 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     const int mt_gu = tc ? (s.ffn + kTcBM - 1) / kTcBM : (s.ffn + kSimtTile - 1) / kSimtTile;
     const int mt_dn = tc ? (s.hidden + kTcBM - 1) / kTcBM : (s.hidden + kSimtTile - 1) / kSimtTile;
 
-    // K splits for small decode batches: enough units to cover every SM twice
-    int splits_gu = 1, kt_gu = s.hidden / kTcBK;
-    if (tc && L.split_capable) {
-        const int kt_total = s.hidden / kTcBK;
-        const int64_t groups_est = std::min<int64_t>(s.num_experts, N * s.top_k) + s.num_shared;
-        const int target = 2 * sm_count();
-        while (groups_est * mt_gu * splits_gu < target && splits_gu * 2 * 4 <= kt_total)
-            splits_gu *= 2;
-        kt_gu = (kt_total + splits_gu - 1) / splits_gu;
-        splits_gu = (kt_total + kt_gu - 1) / kt_gu;
-    }
     int splits_dn = 1, kt_dn = s.ffn / kTcBK;
     if (tc) {
         const int kt_total = s.ffn / kTcBK;
@@ -684,7 +639,6 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     pp.tok_tile_dn = tok_tile_dn;
     pp.mt_gu = mt_gu;
     pp.mt_dn = mt_dn;
-    pp.splits_gu = splits_gu;
     pp.splits_dn = splits_dn;
     pp.grp_count = w.at<int32_t>(L.grp_count);
     pp.slot_of_expert = a->slot_of_expert;
@@ -715,10 +669,6 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     sp.slot_tok = w.at<int32_t>(L.slot_tok);
     sp.slot_coef = w.at<float>(L.slot_coef);
     sp.copy_rows = tc ? 1 : 0;
-    if (tc && splits_gu > 1) {  // split-K partials accumulate into `gu`
-        sp.zero = reinterpret_cast<float4*>(w.ws + L.gu);
-        sp.zero_count4 = static_cast<int64_t>((N * s.top_k + s.num_shared * N) * 2 * s.ffn / 4);
-    }
     if (fused_plan) {
         sp.copy_rows = 0;
         sp.slot_map = tc ? w.at<int32_t>(L.slot_map) : nullptr;
@@ -739,15 +689,13 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
             return fail(CHRONOS_ERR_INVALID_ARG, "internal: fp32 on the tensor-core path");
         } else {
             switch (bn) {
-                case 16: rc = launch_tc_pair<T, 16, 16>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot, direct); break;
-                case 32: rc = launch_tc_pair<T, 32, 32>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot, direct); break;
-                case 64: rc = launch_tc_pair<T, 64, 64>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot, direct); break;
+                case 16: rc = launch_tc_pair<T, 16, 16>(a, w, st, kt_dn, slot, direct); break;
+                case 32: rc = launch_tc_pair<T, 32, 32>(a, w, st, kt_dn, slot, direct); break;
+                case 64: rc = launch_tc_pair<T, 64, 64>(a, w, st, kt_dn, slot, direct); break;
                 default:
                     rc = bn_dn == 256
-                             ? launch_tc_pair<T, 128, 256>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot,
-                                                           direct)
-                             : launch_tc_pair<T, 128, 128>(a, w, st, splits_gu, splits_dn, kt_gu, kt_dn, slot,
-                                                           direct);
+                             ? launch_tc_pair<T, 128, 256>(a, w, st, kt_dn, slot, direct)
+                             : launch_tc_pair<T, 128, 128>(a, w, st, kt_dn, slot, direct);
                     break;
             }
         }

@@ -7,8 +7,7 @@
 //           tile of 128 rows of its gate/up weights x BN token rows,
 //             G = W_gate[rows] . X^T,  U = W_up[rows] . X^T   (two MMAs, one
 //           shared B tile), epilogue h[token][f] = silu(G) * U in the input
-//           dtype (or, with SPLIT, fp32 partial sums reduced into a [slot, 2F]
-//           buffer when K is split across CTAs for small decode batches);
+//           dtype;
 //   DOWN:   D = W_down[rows] . h^T, epilogue y_acc[token][n] += coef * D with
 //           coef = w * a for routed slots and (1 + sum w (1-a)) / S_h for
 //           shared slots — the availability blend and the weighted combine of
@@ -53,7 +52,6 @@ struct TcGemmParams {
     int out_cols;      // F (gate/up) or H (down)
     int f, h;
     void* hid;               // GATEUP: [slots, F]
-    float* gu;               // GATEUP + SPLIT: [slots, 2F]
     float* y_acc;            // DOWN: [N, H]
     const int32_t* slot_tok;
     const float* slot_coef;
@@ -75,20 +73,20 @@ __host__ __device__ constexpr int tc_stage_bytes(int bn, bool gateup) {
     return kTcBM * kTcBK * 2 * (gateup ? 2 : 1) + bn * kTcBK * 2;
 }
 // Epilogue staging: one output row per token of the tile, written to global
-// memory by per-token bulk copies (h rows: 128 bf16; split partials: 128 fp32
-// gate + 128 fp32 up; down: 128 fp32 to reduce into the accumulator).
-__host__ __device__ constexpr int tc_stage_row_bytes(bool gateup, bool split) {
-    return gateup ? (split ? 2 * kTcBM * 4 : kTcBM * 2) : kTcBM * 4;
+// memory by per-token bulk copies (h rows: 128 bf16; down: 128 fp32 to reduce
+// into the accumulator, or 128 output elements stored directly).
+__host__ __device__ constexpr int tc_stage_row_bytes(bool gateup) {
+    return gateup ? kTcBM * 2 : kTcBM * 4;
 }
 // Rows staged at a time (a 256-token tile is drained in two halves).
 __host__ __device__ constexpr int tc_staging_rows(int bn) { return bn < 128 ? bn : 128; }
-__host__ __device__ constexpr int tc_staging_bytes(int bn, bool gateup, bool split) {
-    return tc_staging_rows(bn) * tc_stage_row_bytes(gateup, split);
+__host__ __device__ constexpr int tc_staging_bytes(int bn, bool gateup) {
+    return tc_staging_rows(bn) * tc_stage_row_bytes(gateup);
 }
-__host__ __device__ constexpr int tc_stages(int bn, bool gateup, bool split) {
-    return (220 * 1024 - tc_staging_bytes(bn, gateup, split)) / tc_stage_bytes(bn, gateup) > 8
+__host__ __device__ constexpr int tc_stages(int bn, bool gateup) {
+    return (220 * 1024 - tc_staging_bytes(bn, gateup)) / tc_stage_bytes(bn, gateup) > 8
                ? 8
-               : (220 * 1024 - tc_staging_bytes(bn, gateup, split)) / tc_stage_bytes(bn, gateup);
+               : (220 * 1024 - tc_staging_bytes(bn, gateup)) / tc_stage_bytes(bn, gateup);
 }
 __host__ __device__ constexpr int tc_tmem_cols(int bn, bool gateup) {
     // two accumulator buffers of (gateup ? 2 : 1) * bn fp32 columns, power of two >= 32
@@ -98,9 +96,9 @@ __host__ __device__ constexpr int tc_tmem_cols(int bn, bool gateup) {
            : (2 * bn * (gateup ? 2 : 1)) <= 256 ? 256
                                                  : 512;
 }
-__host__ __device__ constexpr int tc_smem_bytes(int bn, bool gateup, bool split) {
-    return 1024 /* alignment slack */ + tc_stages(bn, gateup, split) * tc_stage_bytes(bn, gateup) +
-           tc_staging_bytes(bn, gateup, split) + 4 * bn * 4 /* per-unit slot tables x2 */ + 256;
+__host__ __device__ constexpr int tc_smem_bytes(int bn, bool gateup) {
+    return 1024 /* alignment slack */ + tc_stages(bn, gateup) * tc_stage_bytes(bn, gateup) +
+           tc_staging_bytes(bn, gateup) + 4 * bn * 4 /* per-unit slot tables x2 */ + 256;
 }
 
 struct TcUnit {
@@ -126,7 +124,7 @@ __device__ __forceinline__ TcUnit tc_decode(const TcGemmParams& p, int num_activ
     return r;
 }
 
-template <typename T, int BN, bool GATEUP, bool SPLIT, bool DENSE = false>
+template <typename T, int BN, bool GATEUP, bool DENSE = false>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_grouped_gemm(const __grid_constant__ CUtensorMap tm_a0r,  // routed gate (or down)
                     const __grid_constant__ CUtensorMap tm_a1r,  // routed up
@@ -138,8 +136,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     constexpr int A_BYTES = kTcBM * kTcBK * 2;
     constexpr int B_BYTES = BN * kTcBK * 2;
     constexpr int STAGE_BYTES = tc_stage_bytes(BN, GATEUP);
-    constexpr int STAGES = tc_stages(BN, GATEUP, SPLIT);
-    constexpr int ROW_BYTES = tc_stage_row_bytes(GATEUP, SPLIT);
+    constexpr int STAGES = tc_stages(BN, GATEUP);
+    constexpr int ROW_BYTES = tc_stage_row_bytes(GATEUP);
     constexpr int ACC_COLS = GATEUP ? 2 * BN : BN;
     constexpr int TMEM_COLS = tc_tmem_cols(BN, GATEUP);
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N must be a multiple of 16");
@@ -147,7 +145,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                   "operand tiles must keep the 1024-byte alignment of the 128-B swizzle atoms");
     static_assert(2 * ACC_COLS <= 512, "two accumulator buffers must fit in TMEM");
     static_assert(STAGES >= 2, "shared memory holds fewer than two pipeline stages");
-    static_assert(tc_smem_bytes(BN, GATEUP, SPLIT) <= 232448, "shared memory over the per-CTA limit");
+    static_assert(tc_smem_bytes(BN, GATEUP) <= 232448, "shared memory over the per-CTA limit");
 
     extern __shared__ uint8_t tc_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -302,8 +300,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // ------------------------------ epilogue ------------------------------
         // Each unit: TMEM -> registers -> staging rows in shared memory (one row
         // per token, 128 output columns), then one bulk copy per valid token
-        // row: a TMA reduce-add into the fp32 accumulator (down, split
-        // partials) or a plain bulk store of the hidden row (gate/up).
+        // row: a TMA reduce-add into the fp32 accumulator (down) or a plain
+        // bulk store (gate/up hidden rows; down rows in direct-output mode).
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         const int row_in_tile = q * 32 + lane;
         const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
@@ -366,13 +364,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
                             uint8_t* row = staging + (c - c0 + j) * ROW_BYTES;
-                            if constexpr (SPLIT) {
-                                reinterpret_cast<float*>(row)[row_in_tile] = g[j];
-                                reinterpret_cast<float*>(row)[kTcBM + row_in_tile] = uu[j];
-                            } else {
-                                reinterpret_cast<T*>(row)[row_in_tile] =
-                                    from_f32<T>(silu_f32(g[j]) * uu[j]);
-                            }
+                            reinterpret_cast<T*>(row)[row_in_tile] = from_f32<T>(silu_f32(g[j]) * uu[j]);
                         }
                     } else {
                         tmem_wait_ld();
@@ -411,15 +403,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                     const uint8_t* row = staging + r * ROW_BYTES;
                     if constexpr (GATEUP) {
-                        if constexpr (SPLIT) {
-                            float* dst = p.gu + slot * 2 * p.f + m0;
-                            bulk_reduce_add_f32(dst, row, static_cast<uint32_t>(ncols * 4));
-                            bulk_reduce_add_f32(dst + p.f, row + kTcBM * 4,
-                                                static_cast<uint32_t>(ncols * 4));
-                        } else {
-                            bulk_store(static_cast<T*>(p.hid) + slot * p.f + m0, row,
-                                       static_cast<uint32_t>(ncols * sizeof(T)));
-                        }
+                        bulk_store(static_cast<T*>(p.hid) + slot * p.f + m0, row,
+                                   static_cast<uint32_t>(ncols * sizeof(T)));
                     } else {
                         const int64_t t = tk[c0 + r];
                         if (p.y_direct != nullptr)

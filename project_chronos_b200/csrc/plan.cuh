@@ -34,7 +34,7 @@ struct PlanParams {
     int tok_tile;                 // token rows per gate/up GEMM tile
     int tok_tile_dn;              // token rows per down GEMM tile
     int mt_gu, mt_dn;             // weight-row tiles per group (gate/up, down)
-    int splits_gu, splits_dn;     // K splits per tile
+    int splits_dn;                // K splits per down tile
     const int32_t* grp_count;     // [E]
     const int32_t* slot_of_expert;  // [E] or null
     PlanHeader* hdr;
@@ -91,7 +91,7 @@ __device__ __forceinline__ void plan_tables(const PlanParams& p, int cnt, int in
     const int is_act = (tid < E && cnt > 0) ? 1 : 0;
     const int tt = (cnt + p.tok_tile - 1) / p.tok_tile;
     const int tt_dn = (cnt + p.tok_tile_dn - 1) / p.tok_tile_dn;
-    const int ugu = is_act ? tt * p.mt_gu * p.splits_gu : 0;
+    const int ugu = is_act ? tt * p.mt_gu : 0;
     const int udn = is_act ? tt_dn * p.mt_dn * p.splits_dn : 0;
     const int inc_act = block_inclusive_scan<NT>(is_act, s_scratch);
     const int inc_gu = block_inclusive_scan<NT>(ugu, s_scratch);
@@ -106,7 +106,7 @@ __device__ __forceinline__ void plan_tables(const PlanParams& p, int cnt, int in
     // shared groups first (the largest: N rows each), then routed groups in expert order
     const int tt_sh = (N + p.tok_tile - 1) / p.tok_tile;
     const int tt_sh_dn = (N + p.tok_tile_dn - 1) / p.tok_tile_dn;
-    const int sh_gu = tt_sh * p.mt_gu * p.splits_gu;
+    const int sh_gu = tt_sh * p.mt_gu;
     const int sh_dn = tt_sh_dn * p.mt_dn * p.splits_dn;
     if (tid < E) {
         const int off = inc_cnt - cnt;
@@ -158,8 +158,6 @@ struct ScatterParams {
     int32_t* slot_tok;    // [N*k + S*N]
     float* slot_coef;     // [N*k + S*N]
     int copy_rows;        // 0: only the slot tables (B operand read from x by row index)
-    float4* zero;         // buffer the next kernel accumulates into (split-K partials), or null
-    int64_t zero_count4;  // its size in float4
     int32_t* slot_map;    // decode batches: [E, N] slot of (expert, token) or -1
     int e;                // experts (rows of slot_map)
 };
@@ -180,11 +178,6 @@ __global__ void __launch_bounds__(kScatterThreads) plan_scatter_kernel(PlanParam
     __shared__ int s_off[kPlanThreads];
     const int tid = threadIdx.x;
     pdl_trigger();
-    if (p.zero != nullptr) {  // independent of the routing: before the dependency wait
-        for (int64_t i = static_cast<int64_t>(blockIdx.x) * kScatterThreads + tid; i < p.zero_count4;
-             i += static_cast<int64_t>(gridDim.x) * kScatterThreads)
-            p.zero[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
     pdl_wait();  // routing results
     const int cnt = tid < pp.e ? pp.grp_count[tid] : 0;
     const int inc_cnt = block_inclusive_scan(cnt, s_scratch);
@@ -256,8 +249,6 @@ __global__ void __launch_bounds__(kSelectPlanThreads)
     const int64_t gtid = static_cast<int64_t>(blockIdx.x) * kSelectPlanThreads + tid;
     const int64_t gthreads = static_cast<int64_t>(gridDim.x) * kSelectPlanThreads;
     pdl_trigger();
-    if (sp.zero != nullptr)  // split-K partial buffer: independent of the routing
-        for (int64_t i = gtid; i < sp.zero_count4; i += gthreads) sp.zero[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (sp.slot_map != nullptr)
         for (int64_t i = gtid; i < static_cast<int64_t>(sp.e) * sp.n; i += gthreads) sp.slot_map[i] = -1;
     pdl_wait();  // chunk partials and zeroed counters from the logit kernel
@@ -315,36 +306,6 @@ __global__ void __launch_bounds__(kSelectPlanThreads)
         sp.slot_tok[slot] = static_cast<int32_t>(tt);
         sp.slot_coef[slot] = c;
         if (sp.slot_map != nullptr) sp.slot_map[static_cast<int64_t>(e) * sp.n + tt] = static_cast<int32_t>(slot);
-    }
-}
-
-struct ActParams {
-    const float* gu;   // [rows, 2F] fp32 split-K partial sums (gate | up)
-    void* hid;         // [rows, F]
-    const PlanHeader* hdr;
-    int64_t n;
-    int f, k, num_shared;
-};
-
-// h = silu(g) * u for every slot row in use (routed rows < routed_rows, then
-// the shared rows).
-template <typename T>
-__global__ void act_kernel(ActParams p) {
-    pdl_trigger();
-    pdl_wait();
-    const int64_t routed_cap = p.n * p.k;
-    const int64_t rows_total = routed_cap + p.n * p.num_shared;
-    const int routed_rows = p.hdr->routed_rows;
-    const int64_t per_row = p.f;
-    const int64_t total = rows_total * per_row;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t r = i / per_row;
-        const int c = static_cast<int>(i % per_row);
-        if (r < routed_cap && r >= routed_rows) continue;
-        const float g = p.gu[r * 2 * p.f + c];
-        const float u = p.gu[r * 2 * p.f + p.f + c];
-        static_cast<T*>(p.hid)[r * p.f + c] = from_f32<T>(silu_f32(g) * u);
     }
 }
 

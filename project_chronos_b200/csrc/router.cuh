@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(kPartialThreads) route_partials_kernel(RoutePa
     __shared__ __align__(16) uint8_t ws[kPartialThreads * ROW];
     pdl_trigger();
     if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) zero_route_counters(p);
-    const int E = p.e, C = p.nchunks, H = p.h;
+    const int E = p.e, H = p.h;
     const int c = blockIdx.y;
     const int e0 = blockIdx.z * kPartialThreads;
     const int e = e0 + threadIdx.x;
