@@ -157,6 +157,9 @@ class ChronosMOEFeedForward(nn.Module):
         self._avail_cache = {}
         # Slot pools owned by a pooled ExpertStore (attach_expert_pool), or None.
         self._ext_pool = None
+        # bound fast-path call (ops.LayerCall) and the key of what it was bound to
+        self._call = None
+        self._call_key = None
 
     # ------------------------------------------------------------------
     # bookkeeping attributes (lazy: resolved from device tensors on read)
@@ -368,6 +371,25 @@ class ChronosMOEFeedForward(nn.Module):
         self._avail_cache = {}
         self._pool_dirty = False
 
+    def _layer_call(self, pool, bias) -> "ops.LayerCall":
+        """The bound fast-path call for the current weights (rebuilt when any of
+        them, the router bias or the readiness settings change)."""
+        w = self.gate.weight
+        key = (w.data_ptr(), w.dtype, pool["gate"].data_ptr(), pool["up"].data_ptr(),
+               pool["down"].data_ptr(), None if pool["sh_gate"] is None else pool["sh_gate"].data_ptr(),
+               None if bias is None else (bias.data_ptr(), bias._version),
+               None if pool.get("slot") is None else pool["slot"].data_ptr(),
+               None if self.expert_ready_flags is None else self.expert_ready_flags.data_ptr(),
+               self.expert_ready_epoch, self.expert_ready_timeout_ns, bool(self.norm_topk_prob))
+        if self._call_key != key:
+            self._call = ops.LayerCall(
+                w, pool["gate"], pool["up"], pool["down"], pool["sh_gate"], pool["sh_up"], pool["sh_down"],
+                self.num_experts_per_tok, bool(self.norm_topk_prob), router_bias=bias,
+                slot_of_expert=pool.get("slot"), ready_flags=self.expert_ready_flags,
+                ready_epoch=self.expert_ready_epoch, spin_limit_ns=self.expert_ready_timeout_ns)
+            self._call_key = key
+        return self._call
+
     def _avail_tensor(self, a: np.ndarray, device) -> torch.Tensor:
         key = (a.tobytes(), str(device))
         t = self._avail_cache.get(key)
@@ -570,13 +592,8 @@ class ChronosMOEFeedForward(nn.Module):
                 else:
                     a_np = None
                     avail_t = avail_dev
-            out = ops.moe_forward(
-                x_flat, self.gate.weight, pool["gate"], pool["up"], pool["down"],
-                pool["sh_gate"], pool["sh_up"], pool["sh_down"], k, bool(self.norm_topk_prob),
-                avail=avail_t, router_bias=bias, slot_of_expert=pool.get("slot"),
-                ready_flags=self.expert_ready_flags,
-                ready_epoch=self.expert_ready_epoch, spin_limit_ns=self.expert_ready_timeout_ns,
-                want_probs=True, want_stats=masked)
+            out = self._layer_call(pool, bias)(x_flat, avail=avail_t, want_probs=True,
+                                               want_stats=masked, want_topk=self.training)
             probs = out["probs"]
             if masked:
                 if a_np is None:

@@ -149,6 +149,100 @@ def moe_forward(x: torch.Tensor, router_w: torch.Tensor, w_gate: torch.Tensor, w
     return dict(y=y, probs=probs, topk_idx=topk_idx, topk_weight=topk_w, counts=counts, mass=mass)
 
 
+class LayerCall:
+    """One layer's static arguments bound once, for repeated calls with little host work.
+
+    ``LayerCall(router_w, w_gate, ...)(x, avail=...)`` computes what
+    ``moe_forward`` computes.  The weights, pools, slot map, ready flags and
+    router bias are checked and converted once; each call allocates only its
+    outputs, reuses a workspace per token count (calls are ordered on the
+    current stream, so the reuse is safe on one stream) and copies a prebuilt
+    argument struct.  Rebuild it when any bound tensor is replaced."""
+
+    def __init__(self, router_w, w_gate, w_up, w_down, sh_gate, sh_up, sh_down, top_k: int,
+                 norm_topk: bool, router_bias=None, slot_of_expert=None, ready_flags=None,
+                 ready_epoch: int = 0, spin_limit_ns: int = 0):
+        _check_cuda(router_w, w_gate, w_up, w_down, sh_gate, sh_up, sh_down, router_bias, slot_of_expert,
+                    ready_flags)
+        dt = router_w.dtype
+        for name, t in (("w_gate", w_gate), ("w_up", w_up), ("w_down", w_down), ("sh_gate", sh_gate),
+                        ("sh_up", sh_up), ("sh_down", sh_down)):
+            if t is not None and t.dtype != dt:
+                raise TypeError(f"{name} dtype {t.dtype} != router dtype {dt}")
+        self.dev = router_w.device
+        self.dtype = dt
+        self.e = router_w.shape[0]
+        self.p_slots, self.f, self.h = w_gate.shape
+        self.s = 0 if sh_gate is None else sh_gate.shape[0]
+        self.k = int(top_k)
+        # keep the (contiguous) tensors alive: the struct holds their addresses
+        self._keep = [t.contiguous() if t is not None else None
+                      for t in (router_w, w_gate, w_up, w_down, sh_gate, sh_up, sh_down)]
+        rb = None if router_bias is None else router_bias.to(device=self.dev, dtype=torch.float32).contiguous()
+        self._keep += [rb, slot_of_expert, ready_flags]
+        r, g, u, d, sg, su, sd = self._keep[:7]
+        self._lib = N.load_library()
+        self._tmpl = N.ChronosMoeArgs(
+            shape=_shape(0, self.h, self.e, self.k, self.f, self.s, dt), norm_topk=int(bool(norm_topk)),
+            flags=0, router_w=_ptr(r), router_bias=_ptr(rb), w_gate=_ptr(g), w_up=_ptr(u), w_down=_ptr(d),
+            pool_slots=int(self.p_slots), slot_of_expert=_ptr(slot_of_expert), w_shared_gate=_ptr(sg),
+            w_shared_up=_ptr(su), w_shared_down=_ptr(sd), ready_flags=_ptr(ready_flags),
+            ready_epoch=int(ready_epoch), spin_limit_ns=int(spin_limit_ns),
+            status=_ptr(status_word(self.dev)))
+        self._ws = {}
+
+    def _workspace(self, n: int) -> torch.Tensor:
+        ws = self._ws.get(n)
+        if ws is None:
+            shp = _shape(n, self.h, self.e, self.k, self.f, self.s, self.dtype)
+            size = int(self._lib.chronos_moe_workspace_size(ctypes.byref(shp)))
+            if size == 0 and n > 0:
+                N.check(N.CHRONOS_ERR_INVALID_ARG)
+            ws = torch.empty(max(size, 256), dtype=torch.uint8, device=self.dev)
+            if len(self._ws) > 16:
+                self._ws.clear()
+            self._ws[n] = ws
+        return ws
+
+    def __call__(self, x: torch.Tensor, avail: Optional[torch.Tensor] = None, want_probs: bool = True,
+                 want_stats: bool = False, want_topk: bool = False) -> dict:
+        if not x.is_cuda or x.dtype != self.dtype:
+            raise TypeError(f"x must be a CUDA {self.dtype} tensor")
+        x = x.contiguous()
+        n = x.shape[0]
+        dev = self.dev
+        ws = self._workspace(n)
+        y = torch.empty(n, self.h, dtype=self.dtype, device=dev)
+        probs = torch.empty(n, self.e, dtype=self.dtype, device=dev) if want_probs else None
+        topk_idx = torch.empty(n, self.k, dtype=torch.int32, device=dev) if want_topk else None
+        topk_w = torch.empty(n, self.k, dtype=torch.float32, device=dev) if want_topk else None
+        counts = torch.empty(self.e, dtype=torch.int32, device=dev) if want_stats else None
+        mass = torch.empty(self.e, dtype=torch.float32, device=dev) if want_stats else None
+        if avail is not None and (avail.dtype != torch.float32 or not avail.is_cuda
+                                  or not avail.is_contiguous()):
+            avail = avail.to(device=dev, dtype=torch.float32).contiguous()
+        a = N.ChronosMoeArgs.from_buffer_copy(self._tmpl)
+        a.shape.num_tokens = n
+        a.x = x.data_ptr()
+        a.y = y.data_ptr()
+        a.router_probs = _ptr(probs)
+        a.avail = _ptr(avail)
+        a.topk_idx = _ptr(topk_idx)
+        a.topk_weight = _ptr(topk_w)
+        a.expert_counts = _ptr(counts)
+        a.expert_mass = _ptr(mass)
+        a.workspace = ws.data_ptr()
+        a.workspace_bytes = ws.numel()
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        if torch.cuda.current_device() == dev.index:
+            rc = self._lib.chronos_moe_forward(ctypes.byref(a), ctypes.c_void_p(stream))
+        else:
+            with torch.cuda.device(dev):
+                rc = self._lib.chronos_moe_forward(ctypes.byref(a), ctypes.c_void_p(stream))
+        N.check(rc)
+        return dict(y=y, probs=probs, topk_idx=topk_idx, topk_weight=topk_w, counts=counts, mass=mass)
+
+
 def moe_route(x: torch.Tensor, router_w: torch.Tensor, top_k: int, norm_topk: bool,
               num_shared: int = 0, ffn: int = 64, router_bias: Optional[torch.Tensor] = None,
               want_probs: bool = True, workspace: Optional[torch.Tensor] = None):
