@@ -329,53 +329,32 @@ __device__ __forceinline__ void select_token(const RouteParams& p, int64_t t, in
         return;
     }
     const int C = p.nchunks;
-    const int64_t cs = p.n * E;  // partials[c][t][e]: the warp's lanes read consecutive experts
-    // availability of this lane's experts, loaded up front with the partials
-    float av[EPL], bias[EPL];
-#pragma unroll
-    for (int q = 0; q < EPL; ++q) {
-        const int e = lane + 32 * q;
-        av[q] = e < E ? expert_avail(p, e) : 0.0f;
-        bias[q] = (p.bias != nullptr && e < E) ? p.bias[e] : 0.0f;
-    }
-    // logits: every chunk partial of a group of chunks (all of this lane's experts)
-    // is loaded before the in-order adds, so one group costs one memory latency
-    constexpr int GC = EPL <= 2 ? 16 : (EPL <= 4 ? 8 : 4);
     float v[EPL];
-#pragma unroll
-    for (int q = 0; q < EPL; ++q) v[q] = 0.0f;
-    int c = 0;
-    for (; c + GC <= C; c += GC) {
-        float r[EPL][GC];
-#pragma unroll
-        for (int q = 0; q < EPL; ++q) {
-            const int e = lane + 32 * q;
-            const float* pp = p.partials + t * E + (e < E ? e : 0);
-#pragma unroll
-            for (int u = 0; u < GC; ++u) r[q][u] = pp[(c + u) * cs];
-        }
-#pragma unroll
-        for (int q = 0; q < EPL; ++q)
-#pragma unroll
-            for (int u = 0; u < GC; ++u) v[q] = v[q] + r[q][u];
-    }
-    for (; c < C; ++c) {
-#pragma unroll
-        for (int q = 0; q < EPL; ++q) {
-            const int e = lane + 32 * q;
-            v[q] = v[q] + p.partials[c * cs + t * E + (e < E ? e : 0)];
-        }
-    }
     float m = -INFINITY;
 #pragma unroll
     for (int q = 0; q < EPL; ++q) {
         const int e = lane + 32 * q;
+        float lg = -INFINITY;
         if (e < E) {
-            if (p.bias) v[q] = v[q] + bias[q];
-        } else {
-            v[q] = -INFINITY;
+            // partials[c][t][e]: the warp's lanes read consecutive experts
+            const float* pp = p.partials + t * E + e;
+            const int64_t cs = p.n * E;
+            float s = 0.0f;
+            int c = 0;
+            // loads in groups of 16 ahead of the in-order adds
+            for (; c + 16 <= C; c += 16) {
+                float r[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) r[u] = pp[(c + u) * cs];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) s = s + r[u];
+            }
+            for (; c < C; ++c) s = s + pp[c * cs];
+            if (p.bias) s = s + p.bias[e];
+            lg = s;
         }
-        m = fmaxf(m, v[q]);
+        v[q] = lg;
+        m = fmaxf(m, lg);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -436,24 +415,20 @@ __device__ __forceinline__ void select_token(const RouteParams& p, int64_t t, in
             bi = lo;
         }
         if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-        // probability and availability of the chosen expert, from its owner lane
-        float pe = 0.0f, pa = 0.0f;
+        // probability of the chosen expert, broadcast from its owner lane
+        float pe = 0.0f;
 #pragma unroll
         for (int q = 0; q < EPL; ++q)
-            if ((bi >> 5) == q) {
-                pe = ex[q] * inv;
-                pa = av[q];
-            }
+            if ((bi >> 5) == q) pe = ex[q] * inv;
         pe = __shfl_sync(0xffffffffu, pe, bi & 31);
-        pa = __shfl_sync(0xffffffffu, pa, bi & 31);
         if (lane == j) {
             mine_e = bi;
             mine_w = pe;
-            mine_a = pa;
         }
         wsum += pe;
     }
     if (p.norm_topk) mine_w = mine_w / (wsum + 1e-20f);
+    if (lane < p.k) mine_a = expert_avail(p, mine_e);
     float extra = lane < p.k ? mine_w * (1.0f - mine_a) : 0.0f;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) extra += __shfl_xor_sync(0xffffffffu, extra, o);
