@@ -78,15 +78,29 @@ __host__ __device__ constexpr int tc_stage_bytes(int bn, bool gateup) {
 __host__ __device__ constexpr int tc_stage_row_bytes(bool gateup) {
     return gateup ? kTcBM * 2 : kTcBM * 4;
 }
-// Rows staged at a time (a 256-token tile is drained in two halves).
-__host__ __device__ constexpr int tc_staging_rows(int bn) { return bn < 128 ? bn : 128; }
+// Dynamic shared memory of one CTA: the per-CTA limit (227 KB) minus the
+// 1024-byte alignment slack, the barriers (256 B) and the per-unit slot tables.
+__host__ __device__ constexpr int tc_ring_budget(int bn) { return 232448 - 1024 - 256 - 4 * bn * 4; }
+__host__ __device__ constexpr int tc_stages_with(int bn, bool gateup, int sub) {
+    return (tc_ring_budget(bn) - sub * tc_stage_row_bytes(gateup)) / tc_stage_bytes(bn, gateup) > 8
+               ? 8
+               : (tc_ring_budget(bn) - sub * tc_stage_row_bytes(gateup)) / tc_stage_bytes(bn, gateup);
+}
+// Rows staged at a time: the most (128, 64, 32 or 16, at most BN) that still
+// leaves the TMA ring as many stages as the smallest staging would, so the
+// epilogue buffer never costs the pipeline a stage (a 128-token gate/up tile
+// stages 64 rows: 4 stages instead of 3).
+__host__ __device__ constexpr int tc_staging_rows(int bn, bool gateup) {
+    return (bn >= 128 && tc_stages_with(bn, gateup, 128) >= tc_stages_with(bn, gateup, 16))  ? 128
+           : (bn >= 64 && tc_stages_with(bn, gateup, 64) >= tc_stages_with(bn, gateup, 16)) ? 64
+           : (bn >= 32 && tc_stages_with(bn, gateup, 32) >= tc_stages_with(bn, gateup, 16)) ? 32
+                                                                                               : 16;
+}
 __host__ __device__ constexpr int tc_staging_bytes(int bn, bool gateup) {
-    return tc_staging_rows(bn) * tc_stage_row_bytes(gateup);
+    return tc_staging_rows(bn, gateup) * tc_stage_row_bytes(gateup);
 }
 __host__ __device__ constexpr int tc_stages(int bn, bool gateup) {
-    return (220 * 1024 - tc_staging_bytes(bn, gateup)) / tc_stage_bytes(bn, gateup) > 8
-               ? 8
-               : (220 * 1024 - tc_staging_bytes(bn, gateup)) / tc_stage_bytes(bn, gateup);
+    return tc_stages_with(bn, gateup, tc_staging_rows(bn, gateup));
 }
 __host__ __device__ constexpr int tc_tmem_cols(int bn, bool gateup) {
     // two accumulator buffers of (gateup ? 2 : 1) * bn fp32 columns, power of two >= 32
@@ -150,9 +164,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ uint8_t tc_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint8_t* staging = smem + STAGES * STAGE_BYTES;  // [tc_staging_rows(BN)][ROW_BYTES]
+    uint8_t* staging = smem + STAGES * STAGE_BYTES;  // [tc_staging_rows(BN, GATEUP)][ROW_BYTES]
     // per-unit slot tables of the tile (coefficient, token), double-buffered by accumulator
-    float* s_coef = reinterpret_cast<float*>(staging + tc_staging_rows(BN) * ROW_BYTES);  // [2][BN]
+    float* s_coef = reinterpret_cast<float*>(staging + tc_staging_rows(BN, GATEUP) * ROW_BYTES);  // [2][BN]
     int32_t* s_tok = reinterpret_cast<int32_t*>(s_coef + 2 * BN);                          // [2][BN]
     uint64_t* full = reinterpret_cast<uint64_t*>(s_tok + 2 * BN);
     uint64_t* empty = full + STAGES;
@@ -345,7 +359,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                    static_cast<uint32_t>(acc * ACC_COLS);
             const int m0 = w.mtile * kTcBM;
             const int ncols = min(kTcBM, p.out_cols - m0);
-            constexpr int SUB = tc_staging_rows(BN);
+            constexpr int SUB = tc_staging_rows(BN, GATEUP);
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += SUB) {
                 if (c0 > 0) {
