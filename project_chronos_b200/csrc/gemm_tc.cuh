@@ -86,15 +86,17 @@ __host__ __device__ constexpr int tc_stages_with(int bn, bool gateup, int sub) {
                ? 8
                : (tc_ring_budget(bn) - sub * tc_stage_row_bytes(gateup)) / tc_stage_bytes(bn, gateup);
 }
-// Rows staged at a time: the most (128, 64, 32 or 16, at most BN) that still
-// leaves the TMA ring as many stages as the smallest staging would, so the
-// epilogue buffer never costs the pipeline a stage (a 128-token gate/up tile
-// stages 64 rows: 4 stages instead of 3).
+// Rows staged at a time.  Gate/up: the most (128, 64, 32 or 16, at most BN)
+// that still leaves the TMA ring as many stages as the smallest staging would
+// (a 128-token tile stages 64 rows: 4 stages instead of 3).  Down: up to 128
+// rows; its fp32 rows are drained by reductions, and draining a 256-token tile
+// in smaller pieces measured slower than the extra stage gains.
 __host__ __device__ constexpr int tc_staging_rows(int bn, bool gateup) {
-    return (bn >= 128 && tc_stages_with(bn, gateup, 128) >= tc_stages_with(bn, gateup, 16))  ? 128
-           : (bn >= 64 && tc_stages_with(bn, gateup, 64) >= tc_stages_with(bn, gateup, 16)) ? 64
-           : (bn >= 32 && tc_stages_with(bn, gateup, 32) >= tc_stages_with(bn, gateup, 16)) ? 32
-                                                                                               : 16;
+    return !gateup ? (bn < 128 ? bn : 128)
+           : (bn >= 128 && tc_stages_with(bn, gateup, 128) >= tc_stages_with(bn, gateup, 16)) ? 128
+           : (bn >= 64 && tc_stages_with(bn, gateup, 64) >= tc_stages_with(bn, gateup, 16))   ? 64
+           : (bn >= 32 && tc_stages_with(bn, gateup, 32) >= tc_stages_with(bn, gateup, 16))   ? 32
+                                                                                                 : 16;
 }
 __host__ __device__ constexpr int tc_staging_bytes(int bn, bool gateup) {
     return tc_staging_rows(bn, gateup) * tc_stage_row_bytes(gateup);
