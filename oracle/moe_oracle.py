@@ -14,6 +14,8 @@ What it restates (all citations are files of FonaTech/Project_Chronos):
 * the expert FFN — minimind ``FeedForward``, restated in the reference at
   ``chronos/mlx/moe.py:13-23``: ``down(silu(gate(x)) * up(x))``, bias-free;
 * shared experts — ``moe_chronos.py:90-93``: the MEAN of the shared FFNs;
+* the lookahead router — ``chronos/model/lookahead_router.py:36-55``
+  (``lookahead``);
 * the blend and combine — ``moe_chronos.py:190-268`` with the arithmetic form
   of ``chronos/mlx/moe.py:160-166``:
   ``y_t = sum_k w_tk (a_e E_e(x_t) + (1 - a_e) S(x_t)) + S(x_t)``.
@@ -196,6 +198,17 @@ def moe_forward(x: np.ndarray, router_w: np.ndarray, w_gate: np.ndarray, w_up: n
     if emulate_device and dtype != "fp32":
         y = round_to_dtype(y, dtype)
     return y, idx, wt, probs
+
+
+def lookahead(x: np.ndarray, w1: np.ndarray, w2: np.ndarray, num_experts: int, steps: int) -> np.ndarray:
+    """Lookahead router probabilities [N, K, E] (chronos/model/lookahead_router.py:36-55):
+    softmax over the experts of W2 . silu(W1 . x), per step, fp32."""
+    x = np.asarray(x, np.float32)
+    h1 = _silu((x @ np.asarray(w1, np.float32).T).astype(np.float32)).astype(np.float32)
+    lg = (h1 @ np.asarray(w2, np.float32).T).astype(np.float32).reshape(x.shape[0], steps, num_experts)
+    lg = lg - lg.max(axis=-1, keepdims=True)
+    e = np.exp(lg)
+    return (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)
 
 
 def rel_l2(a: np.ndarray, b: np.ndarray) -> float:

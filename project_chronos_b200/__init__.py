@@ -9,6 +9,8 @@ Public API (mirrors chronos/model/moe_chronos.py of FonaTech/Project_Chronos):
 * ``ExpertStore``, ``LRUCache`` (``expert_store``) and ``CacheManager``
   (``cache_manager``) — pooled expert residency with device ready flags
   (mirrors chronos/io/expert_store.py and chronos/runtime/cache_manager.py);
+* ``LookaheadRouter`` (``lookahead``) — the lookahead routing predictor
+  (chronos/model/lookahead_router.py) as one fused kernel;
 * ``synthetic`` — seeded workloads of the benchmark configurations.
 
 Importing the package does not load the CUDA library; the first layer call
@@ -17,6 +19,7 @@ does, and raises if it is missing.
 from .moe import ChronosMOEFeedForward, FeedForward, LazyExpertPlaceholder  # noqa: F401
 from .expert_store import ExpertStore, LRUCache  # noqa: F401
 from .cache_manager import CacheManager  # noqa: F401
+from .lookahead import LookaheadRouter  # noqa: F401
 
 __all__ = ["ChronosMOEFeedForward", "FeedForward", "LazyExpertPlaceholder", "ExpertStore", "LRUCache",
-           "CacheManager"]
+           "CacheManager", "LookaheadRouter"]

@@ -44,7 +44,7 @@ EXPORTS = ("chronos_moe_workspace_size", "chronos_moe_forward", "chronos_moe_rou
            "chronos_moe_profile_begin", "chronos_moe_profile_end",
            "chronos_moe_kernel_launches", "chronos_moe_forward_noalloc",
            "chronos_ep_dispatch", "chronos_ep_combine", "chronos_ep_dispatch_args_size",
-           "chronos_ep_combine_args_size")
+           "chronos_ep_combine_args_size", "chronos_lookahead_forward", "chronos_lookahead_args_size")
 
 EP_MAX_RANKS = 32  # CHRONOS_EP_MAX_RANKS
 
@@ -135,6 +135,22 @@ class ChronosEpCombineArgs(ctypes.Structure):
     ]
 
 
+class ChronosLookaheadArgs(ctypes.Structure):
+    """Mirror of include/chronos_lookahead.h ChronosLookaheadArgs."""
+    _fields_ = [
+        ("num_tokens", ctypes.c_int64),
+        ("hidden", ctypes.c_int32),
+        ("inner", ctypes.c_int32),
+        ("num_experts", ctypes.c_int32),
+        ("steps", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("x", ctypes.c_void_p),
+        ("w1", ctypes.c_void_p),
+        ("w2", ctypes.c_void_p),
+        ("probs", ctypes.c_void_p),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -186,6 +202,12 @@ def load_library(path: str = LIB_PATH):
         lib.chronos_ep_dispatch_args_size.restype = ctypes.c_size_t
         lib.chronos_ep_combine_args_size.argtypes = []
         lib.chronos_ep_combine_args_size.restype = ctypes.c_size_t
+        lib.chronos_lookahead_forward.argtypes = [ctypes.POINTER(ChronosLookaheadArgs), ctypes.c_void_p]
+        lib.chronos_lookahead_forward.restype = ctypes.c_int
+        lib.chronos_lookahead_args_size.argtypes = []
+        lib.chronos_lookahead_args_size.restype = ctypes.c_size_t
+        if lib.chronos_lookahead_args_size() != ctypes.sizeof(ChronosLookaheadArgs):
+            raise RuntimeError("lookahead args layout mismatch between the library and the binding")
         if (lib.chronos_ep_dispatch_args_size() != ctypes.sizeof(ChronosEpDispatchArgs)
                 or lib.chronos_ep_combine_args_size() != ctypes.sizeof(ChronosEpCombineArgs)):
             raise RuntimeError("expert-parallel args layout mismatch between the library and the binding")

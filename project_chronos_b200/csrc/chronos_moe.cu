@@ -19,9 +19,11 @@
 #include <vector>
 
 #include "chronos_ep.h"
+#include "chronos_lookahead.h"
 #include "chronos_moe.h"
 #include "common.cuh"
 #include "ep.cuh"
+#include "lookahead.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
 #include "plan.cuh"
@@ -993,3 +995,58 @@ extern "C" int chronos_ep_combine(const ChronosEpCombineArgs* a, void* stream) {
 
 extern "C" size_t chronos_ep_dispatch_args_size(void) { return sizeof(ChronosEpDispatchArgs); }
 extern "C" size_t chronos_ep_combine_args_size(void) { return sizeof(ChronosEpCombineArgs); }
+
+// ---------------------------------------------------------------------------
+// lookahead router (include/chronos_lookahead.h)
+// ---------------------------------------------------------------------------
+namespace chronos {
+namespace {
+
+template <typename T>
+int lookahead_impl(const ChronosLookaheadArgs* a, cudaStream_t st) {
+    LookaheadParams p{};
+    p.x = a->x;
+    p.w1 = a->w1;
+    p.w2 = a->w2;
+    p.probs = a->probs;
+    p.n = a->num_tokens;
+    p.h = a->hidden;
+    p.inner = a->inner;
+    p.e = a->num_experts;
+    p.k = a->steps;
+    if (p.n == 0) return CHRONOS_OK;
+    const int per_token = (p.h + p.inner + p.e * p.k) * 4;
+    p.tb = std::max(1, std::min(kLookaheadMaxTB, (160 << 10) / per_token));
+    const int smem = p.tb * per_token;
+    if (int rc = set_smem(lookahead_kernel<T>, smem)) return rc;
+    const unsigned blocks = static_cast<unsigned>((p.n + p.tb - 1) / p.tb);
+    CHRONOS_CUDA_CHECK(launch_kernel(lookahead_kernel<T>, dim3(blocks), dim3(kLookaheadThreads), smem, st,
+                                     false, p));
+    return CHRONOS_OK;
+}
+
+}  // namespace
+}  // namespace chronos
+
+extern "C" int chronos_lookahead_forward(const ChronosLookaheadArgs* a, void* stream) {
+    using namespace chronos;
+    if (a == nullptr) return fail(CHRONOS_ERR_INVALID_ARG, "args is NULL");
+    if (a->num_tokens < 0 || a->num_tokens > (int64_t(1) << 24))
+        return fail(CHRONOS_ERR_INVALID_ARG, "num_tokens %lld out of range", static_cast<long long>(a->num_tokens));
+    if (a->hidden < 1 || a->hidden > 8192 || a->inner < 1 || a->inner > 2048 || a->num_experts < 1 ||
+        a->steps < 1 || static_cast<int64_t>(a->num_experts) * a->steps > 4096)
+        return fail(CHRONOS_ERR_INVALID_ARG, "lookahead shape out of range (H %d, inner %d, E %d, K %d)",
+                    a->hidden, a->inner, a->num_experts, a->steps);
+    if (a->dtype != CHRONOS_DTYPE_BF16 && a->dtype != CHRONOS_DTYPE_FP16 && a->dtype != CHRONOS_DTYPE_FP32)
+        return fail(CHRONOS_ERR_INVALID_ARG, "dtype %d unknown", a->dtype);
+    if (a->num_tokens > 0 && (a->x == nullptr || a->w1 == nullptr || a->w2 == nullptr || a->probs == nullptr))
+        return fail(CHRONOS_ERR_INVALID_ARG, "x, w1, w2 and probs are required");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (a->dtype) {
+        case CHRONOS_DTYPE_BF16: return lookahead_impl<__nv_bfloat16>(a, st);
+        case CHRONOS_DTYPE_FP16: return lookahead_impl<__half>(a, st);
+        default: return lookahead_impl<float>(a, st);
+    }
+}
+
+extern "C" size_t chronos_lookahead_args_size(void) { return sizeof(ChronosLookaheadArgs); }

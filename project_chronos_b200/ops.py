@@ -346,6 +346,30 @@ def ep_combine(recv_y: torch.Tensor, pair_slot: torch.Tensor, top_k: int,
     return y
 
 
+def lookahead_forward(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, num_experts: int,
+                      steps: int) -> torch.Tensor:
+    """Lookahead router (include/chronos_lookahead.h): x [N, H], w1 [H/4, H],
+    w2 [E*K, H/4] -> probs [N, K, E] in x's dtype."""
+    _check_cuda(x, w1, w2)
+    x = x.contiguous()
+    n, h = x.shape
+    for name, t in (("w1", w1), ("w2", w2)):
+        if t.dtype != x.dtype:
+            raise TypeError(f"{name} dtype {t.dtype} != x dtype {x.dtype}")
+    if x.dtype not in _DTYPES:
+        raise TypeError(f"unsupported dtype {x.dtype}")
+    w1, w2 = w1.contiguous(), w2.contiguous()
+    probs = torch.empty(n, steps, num_experts, dtype=x.dtype, device=x.device)
+    args = N.ChronosLookaheadArgs(num_tokens=n, hidden=h, inner=w1.shape[0], num_experts=int(num_experts),
+                                  steps=int(steps), dtype=_DTYPES[x.dtype], x=_ptr(x), w1=_ptr(w1),
+                                  w2=_ptr(w2), probs=_ptr(probs))
+    lib = N.load_library()
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    with torch.cuda.device(x.device):
+        N.check(lib.chronos_lookahead_forward(ctypes.byref(args), ctypes.c_void_p(stream)))
+    return probs
+
+
 def profile_begin(max_calls: int) -> None:
     """Record per-stage CUDA events for the next ``max_calls`` layer calls (this thread)."""
     lib = N.load_library()
