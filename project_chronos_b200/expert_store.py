@@ -28,12 +28,14 @@ kernels:
   ``FeedForward`` (whose weights are views of its slot), so residency checks
   written against the reference's modules keep working.
 
-Disk format: the reference's legacy layout, one ``expert_l{L}_e{E}.pt`` per
+Disk formats (both the reference's): the clustered ``.ctsr`` layout
+(``chronos/io/storage.py``, here ``cluster_storage.py``: a whole cluster read
+with one sequential read into one pinned buffer) when the config's
+``storage_format`` is ``"safetensors"`` (the reference's default) and a
+manifest is present, else the legacy layout, one ``expert_l{L}_e{E}.pt`` per
 (layer, expert) holding fp16 ``{gate,up,down}_proj.weight``
-(``expert_store.py:233-243, 321-322``).  The clustered ``.ctsr`` layout
-(``chronos/io/storage.py``) is not part of this package; a store configured
-for it writes and reads the legacy files.  The warm tier holds pinned tensors
-already in the pool dtype so that promotion is a plain copy.
+(``expert_store.py:233-243, 321-322``).  The warm tier holds pinned tensors in
+the pool dtype so that promotion is a plain copy.
 """
 from __future__ import annotations
 
@@ -46,6 +48,8 @@ from typing import Dict, List, Optional
 import numpy as np
 import torch
 import torch.nn as nn
+
+from .cluster_storage import ClusterStorage
 
 _WEIGHTS = (("gate_proj.weight", "gate"), ("up_proj.weight", "up"), ("down_proj.weight", "down"))
 
@@ -151,9 +155,10 @@ class ExpertStore:
         self._offloaded = False
         self._pending_events: Dict[int, "torch.cuda.Event"] = {}
         self._events_lock = threading.Lock()
-        # the clustered .ctsr layout is not provided: every store uses the .pt files
-        self.storage_format = "pt"
-        self._cluster_storage = None
+        self.storage_format = getattr(config, "storage_format", "safetensors")
+        self._cluster_storage: Optional[ClusterStorage] = None
+        if self.storage_format == "safetensors" and ClusterStorage.has_manifest(ssd_dir):
+            self._cluster_storage = ClusterStorage(ssd_dir)
 
         # device slot pools, created when the routed experts become placeholders
         self._pools: Optional[List[Dict[str, torch.Tensor]]] = None
@@ -262,8 +267,12 @@ class ExpertStore:
     def offload_from_state_dict(self, state_dict: Dict[str, torch.Tensor],
                                 clusters: Optional[List[List[int]]] = None,
                                 replace_live: bool = True):
-        """Write the cold tier straight from a checkpoint (``expert_store.py:245-274``)."""
-        del clusters  # one file per (layer, expert); no cluster layout
+        """Write the cold tier straight from a checkpoint (``expert_store.py:245-274``):
+        one ``.pt`` file per (layer, expert), as the reference does (a raw checkpoint
+        has no co-activation clusters)."""
+        if self.storage_format == "safetensors" and clusters is None:
+            self.storage_format = "pt"
+            self._cluster_storage = None
         for li in range(self.num_layers):
             for ei in range(self.num_experts):
                 path = self._ssd_path(ei, li)
@@ -276,8 +285,17 @@ class ExpertStore:
             self.replace_live_experts_with_placeholders()
 
     def offload_all_to_ssd(self, clusters: Optional[List[List[int]]] = None):
-        """Write every live expert of every layer to its ``.pt`` file."""
-        del clusters
+        """Write every live expert of every layer: ``.ctsr`` clusters + manifest when
+        ``storage_format`` is ``"safetensors"`` (one all-expert cluster when
+        ``clusters`` is None), else one ``.pt`` file per (layer, expert)
+        (``expert_store.py:326-364``)."""
+        if self.storage_format == "safetensors":
+            if clusters is None:
+                clusters = [list(range(self.num_experts))]
+            ClusterStorage.write_clusters(self.moe_layers, clusters, self.ssd_dir, self.num_layers,
+                                          self.num_experts)
+            self._cluster_storage = ClusterStorage(self.ssd_dir)
+            return
         for li, moe in enumerate(self.moe_layers):
             for ei, expert in enumerate(moe.experts):
                 path = self._ssd_path(ei, li)
@@ -314,7 +332,7 @@ class ExpertStore:
             out[li] = {}
             for k, v in state.items():
                 t = v.to(dtype=dt).contiguous()
-                if self._cuda:
+                if self._cuda and not t.is_pinned():
                     try:
                         t = t.pin_memory()
                     except RuntimeError:
@@ -322,8 +340,21 @@ class ExpertStore:
                 out[li][k] = t
         return out
 
+    def attach_cluster_manifest(self, manifest_dir: Optional[str] = None) -> bool:
+        """Use the ``.ctsr`` clusters under ``manifest_dir`` (default: the cache dir)."""
+        root = manifest_dir or self.ssd_dir
+        if not ClusterStorage.has_manifest(root):
+            return False
+        self._cluster_storage = ClusterStorage(root)
+        self.storage_format = "safetensors"
+        return True
+
     def prefetch_to_ram(self, expert_ids: List[int]):
-        """Cold -> warm for each id not already warm (``expert_store.py:389-463``)."""
+        """Cold -> warm for each id not already warm (``expert_store.py:389-463``).
+        With clusters, a request loads its whole cluster (one read per cluster)."""
+        if self._cluster_storage is not None:
+            self._prefetch_clustered(expert_ids or [])
+            return
         for eid in expert_ids or []:
             eid = int(eid)
             if self.ram_lru.contains(eid):
@@ -339,6 +370,33 @@ class ExpertStore:
                 if evicted is not None:
                     self._ram_buffers.pop(evicted, None)
                 self._ram_buffers[eid] = pinned
+
+    def _prefetch_clustered(self, expert_ids: List[int]) -> None:
+        cs = self._cluster_storage
+        to_load: List[int] = []
+        for eid in expert_ids:
+            eid = int(eid)
+            if eid not in cs.manifest.expert_to_cluster:
+                continue
+            if self.ram_lru.contains(eid):
+                self.ram_lru.touch(eid)
+                continue
+            cid = cs.cluster_for_expert(eid)
+            if cid not in to_load:
+                to_load.append(cid)
+        for cid in to_load:
+            nested = cs.load_cluster(cid)
+            self.ram_lru.capacity = self._safe_ram_capacity()
+            for eid, layer_states in nested.items():
+                if self.ram_lru.contains(eid):
+                    self.ram_lru.touch(eid)
+                    continue
+                pinned = self._pin_layer_states(layer_states)
+                with self._ram_lock:
+                    evicted = self.ram_lru.put(eid)
+                    if evicted is not None:
+                        self._ram_buffers.pop(evicted, None)
+                    self._ram_buffers[eid] = pinned
 
     # ------------------------------------------------------------------ hot tier
     def promote_to_vram(self, expert_id: int, blocking: bool = False) -> bool:
@@ -493,8 +551,9 @@ class ExpertStore:
             "pinned_ram_fraction": round(pinned_used_gb / max(available_ram_gb, 1), 4),
             "h2d_stream": "dedicated" if self._h2d_stream is not None else "default",
             "storage_format": self.storage_format,
-            "cluster_aware": False,
-            "num_clusters": 0,
+            "cluster_aware": self._cluster_storage is not None,
+            "num_clusters": (len(self._cluster_storage.manifest.clusters)
+                             if self._cluster_storage is not None else 0),
             "pool_slots": int(self._pools[0]["gate"].shape[0]) if self._pools else 0,
             "device_ready_flags": bool(self._cuda and self.device_ready_flags),
         }

@@ -185,3 +185,57 @@ def test_module_attached_pool_bookkeeping(tmp_path):
     with pytest.raises(RuntimeError, match="CUDA"):
         moe(torch.zeros(1, 1, cfg.hidden_size))
     np.testing.assert_array_equal(store.slot_of_expert(), [-1, 0, -1, -1])
+
+
+# --------------------------------------------------------------------------
+# clustered .ctsr cold tier (chronos/io/storage.py)
+# --------------------------------------------------------------------------
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_tensor_file_format_is_safetensors(tmp_path, dtype):
+    """Our writer and reader against the safetensors package, both directions."""
+    st = pytest.importorskip("safetensors.torch")
+    from project_chronos_b200.cluster_storage import read_tensor_file, write_tensor_file
+    g = torch.Generator().manual_seed(0)
+    tensors = {"l0_e1__gate_proj.weight": torch.randn(6, 5, generator=g).to(dtype),
+               "l1_e0__down_proj.weight": torch.randn(3, 7, generator=g).to(dtype),
+               "l0_e0__up_proj.weight": torch.randn(1, 2, generator=g).to(dtype)}
+    ours = str(tmp_path / "ours.ctsr")
+    write_tensor_file(ours, tensors)
+    back = st.load_file(ours)
+    assert set(back) == set(tensors) and all(torch.equal(back[k], tensors[k]) for k in tensors)
+    theirs = str(tmp_path / "theirs.ctsr")
+    st.save_file(tensors, theirs)
+    got = read_tensor_file(theirs, pin=False)
+    assert set(got) == set(tensors) and all(torch.equal(got[k], tensors[k]) for k in tensors)
+
+
+def test_cluster_cold_tier_round_trip(tmp_path):
+    from project_chronos_b200 import ExpertStore, LazyExpertPlaceholder
+    from project_chronos_b200.cluster_storage import MANIFEST_FILENAME, ClusterStorage
+    torch.manual_seed(4)
+    cfg = _cfg(E=4)
+    cfg.storage_format = "safetensors"
+    model = _Model(cfg, layers=2)
+    with torch.no_grad():  # fp16-representable weights: the cold tier stores fp16
+        for p in model.parameters():
+            p.copy_(p.half().float())
+    want = {k: v.clone() for k, v in model.model.state_dict().items()}
+    store = ExpertStore(model, cfg, ssd_dir=str(tmp_path / "cl"))
+    store.offload_all_to_ssd(clusters=[[0, 2], [1, 3]])
+    assert (tmp_path / "cl" / MANIFEST_FILENAME).exists()
+    assert (tmp_path / "cl" / "cluster_1.ctsr").exists()
+    cs = ClusterStorage(str(tmp_path / "cl"))
+    nested = cs.load_cluster(1, pin=False)
+    assert sorted(nested) == [1, 3] and sorted(nested[3]) == [0, 1]
+    assert torch.equal(nested[3][1]["up_proj.weight"].float(), want["layers.1.mlp.experts.3.up_proj.weight"])
+    store.replace_live_experts_with_placeholders()
+    assert isinstance(store.moe_layers[0].experts[2], LazyExpertPlaceholder)
+    store.prefetch_to_ram([2])                        # loads cluster 0: experts 0 and 2
+    assert store.ram_lru.contains(0) and store.ram_lru.contains(2) and not store.ram_lru.contains(1)
+    assert store.promote_to_vram(3) is True           # cluster 1 read on demand
+    for li in range(2):
+        got = store.moe_layers[li].experts[3].down_proj.weight
+        assert torch.equal(got, want[f"layers.{li}.mlp.experts.3.down_proj.weight"])
+    s = store.stats()
+    assert s["cluster_aware"] is True and s["num_clusters"] == 2 and s["storage_format"] == "safetensors"
