@@ -183,3 +183,24 @@ def test_event_wait_mode_without_flags(tmp_path):
         y_full = full.model.layers[0].mlp(x)
     torch.cuda.synchronize()
     assert _rel(y_lazy, y_full) <= 1e-2
+
+
+def test_cluster_cold_tier_promotes_from_pinned_views(tmp_path):
+    """.ctsr clusters: one pinned buffer per cluster, promotion copies straight from it."""
+    from project_chronos_b200 import CacheManager
+    cfg = _cfg(budget_experts=8)
+    cfg.storage_format = "safetensors"
+    full, lazy, state = _pair(cfg, 1, torch.bfloat16, seed=4)
+    mgr = CacheManager(lazy, cfg, ssd_dir=str(tmp_path / "g"))
+    store = mgr.expert_store
+    store.offload_all_to_ssd(clusters=[[0, 1, 2, 3], [4, 5, 6, 7]])
+    store.replace_live_experts_with_placeholders()
+    x = torch.randn(1, 3, cfg.hidden_size, device=DEV, dtype=torch.bfloat16)
+    need = _selected(full.model.layers[0].mlp, x)
+    with torch.no_grad():
+        mgr.ensure_resident(need)
+        y_lazy = lazy.model.layers[0].mlp(x, available_expert_mask=mgr.availability_mask())
+        y_full = full.model.layers[0].mlp(x)
+    torch.cuda.synchronize()
+    assert store.stats()["cluster_aware"] is True
+    assert _rel(y_lazy, y_full) <= 1e-2
