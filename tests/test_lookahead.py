@@ -64,8 +64,9 @@ def test_kernel_matches_oracle(dtype, tol, H, E, steps, n):
     xd = x.to("cuda", dtype)
     with torch.no_grad():
         got = m(xd).float().cpu().numpy()
-    want = O.lookahead(xd.float().cpu().view(n, H).numpy(), m.proj[0].weight.float().cpu().numpy(),
-                       m.proj[2].weight.float().cpu().numpy(), E, steps + 1).reshape(1, n, steps + 1, E)
+    w1 = m.proj[0].weight.detach().float().cpu().numpy()
+    w2 = m.proj[2].weight.detach().float().cpu().numpy()
+    want = O.lookahead(xd.float().cpu().view(n, H).numpy(), w1, w2, E, steps + 1).reshape(1, n, steps + 1, E)
     assert got.shape == want.shape
     assert np.abs(got - want).max() <= tol
     assert np.allclose(got.sum(-1), 1.0, atol=tol * 4)
