@@ -245,12 +245,25 @@ __global__ void __launch_bounds__(kSelectPlanThreads)
     __shared__ int s_scratch[kSelectPlanWarps];
     __shared__ int s_tot[4];
     __shared__ int s_last;
+    // one block (<= 8 tokens): group counts by shared-memory atomics and the
+    // per-(token, choice) results kept in shared memory, no ticket or re-reads
+    constexpr int kPairs = kSelectPlanWarps * kMaxTopK;
+    __shared__ int s_cnt[kMaxExperts];
+    __shared__ int s_pe[kPairs];
+    __shared__ int s_pp[kPairs];
+    __shared__ float s_pc[kPairs];
+    __shared__ float s_sc[kSelectPlanWarps];
+    const bool single = gridDim.x == 1;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t gtid = static_cast<int64_t>(blockIdx.x) * kSelectPlanThreads + tid;
     const int64_t gthreads = static_cast<int64_t>(gridDim.x) * kSelectPlanThreads;
     pdl_trigger();
     if (sp.slot_map != nullptr)
         for (int64_t i = gtid; i < static_cast<int64_t>(sp.e) * sp.n; i += gthreads) sp.slot_map[i] = -1;
+    if (single) {
+        for (int i = tid; i < kMaxExperts; i += kSelectPlanThreads) s_cnt[i] = 0;
+        __syncthreads();
+    }
     pdl_wait();  // chunk partials and zeroed counters from the logit kernel
 
     // 1) one warp per token: select, position within the expert group
@@ -264,22 +277,37 @@ __global__ void __launch_bounds__(kSelectPlanThreads)
         int mine_e;
         float mine_w, mine_a, shared_extra;
         select_token<T, EPL>(rp, t, lane, mine_e, mine_w, mine_a, shared_extra);
-        if (lane < k) rp.pos[t * k + lane] = mine_a > 0.0f ? atomicAdd(&rp.grp_count[mine_e], 1) : -1;
-        if (lane == 0 && rp.num_shared > 0)
-            rp.shared_coef[t] = (1.0f + shared_extra) / static_cast<float>(rp.num_shared);
+        if (lane < k) {
+            const int ps = mine_a > 0.0f ? atomicAdd(single ? &s_cnt[mine_e] : &rp.grp_count[mine_e], 1) : -1;
+            rp.pos[t * k + lane] = ps;
+            if (single) {
+                s_pe[warp * k + lane] = mine_e;
+                s_pp[warp * k + lane] = ps;
+                s_pc[warp * k + lane] = mine_w * mine_a;
+            }
+        }
+        const float sc = (1.0f + shared_extra) / static_cast<float>(rp.num_shared > 0 ? rp.num_shared : 1);
+        if (lane == 0 && rp.num_shared > 0) {
+            rp.shared_coef[t] = sc;
+            if (single) s_sc[warp] = sc;
+        }
         zero_direct_row<T>(rp, t, lane, mine_a);
     }
 
-    // 2) the last block to arrive sees every block's counts and tables
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = atomicAdd(ticket, 1) == static_cast<int>(gridDim.x) - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
+    // 2) several blocks: the last to arrive sees every block's counts and tables
+    if (single) {
+        __syncthreads();
+    } else {
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) s_last = atomicAdd(ticket, 1) == static_cast<int>(gridDim.x) - 1;
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+    }
 
     // 3) plan: group offsets and the GEMM work tables
-    const int cnt = tid < pp.e ? __ldcg(rp.grp_count + tid) : 0;
+    const int cnt = tid < pp.e ? (single ? s_cnt[tid] : __ldcg(rp.grp_count + tid)) : 0;
     const int inc = block_inclusive_scan<kSelectPlanThreads>(cnt, s_scratch);
     if (tid < pp.e) s_off[tid] = inc - cnt;
     plan_tables<kSelectPlanThreads>(pp, cnt, inc, s_scratch, s_tot);
@@ -290,11 +318,11 @@ __global__ void __launch_bounds__(kSelectPlanThreads)
     for (int64_t i = tid; i < total; i += kSelectPlanThreads) {
         const int64_t tt = i / k;
         const int j = static_cast<int>(i % k);
-        const int ps = __ldcg(rp.pos + i);
-        const int e = __ldcg(rp.topk_idx + i);
-        const float c = __ldcg(rp.sel_coef + i);
+        const int ps = single ? s_pp[i] : __ldcg(rp.pos + i);
+        const int e = single ? s_pe[i] : __ldcg(rp.topk_idx + i);
+        const float c = single ? s_pc[i] : __ldcg(rp.sel_coef + i);
         if (j == 0 && sp.num_shared > 0) {
-            const float sc = __ldcg(rp.shared_coef + tt);
+            const float sc = single ? s_sc[tt] : __ldcg(rp.shared_coef + tt);
             for (int q = 0; q < sp.num_shared; ++q) {
                 const int64_t slot = sp.n * k + q * sp.n + tt;
                 sp.slot_tok[slot] = static_cast<int32_t>(tt);
