@@ -345,7 +345,7 @@ int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool p
             CHRONOS_CUDA_CHECK(launch_kernel(route_partials_kernel<T>, grid, dim3(kPartialThreads), 0, st,
                                              false, rp));
         } else {
-            const dim3 grid(static_cast<unsigned>((N + kRouteTile - 1) / kRouteTile),
+            const dim3 grid(static_cast<unsigned>((N + kTiledTokens - 1) / kTiledTokens),
                             static_cast<unsigned>((s.num_experts + kRouteTile - 1) / kRouteTile),
                             static_cast<unsigned>((rp.nchunks + kTiledChunks - 1) / kTiledChunks));
             CHRONOS_CUDA_CHECK(launch_kernel(route_tiled_kernel<T>, grid, dim3(kTiledThreads), 0, st,

@@ -11,7 +11,7 @@
 //   route_partials_kernel  small batches: one thread per (expert, chunk, group
 //                          of 8 tokens) (parallel over chunks, so a decode
 //                          token's 64 logits are not 2048-long serial chains);
-//   route_tiled_kernel     large batches: 64-token x 64-expert register-tiled
+//   route_tiled_kernel     large batches: 128-token x 64-expert register-tiled
 //                          SIMT GEMM, each block over 4 chunks (512 h) of K
 //                          (the K split gives the grid enough blocks to fill
 //                          every SM; the in-order fold stays in the select).
@@ -29,8 +29,7 @@ namespace chronos {
 constexpr int kRouteChunk = 128;       // h per partial (the contract's chunk)
 constexpr int kRouteGroup = 8;         // tokens per thread in the partials kernel
 constexpr int kRouteSmallMax = 256;    // largest batch routed by the partials kernel
-constexpr int kRouteTile = 64;         // tokens and experts per tiled block
-constexpr int kRouteTileK = 32;        // h per smem stage of the tiled kernel
+constexpr int kRouteTile = 64;         // experts per tiled block
 constexpr int kMaxTopK = 16;
 constexpr int kMaxExperts = 256;
 
@@ -199,51 +198,55 @@ __global__ void __launch_bounds__(kPartialThreads) route_partials_kernel(RoutePa
 // large batches: register-tiled SIMT GEMM, chunk partials folded in order
 // ---------------------------------------------------------------------------
 constexpr int kTiledThreads = 256;
-constexpr int kTilePad = kRouteTileK + 4;
-constexpr int kTiledChunks = 4;  // chunks of K per block (blockIdx.z)
+constexpr int kTiledTokens = 128;  // tokens per block (8 per thread)
+constexpr int kTiledK = 16;        // h per shared-memory stage
+constexpr int kTiledPad = kTiledK + 4;
+constexpr int kTiledChunks = 4;    // chunks of K per block (blockIdx.z)
 
+// Block = 128 tokens x 64 experts x 4 chunks of K; thread = 8 tokens x 4
+// experts (experts eg + 16 j), one fmaf chain per (token, expert, chunk) in
+// increasing h; at each chunk end the partial is written and the chain restarts.
 template <typename T>
-__global__ void __launch_bounds__(kTiledThreads) route_tiled_kernel(RouteParams p) {
-    __shared__ __align__(16) float xs[2][kRouteTile][kTilePad];
-    __shared__ __align__(16) float ws[2][kRouteTile][kTilePad];
+__global__ void __launch_bounds__(kTiledThreads, 2) route_tiled_kernel(RouteParams p) {
+    __shared__ __align__(16) float xs[2][kTiledTokens][kTiledPad];
+    __shared__ __align__(16) float ws[2][kRouteTile][kTiledPad];
     pdl_trigger();
     if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) zero_route_counters(p);
     const int tid = threadIdx.x;
-    const int tg = tid >> 4;  // tokens tg*4 .. tg*4+3
+    const int tg = tid >> 4;  // tokens tg*8 .. tg*8+7
     const int eg = tid & 15;  // experts eg + 16 j
     const int H = p.h, E = p.e;
-    const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kRouteTile;
+    const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kTiledTokens;
     const int e0 = blockIdx.y * kRouteTile;
     const T* x = static_cast<const T*>(p.x);
     const T* w = static_cast<const T*>(p.w);
-    // loader: row lr, 8 consecutive k at lk
-    const int lr = tid >> 2, lk = (tid & 3) * 8;
-    const bool xrow_ok = t0 + lr < p.n;
-    const bool wrow_ok = e0 + lr < E;
-    const T* xrow = x + (t0 + lr) * H;
-    const T* wrow = w + static_cast<int64_t>(e0 + lr) * H;
-    float4 xa, xb, wa, wb;
+    // loaders: x row xr, 8 consecutive h at xk; w row wr, 4 consecutive h at wk
+    const int xr = tid >> 1, xk = (tid & 1) * 8;
+    const int wr = tid >> 2, wk = (tid & 3) * 4;
+    const bool xrow_ok = t0 + xr < p.n;
+    const bool wrow_ok = e0 + wr < E;
+    const T* xrow = x + (t0 + xr) * H;
+    const T* wrow = w + static_cast<int64_t>(e0 + wr) * H;
+    float4 xa, xb, wa;
     auto gload = [&](int kt) {
-        const int h = kt * kRouteTileK + lk;
+        const int h = kt * kTiledK;
         const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-        xa = (xrow_ok && h < H) ? load4<T>(xrow + h) : z;
-        xb = (xrow_ok && h + 4 < H) ? load4<T>(xrow + h + 4) : z;
-        wa = (wrow_ok && h < H) ? load4<T>(wrow + h) : z;
-        wb = (wrow_ok && h + 4 < H) ? load4<T>(wrow + h + 4) : z;
+        xa = (xrow_ok && h + xk < H) ? load4<T>(xrow + h + xk) : z;
+        xb = (xrow_ok && h + xk + 4 < H) ? load4<T>(xrow + h + xk + 4) : z;
+        wa = (wrow_ok && h + wk < H) ? load4<T>(wrow + h + wk) : z;
     };
     auto sstore = [&](int buf) {
-        *reinterpret_cast<float4*>(&xs[buf][lr][lk]) = xa;
-        *reinterpret_cast<float4*>(&xs[buf][lr][lk + 4]) = xb;
-        *reinterpret_cast<float4*>(&ws[buf][lr][lk]) = wa;
-        *reinterpret_cast<float4*>(&ws[buf][lr][lk + 4]) = wb;
+        *reinterpret_cast<float4*>(&xs[buf][xr][xk]) = xa;
+        *reinterpret_cast<float4*>(&xs[buf][xr][xk + 4]) = xb;
+        *reinterpret_cast<float4*>(&ws[buf][wr][wk]) = wa;
     };
-    float acc[4][4];
+    float acc[8][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-    const int KT = (H + kRouteTileK - 1) / kRouteTileK;
-    constexpr int kTilesPerChunk = kRouteChunk / kRouteTileK;
+    const int KT = (H + kTiledK - 1) / kTiledK;
+    constexpr int kTilesPerChunk = kRouteChunk / kTiledK;
     const int kt_begin = blockIdx.z * kTiledChunks * kTilesPerChunk;
     const int kt_end = min(KT, kt_begin + kTiledChunks * kTilesPerChunk);
     gload(kt_begin);
@@ -253,14 +256,14 @@ __global__ void __launch_bounds__(kTiledThreads) route_tiled_kernel(RouteParams 
         const int buf = (kt - kt_begin) & 1;
         if (kt + 1 < kt_end) gload(kt + 1);
 #pragma unroll
-        for (int kk = 0; kk < kRouteTileK; kk += 4) {
-            float4 a[4], b[4];
+        for (int kk = 0; kk < kTiledK; kk += 4) {
+            float4 a[8], b[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) a[i] = *reinterpret_cast<const float4*>(&xs[buf][tg * 4 + i][kk]);
+            for (int i = 0; i < 8; ++i) a[i] = *reinterpret_cast<const float4*>(&xs[buf][tg * 8 + i][kk]);
 #pragma unroll
             for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(&ws[buf][eg + 16 * j][kk]);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < 8; ++i)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     acc[i][j] = fmaf(a[i].x, b[j].x, acc[i][j]);
@@ -273,8 +276,8 @@ __global__ void __launch_bounds__(kTiledThreads) route_tiled_kernel(RouteParams 
             // chunk finished: its partials, experts contiguous across the threads
             float* out = p.partials + static_cast<int64_t>(kt / kTilesPerChunk) * p.n * E;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int64_t t = t0 + tg * 4 + i;
+            for (int i = 0; i < 8; ++i) {
+                const int64_t t = t0 + tg * 8 + i;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int e = e0 + eg + 16 * j;
