@@ -196,7 +196,7 @@ CHRONOS_API size_t chronos_moe_args_size(void);
 #define CHRONOS_STAGE_PLAN 1
 #define CHRONOS_STAGE_SCATTER 2
 #define CHRONOS_STAGE_GATEUP 3
-#define CHRONOS_STAGE_ACT 4
+#define CHRONOS_STAGE_ACT 4 /* no kernel: SiLU-mul runs in the gate/up epilogue */
 #define CHRONOS_STAGE_DOWN 5
 #define CHRONOS_STAGE_FINALIZE 6
 #define CHRONOS_NUM_STAGES 7
