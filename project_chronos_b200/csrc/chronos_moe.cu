@@ -462,7 +462,14 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     pg.w_rows = static_cast<int>(F);
     pg.out_cols = static_cast<int>(F);
     prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
-    if ((rc = launch_tc<T, BN, true, kDense>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st))) return rc;
+    if constexpr (BN == kTmTokens) {
+        // large batches: token-major tiles (one N = 256 MMA for gate and up)
+        if ((rc = set_smem(tc_gateup_tm<T>, kTmSmemBytes))) return rc;
+        CHRONOS_CUDA_CHECK(launch_kernel(tc_gateup_tm<T>, dim3(grid), dim3(kTcThreads), kTmSmemBytes, st, true,
+                                         g_r, u_r, g_s, u_s, xp_m, x_m, pg));
+    } else if ((rc = launch_tc<T, BN, true, kDense>(g_r, u_r, g_s, u_s, xp_m, x_m, pg, grid, st))) {
+        return rc;
+    }
     prof_ran(slot, CHRONOS_STAGE_GATEUP);
     prof_mark(slot, CHRONOS_STAGE_ACT, st);  // SiLU-mul is fused into the gate/up epilogue
     prof_mark(slot, CHRONOS_STAGE_DOWN, st);

@@ -446,4 +446,233 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
+
+// ---------------------------------------------------------------------------
+// Token-major gate/up for large batches.  A = 128 token rows of the group
+// (M = 128), B = the group's 128 gate rows followed by its 128 up rows (one
+// 256-row K-major operand), one MMA of M = 128, N = 256 per 16 k: the token
+// tile is read from shared memory once per k-step for both projections (the
+// weight-major form reads it twice), 3/4 of the operand bytes per FLOP.  The
+// accumulator row is a token: columns [0, 128) gate, [128, 256) up; the
+// epilogue writes each token's h = silu(g) * u segment with one bulk store.
+// ---------------------------------------------------------------------------
+constexpr int kTmTokens = 128;
+constexpr int kTmABytes = kTmTokens * kTcBK * 2;                  // 16 KB
+constexpr int kTmStageBytes = kTmABytes + 2 * kTcBM * kTcBK * 2;  // + 32 KB
+constexpr int kTmHalf = 64;                                       // f columns per epilogue pass
+constexpr int kTmRowBytes = kTmHalf * 2 + 16;                     // padded: conflict-free rows
+constexpr int kTmStagingBytes = kTmTokens * kTmRowBytes;
+constexpr int kTmStages = (232448 - 1024 - 256 - kTmStagingBytes) / kTmStageBytes > 8
+                              ? 8
+                              : (232448 - 1024 - 256 - kTmStagingBytes) / kTmStageBytes;
+constexpr int kTmSmemBytes = 1024 + kTmStages * kTmStageBytes + kTmStagingBytes + 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gateup_tm(const __grid_constant__ CUtensorMap tm_gr,   // routed gate [P*F, H]
+                 const __grid_constant__ CUtensorMap tm_ur,   // routed up
+                 const __grid_constant__ CUtensorMap tm_gs,   // shared gate [S*F, H]
+                 const __grid_constant__ CUtensorMap tm_us,   // shared up
+                 const __grid_constant__ CUtensorMap tm_xr,   // expert-ordered token rows (Xp)
+                 const __grid_constant__ CUtensorMap tm_xs,   // token rows of x (shared groups)
+                 TcGemmParams p) {
+    constexpr int STAGES = kTmStages;
+    constexpr int ACC_COLS = 2 * kTcBM;  // gate | up
+    constexpr int TMEM_COLS = 512;
+    static_assert(STAGES >= 2, "shared memory holds fewer than two pipeline stages");
+    static_assert(kTmSmemBytes <= 232448, "shared memory over the per-CTA limit");
+
+    extern __shared__ uint8_t tc_smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* staging = smem + STAGES * kTmStageBytes;  // [128 tokens][kTmRowBytes]
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + kTmStagingBytes);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    pdl_trigger();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 128);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tm_gr);
+        prefetch_tmap(&tm_xr);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_holder, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    pdl_wait();
+    const int num_active = p.hdr->num_active;
+    const int total = p.hdr->units_gu;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------ TMA producer ------------------------------
+            int stage = 0;
+            uint32_t phase = 0;
+            int polled_eid = -1;
+            for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
+                const TcUnit w = tc_decode(p, num_active, u, kTmTokens, 0);
+                const int eid = p.act_eid[w.a];
+                const bool shared = eid < 0;
+                if (!shared && p.ready_flags != nullptr && eid != polled_eid) {
+                    const uint64_t t0 = globaltimer_ns();
+                    bool ok = true;
+                    while (ld_acquire_gpu(p.ready_flags + eid) < p.ready_epoch) {
+                        if (globaltimer_ns() - t0 > p.ready_limit_ns) { ok = false; break; }
+                        __nanosleep(256);
+                    }
+                    if (!ok) report_status(p.status, CHRONOS_ERR_EXPERT_NOT_READY);
+                    fence_proxy_async_global();
+                    polled_eid = eid;
+                }
+                const int w_row = p.act_wslot[w.a] * p.w_rows + w.mtile * kTcBM;
+                const int x_row = p.act_xrow[w.a] + w.tok_tile * kTmTokens;
+                const CUtensorMap* mg = shared ? &tm_gs : &tm_gr;
+                const CUtensorMap* mu = shared ? &tm_us : &tm_ur;
+                const CUtensorMap* mx = shared ? &tm_xs : &tm_xr;
+                for (int kt = 0; kt < p.k_tiles; ++kt) {
+                    if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, kPipelineLimitNs, abort_flag)) {
+                        *abort_flag = 1;
+                        report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                        break;
+                    }
+                    uint8_t* sb = smem + stage * kTmStageBytes;
+                    mbar_arrive_expect_tx(&full[stage], kTmStageBytes);
+                    tma_load_2d(sb, mx, &full[stage], kt * kTcBK, x_row);
+                    tma_load_2d(sb + kTmABytes, mg, &full[stage], kt * kTcBK, w_row);
+                    tma_load_2d(sb + kTmABytes + kTcBM * kTcBK * 2, mu, &full[stage], kt * kTcBK, w_row);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------ MMA issuer ------------------------------
+            constexpr uint32_t IDESC = idesc_f16(kTmTokens, ACC_COLS, AbFormat<T>::value);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
+                if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, kPipelineLimitNs, abort_flag)) {
+                    *abort_flag = 1;
+                    report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + static_cast<uint32_t>(acc * ACC_COLS);
+                bool failed = false;
+                for (int kt = 0; kt < p.k_tiles; ++kt) {
+                    if (!mbar_wait_bounded(&full[stage], phase, kPipelineLimitNs, abort_flag)) {
+                        *abort_flag = 1;
+                        report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                        failed = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sx = smem_u32(smem + stage * kTmStageBytes);
+                    const uint32_t sw = sx + kTmABytes;
+#pragma unroll
+                    for (int kk = 0; kk < kTcBK / 16; ++kk) {
+                        const uint32_t accum = (kt > 0 || kk > 0) ? 1u : 0u;
+                        umma_f16(d, sdesc_k_sw128(sx + kk * 32), sdesc_k_sw128(sw + kk * 32), IDESC, accum);
+                    }
+                    umma_commit(&empty[stage]);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+                if (failed) break;
+                umma_commit(&tfull[acc]);
+                if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+            }
+        }
+    } else {
+        // ------------------------------ epilogue ------------------------------
+        // thread = one token row of the tile (TMEM lane), two passes of 64 f each
+        const int q = warp & 3;
+        const int row_in_tile = q * 32 + lane;
+        const int et = threadIdx.x - 64;
+        volatile int* ep_ok = abort_flag + 1;
+        uint8_t* my_row = staging + row_in_tile * kTmRowBytes;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int u = blockIdx.x; u < total; u += gridDim.x) {
+            const TcUnit w = tc_decode(p, num_active, u, kTmTokens, 0);
+            const int rows = p.act_rows[w.a];
+            const int64_t hrow0 = p.act_hrow[w.a];
+            const int tok = w.tok_tile * kTmTokens + row_in_tile;
+            const int m0 = w.mtile * kTcBM;
+            const int ncols = min(kTcBM, p.out_cols - m0);
+            if (et == 0) {
+                const bool ok = mbar_wait_bounded(&tfull[acc], acc_phase, kPipelineLimitNs, abort_flag);
+                if (!ok) {
+                    *abort_flag = 1;
+                    report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                }
+                *ep_ok = ok ? 1 : 0;
+            }
+            bulk_wait_read();  // the previous unit's stores are done reading the staging rows
+            epilogue_bar_sync(128);
+            if (!*ep_ok) break;
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(acc * ACC_COLS);
+#pragma unroll 1
+            for (int half = 0; half < 2; ++half) {
+                if (half == 1) bulk_wait_read();  // this thread's first-half store has read its row
+#pragma unroll 1
+                for (int c = half * kTmHalf; c < half * kTmHalf + kTmHalf; c += 16) {
+                    float g[16], uu[16];
+                    tmem_ld16(taddr + c, g);
+                    tmem_ld16(taddr + kTcBM + c, uu);
+                    tmem_wait_ld();
+                    T h[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) h[j] = from_f32<T>(silu_f32(g[j]) * uu[j]);
+                    uint4* dst = reinterpret_cast<uint4*>(my_row + (c - half * kTmHalf) * 2);
+                    dst[0] = reinterpret_cast<const uint4*>(h)[0];
+                    dst[1] = reinterpret_cast<const uint4*>(h)[1];
+                }
+                if (half == 1) {
+                    // accumulator drained: hand the TMEM buffer back to the MMA warp
+                    tc_fence_before();
+                    mbar_arrive(&tempty[acc]);
+                }
+                fence_proxy_async_smem();
+                if (tok < rows && half * kTmHalf < ncols)
+                    bulk_store(static_cast<T*>(p.hid) + (hrow0 + tok) * p.f + m0 + half * kTmHalf, my_row,
+                               static_cast<uint32_t>(kTmHalf * sizeof(T)));
+                bulk_commit();
+            }
+            if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        }
+        bulk_wait_all();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
 }  // namespace chronos
