@@ -140,6 +140,34 @@ __device__ __forceinline__ TcUnit tc_decode(const TcGemmParams& p, int num_activ
     return r;
 }
 
+// Group of unit u for a warp whose previous unit was in group `a`: a CTA visits
+// its units in increasing order, so the 32 lanes test the next 32 group starts
+// at once (one memory round trip for most units instead of a binary search's
+// chain).  Every lane of the warp must call it; all get the same result.
+__device__ __forceinline__ int tc_group_warp(const TcGemmParams& p, int num_active, int a, int u, int lane) {
+    while (true) {
+        const int cand = a + 1 + lane;
+        const bool ok = cand < num_active && p.ustart[cand] <= u;
+        const unsigned m = __ballot_sync(0xffffffffu, ok);
+        if (m == 0u) return a;
+        a += 32 - __clz(m);  // highest passing lane (group starts are increasing)
+        if (m != 0xffffffffu) return a;
+    }
+}
+
+// Unit u of group a: token tile, weight-row tile and K split.
+__device__ __forceinline__ TcUnit tc_unit_at(const TcGemmParams& p, int a, int u, int bn) {
+    TcUnit r;
+    r.a = a;
+    int rem = u - p.ustart[a];
+    const int tt = (p.act_rows[a] + bn - 1) / bn;
+    r.tok_tile = rem % tt;
+    rem /= tt;
+    r.mtile = rem % p.m_tiles;
+    r.split = rem / p.m_tiles;
+    return r;
+}
+
 template <typename T, int BN, bool GATEUP, bool DENSE = false>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_grouped_gemm(const __grid_constant__ CUtensorMap tm_a0r,  // routed gate (or down)
@@ -210,16 +238,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int splits_unused = 0;
 
     if (warp == 0) {
-        if (lane == 0) {
-            // ------------------------------ TMA producer ------------------------------
-            int stage = 0;
-            uint32_t phase = 0;
-            int polled_eid = -1;
-            // decode tiles (one token tile per group): weights streamed once, evict first
-            constexpr bool kStreamA = BN <= 64;
-            const uint64_t pol_a = kStreamA ? l2_evict_first_policy() : 0ull;
-            for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
-                const TcUnit w = tc_decode(p, num_active, u, BN, splits_unused);
+        // ------------------------------ TMA producer ------------------------------
+        // the warp decodes the units, lane 0 issues the waits and the copies
+        int stage = 0;
+        uint32_t phase = 0;
+        int polled_eid = -1;
+        int ga = 0;
+        // decode tiles (one token tile per group): weights streamed once, evict first
+        constexpr bool kStreamA = BN <= 64;
+        const uint64_t pol_a = kStreamA ? l2_evict_first_policy() : 0ull;
+        for (int u = blockIdx.x; u < total; u += gridDim.x) {
+            if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;
+            ga = tc_group_warp(p, num_active, ga, u, lane);
+            if (lane == 0) {
+                const TcUnit w = tc_unit_at(p, ga, u, BN);
                 const int eid = p.act_eid[w.a];
                 const bool shared = eid < 0;
                 if (!shared && p.ready_flags != nullptr && eid != polled_eid) {
@@ -264,6 +296,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
             }
+            __syncwarp();
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -273,9 +306,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
+            const bool unsplit = p.kt_per_split >= p.k_tiles;
             for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
-                const TcUnit w = tc_decode(p, num_active, u, BN, splits_unused);
-                const int kt0 = w.split * p.kt_per_split;
+                // without K splits every unit spans the whole K: no unit decode on this path
+                const int split = unsplit ? 0 : tc_decode(p, num_active, u, BN, splits_unused).split;
+                const int kt0 = split * p.kt_per_split;
                 const int kt1 = min(p.k_tiles, kt0 + p.kt_per_split);
                 if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, kPipelineLimitNs, abort_flag)) {
                     *abort_flag = 1;
@@ -324,8 +359,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         volatile int* ep_ok = abort_flag + 1;  // verdict of the accumulator wait, shared
         int acc = 0;
         uint32_t acc_phase = 0;
+        int ga = 0;
         for (int u = blockIdx.x; u < total; u += gridDim.x) {
-            const TcUnit w = tc_decode(p, num_active, u, BN, splits_unused);
+            ga = tc_group_warp(p, num_active, ga, u, lane);
+            const TcUnit w = tc_unit_at(p, ga, u, BN);
             const int rows = p.act_rows[w.a];
             const int eid = p.act_eid[w.a];
             const int tok0 = w.tok_tile * BN;
@@ -524,13 +561,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int total = p.hdr->units_gu;
 
     if (warp == 0) {
-        if (lane == 0) {
-            // ------------------------------ TMA producer ------------------------------
-            int stage = 0;
-            uint32_t phase = 0;
-            int polled_eid = -1;
-            for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
-                const TcUnit w = tc_decode(p, num_active, u, kTmTokens, 0);
+        // ------------------------------ TMA producer ------------------------------
+        int stage = 0;
+        uint32_t phase = 0;
+        int polled_eid = -1;
+        int ga = 0;
+        for (int u = blockIdx.x; u < total; u += gridDim.x) {
+            if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;
+            ga = tc_group_warp(p, num_active, ga, u, lane);
+            if (lane == 0) {
+                const TcUnit w = tc_unit_at(p, ga, u, kTmTokens);
                 const int eid = p.act_eid[w.a];
                 const bool shared = eid < 0;
                 if (!shared && p.ready_flags != nullptr && eid != polled_eid) {
@@ -563,6 +603,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
             }
+            __syncwarp();
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -614,8 +655,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         uint8_t* my_row = staging + row_in_tile * kTmRowBytes;
         int acc = 0;
         uint32_t acc_phase = 0;
+        int ga = 0;
         for (int u = blockIdx.x; u < total; u += gridDim.x) {
-            const TcUnit w = tc_decode(p, num_active, u, kTmTokens, 0);
+            ga = tc_group_warp(p, num_active, ga, u, lane);
+            const TcUnit w = tc_unit_at(p, ga, u, kTmTokens);
             const int rows = p.act_rows[w.a];
             const int64_t hrow0 = p.act_hrow[w.a];
             const int tok = w.tok_tile * kTmTokens + row_in_tile;
