@@ -53,7 +53,8 @@ int fail(int code, const char* fmt, ...) {
                         cudaGetErrorString(err_), __FILE__, __LINE__);                        \
     } while (0)
 
-constexpr int kDownWideMinTokens = 1024;  // batches from this size use 256-token down tiles
+constexpr int kDownWideMinTokens = 1024;  // batches from this size use token-major down tiles
+constexpr int kDmPass = 128;               // token-major down: output columns per epilogue pass
 
 std::atomic<uint64_t> g_kernel_launches{0};
 
@@ -398,9 +399,9 @@ int launch_tc(const CUtensorMap& a0r, const CUtensorMap& a1r, const CUtensorMap&
     return CHRONOS_OK;
 }
 
-template <typename T, int BN, int BN_DN>
+template <typename T, int BN, int BN_DN, bool TM_DN = false>
 int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int kt_per_split_dn, int slot,
-                   bool direct) {
+                   bool direct, bool shared_last) {
     const ChronosMoeShape& s = a->shape;
     const int dt = s.dtype;
     const uint64_t N = static_cast<uint64_t>(s.num_tokens), H = s.hidden, F = s.ffn;
@@ -478,12 +479,25 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     pd.ustart = w.at<int32_t>(w.L->ustart_dn);
     pd.k_tiles = static_cast<int>(F / kTcBK);
     pd.kt_per_split = kt_per_split_dn;
-    pd.m_tiles = static_cast<int>((H + kTcBM - 1) / kTcBM);
+    pd.m_tiles = static_cast<int>(TM_DN ? (H + kDmCols - 1) / kDmCols : (H + kTcBM - 1) / kTcBM);
     pd.w_rows = static_cast<int>(H);
     pd.out_cols = static_cast<int>(H);
     pd.y_direct = direct ? a->y : nullptr;
-    if ((rc = launch_tc<T, BN_DN, false>(d_r, d_r, d_s, d_s, h_m, h_m, pd, grid, st)))
+    if (shared_last) {
+        pd.sf_shared = static_cast<int>(S);
+        pd.sh_hrow = static_cast<int64_t>(N * K);
+        pd.dn_done = &w.at<PlanHeader>(w.L->hdr)->dn_done;
+        pd.y_out = a->y;
+    }
+    if constexpr (TM_DN) {
+        // large batches: token-major tiles (128 tokens x 256 output columns)
+        constexpr int smem = tc_dm_smem_bytes(kDmPass);
+        if ((rc = set_smem(tc_down_tm<T, kDmPass>, smem))) return rc;
+        CHRONOS_CUDA_CHECK(launch_kernel(tc_down_tm<T, kDmPass>, dim3(grid), dim3(kTcThreads), smem, st, true,
+                                         d_r, d_s, h_m, pd));
+    } else if ((rc = launch_tc<T, BN_DN, false>(d_r, d_r, d_s, d_s, h_m, h_m, pd, grid, st))) {
         return rc;
+    }
     prof_ran(slot, CHRONOS_STAGE_DOWN);
     return CHRONOS_OK;
 }
@@ -591,18 +605,20 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
                                            aligned16(a->w_shared_down)));
     int bn = 128;
     if (tc) bn = N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128;
-    // large batches whose experts get many rows each: 256-token tiles for the down GEMM
-    // (half the weight-operand traffic per FLOP); with ~128 rows per expert (e.g. 256
-    // experts, top-8, 4096 tokens) a 256-row tile would be half padding
-    const int64_t avg_rows = N * s.top_k / s.num_experts;
-    const int bn_dn = (tc && N >= kDownWideMinTokens && avg_rows >= 384) ? 256 : bn;
+    // large batches: token-major down tiles, 128 tokens x 256 output columns (the
+    // MMA's N = 256 halves the weight-operand traffic per FLOP of 128-column
+    // tiles; 128-token tiles keep small expert groups' padding low)
+    const bool tm_dn = tc && N >= kDownWideMinTokens;
+    const int bn_dn = tm_dn ? kTmTokens : bn;
     const int tok_tile = tc ? bn : kSimtTile;
     const int tok_tile_dn = tc ? bn_dn : kSimtTile;
     const int mt_gu = tc ? (s.ffn + kTcBM - 1) / kTcBM : (s.ffn + kSimtTile - 1) / kSimtTile;
-    const int mt_dn = tc ? (s.hidden + kTcBM - 1) / kTcBM : (s.hidden + kSimtTile - 1) / kSimtTile;
+    const int mt_dn = tm_dn ? (s.hidden + kDmCols - 1) / kDmCols
+                      : tc  ? (s.hidden + kTcBM - 1) / kTcBM
+                            : (s.hidden + kSimtTile - 1) / kSimtTile;
 
     int splits_dn = 1, kt_dn = s.ffn / kTcBK;
-    if (tc) {
+    if (tc && !tm_dn) {
         const int kt_total = s.ffn / kTcBK;
         const int64_t groups_est = std::min<int64_t>(s.num_experts, N * s.top_k) + s.num_shared;
         const int64_t tiles_est = groups_est * ((N + bn_dn - 1) / bn_dn);
@@ -623,6 +639,12 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
         splits_dn = 1;
         kt_dn = s.ffn / kTcBK;
     }
+    // shared experts present: they run last in the down GEMM as one K = S_h * F
+    // product per output tile, whose epilogue adds the routed accumulator and
+    // writes the output (no finalize pass, no shared reduce-adds)
+    // (when its tiles, one per 128 or BN tokens and output-column tile, cover the SMs)
+    const bool shared_last = tc && !direct && s.num_shared > 0 && aligned16(a->y) &&
+                             (N + bn_dn - 1) / bn_dn * mt_dn >= sm_count();
 
     int rc;
     // counters: zeroed by the logit kernel, or here when routing is skipped
@@ -649,6 +671,7 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     pp.mt_gu = mt_gu;
     pp.mt_dn = mt_dn;
     pp.splits_dn = splits_dn;
+    pp.shared_fin = shared_last ? 1 : 0;
     pp.grp_count = w.at<int32_t>(L.grp_count);
     pp.slot_of_expert = a->slot_of_expert;
     pp.hdr = w.at<PlanHeader>(L.hdr);
@@ -698,13 +721,12 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
             return fail(CHRONOS_ERR_INVALID_ARG, "internal: fp32 on the tensor-core path");
         } else {
             switch (bn) {
-                case 16: rc = launch_tc_pair<T, 16, 16>(a, w, st, kt_dn, slot, direct); break;
-                case 32: rc = launch_tc_pair<T, 32, 32>(a, w, st, kt_dn, slot, direct); break;
-                case 64: rc = launch_tc_pair<T, 64, 64>(a, w, st, kt_dn, slot, direct); break;
+                case 16: rc = launch_tc_pair<T, 16, 16>(a, w, st, kt_dn, slot, direct, shared_last); break;
+                case 32: rc = launch_tc_pair<T, 32, 32>(a, w, st, kt_dn, slot, direct, shared_last); break;
+                case 64: rc = launch_tc_pair<T, 64, 64>(a, w, st, kt_dn, slot, direct, shared_last); break;
                 default:
-                    rc = bn_dn == 256
-                             ? launch_tc_pair<T, 128, 256>(a, w, st, kt_dn, slot, direct)
-                             : launch_tc_pair<T, 128, 128>(a, w, st, kt_dn, slot, direct);
+                    rc = tm_dn ? launch_tc_pair<T, 128, 128, true>(a, w, st, kt_dn, slot, direct, shared_last)
+                               : launch_tc_pair<T, 128, 128>(a, w, st, kt_dn, slot, direct, shared_last);
                     break;
             }
         }
@@ -714,7 +736,7 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     if (rc) return rc;
 
     prof_mark(slot, CHRONOS_STAGE_FINALIZE, st);
-    if (direct) {
+    if (direct || shared_last) {
         prof_mark(slot, kBoundaries - 1, st);
         return CHRONOS_OK;
     }

@@ -277,6 +277,23 @@ __device__ __forceinline__ void red_add_f32(float* addr, float v) {
     asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
 }
 
+// Counter increment with release semantics at GPU scope (orders this thread's
+// earlier writes, and those it observed, before the increment).
+__device__ __forceinline__ void red_release_add_s32(int32_t* addr, int32_t v) {
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+// shared[dst .. dst+bytes) = global[src ..], completing on `bar` (complete_tx).
+// Plain (untiled) bulk copy, no cluster multicast; both addresses 16-byte
+// aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ int32_t ld_acquire_gpu(const int32_t* p) {
     int32_t v;
     asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -67,6 +67,17 @@ struct TcGemmParams {
     // coef * D stored straight into the output [N, H] (x dtype) instead of
     // reduce-added into y_acc; null otherwise
     void* y_direct;
+    // DOWN, shared experts last (sf_shared = S_h > 0): after the routed units
+    // (units_dn of them) come the shared units, one per (128 output columns,
+    // BN tokens), each a K = S_h * F product over the S_h shared experts'
+    // hidden rows (sh_hrow + s * n_tokens + token).  Their epilogue waits until
+    // every CTA with routed units has counted itself in *dn_done, then writes
+    // y_out = y_acc + shared_coef * D in the output dtype: the finalize pass
+    // and the shared experts' reduce-adds are folded in.
+    int sf_shared;
+    int64_t sh_hrow;
+    int32_t* dn_done;
+    void* y_out;
 };
 
 __host__ __device__ constexpr int tc_stage_bytes(int bn, bool gateup) {
@@ -168,6 +179,18 @@ __device__ __forceinline__ TcUnit tc_unit_at(const TcGemmParams& p, int a, int u
     return r;
 }
 
+// Shared-last down GEMM: an epilogue's routed reduce-adds are complete; count
+// its CTA in (all 128 epilogue threads call this together).
+__device__ __forceinline__ void tc_count_routed_done(int32_t* counter, int et) {
+    bulk_wait_all();
+    fence_proxy_async_global();
+    epilogue_bar_sync(128);
+    if (et == 0) {
+        __threadfence();
+        red_release_add_s32(counter, 1);
+    }
+}
+
 template <typename T, int BN, bool GATEUP, bool DENSE = false>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_grouped_gemm(const __grid_constant__ CUtensorMap tm_a0r,  // routed gate (or down)
@@ -202,7 +225,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+    uint64_t* ybar = tempty + 2;  // shared-last units: accumulator rows landed in staging
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(ybar + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -218,6 +242,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], 128);
         }
+        mbar_init(ybar, 1);
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tmap(&tm_a0r);
@@ -234,7 +259,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     pdl_wait();  // everything below reads what earlier kernels of the call wrote
     const int num_active = p.hdr->num_active;
-    const int total = GATEUP ? p.hdr->units_gu : p.hdr->units_dn;
+    const int total_main = GATEUP ? p.hdr->units_gu : p.hdr->units_dn;
+    // shared-last units of the down GEMM: (output column tile, token tile) pairs after the routed ones
+    const int sf_tt = (!GATEUP && p.sf_shared > 0) ? static_cast<int>((p.n_tokens + BN - 1) / BN) : 0;
+    const int total = total_main + sf_tt * p.m_tiles;
     const int splits_unused = 0;
 
     if (warp == 0) {
@@ -249,6 +277,38 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint64_t pol_a = kStreamA ? l2_evict_first_policy() : 0ull;
         for (int u = blockIdx.x; u < total; u += gridDim.x) {
             if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;
+            if constexpr (!GATEUP) {
+                if (u >= total_main) {
+                    // shared-last unit: K runs over the S_h shared experts back to back
+                    if (lane == 0) {
+                        const int rem = u - total_main;
+                        const int tok0 = (rem % sf_tt) * BN;
+                        const int m0 = (rem / sf_tt) * kTcBM;
+                        const int ktot = p.sf_shared * p.k_tiles;
+                        for (int kt = 0; kt < ktot; ++kt) {
+                            const int sx = kt / p.k_tiles;
+                            const int kk = kt - sx * p.k_tiles;
+                            if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, kPipelineLimitNs, abort_flag)) {
+                                *abort_flag = 1;
+                                report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                                break;
+                            }
+                            uint8_t* sb = smem + stage * STAGE_BYTES;
+                            mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+                            const int a_row = sx * p.w_rows + m0;
+                            const int b_row = static_cast<int>(p.sh_hrow + sx * p.n_tokens) + tok0;
+                            if constexpr (kStreamA)
+                                tma_load_2d_hint(sb, &tm_a0s, &full[stage], kk * kTcBK, a_row, pol_a);
+                            else
+                                tma_load_2d(sb, &tm_a0s, &full[stage], kk * kTcBK, a_row);
+                            tma_load_2d(sb + A_BYTES, &tm_br, &full[stage], kk * kTcBK, b_row);
+                            if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                        }
+                    }
+                    __syncwarp();
+                    continue;
+                }
+            }
             ga = tc_group_warp(p, num_active, ga, u, lane);
             if (lane == 0) {
                 const TcUnit w = tc_unit_at(p, ga, u, BN);
@@ -309,9 +369,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const bool unsplit = p.kt_per_split >= p.k_tiles;
             for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
                 // without K splits every unit spans the whole K: no unit decode on this path
-                const int split = unsplit ? 0 : tc_decode(p, num_active, u, BN, splits_unused).split;
+                const bool sfu = !GATEUP && u >= total_main;
+                const int split = (unsplit || sfu) ? 0 : tc_decode(p, num_active, u, BN, splits_unused).split;
                 const int kt0 = split * p.kt_per_split;
-                const int kt1 = min(p.k_tiles, kt0 + p.kt_per_split);
+                const int kt1 = sfu ? p.sf_shared * p.k_tiles : min(p.k_tiles, kt0 + p.kt_per_split);
                 if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, kPipelineLimitNs, abort_flag)) {
                     *abort_flag = 1;
                     report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
@@ -360,7 +421,107 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         int ga = 0;
+        // shared-last mode: a CTA with routed units counts itself in once their
+        // reduce-adds are complete; shared-last units wait until all such CTAs have
+        const bool sf_count = !GATEUP && p.sf_shared > 0 && static_cast<int>(blockIdx.x) < total_main;
+        const int sf_target = min(static_cast<int>(gridDim.x), total_main);
+        bool sf_counted = false, sf_ready = false;
+        uint32_t yphase = 0;
         for (int u = blockIdx.x; u < total; u += gridDim.x) {
+            if constexpr (!GATEUP) {
+                if (u >= total_main) {
+                    // ---- shared-last unit: y_out = y_acc + shared_coef * D ----
+                    if (sf_count && !sf_counted) {
+                        tc_count_routed_done(p.dn_done, et);
+                        sf_counted = true;
+                    }
+                    const int rem = u - total_main;
+                    const int tok0 = (rem % sf_tt) * BN;
+                    const int m0 = (rem / sf_tt) * kTcBM;
+                    const int ncols = min(kTcBM, p.out_cols - m0);
+                    float* cf = s_coef + acc * BN;
+                    for (int r = et; r < BN; r += 128) {
+                        const int64_t tok = tok0 + r;
+                        cf[r] = tok < p.n_tokens ? p.slot_coef[p.sh_hrow + tok] : 0.0f;
+                    }
+                    if (et == 0) {
+                        bool ok = mbar_wait_bounded(&tfull[acc], acc_phase, kPipelineLimitNs, abort_flag);
+                        if (ok && !sf_ready) {
+                            // every routed contribution must be in the accumulator
+                            const uint64_t t0 = globaltimer_ns();
+                            while (ld_acquire_gpu(p.dn_done) < sf_target) {
+                                if (*abort_flag || globaltimer_ns() - t0 > kPipelineLimitNs) {
+                                    ok = false;
+                                    break;
+                                }
+                                __nanosleep(64);
+                            }
+                        }
+                        if (!ok) {
+                            *abort_flag = 1;
+                            report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                        }
+                        *ep_ok = ok ? 1 : 0;
+                    }
+                    sf_ready = true;
+                    bulk_wait_read();
+                    epilogue_bar_sync(128);
+                    if (!*ep_ok) break;
+                    tc_fence_after();
+                    fence_proxy_async_global();  // accumulator rows are read by bulk copies below
+                    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                           static_cast<uint32_t>(acc * ACC_COLS);
+                    constexpr int SUB = tc_staging_rows(BN, GATEUP);
+                    constexpr int ROW_F = ROW_BYTES / 4;
+                    const float* ys = reinterpret_cast<const float*>(staging);
+    #pragma unroll 1
+                    for (int c0 = 0; c0 < BN; c0 += SUB) {
+                        const int64_t left = p.n_tokens - (tok0 + c0);
+                        const int nrows = left < SUB ? static_cast<int>(left) : SUB;
+                        if (nrows <= 0) break;
+                        const bool last = c0 + SUB >= BN || tok0 + c0 + SUB >= p.n_tokens;
+                        if (c0 > 0) bulk_wait_read();
+                        if (et == 0) mbar_arrive_expect_tx(ybar, static_cast<uint32_t>(nrows * ncols * 4));
+                        epilogue_bar_sync(128);
+                        // the SUB accumulator rows of these tokens -> staging (fp32)
+                        if (et < nrows)
+                            bulk_load(staging + et * ROW_BYTES, p.y_acc + (tok0 + c0 + et) * p.h + m0,
+                                      static_cast<uint32_t>(ncols * 4), ybar);
+                        if (!mbar_wait_bounded(ybar, yphase, kPipelineLimitNs, abort_flag)) {
+                            *abort_flag = 1;
+                            report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                        }
+                        yphase ^= 1u;
+    #pragma unroll 1
+                        for (int c = c0; c < c0 + SUB; c += 16) {
+                            float g[16];
+                            tmem_ld16(taddr + c, g);
+                            tmem_wait_ld();
+                            float yv[16];
+    #pragma unroll
+                            for (int j = 0; j < 16; ++j) yv[j] = ys[(c - c0 + j) * ROW_F + row_in_tile];
+                            // all 128 columns of these 16 rows read before they are overwritten
+                            epilogue_bar_sync(128);
+    #pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                reinterpret_cast<T*>(staging + (c - c0 + j) * ROW_BYTES)[row_in_tile] =
+                                    from_f32<T>(fmaf(cf[c + j], g[j], yv[j]));
+                        }
+                        if (last) {
+                            tc_fence_before();
+                            mbar_arrive(&tempty[acc]);
+                        }
+                        fence_proxy_async_smem();
+                        epilogue_bar_sync(128);
+                        if (et < nrows)
+                            bulk_store(static_cast<T*>(p.y_out) + (tok0 + c0 + et) * p.h + m0,
+                                       staging + et * ROW_BYTES, static_cast<uint32_t>(ncols * sizeof(T)));
+                        bulk_commit();
+                    }
+                    if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+                    continue;
+                }
+            }
             ga = tc_group_warp(p, num_active, ga, u, lane);
             const TcUnit w = tc_unit_at(p, ga, u, BN);
             const int rows = p.act_rows[w.a];
@@ -472,6 +633,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         }
+        // a CTA without shared-last units (or that stopped early) still counts itself in
+        if (sf_count && !sf_counted) tc_count_routed_done(p.dn_done, et);
         bulk_wait_all();
     }
 
@@ -707,6 +870,355 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         }
+        bulk_wait_all();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+
+// ---------------------------------------------------------------------------
+// Token-major down GEMM for large batches.  A = 128 hidden rows of the group
+// (its tokens, M = 128), B = 256 rows of the group's down weights (two
+// 128-row boxes, N = 256), K = F.  Token tiles of 128 rows leave less padding
+// in small expert groups than 256-token tiles, at the same operand bytes per
+// FLOP.  The accumulator row is a token: the epilogue thread owning it scales
+// the row by the slot coefficient and reduce-adds it into the token's y_acc
+// row, PASS columns at a time, through its own padded staging row (no
+// transposition, no barriers between the epilogue threads).  Direct output
+// (k = 1, no shared experts) and shared-last units (sf_shared > 0) behave as
+// in tc_grouped_gemm: shared-last units follow the routed ones, run K over
+// the S_h shared experts back to back and write y_out = y_acc + coef * D.
+// ---------------------------------------------------------------------------
+constexpr int kDmCols = 256;                                    // output columns per tile (MMA N)
+constexpr int kDmStageBytes = kTmABytes + kDmCols * kTcBK * 2;  // 16 KB tokens + 32 KB weights
+__host__ __device__ constexpr int tc_dm_row_bytes(int pass) { return pass * 4 + 16; }
+__host__ __device__ constexpr int tc_dm_stages(int pass) {
+    return (232448 - 1024 - 256 - kTmTokens * tc_dm_row_bytes(pass)) / kDmStageBytes > 8
+               ? 8
+               : (232448 - 1024 - 256 - kTmTokens * tc_dm_row_bytes(pass)) / kDmStageBytes;
+}
+__host__ __device__ constexpr int tc_dm_smem_bytes(int pass) {
+    return 1024 + tc_dm_stages(pass) * kDmStageBytes + kTmTokens * tc_dm_row_bytes(pass) + 256;
+}
+
+template <typename T, int PASS>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_down_tm(const __grid_constant__ CUtensorMap tm_dr,  // routed down [P*H, F], 128-row boxes
+               const __grid_constant__ CUtensorMap tm_ds,  // shared down [S*H, F]
+               const __grid_constant__ CUtensorMap tm_h,   // hidden rows [slots, F], 128-row boxes
+               TcGemmParams p) {
+    constexpr int STAGES = tc_dm_stages(PASS);
+    constexpr int ROW_BYTES = tc_dm_row_bytes(PASS);
+    constexpr int ACC_COLS = kDmCols;
+    constexpr int TMEM_COLS = 512;
+    static_assert(kDmCols % PASS == 0 && PASS % 16 == 0, "passes must tile the 256 columns");
+    static_assert(STAGES >= 2, "shared memory holds fewer than two pipeline stages");
+    static_assert(tc_dm_smem_bytes(PASS) <= 232448, "shared memory over the per-CTA limit");
+
+    extern __shared__ uint8_t tc_smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* staging = smem + STAGES * kDmStageBytes;  // [128 tokens][ROW_BYTES]
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + kTmTokens * ROW_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* ybar = tempty + 2;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(ybar + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    pdl_trigger();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 128);
+        }
+        mbar_init(ybar, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tm_dr);
+        prefetch_tmap(&tm_h);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_holder, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    pdl_wait();
+    const int num_active = p.hdr->num_active;
+    const int total_main = p.hdr->units_dn;
+    const int sf_tt = p.sf_shared > 0 ? static_cast<int>((p.n_tokens + kTmTokens - 1) / kTmTokens) : 0;
+    const int total = total_main + sf_tt * p.m_tiles;
+
+    if (warp == 0) {
+        // ------------------------------ TMA producer ------------------------------
+        int stage = 0;
+        uint32_t phase = 0;
+        int polled_eid = -1;
+        int ga = 0;
+        for (int u = blockIdx.x; u < total; u += gridDim.x) {
+            if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;
+            const bool sfu = u >= total_main;
+            if (!sfu) ga = tc_group_warp(p, num_active, ga, u, lane);
+            if (lane == 0) {
+                int h_row, w_row, ktot;
+                const CUtensorMap* mw;
+                if (sfu) {
+                    const int rem = u - total_main;
+                    h_row = static_cast<int>(p.sh_hrow) + (rem % sf_tt) * kTmTokens;
+                    w_row = (rem / sf_tt) * kDmCols;
+                    ktot = p.sf_shared * p.k_tiles;
+                    mw = &tm_ds;
+                } else {
+                    const TcUnit w = tc_unit_at(p, ga, u, kTmTokens);
+                    const int eid = p.act_eid[w.a];
+                    const bool shared = eid < 0;
+                    if (!shared && p.ready_flags != nullptr && eid != polled_eid) {
+                        const uint64_t t0 = globaltimer_ns();
+                        bool ok = true;
+                        while (ld_acquire_gpu(p.ready_flags + eid) < p.ready_epoch) {
+                            if (globaltimer_ns() - t0 > p.ready_limit_ns) { ok = false; break; }
+                            __nanosleep(256);
+                        }
+                        if (!ok) report_status(p.status, CHRONOS_ERR_EXPERT_NOT_READY);
+                        fence_proxy_async_global();
+                        polled_eid = eid;
+                    }
+                    h_row = p.act_hrow[w.a] + w.tok_tile * kTmTokens;
+                    w_row = p.act_wslot[w.a] * p.w_rows + w.mtile * kDmCols;
+                    ktot = p.k_tiles;
+                    mw = shared ? &tm_ds : &tm_dr;
+                }
+                for (int kt = 0; kt < ktot; ++kt) {
+                    // shared-last units: k tiles of shared expert sx, whose hidden rows
+                    // follow the previous expert's N rows
+                    const int sx = sfu ? kt / p.k_tiles : 0;
+                    const int kk = kt - sx * p.k_tiles;
+                    const int hr = h_row + static_cast<int>(sx * p.n_tokens);
+                    const int wr = w_row + sx * p.w_rows;
+                    if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, kPipelineLimitNs, abort_flag)) {
+                        *abort_flag = 1;
+                        report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                        break;
+                    }
+                    uint8_t* sb = smem + stage * kDmStageBytes;
+                    mbar_arrive_expect_tx(&full[stage], kDmStageBytes);
+                    tma_load_2d(sb, &tm_h, &full[stage], kk * kTcBK, hr);
+                    tma_load_2d(sb + kTmABytes, mw, &full[stage], kk * kTcBK, wr);
+                    tma_load_2d(sb + kTmABytes + kTcBM * kTcBK * 2, mw, &full[stage], kk * kTcBK, wr + kTcBM);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+            __syncwarp();
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------ MMA issuer ------------------------------
+            constexpr uint32_t IDESC = idesc_f16(kTmTokens, kDmCols, AbFormat<T>::value);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
+                const int ktot = u >= total_main ? p.sf_shared * p.k_tiles : p.k_tiles;
+                if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, kPipelineLimitNs, abort_flag)) {
+                    *abort_flag = 1;
+                    report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + static_cast<uint32_t>(acc * ACC_COLS);
+                bool failed = false;
+                for (int kt = 0; kt < ktot; ++kt) {
+                    if (!mbar_wait_bounded(&full[stage], phase, kPipelineLimitNs, abort_flag)) {
+                        *abort_flag = 1;
+                        report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                        failed = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sh = smem_u32(smem + stage * kDmStageBytes);
+                    const uint32_t sw = sh + kTmABytes;
+#pragma unroll
+                    for (int kk = 0; kk < kTcBK / 16; ++kk) {
+                        const uint32_t accum = (kt > 0 || kk > 0) ? 1u : 0u;
+                        umma_f16(d, sdesc_k_sw128(sh + kk * 32), sdesc_k_sw128(sw + kk * 32), IDESC, accum);
+                    }
+                    umma_commit(&empty[stage]);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+                if (failed) break;
+                umma_commit(&tfull[acc]);
+                if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+            }
+        }
+    } else {
+        // ------------------------------ epilogue ------------------------------
+        // thread = one token row of the tile (TMEM lane)
+        const int q = warp & 3;
+        const int row_in_tile = q * 32 + lane;
+        const int et = threadIdx.x - 64;
+        volatile int* ep_ok = abort_flag + 1;
+        uint8_t* my_row = staging + row_in_tile * ROW_BYTES;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        int ga = 0;
+        const bool sf_count = p.sf_shared > 0 && static_cast<int>(blockIdx.x) < total_main;
+        const int sf_target = min(static_cast<int>(gridDim.x), total_main);
+        bool sf_counted = false, sf_ready = false;
+        uint32_t yphase = 0;
+        for (int u = blockIdx.x; u < total; u += gridDim.x) {
+            const bool sfu = u >= total_main;
+            int64_t out_row = -1;  // y row of this thread's token, -1: padding row
+            float coef = 0.0f;
+            int n0;
+            if (sfu) {
+                if (sf_count && !sf_counted) {
+                    tc_count_routed_done(p.dn_done, et);
+                    sf_counted = true;
+                }
+                const int rem = u - total_main;
+                const int64_t tok = static_cast<int64_t>(rem % sf_tt) * kTmTokens + row_in_tile;
+                n0 = (rem / sf_tt) * kDmCols;
+                if (tok < p.n_tokens) {
+                    out_row = tok;
+                    coef = p.slot_coef[p.sh_hrow + tok];
+                }
+            } else {
+                ga = tc_group_warp(p, num_active, ga, u, lane);
+                const TcUnit w = tc_unit_at(p, ga, u, kTmTokens);
+                const int tok = w.tok_tile * kTmTokens + row_in_tile;
+                n0 = w.mtile * kDmCols;
+                if (tok < p.act_rows[w.a]) {
+                    const int64_t slot = p.act_hrow[w.a] + tok;
+                    out_row = p.slot_tok[slot];
+                    coef = p.slot_coef[slot];
+                }
+            }
+            const int ncols = min(kDmCols, p.out_cols - n0);
+            if (et == 0) {
+                bool ok = mbar_wait_bounded(&tfull[acc], acc_phase, kPipelineLimitNs, abort_flag);
+                if (ok && sfu && !sf_ready) {
+                    // every routed contribution must be in the accumulator
+                    const uint64_t t0 = globaltimer_ns();
+                    while (ld_acquire_gpu(p.dn_done) < sf_target) {
+                        if (*abort_flag || globaltimer_ns() - t0 > kPipelineLimitNs) {
+                            ok = false;
+                            break;
+                        }
+                        __nanosleep(64);
+                    }
+                }
+                if (!ok) {
+                    *abort_flag = 1;
+                    report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                }
+                *ep_ok = ok ? 1 : 0;
+            }
+            if (sfu) sf_ready = true;
+            bulk_wait_read();  // this thread's previous copies are done reading its row
+            epilogue_bar_sync(128);
+            if (!*ep_ok) break;
+            tc_fence_after();
+            if (sfu) fence_proxy_async_global();  // accumulator rows are read by bulk copies below
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(acc * ACC_COLS);
+#pragma unroll 1
+            for (int c0 = 0; c0 < kDmCols; c0 += PASS) {
+                const int nc = min(PASS, ncols - c0);  // uniform over the tile
+                if (nc <= 0) break;
+                const bool last = c0 + PASS >= ncols;
+                if (c0 > 0) bulk_wait_read();
+                if (sfu) {
+                    // this pass's accumulator segment of every valid token row -> its
+                    // staging row (the barrier orders the expected bytes before the copies)
+                    const int64_t tile_tok0 = static_cast<int64_t>((u - total_main) % sf_tt) * kTmTokens;
+                    const int64_t left = p.n_tokens - tile_tok0;
+                    const int nrows = left < kTmTokens ? static_cast<int>(left) : kTmTokens;
+                    if (et == 0) mbar_arrive_expect_tx(ybar, static_cast<uint32_t>(nrows * nc * 4));
+                    epilogue_bar_sync(128);
+                    if (out_row >= 0)
+                        bulk_load(my_row, p.y_acc + out_row * p.h + n0 + c0, static_cast<uint32_t>(nc * 4), ybar);
+                    if (!mbar_wait_bounded(ybar, yphase, kPipelineLimitNs, abort_flag)) {
+                        *abort_flag = 1;
+                        report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                    }
+                    yphase ^= 1u;
+                }
+#pragma unroll 1
+                for (int c = c0; c < c0 + PASS; c += 16) {
+                    float g[16];
+                    tmem_ld16(taddr + c, g);
+                    tmem_wait_ld();
+                    float4* row16 = reinterpret_cast<float4*>(my_row + (c - c0) * 4);
+                    if (sfu || p.y_direct != nullptr) {
+                        // output dtype, written over the front of the row (columns
+                        // already consumed: 2 bytes per column behind 4 bytes per column)
+                        float yv[16];
+                        if (sfu) {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const float4 v = row16[j];
+                                yv[4 * j] = v.x;
+                                yv[4 * j + 1] = v.y;
+                                yv[4 * j + 2] = v.z;
+                                yv[4 * j + 3] = v.w;
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) yv[j] = 0.0f;
+                        }
+                        T o[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) o[j] = from_f32<T>(fmaf(coef, g[j], yv[j]));
+                        uint4* dst = reinterpret_cast<uint4*>(my_row + (c - c0) * 2);
+                        dst[0] = reinterpret_cast<const uint4*>(o)[0];
+                        dst[1] = reinterpret_cast<const uint4*>(o)[1];
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            row16[j] = make_float4(coef * g[4 * j], coef * g[4 * j + 1], coef * g[4 * j + 2],
+                                                   coef * g[4 * j + 3]);
+                    }
+                }
+                if (last) {
+                    // accumulator drained: hand the TMEM buffer back to the MMA warp
+                    tc_fence_before();
+                    mbar_arrive(&tempty[acc]);
+                }
+                fence_proxy_async_smem();
+                if (out_row >= 0) {
+                    if (sfu)
+                        bulk_store(static_cast<T*>(p.y_out) + out_row * p.h + n0 + c0, my_row,
+                                   static_cast<uint32_t>(nc * sizeof(T)));
+                    else if (p.y_direct != nullptr)
+                        bulk_store(static_cast<T*>(p.y_direct) + out_row * p.h + n0 + c0, my_row,
+                                   static_cast<uint32_t>(nc * sizeof(T)));
+                    else
+                        bulk_reduce_add_f32(p.y_acc + out_row * p.h + n0 + c0, my_row,
+                                            static_cast<uint32_t>(nc * 4));
+                }
+                bulk_commit();
+            }
+            if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        }
+        if (sf_count && !sf_counted) tc_count_routed_done(p.dn_done, et);
         bulk_wait_all();
     }
 

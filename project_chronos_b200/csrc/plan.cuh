@@ -25,7 +25,8 @@ struct PlanHeader {
     int32_t units_gu;        // work units of the gate/up GEMM
     int32_t units_dn;        // work units of the down GEMM
     int32_t max_rows;        // largest group
-    int32_t pad[3];
+    int32_t dn_done;         // down GEMM CTAs whose routed units are complete (shared-last mode)
+    int32_t pad[2];
 };
 
 struct PlanParams {
@@ -35,6 +36,7 @@ struct PlanParams {
     int tok_tile_dn;              // token rows per down GEMM tile
     int mt_gu, mt_dn;             // weight-row tiles per group (gate/up, down)
     int splits_dn;                // K splits per down tile
+    int shared_fin;               // shared experts run last in the down GEMM, merged (no down units here)
     const int32_t* grp_count;     // [E]
     const int32_t* slot_of_expert;  // [E] or null
     PlanHeader* hdr;
@@ -107,7 +109,7 @@ __device__ __forceinline__ void plan_tables(const PlanParams& p, int cnt, int in
     const int tt_sh = (N + p.tok_tile - 1) / p.tok_tile;
     const int tt_sh_dn = (N + p.tok_tile_dn - 1) / p.tok_tile_dn;
     const int sh_gu = tt_sh * p.mt_gu;
-    const int sh_dn = tt_sh_dn * p.mt_dn * p.splits_dn;
+    const int sh_dn = p.shared_fin ? 0 : tt_sh_dn * p.mt_dn * p.splits_dn;
     if (tid < E) {
         const int off = inc_cnt - cnt;
         p.grp_off[tid] = off;
@@ -142,6 +144,7 @@ __device__ __forceinline__ void plan_tables(const PlanParams& p, int cnt, int in
         p.hdr->units_gu = tot_gu;
         p.hdr->units_dn = tot_dn;
         p.hdr->max_rows = S > 0 ? N : 0;
+        p.hdr->dn_done = 0;
     }
 }
 

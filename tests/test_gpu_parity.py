@@ -163,7 +163,31 @@ def test_no_shared_experts_and_nothing_available_gives_zero(n):
     assert float(out["y"].float().abs().max()) == 0.0
 
 
-@pytest.mark.parametrize("n", [1, 5, 64, 65, 700])
+@pytest.mark.parametrize("n,h", [(1000, 2560), (2000, 2624)])
+def test_shared_experts_last_in_down_gemm(n, h):
+    """Shapes whose shared-expert tiles cover the SMs: the shared experts run
+    last in the down GEMM as one K = S_h * F product per tile and write the
+    output rows (routed accumulator + shared term) themselves, with no
+    finalize pass.  n = 1000: 128-column weight-major tiles; n = 2000:
+    token-major tiles, ragged in tokens (2000 = 15 * 128 + 80) and in output
+    columns (2624 = 10 * 256 + 64).  The output starts NaN-filled, so every
+    row and column must be written."""
+    wl = _workload(h, 16, 4, 192, 2, n, seed=n + h, avail_p=0.7)
+    avail = wl.mask.to(torch.float32)
+    y0 = torch.full((n, h), float("nan"), dtype=wl.x.dtype, device=DEV)
+    out = _run(wl, 4, True, avail=avail, out=y0)
+    torch.cuda.synchronize()
+    _ops().check_status()
+    y = _np(out["y"])
+    assert np.isfinite(y).all()
+    ref, o_idx, _, _ = _oracle(wl, 4, True, avail=avail)
+    assert np.array_equal(out["topk_idx"].cpu().numpy(), o_idx)
+    assert O.rel_l2(y, ref) <= 1e-2
+    emu, *_ = _oracle(wl, 4, True, avail=avail, emulate=True)
+    assert O.rel_l2(y, emu) <= 3e-3
+
+
+@pytest.mark.parametrize("n", [1, 5, 64, 65, 700, 1300])
 def test_one_choice_no_shared_direct_output(n):
     """k = 1, S_h = 0: the down GEMM stores the output rows itself (no fp32
     accumulator); tokens whose one expert is unavailable get exact zeros;
