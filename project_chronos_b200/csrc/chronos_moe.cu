@@ -54,7 +54,7 @@ int fail(int code, const char* fmt, ...) {
     } while (0)
 
 constexpr int kDownWideMinTokens = 1024;  // batches from this size use token-major down tiles
-constexpr int kDmPass = 128;               // token-major down: output columns per epilogue pass
+constexpr int kDmPass = 64;  // token-major down: output columns per epilogue pass
 
 std::atomic<uint64_t> g_kernel_launches{0};
 

@@ -898,13 +898,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 constexpr int kDmCols = 256;                                    // output columns per tile (MMA N)
 constexpr int kDmStageBytes = kTmABytes + kDmCols * kTcBK * 2;  // 16 KB tokens + 32 KB weights
 __host__ __device__ constexpr int tc_dm_row_bytes(int pass) { return pass * 4 + 16; }
+// No alignment slack: the dynamic shared memory of a CTA that has no static
+// shared memory starts 1024-byte aligned (the kernel checks it and reports
+// CHRONOS_ERR_CUDA otherwise), which buys the ring its fourth stage.
 __host__ __device__ constexpr int tc_dm_stages(int pass) {
-    return (232448 - 1024 - 256 - kTmTokens * tc_dm_row_bytes(pass)) / kDmStageBytes > 8
+    return (232448 - 256 - kTmTokens * tc_dm_row_bytes(pass)) / kDmStageBytes > 8
                ? 8
-               : (232448 - 1024 - 256 - kTmTokens * tc_dm_row_bytes(pass)) / kDmStageBytes;
+               : (232448 - 256 - kTmTokens * tc_dm_row_bytes(pass)) / kDmStageBytes;
 }
 __host__ __device__ constexpr int tc_dm_smem_bytes(int pass) {
-    return 1024 + tc_dm_stages(pass) * kDmStageBytes + kTmTokens * tc_dm_row_bytes(pass) + 256;
+    return tc_dm_stages(pass) * kDmStageBytes + kTmTokens * tc_dm_row_bytes(pass) + 256;
 }
 
 template <typename T, int PASS>
@@ -921,9 +924,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     static_assert(STAGES >= 2, "shared memory holds fewer than two pipeline stages");
     static_assert(tc_dm_smem_bytes(PASS) <= 232448, "shared memory over the per-CTA limit");
 
-    extern __shared__ uint8_t tc_smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>(
-        (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    extern __shared__ __align__(1024) uint8_t tc_dm_smem[];
+    if ((smem_u32(tc_dm_smem) & 1023u) != 0u) {
+        // operand tiles need 1024-byte alignment (128-byte swizzle atoms)
+        if (threadIdx.x == 0) report_status(p.status, CHRONOS_ERR_CUDA);
+        return;
+    }
+    uint8_t* smem = tc_dm_smem;
     uint8_t* staging = smem + STAGES * kDmStageBytes;  // [128 tokens][ROW_BYTES]
     uint64_t* full = reinterpret_cast<uint64_t*>(staging + kTmTokens * ROW_BYTES);
     uint64_t* empty = full + STAGES;
@@ -1144,9 +1151,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int nc = min(PASS, ncols - c0);  // uniform over the tile
                 if (nc <= 0) break;
                 const bool last = c0 + PASS >= ncols;
-                if (c0 > 0) bulk_wait_read();
+                // this pass's accumulator columns -> registers first: the TMEM reads
+                // overlap the wait for the staging row, and the last pass hands the
+                // accumulator back before the row is written
+                float g[PASS];
+#pragma unroll
+                for (int j = 0; j < PASS; j += 16) tmem_ld16(taddr + c0 + j, *reinterpret_cast<float(*)[16]>(g + j));
+                tmem_wait_ld();
+                if (last) {
+                    tc_fence_before();
+                    mbar_arrive(&tempty[acc]);
+                }
+                if (c0 > 0) bulk_wait_read();  // this thread's previous copy has read its row
+                float4* row4 = reinterpret_cast<float4*>(my_row);
                 if (sfu) {
-                    // this pass's accumulator segment of every valid token row -> its
+                    // the pass's accumulator segment of every valid token row -> its
                     // staging row (the barrier orders the expected bytes before the copies)
                     const int64_t tile_tok0 = static_cast<int64_t>((u - total_main) % sf_tt) * kTmTokens;
                     const int64_t left = p.n_tokens - tile_tok0;
@@ -1161,20 +1180,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                     yphase ^= 1u;
                 }
-#pragma unroll 1
-                for (int c = c0; c < c0 + PASS; c += 16) {
-                    float g[16];
-                    tmem_ld16(taddr + c, g);
-                    tmem_wait_ld();
-                    float4* row16 = reinterpret_cast<float4*>(my_row + (c - c0) * 4);
-                    if (sfu || p.y_direct != nullptr) {
-                        // output dtype, written over the front of the row (columns
-                        // already consumed: 2 bytes per column behind 4 bytes per column)
+                if (sfu || p.y_direct != nullptr) {
+                    // output dtype, written over the front of the row (2 bytes per
+                    // column behind the 4-byte columns already read)
+#pragma unroll
+                    for (int c = 0; c < PASS; c += 16) {
                         float yv[16];
                         if (sfu) {
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {
-                                const float4 v = row16[j];
+                                const float4 v = row4[c / 4 + j];
                                 yv[4 * j] = v.x;
                                 yv[4 * j + 1] = v.y;
                                 yv[4 * j + 2] = v.z;
@@ -1186,21 +1201,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         }
                         T o[16];
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) o[j] = from_f32<T>(fmaf(coef, g[j], yv[j]));
-                        uint4* dst = reinterpret_cast<uint4*>(my_row + (c - c0) * 2);
+                        for (int j = 0; j < 16; ++j) o[j] = from_f32<T>(fmaf(coef, g[c + j], yv[j]));
+                        uint4* dst = reinterpret_cast<uint4*>(my_row + c * 2);
                         dst[0] = reinterpret_cast<const uint4*>(o)[0];
                         dst[1] = reinterpret_cast<const uint4*>(o)[1];
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            row16[j] = make_float4(coef * g[4 * j], coef * g[4 * j + 1], coef * g[4 * j + 2],
-                                                   coef * g[4 * j + 3]);
                     }
-                }
-                if (last) {
-                    // accumulator drained: hand the TMEM buffer back to the MMA warp
-                    tc_fence_before();
-                    mbar_arrive(&tempty[acc]);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < PASS; c += 4)
+                        row4[c / 4] = make_float4(coef * g[c], coef * g[c + 1], coef * g[c + 2], coef * g[c + 3]);
                 }
                 fence_proxy_async_smem();
                 if (out_row >= 0) {
