@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(kTiledThreads, 2) route_tiled_kernel(RoutePara
 // ---------------------------------------------------------------------------
 // per token: finish logits, softmax, top-k, blend coefficients
 // ---------------------------------------------------------------------------
-constexpr int kSelectThreads = 256;
+constexpr int kSelectThreads = 512;
 
 __device__ __forceinline__ float expert_avail(const RouteParams& p, int e) {
     float a = p.avail ? p.avail[e] : 1.0f;
@@ -307,10 +307,13 @@ __device__ __forceinline__ float expert_avail(const RouteParams& p, int e) {
 // renormalisation; or, with pre-routed inputs, read the given top-k.  Lane
 // j < k returns choice j (expert, weight, availability) and has written its
 // top-k outputs; every lane returns the token's shared-expert extra weight
-// sum_k w (1 - a).  EPL = experts per lane (E <= 32 * EPL).
+// sum_k w (1 - a).  EPL = experts per lane (E <= 32 * EPL).  The per-expert
+// statistics go to s_counts / s_mass (shared memory, the caller adds them to
+// the global ones once per block) when given, else straight to global memory.
 template <typename T, int EPL>
 __device__ __forceinline__ void select_token(const RouteParams& p, int64_t t, int lane, int& mine_e,
-                                             float& mine_w, float& mine_a, float& shared_extra) {
+                                             float& mine_w, float& mine_a, float& shared_extra,
+                                             int* s_counts = nullptr, float* s_mass = nullptr) {
     const int E = p.e;
     mine_e = 0;
     mine_w = 0.0f;
@@ -441,8 +444,8 @@ __device__ __forceinline__ void select_token(const RouteParams& p, int64_t t, in
         p.topk_idx[o] = mine_e;
         p.topk_w[o] = mine_w;
         p.sel_coef[o] = mine_w * mine_a;
-        if (p.counts_all) atomicAdd(&p.counts_all[mine_e], 1);
-        if (p.mass_all) atomicAdd(&p.mass_all[mine_e], mine_w);
+        if (p.counts_all) atomicAdd(s_counts ? &s_counts[mine_e] : &p.counts_all[mine_e], 1);
+        if (p.mass_all) atomicAdd(s_mass ? &s_mass[mine_e] : &p.mass_all[mine_e], mine_w);
     }
 }
 
@@ -458,26 +461,51 @@ __device__ __forceinline__ void zero_direct_row(const RouteParams& p, int64_t t,
     for (int i = lane; i < n16; i += 32) yv[i] = make_uint4(0u, 0u, 0u, 0u);
 }
 
-// One warp per token: select, then a global atomic gives each available
-// selection its position in its expert group.
+// One warp per token: select; each available selection gets its position in
+// its expert group.  The block's selections are counted per expert in shared
+// memory first and one global atomic per (block, expert) reserves the block's
+// positions, so a popular expert's counter sees one atomic per block instead
+// of one per selection (the same for the routing statistics).
 template <typename T, int EPL>
 __global__ void __launch_bounds__(kSelectThreads) route_select_kernel(RouteParams p) {
+    __shared__ int s_cnt[kMaxExperts];    // available selections per expert
+    __shared__ int s_base[kMaxExperts];   // first group position of this block's selections
+    __shared__ int s_hits[kMaxExperts];   // all selections per expert (statistics)
+    __shared__ float s_mass[kMaxExperts];
+    const int tid = threadIdx.x;
+    for (int e = tid; e < p.e; e += kSelectThreads) {
+        s_cnt[e] = 0;
+        s_hits[e] = 0;
+        s_mass[e] = 0.0f;
+    }
+    __syncthreads();
     pdl_trigger();
     pdl_wait();  // partials and zeroed counters from the logit kernel
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = tid >> 5, lane = tid & 31;
     const int64_t t = static_cast<int64_t>(blockIdx.x) * (kSelectThreads / 32) + warp;
-    if (t >= p.n) return;
-    if (p.y_acc != nullptr) {
-        float4* yv = reinterpret_cast<float4*>(p.y_acc + t * p.h);
-        for (int i = lane; i < p.h / 4; i += 32) yv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const bool valid = t < p.n;
+    int mine_e = 0, rank = -1;
+    float mine_w = 0.0f, mine_a = 0.0f, shared_extra = 0.0f;
+    if (valid) {
+        if (p.y_acc != nullptr) {
+            float4* yv = reinterpret_cast<float4*>(p.y_acc + t * p.h);
+            for (int i = lane; i < p.h / 4; i += 32) yv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        select_token<T, EPL>(p, t, lane, mine_e, mine_w, mine_a, shared_extra, s_hits, s_mass);
+        if (lane < p.k && mine_a > 0.0f) rank = atomicAdd(&s_cnt[mine_e], 1);
+        if (lane == 0 && p.num_shared > 0)
+            p.shared_coef[t] = (1.0f + shared_extra) / static_cast<float>(p.num_shared);
+        zero_direct_row<T>(p, t, lane, mine_a);
     }
-    int mine_e;
-    float mine_w, mine_a, shared_extra;
-    select_token<T, EPL>(p, t, lane, mine_e, mine_w, mine_a, shared_extra);
-    if (lane < p.k) p.pos[t * p.k + lane] = mine_a > 0.0f ? atomicAdd(&p.grp_count[mine_e], 1) : -1;
-    if (lane == 0 && p.num_shared > 0)
-        p.shared_coef[t] = (1.0f + shared_extra) / static_cast<float>(p.num_shared);
-    zero_direct_row<T>(p, t, lane, mine_a);
+    __syncthreads();
+    for (int e = tid; e < p.e; e += kSelectThreads) {
+        const int c = s_cnt[e];
+        if (c > 0) s_base[e] = atomicAdd(&p.grp_count[e], c);
+        if (p.counts_all && s_hits[e] > 0) atomicAdd(&p.counts_all[e], s_hits[e]);
+        if (p.mass_all && s_hits[e] > 0) atomicAdd(&p.mass_all[e], s_mass[e]);
+    }
+    __syncthreads();
+    if (valid && lane < p.k) p.pos[t * p.k + lane] = rank >= 0 ? s_base[mine_e] + rank : -1;
 }
 
 }  // namespace chronos
