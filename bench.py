@@ -426,7 +426,7 @@ def run_ours(args, dist: Dist):
     pre_gateup_flops = 2.0 * 2 * shape.ffn * shape.hidden * (pre_slots_routed
                                                               + PREFILL_TOKENS * shape.num_shared)
     pre_gu_tflops = pre_gateup_flops / (pre_gateup_ms / 1e3) / 1e12
-    pre_roof = dict(kernel="tc_grouped_gemm (gateup) prefill", bound="tensor",
+    pre_roof = dict(kernel="tc_gateup_tm (gate/up, token-major) prefill", bound="tensor",
                     achieved=round(pre_gu_tflops, 1), peak=peaks["bf16_tflops"], unit="TFLOP/s",
                     frac=round(pre_gu_tflops / peaks["bf16_tflops"], 4),
                     traffic=traffic.get("prefill_gateup_bytes_per_launch"),

@@ -349,7 +349,9 @@ int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool p
             const dim3 grid(static_cast<unsigned>((N + kTiledTokens - 1) / kTiledTokens),
                             static_cast<unsigned>((s.num_experts + kRouteTile - 1) / kRouteTile),
                             static_cast<unsigned>((rp.nchunks + kTiledChunks - 1) / kTiledChunks));
-            CHRONOS_CUDA_CHECK(launch_kernel(route_tiled_kernel<T>, grid, dim3(kTiledThreads), 0, st,
+            constexpr int smem = tiled_smem_bytes<T>();
+            if (int rc = set_smem(route_tiled_kernel<T>, smem)) return rc;
+            CHRONOS_CUDA_CHECK(launch_kernel(route_tiled_kernel<T>, grid, dim3(kTiledThreads), smem, st,
                                              false, rp));
         }
     }

@@ -199,17 +199,51 @@ __global__ void __launch_bounds__(kPartialThreads) route_partials_kernel(RoutePa
 // ---------------------------------------------------------------------------
 constexpr int kTiledThreads = 256;
 constexpr int kTiledTokens = 128;  // tokens per block (8 per thread)
-constexpr int kTiledK = 16;        // h per shared-memory stage
-constexpr int kTiledPad = kTiledK + 4;
 constexpr int kTiledChunks = 4;    // chunks of K per block (blockIdx.z)
+// h per shared-memory stage: 32 for 2-byte inputs (a stage computes for about
+// as long as a DRAM round trip takes, so the one-stage-ahead register prefetch
+// is hidden), 16 for fp32 inputs (their prefetch registers are twice as many)
+template <typename T>
+__host__ __device__ constexpr int tiled_k() { return sizeof(T) == 2 ? 32 : 16; }
+template <typename T>
+__host__ __device__ constexpr int tiled_smem_bytes() {
+    return 2 * (kTiledTokens + kRouteTile) * (tiled_k<T>() + 4) * 4;  // double-buffered fp32 stages
+}
+
+// 4 consecutive inputs as loaded from global memory (converted when staged)
+template <typename T>
+struct Raw4 {
+    uint2 v;
+};
+template <>
+struct Raw4<float> {
+    float4 v;
+};
+template <typename T>
+__device__ __forceinline__ Raw4<T> load_raw4(const T* p) {
+    Raw4<T> r;
+    r.v = *reinterpret_cast<const decltype(r.v)*>(p);
+    return r;
+}
+template <typename T>
+__device__ __forceinline__ float4 raw4_to_f32(const Raw4<T>& r) {
+    return load4<T>(reinterpret_cast<const T*>(&r.v));
+}
 
 // Block = 128 tokens x 64 experts x 4 chunks of K; thread = 8 tokens x 4
 // experts (experts eg + 16 j), one fmaf chain per (token, expert, chunk) in
 // increasing h; at each chunk end the partial is written and the chain restarts.
+// Stages of K_T h are double-buffered in shared memory (fp32); the next stage's
+// inputs are held in registers as loaded while the current one is computed.
 template <typename T>
 __global__ void __launch_bounds__(kTiledThreads, 2) route_tiled_kernel(RouteParams p) {
-    __shared__ __align__(16) float xs[2][kTiledTokens][kTiledPad];
-    __shared__ __align__(16) float ws[2][kRouteTile][kTiledPad];
+    constexpr int KT_H = tiled_k<T>();
+    constexpr int PAD = KT_H + 4;
+    constexpr int EX = KT_H / 2;  // x elements per thread per stage (2 threads per row)
+    constexpr int EW = KT_H / 4;  // w elements per thread per stage (4 threads per row)
+    extern __shared__ __align__(16) float route_smem[];
+    float* xs = route_smem;                        // [2][kTiledTokens][PAD]
+    float* ws = route_smem + 2 * kTiledTokens * PAD;  // [2][kRouteTile][PAD]
     pdl_trigger();
     if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) zero_route_counters(p);
     const int tid = threadIdx.x;
@@ -220,33 +254,40 @@ __global__ void __launch_bounds__(kTiledThreads, 2) route_tiled_kernel(RoutePara
     const int e0 = blockIdx.y * kRouteTile;
     const T* x = static_cast<const T*>(p.x);
     const T* w = static_cast<const T*>(p.w);
-    // loaders: x row xr, 8 consecutive h at xk; w row wr, 4 consecutive h at wk
-    const int xr = tid >> 1, xk = (tid & 1) * 8;
-    const int wr = tid >> 2, wk = (tid & 3) * 4;
+    // loaders: x row xr, EX consecutive h at xk; w row wr, EW consecutive h at wk
+    const int xr = tid >> 1, xk = (tid & 1) * EX;
+    const int wr = tid >> 2, wk = (tid & 3) * EW;
     const bool xrow_ok = t0 + xr < p.n;
     const bool wrow_ok = e0 + wr < E;
     const T* xrow = x + (t0 + xr) * H;
     const T* wrow = w + static_cast<int64_t>(e0 + wr) * H;
-    float4 xa, xb, wa;
+    Raw4<T> xraw[EX / 4], wraw[EW / 4];
     auto gload = [&](int kt) {
-        const int h = kt * kTiledK;
-        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-        xa = (xrow_ok && h + xk < H) ? load4<T>(xrow + h + xk) : z;
-        xb = (xrow_ok && h + xk + 4 < H) ? load4<T>(xrow + h + xk + 4) : z;
-        wa = (wrow_ok && h + wk < H) ? load4<T>(wrow + h + wk) : z;
+        const int h = kt * KT_H;
+        Raw4<T> z;
+        z.v = {};
+#pragma unroll
+        for (int q = 0; q < EX / 4; ++q)  // H % 4 == 0: each group of 4 is in or out as a whole
+            xraw[q] = (xrow_ok && h + xk + 4 * q < H) ? load_raw4<T>(xrow + h + xk + 4 * q) : z;
+#pragma unroll
+        for (int q = 0; q < EW / 4; ++q)
+            wraw[q] = (wrow_ok && h + wk + 4 * q < H) ? load_raw4<T>(wrow + h + wk + 4 * q) : z;
     };
     auto sstore = [&](int buf) {
-        *reinterpret_cast<float4*>(&xs[buf][xr][xk]) = xa;
-        *reinterpret_cast<float4*>(&xs[buf][xr][xk + 4]) = xb;
-        *reinterpret_cast<float4*>(&ws[buf][wr][wk]) = wa;
+#pragma unroll
+        for (int q = 0; q < EX / 4; ++q)
+            *reinterpret_cast<float4*>(&xs[(buf * kTiledTokens + xr) * PAD + xk + 4 * q]) = raw4_to_f32<T>(xraw[q]);
+#pragma unroll
+        for (int q = 0; q < EW / 4; ++q)
+            *reinterpret_cast<float4*>(&ws[(buf * kRouteTile + wr) * PAD + wk + 4 * q]) = raw4_to_f32<T>(wraw[q]);
     };
     float acc[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-    const int KT = (H + kTiledK - 1) / kTiledK;
-    constexpr int kTilesPerChunk = kRouteChunk / kTiledK;
+    const int KT = (H + KT_H - 1) / KT_H;
+    constexpr int kTilesPerChunk = kRouteChunk / KT_H;
     const int kt_begin = blockIdx.z * kTiledChunks * kTilesPerChunk;
     const int kt_end = min(KT, kt_begin + kTiledChunks * kTilesPerChunk);
     gload(kt_begin);
@@ -255,13 +296,15 @@ __global__ void __launch_bounds__(kTiledThreads, 2) route_tiled_kernel(RoutePara
     for (int kt = kt_begin; kt < kt_end; ++kt) {
         const int buf = (kt - kt_begin) & 1;
         if (kt + 1 < kt_end) gload(kt + 1);
+        const float* xb = xs + (buf * kTiledTokens + tg * 8) * PAD;
+        const float* wb = ws + (buf * kRouteTile + eg) * PAD;
 #pragma unroll
-        for (int kk = 0; kk < kTiledK; kk += 4) {
+        for (int kk = 0; kk < KT_H; kk += 4) {
             float4 a[8], b[4];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) a[i] = *reinterpret_cast<const float4*>(&xs[buf][tg * 8 + i][kk]);
+            for (int i = 0; i < 8; ++i) a[i] = *reinterpret_cast<const float4*>(xb + i * PAD + kk);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(&ws[buf][eg + 16 * j][kk]);
+            for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(wb + 16 * j * PAD + kk);
 #pragma unroll
             for (int i = 0; i < 8; ++i)
 #pragma unroll
