@@ -464,6 +464,11 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     pg.m_tiles = static_cast<int>((F + kTcBM - 1) / kTcBM);
     pg.w_rows = static_cast<int>(F);
     pg.out_cols = static_cast<int>(F);
+    if (kDense && S > 0) {
+        // decode: the shared experts' units run before the plan of the call exists
+        pg.pre_units = static_cast<int>(S) * pg.m_tiles;
+        pg.sh_hrow = static_cast<int64_t>(N * K);
+    }
     prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
     if constexpr (BN == kTmTokens) {
         // large batches: token-major tiles (one N = 256 MMA for gate and up)

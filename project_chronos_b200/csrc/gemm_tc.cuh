@@ -78,6 +78,10 @@ struct TcGemmParams {
     int64_t sh_hrow;
     int32_t* dn_done;
     void* y_out;
+    // DENSE gate/up (decode): the first pre_units units are the shared experts'
+    // (S_h x m_tiles, one token tile each), run before this call's plan exists;
+    // their hidden rows start at sh_hrow + s * n_tokens
+    int pre_units;
 };
 
 __host__ __device__ constexpr int tc_stage_bytes(int bn, bool gateup) {
@@ -257,12 +261,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
 
-    pdl_wait();  // everything below reads what earlier kernels of the call wrote
-    const int num_active = p.hdr->num_active;
-    const int total_main = GATEUP ? p.hdr->units_gu : p.hdr->units_dn;
-    // shared-last units of the down GEMM: (output column tile, token tile) pairs after the routed ones
-    const int sf_tt = (!GATEUP && p.sf_shared > 0) ? static_cast<int>((p.n_tokens + BN - 1) / BN) : 0;
-    const int total = total_main + sf_tt * p.m_tiles;
+    // Decode gate/up: the shared experts' units come first in the unit order and
+    // their tables follow from the shape, so they run before this call's plan
+    // exists (while the routing kernels are still running).  Everything else
+    // waits for the earlier kernels of the call before reading the plan.
+    const int pre_units = (GATEUP && DENSE) ? p.pre_units : 0;
+    int num_active = 0, total_main = 0, sf_tt = 0, total = 0;
+    bool planned = false;
+    auto load_plan = [&]() {
+        pdl_wait();
+        num_active = p.hdr->num_active;
+        total_main = GATEUP ? p.hdr->units_gu : p.hdr->units_dn;
+        // shared-last units of the down GEMM: (output column tile, token tile) pairs after the routed ones
+        sf_tt = (!GATEUP && p.sf_shared > 0) ? static_cast<int>((p.n_tokens + BN - 1) / BN) : 0;
+        total = total_main + sf_tt * p.m_tiles;
+        planned = true;
+    };
+    if (pre_units == 0) load_plan();
     const int splits_unused = 0;
 
     if (warp == 0) {
@@ -275,8 +290,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // decode tiles (one token tile per group): weights streamed once, evict first
         constexpr bool kStreamA = BN <= 64;
         const uint64_t pol_a = kStreamA ? l2_evict_first_policy() : 0ull;
-        for (int u = blockIdx.x; u < total; u += gridDim.x) {
+        for (int u = blockIdx.x;; u += gridDim.x) {
+            if (u >= pre_units) {
+                if (!planned) load_plan();
+                if (u >= total) break;
+            }
             if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;
+            if constexpr (GATEUP && DENSE) {
+                if (u < pre_units) {
+                    // shared expert u / m_tiles, weight-row tile u % m_tiles; B = x rows [0, BN)
+                    if (lane == 0) {
+                        const int sx = u / p.m_tiles;
+                        const int a_row = sx * p.w_rows + (u - sx * p.m_tiles) * kTcBM;
+                        for (int kt = 0; kt < p.k_tiles; ++kt) {
+                            if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, kPipelineLimitNs, abort_flag)) {
+                                *abort_flag = 1;
+                                report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
+                                break;
+                            }
+                            uint8_t* sb = smem + stage * STAGE_BYTES;
+                            mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+                            tma_load_2d_hint(sb, &tm_a0s, &full[stage], kt * kTcBK, a_row, pol_a);
+                            tma_load_2d_hint(sb + A_BYTES, &tm_a1s, &full[stage], kt * kTcBK, a_row, pol_a);
+                            tma_load_2d(sb + 2 * A_BYTES, &tm_bs, &full[stage], kt * kTcBK, 0);
+                            if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                        }
+                    }
+                    __syncwarp();
+                    continue;
+                }
+            }
             if constexpr (!GATEUP) {
                 if (u >= total_main) {
                     // shared-last unit: K runs over the S_h shared experts back to back
@@ -367,7 +410,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             int acc = 0;
             uint32_t acc_phase = 0;
             const bool unsplit = p.kt_per_split >= p.k_tiles;
-            for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
+            for (int u = blockIdx.x; !*abort_flag; u += gridDim.x) {
+                if (u >= pre_units) {
+                    if (!planned) load_plan();
+                    if (u >= total) break;
+                }
                 // without K splits every unit spans the whole K: no unit decode on this path
                 const bool sfu = !GATEUP && u >= total_main;
                 const int split = (unsplit || sfu) ? 0 : tc_decode(p, num_active, u, BN, splits_unused).split;
@@ -427,7 +474,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int sf_target = min(static_cast<int>(gridDim.x), total_main);
         bool sf_counted = false, sf_ready = false;
         uint32_t yphase = 0;
-        for (int u = blockIdx.x; u < total; u += gridDim.x) {
+        for (int u = blockIdx.x;; u += gridDim.x) {
+            if (u >= pre_units) {
+                if (!planned) load_plan();
+                if (u >= total) break;
+            }
             if constexpr (!GATEUP) {
                 if (u >= total_main) {
                     // ---- shared-last unit: y_out = y_acc + shared_coef * D ----
@@ -522,12 +573,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     continue;
                 }
             }
-            ga = tc_group_warp(p, num_active, ga, u, lane);
-            const TcUnit w = tc_unit_at(p, ga, u, BN);
-            const int rows = p.act_rows[w.a];
-            const int eid = p.act_eid[w.a];
+            TcUnit w;
+            int rows, eid;
+            int64_t hrow0;
+            if (GATEUP && DENSE && u < pre_units) {
+                // shared expert before the plan: all tokens, hidden rows after the routed slots
+                const int sx = u / p.m_tiles;
+                w.a = sx;
+                w.tok_tile = 0;
+                w.mtile = u - sx * p.m_tiles;
+                w.split = 0;
+                rows = static_cast<int>(p.n_tokens);
+                eid = -1;
+                hrow0 = p.sh_hrow + sx * p.n_tokens;
+            } else {
+                ga = tc_group_warp(p, num_active, ga, u, lane);
+                w = tc_unit_at(p, ga, u, BN);
+                rows = p.act_rows[w.a];
+                eid = p.act_eid[w.a];
+                hrow0 = p.act_hrow[w.a];
+            }
             const int tok0 = w.tok_tile * BN;
-            const int64_t hrow0 = p.act_hrow[w.a];
             float* cf = s_coef + acc * BN;
             int32_t* tk = s_tok + acc * BN;
             if constexpr (!GATEUP) {
