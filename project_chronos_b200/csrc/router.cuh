@@ -231,7 +231,7 @@ __device__ __forceinline__ float4 raw4_to_f32(const Raw4<T>& r) {
 }
 
 // Block = 128 tokens x 64 experts x 4 chunks of K; thread = 8 tokens x 4
-// experts (experts eg + 16 j), one fmaf chain per (token, expert, chunk) in
+// experts (tokens tg + 16 i, experts eg + 16 j), one fmaf chain per (token, expert, chunk) in
 // increasing h; at each chunk end the partial is written and the chain restarts.
 // Stages of K_T h are double-buffered in shared memory (fp32); the next stage's
 // inputs are held in registers as loaded while the current one is computed.
@@ -247,7 +247,9 @@ __global__ void __launch_bounds__(kTiledThreads, 2) route_tiled_kernel(RoutePara
     pdl_trigger();
     if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) zero_route_counters(p);
     const int tid = threadIdx.x;
-    const int tg = tid >> 4;  // tokens tg*8 .. tg*8+7
+    // tokens tg + 16 i: a warp's two token groups read adjacent shared-memory rows
+    // (different banks), not rows 8 apart (the same banks at this row pitch)
+    const int tg = tid >> 4;
     const int eg = tid & 15;  // experts eg + 16 j
     const int H = p.h, E = p.e;
     const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kTiledTokens;
@@ -296,13 +298,13 @@ __global__ void __launch_bounds__(kTiledThreads, 2) route_tiled_kernel(RoutePara
     for (int kt = kt_begin; kt < kt_end; ++kt) {
         const int buf = (kt - kt_begin) & 1;
         if (kt + 1 < kt_end) gload(kt + 1);
-        const float* xb = xs + (buf * kTiledTokens + tg * 8) * PAD;
+        const float* xb = xs + (buf * kTiledTokens + tg) * PAD;
         const float* wb = ws + (buf * kRouteTile + eg) * PAD;
 #pragma unroll
         for (int kk = 0; kk < KT_H; kk += 4) {
             float4 a[8], b[4];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) a[i] = *reinterpret_cast<const float4*>(xb + i * PAD + kk);
+            for (int i = 0; i < 8; ++i) a[i] = *reinterpret_cast<const float4*>(xb + 16 * i * PAD + kk);
 #pragma unroll
             for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(wb + 16 * j * PAD + kk);
 #pragma unroll
@@ -320,7 +322,7 @@ __global__ void __launch_bounds__(kTiledThreads, 2) route_tiled_kernel(RoutePara
             float* out = p.partials + static_cast<int64_t>(kt / kTilesPerChunk) * p.n * E;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const int64_t t = t0 + tg * 8 + i;
+                const int64_t t = t0 + tg + 16 * i;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int e = e0 + eg + 16 * j;
