@@ -187,6 +187,23 @@ def test_shared_experts_last_in_down_gemm(n, h):
     assert O.rel_l2(y, emu) <= 3e-3
 
 
+@pytest.mark.parametrize("n,h", [(1000, 2560), (2000, 2624)])
+def test_shared_experts_last_with_few_ctas(n, h):
+    """The shared-last units wait until every CTA with routed units has counted
+    itself in; with the GEMMs capped at 5 CTAs (the C ABI's max_ctas, e.g. to
+    leave SMs to a concurrent all-to-all) each CTA walks many units before its
+    shared-last ones and the count must still complete."""
+    wl = _workload(h, 16, 4, 192, 2, n, seed=n + h + 1, avail_p=0.7)
+    avail = wl.mask.to(torch.float32)
+    out = _run(wl, 4, True, avail=avail, max_ctas=5)
+    torch.cuda.synchronize()
+    _ops().check_status()
+    y = _np(out["y"])
+    ref, o_idx, _, _ = _oracle(wl, 4, True, avail=avail)
+    assert np.array_equal(out["topk_idx"].cpu().numpy(), o_idx)
+    assert O.rel_l2(y, ref) <= 1e-2
+
+
 @pytest.mark.parametrize("n", [1, 5, 64, 65, 700, 1300])
 def test_one_choice_no_shared_direct_output(n):
     """k = 1, S_h = 0: the down GEMM stores the output rows itself (no fp32
