@@ -192,7 +192,8 @@ def decode_config(shape):
 
 def algorithmic_bytes(stage: str, shape, n_tokens: int, experts_applied: int, slots: int,
                       elem: int = 2) -> float:
-    """HBM bytes one launch of a stage must move at minimum:
+    """HBM bytes one launch of a stage must move at minimum, the numerator of the
+    decode roofline (each weight byte read once per call):
     gate/up: gate+up weights of every expert applied (routed + shared), the
     token rows read and the hidden rows written; down: down weights of every
     expert applied, hidden rows read, fp32 output accumulator written."""

@@ -464,7 +464,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         const int row_in_tile = q * 32 + lane;
         const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
-        volatile int* ep_ok = abort_flag + 1;  // verdict of the accumulator wait, shared
+        volatile int* ep_ok = abort_flag + 1;  // outcome of the accumulator wait, shared
         int acc = 0;
         uint32_t acc_phase = 0;
         int ga = 0;
@@ -607,7 +607,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
             // one thread waits (bounded) for the accumulator; the barrier hands its
-            // verdict to the other 127, so they all leave together on a timeout
+            // outcome to the other 127, so they all leave together on a timeout
             if (et == 0) {
                 const bool ok = mbar_wait_bounded(&tfull[acc], acc_phase, kPipelineLimitNs, abort_flag);
                 if (!ok) {
