@@ -251,6 +251,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         fence_mbar_init();
         prefetch_tmap(&tm_a0r);
         prefetch_tmap(&tm_br);
+        prefetch_tmap(&tm_a0s);
+        prefetch_tmap(&tm_bs);
+        if (GATEUP) {
+            prefetch_tmap(&tm_a1r);
+            prefetch_tmap(&tm_a1s);
+        }
     }
     if (warp == 1) {
         tmem_alloc(tmem_holder, TMEM_COLS);
