@@ -160,6 +160,7 @@ class ChronosMOEFeedForward(nn.Module):
         # bound fast-path call (ops.LayerCall) and the key of what it was bound to
         self._call = None
         self._call_key = None
+        self._eval_zero: Optional[torch.Tensor] = None
 
     # ------------------------------------------------------------------
     # bookkeeping attributes (lazy: resolved from device tensors on read)
@@ -419,11 +420,15 @@ class ChronosMOEFeedForward(nn.Module):
             self._sync_pool(dev, dt)
         pool = self._pool
         live = self._live_np
-        self._stats_pending = None
-        self._last_on_demand_experts = []
-        self._last_fallback_experts = []
-        self._last_on_demand_weight_mass = 0.0
-        self._last_fallback_weight_mass = 0.0
+        # per-call bookkeeping: plain attributes (never parameters, buffers or
+        # submodules), written past nn.Module.__setattr__'s type checks, which
+        # cost more host time than the kernels of a one-token call
+        _set = object.__setattr__
+        _set(self, "_stats_pending", None)
+        _set(self, "_last_on_demand_experts", [])
+        _set(self, "_last_fallback_experts", [])
+        _set(self, "_last_on_demand_weight_mass", 0.0)
+        _set(self, "_last_fallback_weight_mass", 0.0)
 
         training_fallback_mask = None
         if (available_expert_mask is None and self.training and self.fallback_mask_prob > 0.0
@@ -600,25 +605,31 @@ class ChronosMOEFeedForward(nn.Module):
                     a_np = avail_t.cpu().numpy()
                 if eval_with_mask and mask_np is None:
                     # CUDA mask in eval: read lazily together with the counts
-                    self._stats_pending = dict(counts=out["counts"], mass=out["mass"], a=a_np,
-                                               on_demand=_LazyOnDemand(available_expert_mask, live))
+                    _set(self, "_stats_pending", dict(counts=out["counts"], mass=out["mass"], a=a_np,
+                                                      on_demand=_LazyOnDemand(available_expert_mask, live)))
                 else:
-                    self._stats_pending = dict(counts=out["counts"], mass=out["mass"], a=a_np,
-                                               on_demand=on_demand)
+                    _set(self, "_stats_pending", dict(counts=out["counts"], mass=out["mass"], a=a_np,
+                                                      on_demand=on_demand))
 
         y = out["y"]
         scores_bse = probs.view(B, S, E)
-        self.last_router_probs_grad = scores_bse
-        self.last_router_probs = scores_bse.detach()
+        _set(self, "last_router_probs_grad", scores_bse)
+        _set(self, "last_router_probs", scores_bse.detach())
         if self.training:
             topk_idx = out["topk_idx"].long()
             load = torch.bincount(topk_idx.reshape(-1), minlength=E).float() / max(1, x_flat.shape[0])
             aux_raw = (load * probs.float().mean(0)).sum() * E
-            self.aux_loss_raw = aux_raw
-            self.aux_loss = aux_raw * self.router_aux_loss_coef
+            _set(self, "aux_loss_raw", aux_raw)
+            _set(self, "aux_loss", aux_raw * self.router_aux_loss_coef)
         else:
-            self.aux_loss_raw = probs.new_zeros(())
-            self.aux_loss = probs.new_zeros(())
+            # eval: a zero scalar on the layer's device, made once and reused (a
+            # fresh one per call is a device fill per call)
+            z = self._eval_zero
+            if z is None or z.device != probs.device or z.dtype != probs.dtype:
+                z = probs.new_zeros(())
+                _set(self, "_eval_zero", z)
+            _set(self, "aux_loss_raw", z)
+            _set(self, "aux_loss", z)
         return y.view(B, S, H)
 
 

@@ -149,6 +149,15 @@ def moe_forward(x: torch.Tensor, router_w: torch.Tensor, w_gate: torch.Tensor, w
     return dict(y=y, probs=probs, topk_idx=topk_idx, topk_weight=topk_w, counts=counts, mass=mass)
 
 
+def _raw_stream(index: int) -> int:
+    """Handle of the current CUDA stream of device `index` (torch's raw accessor when
+    present: a fraction of the host time of building a torch.cuda.Stream)."""
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return raw(index)
+    return torch.cuda.current_stream(index).cuda_stream
+
+
 class LayerCall:
     """One layer's static arguments bound once, for repeated calls with little host work.
 
@@ -233,7 +242,7 @@ class LayerCall:
         a.expert_mass = _ptr(mass)
         a.workspace = ws.data_ptr()
         a.workspace_bytes = ws.numel()
-        stream = torch.cuda.current_stream(dev).cuda_stream
+        stream = _raw_stream(dev.index)
         if torch.cuda.current_device() == dev.index:
             rc = self._lib.chronos_moe_forward(ctypes.byref(a), ctypes.c_void_p(stream))
         else:
