@@ -281,9 +281,23 @@ int sm_count() {
 
 template <typename K>
 int set_smem(K kernel, int bytes) {
-    // idempotent; cheap enough to do per launch for the kernels that need > 48 KB
+    // once per (kernel, device, size): the attribute sticks to the function on that
+    // device, and setting it costs host time on every layer call otherwise
+    static std::mutex mu;
+    static std::vector<std::pair<const void*, long long>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const void* fn = reinterpret_cast<const void*>(kernel);
+    const long long tag = (static_cast<long long>(dev) << 32) | static_cast<unsigned>(bytes);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        for (const auto& d : done)
+            if (d.first == fn && d.second == tag) return CHRONOS_OK;
+    }
     CHRONOS_CUDA_CHECK(
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    std::lock_guard<std::mutex> lk(mu);
+    done.emplace_back(fn, tag);
     return CHRONOS_OK;
 }
 

@@ -161,6 +161,7 @@ class ChronosMOEFeedForward(nn.Module):
         self._call = None
         self._call_key = None
         self._eval_zero: Optional[torch.Tensor] = None
+        self._has_placeholder = None  # (live array, any placeholder in it)
 
     # ------------------------------------------------------------------
     # bookkeeping attributes (lazy: resolved from device tensors on read)
@@ -441,7 +442,11 @@ class ChronosMOEFeedForward(nn.Module):
         masked = available_expert_mask is not None or training_fallback_mask is not None
         mask_t = available_expert_mask if available_expert_mask is not None else training_fallback_mask
         eval_with_mask = available_expert_mask is not None and not self.training
-        has_placeholder = bool((live == 0).any())
+        hp = self._has_placeholder
+        if hp is None or hp[0] is not live:  # recomputed only when the pool was re-synced
+            hp = (live, bool((live == 0).any()))
+            _set(self, "_has_placeholder", hp)
+        has_placeholder = hp[1]
         touch = getattr(self, "runtime_touch_expert", None)
         loader = getattr(self, "runtime_on_demand_loader", None)
         policy = getattr(self, "runtime_miss_policy", "fallback_diagnostic")
@@ -581,14 +586,14 @@ class ChronosMOEFeedForward(nn.Module):
             self._last_fallback_weight_mass = fbm
         else:
             # ---- fast path: one call, no host synchronisation ----
-            on_demand = np.zeros(E, dtype=bool)
+            on_demand = _NO_ON_DEMAND
             if not masked:
-                a_np = np.ones(E, dtype=np.float32)
+                a_np = None
                 avail_t = None
             elif eval_with_mask:
                 a_np = live.copy()  # live experts run even when marked unavailable
                 if mask_np is not None:
-                    on_demand = (mask_np <= 0.0) & (live > 0)
+                    on_demand = _LazyOnDemand(mask_np, live)  # built when the statistics are read
                 avail_t = self._avail_tensor(a_np, dev)
             else:
                 if mask_np is not None:
@@ -634,16 +639,29 @@ class ChronosMOEFeedForward(nn.Module):
 
 
 class _LazyOnDemand:
-    """on_demand[e] = mask[e] <= 0 and live[e], read from a CUDA mask on first use."""
+    """on_demand[e] = mask[e] <= 0 and live[e], computed on first use (from a host
+    array, or read back from a CUDA mask)."""
 
-    def __init__(self, mask: torch.Tensor, live: np.ndarray):
+    def __init__(self, mask, live: np.ndarray):
         self.mask = mask
         self.live = live
         self._v = None
 
     def __getitem__(self, e):
         if self._v is None:
-            m = self.mask.detach().to(torch.float32).cpu().numpy()
+            m = self.mask
+            if isinstance(m, torch.Tensor):
+                m = m.detach().to(torch.float32).cpu().numpy()
             self._v = (m <= 0.0) & (self.live > 0)
         return self._v[e]
+
+
+class _NoOnDemand:
+    """on_demand[e] = False for every e (calls without an eval-time mask)."""
+
+    def __getitem__(self, e):
+        return False
+
+
+_NO_ON_DEMAND = _NoOnDemand()
 
