@@ -239,3 +239,33 @@ def test_cluster_cold_tier_round_trip(tmp_path):
         assert torch.equal(got, want[f"layers.{li}.mlp.experts.3.down_proj.weight"])
     s = store.stats()
     assert s["cluster_aware"] is True and s["num_clusters"] == 2 and s["storage_format"] == "safetensors"
+
+
+def test_bookkeeping_resolves_from_pending_statistics():
+    """The fast path leaves the per-call statistics pending (device counts and
+    weight mass, the availability used, and an on-demand mask built only when
+    read); reading a bookkeeping attribute resolves them the way the reference
+    fills its lists (moe_chronos.py:231-256): a selected expert that ran counts
+    as on-demand when the mask marked it unavailable but it was live, a selected
+    expert that did not run is a fallback."""
+    from project_chronos_b200.moe import ChronosMOEFeedForward, _LazyOnDemand, _NO_ON_DEMAND
+    cfg = _cfg(E=4)
+    moe = ChronosMOEFeedForward(cfg)
+    live = np.array([1, 1, 0, 1], dtype=np.float32)
+    mask = np.array([1, 0, 0, 0], dtype=np.float32)
+    counts = torch.tensor([3, 2, 1, 0], dtype=torch.int32)
+    mass = torch.tensor([0.5, 0.25, 0.125, 0.0])
+    lazy = _LazyOnDemand(mask, live)
+    moe._stats_pending = dict(counts=counts, mass=mass, a=live.copy(), on_demand=lazy)
+    assert lazy._v is None  # nothing computed until a bookkeeping attribute is read
+    assert moe.last_on_demand_experts == [1]
+    assert moe.last_fallback_experts == [2]
+    assert moe.last_on_demand_weight_mass == pytest.approx(0.25)
+    assert moe.last_fallback_weight_mass == pytest.approx(0.125)
+    # without an eval-time mask nothing is on demand
+    moe._stats_pending = dict(counts=counts, mass=mass, a=np.array([1, 1, 0, 1], np.float32),
+                              on_demand=_NO_ON_DEMAND)
+    assert moe.last_on_demand_experts == [] and moe.last_fallback_experts == [2]
+    # a CUDA-less tensor mask is read back the same way
+    lazy_t = _LazyOnDemand(torch.from_numpy(mask), live)
+    assert [bool(lazy_t[e]) for e in range(4)] == [False, True, False, True]
