@@ -198,7 +198,8 @@ CHRONOS_API size_t chronos_moe_args_size(void);
 #define CHRONOS_STAGE_GATEUP 3
 #define CHRONOS_STAGE_ACT 4 /* no kernel: SiLU-mul runs in the gate/up epilogue */
 #define CHRONOS_STAGE_DOWN 5
-#define CHRONOS_STAGE_FINALIZE 6
+#define CHRONOS_STAGE_FINALIZE 6 /* empty when the down GEMM writes the output itself (direct
+                                  output; shared experts last at large batches) */
 #define CHRONOS_NUM_STAGES 7
 
 /* After chronos_moe_profile_begin(max_calls), the next max_calls forward
