@@ -16,6 +16,8 @@ What it restates (all citations are files of FonaTech/Project_Chronos):
 * shared experts — ``moe_chronos.py:90-93``: the MEAN of the shared FFNs;
 * the lookahead router — ``chronos/model/lookahead_router.py:36-55``
   (``lookahead``);
+* the training load-balance loss — ``moe_chronos.py:175-185`` and
+  ``:270-276`` (``aux_loss``);
 * the blend and combine — ``moe_chronos.py:190-268`` with the arithmetic form
   of ``chronos/mlx/moe.py:160-166``:
   ``y_t = sum_k w_tk (a_e E_e(x_t) + (1 - a_e) S(x_t)) + S(x_t)``.
@@ -209,6 +211,19 @@ def lookahead(x: np.ndarray, w1: np.ndarray, w2: np.ndarray, num_experts: int, s
     lg = lg - lg.max(axis=-1, keepdims=True)
     e = np.exp(lg)
     return (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)
+
+
+def aux_loss(idx: np.ndarray, probs: np.ndarray, num_experts: int) -> float:
+    """Raw load-balance loss of a training forward (``moe_chronos.py:177-178``):
+    ``E * sum_{j,e} onehot(idx)[:, j, e].mean(0) * probs.mean(0)[e]``, i.e. E
+    times the sum over experts of (selections of e / tokens) x (mean router
+    probability of e); float64 accumulation."""
+    idx = np.asarray(idx)
+    n = idx.shape[0]
+    if n == 0:
+        return 0.0
+    load = np.bincount(idx.reshape(-1), minlength=num_experts).astype(np.float64) / n
+    return float(num_experts * np.sum(load * np.asarray(probs, np.float64).mean(axis=0)))
 
 
 def rel_l2(a: np.ndarray, b: np.ndarray) -> float:

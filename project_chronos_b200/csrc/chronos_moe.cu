@@ -12,6 +12,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <type_traits>
 #include <string>
@@ -281,23 +282,22 @@ int sm_count() {
 
 template <typename K>
 int set_smem(K kernel, int bytes) {
-    // once per (kernel, device, size): the attribute sticks to the function on that
-    // device, and setting it costs host time on every layer call otherwise
+    // The attribute is a limit that sticks to the function on its device, and
+    // setting it costs host time on every layer call: raise it only when a launch
+    // needs more than the largest value set so far on this device (a smaller
+    // launch fits under a larger limit; lowering it would break a later larger
+    // launch that found its size "already set").
     static std::mutex mu;
-    static std::vector<std::pair<const void*, long long>> done;
+    static std::map<std::pair<const void*, int>, int> limit;
     int dev = 0;
     cudaGetDevice(&dev);
-    const void* fn = reinterpret_cast<const void*>(kernel);
-    const long long tag = (static_cast<long long>(dev) << 32) | static_cast<unsigned>(bytes);
-    {
-        std::lock_guard<std::mutex> lk(mu);
-        for (const auto& d : done)
-            if (d.first == fn && d.second == tag) return CHRONOS_OK;
-    }
+    const auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = limit.find(key);
+    if (it != limit.end() && it->second >= bytes) return CHRONOS_OK;
     CHRONOS_CUDA_CHECK(
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-    std::lock_guard<std::mutex> lk(mu);
-    done.emplace_back(fn, tag);
+    limit[key] = bytes;
     return CHRONOS_OK;
 }
 

@@ -21,8 +21,10 @@ DEV = "cuda"
 def _cfg(c, dropout=0.0):
     return types.SimpleNamespace(hidden_size=c["H"], num_experts=c["E"], num_experts_per_tok=c["k"],
                                  moe_intermediate_size=c["F"], num_shared_experts=c["S"],
-                                 norm_topk_prob=c["norm"], router_aux_loss_coef=5e-4,
-                                 hidden_act="silu", dropout=dropout, fallback_mask_prob=0.0,
+                                 norm_topk_prob=c["norm"],
+                                 router_aux_loss_coef=c.get("aux_coef", 5e-4),
+                                 hidden_act="silu", dropout=dropout,
+                                 fallback_mask_prob=c.get("fallback_p", 0.0),
                                  intermediate_size=c["F"])
 
 
@@ -51,11 +53,13 @@ def _placeholders(m, c, mask):
 
 
 @pytest.mark.parametrize("name", [c["name"] for c in G.cases()])
-def test_module_matches_reference_golden(name):
+def test_module_matches_reference_golden(name, monkeypatch):
     c = G.case(name)
     d = G.load(c)
     wl = G.inputs(c)
     m = _module(c, wl)
+    if wl.bias is not None:
+        m.router_logit_bias = wl.bias.to(DEV)
     x = wl.x.to(DEV).view(c["B"], c["T"], c["H"])
     mask = None
     if c["mode"] == "eval":
@@ -68,11 +72,29 @@ def test_module_matches_reference_golden(name):
     elif c["mode"] == "train_mask":
         m.train()
         mask = torch.tensor(c["float_mask"], dtype=torch.float32)
+    elif c["mode"] == "train_nomask":
+        m.train()
+    elif c["mode"] == "train_fallback":
+        # the layer draws its miss-simulation keep mask with torch.rand(E) as the
+        # reference does (moe_chronos.py:141); hand it the reference's draws
+        m.train()
+        draws = torch.from_numpy(d["keep_draws"])
+        real_rand = torch.rand
+
+        def rand(*size, **kw):
+            if tuple(size) == (c["E"],):
+                return draws.to(kw.get("device") or "cpu")
+            return real_rand(*size, **kw)
+
+        monkeypatch.setattr(torch, "rand", rand)
     else:
         m.eval()
     with torch.no_grad():
         y = m(x, available_expert_mask=mask)
     torch.cuda.synchronize()
+    if "aux_loss_raw" in c:
+        assert abs(float(m.aux_loss_raw) - c["aux_loss_raw"]) <= 1e-5 * max(1.0, abs(c["aux_loss_raw"]))
+        assert abs(float(m.aux_loss) - c["aux_loss"]) <= 1e-5 * max(abs(c["aux_loss"]), 1e-6)
     assert y.shape == x.shape and y.dtype == x.dtype
     ref = G.reference_y(c, d)
     tol = 1e-5 if c["dtype"] == "fp32" else 1e-2
@@ -84,7 +106,37 @@ def test_module_matches_reference_golden(name):
     assert m.last_on_demand_experts == c["on_demand"]
     assert abs(m.last_fallback_weight_mass - c["fallback_mass"]) < 1e-4
     assert abs(m.last_on_demand_weight_mass - c["on_demand_mass"]) < 1e-4
-    assert float(m.aux_loss) == 0.0 or c["mode"] == "train_mask"
+    assert float(m.aux_loss) == 0.0 or c["mode"].startswith("train")
+
+
+def test_training_miss_simulation_draws_on_the_device():
+    """fallback_mask_prob > 0 in training with no mask (moe_chronos.py:132-144): the
+    layer draws keep = rand(E) >= p on the device; with that mask (recovered by
+    re-seeding the device generator) the output equals the oracle's and the
+    fallback list names the selected experts that were not kept."""
+    c = dict(G.case("train_fallback"))
+    wl = G.inputs(c)
+    m = _module(c, wl).train()
+    x = wl.x.to(DEV).view(c["B"], c["T"], c["H"])
+    for seed in (0, 1, 2):
+        torch.cuda.manual_seed(seed)
+        with torch.no_grad():
+            y = m(x)
+        torch.cuda.synchronize()
+        torch.cuda.manual_seed(seed)
+        keep = (torch.rand(c["E"], device=DEV) >= c["fallback_p"]).cpu().numpy()
+        if not keep.any():
+            continue
+        w = wl.weights
+        f = lambda t: t.float().numpy()  # noqa: E731
+        ref, idx, _, probs = O.moe_forward(f(wl.x), f(w.router), f(w.gate), f(w.up), f(w.down),
+                                           f(w.sh_gate), f(w.sh_up), f(w.sh_down), c["k"], c["norm"],
+                                           avail=keep.astype(np.float32))
+        assert O.rel_l2(y.float().cpu().numpy().reshape(-1, c["H"]), ref) <= 1e-5
+        sel = sorted(set(np.unique(idx).tolist()))
+        assert m.last_fallback_experts == [e for e in sel if not keep[e]]
+        aux = O.aux_loss(idx, probs, c["E"])
+        assert abs(float(m.aux_loss_raw) - aux) <= 1e-5 * max(1.0, aux)
 
 
 def test_all_available_matches_no_mask():

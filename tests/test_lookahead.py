@@ -73,3 +73,31 @@ def test_kernel_matches_oracle(dtype, tol, H, E, steps, n):
     with torch.no_grad():
         idx = m.predict_next_experts(xd, top_k=2)
     assert tuple(idx.shape) == (1, n, steps, 2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["lookahead_fp32", "lookahead_bf16", "lookahead_decode_bf16"])
+def test_kernel_matches_reference_golden(name):
+    """The fused kernel against the reference's own LookaheadRouter
+    (chronos/model/lookahead_router.py:36-42), golden vectors from
+    tests/golden/make_golden.py: fp32 within 1e-5; bf16 within 5e-3 of the
+    reference run in fp32 on the bf16 values and 1e-2 of its bf16 run."""
+    from project_chronos_b200 import LookaheadRouter
+    from tests import _golden as G
+    c = G.case(name)
+    d = G.load(c)
+    w1, w2, x = G.lookahead_inputs(c)
+    dt = torch.bfloat16 if c["dtype"] == "bf16" else torch.float32
+    m = LookaheadRouter(_cfg(c["H"], c["E"], c["steps"]))
+    with torch.no_grad():
+        m.proj[0].weight.copy_(w1)
+        m.proj[2].weight.copy_(w2)
+    m = m.to("cuda", dt).eval()
+    with torch.no_grad():
+        got = m(x.to("cuda", dt)).float().cpu().numpy()
+    assert got.shape == d["probs_ref"].shape
+    if dt == torch.float32:
+        assert np.abs(got - d["probs_ref"]).max() <= 1e-5
+    else:
+        assert np.abs(got - d["probs_ref_fp32"]).max() <= 5e-3
+        assert np.abs(got - d["probs_ref"]).max() <= 1e-2
