@@ -134,13 +134,12 @@ def test_eviction_without_warm_copy_writes_back(tmp_path):
     store = ExpertStore(model, cfg, ssd_dir=str(tmp_path / "c"))
     store.offload_from_state_dict(state)
     store.promote_to_vram(1)
-    with store._ram_lock:
-        store._ram_buffers.pop(1)          # warm copy gone
-    store.ram_lru.remove(1)
+    store.ram_lru.remove(1)                 # warm copy gone
+    assert store.ram_lru.get(1) is None
     for e in (2, 3):                        # evicts 1
         store.promote_to_vram(e)
     assert store.slot_of_expert()[1] == -1
-    got = store._ram_buffers[1][0]["gate_proj.weight"]
+    got = store.ram_lru.get(1)[0]["gate_proj.weight"]
     assert torch.equal(got, state["model.layers.0.mlp.experts.1.gate_proj.weight"])
 
 
@@ -269,3 +268,187 @@ def test_bookkeeping_resolves_from_pending_statistics():
     # a CUDA-less tensor mask is read back the same way
     lazy_t = _LazyOnDemand(torch.from_numpy(mask), live)
     assert [bool(lazy_t[e]) for e in range(4)] == [False, True, False, True]
+
+
+def test_slot_table_capacity_and_order():
+    """The device tier's residency record: slots reused coldest first, a lowered
+    capacity applied at the next promotion, scores re-ordering the victims."""
+    from project_chronos_b200.expert_store import SlotTable
+    t = SlotTable(num_experts=6, num_slots=3, capacity=3)
+    for e in (4, 1, 5):
+        assert t.victims_for(e) == []
+        t.occupy(e)
+    assert t.keys() == [4, 1, 5] and len(t) == 3 and t.contains(1) and not t.contains(0)
+    t.touch(4)
+    assert t.victims_for(0) == [1]
+    s1 = t.release(1)
+    assert t.occupy(0) == s1 and t.slot_of[0] == s1 and t.slot_of[1] == -1
+    t.reorder_by_score({5: 0.9, 4: 0.1, 0: 0.5})
+    assert t.keys() == [4, 0, 5]
+    t.capacity = 1
+    assert t.victims_for(2) == [4, 0, 5]
+
+
+def test_offload_from_state_reader_matches_state_dict(tmp_path):
+    """offload_from_state_reader (expert_store.py:276-312) writes the same shards
+    as offload_from_state_dict, reading each tensor through get_tensor."""
+    from project_chronos_b200 import ExpertStore
+    torch.manual_seed(5)
+    cfg = _cfg()
+    model = _Model(cfg)
+    state = _half_state(model)
+    reads = []
+
+    class Reader:
+        def keys(self):
+            return list(state.keys())
+
+        def get_tensor(self, key):
+            reads.append(key)
+            return state[key]
+
+    a = ExpertStore(model, cfg, ssd_dir=str(tmp_path / "a"))
+    a.offload_from_state_reader(Reader(), replace_live=False)
+    b = ExpertStore(_Model(cfg), cfg, ssd_dir=str(tmp_path / "b"))
+    b.offload_from_state_dict(state, replace_live=False)
+    assert a.storage_format == "pt"
+    assert sorted(reads) == sorted(k for k in state if ".mlp.experts." in k)
+    for li in range(2):
+        for ei in range(4):
+            x = torch.load(tmp_path / "a" / f"expert_l{li}_e{ei}.pt")
+            y = torch.load(tmp_path / "b" / f"expert_l{li}_e{ei}.pt")
+            assert sorted(x) == sorted(y) == ["down_proj.weight", "gate_proj.weight", "up_proj.weight"]
+            assert all(torch.equal(x[k], y[k]) and x[k].dtype == torch.float16 for k in x)
+
+
+def test_warm_loader_reads_in_background(tmp_path, monkeypatch):
+    """prefetch_experts_to_ram returns without touching the disk once the loader
+    runs (async_prefetcher.py:81-138): with 150 ms per simulated SSD read the
+    call returns at once and the experts turn warm later."""
+    import time
+    from project_chronos_b200 import CacheManager
+    torch.manual_seed(6)
+    cfg = _cfg(E=6, budget_experts=3)
+    model = _Model(cfg)
+    mgr = CacheManager(model, cfg, ssd_dir=str(tmp_path / "w"))
+    mgr.expert_store.offload_from_state_dict(_half_state(model))
+    monkeypatch.setenv("CHRONOS_SIM_SSD_MS", "150")
+    mgr.start()
+    try:
+        t0 = time.monotonic()
+        assert mgr.prefetch_experts_to_ram([4, 5, 4]) == [4, 5]
+        assert time.monotonic() - t0 < 0.1
+        assert not mgr.expert_store.ram_lru.contains(4)
+        assert mgr.prefetcher.wait_for(5, timeout=5.0)
+        assert mgr.prefetcher.drain(5.0)
+        assert mgr.expert_store.ram_lru.contains(4)
+        st = mgr.stats()
+        assert st["total_requests"] == 2 and st["prefetch_hits"] == 1 and "hit_rate" in st
+    finally:
+        mgr.stop()
+
+
+def test_warm_loader_drops_the_oldest_request_when_full(tmp_path, monkeypatch):
+    from project_chronos_b200.cache_manager import WarmLoader
+    from project_chronos_b200 import ExpertStore
+    cfg = _cfg(E=6, budget_experts=3)
+    model = _Model(cfg)
+    store = ExpertStore(model, cfg, ssd_dir=str(tmp_path / "q"))
+    store.offload_from_state_dict(_half_state(model))
+    monkeypatch.setenv("CHRONOS_SIM_SSD_MS", "200")
+    loader = WarmLoader(store, queue_depth=1)
+    loader.start()
+    try:
+        loader.submit([0])          # taken by the worker (busy ~200 ms)
+        import time
+        time.sleep(0.05)
+        loader.submit([1])          # queued
+        loader.submit([2])          # queue full: [1] dropped
+        assert loader.drain(5.0)
+        assert store.ram_lru.contains(0) and store.ram_lru.contains(2)
+        assert not store.ram_lru.contains(1)
+        assert loader.stats["dropped"] == 1
+    finally:
+        loader.stop()
+
+
+def test_prefetch_for_next_step_and_step(tmp_path):
+    """prefetch_for_next_step (cache_manager.py:94-98 -> async_prefetcher.py:198-223):
+    per future step of the last token, the top-k experts of every row; step()
+    promotes the current experts, queues the predictions and syncs."""
+    from project_chronos_b200 import CacheManager
+    cfg = _cfg(E=6, k=2, budget_experts=3)
+    model = _Model(cfg)
+    mgr = CacheManager(model, cfg, ssd_dir=str(tmp_path / "s"))
+    mgr.expert_store.offload_from_state_dict(_half_state(model))
+    lp = torch.zeros(2, 3, 3, 6)          # [B, S, K+1, E]
+    lp[0, -1, 1, [5, 1]] = torch.tensor([0.6, 0.3])
+    lp[1, -1, 1, [1, 2]] = torch.tensor([0.5, 0.4])
+    lp[0, -1, 2, [0, 3]] = torch.tensor([0.7, 0.2])
+    lp[1, -1, 2, [3, 4]] = torch.tensor([0.8, 0.1])
+    lp[:, -1, 0, 2] = 1.0                 # the current step is not a prediction
+    assert mgr.predicted_experts(lp) == [[1, 2, 5], [0, 3, 4]]
+    assert mgr.prefetch_for_next_step(lp) == [1, 2, 5, 0, 3, 4]
+    assert all(mgr.expert_store.ram_lru.contains(e) for e in (0, 1, 2, 3, 4, 5))  # not started: read inline
+    assert mgr.prefetch_for_next_step(None) == []
+    mgr.step(lp, [4, 0])
+    assert mgr.availability_mask().tolist() == [True, False, False, False, True, False]
+
+
+def test_reads_cluster_files_written_by_the_reference():
+    """.ctsr files and manifest written by the reference's ClusterStorage.write_clusters
+    (chronos/io/storage.py:182-233) load here with the weights they were given."""
+    from project_chronos_b200 import synthetic as syn
+    from project_chronos_b200.cluster_storage import ClusterStorage
+    from tests import _golden as G
+    root, c = G.ctsr_fixture()
+    cs = ClusterStorage(root)
+    m = cs.manifest
+    assert m.num_experts == c["E"] and m.num_layers == c["L"]
+    assert [cs.experts_in_cluster(i) for i in range(len(c["clusters"]))] == c["clusters"]
+    want = [syn.make_workload(syn.MoEShape(c["H"], c["E"], 2, c["F"], c["S"]), 1, seed=s).weights
+            for s in c["seeds"]]
+    for cid, members in enumerate(c["clusters"]):
+        nested = cs.load_cluster(cid, pin=False)
+        assert sorted(nested) == sorted(members)
+        for e in members:
+            assert cs.cluster_for_expert(e) == cid
+            for li in range(c["L"]):
+                st = nested[e][li]
+                assert st["gate_proj.weight"].dtype == torch.float16
+                assert torch.equal(st["gate_proj.weight"], want[li].gate[e].half())
+                assert torch.equal(st["up_proj.weight"], want[li].up[e].half())
+                assert torch.equal(st["down_proj.weight"], want[li].down[e].half())
+
+
+def test_store_serves_the_reference_written_clusters(tmp_path):
+    """An ExpertStore attached to the reference-written cluster directory reads a
+    whole cluster per request into the warm tier."""
+    import shutil
+    from project_chronos_b200 import ExpertStore
+    from tests import _golden as G
+    root, c = G.ctsr_fixture()
+    cfg = _cfg(E=c["E"], H=c["H"], F=c["F"], budget_experts=2)
+    cfg.storage_format = "safetensors"
+    shutil.copytree(root, tmp_path / "ref")
+    model = _Model(cfg, layers=c["L"])
+    store = ExpertStore(model, cfg, ssd_dir=str(tmp_path / "ref"))
+    assert store.stats()["cluster_aware"] is True
+    store.replace_live_experts_with_placeholders()
+    store.prefetch_to_ram([3])
+    assert store.ram_lru.contains(1) and store.ram_lru.contains(3) and not store.ram_lru.contains(0)
+    assert store.promote_to_vram(3) is True
+    assert store.vram_availability_mask().tolist() == [False, False, False, True]
+
+
+def test_bookkeeping_uses_the_mask_of_the_call():
+    """The on-demand statistics are resolved lazily, but from the mask as it was
+    at forward time: a caller that updates its mask in place afterwards does not
+    change them (the reference fills its lists during forward)."""
+    from project_chronos_b200.moe import _LazyOnDemand
+    mask = torch.tensor([1.0, 0.0, 0.0, 1.0])
+    live = np.array([1, 1, 0, 1], dtype=np.float32)
+    snap = np.array(mask.detach().to(torch.float32).numpy(), copy=True)
+    lazy = _LazyOnDemand(snap, live)
+    mask.zero_()
+    assert [bool(lazy[e]) for e in range(4)] == [False, True, False, False]

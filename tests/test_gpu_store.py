@@ -204,3 +204,103 @@ def test_cluster_cold_tier_promotes_from_pinned_views(tmp_path):
     torch.cuda.synchronize()
     assert store.stats()["cluster_aware"] is True
     assert _rel(y_lazy, y_full) <= 1e-2
+
+
+def _engine_hooks(mgr, policy):
+    """The hooks the reference's engine installs (inference_engine.py:118-167):
+    a miss already warm (or any miss under sync_on_demand) is promoted; a cold
+    miss under on_demand is queued for the background reader and falls back."""
+    store = mgr.expert_store
+
+    def load_one(eid):
+        eid = int(eid)
+        if store.vram_lru.contains(eid) or store.ram_lru.contains(eid) or policy == "sync_on_demand":
+            mgr.ensure_resident([eid])
+            return {"ok": store.vram_lru.contains(eid)}
+        mgr.prefetch_experts_to_ram([eid])
+        return {"ok": False}
+
+    return load_one, store.touch_expert
+
+
+@pytest.mark.parametrize("policy", ["sync_on_demand", "on_demand"])
+def test_decode_loop_replay(tmp_path, monkeypatch, policy):
+    """The reference's decode-step call sequence (inference_engine.py:600-663)
+    against the drop-ins: prefetch_experts_to_ram and prefetch_for_next_step of
+    the previous step's lookahead predictions, ensure_resident of the warm
+    candidates, availability_masks_all_layers, then every layer's forward with
+    the engine's runtime hooks.  The SSD is slowed to 100 ms per read: the
+    prefetch calls must not wait for one (each stays under half a read, though
+    the background reader competes for the host meanwhile).  sync_on_demand must reproduce the
+    full-resident model; on_demand must equal the blend with the fallbacks the
+    layer reports (cold misses go to the shared expert)."""
+    import time
+    from oracle import moe_oracle as O
+    from project_chronos_b200 import CacheManager
+    cfg = _cfg(E=8, budget_experts=4)
+    cfg.lookahead_steps = 2
+    L, B, dtype = 2, 2, torch.bfloat16
+    full, lazy, state = _pair(cfg, L, dtype, seed=7)
+    mgr = CacheManager(lazy, cfg, ssd_dir=str(tmp_path / "loop"))
+    store = mgr.expert_store
+    store.offload_from_state_dict(state)
+    mgr.start()
+    monkeypatch.setenv("CHRONOS_SIM_SSD_MS", "100")
+    load_one, touch_one = _engine_hooks(mgr, policy)
+    for blk in lazy.model.layers:
+        blk.mlp.runtime_miss_policy = policy
+        blk.mlp.runtime_on_demand_loader = load_one
+        blk.mlp.runtime_touch_expert = touch_one
+    g = torch.Generator(device=DEV).manual_seed(11)
+    prev_lp = None
+    slowest_prefetch = 0.0
+    try:
+        mgr.warm_up([0, 1])
+        for step in range(6):
+            if prev_lp is not None:
+                t0 = time.monotonic()
+                ram_ids = sorted({e for ids in mgr.predicted_experts(prev_lp) for e in ids})
+                mgr.prefetch_experts_to_ram(ram_ids)
+                mgr.prefetch_for_next_step(prev_lp)
+                slowest_prefetch = max(slowest_prefetch, time.monotonic() - t0)
+                ready = [e for e in ram_ids if store.vram_lru.contains(e) or store.ram_lru.contains(e)]
+                mgr.ensure_resident(ready[:store.vram_capacity])
+            masks = mgr.availability_masks_all_layers()
+            x = torch.randn(B, 1, cfg.hidden_size, device=DEV, generator=g).to(dtype)
+            xl_full, xl_lazy = x, x
+            with torch.no_grad():
+                for li in range(L):
+                    f_moe, l_moe = full.model.layers[li].mlp, lazy.model.layers[li].mlp
+                    y_full = f_moe(xl_full)
+                    y_lazy = l_moe(xl_lazy, available_expert_mask=masks[li])
+                    torch.cuda.synchronize()
+                    if policy == "sync_on_demand":
+                        assert l_moe.last_fallback_experts == []
+                        assert _rel(y_lazy, y_full) <= 1e-2, (step, li)
+                    else:
+                        a = np.ones(cfg.num_experts, np.float32)
+                        a[l_moe.last_fallback_experts] = 0.0
+                        sd = {k: v.float().cpu().numpy() for k, v in f_moe.state_dict().items()}
+                        stack = lambda n: np.stack([sd[f"experts.{e}.{n}.weight"]  # noqa: E731
+                                                    for e in range(cfg.num_experts)])
+                        want, *_ = O.moe_forward(
+                            xl_lazy.float().cpu().numpy().reshape(B, -1), sd["gate.weight"],
+                            stack("gate_proj"), stack("up_proj"), stack("down_proj"),
+                            sd["shared_experts.0.gate_proj.weight"][None],
+                            sd["shared_experts.0.up_proj.weight"][None],
+                            sd["shared_experts.0.down_proj.weight"][None], cfg.num_experts_per_tok, True,
+                            avail=a)
+                        got = y_lazy.float().cpu().numpy().reshape(B, -1)
+                        assert O.rel_l2(got, want) <= 1e-2, (step, li)
+                    xl_full = xl_full + y_full
+                    xl_lazy = xl_lazy + (y_full if policy == "sync_on_demand" else y_lazy)
+            prev_lp = torch.softmax(torch.randn(B, 1, cfg.lookahead_steps + 1, cfg.num_experts,
+                                                device=DEV, generator=g), dim=-1)
+        assert slowest_prefetch < 0.05, slowest_prefetch
+        assert mgr.prefetcher.drain(10.0)
+        st = mgr.stats()
+        assert st["vram_experts"] <= store.vram_capacity and st["total_requests"] > 0
+    finally:
+        mgr.stop()
+    ops_status = __import__("project_chronos_b200").ops.check_status(torch.device(DEV))
+    assert ops_status == 0
