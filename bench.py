@@ -368,8 +368,12 @@ def run_ours(args, dist: Dist):
         for _ in range(max(1, args.warmup)):
             e2e_step()
         torch.cuda.synchronize()
+        # more steps than the device-timed loop: one host pause (another process
+        # on the host, the OS) then moves the mean by a fraction, and the
+        # per-step distribution shows whether the mean is such a pause
+        KE = max(K, E2E_MIN_STEPS)
         eev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(K)]
+               for _ in range(KE)]
         dist.barrier()
         torch.cuda.synchronize()
         # the timed steps include host-side Python: a full collection before them
@@ -377,7 +381,7 @@ def run_ours(args, dist: Dist):
         gc.collect()
         gc.disable()
         try:
-            for i in range(K):
+            for i in range(KE):
                 flush.zero_()
                 eev[i][0].record()
                 e2e_step()
@@ -389,7 +393,8 @@ def run_ours(args, dist: Dist):
                               rtol=1e-2, atol=1e-2):
             raise RuntimeError("end-to-end output disagrees with the graph-replayed layer")
         dist.barrier()
-        e2e_ms = dist.max(sum(s.elapsed_time(e) for s, e in eev)) / K
+        e2e_steps_ms = np.array([s.elapsed_time(e) for s, e in eev])
+        e2e_ms = dist.max(float(e2e_steps_ms.sum())) / KE
         h2d = sum(x_host[b].numel() * x_host[b].element_size() for b in DECODE_BATCHES)
         d2h = sum(y_host[b].numel() * y_host[b].element_size() for b in DECODE_BATCHES)
 
@@ -458,31 +463,21 @@ def run_ours(args, dist: Dist):
                                       if s != "calls"})
     e2e = dict(value=round(tokens_step * dist.world / (e2e_ms / 1e3), 1), unit="tokens/s",
                h2d_bytes_per_step=int(h2d), d2h_bytes_per_step=int(d2h),
-               ms_per_step=round(e2e_ms, 4),
+               ms_per_step=round(e2e_ms, 4), steps=int(KE),
+               median_ms=round(float(np.median(e2e_steps_ms)), 4),
+               p90_ms=round(float(np.percentile(e2e_steps_ms, 90)), 4),
+               max_ms=round(float(e2e_steps_ms.max()), 4),
+               over_device_step=round(e2e_ms / dec_ms_step, 3),
                path=("ChronosMOEFeedForward.forward (eager), pinned host x -> device -> host y, "
                      "copies on their own streams"))
 
     head = {"decode": decode, "prefill": prefill, "ep": ep}[args.workload]
-    workload_desc = {
-        "decode": ("decode: MoE layer d_model 2048, 64 experts top-6 + 2 shared, d_ff 1408 "
-                   "(DeepSeek-MoE-16B shape), batches 1/8/32/64, availability Bernoulli(0.9)"),
-        "prefill": "prefill: same layer, 8192 tokens, Zipf(1.1) router bias, all available",
-        "ep": ("expert parallel: MoE layer d_model 7168, 256 experts top-8 + 1 shared, d_ff 2048 "
-               "(DeepSeek-V3 shape), 4096 tokens per GPU, experts sharded evenly over the GPUs, "
-               "NCCL all-to-all dispatch/combine"),
-    }[args.workload]
     line = {
         "metric": head["metric"], "value": head["value"], "unit": head["unit"],
         "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, N(0,0.02) weights)",
-        "config": {
-            "workload": workload_desc,
-            "l2": "flushed before every timed call (256 MB write)",
-            "graphs": "decode calls replayed as CUDA graphs" if args.workload == "decode" else "eager",
-            "parallelism": (f"ep{dist.world} (experts sharded)" if args.workload == "ep"
-                            else f"replicas x{dist.world} (decode/prefill), ep{dist.world} (ep)"),
-        },
+        "config": bench_config(args, dist.world),
         "roofline": {"decode": dec_roof, "prefill": pre_roof, "ep": ep["roofline"]}[args.workload],
         "e2e": e2e,
         "clocks": clocks,
@@ -496,11 +491,34 @@ def run_ours(args, dist: Dist):
         "e2e_decode": e2e_dec,
     }
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(w, wl.x, mask_host, shape, args.workload,
-                                            xp_dev=xp, bias=bias)
+        line["cpu_baseline"], line["parity"] = cpu_baseline(
+            w, wl.x, mask_host, shape, args.workload, xp_dev=xp, bias=bias,
+            gpu_out={b: gouts[b].view(b, -1) for b in DECODE_BATCHES})
     return line
 
 
+WORKLOAD_DESC = {
+    "decode": ("decode: MoE layer d_model 2048, 64 experts top-6 + 2 shared, d_ff 1408 "
+               "(DeepSeek-MoE-16B shape), batches 1/8/32/64, availability Bernoulli(0.9)"),
+    "prefill": "prefill: same layer, 8192 tokens, Zipf(1.1) router bias, all available",
+    "ep": ("expert parallel: MoE layer d_model 7168, 256 experts top-8 + 1 shared, d_ff 2048 "
+           "(DeepSeek-V3 shape), 4096 tokens per GPU, experts sharded evenly over the GPUs, "
+           "NCCL all-to-all dispatch/combine"),
+}
+
+
+def bench_config(args, world: int) -> dict:
+    """The ``config`` of both arms' JSON lines (same workload, same keys)."""
+    return {
+        "workload": WORKLOAD_DESC[args.workload],
+        "l2": "flushed before every timed call (256 MB write)",
+        "graphs": "decode calls replayed as CUDA graphs" if args.workload == "decode" else "eager",
+        "parallelism": (f"ep{world} (experts sharded)" if args.workload == "ep"
+                        else f"replicas x{world} (decode/prefill), ep{world} (ep)"),
+    }
+
+
+E2E_MIN_STEPS = 200
 E2E_LAYERS = 8
 E2E_PROMPT = 512
 E2E_STEPS = 256
@@ -658,10 +676,23 @@ def run_ep(args, dist: Dist, dev, peaks, flush) -> dict:
     sc = m.last_send_counts or [n * k]
     remote_rows = sum(c for g, c in enumerate(sc) if g != dist.rank)
     a2a_bytes = remote_rows * H * 2
-    roof = dict(kernel="expert-parallel layer (all kernels + all-to-all), per GPU", bound="tensor",
-                achieved=round(tflops, 1), peak=peaks["bf16_tflops_sustained"], unit="TFLOP/s",
-                frac=round(tflops / peaks["bf16_tflops_sustained"], 4), traffic=None,
-                algorithmic_flops_per_step=flops, peak_source=peaks["source"] + " (sustained)")
+    # the floor that binds: the rank's expert weights read once (HBM) or its FLOPs
+    # at the sustained tensor peak (a seconds-long step sequence)
+    weight_bytes = 2.0 * (3 * H * F * (E // dist.world + S) + H * E)
+    t_hbm = weight_bytes / (peaks["hbm_gbs"] * 1e9)
+    t_tc = flops / (peaks["bf16_tflops_sustained"] * 1e12)
+    if t_hbm >= t_tc:
+        gbs = weight_bytes / (ms / 1e3) / 1e9
+        roof = dict(kernel="expert-parallel layer (all kernels + all-to-all), per GPU", bound="hbm",
+                    achieved=round(gbs, 1), peak=peaks["hbm_gbs"], unit="GB/s",
+                    frac=round(gbs / peaks["hbm_gbs"], 4), traffic=None,
+                    algorithmic_bytes_per_step=weight_bytes, peak_source=peaks["source"])
+    else:
+        roof = dict(kernel="expert-parallel layer (all kernels + all-to-all), per GPU", bound="tensor",
+                    achieved=round(tflops, 1), peak=peaks["bf16_tflops_sustained"], unit="TFLOP/s",
+                    frac=round(tflops / peaks["bf16_tflops_sustained"], 4), traffic=None,
+                    algorithmic_flops_per_step=flops, peak_source=peaks["source"] + " (sustained)")
+    roof["floors_ms"] = dict(weights_over_hbm=round(t_hbm * 1e3, 3), flops_over_tc=round(t_tc * 1e3, 3))
     return dict(metric="MoE-layer tokens/s (expert parallel, DeepSeek-V3 shape, 4096 tokens/GPU)",
                 value=round(n * dist.world / (ms / 1e3), 1), unit="tokens/s", ms_per_step=round(ms, 4),
                 steps=K, ranks=dist.world, experts_per_rank=E // dist.world,
@@ -697,31 +728,69 @@ def _oracle_call(cw, x, avail, shape, bias=None):
                          bias=bias)
 
 
-def cpu_baseline(w, x_dev, mask_host, shape, workload, xp_dev=None, bias=None, budget_s=15.0):
+def _published_literal_mismatches() -> dict:
+    """Literal bf16 reference routing vs the routing contract, per golden case
+    (counts and their classification as committed in tests/golden/cases.json)."""
+    try:
+        with open(os.path.join(REPO, "tests", "golden", "cases.json")) as f:
+            cases = json.load(f)["cases"]
+    except OSError:
+        return {}
+    return {c["name"]: {k: c["literal_bf16_routing"][k] for k in
+                        ("tokens", "mismatched_tokens", "bf16_tie", "logit_rounding", "other")}
+            for c in cases if "literal_bf16_routing" in c}
+
+
+def _decode_parity(x, w, cw, avail, shape, oracle_out, gpu_out) -> dict:
+    """The timed layer's decode outputs against the oracle on the same inputs:
+    top-k indices (bit-exact contract) and rel-L2 of the output."""
+    from oracle import moe_oracle as O
+    from project_chronos_b200 import ops
+    res = {}
+    for b in DECODE_BATCHES:
+        y_o, idx_o, _, _ = oracle_out[b]
+        r = ops.moe_route(x[:b], w.router, shape.top_k, shape.norm_topk, want_probs=False)
+        idx = r["topk_idx"].cpu().numpy()
+        res[str(b)] = dict(index_mismatches=int((idx != idx_o).any(axis=1).sum()),
+                           rel_l2=float(f"{O.rel_l2(gpu_out[b].float().cpu().numpy(), y_o):.3e}"))
+    return dict(decode_vs_oracle=res, tolerance="indices bit-exact, rel-L2 <= 1e-2 (bf16)",
+                literal_bf16_reference_vs_contract=_published_literal_mismatches())
+
+
+def cpu_baseline(w, x_dev, mask_host, shape, workload, xp_dev=None, bias=None, budget_s=15.0,
+                 gpu_out=None):
+    """(the timed oracle port on the host cores, parity of the GPU results on the
+    same inputs)."""
     cw = _cpu_weights(w)
     avail = mask_host.numpy().astype(np.float32)
+    parity = None
     if workload == "decode":
         x = x_dev.float().cpu().numpy()
         t0 = time.perf_counter()
         reps = 0
+        first = {}
         while True:
             for b in DECODE_BATCHES:
-                _oracle_call(cw, x[:b], avail, shape)
+                out = _oracle_call(cw, x[:b], avail, shape)
+                if b not in first:
+                    first[b] = out
             reps += 1
             if time.perf_counter() - t0 > budget_s or reps >= 5:
                 break
         dt = time.perf_counter() - t0
+        if gpu_out is not None:
+            parity = _decode_parity(x_dev, w, cw, avail, shape, first, gpu_out)
         return dict(value=round(reps * sum(DECODE_BATCHES) / dt, 2), unit="tokens/s",
                     cores=_threads(), kind="port",
                     sample=f"{reps} decode step(s) (batches 1/8/32/64) of the oracle port "
-                           "(C router + numpy/BLAS fp32 experts)")
+                           "(C router + numpy/BLAS fp32 experts)"), parity
     x = xp_dev[:512].float().cpu().numpy()
     b = bias.float().cpu().numpy()
     t0 = time.perf_counter()
     _oracle_call(cw, x, None, shape, bias=b)
     dt = time.perf_counter() - t0
     return dict(value=round(512 / dt, 2), unit="tokens/s", cores=_threads(), kind="port",
-                sample="512 of the 8192 prefill tokens through the oracle port")
+                sample="512 of the 8192 prefill tokens through the oracle port"), parity
 
 
 def run_reference(args, dist: Dist):
@@ -766,7 +835,8 @@ def run_reference(args, dist: Dist):
         "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": metric, "parallelism": "cpu (rank 0 only)"},
+        "config": bench_config(args, dist.world),
+        "host_side": "the oracle port on the host cores (rank 0 only), fp32",
         "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": cores,
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,

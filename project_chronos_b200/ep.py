@@ -24,7 +24,13 @@ call instead):
 
 Same arithmetic as the single-device layer (the blend of
 ``chronos/mlx/moe.py:160-166``); each routed contribution is rounded once to the
-layer dtype before the fp32 combine.  All compute runs in the sm_100a
+layer dtype before the fp32 combine.  ``available_expert_mask`` is applied as
+that arithmetic availability, a_e = mask[e], in eval as in training: every
+expert of a sharded layer is resident, so there is no live-but-marked-
+unavailable expert to run anyway, as the torch module does in eval
+(``moe_chronos.py:221-227``).  A mask with zeros therefore sends those
+experts' selections to the shared term here, while
+``ChronosMOEFeedForward`` in eval would still run its loaded experts.  All compute runs in the sm_100a
 extension; ``backend`` exists so the host orchestration can be exercised
 with CPU stand-ins in tests.
 """

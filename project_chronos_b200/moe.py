@@ -462,10 +462,11 @@ class ChronosMOEFeedForward(nn.Module):
                 avail_dev = (mask_t.to(torch.float32) > 0).to(torch.float32) * \
                     torch.from_numpy(live).to(dev)
             else:
-                mask_np = mask_t.detach().to(torch.float32).numpy()
+                mask_np = np.array(mask_t.detach().to(torch.float32).numpy(), copy=True)
                 avail_dev = None
         if masked and available_expert_mask is not None and not available_expert_mask.is_cuda:
-            mask_np = available_expert_mask.detach().to(torch.float32).numpy()
+            # a snapshot: the statistics read later must see the mask of this call
+            mask_np = np.array(available_expert_mask.detach().to(torch.float32).numpy(), copy=True)
 
         bias = self.router_logit_bias
         probs = None
@@ -610,8 +611,9 @@ class ChronosMOEFeedForward(nn.Module):
                     a_np = avail_t.cpu().numpy()
                 if eval_with_mask and mask_np is None:
                     # CUDA mask in eval: read lazily together with the counts
-                    _set(self, "_stats_pending", dict(counts=out["counts"], mass=out["mass"], a=a_np,
-                                                      on_demand=_LazyOnDemand(available_expert_mask, live)))
+                    _set(self, "_stats_pending", dict(
+                        counts=out["counts"], mass=out["mass"], a=a_np,
+                        on_demand=_LazyOnDemand(available_expert_mask.detach().clone(), live)))
                 else:
                     _set(self, "_stats_pending", dict(counts=out["counts"], mass=out["mass"], a=a_np,
                                                       on_demand=on_demand))

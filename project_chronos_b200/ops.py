@@ -158,15 +158,57 @@ def _raw_stream(index: int) -> int:
     return torch.cuda.current_stream(index).cuda_stream
 
 
+class _SharedWorkspace:
+    """One workspace per (device, stream), shared by every layer that runs there.
+
+    Calls on one stream run one after another, so every layer can use the same
+    buffer; it grows to the largest size requested and never shrinks (a
+    smaller call uses a prefix: the extension only requires ``workspace_bytes
+    >= need``).  A buffer is allocated while its stream is the current stream,
+    so when a larger one replaces it the caching allocator hands the old block
+    out again only after the work already queued on that stream.  The memory
+    held is the workspace of the largest call per stream, e.g. ~0.45 GB for
+    8192 tokens of the d_model 2048, 64-expert top-6 layer (~9.4 MB for 64).
+
+    A buffer that a CUDA graph captured is never freed: the graph replays
+    into its address, so when it is outgrown it is retired, not released."""
+
+    def __init__(self):
+        self._bufs: Dict[tuple, torch.Tensor] = {}
+        self._captured: set = set()              # data_ptr of buffers a graph holds
+        self._retired: List[torch.Tensor] = []    # outgrown buffers graphs still hold
+
+    def get(self, dev: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+        key = (dev.index, stream)
+        buf = self._bufs.get(key)
+        if buf is None or buf.numel() < nbytes:
+            if buf is not None and buf.data_ptr() in self._captured:
+                self._retired.append(buf)
+            # round up so that slowly growing token counts do not reallocate every call
+            buf = torch.empty(max(256, nbytes + nbytes // 8), dtype=torch.uint8, device=dev)
+            self._bufs[key] = buf
+        if torch.cuda.is_current_stream_capturing():
+            self._captured.add(buf.data_ptr())
+        return buf
+
+    def release(self) -> None:
+        """Drop the cached buffers no captured graph holds (call when no layer
+        call is in flight)."""
+        self._bufs = {k: b for k, b in self._bufs.items() if b.data_ptr() in self._captured}
+
+
+shared_workspace = _SharedWorkspace()
+
+
 class LayerCall:
     """One layer's static arguments bound once, for repeated calls with little host work.
 
     ``LayerCall(router_w, w_gate, ...)(x, avail=...)`` computes what
     ``moe_forward`` computes.  The weights, pools, slot map, ready flags and
     router bias are checked and converted once; each call allocates only its
-    outputs, reuses a workspace per token count (calls are ordered on the
-    current stream, so the reuse is safe on one stream) and copies a prebuilt
-    argument struct.  Rebuild it when any bound tensor is replaced."""
+    outputs, takes the workspace shared by all layers on the current stream
+    (``shared_workspace``) and copies a prebuilt argument struct.  Rebuild it
+    when any bound tensor is replaced."""
 
     def __init__(self, router_w, w_gate, w_up, w_down, sh_gate, sh_up, sh_down, top_k: int,
                  norm_topk: bool, router_bias=None, slot_of_expert=None, ready_flags=None,
@@ -198,20 +240,19 @@ class LayerCall:
             w_shared_up=_ptr(su), w_shared_down=_ptr(sd), ready_flags=_ptr(ready_flags),
             ready_epoch=int(ready_epoch), spin_limit_ns=int(spin_limit_ns),
             status=_ptr(status_word(self.dev)))
-        self._ws = {}
+        self._need = {}   # token count -> workspace bytes
 
-    def _workspace(self, n: int) -> torch.Tensor:
-        ws = self._ws.get(n)
-        if ws is None:
+    def _workspace_bytes(self, n: int) -> int:
+        size = self._need.get(n)
+        if size is None:
             shp = _shape(n, self.h, self.e, self.k, self.f, self.s, self.dtype)
             size = int(self._lib.chronos_moe_workspace_size(ctypes.byref(shp)))
             if size == 0 and n > 0:
                 N.check(N.CHRONOS_ERR_INVALID_ARG)
-            ws = torch.empty(max(size, 256), dtype=torch.uint8, device=self.dev)
-            if len(self._ws) > 16:
-                self._ws.clear()
-            self._ws[n] = ws
-        return ws
+            if len(self._need) > 64:
+                self._need.clear()
+            self._need[n] = size
+        return size
 
     def __call__(self, x: torch.Tensor, avail: Optional[torch.Tensor] = None, want_probs: bool = True,
                  want_stats: bool = False, want_topk: bool = False) -> dict:
@@ -220,7 +261,8 @@ class LayerCall:
         x = x.contiguous()
         n = x.shape[0]
         dev = self.dev
-        ws = self._workspace(n)
+        stream = _raw_stream(dev.index)
+        ws = shared_workspace.get(dev, stream, self._workspace_bytes(n))
         y = torch.empty(n, self.h, dtype=self.dtype, device=dev)
         probs = torch.empty(n, self.e, dtype=self.dtype, device=dev) if want_probs else None
         topk_idx = torch.empty(n, self.k, dtype=torch.int32, device=dev) if want_topk else None
@@ -242,7 +284,6 @@ class LayerCall:
         a.expert_mass = _ptr(mass)
         a.workspace = ws.data_ptr()
         a.workspace_bytes = ws.numel()
-        stream = _raw_stream(dev.index)
         if torch.cuda.current_device() == dev.index:
             rc = self._lib.chronos_moe_forward(ctypes.byref(a), ctypes.c_void_p(stream))
         else:

@@ -120,3 +120,45 @@ def test_two_ranks_nccl_match_single_device():
         assert status == "ok", val
         assert val <= 1e-2, (rank, val)
     assert res[0][3][1] == res[1][4][0] and res[1][3][0] == res[0][4][1]
+
+
+def test_mask_is_the_arithmetic_availability_in_eval():
+    """ExpertParallelMoE applies the mask as a_e = mask[e] (the blend of
+    chronos/mlx/moe.py:160-166) in eval too, while ChronosMOEFeedForward in eval
+    runs a loaded expert even where the mask says unavailable
+    (moe_chronos.py:221-227): on the same layer and mask the two differ, each
+    as the oracle predicts."""
+    import types
+    from oracle import moe_oracle as O
+    from project_chronos_b200 import ChronosMOEFeedForward
+    from project_chronos_b200.ep import ExpertParallelMoE
+    H, E, k, F = 256, 8, 2, 128
+    cfg = types.SimpleNamespace(hidden_size=H, num_experts=E, num_experts_per_tok=k,
+                                moe_intermediate_size=F, num_shared_experts=1, norm_topk_prob=True,
+                                router_aux_loss_coef=0.0, hidden_act="silu", dropout=0.0,
+                                fallback_mask_prob=0.0, intermediate_size=F)
+    torch.manual_seed(0)
+    layer = ChronosMOEFeedForward(cfg)
+    with torch.no_grad():
+        for p in layer.parameters():
+            p.normal_(0.0, 0.05)
+    layer = layer.to(DEV).eval()
+    ep = ExpertParallelMoE.from_layer(layer)
+    x = torch.randn(1, 24, H, device=DEV)
+    mask = torch.tensor([1, 0, 1, 1, 0, 1, 1, 1], dtype=torch.bool)
+    with torch.no_grad():
+        y_layer = layer(x, available_expert_mask=mask)
+        y_ep = ep(x, available_expert_mask=mask)
+    torch.cuda.synchronize()
+    sd = {kk: v.float().cpu().numpy() for kk, v in layer.state_dict().items()}
+    st = lambda n: np.stack([sd[f"experts.{e}.{n}.weight"] for e in range(E)])  # noqa: E731
+    args = (x.cpu().numpy().reshape(-1, H), sd["gate.weight"], st("gate_proj"), st("up_proj"),
+            st("down_proj"), sd["shared_experts.0.gate_proj.weight"][None],
+            sd["shared_experts.0.up_proj.weight"][None], sd["shared_experts.0.down_proj.weight"][None],
+            k, True)
+    want_live, idx, _, _ = O.moe_forward(*args)
+    want_blend, _, _, _ = O.moe_forward(*args, avail=mask.float().numpy())
+    assert (np.isin(idx, [1, 4])).any()
+    assert O.rel_l2(y_layer.cpu().numpy().reshape(-1, H), want_live) <= 1e-5
+    assert O.rel_l2(y_ep.cpu().numpy().reshape(-1, H), want_blend) <= 1e-5
+    assert O.rel_l2(want_live, want_blend) > 1e-3
