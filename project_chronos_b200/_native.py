@@ -1,4 +1,5 @@
-"""ctypes binding of the C ABI declared in include/chronos_moe.h.
+"""ctypes binding of the C ABI declared in include/chronos_moe.h (and the
+expert-parallel, lookahead and attention headers beside it).
 
 The library is ``project_chronos_b200/libchronos_moe.so`` (built in-tree by
 ``project_chronos_b200.build``).  Loading fails loudly: there is no other
@@ -44,7 +45,9 @@ EXPORTS = ("chronos_moe_workspace_size", "chronos_moe_forward", "chronos_moe_rou
            "chronos_moe_profile_begin", "chronos_moe_profile_end",
            "chronos_moe_kernel_launches", "chronos_moe_forward_noalloc",
            "chronos_ep_dispatch", "chronos_ep_combine", "chronos_ep_dispatch_args_size",
-           "chronos_ep_combine_args_size", "chronos_lookahead_forward", "chronos_lookahead_args_size")
+           "chronos_ep_combine_args_size", "chronos_lookahead_forward", "chronos_lookahead_args_size",
+           "chronos_mla_decode", "chronos_sw_decode", "chronos_add_rmsnorm", "chronos_attn_args_size",
+           "chronos_norm_args_size")
 
 EP_MAX_RANKS = 32  # CHRONOS_EP_MAX_RANKS
 
@@ -151,6 +154,51 @@ class ChronosLookaheadArgs(ctypes.Structure):
     ]
 
 
+class ChronosAttnArgs(ctypes.Structure):
+    """include/chronos_attention.h"""
+    _fields_ = [
+        ("batch", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("rope_dim", ctypes.c_int32),
+        ("latent", ctypes.c_int32),
+        ("window", ctypes.c_int32),
+        ("max_len", ctypes.c_int32),
+        ("table_len", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+        ("pos", ctypes.c_void_p),
+        ("proj", ctypes.c_void_p),
+        ("norm_q", ctypes.c_void_p),
+        ("norm_q2", ctypes.c_void_p),
+        ("norm_kv", ctypes.c_void_p),
+        ("w_krope", ctypes.c_void_p),
+        ("w_knope", ctypes.c_void_p),
+        ("w_v", ctypes.c_void_p),
+        ("cos", ctypes.c_void_p),
+        ("sin", ctypes.c_void_p),
+        ("cache_a", ctypes.c_void_p),
+        ("cache_b", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+    ]
+
+
+class ChronosNormArgs(ctypes.Structure):
+    """include/chronos_attention.h"""
+    _fields_ = [
+        ("rows", ctypes.c_int64),
+        ("width", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+        ("x", ctypes.c_void_p),
+        ("residual", ctypes.c_void_p),
+        ("sum_out", ctypes.c_void_p),
+        ("weight", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -206,6 +254,17 @@ def load_library(path: str = LIB_PATH):
         lib.chronos_lookahead_forward.restype = ctypes.c_int
         lib.chronos_lookahead_args_size.argtypes = []
         lib.chronos_lookahead_args_size.restype = ctypes.c_size_t
+        for fn, st in (("chronos_mla_decode", ChronosAttnArgs), ("chronos_sw_decode", ChronosAttnArgs),
+                       ("chronos_add_rmsnorm", ChronosNormArgs)):
+            getattr(lib, fn).argtypes = [ctypes.POINTER(st), ctypes.c_void_p]
+            getattr(lib, fn).restype = ctypes.c_int
+        lib.chronos_attn_args_size.argtypes = []
+        lib.chronos_attn_args_size.restype = ctypes.c_size_t
+        lib.chronos_norm_args_size.argtypes = []
+        lib.chronos_norm_args_size.restype = ctypes.c_size_t
+        if (lib.chronos_attn_args_size() != ctypes.sizeof(ChronosAttnArgs)
+                or lib.chronos_norm_args_size() != ctypes.sizeof(ChronosNormArgs)):
+            raise RuntimeError("attention args layout mismatch between the library and the binding")
         if lib.chronos_lookahead_args_size() != ctypes.sizeof(ChronosLookaheadArgs):
             raise RuntimeError("lookahead args layout mismatch between the library and the binding")
         if (lib.chronos_ep_dispatch_args_size() != ctypes.sizeof(ChronosEpDispatchArgs)

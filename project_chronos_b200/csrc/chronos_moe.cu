@@ -19,10 +19,12 @@
 #include <unordered_map>
 #include <vector>
 
+#include "chronos_attention.h"
 #include "chronos_ep.h"
 #include "chronos_lookahead.h"
 #include "chronos_moe.h"
 #include "common.cuh"
+#include "attention.cuh"
 #include "ep.cuh"
 #include "lookahead.cuh"
 #include "gemm_simt.cuh"
@@ -1100,3 +1102,186 @@ extern "C" int chronos_lookahead_forward(const ChronosLookaheadArgs* a, void* st
 }
 
 extern "C" size_t chronos_lookahead_args_size(void) { return sizeof(ChronosLookaheadArgs); }
+
+// ---------------------------------------------------------------------------
+// hybrid-attention decode and residual add + RMSNorm (include/chronos_attention.h)
+// ---------------------------------------------------------------------------
+namespace chronos {
+namespace {
+
+constexpr int kAttnMaxSmem = 200 << 10;
+
+bool known_dtype(int32_t d) {
+    return d == CHRONOS_DTYPE_BF16 || d == CHRONOS_DTYPE_FP16 || d == CHRONOS_DTYPE_FP32;
+}
+
+int attn_common_checks(const ChronosAttnArgs* a, const char* what) {
+    if (a == nullptr) return fail(CHRONOS_ERR_INVALID_ARG, "%s: args is NULL", what);
+    if (a->batch < 0 || a->heads < 1 || a->kv_heads < 1 || a->heads % a->kv_heads != 0 ||
+        a->heads / a->kv_heads > kAttnMaxRep)
+        return fail(CHRONOS_ERR_INVALID_ARG, "%s: batch %d, heads %d, kv_heads %d (heads must be a "
+                    "multiple of kv_heads, at most %d per kv head)", what, a->batch, a->heads, a->kv_heads,
+                    kAttnMaxRep);
+    if (a->head_dim < 2 || a->head_dim > 256 || (a->head_dim & 1))
+        return fail(CHRONOS_ERR_INVALID_ARG, "%s: head_dim %d (even, <= 256)", what, a->head_dim);
+    if (!known_dtype(a->dtype)) return fail(CHRONOS_ERR_INVALID_ARG, "%s: dtype %d unknown", what, a->dtype);
+    if (a->table_len < 1) return fail(CHRONOS_ERR_INVALID_ARG, "%s: table_len %d", what, a->table_len);
+    if (a->batch > 0 && (a->pos == nullptr || a->proj == nullptr || a->norm_q == nullptr ||
+                         a->norm_q2 == nullptr || a->cos == nullptr || a->sin == nullptr ||
+                         a->cache_a == nullptr || a->cache_b == nullptr || a->out == nullptr))
+        return fail(CHRONOS_ERR_INVALID_ARG, "%s: a required pointer is NULL", what);
+    return CHRONOS_OK;
+}
+
+AttnParams attn_params(const ChronosAttnArgs* a) {
+    AttnParams p{};
+    p.heads = a->heads;
+    p.kv_heads = a->kv_heads;
+    p.rep = a->heads / a->kv_heads;
+    p.head_dim = a->head_dim;
+    p.rope_dim = a->rope_dim;
+    p.nope = a->head_dim - a->rope_dim;
+    p.latent = a->latent;
+    p.window = a->window;
+    p.max_len = a->max_len;
+    p.table_len = a->table_len;
+    p.eps = a->eps;
+    p.scale = 1.0f / sqrtf(static_cast<float>(a->head_dim));
+    p.pos = a->pos;
+    p.proj = a->proj;
+    p.norm_q = a->norm_q;
+    p.norm_q2 = a->norm_q2;
+    p.norm_kv = a->norm_kv;
+    p.w_krope = a->w_krope;
+    p.w_knope = a->w_knope;
+    p.w_v = a->w_v;
+    p.cos = a->cos;
+    p.sin = a->sin;
+    p.cache_a = a->cache_a;
+    p.cache_b = a->cache_b;
+    p.out = a->out;
+    return p;
+}
+
+// Shared memory of one decode block, in the order the kernels lay it out.
+size_t mla_smem(const AttnParams& p) {
+    const size_t rep = static_cast<size_t>(p.rep);
+    return sizeof(float) * (rep * p.nope               // qn
+                            + rep * p.rope_dim         // qr
+                            + 2 * rep * p.latent       // qabs, ctx
+                            + p.latent + p.rope_dim    // cnew, krn
+                            + (rep + 1) * p.rope_dim   // tmp
+                            + rep * p.max_len);        // scores
+}
+
+size_t sw_smem(const AttnParams& p) {
+    const size_t rep = static_cast<size_t>(p.rep);
+    return sizeof(float) * (rep * p.head_dim           // q
+                            + 2 * p.head_dim           // kn, vn
+                            + (rep + 1) * p.head_dim   // tmp
+                            + rep * p.window);         // scores
+}
+
+template <typename T>
+int mla_impl(const AttnParams& p, int batch, cudaStream_t st) {
+    const int smem = static_cast<int>(mla_smem(p));
+    if (int rc = set_smem(mla_decode_kernel<T>, smem)) return rc;
+    CHRONOS_CUDA_CHECK(launch_kernel(mla_decode_kernel<T>, dim3(p.kv_heads, batch), dim3(kAttnThreads), smem,
+                                     st, false, p));
+    return CHRONOS_OK;
+}
+
+template <typename T>
+int sw_impl(const AttnParams& p, int batch, cudaStream_t st) {
+    const int smem = static_cast<int>(sw_smem(p));
+    if (int rc = set_smem(sw_decode_kernel<T>, smem)) return rc;
+    CHRONOS_CUDA_CHECK(launch_kernel(sw_decode_kernel<T>, dim3(p.kv_heads, batch), dim3(kAttnThreads), smem,
+                                     st, false, p));
+    return CHRONOS_OK;
+}
+
+template <typename T>
+int norm_impl(const ChronosNormArgs* a, cudaStream_t st) {
+    NormParams p{};
+    p.rows = a->rows;
+    p.width = a->width;
+    p.eps = a->eps;
+    p.x = a->x;
+    p.residual = a->residual;
+    p.sum_out = a->sum_out;
+    p.weight = a->weight;
+    p.out = a->out;
+    const int smem = static_cast<int>(sizeof(float) * (a->width + kAttnWarps));
+    if (int rc = set_smem(add_rmsnorm_kernel<T>, smem)) return rc;
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(a->rows, 1 << 20));
+    CHRONOS_CUDA_CHECK(launch_kernel(add_rmsnorm_kernel<T>, dim3(grid), dim3(kAttnThreads), smem, st, false, p));
+    return CHRONOS_OK;
+}
+
+}  // namespace
+}  // namespace chronos
+
+extern "C" int chronos_mla_decode(const ChronosAttnArgs* a, void* stream) {
+    using namespace chronos;
+    g_last_error.clear();
+    if (int rc = attn_common_checks(a, "chronos_mla_decode")) return rc;
+    if (a->rope_dim < 2 || (a->rope_dim & 1) || a->rope_dim >= a->head_dim || a->latent < 1 ||
+        a->latent > 256 || a->max_len < 1 || a->max_len > 8192)
+        return fail(CHRONOS_ERR_INVALID_ARG, "chronos_mla_decode: rope_dim %d (even, < head_dim %d), latent %d "
+                    "(1..256), max_len %d (1..8192)", a->rope_dim, a->head_dim, a->latent, a->max_len);
+    if (a->batch > 0 && (a->norm_kv == nullptr || a->w_krope == nullptr || a->w_knope == nullptr ||
+                         a->w_v == nullptr))
+        return fail(CHRONOS_ERR_INVALID_ARG, "chronos_mla_decode: norm_kv, w_krope, w_knope and w_v are required");
+    const AttnParams p = attn_params(a);
+    if (mla_smem(p) > static_cast<size_t>(kAttnMaxSmem))
+        return fail(CHRONOS_ERR_INVALID_ARG, "chronos_mla_decode: max_len %d x %d heads per kv head needs %zu "
+                    "bytes of shared memory (limit %d)", a->max_len, p.rep, mla_smem(p), kAttnMaxSmem);
+    if (a->batch == 0) return CHRONOS_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (a->dtype) {
+        case CHRONOS_DTYPE_BF16: return mla_impl<__nv_bfloat16>(p, a->batch, st);
+        case CHRONOS_DTYPE_FP16: return mla_impl<__half>(p, a->batch, st);
+        default: return mla_impl<float>(p, a->batch, st);
+    }
+}
+
+extern "C" int chronos_sw_decode(const ChronosAttnArgs* a, void* stream) {
+    using namespace chronos;
+    g_last_error.clear();
+    if (int rc = attn_common_checks(a, "chronos_sw_decode")) return rc;
+    if (a->rope_dim != a->head_dim || a->window < 1 || a->max_len != a->window)
+        return fail(CHRONOS_ERR_INVALID_ARG, "chronos_sw_decode: rope_dim %d must equal head_dim %d, window %d "
+                    ">= 1 and max_len %d == window", a->rope_dim, a->head_dim, a->window, a->max_len);
+    const AttnParams p = attn_params(a);
+    if (sw_smem(p) > static_cast<size_t>(kAttnMaxSmem))
+        return fail(CHRONOS_ERR_INVALID_ARG, "chronos_sw_decode: window %d x %d heads per kv head needs %zu "
+                    "bytes of shared memory (limit %d)", a->window, p.rep, sw_smem(p), kAttnMaxSmem);
+    if (a->batch == 0) return CHRONOS_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (a->dtype) {
+        case CHRONOS_DTYPE_BF16: return sw_impl<__nv_bfloat16>(p, a->batch, st);
+        case CHRONOS_DTYPE_FP16: return sw_impl<__half>(p, a->batch, st);
+        default: return sw_impl<float>(p, a->batch, st);
+    }
+}
+
+extern "C" int chronos_add_rmsnorm(const ChronosNormArgs* a, void* stream) {
+    using namespace chronos;
+    g_last_error.clear();
+    if (a == nullptr) return fail(CHRONOS_ERR_INVALID_ARG, "chronos_add_rmsnorm: args is NULL");
+    if (a->rows < 0 || a->width < 1 || a->width > 16384 || !known_dtype(a->dtype))
+        return fail(CHRONOS_ERR_INVALID_ARG, "chronos_add_rmsnorm: rows %lld, width %d (1..16384), dtype %d",
+                    static_cast<long long>(a->rows), a->width, a->dtype);
+    if (a->rows > 0 && (a->x == nullptr || a->weight == nullptr || a->out == nullptr))
+        return fail(CHRONOS_ERR_INVALID_ARG, "chronos_add_rmsnorm: x, weight and out are required");
+    if (a->rows == 0) return CHRONOS_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (a->dtype) {
+        case CHRONOS_DTYPE_BF16: return norm_impl<__nv_bfloat16>(a, st);
+        case CHRONOS_DTYPE_FP16: return norm_impl<__half>(a, st);
+        default: return norm_impl<float>(a, st);
+    }
+}
+
+extern "C" size_t chronos_attn_args_size(void) { return sizeof(ChronosAttnArgs); }
+extern "C" size_t chronos_norm_args_size(void) { return sizeof(ChronosNormArgs); }

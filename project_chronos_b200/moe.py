@@ -146,6 +146,14 @@ class ChronosMOEFeedForward(nn.Module):
         self._last_fallback_weight_mass = 0.0
         # Benchmark knob: fp32 [E] offset added to the router logits (None in models).
         self.router_logit_bias: Optional[torch.Tensor] = None
+        # How an eval-time mask is read.  "reference": as moe_chronos.py:221-227
+        # (a live expert runs even where the mask says unavailable; only
+        # placeholders fall back).  "residency": the mask names the experts that
+        # are resident, a_e = mask_e (the blend of chronos/mlx/moe.py:160-166), as a
+        # pooled store whose non-resident experts are placeholders behaves; a CUDA
+        # mask is then applied on the device without a host read, so the call can
+        # be captured in a CUDA graph.
+        self.mask_semantics = "reference"
         # Expert residency (set by a pooled ExpertStore): per-expert device ready
         # flags the GEMMs wait on for selected experts only.
         self.expert_ready_flags: Optional[torch.Tensor] = None
@@ -173,6 +181,8 @@ class ChronosMOEFeedForward(nn.Module):
         self._stats_pending = None
         counts = pend["counts"].cpu().numpy()
         mass = pend["mass"].cpu().numpy().astype(np.float64)
+        if isinstance(pend["a"], torch.Tensor):  # availability built on the device
+            pend = dict(pend, a=pend["a"].cpu().numpy())
         od, fb = [], []
         odm = fbm = 0.0
         for e in range(self.num_experts):
@@ -591,6 +601,16 @@ class ChronosMOEFeedForward(nn.Module):
             if not masked:
                 a_np = None
                 avail_t = None
+            elif eval_with_mask and self.mask_semantics == "residency":
+                # the mask names the resident experts: a_e = mask_e for live experts
+                # (a CUDA mask is applied on the device, with no host read)
+                if mask_np is not None:
+                    a_np = ((mask_np > 0.0) & (live > 0)).astype(np.float32)
+                    avail_t = self._avail_tensor(a_np, dev)
+                else:
+                    a_np = None
+                    avail_t = (available_expert_mask.to(torch.float32) > 0).to(torch.float32) * \
+                        self._avail_tensor(live, dev)
             elif eval_with_mask:
                 a_np = live.copy()  # live experts run even when marked unavailable
                 if mask_np is not None:
@@ -608,8 +628,11 @@ class ChronosMOEFeedForward(nn.Module):
             probs = out["probs"]
             if masked:
                 if a_np is None:
-                    a_np = avail_t.cpu().numpy()
-                if eval_with_mask and mask_np is None:
+                    a_np = avail_t  # read back only when the statistics are read
+                if eval_with_mask and self.mask_semantics == "residency":
+                    _set(self, "_stats_pending", dict(counts=out["counts"], mass=out["mass"], a=a_np,
+                                                      on_demand=_NO_ON_DEMAND))
+                elif eval_with_mask and mask_np is None:
                     # CUDA mask in eval: read lazily together with the counts
                     _set(self, "_stats_pending", dict(
                         counts=out["counts"], mass=out["mass"], a=a_np,

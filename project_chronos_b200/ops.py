@@ -420,6 +420,59 @@ def lookahead_forward(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, num_e
     return probs
 
 
+def add_rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None,
+                sum_out: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """RMSNorm(x + residual) * weight over the last dim (include/chronos_attention.h);
+    ``sum_out`` (may be ``x`` or ``residual``) receives x + residual."""
+    _check_cuda(x, weight, residual, sum_out, out)
+    if x.dtype not in _DTYPES or weight.dtype != x.dtype:
+        raise TypeError(f"x {x.dtype} / weight {weight.dtype}: one supported dtype expected")
+    w = x.shape[-1]
+    for t in (x, residual, sum_out, out):
+        if t is not None and not t.is_contiguous():
+            raise ValueError("add_rmsnorm needs contiguous tensors")
+    out = torch.empty_like(x) if out is None else out
+    args = N.ChronosNormArgs(rows=x.numel() // max(w, 1), width=w, dtype=_DTYPES[x.dtype], eps=float(eps),
+                             x=_ptr(x), residual=_ptr(residual), sum_out=_ptr(sum_out),
+                             weight=_ptr(weight.contiguous()), out=_ptr(out))
+    lib = N.load_library()
+    N.check(lib.chronos_add_rmsnorm(ctypes.byref(args), ctypes.c_void_p(_raw_stream(x.device.index))))
+    return out
+
+
+def attn_decode(kind: str, proj: torch.Tensor, pos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                cache_a: torch.Tensor, cache_b: torch.Tensor, heads: int, kv_heads: int, head_dim: int,
+                rope_dim: int, latent: int, window: int, eps: float, norm_q: torch.Tensor,
+                norm_q2: torch.Tensor, norm_kv: Optional[torch.Tensor] = None,
+                w_krope: Optional[torch.Tensor] = None, w_knope: Optional[torch.Tensor] = None,
+                w_v: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One cached decode step of an MLA (``kind="mla"``) or sliding-window
+    (``"sw"``) layer: proj [B, width] -> out [B, heads*head_dim]; appends the new
+    token to the caches.  ``pos`` is a device int32 scalar (the new token's
+    position).  Every tensor must be contiguous, on one device, in one dtype."""
+    _check_cuda(proj, pos, cos, sin, cache_a, cache_b, norm_q, norm_q2, norm_kv, w_krope, w_knope, w_v, out)
+    dt = proj.dtype
+    if dt not in _DTYPES:
+        raise TypeError(f"unsupported dtype {dt}")
+    for t in (cos, sin, cache_a, cache_b, norm_q, norm_q2, norm_kv, w_krope, w_knope, w_v):
+        if t is not None and (t.dtype != dt or not t.is_contiguous()):
+            raise TypeError("attention operands must be contiguous and share proj's dtype")
+    if pos.dtype != torch.int32:
+        raise TypeError("pos must be a device int32 scalar")
+    b = proj.shape[0]
+    out = torch.empty(b, heads * head_dim, dtype=dt, device=proj.device) if out is None else out
+    args = N.ChronosAttnArgs(
+        batch=b, heads=heads, kv_heads=kv_heads, head_dim=head_dim, rope_dim=rope_dim, latent=latent,
+        window=window, max_len=cache_a.shape[1], table_len=cos.shape[0], dtype=_DTYPES[dt], eps=float(eps),
+        pos=_ptr(pos), proj=_ptr(proj), norm_q=_ptr(norm_q), norm_q2=_ptr(norm_q2), norm_kv=_ptr(norm_kv),
+        w_krope=_ptr(w_krope), w_knope=_ptr(w_knope), w_v=_ptr(w_v), cos=_ptr(cos), sin=_ptr(sin),
+        cache_a=_ptr(cache_a), cache_b=_ptr(cache_b), out=_ptr(out))
+    lib = N.load_library()
+    fn = lib.chronos_mla_decode if kind == "mla" else lib.chronos_sw_decode
+    N.check(fn(ctypes.byref(args), ctypes.c_void_p(_raw_stream(proj.device.index))))
+    return out
+
+
 def profile_begin(max_calls: int) -> None:
     """Record per-stage CUDA events for the next ``max_calls`` layer calls (this thread)."""
     lib = N.load_library()

@@ -190,6 +190,26 @@ def named_workload(name: str, tokens: Optional[int] = None, seed: int = 0, devic
                          zipf_s=spec["zipf_s"])
 
 
+def model_state(shapes, seed: int, std: float = 0.02, embed_std: float = 0.5,
+                norm_std: float = 0.1) -> dict:
+    """Seeded weights of a whole model by parameter name, drawn in sorted-name
+    order from one CPU generator: RMSNorm weights (names ending in
+    ``norm.weight``) 1 + N(0, norm_std), the token embedding N(0, embed_std),
+    every other matrix N(0, std).  ``shapes``: {name: shape}; pass one name of
+    a tied pair only."""
+    g = make_generator(seed)
+    out = {}
+    for name in sorted(shapes):
+        shp = tuple(shapes[name])
+        if name.endswith("norm.weight"):
+            out[name] = 1.0 + _randn(g, shp, norm_std, "cpu")
+        elif "embed_tokens" in name:
+            out[name] = _randn(g, shp, embed_std, "cpu")
+        else:
+            out[name] = _randn(g, shp, std, "cpu")
+    return out
+
+
 def flops_per_token_routed(shape: MoEShape) -> float:
     """FLOPs of one routed or shared SwiGLU application to one token."""
     return 2.0 * 3.0 * shape.hidden * shape.ffn
@@ -220,5 +240,6 @@ def decode_bytes(shape: MoEShape, tokens: int, experts_read: int, elem_bytes: in
 
 __all__ = ["MoEShape", "MoEWeights", "Workload", "WORKLOADS", "make_generator", "make_weights",
            "make_hidden", "make_mask", "make_zipf_bias", "make_workload", "named_workload",
-           "layer_flops", "decode_bytes", "expert_bytes", "flops_per_token_routed", "make_ep_weights"]
+           "layer_flops", "decode_bytes", "expert_bytes", "flops_per_token_routed", "make_ep_weights",
+           "model_state"]
 

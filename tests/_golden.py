@@ -142,3 +142,26 @@ def classify_literal(idx_lit, idx_ref, probs_lit, logits64, logits64_lit=None) -
             worst = max(worst, cls)
         res[("bf16_tie", "logit_rounding", "other")[worst]] += 1
     return res
+
+
+def model_case():
+    return _manifest()["model"]
+
+
+def attn_case():
+    return _manifest()["attn"]
+
+
+def model_config(cfg: dict):
+    """A config namespace for this package's model from a golden case's
+    ChronosConfig keyword arguments, with the defaults ChronosConfig and
+    minimind's config supply for the fields not given."""
+    import types
+    d = dict(rope_scaling=None, use_hybrid_attention=True, router_aux_loss_coef=5e-4, lookahead_steps=2,
+             num_shared_experts=1, kv_latent_dim=64, rope_dim=32, sliding_window_size=2048,
+             tie_word_embeddings=True, rms_norm_eps=1e-5, rope_theta=1e6, dropout=0.0, hidden_act="silu",
+             fallback_mask_prob=0.0, norm_topk_prob=True)
+    d.update(cfg)
+    d.setdefault("intermediate_size", d.get("moe_intermediate_size"))
+    d.setdefault("head_dim", d["hidden_size"] // d["num_attention_heads"])
+    return types.SimpleNamespace(**d)

@@ -46,7 +46,13 @@ literal bf16 routing against the fp32 routing contract, each mismatch
 classified (``tests/_golden.py:classify_literal``).
 
 Lookahead cases run the reference's ``LookaheadRouter`` (``probs_ref``
-[B, S, K, E], plus ``probs_ref_fp32`` for bf16).  The ``ctsr_ref`` directory
+[B, S, K, E], plus ``probs_ref_fp32`` for bf16).  ``model_tf`` runs the
+reference's ``ChronosForCausalLM`` (hybrid attention, MoE blocks, lookahead
+router) teacher-forced: ``logits_{fp32,bf16}`` [steps+1, B, V] and
+``lookahead_{fp32,bf16}`` [steps+1, B, K, E] at the last position of the
+prompt and of every cached one-token step, and the token ids.
+``attn_decode`` steps the reference's two attention modules alone, one token
+at a time with their caches (``y_mla``, ``y_sw`` [steps, B, H], inputs ``x``).  The ``ctsr_ref`` directory
 holds cluster files written by the reference's ``ClusterStorage.write_clusters``
 (``chronos/io/storage.py:182-233``) for the readers here to load.
 """
@@ -125,6 +131,17 @@ LOOKAHEAD_CASES = [
 ]
 
 CTSR = dict(name="ctsr_ref", H=32, E=4, F=64, S=1, L=2, clusters=[[0, 2], [1, 3]], seeds=[40, 41])
+
+# A small hybrid-attention model (MLA on even layers, sliding window on odd),
+# run teacher-forced: a prompt, then one cached token per step past the window.
+MODEL = dict(name="model_tf", seed=50, ids_seed=51, B=2, prompt=8, steps=8,
+             config=dict(vocab_size=512, hidden_size=256, num_hidden_layers=4, num_attention_heads=4,
+                         num_key_value_heads=2, max_position_embeddings=64, num_experts=8,
+                         num_experts_per_tok=2, moe_intermediate_size=256, num_shared_experts=1,
+                         norm_topk_prob=True, kv_latent_dim=64, rope_dim=32, sliding_window_size=12,
+                         lookahead_steps=2, dropout=0.0, hidden_act="silu", flash_attn=True,
+                         rms_norm_eps=1e-5, rope_theta=1e6, tie_word_embeddings=True,
+                         fallback_mask_prob=0.0))
 
 
 def import_reference(ref_root: str):
@@ -316,6 +333,83 @@ def ctsr_fixture(refs):
     return dict(c)
 
 
+ATTN = dict(name="attn_decode", B=2, steps=12, seed=60, x_seed=61,
+            config=dict(hidden_size=256, num_attention_heads=4, num_key_value_heads=2, kv_latent_dim=64,
+                        rope_dim=32, sliding_window_size=5, max_position_embeddings=64, rms_norm_eps=1e-5,
+                        dropout=0.0, flash_attn=True, rope_theta=1e6))
+
+
+def attn_case(refs):
+    """The reference's MLAAttention and SlidingWindowAttention
+    (chronos/model/hybrid_attention.py:62-258) stepped one token at a time with
+    their own caches (past the window), fp32: the output of every step."""
+    from chronos.model.hybrid_attention import MLAAttention, SlidingWindowAttention
+    from model.model_minimind import precompute_freqs_cis
+    from project_chronos_b200 import synthetic as syn
+    c = ATTN
+    cfg = refs[0](**c["config"])
+    cos, sin = precompute_freqs_cis(dim=cfg.head_dim, end=cfg.max_position_embeddings, rope_base=cfg.rope_theta)
+    g = torch.Generator().manual_seed(c["x_seed"])
+    xs = torch.randn(c["steps"], c["B"], 1, cfg.hidden_size, generator=g)
+    out, shapes = {"x": xs.numpy()}, {}
+    for tag, cls, seed in (("mla", MLAAttention, c["seed"]), ("sw", SlidingWindowAttention, c["seed"] + 1)):
+        m = cls(cfg).eval()
+        shp = {k: v.shape for k, v in m.state_dict().items()}
+        shapes[tag] = {k: list(v) for k, v in shp.items()}
+        m.load_state_dict(syn.model_state(shp, seed))
+        past, ys = None, []
+        with torch.no_grad():
+            for t in range(c["steps"]):
+                y, past = m(xs[t], (cos, sin), past, use_cache=True)
+                ys.append(y[:, 0])
+        out[f"y_{tag}"] = torch.stack(ys).numpy()
+    np.savez_compressed(HERE / f"{c['name']}.npz", **out)
+    print(f"{c['name']}: {out['y_mla'].shape} / {out['y_sw'].shape}")
+    return dict(c, state_shapes=shapes, head_dim=cfg.head_dim)
+
+
+def model_case(refs):
+    """Teacher-forced logits of the reference's ChronosForCausalLM
+    (chronos/model/model_chronos.py:166-222): the prompt's last position, then
+    one cached token per step; in fp32 and in bf16 on the same bf16-valued weights."""
+    from chronos.model.model_chronos import ChronosForCausalLM
+    from project_chronos_b200 import synthetic as syn
+    ChronosConfig = refs[0]
+    c = MODEL
+    cfg = ChronosConfig(**c["config"])
+    ref = ChronosForCausalLM(cfg)
+    shapes = {k: v.shape for k, v in ref.state_dict().items() if k != "lm_head.weight"}
+    state = {k: v.to(torch.bfloat16).float() for k, v in syn.model_state(shapes, c["seed"]).items()}
+    g = torch.Generator().manual_seed(c["ids_seed"])
+    ids = torch.randint(0, cfg.vocab_size, (c["B"], c["prompt"] + c["steps"]), generator=g)
+    out = {}
+    for tag, dt in (("fp32", torch.float32), ("bf16", torch.bfloat16)):
+        m = ChronosForCausalLM(cfg)
+        missing, unexpected = m.load_state_dict(state, strict=False)
+        assert set(missing) <= {"lm_head.weight"} and not unexpected, (missing, unexpected)
+        m = m.to(dt).eval()
+        logits, look = [], []
+        with torch.no_grad():
+            o, lp = m(ids[:, :c["prompt"]], use_cache=True)
+            logits.append(o.logits[:, -1].float())
+            look.append(lp[:, -1].float())
+            pkv = o.past_key_values
+            for t in range(c["steps"]):
+                j = c["prompt"] + t
+                o, lp = m(ids[:, j:j + 1], past_key_values=pkv, use_cache=True)
+                logits.append(o.logits[:, -1].float())
+                look.append(lp[:, -1].float())
+                pkv = o.past_key_values
+        out[f"logits_{tag}"] = torch.stack(logits).numpy()
+        out[f"lookahead_{tag}"] = torch.stack(look).numpy()
+    out["ids"] = ids.numpy().astype(np.int64)
+    np.savez_compressed(HERE / f"{c['name']}.npz", **out)
+    rel = float(np.linalg.norm(out["logits_bf16"] - out["logits_fp32"]) / np.linalg.norm(out["logits_fp32"]))
+    print(f"{c['name']}: logits {out['logits_fp32'].shape}, bf16 vs fp32 rel-L2 {rel:.3e}")
+    return dict(c, reference_bf16_vs_fp32=rel,
+                state_shapes={k: list(v.shape) for k, v in ref.state_dict().items()})
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -336,11 +430,17 @@ def main():
             look[c["name"]] = lookahead_case(args.ref, c)
     if not args.only or args.only == CTSR["name"]:
         ctsr = ctsr_fixture(refs)
+    attn = old.get("attn")
+    if not args.only or args.only == ATTN["name"]:
+        attn = attn_case(refs)
+    model = old.get("model")
+    if not args.only or args.only == MODEL["name"]:
+        model = model_case(refs)
     with open(path, "w") as f:
         json.dump({"generator": "tests/golden/make_golden.py", "torch": torch.__version__,
                    "cases": [moe[c["name"]] for c in CASES if c["name"] in moe],
                    "lookahead": [look[c["name"]] for c in LOOKAHEAD_CASES if c["name"] in look],
-                   "ctsr": ctsr}, f, indent=1)
+                   "ctsr": ctsr, "attn": attn, "model": model}, f, indent=1)
 
 
 if __name__ == "__main__":
