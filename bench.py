@@ -401,7 +401,8 @@ def run_ours(args, dist: Dist):
         # ---------------- expert parallel (DeepSeek-V3 shape) ----------------
         ep = run_ep(args, dist, dev, peaks, flush)
         # ---------------- 8-layer decode, MoE FFNs (e2e workload) ----------------
-        e2e_dec = run_e2e_decode(args, dist, dev, peaks)
+        e2e_dec = run_model_decode(args, dist, dev, peaks)
+        e2e_dec["moe_layers_alone"] = run_moe_layers_decode(args, dist, dev, peaks)
 
     clocks = sampler.stop()
 
@@ -519,22 +520,130 @@ def bench_config(args, world: int) -> dict:
 
 
 E2E_MIN_STEPS = 200
+E2E_BATCH = 32
 E2E_LAYERS = 8
 E2E_PROMPT = 512
 E2E_STEPS = 256
 
 
-def run_e2e_decode(args, dist: Dist, dev, peaks) -> dict:
-    """The MoE FFNs of an 8-layer decode: d_model 1024, 16 experts top-2 + 1 shared,
-    d_ff 2048, bf16, batch 32, a 512-token prompt then 256 decode steps; every
-    layer's availability mask is a fresh Bernoulli(0.85) draw per step (experts
-    drawn unavailable are served by the shared fallback, as a non-resident expert
-    is) and the per-expert device ready flags are on.  Only the MoE layers run;
-    attention, embeddings and the LM head are not part of this build, so each
-    layer call of a step gets its own fresh N(0, 1) hidden states (what attention
-    would hand it) instead of the previous layer's output.  Each decode step (8
-    layer calls) is one CUDA-graph replay after the step's masks and inputs are
-    copied into the graph's buffers."""
+
+
+def _model_step_bytes(cfg, B: int, ctx: int, experts_read: float) -> float:
+    """Algorithmic HBM bytes of one decode step of the model (bf16): every weight
+    the step reads once (attention projections, the router, the shared expert and
+    the experts read (selected and available, summed over layers), the lookahead
+    router, the tied LM head), the caches read (MLA latent and rope keys of
+    ``ctx`` positions, sliding-window keys and values of min(ctx, window) slots)."""
+    H, nh, nkv, D = cfg["hidden_size"], cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"]
+    L, R, W, E, F = cfg["kv_latent_dim"], cfg["rope_dim"], cfg["sliding_window_size"], cfg["num_experts"], \
+        cfg["moe_intermediate_size"]
+    nope = D - R
+    mla_w = H * (nh * (nope + R) + L) + L * nkv * (nope + R + D) + nh * D * H
+    sw_w = H * (nh + 2 * nkv) * D + nh * D * H
+    n_layers = cfg["num_hidden_layers"]
+    n_mla = (n_layers + 1) // 2
+    attn_w = n_mla * mla_w + (n_layers - n_mla) * sw_w
+    moe_w = n_layers * (E * H + cfg["num_shared_experts"] * 3 * H * F) + experts_read * 3 * H * F
+    look_w = H * (H // 4) + (H // 4) * E * (cfg["lookahead_steps"] + 1)
+    head_w = cfg["vocab_size"] * H
+    caches = B * (n_mla * ctx * (L + nkv * R) + (n_layers - n_mla) * min(ctx, W) * nkv * D * 2)
+    return 2.0 * (attn_w + moe_w + look_w + head_w + caches)
+
+
+def run_model_decode(args, dist: Dist, dev, peaks) -> dict:
+    """The 8-layer Chronos model decode: d_model 1024, 8 heads (2 kv heads),
+    MLA on even and sliding-window attention on odd layers, MoE blocks of 16
+    experts top-2 + 1 shared with d_ff 2048, the lookahead router and the tied
+    LM head; bf16, random-init weights, batch 32, a 512-token random prompt
+    then 256 greedy decode steps.  Each layer's expert availability is a fresh
+    Bernoulli(0.85) draw per step (the experts drawn unavailable are treated as
+    not resident: their selections go to the shared expert), device ready flags
+    gate every selected expert.  Each step is one CUDA-graph replay of the whole
+    model step (embedding, 8 blocks, lookahead router, LM head, greedy pick);
+    the step's masks are copied into the graph's buffer before it."""
+    import types
+    from project_chronos_b200 import ops
+    from project_chronos_b200.model import ChronosForCausalLM, GraphedDecoder
+
+    from project_chronos_b200 import synthetic as syn
+    cfg = types.SimpleNamespace(**syn.DECODE_MODEL)
+    B, P, T = E2E_BATCH, E2E_PROMPT, E2E_STEPS
+    lm = ChronosForCausalLM.on_device(cfg, dev, torch.bfloat16)
+    syn.init_model_(lm, 8800 + dist.rank, dev)
+    lm = lm.eval()
+    g = torch.Generator(device=dev)
+    g.manual_seed(8900 + dist.rank)
+    L, E = cfg.num_hidden_layers, cfg.num_experts
+    flags = torch.ones(E, dtype=torch.int32, device=dev)
+    for blk in lm.model.layers:
+        blk.mlp.mask_semantics = "residency"
+        blk.mlp.expert_ready_flags = flags
+        blk.mlp.expert_ready_epoch = 1
+    ids = torch.randint(0, cfg.vocab_size, (B, P), generator=g, device=dev)
+    masks = (torch.rand(T + 32, L, E, generator=g, device=dev) < 0.85).float()
+    pa, pb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.no_grad():
+        lm(ids, use_cache=True, cache_capacity=P + T + 40)          # warm-up prompt
+        torch.cuda.synchronize()
+        pa.record()
+        out, _ = lm(ids, use_cache=True, cache_capacity=P + T + 40)
+        pb.record()
+        cache = out.past_key_values
+        gd = GraphedDecoder(lm, cache)
+        gd.ids.copy_(torch.argmax(out.logits[:, -1], dim=-1).view(-1, 1))
+        launches0 = ops.kernel_launches()
+        gd.masks.copy_(masks[0])
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for t in range(T):
+            gd.masks.copy_(masks[t])
+            gd.step()
+        b.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        del launches0
+        # experts read per step, sampled on further (untimed) steps through the
+        # statistics buffers the captured MoE calls write
+        pend = [blk.mlp._stats_pending for blk in lm.model.layers]
+        reads = []
+        for t in range(T, T + 16):
+            gd.masks.copy_(masks[t])
+            gd.step()
+            torch.cuda.synchronize()
+            reads.append(sum(int(((pd["counts"] > 0) & (pd["a"] > 0)).sum()) for pd in pend
+                             if pd is not None and isinstance(pd.get("a"), torch.Tensor)))
+    ops.check_status(dev)
+    ms = dist.max(a.elapsed_time(b)) / T
+    prompt_ms = pa.elapsed_time(pb)
+    experts_read = float(np.mean(reads)) if reads else float("nan")
+    step_bytes = _model_step_bytes(syn.DECODE_MODEL, B, P + T // 2, experts_read)
+    gbs = step_bytes / (ms / 1e3) / 1e9
+    return dict(metric="Chronos model decode tokens/s (8 layers, hybrid attention + MoE, batch 32)",
+                value=round(B * dist.world / (ms / 1e3), 1), unit="tokens/s",
+                us_per_step=round(ms * 1e3, 2), steps=T, prompt_tokens=B * P,
+                prompt_ms=round(prompt_ms, 3),
+                prompt_tokens_per_s=round(B * P / (prompt_ms / 1e3), 1),
+                experts_read_per_step=round(experts_read, 2),
+                step_bytes_mid_sequence=int(step_bytes), step_gbs=round(gbs, 1),
+                hbm_frac=round(gbs / peaks["hbm_gbs"], 4),
+                cache_bytes=int(cache.nbytes()),
+                gpu_launches_per_step=int(gd.launches_per_step),
+                gpu_launches=int(gd.launches_per_step) * T,
+                note=("ChronosForCausalLM: attention decode kernels (MLA latent cache, sliding-window ring), "
+                      "MoE kernels, lookahead kernel, cuBLAS projections and LM head; greedy; "
+                      "availability Bernoulli(0.85) per step and layer, ready flags on; one CUDA graph "
+                      "replay per step"))
+
+
+def run_moe_layers_decode(args, dist: Dist, dev, peaks) -> dict:
+    """The MoE layers ALONE of the 8-layer decode (for the MoE share of the model
+    step): d_model 1024, 16 experts top-2 + 1 shared, d_ff 2048, bf16, batch 32,
+    a 512-token prompt then 256 steps; each layer's availability a fresh
+    Bernoulli(0.85) draw per step, device ready flags on; each layer call gets
+    fresh N(0, 1) hidden states; one CUDA-graph replay per step."""
     from project_chronos_b200 import ops, synthetic as syn
 
     spec = syn.WORKLOADS["e2e"]
@@ -625,13 +734,13 @@ def run_e2e_decode(args, dist: Dist, dev, peaks) -> dict:
             tot += ebytes * (len(avail_sel) + shape.num_shared) + E * shape.hidden * 2
     tot //= len(sample)
     hbm = tot / (ms / 1e3) / 1e9
-    return dict(metric="MoE FFN time per decode step, 8 layers (e2e decode workload)",
+    return dict(metric="MoE FFN time per decode step, 8 layers alone",
                 us_per_step=round(ms * 1e3, 2), tokens_per_s_moe_only=round(B * dist.world / (ms / 1e3), 1),
                 step_bytes=int(tot), step_gbs=round(hbm, 1), hbm_frac=round(hbm / peaks["hbm_gbs"], 4),
                 prompt_ms=round(prompt_ms, 3), prompt_tokens=B * E2E_PROMPT, steps=E2E_STEPS,
                 gpu_launches_per_step=launches_per_step,
-                note=("MoE layers only; attention/embedding/LM head not built; masks Bernoulli(0.85) per "
-                      "step and layer; device ready flags on; one CUDA graph replay per step"))
+                note=("MoE layers only, fresh inputs per layer call; masks Bernoulli(0.85) per step and "
+                      "layer; device ready flags on; one CUDA graph replay per step"))
 
 
 def run_ep(args, dist: Dist, dev, peaks, flush) -> dict:
@@ -670,6 +779,19 @@ def run_ep(args, dist: Dist, dev, peaks, flush) -> dict:
     launches = ops.kernel_launches() - launches0
     ms = dist.max(sum(a.elapsed_time(b) for a, b in evs) / K)
     ops.check_status(dev)
+    # phases of a few more (untimed) calls: the exchange waits vs the expert GEMMs
+    phases = None
+    if dist.world > 1:
+        m.phase_events = []
+        for _ in range(3):
+            m(x)
+        torch.cuda.synchronize()
+        names = ["start", "dispatched", "counts_exchanged", "shared_done", "rows_arrived", "experts_done",
+                 "rows_returned", "combined"]
+        per = {f"{a}->{b}": float(np.median([pe[a].elapsed_time(pe[b]) for pe in m.phase_events]))
+               for a, b in zip(names[:-1], names[1:])}
+        m.phase_events = None
+        phases = {k2: round(dist.max(v), 4) for k2, v in per.items()}
     H, F, E, k, S = shape.hidden, shape.ffn, shape.num_experts, shape.top_k, shape.num_shared
     flops = 2.0 * n * (H * E + 3 * H * F * (k + S))          # per rank
     tflops = flops / (ms / 1e3) / 1e12
@@ -699,6 +821,10 @@ def run_ep(args, dist: Dist, dev, peaks, flush) -> dict:
                 layer_tflops_per_gpu=round(tflops, 1),
                 a2a_bytes_per_gpu_per_direction=int(a2a_bytes),
                 a2a_gbs_if_serial=round(a2a_bytes / (ms / 1e3) / 1e9, 1),
+                phases_ms=phases,
+                # the return exchange overlaps nothing (one chunk): bytes / its time
+                a2a_return_gbs=(None if not phases else round(
+                    a2a_bytes / (phases["experts_done->rows_returned"] / 1e3 + 1e-12) / 1e9, 1)),
                 send_counts_rank0=sc, gpu_launches=launches, roofline=roof)
 
 

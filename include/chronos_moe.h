@@ -214,6 +214,21 @@ CHRONOS_API int chronos_moe_profile_end(float* stage_ms, int32_t* stage_launches
 /* Kernels launched by this library since it was loaded (all threads). */
 CHRONOS_API uint64_t chronos_moe_kernel_launches(void);
 
+/* Process-wide switches of the launch sequence (no counterpart in the
+ * reference; the results are bit-identical either way):
+ *   "fused_route"  1: a decode call (N <= 64 tokens, d_model <= 4096) routes in
+ *                  ONE launch, a thread-block cluster that computes the chunk
+ *                  partials, the selection and the plan; 0 (default): the logit
+ *                  kernel and the select + plan kernel.
+ *   "two_phase_combine"  1 (default): a large call whose shared experts run last
+ *                  in the token-major down GEMM combines in two phases: routed
+ *                  units store coef * expert(x) rounded to the layer dtype per
+ *                  slot, the shared units sum each token's slots in choice order
+ *                  (deterministic; no fp32 accumulator); 0: fp32 reduce-adds
+ *                  into an accumulator.
+ * Returns CHRONOS_OK, or CHRONOS_ERR_INVALID_ARG for an unknown name. */
+CHRONOS_API int chronos_moe_set_option(const char* name, int64_t value);
+
 #ifdef __cplusplus
 }
 #endif

@@ -43,7 +43,7 @@ ABI_VERSION = 2
 EXPORTS = ("chronos_moe_workspace_size", "chronos_moe_forward", "chronos_moe_route",
            "chronos_moe_last_error", "chronos_moe_abi_version", "chronos_moe_args_size",
            "chronos_moe_profile_begin", "chronos_moe_profile_end",
-           "chronos_moe_kernel_launches", "chronos_moe_forward_noalloc",
+           "chronos_moe_kernel_launches", "chronos_moe_forward_noalloc", "chronos_moe_set_option",
            "chronos_ep_dispatch", "chronos_ep_combine", "chronos_ep_dispatch_args_size",
            "chronos_ep_combine_args_size", "chronos_lookahead_forward", "chronos_lookahead_args_size",
            "chronos_mla_decode", "chronos_sw_decode", "chronos_add_rmsnorm", "chronos_attn_args_size",
@@ -242,6 +242,8 @@ def load_library(path: str = LIB_PATH):
         lib.chronos_moe_forward_noalloc.argtypes = [ctypes.POINTER(ChronosMoeArgs),
                                                     ctypes.c_void_p]
         lib.chronos_moe_forward_noalloc.restype = ctypes.c_int
+        lib.chronos_moe_set_option.argtypes = [ctypes.c_char_p, ctypes.c_int64]
+        lib.chronos_moe_set_option.restype = ctypes.c_int
         lib.chronos_ep_dispatch.argtypes = [ctypes.POINTER(ChronosEpDispatchArgs), ctypes.c_void_p]
         lib.chronos_ep_dispatch.restype = ctypes.c_int
         lib.chronos_ep_combine.argtypes = [ctypes.POINTER(ChronosEpCombineArgs), ctypes.c_void_p]

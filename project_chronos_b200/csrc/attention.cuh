@@ -21,6 +21,7 @@ constexpr int kAttnMaxRep = 8;
 
 struct AttnParams {
     int heads, kv_heads, rep, head_dim, rope_dim, nope, latent, window, max_len, table_len;
+    int stage_w;   // MLA: 1 = the group's weight slices are staged in shared memory
     float eps, scale;
     const int32_t* pos;
     const void* proj;
@@ -144,16 +145,112 @@ __global__ void __launch_bounds__(kAttnThreads) add_rmsnorm_kernel(NormParams p)
     }
 }
 
+// 8 consecutive values as fp32: one 16-byte load for 2-byte types, two for fp32
+// (the caller guarantees 16-byte alignment).
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float* v);
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float* v) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float* v) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+}
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float* v) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+    }
+}
+
+// Copy `count` elements (a multiple of 8) into shared memory with 16-byte vectors.
+template <typename T>
+__device__ __forceinline__ void stage_rows(T* dst, const T* src, int count) {
+    constexpr int EPV = 16 / static_cast<int>(sizeof(T));
+    for (int i = threadIdx.x; i < count / EPV; i += kAttnThreads)
+        reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+}
+
+// Weighted sum of `n` cached rows for every head of the group:
+// out[h][c] = sum_t p[h][t] * row_t[c] for the `width` columns of a row, rows
+// `stride` elements apart; the row at `fresh_t` comes from shared memory
+// (`fresh`, fp32) instead.  Warps take 8-column groups, lanes take every 32nd
+// row (many independent 16-byte loads in flight), and a warp reduction
+// gathers the lanes; `emit(h, c, value)` receives each result.
+template <typename T, typename Emit>
+__device__ __forceinline__ void weighted_rows(const T* rows, int64_t stride, int n, int width, const float* p,
+                                              int p_stride, int rep, int fresh_t, const float* fresh, int warp,
+                                              int lane, Emit&& emit) {
+    for (int cg = warp; cg < width / 8; cg += kAttnWarps) {
+        float acc[kAttnMaxRep][8];
+#pragma unroll
+        for (int h = 0; h < kAttnMaxRep; ++h)
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc[h][u] = 0.0f;
+#pragma unroll 4
+        for (int t = lane; t < n; t += 32) {
+            float v[8];
+            if (t == fresh_t) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = fresh[cg * 8 + u];
+            } else {
+                load8<T>(rows + static_cast<int64_t>(t) * stride + cg * 8, v);
+            }
+#pragma unroll
+            for (int h = 0; h < kAttnMaxRep; ++h) {
+                if (h < rep) {
+                    const float ph = p[h * p_stride + t];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) acc[h][u] = fmaf(ph, v[u], acc[h][u]);
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < kAttnMaxRep; ++h) {
+            if (h < rep) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const float r = warp_sum(acc[h][u]);
+                    if (lane == 0) emit(h, cg * 8 + u, r);
+                }
+            }
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // MLA decode (hybrid_attention.py:116-179 with a cache, S = 1)
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) {
-    extern __shared__ float msm[];
+    extern __shared__ __align__(16) float msm[];
     const int g = blockIdx.x, b = blockIdx.y;
     const int rep = p.rep, nope = p.nope, R = p.rope_dim, L = p.latent, D = p.head_dim;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* qn = msm;                       // [rep][nope]
+    // the group's slices of k_nope_proj [nope, L], k_rope_proj [R, L], v_proj [D, L]:
+    // staged in shared memory when they fit, else read where they are (L2)
+    const T* wkn_g = static_cast<const T*>(p.w_knope) + static_cast<int64_t>(g) * nope * L;
+    const T* wkr_g = static_cast<const T*>(p.w_krope) + static_cast<int64_t>(g) * R * L;
+    const T* wv_g = static_cast<const T*>(p.w_v) + static_cast<int64_t>(g) * D * L;
+    T* wstage = reinterpret_cast<T*>(msm);
+    const int wcount = p.stage_w ? L * (nope + R + D) : 0;
+    const T* wkn = p.stage_w ? wstage : wkn_g;
+    const T* wkr = p.stage_w ? wstage + nope * L : wkr_g;
+    const T* wv = p.stage_w ? wstage + (nope + R) * L : wv_g;
+    float* qn = reinterpret_cast<float*>(wstage + wcount);   // [rep][nope]
     float* qr = qn + rep * nope;           // [rep][R]
     float* qabs = qr + rep * R;            // [rep][L]
     float* ctx = qabs + rep * L;           // [rep][L]
@@ -170,6 +267,11 @@ __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) 
     const int n = pos + 1;
     const int width = p.heads * (nope + R) + L;
     const T* row = static_cast<const T*>(p.proj) + static_cast<int64_t>(b) * width;
+    if (p.stage_w) {
+        stage_rows<T>(wstage, wkn_g, nope * L);
+        stage_rows<T>(wstage + nope * L, wkr_g, R * L);
+        stage_rows<T>(wstage + (nope + R) * L, wv_g, D * L);
+    }
     for (int i = threadIdx.x; i < rep * nope; i += kAttnThreads)
         qn[i] = to_f32<T>(row[(g * rep) * nope + i]);
     for (int i = threadIdx.x; i < rep * R; i += kAttnThreads)
@@ -184,14 +286,12 @@ __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) 
     }
     __syncthreads();
     // k_rope of the new token: k_rope_proj(c) (rounded as the bf16 linear rounds)
-    const T* wkr = static_cast<const T*>(p.w_krope) + static_cast<int64_t>(g) * R * L;
     for (int r = threadIdx.x; r < R; r += kAttnThreads) {
         float acc = 0.0f;
         for (int j = 0; j < L; ++j) acc = fmaf(to_f32<T>(wkr[r * L + j]), cnew[j], acc);
         krn[r] = round_to<T>(acc);
     }
     // q_abs = W_kn^T q_nope: the key up-projection folded into the query
-    const T* wkn = static_cast<const T*>(p.w_knope) + static_cast<int64_t>(g) * nope * L;
     for (int i = threadIdx.x; i < rep * L; i += kAttnThreads) {
         const int h = i / L, j = i % L;
         const float* q = qn + h * nope;
@@ -221,24 +321,43 @@ __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) 
             cache_c[static_cast<int64_t>(pos) * L + j] = from_f32<T>(cnew[j]);
     for (int r = threadIdx.x; r < R; r += kAttnThreads)
         cache_k[(static_cast<int64_t>(pos) * p.kv_heads + g) * R + r] = from_f32<T>(krn[r]);
-    // scores: one token per thread, every head of the group
+    // scores: one cached token per thread (its latent and rope key as 16-byte loads),
+    // every head of the group
     for (int t = threadIdx.x; t < n; t += kAttnThreads) {
         float acc[kAttnMaxRep];
 #pragma unroll
         for (int h = 0; h < kAttnMaxRep; ++h) acc[h] = 0.0f;
         const T* ct = cache_c + static_cast<int64_t>(t) * L;
-        for (int j = 0; j < L; ++j) {
-            const float c = t == pos ? cnew[j] : to_f32<T>(ct[j]);
+#pragma unroll 4
+        for (int j8 = 0; j8 < L; j8 += 8) {
+            float c[8];
+            if (t == pos) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) c[u] = cnew[j8 + u];
+            } else {
+                load8<T>(ct + j8, c);
+            }
 #pragma unroll
             for (int h = 0; h < kAttnMaxRep; ++h)
-                if (h < rep) acc[h] = fmaf(qabs[h * L + j], c, acc[h]);
+                if (h < rep)
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) acc[h] = fmaf(qabs[h * L + j8 + u], c[u], acc[h]);
         }
         const T* kt = cache_k + (static_cast<int64_t>(t) * p.kv_heads + g) * R;
-        for (int r = 0; r < R; ++r) {
-            const float k = t == pos ? krn[r] : to_f32<T>(kt[r]);
+#pragma unroll 4
+        for (int r8 = 0; r8 < R; r8 += 8) {
+            float k[8];
+            if (t == pos) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) k[u] = krn[r8 + u];
+            } else {
+                load8<T>(kt + r8, k);
+            }
 #pragma unroll
             for (int h = 0; h < kAttnMaxRep; ++h)
-                if (h < rep) acc[h] = fmaf(qr[h * R + r], k, acc[h]);
+                if (h < rep)
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) acc[h] = fmaf(qr[h * R + r8 + u], k[u], acc[h]);
         }
 #pragma unroll
         for (int h = 0; h < kAttnMaxRep; ++h)
@@ -248,16 +367,10 @@ __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) 
     heads_softmax<T>(sc, rep, p.max_len, n, warp, lane);
     __syncthreads();
     // ctx = sum_t p_t c_t per head
-    for (int i = threadIdx.x; i < rep * L; i += kAttnThreads) {
-        const int h = i / L, j = i % L;
-        const float* ph = sc + h * p.max_len;
-        float acc = 0.0f;
-        for (int t = 0; t < pos; ++t) acc = fmaf(ph[t], to_f32<T>(cache_c[static_cast<int64_t>(t) * L + j]), acc);
-        ctx[i] = fmaf(ph[pos], cnew[j], acc);
-    }
+    weighted_rows<T>(cache_c, L, n, L, sc, p.max_len, rep, pos, cnew, warp, lane,
+                     [&](int h, int c, float v) { ctx[h * L + c] = v; });
     __syncthreads();
     // out = W_v ctx: the value up-projection applied once to the weighted latent
-    const T* wv = static_cast<const T*>(p.w_v) + static_cast<int64_t>(g) * D * L;
     for (int i = threadIdx.x; i < rep * D; i += kAttnThreads) {
         const int h = i / D, d = i % D;
         const float* c = ctx + h * L;
@@ -272,7 +385,7 @@ __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) 
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(kAttnThreads) sw_decode_kernel(AttnParams p) {
-    extern __shared__ float ssm[];
+    extern __shared__ __align__(16) float ssm[];
     const int g = blockIdx.x, b = blockIdx.y;
     const int rep = p.rep, D = p.head_dim, W = p.window;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -321,16 +434,26 @@ __global__ void __launch_bounds__(kAttnThreads) sw_decode_kernel(AttnParams p) {
         kc[(static_cast<int64_t>(slot) * p.kv_heads + g) * D + i] = from_f32<T>(kn[i]);
         vc[(static_cast<int64_t>(slot) * p.kv_heads + g) * D + i] = from_f32<T>(vn[i]);
     }
+    // scores: one ring slot per thread, its key as 16-byte loads
     for (int t = threadIdx.x; t < n; t += kAttnThreads) {
         float acc[kAttnMaxRep];
 #pragma unroll
         for (int h = 0; h < kAttnMaxRep; ++h) acc[h] = 0.0f;
         const T* kt = kc + (static_cast<int64_t>(t) * p.kv_heads + g) * D;
-        for (int d = 0; d < D; ++d) {
-            const float k = t == slot ? kn[d] : to_f32<T>(kt[d]);
+#pragma unroll 4
+        for (int d8 = 0; d8 < D; d8 += 8) {
+            float k[8];
+            if (t == slot) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) k[u] = kn[d8 + u];
+            } else {
+                load8<T>(kt + d8, k);
+            }
 #pragma unroll
             for (int h = 0; h < kAttnMaxRep; ++h)
-                if (h < rep) acc[h] = fmaf(q[h * D + d], k, acc[h]);
+                if (h < rep)
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) acc[h] = fmaf(q[h * D + d8 + u], k[u], acc[h]);
         }
 #pragma unroll
         for (int h = 0; h < kAttnMaxRep; ++h)
@@ -339,16 +462,8 @@ __global__ void __launch_bounds__(kAttnThreads) sw_decode_kernel(AttnParams p) {
     __syncthreads();
     heads_softmax<T>(sc, rep, W, n, warp, lane);
     __syncthreads();
-    for (int i = threadIdx.x; i < rep * D; i += kAttnThreads) {
-        const int h = i / D, d = i % D;
-        const float* ph = sc + h * W;
-        float acc = 0.0f;
-        for (int t = 0; t < n; ++t) {
-            const float v = t == slot ? vn[d] : to_f32<T>(vc[(static_cast<int64_t>(t) * p.kv_heads + g) * D + d]);
-            acc = fmaf(ph[t], v, acc);
-        }
-        out[i] = from_f32<T>(acc);
-    }
+    weighted_rows<T>(vc + static_cast<int64_t>(g) * D, static_cast<int64_t>(p.kv_heads) * D, n, D, sc, W, rep,
+                     slot, vn, warp, lane, [&](int h, int c, float v) { out[h * D + c] = from_f32<T>(v); });
 }
 
 }  // namespace chronos

@@ -31,6 +31,7 @@
 #include "gemm_tc.cuh"
 #include "plan.cuh"
 #include "router.cuh"
+#include "route_fused.cuh"
 
 namespace chronos {
 namespace {
@@ -60,6 +61,15 @@ constexpr int kDownWideMinTokens = 1024;  // batches from this size use token-ma
 constexpr int kDmPass = 64;  // token-major down: output columns per epilogue pass
 
 std::atomic<uint64_t> g_kernel_launches{0};
+
+// Decode routing as one cluster launch (route_fused.cuh); off: the two-kernel
+// path.  Set by chronos_moe_set_option("fused_route", 0/1).
+std::atomic<bool> g_fused_route_enabled{false};
+
+// Prefill-sized calls (token-major down GEMM, shared experts last): combine the
+// routed rows in two phases (stores + an ordered per-token sum) instead of fp32
+// reduce-adds.  Set by chronos_moe_set_option("two_phase_combine", 0/1).
+std::atomic<bool> g_two_phase_enabled{true};
 
 inline void count_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
 
@@ -118,8 +128,8 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // Workspace regions, a function of the shape only.
 struct Layout {
     size_t grp_count, grp_off, act_rows, act_xrow, act_hrow, act_wslot, act_eid, ustart_gu, partials,
-        ustart_dn, hdr, pos, sel_coef, shared_coef, topk_idx, topk_w, slot_tok, slot_coef, slot_map, xp,
-        hid, y_acc, total;
+        ustart_dn, hdr, pos, sel_coef, shared_coef, topk_idx, topk_w, slot_tok, slot_coef, slot_map, pair_slot,
+        xp, hid, y_acc, total;
 };
 
 Layout make_layout(const ChronosMoeShape& s) {
@@ -153,6 +163,9 @@ Layout make_layout(const ChronosMoeShape& s) {
     L.slot_tok = take(4 * (N * K + S * N));
     L.slot_coef = take(4 * (N * K + S * N));
     L.slot_map = N <= static_cast<size_t>(kSelectPlanMaxTokens) ? take(4 * E * N) : off;
+    L.pair_slot = take(4 * N * K);
+    // x rows in expert order for the gate/up GEMM; once that GEMM is done, the
+    // two-phase down GEMM's scaled slot rows (same size) go here
     L.xp = take(es * N * K * H);
     L.hid = take(es * (N * K + S * N) * F);
     L.y_acc = take(4 * N * H);
@@ -317,12 +330,8 @@ int experts_per_lane(int num_experts) {
     return num_experts <= 32 ? 1 : num_experts <= 64 ? 2 : num_experts <= 128 ? 4 : 8;
 }
 
-// Launches the logit kernel and (unless `out_params` is given, in which case
-// the parameters are returned for the fused select + plan kernel) the select kernel.
-template <typename T>
-int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool prerouted,
-                 int32_t* topk_idx, float* topk_w, bool zero_acc, RouteParams* out_params = nullptr,
-                 void* y_direct = nullptr) {
+RouteParams route_params(const ChronosMoeArgs* a, const Ptrs& w, bool prerouted, int32_t* topk_idx,
+                         float* topk_w, bool zero_acc, void* y_direct) {
     const ChronosMoeShape& s = a->shape;
     RouteParams rp{};
     rp.x = a->x;
@@ -349,9 +358,104 @@ int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool p
     rp.y_acc = (zero_acc && y_direct == nullptr) ? w.at<float>(w.L->y_acc) : nullptr;
     rp.y_direct = y_direct;
     rp.partials = w.at<float>(w.L->partials);
+    rp.nchunks = route_chunks(s.hidden);
+    return rp;
+}
+
+// The cluster shape of the fused decode routing kernel for this call, or
+// false when the call takes the two-kernel path (a batch above 64 tokens,
+// d_model above 4096, shared memory above the limit, or a cluster this GPU
+// cannot place).  The placement check runs once per (kernel, shape).
+template <typename T, int EPL>
+bool fused_route_fits_epl(int ncta, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::pair<int, size_t>, bool> seen;
+    std::lock_guard<std::mutex> lk(mu);
+    const auto key = std::make_pair(ncta, smem);
+    auto it = seen.find(key);
+    if (it != seen.end()) return it->second;
+    bool ok = set_smem(route_decode_fused_kernel<T, EPL>, static_cast<int>(smem)) == CHRONOS_OK;
+    if (ok) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(ncta);
+        cfg.blockDim = dim3(kFusedRouteThreads);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = ncta;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        ok = cudaOccupancyMaxActiveClusters(&clusters, route_decode_fused_kernel<T, EPL>, &cfg) == cudaSuccess &&
+             clusters >= 1;
+        cudaGetLastError();   // a refused query leaves no error behind
+    }
+    seen[key] = ok;
+    return ok;
+}
+
+template <typename T>
+bool fused_route_shape(const ChronosMoeShape& s, int* ncta, int* cpc, size_t* smem) {
+    if (s.num_tokens < 1 || s.num_tokens > kFusedRouteMaxTokens) return false;
+    const int C = route_chunks(s.hidden);
+    *ncta = std::min(kFusedRouteMaxCtas, C);
+    *cpc = (C + *ncta - 1) / *ncta;
+    if (*ncta * *cpc > kFusedRouteMaxChunks) return false;
+    *smem = fused_route_smem<T>(s.num_tokens, s.num_experts, *cpc);
+    if (*smem > static_cast<size_t>(180 << 10)) return false;
+    switch (experts_per_lane(s.num_experts)) {
+        case 1: return fused_route_fits_epl<T, 1>(*ncta, *smem);
+        case 2: return fused_route_fits_epl<T, 2>(*ncta, *smem);
+        case 4: return fused_route_fits_epl<T, 4>(*ncta, *smem);
+        default: return fused_route_fits_epl<T, 8>(*ncta, *smem);
+    }
+}
+
+template <typename T, int EPL>
+cudaError_t launch_fused_route_epl(const RouteParams& rp, const PlanParams& pp, const ScatterParams& sp,
+                                   int ncta, int cpc, size_t smem, cudaStream_t st) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(ncta);
+    cfg.blockDim = dim3(kFusedRouteThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = ncta;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    count_launch();
+    return cudaLaunchKernelEx(&cfg, route_decode_fused_kernel<T, EPL>, rp, pp, sp, cpc);
+}
+
+template <typename T>
+int launch_fused_route(const RouteParams& rp, const PlanParams& pp, const ScatterParams& sp, int ncta, int cpc,
+                       size_t smem, cudaStream_t st) {
+    cudaError_t err;
+    switch (experts_per_lane(rp.e)) {
+        case 1: err = launch_fused_route_epl<T, 1>(rp, pp, sp, ncta, cpc, smem, st); break;
+        case 2: err = launch_fused_route_epl<T, 2>(rp, pp, sp, ncta, cpc, smem, st); break;
+        case 4: err = launch_fused_route_epl<T, 4>(rp, pp, sp, ncta, cpc, smem, st); break;
+        default: err = launch_fused_route_epl<T, 8>(rp, pp, sp, ncta, cpc, smem, st); break;
+    }
+    CHRONOS_CUDA_CHECK(err);
+    return CHRONOS_OK;
+}
+
+// Launches the logit kernel and (unless `out_params` is given, in which case
+// the parameters are returned for the fused select + plan kernel) the select kernel.
+template <typename T>
+int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool prerouted,
+                 int32_t* topk_idx, float* topk_w, bool zero_acc, RouteParams* out_params = nullptr,
+                 void* y_direct = nullptr) {
+    const ChronosMoeShape& s = a->shape;
+    RouteParams rp = route_params(a, w, prerouted, topk_idx, topk_w, zero_acc, y_direct);
     const int64_t N = s.num_tokens;
     const bool small = N <= kRouteSmallMax;
-    rp.nchunks = route_chunks(s.hidden);
     // the logit kernel is the call's first launch (no PDL) and zeroes the counters;
     // with pre-routed inputs the caller zeroed them and the select kernel comes first
     if (!prerouted) {
@@ -419,7 +523,7 @@ int launch_tc(const CUtensorMap& a0r, const CUtensorMap& a1r, const CUtensorMap&
 
 template <typename T, int BN, int BN_DN, bool TM_DN = false>
 int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int kt_per_split_dn, int slot,
-                   bool direct, bool shared_last) {
+                   bool direct, bool shared_last, bool two_phase = false) {
     const ChronosMoeShape& s = a->shape;
     const int dt = s.dtype;
     const uint64_t N = static_cast<uint64_t>(s.num_tokens), H = s.hidden, F = s.ffn;
@@ -511,6 +615,11 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
         pd.sh_hrow = static_cast<int64_t>(N * K);
         pd.dn_done = &w.at<PlanHeader>(w.L->hdr)->dn_done;
         pd.y_out = a->y;
+        if (two_phase) {
+            pd.ys = w.ws + w.L->xp;
+            pd.pair_slot = w.at<int32_t>(w.L->pair_slot);
+            pd.k_pairs = static_cast<int>(K);
+        }
     }
     if constexpr (TM_DN) {
         // large batches: token-major tiles (128 tokens x 256 output columns)
@@ -668,18 +777,30 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     // (when its tiles, one per 128 or BN tokens and output-column tile, cover the SMs)
     const bool shared_last = tc && !direct && s.num_shared > 0 && aligned16(a->y) &&
                              (N + bn_dn - 1) / bn_dn * mt_dn >= sm_count();
+    // token-major shared-last calls combine in two phases: the routed units store
+    // their scaled rows (layer dtype) into the expert-ordered x buffer, dead once
+    // gate/up is done, and the shared units sum each token's rows in choice order
+    // (no fp32 accumulator: no zeroing, no reduce-adds)
+    const bool two_phase = tm_dn && shared_last && g_two_phase_enabled;
 
     int rc;
     // counters: zeroed by the logit kernel, or here when routing is skipped
     if (prerouted)
         CHRONOS_CUDA_CHECK(cudaMemsetAsync(w.ws + L.grp_count, 0, 4 * (s.num_experts + 1), st));
     const int slot = prof_begin_call();
-    // decode batches: the routing selection, plan and slot tables run in one block
+    // decode batches: the routing selection, plan and slot tables run in one block;
+    // with a cluster the logits run in that same launch (route_fused.cuh)
     const bool fused_plan = N <= kSelectPlanMaxTokens;
+    int f_ncta = 0, f_cpc = 0;
+    size_t f_smem = 0;
+    const bool cluster_route = fused_plan && !prerouted && g_fused_route_enabled &&
+                               fused_route_shape<T>(s, &f_ncta, &f_cpc, &f_smem);
     RouteParams rp{};
     prof_mark(slot, CHRONOS_STAGE_ROUTE, st);
-    if ((rc = launch_route<T>(a, w, st, prerouted, topk_idx, topk_w, true, fused_plan ? &rp : nullptr,
-                              direct ? a->y : nullptr)))
+    if (cluster_route)
+        rp = route_params(a, w, false, topk_idx, topk_w, true, direct ? a->y : nullptr);
+    else if ((rc = launch_route<T>(a, w, st, prerouted, topk_idx, topk_w, !two_phase,
+                                   fused_plan ? &rp : nullptr, direct ? a->y : nullptr)))
         return rc;
     prof_ran(slot, CHRONOS_STAGE_ROUTE);
     prof_mark(slot, CHRONOS_STAGE_PLAN, st);
@@ -724,12 +845,17 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     sp.slot_tok = w.at<int32_t>(L.slot_tok);
     sp.slot_coef = w.at<float>(L.slot_coef);
     sp.copy_rows = tc ? 1 : 0;
+    sp.pair_slot = two_phase ? w.at<int32_t>(L.pair_slot) : nullptr;
     if (fused_plan) {
         sp.copy_rows = 0;
         sp.slot_map = tc ? w.at<int32_t>(L.slot_map) : nullptr;
         sp.e = s.num_experts;
-        // first launch of the call when routing was skipped (pre-routed inputs)
-        if ((rc = launch_select_plan<T>(rp, pp, sp, s.num_experts, !prerouted, st))) return rc;
+        if (cluster_route) {
+            if ((rc = launch_fused_route<T>(rp, pp, sp, f_ncta, f_cpc, f_smem, st))) return rc;
+        } else if ((rc = launch_select_plan<T>(rp, pp, sp, s.num_experts, !prerouted, st))) {
+            // (the first launch of the call when routing was skipped: pre-routed inputs)
+            return rc;
+        }
     } else {
         const int64_t warps = N * s.top_k;
         const unsigned blocks =
@@ -748,7 +874,8 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
                 case 32: rc = launch_tc_pair<T, 32, 32>(a, w, st, kt_dn, slot, direct, shared_last); break;
                 case 64: rc = launch_tc_pair<T, 64, 64>(a, w, st, kt_dn, slot, direct, shared_last); break;
                 default:
-                    rc = tm_dn ? launch_tc_pair<T, 128, 128, true>(a, w, st, kt_dn, slot, direct, shared_last)
+                    rc = tm_dn ? launch_tc_pair<T, 128, 128, true>(a, w, st, kt_dn, slot, direct, shared_last,
+                                                                    two_phase)
                                : launch_tc_pair<T, 128, 128>(a, w, st, kt_dn, slot, direct, shared_last);
                     break;
             }
@@ -924,6 +1051,19 @@ extern "C" int chronos_moe_profile_end(float* stage_ms, int32_t* stage_launches,
 
 extern "C" uint64_t chronos_moe_kernel_launches(void) {
     return g_kernel_launches.load(std::memory_order_relaxed);
+}
+
+extern "C" int chronos_moe_set_option(const char* name, int64_t value) {
+    g_last_error.clear();
+    if (name != nullptr && std::strcmp(name, "fused_route") == 0) {
+        g_fused_route_enabled.store(value != 0);
+        return CHRONOS_OK;
+    }
+    if (name != nullptr && std::strcmp(name, "two_phase_combine") == 0) {
+        g_two_phase_enabled.store(value != 0);
+        return CHRONOS_OK;
+    }
+    return fail(CHRONOS_ERR_INVALID_ARG, "unknown option %s", name ? name : "(null)");
 }
 
 // ---------------------------------------------------------------------------
@@ -1122,8 +1262,8 @@ int attn_common_checks(const ChronosAttnArgs* a, const char* what) {
         return fail(CHRONOS_ERR_INVALID_ARG, "%s: batch %d, heads %d, kv_heads %d (heads must be a "
                     "multiple of kv_heads, at most %d per kv head)", what, a->batch, a->heads, a->kv_heads,
                     kAttnMaxRep);
-    if (a->head_dim < 2 || a->head_dim > 256 || (a->head_dim & 1))
-        return fail(CHRONOS_ERR_INVALID_ARG, "%s: head_dim %d (even, <= 256)", what, a->head_dim);
+    if (a->head_dim < 8 || a->head_dim > 256 || (a->head_dim % 8))
+        return fail(CHRONOS_ERR_INVALID_ARG, "%s: head_dim %d (a multiple of 8, <= 256)", what, a->head_dim);
     if (!known_dtype(a->dtype)) return fail(CHRONOS_ERR_INVALID_ARG, "%s: dtype %d unknown", what, a->dtype);
     if (a->table_len < 1) return fail(CHRONOS_ERR_INVALID_ARG, "%s: table_len %d", what, a->table_len);
     if (a->batch > 0 && (a->pos == nullptr || a->proj == nullptr || a->norm_q == nullptr ||
@@ -1164,7 +1304,12 @@ AttnParams attn_params(const ChronosAttnArgs* a) {
 }
 
 // Shared memory of one decode block, in the order the kernels lay it out.
-size_t mla_smem(const AttnParams& p) {
+// The weight slices of an MLA block, when staged in shared memory.
+size_t mla_wstage_bytes(const AttnParams& p, size_t elem) {
+    return elem * static_cast<size_t>(p.latent) * (p.nope + p.rope_dim + p.head_dim);
+}
+
+size_t mla_smem_base(const AttnParams& p) {
     const size_t rep = static_cast<size_t>(p.rep);
     return sizeof(float) * (rep * p.nope               // qn
                             + rep * p.rope_dim         // qr
@@ -1184,7 +1329,7 @@ size_t sw_smem(const AttnParams& p) {
 
 template <typename T>
 int mla_impl(const AttnParams& p, int batch, cudaStream_t st) {
-    const int smem = static_cast<int>(mla_smem(p));
+    const int smem = static_cast<int>(mla_smem_base(p) + (p.stage_w ? mla_wstage_bytes(p, sizeof(T)) : 0));
     if (int rc = set_smem(mla_decode_kernel<T>, smem)) return rc;
     CHRONOS_CUDA_CHECK(launch_kernel(mla_decode_kernel<T>, dim3(p.kv_heads, batch), dim3(kAttnThreads), smem,
                                      st, false, p));
@@ -1225,17 +1370,21 @@ extern "C" int chronos_mla_decode(const ChronosAttnArgs* a, void* stream) {
     using namespace chronos;
     g_last_error.clear();
     if (int rc = attn_common_checks(a, "chronos_mla_decode")) return rc;
-    if (a->rope_dim < 2 || (a->rope_dim & 1) || a->rope_dim >= a->head_dim || a->latent < 1 ||
-        a->latent > 256 || a->max_len < 1 || a->max_len > 8192)
-        return fail(CHRONOS_ERR_INVALID_ARG, "chronos_mla_decode: rope_dim %d (even, < head_dim %d), latent %d "
-                    "(1..256), max_len %d (1..8192)", a->rope_dim, a->head_dim, a->latent, a->max_len);
+    if (a->rope_dim < 8 || (a->rope_dim % 8) || a->rope_dim >= a->head_dim || a->latent < 8 ||
+        a->latent > 256 || (a->latent % 8) || a->max_len < 1 || a->max_len > 8192)
+        return fail(CHRONOS_ERR_INVALID_ARG, "chronos_mla_decode: rope_dim %d (a multiple of 8, < head_dim %d), "
+                    "latent %d (a multiple of 8, <= 256), max_len %d (1..8192)", a->rope_dim, a->head_dim,
+                    a->latent, a->max_len);
     if (a->batch > 0 && (a->norm_kv == nullptr || a->w_krope == nullptr || a->w_knope == nullptr ||
                          a->w_v == nullptr))
         return fail(CHRONOS_ERR_INVALID_ARG, "chronos_mla_decode: norm_kv, w_krope, w_knope and w_v are required");
-    const AttnParams p = attn_params(a);
-    if (mla_smem(p) > static_cast<size_t>(kAttnMaxSmem))
+    AttnParams p = attn_params(a);
+    const size_t wbytes = mla_wstage_bytes(p, a->dtype == CHRONOS_DTYPE_FP32 ? 4 : 2);
+    p.stage_w = mla_smem_base(p) + wbytes <= static_cast<size_t>(kAttnMaxSmem) ? 1 : 0;
+    const size_t need = mla_smem_base(p) + (p.stage_w ? wbytes : 0);
+    if (need > static_cast<size_t>(kAttnMaxSmem))
         return fail(CHRONOS_ERR_INVALID_ARG, "chronos_mla_decode: max_len %d x %d heads per kv head needs %zu "
-                    "bytes of shared memory (limit %d)", a->max_len, p.rep, mla_smem(p), kAttnMaxSmem);
+                    "bytes of shared memory (limit %d)", a->max_len, p.rep, need, kAttnMaxSmem);
     if (a->batch == 0) return CHRONOS_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     switch (a->dtype) {

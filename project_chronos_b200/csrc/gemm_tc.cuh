@@ -82,6 +82,14 @@ struct TcGemmParams {
     // (S_h x m_tiles, one token tile each), run before this call's plan exists;
     // their hidden rows start at sh_hrow + s * n_tokens
     int pre_units;
+    // Token-major down, two-phase combine (shared-last mode, large batches):
+    // routed units STORE coef * D rounded to the layer dtype into ys[slot]
+    // ([slots, H], no fp32 reduce-adds, no accumulator); the shared units then
+    // write y = sum_j ys[pair_slot[t, j]] (j ascending, fp32) + shared_coef * D.
+    // Null: routed units reduce-add into y_acc.
+    void* ys;
+    const int32_t* pair_slot;  // [n_tokens, k_pairs], -1 = no contribution
+    int k_pairs;
 };
 
 __host__ __device__ constexpr int tc_stage_bytes(int bn, bool gateup) {
@@ -1162,9 +1170,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int sf_target = min(static_cast<int>(gridDim.x), total_main);
         bool sf_counted = false, sf_ready = false;
         uint32_t yphase = 0;
+        const bool two_phase = p.ys != nullptr;
         for (int u = blockIdx.x; u < total; u += gridDim.x) {
             const bool sfu = u >= total_main;
             int64_t out_row = -1;  // y row of this thread's token, -1: padding row
+            int64_t out_slot = -1; // two-phase routed units: the row's slot in ys
             float coef = 0.0f;
             int n0;
             if (sfu) {
@@ -1187,6 +1197,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (tok < p.act_rows[w.a]) {
                     const int64_t slot = p.act_hrow[w.a] + tok;
                     out_row = p.slot_tok[slot];
+                    out_slot = slot;
                     coef = p.slot_coef[slot];
                 }
             }
@@ -1236,7 +1247,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 if (c0 > 0) bulk_wait_read();  // this thread's previous copy has read its row
                 float4* row4 = reinterpret_cast<float4*>(my_row);
-                if (sfu) {
+                if (sfu && !two_phase) {
                     // the pass's accumulator segment of every valid token row -> its
                     // staging row (the barrier orders the expected bytes before the copies)
                     const int64_t tile_tok0 = static_cast<int64_t>((u - total_main) % sf_tt) * kTmTokens;
@@ -1252,13 +1263,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                     yphase ^= 1u;
                 }
-                if (sfu || p.y_direct != nullptr) {
+                if (sfu || p.y_direct != nullptr || two_phase) {
                     // output dtype, written over the front of the row (2 bytes per
                     // column behind the 4-byte columns already read)
 #pragma unroll
                     for (int c = 0; c < PASS; c += 16) {
                         float yv[16];
-                        if (sfu) {
+                        if (sfu && two_phase) {
+                            // the token's routed contributions, in choice order
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) yv[j] = 0.0f;
+                            if (out_row >= 0) {
+                                for (int q2 = 0; q2 < p.k_pairs; ++q2) {
+                                    const int sl = __ldcg(p.pair_slot + out_row * p.k_pairs + q2);
+                                    if (sl < 0) continue;
+                                    const uint4* src = reinterpret_cast<const uint4*>(
+                                        static_cast<const T*>(p.ys) + static_cast<int64_t>(sl) * p.h + n0 + c0 + c);
+                                    const uint4 v0 = __ldcg(src), v1 = __ldcg(src + 1);
+                                    const T* e0 = reinterpret_cast<const T*>(&v0);
+                                    const T* e1 = reinterpret_cast<const T*>(&v1);
+#pragma unroll
+                                    for (int j = 0; j < 8; ++j) {
+                                        yv[j] += to_f32<T>(e0[j]);
+                                        yv[8 + j] += to_f32<T>(e1[j]);
+                                    }
+                                }
+                            }
+                        } else if (sfu) {
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {
                                 const float4 v = row4[c / 4 + j];
@@ -1287,6 +1318,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (out_row >= 0) {
                     if (sfu)
                         bulk_store(static_cast<T*>(p.y_out) + out_row * p.h + n0 + c0, my_row,
+                                   static_cast<uint32_t>(nc * sizeof(T)));
+                    else if (two_phase)
+                        bulk_store(static_cast<T*>(p.ys) + out_slot * p.h + n0 + c0, my_row,
                                    static_cast<uint32_t>(nc * sizeof(T)));
                     else if (p.y_direct != nullptr)
                         bulk_store(static_cast<T*>(p.y_direct) + out_row * p.h + n0 + c0, my_row,

@@ -163,6 +163,7 @@ struct ScatterParams {
     int copy_rows;        // 0: only the slot tables (B operand read from x by row index)
     int32_t* slot_map;    // decode batches: [E, N] slot of (expert, token) or -1
     int e;                // experts (rows of slot_map)
+    int32_t* pair_slot;   // [N, k] slot of (token, choice), -1 if unavailable; or null
 };
 
 constexpr int kScatterThreads = kPlanThreads;
@@ -200,12 +201,16 @@ __global__ void __launch_bounds__(kScatterThreads) plan_scatter_kernel(PlanParam
         p.slot_coef[s] = p.shared_coef[t];
     }
     const int ps = p.pos[gw];
-    if (ps < 0) return;
+    if (ps < 0) {
+        if (lane == 0 && p.pair_slot != nullptr) p.pair_slot[gw] = -1;
+        return;
+    }
     const int e = p.topk_idx[gw];
     const int64_t slot = static_cast<int64_t>(s_off[e]) + ps;
     if (lane == 0) {
         p.slot_tok[slot] = static_cast<int32_t>(t);
         p.slot_coef[slot] = p.sel_coef[gw];
+        if (p.pair_slot != nullptr) p.pair_slot[gw] = static_cast<int32_t>(slot);
     }
     if (!p.copy_rows) return;
     const T* src = static_cast<const T*>(p.x) + t * p.h;

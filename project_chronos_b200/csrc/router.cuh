@@ -355,11 +355,15 @@ __device__ __forceinline__ float expert_avail(const RouteParams& p, int e) {
 // sum_k w (1 - a).  EPL = experts per lane (E <= 32 * EPL).  The per-expert
 // statistics go to s_counts / s_mass (shared memory, the caller adds them to
 // the global ones once per block) when given, else straight to global memory.
+template <typename T, int EPL, typename Logits>
+__device__ __forceinline__ void select_from_logits(const RouteParams& p, int64_t t, int lane, Logits&& logits,
+                                                   int& mine_e, float& mine_w, float& mine_a,
+                                                   float& shared_extra, int* s_counts, float* s_mass);
+
 template <typename T, int EPL>
 __device__ __forceinline__ void select_token(const RouteParams& p, int64_t t, int lane, int& mine_e,
                                              float& mine_w, float& mine_a, float& shared_extra,
                                              int* s_counts = nullptr, float* s_mass = nullptr) {
-    const int E = p.e;
     mine_e = 0;
     mine_w = 0.0f;
     mine_a = 0.0f;
@@ -380,30 +384,45 @@ __device__ __forceinline__ void select_token(const RouteParams& p, int64_t t, in
         return;
     }
     const int C = p.nchunks;
+    const int E = p.e;
+    // partials[c][t][e] in global memory: the warp's lanes read consecutive experts,
+    // loads in groups of 16 ahead of the in-order adds
+    select_from_logits<T, EPL>(p, t, lane, [&](int e) {
+        const float* pp = p.partials + t * E + e;
+        const int64_t cs = p.n * E;
+        float s = 0.0f;
+        int c = 0;
+        for (; c + 16 <= C; c += 16) {
+            float r[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) r[u] = pp[(c + u) * cs];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) s = s + r[u];
+        }
+        for (; c < C; ++c) s = s + pp[c * cs];
+        if (p.bias) s = s + p.bias[e];
+        return s;
+    }, mine_e, mine_w, mine_a, shared_extra, s_counts, s_mass);
+}
+
+// The rest of a token's routing given its logits (`logits(e)`: the in-order
+// chunk sum plus bias of expert e): softmax, top-k by (logit desc, index asc),
+// optional renormalisation, availability, the top-k outputs and statistics.
+template <typename T, int EPL, typename Logits>
+__device__ __forceinline__ void select_from_logits(const RouteParams& p, int64_t t, int lane, Logits&& logits,
+                                                   int& mine_e, float& mine_w, float& mine_a,
+                                                   float& shared_extra, int* s_counts, float* s_mass) {
+    const int E = p.e;
+    mine_e = 0;
+    mine_w = 0.0f;
+    mine_a = 0.0f;
+    shared_extra = 0.0f;
     float v[EPL];
     float m = -INFINITY;
 #pragma unroll
     for (int q = 0; q < EPL; ++q) {
         const int e = lane + 32 * q;
-        float lg = -INFINITY;
-        if (e < E) {
-            // partials[c][t][e]: the warp's lanes read consecutive experts
-            const float* pp = p.partials + t * E + e;
-            const int64_t cs = p.n * E;
-            float s = 0.0f;
-            int c = 0;
-            // loads in groups of 16 ahead of the in-order adds
-            for (; c + 16 <= C; c += 16) {
-                float r[16];
-#pragma unroll
-                for (int u = 0; u < 16; ++u) r[u] = pp[(c + u) * cs];
-#pragma unroll
-                for (int u = 0; u < 16; ++u) s = s + r[u];
-            }
-            for (; c < C; ++c) s = s + pp[c * cs];
-            if (p.bias) s = s + p.bias[e];
-            lg = s;
-        }
+        const float lg = e < E ? logits(e) : -INFINITY;
         v[q] = lg;
         m = fmaxf(m, lg);
     }

@@ -79,6 +79,9 @@ class ExpertParallelMoE(nn.Module):
         # the CTAs the expert GEMMs may use while chunks are exchanged beside them
         self.chunks = 1
         self.gemm_ctas = 132
+        # optional phase timing: a list that each forward appends
+        # {phase: torch.cuda.Event} to (events on the compute stream)
+        self.phase_events = None
 
     @classmethod
     def from_stacked(cls, config, router: torch.Tensor, gate: torch.Tensor, up: torch.Tensor,
@@ -145,6 +148,15 @@ class ExpertParallelMoE(nn.Module):
             self.last_send_counts = self.last_recv_counts = None
             return y.view(shp)
 
+        marks = {} if self.phase_events is not None else None
+
+        def mark(name):
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks[name] = ev
+
+        mark("start")
         # 1-2: route, build the send buffers (rows ordered by token chunk, then rank)
         r = be.moe_route(xf, self.router, k, self.norm_topk_prob, num_shared=self.num_shared,
                          ffn=F, router_bias=self.router_logit_bias, want_probs=False)
@@ -154,6 +166,7 @@ class ExpertParallelMoE(nn.Module):
         max_ctas = 0 if C == 1 else self.gemm_ctas
         d = be.ep_dispatch(xf, r["topk_idx"], r["topk_weight"], E, G, avail=avail, num_chunks=C)
 
+        mark("dispatched")
         # 3: counts [C, G] -> per destination [G, C]; one host sync for every split size
         send_gc = d["send_counts"].reshape(C, G).t().contiguous()
         recv_gc = torch.empty_like(send_gc)
@@ -179,6 +192,7 @@ class ExpertParallelMoE(nn.Module):
             recv_x.append(rx)
             recv_meta.append(rm)
 
+        mark("counts_exchanged")
         y_shared = None
         if self.num_shared:
             no_slot = torch.full((E,), -1, dtype=torch.int32, device=dev)
@@ -193,10 +207,13 @@ class ExpertParallelMoE(nn.Module):
         local_router = torch.empty(self.experts_per_rank, H, dtype=dt, device=dev)
         back = torch.empty(n_send, H, dtype=dt, device=dev)
         back_works = []
+        mark("shared_done")
         for c in range(C):
             for w in works[c]:
                 if w is not None:
                     w.wait()
+            if c == 0:
+                mark("rows_arrived")
             rm = recv_meta[c]
             eid = rm[:, 0:1].contiguous()
             wgt = rm[:, 1:2].contiguous().view(torch.float32)
@@ -205,10 +222,15 @@ class ExpertParallelMoE(nn.Module):
                                    max_ctas=max_ctas)["y"]
             back_works.append(self._exchange(back[send_off[c]:send_off[c + 1]], y_loc, sc[c], rc[c],
                                              async_op=True))
+        mark("experts_done")
         for w in back_works:
             if w is not None:
                 w.wait()
+        mark("rows_returned")
 
         # 6: fold the returned rows and the shared term
         y = be.ep_combine(back, d["pair_slot"], k, y_shared=y_shared, num_tokens=xf.shape[0])
+        mark("combined")
+        if marks is not None:
+            self.phase_events.append(marks)
         return y.view(shp)

@@ -359,6 +359,20 @@ class ChronosForCausalLM(nn.Module):
         if getattr(config, "tie_word_embeddings", True):
             self.model.embed_tokens.weight = self.lm_head.weight
 
+    @classmethod
+    def on_device(cls, config, device, dtype) -> "ChronosForCausalLM":
+        """A model with uninitialised parameters allocated straight on ``device`` in
+        ``dtype`` (no host copy), rotary tables computed; fill the weights with
+        ``load_state_dict`` or an initialiser."""
+        with torch.device("meta"):
+            m = cls(config)
+        m = m.to_empty(device=device)
+        head_dim = getattr(config, "head_dim", None) or config.hidden_size // config.num_attention_heads
+        cos, sin = precompute_freqs_cis(head_dim, config.max_position_embeddings, config.rope_theta,
+                                        getattr(config, "rope_scaling", None))
+        m.model.freqs_cos, m.model.freqs_sin = cos.to(device), sin.to(device)
+        return m.to(dtype)
+
     def forward(self, input_ids, attention_mask=None, past_key_values=None, use_cache=False,
                 logits_to_keep: int = 0, labels=None, available_expert_masks=None, **kwargs):
         hidden, cache, aux, look = self.model(input_ids, attention_mask, past_key_values, use_cache,
@@ -398,8 +412,11 @@ class GraphedDecoder:
             self._body(advance=False)
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
+        before = ops.kernel_launches()
         with torch.cuda.graph(self.graph):
             self.logits, self.lookahead = self._body(advance=True)
+        # kernels of this package in one step (the graph replays exactly these)
+        self.launches_per_step = ops.kernel_launches() - before
 
     def _body(self, advance: bool):
         m = self.lm.model

@@ -493,6 +493,12 @@ def profile_end() -> dict:
     return out
 
 
+def set_option(name: str, value: int) -> None:
+    """Process-wide launch-sequence switch (``chronos_moe_set_option``), e.g.
+    ``set_option("fused_route", 0)`` for the two-kernel decode routing."""
+    N.check(N.load_library().chronos_moe_set_option(name.encode(), int(value)))
+
+
 def kernel_launches() -> int:
     """Kernels launched by the extension since it was loaded."""
     return int(N.load_library().chronos_moe_kernel_launches())

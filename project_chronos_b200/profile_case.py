@@ -3,6 +3,8 @@
     python -m project_chronos_b200.profile_case --workload prefill --calls 3
     python -m project_chronos_b200.profile_case --workload decode --tokens 1 --calls 3
     python -m project_chronos_b200.profile_case --workload ep --calls 3
+    python -m project_chronos_b200.profile_case --workload decode --tokens 64 --fused-route --calls 3
+    python -m project_chronos_b200.profile_case --workload model --tokens 32 --calls 3
 
 Builds the named synthetic workload on cuda:0 (``synthetic.WORKLOADS``),
 calls ``ops.moe_forward`` ``--calls`` times with an L2 flush (256 MB write)
@@ -22,15 +24,20 @@ from . import ops, synthetic as syn
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", default="prefill", choices=sorted(syn.WORKLOADS))
+    ap.add_argument("--workload", default="prefill", choices=sorted(syn.WORKLOADS) + ["model"])
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--calls", type=int, default=3)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--fused-route", action="store_true",
+                    help="decode routing as one cluster launch (chronos_moe_set_option)")
     args = ap.parse_args(argv)
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    ops.set_option("fused_route", 1 if args.fused_route else 0)
     if args.workload == "ep":
         return _ep(args, dev)
+    if args.workload == "model":
+        return _model(args, dev)
     wl = syn.named_workload(args.workload, tokens=args.tokens, seed=args.seed, device=dev)
     w = wl.weights
     s = wl.shape
@@ -52,6 +59,37 @@ def main(argv=None) -> int:
     ops.check_status(dev)
     print(f"{args.workload} tokens={wl.x.shape[0]} calls={args.calls} "
           f"avg_ms={total_ms / args.calls:.4f}")
+    return 0
+
+
+def _model(args, dev) -> int:
+    """Eager decode steps of the 8-layer model (synthetic.DECODE_MODEL): a
+    512-token prompt of --tokens rows, then --calls one-token steps."""
+    import types
+    from .model import ChronosForCausalLM
+    cfg = types.SimpleNamespace(**syn.DECODE_MODEL)
+    lm = ChronosForCausalLM.on_device(cfg, dev, torch.bfloat16)
+    syn.init_model_(lm, args.seed, dev)
+    lm.eval()
+    b = args.tokens or 32
+    g = torch.Generator(device=dev).manual_seed(args.seed + 1)
+    ids = torch.randint(0, cfg.vocab_size, (b, 512), generator=g, device=dev)
+    total_ms = 0.0
+    with torch.no_grad():
+        out, _ = lm(ids, use_cache=True, cache_capacity=512 + args.calls + 8)
+        cache = out.past_key_values
+        nxt = torch.argmax(out.logits[:, -1], dim=-1).view(-1, 1)
+        for _ in range(args.calls):
+            a = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            a.record()
+            out, _ = lm(nxt, past_key_values=cache, use_cache=True)
+            e.record()
+            torch.cuda.synchronize()
+            total_ms += a.elapsed_time(e)
+            nxt = torch.argmax(out.logits[:, -1], dim=-1).view(-1, 1)
+    ops.check_status(dev)
+    print(f"model batch={b} steps={args.calls} avg_ms={total_ms / args.calls:.4f}")
     return 0
 
 

@@ -210,6 +210,35 @@ def model_state(shapes, seed: int, std: float = 0.02, embed_std: float = 0.5,
     return out
 
 
+# The 8-layer Chronos model of the end-to-end decode workload (d_model 1024,
+# 8 heads / 2 kv heads of 128, MLA latent 64 + rope 32 on even layers, a
+# 2048-token window on odd layers, 16 experts top-2 + 1 shared, d_ff 2048,
+# vocab 6400, tied LM head, lookahead router of 2 steps).
+DECODE_MODEL = dict(vocab_size=6400, hidden_size=1024, num_hidden_layers=8, num_attention_heads=8,
+                    num_key_value_heads=2, max_position_embeddings=32768, num_experts=16,
+                    num_experts_per_tok=2, moe_intermediate_size=2048, num_shared_experts=1,
+                    norm_topk_prob=True, kv_latent_dim=64, rope_dim=32, sliding_window_size=2048,
+                    lookahead_steps=2, dropout=0.0, hidden_act="silu", rms_norm_eps=1e-5, rope_theta=1e6,
+                    tie_word_embeddings=True, rope_scaling=None, use_hybrid_attention=True,
+                    router_aux_loss_coef=5e-4, fallback_mask_prob=0.0, intermediate_size=2048, head_dim=128)
+
+
+def init_model_(model, seed: int, device) -> None:
+    """Seeded random init of a model's parameters on ``device``, in sorted-name
+    order with one device generator (RMSNorm weights N(1, 0.1), the embedding
+    N(0, 0.5), every other matrix N(0, 0.02))."""
+    g = torch.Generator(device=device)
+    g.manual_seed(int(seed))
+    with torch.no_grad():
+        for name, p in sorted(model.named_parameters()):
+            if name.endswith("norm.weight"):
+                p.normal_(1.0, 0.1, generator=g)
+            elif "embed_tokens" in name:
+                p.normal_(0.0, 0.5, generator=g)
+            else:
+                p.normal_(0.0, 0.02, generator=g)
+
+
 def flops_per_token_routed(shape: MoEShape) -> float:
     """FLOPs of one routed or shared SwiGLU application to one token."""
     return 2.0 * 3.0 * shape.hidden * shape.ffn
@@ -241,5 +270,5 @@ def decode_bytes(shape: MoEShape, tokens: int, experts_read: int, elem_bytes: in
 __all__ = ["MoEShape", "MoEWeights", "Workload", "WORKLOADS", "make_generator", "make_weights",
            "make_hidden", "make_mask", "make_zipf_bias", "make_workload", "named_workload",
            "layer_flops", "decode_bytes", "expert_bytes", "flops_per_token_routed", "make_ep_weights",
-           "model_state"]
+           "model_state", "DECODE_MODEL", "init_model_"]
 

@@ -308,3 +308,68 @@ def test_custom_op_registration():
                           True)
     assert torch.equal(idx, ref["topk_idx"])
     assert O.rel_l2(_np(y), _np(ref["y"])) < 1e-3  # bf16, run-order-dependent combine
+
+
+@pytest.mark.parametrize("n,h,e,k,s,dtype", [
+    (1, 2048, 64, 6, 2, torch.bfloat16), (8, 2048, 64, 6, 2, torch.bfloat16),
+    (33, 2048, 64, 6, 2, torch.bfloat16), (64, 2048, 64, 6, 2, torch.bfloat16),
+    (32, 1024, 16, 2, 1, torch.bfloat16), (17, 256, 256, 8, 1, torch.bfloat16),
+    (64, 4096, 64, 6, 0, torch.bfloat16), (3, 320, 8, 2, 1, torch.float32),
+    (12, 512, 16, 1, 0, torch.bfloat16)])
+def test_fused_decode_routing_matches_two_kernel_path(n, h, e, k, s, dtype):
+    """Decode routing as one cluster launch (route_fused.cuh) against the logit +
+    select/plan kernels: identical indices, weights, probabilities and
+    statistics; the layer output equal up to the order of fp32 reduce-adds;
+    indices equal to the oracle's."""
+    ops = _ops()
+    f = 64 if h % 64 == 0 else 48
+    wl = _workload(h, e, k, f, s, n, dtype=dtype, seed=n * 7 + e, avail_p=0.8)
+    avail = wl.mask.to(torch.float32)
+    outs = []
+    try:
+        for fused in (0, 1):
+            ops.set_option("fused_route", fused)
+            outs.append(_run(wl, k, True, avail=avail, want_stats=True))
+            torch.cuda.synchronize()
+            ops.check_status()
+    finally:
+        ops.set_option("fused_route", 0)
+    a, b = outs
+    for key in ("topk_idx", "topk_weight", "probs", "counts"):
+        assert torch.equal(a[key], b[key]), key
+    # a float sum of atomics: its order (and last bits) is scheduling-dependent in both paths
+    assert torch.allclose(a["mass"], b["mass"], rtol=1e-5, atol=1e-6)
+    tol = 1e-5 if dtype == torch.float32 else 1e-3
+    assert O.rel_l2(_np(b["y"]), _np(a["y"])) <= tol
+    o_idx, _, _, _ = O.route(_np(wl.x), _np(wl.weights.router), k, True)
+    assert np.array_equal(b["topk_idx"].cpu().numpy(), o_idx)
+
+
+# shapes whose (128-token x 256-column) output tiles cover the SMs, so the shared
+# experts run last in the token-major down GEMM
+@pytest.mark.parametrize("n,h,e,k,f,s", [(4096, 2048, 32, 4, 256, 2), (2560, 2560, 16, 2, 128, 1),
+                                         (8192, 1024, 64, 6, 192, 2)])
+def test_two_phase_combine_matches_reduce_adds(n, h, e, k, f, s):
+    """Large calls with the shared experts last in the token-major down GEMM:
+    the two-phase combine (slot rows stored in the layer dtype, summed per token
+    in choice order) against the fp32 reduce-add path and the oracle; the
+    two-phase output is bitwise reproducible run to run."""
+    ops = _ops()
+    wl = _workload(h, e, k, f, s, n, seed=n + e, avail_p=0.85)
+    avail = wl.mask.to(torch.float32)
+    outs = []
+    try:
+        for two in (0, 1, 1):
+            ops.set_option("two_phase_combine", two)
+            outs.append(_run(wl, k, True, avail=avail))
+            torch.cuda.synchronize()
+            ops.check_status()
+    finally:
+        ops.set_option("two_phase_combine", 1)
+    red, two, two_again = (_np(o["y"]) for o in outs)
+    assert np.array_equal(two, two_again)
+    assert O.rel_l2(two, red) <= 3e-3
+    emu, *_ = _oracle(wl, k, True, avail=avail, emulate=True)
+    assert O.rel_l2(two, emu) <= 3e-3
+    ref, *_ = _oracle(wl, k, True, avail=avail)
+    assert O.rel_l2(two, ref) <= 1e-2
