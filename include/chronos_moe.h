@@ -226,6 +226,10 @@ CHRONOS_API uint64_t chronos_moe_kernel_launches(void);
  *                  slot, the shared units sum each token's slots in choice order
  *                  (deterministic; no fp32 accumulator); 0: fp32 reduce-adds
  *                  into an accumulator.
+ *   "fold_finalize"  1 (default): a call below 1024 tokens with shared experts
+ *                  writes its output from the down GEMM, each 128-column tile
+ *                  converted by the CTA whose contribution completes it; 0: a
+ *                  separate finalize kernel.
  * Returns CHRONOS_OK, or CHRONOS_ERR_INVALID_ARG for an unknown name. */
 CHRONOS_API int chronos_moe_set_option(const char* name, int64_t value);
 

@@ -71,6 +71,11 @@ std::atomic<bool> g_fused_route_enabled{false};
 // reduce-adds.  Set by chronos_moe_set_option("two_phase_combine", 0/1).
 std::atomic<bool> g_two_phase_enabled{true};
 
+// Weight-major calls with shared experts: the down GEMM writes the output as
+// each column tile completes (no finalize kernel).  Set by
+// chronos_moe_set_option("fold_finalize", 0/1).
+std::atomic<bool> g_fold_enabled{true};
+
 inline void count_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
 
 // Launch with programmatic stream serialisation (`pdl`): the kernel may start
@@ -129,7 +134,7 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 struct Layout {
     size_t grp_count, grp_off, act_rows, act_xrow, act_hrow, act_wslot, act_eid, ustart_gu, partials,
         ustart_dn, hdr, pos, sel_coef, shared_coef, topk_idx, topk_w, slot_tok, slot_coef, slot_map, pair_slot,
-        xp, hid, y_acc, total;
+        tile_cnt, xp, hid, y_acc, total;
 };
 
 Layout make_layout(const ChronosMoeShape& s) {
@@ -164,6 +169,7 @@ Layout make_layout(const ChronosMoeShape& s) {
     L.slot_coef = take(4 * (N * K + S * N));
     L.slot_map = N <= static_cast<size_t>(kSelectPlanMaxTokens) ? take(4 * E * N) : off;
     L.pair_slot = take(4 * N * K);
+    L.tile_cnt = take(4 * ((H + 127) / 128));
     // x rows in expert order for the gate/up GEMM; once that GEMM is done, the
     // two-phase down GEMM's scaled slot rows (same size) go here
     L.xp = take(es * N * K * H);
@@ -523,7 +529,7 @@ int launch_tc(const CUtensorMap& a0r, const CUtensorMap& a1r, const CUtensorMap&
 
 template <typename T, int BN, int BN_DN, bool TM_DN = false>
 int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int kt_per_split_dn, int slot,
-                   bool direct, bool shared_last, bool two_phase = false) {
+                   bool direct, bool shared_last, bool two_phase = false, bool fold = false) {
     const ChronosMoeShape& s = a->shape;
     const int dt = s.dtype;
     const uint64_t N = static_cast<uint64_t>(s.num_tokens), H = s.hidden, F = s.ffn;
@@ -610,6 +616,10 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     pd.w_rows = static_cast<int>(H);
     pd.out_cols = static_cast<int>(H);
     pd.y_direct = direct ? a->y : nullptr;
+    if (fold) {
+        pd.tile_cnt = w.at<int32_t>(w.L->tile_cnt);
+        pd.y_fold = a->y;
+    }
     if (shared_last) {
         pd.sf_shared = static_cast<int>(S);
         pd.sh_hrow = static_cast<int64_t>(N * K);
@@ -782,6 +792,9 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     // gate/up is done, and the shared units sum each token's rows in choice order
     // (no fp32 accumulator: no zeroing, no reduce-adds)
     const bool two_phase = tm_dn && shared_last && g_two_phase_enabled;
+    // weight-major calls with shared experts (every output tile has units): the
+    // down GEMM writes the output tile by tile as the last contribution lands
+    const bool fold = tc && !tm_dn && !direct && !shared_last && s.num_shared > 0 && g_fold_enabled;
 
     int rc;
     // counters: zeroed by the logit kernel, or here when routing is skipped
@@ -827,6 +840,8 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     pp.act_eid = w.at<int32_t>(L.act_eid);
     pp.ustart_gu = w.at<int32_t>(L.ustart_gu);
     pp.ustart_dn = w.at<int32_t>(L.ustart_dn);
+    pp.tile_cnt = fold ? w.at<int32_t>(L.tile_cnt) : nullptr;
+    pp.n_tile_cnt = fold ? mt_dn : 0;
     // the plan is computed inside the scatter launch (stage "plan" stays empty)
     prof_mark(slot, CHRONOS_STAGE_SCATTER, st);
 
@@ -870,13 +885,14 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
             return fail(CHRONOS_ERR_INVALID_ARG, "internal: fp32 on the tensor-core path");
         } else {
             switch (bn) {
-                case 16: rc = launch_tc_pair<T, 16, 16>(a, w, st, kt_dn, slot, direct, shared_last); break;
-                case 32: rc = launch_tc_pair<T, 32, 32>(a, w, st, kt_dn, slot, direct, shared_last); break;
-                case 64: rc = launch_tc_pair<T, 64, 64>(a, w, st, kt_dn, slot, direct, shared_last); break;
+                case 16: rc = launch_tc_pair<T, 16, 16>(a, w, st, kt_dn, slot, direct, shared_last, false, fold); break;
+                case 32: rc = launch_tc_pair<T, 32, 32>(a, w, st, kt_dn, slot, direct, shared_last, false, fold); break;
+                case 64: rc = launch_tc_pair<T, 64, 64>(a, w, st, kt_dn, slot, direct, shared_last, false, fold); break;
                 default:
                     rc = tm_dn ? launch_tc_pair<T, 128, 128, true>(a, w, st, kt_dn, slot, direct, shared_last,
                                                                     two_phase)
-                               : launch_tc_pair<T, 128, 128>(a, w, st, kt_dn, slot, direct, shared_last);
+                               : launch_tc_pair<T, 128, 128>(a, w, st, kt_dn, slot, direct, shared_last, false,
+                                                             fold);
                     break;
             }
         }
@@ -886,7 +902,7 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     if (rc) return rc;
 
     prof_mark(slot, CHRONOS_STAGE_FINALIZE, st);
-    if (direct || shared_last) {
+    if (direct || shared_last || fold) {
         prof_mark(slot, kBoundaries - 1, st);
         return CHRONOS_OK;
     }
@@ -1057,6 +1073,10 @@ extern "C" int chronos_moe_set_option(const char* name, int64_t value) {
     g_last_error.clear();
     if (name != nullptr && std::strcmp(name, "fused_route") == 0) {
         g_fused_route_enabled.store(value != 0);
+        return CHRONOS_OK;
+    }
+    if (name != nullptr && std::strcmp(name, "fold_finalize") == 0) {
+        g_fold_enabled.store(value != 0);
         return CHRONOS_OK;
     }
     if (name != nullptr && std::strcmp(name, "two_phase_combine") == 0) {

@@ -267,6 +267,8 @@ __device__ __forceinline__ void bulk_wait_read() {
 }
 // Wait until this thread's committed bulk copies completed.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Every bulk group of this thread but the newest is complete (writes done).
+__device__ __forceinline__ void bulk_wait_group_1() { asm volatile("cp.async.bulk.wait_group 1;" ::: "memory"); }
 
 // Barrier among the `count` threads of the epilogue warps (id 1; id 0 is __syncthreads).
 __device__ __forceinline__ void epilogue_bar_sync(int count) {

@@ -90,6 +90,13 @@ struct TcGemmParams {
     void* ys;
     const int32_t* pair_slot;  // [n_tokens, k_pairs], -1 = no contribution
     int k_pairs;
+    // Weight-major down (decode), finalize folded in: when a unit's reduce-adds
+    // into output-column tile m are complete, its CTA counts them in
+    // tile_cnt[m]; the CTA whose count completes the tile (units_dn / m_tiles
+    // units) writes that tile of y_fold = y_acc in the output dtype.  Null: a
+    // finalize kernel follows.
+    int32_t* tile_cnt;
+    void* y_fold;
 };
 
 __host__ __device__ constexpr int tc_stage_bytes(int bn, bool gateup) {
@@ -488,6 +495,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int sf_target = min(static_cast<int>(gridDim.x), total_main);
         bool sf_counted = false, sf_ready = false;
         uint32_t yphase = 0;
+        // folded finalize: the output-column tile of the previous unit, counted in
+        // once its reduce-adds are complete (one unit later: no wait on the newest)
+        int fold_pending = -1;
+        volatile int* fold_last = abort_flag + 2;
+        auto fold_retire = [&](int tile) {
+            fence_proxy_async_global();
+            epilogue_bar_sync(128);
+            if (et == 0) {
+                __threadfence();
+                const int done = atomicAdd(p.tile_cnt + tile, 1) + 1;
+                const bool last = done == p.hdr->units_dn / p.m_tiles;
+                if (last) __threadfence();
+                *fold_last = last ? 1 : 0;
+            }
+            epilogue_bar_sync(128);
+            if (*fold_last) {
+                const int m0f = tile * kTcBM;
+                const int ncf = min(kTcBM, p.out_cols - m0f);
+                const int64_t cnt = p.n_tokens * ncf;
+                for (int64_t i = et; i < cnt; i += 128) {
+                    const int64_t t = i / ncf;
+                    const int c = static_cast<int>(i - t * ncf);
+                    static_cast<T*>(p.y_fold)[t * p.h + m0f + c] =
+                        from_f32<T>(__ldcg(p.y_acc + t * p.h + m0f + c));
+                }
+            }
+        };
         for (int u = blockIdx.x;; u += gridDim.x) {
             if (u >= pre_units) {
                 if (!planned) load_plan();
@@ -711,11 +745,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 bulk_commit();
             }
+            if constexpr (!GATEUP) {
+                if (p.y_fold != nullptr) {
+                    // one bulk group per unit (BN <= 128 staging rows): waiting for all
+                    // but the newest leaves the previous unit's reduce-adds complete
+                    static_assert(GATEUP || BN <= 128, "one bulk group per down unit");
+                    if (fold_pending >= 0) {
+                        bulk_wait_group_1();
+                        fold_retire(fold_pending);
+                    }
+                    fold_pending = w.mtile;
+                }
+            }
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         }
         // a CTA without shared-last units (or that stopped early) still counts itself in
         if (sf_count && !sf_counted) tc_count_routed_done(p.dn_done, et);
         bulk_wait_all();
+        if constexpr (!GATEUP) {
+            if (p.y_fold != nullptr && fold_pending >= 0 && *ep_ok) fold_retire(fold_pending);
+        }
     }
 
     tc_fence_before();

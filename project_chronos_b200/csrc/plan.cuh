@@ -49,6 +49,8 @@ struct PlanParams {
     int32_t* act_eid;    // routed expert id, or -1 for a shared group
     int32_t* ustart_gu;  // [A + 1]
     int32_t* ustart_dn;  // [A + 1]
+    int32_t* tile_cnt;   // [n_tile_cnt] down output-tile counters (folded finalize), zeroed here; or null
+    int n_tile_cnt;
 };
 
 constexpr int kPlanThreads = 256;  // >= the 256 experts the ABI accepts: one expert per thread
@@ -124,6 +126,7 @@ __device__ __forceinline__ void plan_tables(const PlanParams& p, int cnt, int in
             p.ustart_dn[a] = S * sh_dn + inc_dn - udn;
         }
     }
+    for (int i = tid; i < p.n_tile_cnt; i += NT) p.tile_cnt[i] = 0;
     if (tid < S) {
         p.act_rows[tid] = N;
         p.act_xrow[tid] = 0;

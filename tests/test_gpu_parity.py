@@ -373,3 +373,27 @@ def test_two_phase_combine_matches_reduce_adds(n, h, e, k, f, s):
     assert O.rel_l2(two, emu) <= 3e-3
     ref, *_ = _oracle(wl, k, True, avail=avail)
     assert O.rel_l2(two, ref) <= 1e-2
+
+
+@pytest.mark.parametrize("n", [1, 8, 33, 64, 200, 700])
+def test_folded_finalize_matches_finalize_kernel(n):
+    """Calls below 1024 tokens with shared experts: the down GEMM writing each
+    output-column tile when its last contribution lands, against the separate
+    finalize kernel and the oracle (several calls in a row: the tile counters
+    are re-armed by every call's plan)."""
+    ops = _ops()
+    wl = _workload(512, 32, 4, 256, 2, n, seed=n + 5, avail_p=0.8)
+    avail = wl.mask.to(torch.float32)
+    outs = []
+    try:
+        for fold in (0, 1, 1, 1):
+            ops.set_option("fold_finalize", fold)
+            outs.append(_np(_run(wl, 4, True, avail=avail)["y"]))
+            torch.cuda.synchronize()
+            ops.check_status()
+    finally:
+        ops.set_option("fold_finalize", 1)
+    for y in outs[1:]:
+        assert O.rel_l2(y, outs[0]) <= 1e-3
+    emu, idx, _, _ = _oracle(wl, 4, True, avail=avail, emulate=True)
+    assert O.rel_l2(outs[-1], emu) <= 3e-3
