@@ -100,6 +100,12 @@ typedef struct ChronosNormArgs {
 
 CHRONOS_API int chronos_add_rmsnorm(const ChronosNormArgs* args, void* cuda_stream);
 
+/* The index of the first maximal value of every row of x [rows, cols] (NaN
+ * counts as the maximum), into out [rows] (int64): the greedy pick of a decode
+ * step, torch.argmax(logits, dim=-1).  One block per row. */
+CHRONOS_API int chronos_argmax_rows(const void* x, int64_t rows, int32_t cols, int32_t dtype, int64_t* out,
+                                    void* cuda_stream);
+
 CHRONOS_API size_t chronos_attn_args_size(void);
 CHRONOS_API size_t chronos_norm_args_size(void);
 

@@ -8,8 +8,9 @@
  *
  * with K = lookahead_steps + 1 (s = 0 the current step, s >= 1 the predicted
  * future steps).  One launch per call: both projections, the SiLU and the K
- * softmaxes of a group of tokens run in one block, accumulating in fp32 and
- * rounding once to the output type.  Conventions as in chronos_moe.h.
+ * softmaxes of a group of up to 8 tokens run in one thread-block cluster (W1's
+ * rows split over its CTAs), accumulating in fp32 and rounding once to the
+ * output type.  Conventions as in chronos_moe.h.
  */
 #ifndef CHRONOS_LOOKAHEAD_H_
 #define CHRONOS_LOOKAHEAD_H_

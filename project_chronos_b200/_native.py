@@ -47,7 +47,7 @@ EXPORTS = ("chronos_moe_workspace_size", "chronos_moe_forward", "chronos_moe_rou
            "chronos_ep_dispatch", "chronos_ep_combine", "chronos_ep_dispatch_args_size",
            "chronos_ep_combine_args_size", "chronos_lookahead_forward", "chronos_lookahead_args_size",
            "chronos_mla_decode", "chronos_sw_decode", "chronos_add_rmsnorm", "chronos_attn_args_size",
-           "chronos_norm_args_size")
+           "chronos_norm_args_size", "chronos_argmax_rows")
 
 EP_MAX_RANKS = 32  # CHRONOS_EP_MAX_RANKS
 
@@ -260,6 +260,9 @@ def load_library(path: str = LIB_PATH):
                        ("chronos_add_rmsnorm", ChronosNormArgs)):
             getattr(lib, fn).argtypes = [ctypes.POINTER(st), ctypes.c_void_p]
             getattr(lib, fn).restype = ctypes.c_int
+        lib.chronos_argmax_rows.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                            ctypes.c_void_p, ctypes.c_void_p]
+        lib.chronos_argmax_rows.restype = ctypes.c_int
         lib.chronos_attn_args_size.argtypes = []
         lib.chronos_attn_args_size.restype = ctypes.c_size_t
         lib.chronos_norm_args_size.argtypes = []

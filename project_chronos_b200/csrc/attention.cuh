@@ -1,15 +1,18 @@
 // attention.cuh — one-token decode of the hybrid attention
 // (chronos/model/hybrid_attention.py) and the residual add + RMSNorm of a block.
 //
-// Both decode kernels run one block per (kv head g, batch row b), 256 threads,
-// and do, in one launch: the per-head RMSNorms of the new token's projections,
-// RoPE at its position, the cache append, the scores of the group's n_rep
-// query heads against every cached token, the softmax and the weighted sum.
+// Both decode kernels run one thread-block cluster per (kv head g, batch row
+// b), `splits` CTAs of 256 threads that share the cached positions, and do, in
+// one launch: the per-head RMSNorms of the new token's projections, RoPE at its
+// position, the cache append, the scores of the group's n_rep query heads
+// against every cached token, the softmax and the weighted sum.
 // Arithmetic is fp32; values are rounded to the layer type where the
 // reference's torch code holds a tensor in that type (norm and RoPE outputs,
 // the new cache entries, the softmax probabilities, the output), so a bf16
 // layer rounds where the reference's bf16 run rounds.
 #pragma once
+
+#include <cooperative_groups.h>
 
 #include "common.cuh"
 
@@ -22,6 +25,8 @@ constexpr int kAttnMaxRep = 8;
 struct AttnParams {
     int heads, kv_heads, rep, head_dim, rope_dim, nope, latent, window, max_len, table_len;
     int stage_w;   // MLA: 1 = the group's weight slices are staged in shared memory
+    int splits;    // CTAs per (kv head, batch row): the cluster size
+    int cap;       // score slots per head and CTA: ceil(cached positions / splits)
     float eps, scale;
     const int32_t* pos;
     const void* proj;
@@ -54,12 +59,6 @@ __device__ __forceinline__ float round_to(float v) {
     return to_f32<T>(from_f32<T>(v));
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -86,26 +85,6 @@ __device__ __forceinline__ float rope_value(const float* x, int i, int len, cons
     const int half = len >> 1;
     const float rot = i < half ? -x[i + half] : x[i - half];
     return round_to<T>(round_to<T>(x[i] * to_f32<T>(crow[i])) + round_to<T>(rot * to_f32<T>(srow[i])));
-}
-
-// Softmax over each head's scores (one warp per head), probabilities rounded to T.
-template <typename T>
-__device__ __forceinline__ void heads_softmax(float* sc, int rep, int stride, int n, int warp, int lane) {
-    for (int h = warp; h < rep; h += kAttnWarps) {
-        float* s = sc + h * stride;
-        float m = -INFINITY;
-        for (int t = lane; t < n; t += 32) m = fmaxf(m, s[t]);
-        m = warp_max(m);
-        float sum = 0.0f;
-        for (int t = lane; t < n; t += 32) {
-            const float e = __expf(s[t] - m);
-            s[t] = e;
-            sum += e;
-        }
-        const float inv = 1.0f / warp_sum(sum);
-        __syncwarp();
-        for (int t = lane; t < n; t += 32) s[t] = round_to<T>(s[t] * inv);
-    }
 }
 
 // ---------------------------------------------------------------------------
@@ -145,34 +124,45 @@ __global__ void __launch_bounds__(kAttnThreads) add_rmsnorm_kernel(NormParams p)
     }
 }
 
-// 8 consecutive values as fp32: one 16-byte load for 2-byte types, two for fp32
-// (the caller guarantees 16-byte alignment).
+// ---------------------------------------------------------------------------
+// arg-max of every row (the greedy pick of a decode step): the index of the
+// first maximal value, NaN counting as the maximum (as torch.argmax does).
+// One block per row, threads over columns, then a warp and a block reduction.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ bool argmax_better(float v, int i, float bv, int bi) {
+    const bool vn = v != v, bn = bv != bv;
+    if (vn || bn) return vn && (!bn || i < bi);
+    return v > bv || (v == bv && i < bi);
+}
+
 template <typename T>
-__device__ __forceinline__ void load8(const T* p, float* v);
-template <>
-__device__ __forceinline__ void load8<float>(const float* p, float* v) {
-    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-}
-template <>
-__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float* v) {
-    const uint4 u = *reinterpret_cast<const uint4*>(p);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+__global__ void __launch_bounds__(kAttnThreads) argmax_rows_kernel(const T* x, int64_t rows, int cols,
+                                                                   int64_t* out) {
+    __shared__ float s_v[kAttnWarps];
+    __shared__ int s_i[kAttnWarps];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const T* row = x + r * cols;
+        float bv = -INFINITY;
+        int bi = cols;
+        for (int c = threadIdx.x; c < cols; c += kAttnThreads) {
+            const float v = to_f32<T>(row[c]);
+            if (argmax_better(v, c, bv, bi)) { bv = v; bi = c; }
+        }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        v[2 * i] = __uint_as_float(w[i] << 16);
-        v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-    }
-}
-template <>
-__device__ __forceinline__ void load8<__half>(const __half* p, float* v) {
-    const uint4 u = *reinterpret_cast<const uint4*>(p);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-        v[2 * i] = f.x;
-        v[2 * i + 1] = f.y;
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (argmax_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) { s_v[warp] = bv; s_i[warp] = bi; }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int w = 1; w < kAttnWarps; ++w)
+                if (argmax_better(s_v[w], s_i[w], bv, bi)) { bv = s_v[w]; bi = s_i[w]; }
+            out[r] = bi < cols ? bi : 0;
+        }
+        __syncthreads();
     }
 }
 
@@ -232,37 +222,148 @@ __device__ __forceinline__ void weighted_rows(const T* rows, int64_t stride, int
 }
 
 // ---------------------------------------------------------------------------
+// Split decode.  The cached positions of one (kv head g, batch row b) are
+// divided over a thread-block cluster of `splits` CTAs.  Every CTA computes the
+// token's query (norms, RoPE) itself; CTA s scores positions
+// [s*chunk, (s+1)*chunk).  The cluster agrees on each head's maximum and
+// exponential sum through distributed shared memory before any probability is
+// rounded, so every probability is the one a single block would round; each
+// CTA then forms the weighted sum of its positions, and the partial sums are
+// added in CTA order.  Four cluster barriers, reached by every thread of every
+// CTA; the last keeps each CTA's shared memory alive until its peers have read
+// it.
+// ---------------------------------------------------------------------------
+
+// Scores of positions [t_lo, t_hi) for every head of the group into
+// sc[h * cap + t - t_lo].  Four lanes per position (lane sub takes the 8-column
+// groups sub, sub + 4, ...), summed by two butterfly steps.  Column group
+// q < w1/8 comes from `rows1` (row stride st1, query q1 [rep][w1]), the others
+// from `rows2` (st2, q2 [rep][w2]); the row at `fresh_t` comes from shared
+// memory (f1, f2) instead.
+template <typename T>
+__device__ __forceinline__ void split_scores(const T* rows1, int64_t st1, const float* q1, int w1, const float* f1,
+                                             const T* rows2, int64_t st2, const float* q2, int w2,
+                                             const float* f2, int t_lo, int t_hi, int fresh_t, int rep,
+                                             float scale, float* sc, int cap, int warp, int lane) {
+    const int g1 = w1 / 8, gall = g1 + w2 / 8, sub = lane & 3;
+    for (int base = t_lo + warp * 8; base < t_hi; base += kAttnWarps * 8) {   // uniform per warp
+        const int t = base + (lane >> 2);
+        const bool ok = t < t_hi;
+        float acc[kAttnMaxRep];
+#pragma unroll
+        for (int h = 0; h < kAttnMaxRep; ++h) acc[h] = 0.0f;
+        if (ok) {
+            const bool fresh = t == fresh_t;
+#pragma unroll 4
+            for (int q = sub; q < gall; q += 4) {
+                const bool first = q < g1;
+                const int c = first ? q * 8 : (q - g1) * 8;
+                float v[8];
+                if (fresh) {
+                    const float* f = first ? f1 : f2;
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) v[u] = f[c + u];
+                } else {
+                    load8<T>(first ? rows1 + static_cast<int64_t>(t) * st1 + c
+                                   : rows2 + static_cast<int64_t>(t) * st2 + c, v);
+                }
+                const float* qq = first ? q1 + c : q2 + c;
+                const int qs = first ? w1 : w2;
+#pragma unroll
+                for (int h = 0; h < kAttnMaxRep; ++h)
+                    if (h < rep)
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) acc[h] = fmaf(qq[h * qs + u], v[u], acc[h]);
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < kAttnMaxRep; ++h) {
+            acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 1);
+            acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 2);
+        }
+        if (ok && sub == 0)
+#pragma unroll
+            for (int h = 0; h < kAttnMaxRep; ++h)
+                if (h < rep) sc[h * cap + (t - t_lo)] = acc[h] * scale;
+    }
+}
+
+// The cluster-wide softmax of the scores sc[h * cap + i], i < cnt, rounded to T
+// in place.  red[0..rep) and red[kAttnMaxRep..+rep) are this CTA's published
+// maximum and sum.  Contains two cluster barriers.
+template <typename T>
+__device__ __forceinline__ void split_softmax(cooperative_groups::cluster_group& cluster, float* sc, int cap,
+                                              int cnt, int rep, float* red, int warp, int lane) {
+    const int splits = static_cast<int>(cluster.num_blocks());
+    for (int h = warp; h < rep; h += kAttnWarps) {
+        float m = -INFINITY;
+        for (int i = lane; i < cnt; i += 32) m = fmaxf(m, sc[h * cap + i]);
+        m = warp_max(m);
+        if (lane == 0) red[h] = m;
+    }
+    cluster.sync();
+    for (int h = warp; h < rep; h += kAttnWarps) {
+        float m = lane < splits ? cluster.map_shared_rank(red, lane)[h] : -INFINITY;
+        m = warp_max(m);
+        float sum = 0.0f;
+        for (int i = lane; i < cnt; i += 32) {
+            const float e = __expf(sc[h * cap + i] - m);
+            sc[h * cap + i] = e;
+            sum += e;
+        }
+        sum = warp_sum(sum);
+        if (lane == 0) red[kAttnMaxRep + h] = sum;
+    }
+    cluster.sync();
+    for (int h = warp; h < rep; h += kAttnWarps) {
+        float tot = 0.0f;
+        if (lane == 0)
+            for (int r = 0; r < splits; ++r) tot += cluster.map_shared_rank(red, r)[kAttnMaxRep + h];
+        const float inv = 1.0f / __shfl_sync(0xffffffffu, tot, 0);
+        for (int i = lane; i < cnt; i += 32) sc[h * cap + i] = round_to<T>(sc[h * cap + i] * inv);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // MLA decode (hybrid_attention.py:116-179 with a cache, S = 1)
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) {
+    namespace cg = cooperative_groups;
     extern __shared__ __align__(16) float msm[];
-    const int g = blockIdx.x, b = blockIdx.y;
-    const int rep = p.rep, nope = p.nope, R = p.rope_dim, L = p.latent, D = p.head_dim;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int splits = p.splits;
+    const int sidx = blockIdx.x % splits, g = blockIdx.x / splits, b = blockIdx.y;
+    const int rep = p.rep, nope = p.nope, R = p.rope_dim, L = p.latent, D = p.head_dim, cap = p.cap;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // the group's slices of k_nope_proj [nope, L], k_rope_proj [R, L], v_proj [D, L]:
-    // staged in shared memory when they fit, else read where they are (L2)
+    // this CTA's output rows d0 .. d1 - 1 of the value up-projection
+    const int dper = (D + splits - 1) / splits;
+    const int d0 = min(D, sidx * dper), d1 = min(D, d0 + dper);
+    // the group's k_nope_proj [nope, L] and k_rope_proj [R, L] slices and this
+    // CTA's v_proj rows: staged in shared memory when they fit, else read in L2
     const T* wkn_g = static_cast<const T*>(p.w_knope) + static_cast<int64_t>(g) * nope * L;
     const T* wkr_g = static_cast<const T*>(p.w_krope) + static_cast<int64_t>(g) * R * L;
-    const T* wv_g = static_cast<const T*>(p.w_v) + static_cast<int64_t>(g) * D * L;
+    const T* wv_g = static_cast<const T*>(p.w_v) + (static_cast<int64_t>(g) * D + d0) * L;
     T* wstage = reinterpret_cast<T*>(msm);
-    const int wcount = p.stage_w ? L * (nope + R + D) : 0;
+    const int wcount = p.stage_w ? L * (nope + R + dper) : 0;
     const T* wkn = p.stage_w ? wstage : wkn_g;
     const T* wkr = p.stage_w ? wstage + nope * L : wkr_g;
-    const T* wv = p.stage_w ? wstage + (nope + R) * L : wv_g;
+    const T* wv = p.stage_w ? wstage + (nope + R) * L : wv_g;   // rows d0 ..
     float* qn = reinterpret_cast<float*>(wstage + wcount);   // [rep][nope]
     float* qr = qn + rep * nope;           // [rep][R]
     float* qabs = qr + rep * R;            // [rep][L]
-    float* ctx = qabs + rep * L;           // [rep][L]
-    float* cnew = ctx + rep * L;           // [L]
+    float* ctx = qabs + rep * L;           // [rep][L] combined weighted latent
+    float* part = ctx + rep * L;           // [rep][L] this CTA's weighted latent
+    float* cnew = part + rep * L;          // [L]
     float* krn = cnew + L;                 // [R]
     float* tmp = krn + R;                  // [(rep+1)*R] rotated q_rope heads and k_rope
-    float* sc = tmp + (rep + 1) * R;       // [rep][max_len]
+    float* red = tmp + (rep + 1) * R;      // [2 * kAttnMaxRep]
+    float* sc = red + 2 * kAttnMaxRep;     // [rep][cap]
     const int pos = *p.pos;
     T* out = static_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.heads + g * rep) * D;
     if (pos < 0 || pos >= p.max_len || pos >= p.table_len) {   // outside the cache: no access
         for (int i = threadIdx.x; i < rep * D; i += kAttnThreads) out[i] = from_f32<T>(0.0f);
-        return;
+        return;   // every CTA of the cluster returns here (same pos)
     }
     const int n = pos + 1;
     const int width = p.heads * (nope + R) + L;
@@ -270,7 +371,7 @@ __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) 
     if (p.stage_w) {
         stage_rows<T>(wstage, wkn_g, nope * L);
         stage_rows<T>(wstage + nope * L, wkr_g, R * L);
-        stage_rows<T>(wstage + (nope + R) * L, wv_g, D * L);
+        stage_rows<T>(wstage + (nope + R) * L, wv_g, (d1 - d0) * L);
     }
     for (int i = threadIdx.x; i < rep * nope; i += kAttnThreads)
         qn[i] = to_f32<T>(row[(g * rep) * nope + i]);
@@ -285,11 +386,12 @@ __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) 
         else warp_rmsnorm<T>(cnew, L, static_cast<const T*>(p.norm_kv), p.eps, lane);
     }
     __syncthreads();
-    // k_rope of the new token: k_rope_proj(c) (rounded as the bf16 linear rounds)
-    for (int r = threadIdx.x; r < R; r += kAttnThreads) {
+    // k_rope of the new token: k_rope_proj(c), a warp per output (rounded as the bf16 linear rounds)
+    for (int r = warp; r < R; r += kAttnWarps) {
         float acc = 0.0f;
-        for (int j = 0; j < L; ++j) acc = fmaf(to_f32<T>(wkr[r * L + j]), cnew[j], acc);
-        krn[r] = round_to<T>(acc);
+        for (int j = lane; j < L; j += 32) acc = fmaf(to_f32<T>(wkr[r * L + j]), cnew[j], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) krn[r] = round_to<T>(acc);
     }
     // q_abs = W_kn^T q_nope: the key up-projection folded into the query
     for (int i = threadIdx.x; i < rep * L; i += kAttnThreads) {
@@ -313,71 +415,55 @@ __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) 
         (h < rep ? qr + h * R : krn)[e] = tmp[i];
     }
     __syncthreads();
-    // append the new token to the cache (the latent once, by the group-0 block)
+    // append the new token to the cache (by CTA 0 of the cluster; the latent once, by group 0)
     T* cache_c = static_cast<T*>(p.cache_a) + static_cast<int64_t>(b) * p.max_len * L;
     T* cache_k = static_cast<T*>(p.cache_b) + static_cast<int64_t>(b) * p.max_len * p.kv_heads * R;
-    if (g == 0)
-        for (int j = threadIdx.x; j < L; j += kAttnThreads)
-            cache_c[static_cast<int64_t>(pos) * L + j] = from_f32<T>(cnew[j]);
-    for (int r = threadIdx.x; r < R; r += kAttnThreads)
-        cache_k[(static_cast<int64_t>(pos) * p.kv_heads + g) * R + r] = from_f32<T>(krn[r]);
-    // scores: one cached token per thread (its latent and rope key as 16-byte loads),
-    // every head of the group
-    for (int t = threadIdx.x; t < n; t += kAttnThreads) {
+    if (sidx == 0) {
+        if (g == 0)
+            for (int j = threadIdx.x; j < L; j += kAttnThreads)
+                cache_c[static_cast<int64_t>(pos) * L + j] = from_f32<T>(cnew[j]);
+        for (int r = threadIdx.x; r < R; r += kAttnThreads)
+            cache_k[(static_cast<int64_t>(pos) * p.kv_heads + g) * R + r] = from_f32<T>(krn[r]);
+    }
+    // this CTA's positions: latent against q_abs, rope key against q_rope
+    const int chunk = (n + splits - 1) / splits;
+    const int t_lo = min(n, sidx * chunk), t_hi = min(n, t_lo + chunk), cnt = t_hi - t_lo;
+    split_scores<T>(cache_c, L, qabs, L, cnew, cache_k + g * R, static_cast<int64_t>(p.kv_heads) * R, qr, R, krn,
+                    t_lo, t_hi, pos, rep, p.scale, sc, cap, warp, lane);
+    __syncthreads();
+    split_softmax<T>(cluster, sc, cap, cnt, rep, red, warp, lane);
+    __syncthreads();
+    // this CTA's weighted latent sum_t p_t c_t per head
+    weighted_rows<T>(cache_c + static_cast<int64_t>(t_lo) * L, L, cnt, L, sc, cap, rep, pos - t_lo, cnew, warp,
+                     lane, [&](int h, int c, float v) { part[h * L + c] = v; });
+    cluster.sync();
+    for (int i = threadIdx.x; i < rep * L; i += kAttnThreads) {
+        float v = 0.0f;
+        for (int r = 0; r < splits; ++r) v += cluster.map_shared_rank(part, r)[i];
+        ctx[i] = v;
+    }
+    __syncthreads();
+    // out = W_v ctx for this CTA's rows: the value up-projection applied once to the weighted latent
+    for (int d = d0 + warp; d < d1; d += kAttnWarps) {
+        const T* wrow = wv + static_cast<int64_t>(d - d0) * L;
         float acc[kAttnMaxRep];
 #pragma unroll
         for (int h = 0; h < kAttnMaxRep; ++h) acc[h] = 0.0f;
-        const T* ct = cache_c + static_cast<int64_t>(t) * L;
-#pragma unroll 4
-        for (int j8 = 0; j8 < L; j8 += 8) {
-            float c[8];
-            if (t == pos) {
-#pragma unroll
-                for (int u = 0; u < 8; ++u) c[u] = cnew[j8 + u];
-            } else {
-                load8<T>(ct + j8, c);
-            }
+        for (int j = lane; j < L; j += 32) {
+            const float w = to_f32<T>(wrow[j]);
 #pragma unroll
             for (int h = 0; h < kAttnMaxRep; ++h)
-                if (h < rep)
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) acc[h] = fmaf(qabs[h * L + j8 + u], c[u], acc[h]);
+                if (h < rep) acc[h] = fmaf(w, ctx[h * L + j], acc[h]);
         }
-        const T* kt = cache_k + (static_cast<int64_t>(t) * p.kv_heads + g) * R;
-#pragma unroll 4
-        for (int r8 = 0; r8 < R; r8 += 8) {
-            float k[8];
-            if (t == pos) {
 #pragma unroll
-                for (int u = 0; u < 8; ++u) k[u] = krn[r8 + u];
-            } else {
-                load8<T>(kt + r8, k);
+        for (int h = 0; h < kAttnMaxRep; ++h) {
+            if (h < rep) {
+                const float v = warp_sum(acc[h]);
+                if (lane == 0) out[h * D + d] = from_f32<T>(v);
             }
-#pragma unroll
-            for (int h = 0; h < kAttnMaxRep; ++h)
-                if (h < rep)
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) acc[h] = fmaf(qr[h * R + r8 + u], k[u], acc[h]);
         }
-#pragma unroll
-        for (int h = 0; h < kAttnMaxRep; ++h)
-            if (h < rep) sc[h * p.max_len + t] = acc[h] * p.scale;
     }
-    __syncthreads();
-    heads_softmax<T>(sc, rep, p.max_len, n, warp, lane);
-    __syncthreads();
-    // ctx = sum_t p_t c_t per head
-    weighted_rows<T>(cache_c, L, n, L, sc, p.max_len, rep, pos, cnew, warp, lane,
-                     [&](int h, int c, float v) { ctx[h * L + c] = v; });
-    __syncthreads();
-    // out = W_v ctx: the value up-projection applied once to the weighted latent
-    for (int i = threadIdx.x; i < rep * D; i += kAttnThreads) {
-        const int h = i / D, d = i % D;
-        const float* c = ctx + h * L;
-        float acc = 0.0f;
-        for (int j = 0; j < L; ++j) acc = fmaf(to_f32<T>(wv[d * L + j]), c[j], acc);
-        out[i] = from_f32<T>(acc);
-    }
+    cluster.sync();   // no CTA leaves while a peer may still read its partial sums
 }
 
 // ---------------------------------------------------------------------------
@@ -385,21 +471,26 @@ __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) 
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(kAttnThreads) sw_decode_kernel(AttnParams p) {
+    namespace cg = cooperative_groups;
     extern __shared__ __align__(16) float ssm[];
-    const int g = blockIdx.x, b = blockIdx.y;
-    const int rep = p.rep, D = p.head_dim, W = p.window;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int splits = p.splits;
+    const int sidx = blockIdx.x % splits, g = blockIdx.x / splits, b = blockIdx.y;
+    const int rep = p.rep, D = p.head_dim, W = p.window, cap = p.cap;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float* q = ssm;                        // [rep][D]
     float* kn = q + rep * D;               // [D]
     float* vn = kn + D;                    // [D]
     float* tmp = vn + D;                   // [(rep+1)*D]
-    float* sc = tmp + (rep + 1) * D;       // [rep][W]
+    float* part = tmp + (rep + 1) * D;     // [rep][D] this CTA's weighted values
+    float* red = part + rep * D;           // [2 * kAttnMaxRep]
+    float* sc = red + 2 * kAttnMaxRep;     // [rep][cap]
     const int pos = *p.pos;
     T* out = static_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.heads + g * rep) * D;
     const int rpos = pos < W ? pos : W;    // the cache length before this token
     if (pos < 0 || rpos >= p.table_len) {
         for (int i = threadIdx.x; i < rep * D; i += kAttnThreads) out[i] = from_f32<T>(0.0f);
-        return;
+        return;   // every CTA of the cluster returns here (same pos)
     }
     const int slot = pos % W;
     const int n = pos + 1 < W ? pos + 1 : W;
@@ -430,40 +521,32 @@ __global__ void __launch_bounds__(kAttnThreads) sw_decode_kernel(AttnParams p) {
     __syncthreads();
     T* kc = static_cast<T*>(p.cache_a) + static_cast<int64_t>(b) * W * p.kv_heads * D;
     T* vc = static_cast<T*>(p.cache_b) + static_cast<int64_t>(b) * W * p.kv_heads * D;
-    for (int i = threadIdx.x; i < D; i += kAttnThreads) {
-        kc[(static_cast<int64_t>(slot) * p.kv_heads + g) * D + i] = from_f32<T>(kn[i]);
-        vc[(static_cast<int64_t>(slot) * p.kv_heads + g) * D + i] = from_f32<T>(vn[i]);
-    }
-    // scores: one ring slot per thread, its key as 16-byte loads
-    for (int t = threadIdx.x; t < n; t += kAttnThreads) {
-        float acc[kAttnMaxRep];
-#pragma unroll
-        for (int h = 0; h < kAttnMaxRep; ++h) acc[h] = 0.0f;
-        const T* kt = kc + (static_cast<int64_t>(t) * p.kv_heads + g) * D;
-#pragma unroll 4
-        for (int d8 = 0; d8 < D; d8 += 8) {
-            float k[8];
-            if (t == slot) {
-#pragma unroll
-                for (int u = 0; u < 8; ++u) k[u] = kn[d8 + u];
-            } else {
-                load8<T>(kt + d8, k);
-            }
-#pragma unroll
-            for (int h = 0; h < kAttnMaxRep; ++h)
-                if (h < rep)
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) acc[h] = fmaf(q[h * D + d8 + u], k[u], acc[h]);
+    if (sidx == 0)
+        for (int i = threadIdx.x; i < D; i += kAttnThreads) {
+            kc[(static_cast<int64_t>(slot) * p.kv_heads + g) * D + i] = from_f32<T>(kn[i]);
+            vc[(static_cast<int64_t>(slot) * p.kv_heads + g) * D + i] = from_f32<T>(vn[i]);
         }
-#pragma unroll
-        for (int h = 0; h < kAttnMaxRep; ++h)
-            if (h < rep) sc[h * W + t] = acc[h] * p.scale;
+    // this CTA's ring slots; the new token's slot comes from shared memory
+    const int chunk = (n + splits - 1) / splits;
+    const int t_lo = min(n, sidx * chunk), t_hi = min(n, t_lo + chunk), cnt = t_hi - t_lo;
+    const int64_t rs = static_cast<int64_t>(p.kv_heads) * D;
+    split_scores<T>(kc + g * D, rs, q, D, kn, kc, rs, q, 0, kn, t_lo, t_hi, slot, rep, p.scale, sc, cap, warp,
+                    lane);
+    __syncthreads();
+    split_softmax<T>(cluster, sc, cap, cnt, rep, red, warp, lane);
+    __syncthreads();
+    weighted_rows<T>(vc + static_cast<int64_t>(t_lo) * rs + g * D, rs, cnt, D, sc, cap, rep, slot - t_lo, vn,
+                     warp, lane, [&](int h, int c, float v) { part[h * D + c] = v; });
+    cluster.sync();
+    // this CTA's share of the outputs: the partial sums added in CTA order
+    const int per = (rep * D + splits - 1) / splits;
+    const int i1 = min(rep * D, (sidx + 1) * per);
+    for (int i = sidx * per + threadIdx.x; i < i1; i += kAttnThreads) {
+        float v = 0.0f;
+        for (int r = 0; r < splits; ++r) v += cluster.map_shared_rank(part, r)[i];
+        out[i] = from_f32<T>(v);
     }
-    __syncthreads();
-    heads_softmax<T>(sc, rep, W, n, warp, lane);
-    __syncthreads();
-    weighted_rows<T>(vc + static_cast<int64_t>(g) * D, static_cast<int64_t>(p.kv_heads) * D, n, D, sc, W, rep,
-                     slot, vn, warp, lane, [&](int h, int c, float v) { out[h * D + c] = from_f32<T>(v); });
+    cluster.sync();   // no CTA leaves while a peer may still read its partial sums
 }
 
 }  // namespace chronos

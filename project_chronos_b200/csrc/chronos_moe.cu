@@ -14,6 +14,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <type_traits>
 #include <string>
 #include <unordered_map>
@@ -1214,6 +1215,37 @@ extern "C" size_t chronos_ep_combine_args_size(void) { return sizeof(ChronosEpCo
 namespace chronos {
 namespace {
 
+// Whether a cluster of `cs` lookahead CTAs with `smem` bytes each can be
+// placed on this GPU (checked once per shape and device).
+template <typename T>
+bool lookahead_cluster_fits(int cs, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, size_t>, bool> seen;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    const auto key = std::make_tuple(dev, cs, smem);
+    auto it = seen.find(key);
+    if (it != seen.end()) return it->second;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(cs);
+    cfg.blockDim = dim3(kLookaheadThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    const bool ok = cudaOccupancyMaxActiveClusters(&clusters, lookahead_kernel<T>, &cfg) == cudaSuccess &&
+                    clusters >= 1;
+    cudaGetLastError();   // a refused query leaves no error behind
+    seen[key] = ok;
+    return ok;
+}
+
 template <typename T>
 int lookahead_impl(const ChronosLookaheadArgs* a, cudaStream_t st) {
     LookaheadParams p{};
@@ -1227,13 +1259,37 @@ int lookahead_impl(const ChronosLookaheadArgs* a, cudaStream_t st) {
     p.e = a->num_experts;
     p.k = a->steps;
     if (p.n == 0) return CHRONOS_OK;
-    const int per_token = (p.h + p.inner + p.e * p.k) * 4;
-    p.tb = std::max(1, std::min(kLookaheadMaxTB, (160 << 10) / per_token));
-    const int smem = p.tb * per_token;
-    if (int rc = set_smem(lookahead_kernel<T>, smem)) return rc;
-    const unsigned blocks = static_cast<unsigned>((p.n + p.tb - 1) / p.tb);
-    CHRONOS_CUDA_CHECK(launch_kernel(lookahead_kernel<T>, dim3(blocks), dim3(kLookaheadThreads), smem, st,
-                                     false, p));
+    auto aligned16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    p.vec1 = (p.h % 8 == 0 && aligned16(p.x) && aligned16(p.w1)) ? 1 : 0;
+    p.vec2 = (p.inner % 8 == 0 && aligned16(p.w2)) ? 1 : 0;
+    p.tb = std::max(1, std::min<int>(kLookaheadMaxTB, kLookaheadXBytes / (p.h * 4)));
+    // one CTA per 32 W1 rows (a pass of 8 warps x 4 rows), at most 8
+    int cs = std::min(kLookaheadMaxCluster, std::max(1, (p.inner + 31) / 32));
+    size_t smem = 0;
+    for (;; cs /= 2) {
+        p.rpc = (p.inner + cs - 1) / cs;
+        smem = lookahead_smem(p.tb, p.h, p.rpc, p.inner, p.e * p.k);
+        if (int rc = set_smem(lookahead_kernel<T>, static_cast<int>(smem))) return rc;
+        if (cs == 1 || lookahead_cluster_fits<T>(cs, smem)) break;
+    }
+    const int64_t groups = (p.n + p.tb - 1) / p.tb;
+    if (groups * cs > (int64_t(1) << 31) - 1)
+        return fail(CHRONOS_ERR_INVALID_ARG, "lookahead: %lld tokens need too many blocks",
+                    static_cast<long long>(p.n));
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(groups * cs));
+    cfg.blockDim = dim3(kLookaheadThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    count_launch();
+    CHRONOS_CUDA_CHECK(cudaLaunchKernelEx(&cfg, lookahead_kernel<T>, p));
     return CHRONOS_OK;
 }
 
@@ -1270,6 +1326,7 @@ namespace chronos {
 namespace {
 
 constexpr int kAttnMaxSmem = 200 << 10;
+constexpr int kAttnMaxSplits = 8;   // CTAs per (kv head, batch row): a portable cluster
 
 bool known_dtype(int32_t d) {
     return d == CHRONOS_DTYPE_BF16 || d == CHRONOS_DTYPE_FP16 || d == CHRONOS_DTYPE_FP32;
@@ -1323,20 +1380,23 @@ AttnParams attn_params(const ChronosAttnArgs* a) {
     return p;
 }
 
-// Shared memory of one decode block, in the order the kernels lay it out.
-// The weight slices of an MLA block, when staged in shared memory.
+// Shared memory of one decode CTA, in the order the kernels lay it out.
+// The weight slices of an MLA CTA (k_nope_proj and k_rope_proj slices of its
+// kv head, its share of the v_proj rows), when staged in shared memory.
 size_t mla_wstage_bytes(const AttnParams& p, size_t elem) {
-    return elem * static_cast<size_t>(p.latent) * (p.nope + p.rope_dim + p.head_dim);
+    const int dper = (p.head_dim + p.splits - 1) / p.splits;
+    return elem * static_cast<size_t>(p.latent) * (p.nope + p.rope_dim + dper);
 }
 
 size_t mla_smem_base(const AttnParams& p) {
     const size_t rep = static_cast<size_t>(p.rep);
     return sizeof(float) * (rep * p.nope               // qn
                             + rep * p.rope_dim         // qr
-                            + 2 * rep * p.latent       // qabs, ctx
+                            + 3 * rep * p.latent       // qabs, ctx, part
                             + p.latent + p.rope_dim    // cnew, krn
                             + (rep + 1) * p.rope_dim   // tmp
-                            + rep * p.max_len);        // scores
+                            + 2 * kAttnMaxRep          // red
+                            + rep * p.cap);            // scores
 }
 
 size_t sw_smem(const AttnParams& p) {
@@ -1344,25 +1404,116 @@ size_t sw_smem(const AttnParams& p) {
     return sizeof(float) * (rep * p.head_dim           // q
                             + 2 * p.head_dim           // kn, vn
                             + (rep + 1) * p.head_dim   // tmp
-                            + rep * p.window);         // scores
+                            + rep * p.head_dim         // part
+                            + 2 * kAttnMaxRep          // red
+                            + rep * p.cap);            // scores
 }
 
-template <typename T>
-int mla_impl(const AttnParams& p, int batch, cudaStream_t st) {
-    const int smem = static_cast<int>(mla_smem_base(p) + (p.stage_w ? mla_wstage_bytes(p, sizeof(T)) : 0));
-    if (int rc = set_smem(mla_decode_kernel<T>, smem)) return rc;
-    CHRONOS_CUDA_CHECK(launch_kernel(mla_decode_kernel<T>, dim3(p.kv_heads, batch), dim3(kAttnThreads), smem,
-                                     st, false, p));
+// CTAs per (kv head, batch row) pair: about two CTAs per SM in all, at most a
+// portable cluster of 8.
+int attn_splits(int64_t items) {
+    static int sms[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int& n = sms[dev & 63];
+    if (n == 0 && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n = 148;
+    const int64_t target = 2 * static_cast<int64_t>(n);
+    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(kAttnMaxSplits, (target + items - 1) / items)));
+}
+
+// Whether a cluster of `splits` CTAs of `kernel` with `smem` bytes each can be
+// placed on this GPU (checked once per kernel, device and shape).
+bool attn_cluster_fits(void (*kernel)(AttnParams), int splits, size_t smem) {
+    if (splits <= 1) return true;
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, int, int, size_t>, bool> seen;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    const auto key = std::make_tuple(reinterpret_cast<const void*>(kernel), dev, splits, smem);
+    auto it = seen.find(key);
+    if (it != seen.end()) return it->second;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(splits);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    const bool ok = cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) == cudaSuccess && clusters >= 1;
+    cudaGetLastError();   // a refused query leaves no error behind
+    seen[key] = ok;
+    return ok;
+}
+
+// Split the positions over `splits` CTAs: the score capacity per CTA and, for
+// MLA, whether the weight slices fit in shared memory beside everything else.
+size_t attn_layout(AttnParams& p, bool mla, int splits, size_t elem) {
+    p.splits = splits;
+    p.cap = ((mla ? p.max_len : p.window) + splits - 1) / splits;
+    if (!mla) return sw_smem(p);
+    const size_t base = mla_smem_base(p), w = mla_wstage_bytes(p, elem);
+    p.stage_w = base + w <= static_cast<size_t>(kAttnMaxSmem) ? 1 : 0;
+    return base + (p.stage_w ? w : 0);
+}
+
+// Choose the split of this call: the parallel choice, raised until shared
+// memory fits, lowered while the cluster cannot be placed.  0 or an error.
+int attn_plan(AttnParams& p, bool mla, int batch, size_t elem, void (*kernel)(AttnParams), size_t* smem,
+              const char* what) {
+    int splits = attn_splits(static_cast<int64_t>(p.kv_heads) * std::max(1, batch));
+    *smem = attn_layout(p, mla, splits, elem);
+    while (*smem > static_cast<size_t>(kAttnMaxSmem) && splits < kAttnMaxSplits)
+        *smem = attn_layout(p, mla, ++splits, elem);
+    if (*smem > static_cast<size_t>(kAttnMaxSmem))
+        return fail(CHRONOS_ERR_INVALID_ARG, "%s: %d cached positions x %d heads per kv head need %zu bytes of "
+                    "shared memory per CTA at %d CTAs per head group (limit %d)", what,
+                    mla ? p.max_len : p.window, p.rep, *smem, splits, kAttnMaxSmem);
+    if (batch == 0) return CHRONOS_OK;
+    if (int rc = set_smem(kernel, static_cast<int>(*smem))) return rc;
+    while (splits > 1 && !attn_cluster_fits(kernel, splits, *smem)) {
+        const size_t next = attn_layout(p, mla, splits - 1, elem);
+        if (next > static_cast<size_t>(kAttnMaxSmem)) break;
+        --splits;
+        *smem = next;
+        if (int rc = set_smem(kernel, static_cast<int>(*smem))) return rc;
+    }
+    if (!attn_cluster_fits(kernel, splits, *smem))
+        return fail(CHRONOS_ERR_CUDA, "%s: a cluster of %d CTAs with %zu bytes of shared memory cannot be placed",
+                    what, splits, *smem);
+    return CHRONOS_OK;
+}
+
+int attn_launch(void (*kernel)(AttnParams), const AttnParams& p, int batch, size_t smem, cudaStream_t st) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(p.kv_heads * p.splits), static_cast<unsigned>(batch));
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = p.splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    count_launch();
+    CHRONOS_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, p));
     return CHRONOS_OK;
 }
 
 template <typename T>
-int sw_impl(const AttnParams& p, int batch, cudaStream_t st) {
-    const int smem = static_cast<int>(sw_smem(p));
-    if (int rc = set_smem(sw_decode_kernel<T>, smem)) return rc;
-    CHRONOS_CUDA_CHECK(launch_kernel(sw_decode_kernel<T>, dim3(p.kv_heads, batch), dim3(kAttnThreads), smem,
-                                     st, false, p));
-    return CHRONOS_OK;
+int attn_impl(AttnParams p, bool mla, int batch, cudaStream_t st, const char* what) {
+    void (*kernel)(AttnParams) = mla ? mla_decode_kernel<T> : sw_decode_kernel<T>;
+    size_t smem = 0;
+    if (int rc = attn_plan(p, mla, batch, sizeof(T), kernel, &smem, what)) return rc;
+    if (batch == 0) return CHRONOS_OK;
+    return attn_launch(kernel, p, batch, smem, st);
 }
 
 template <typename T>
@@ -1398,19 +1549,12 @@ extern "C" int chronos_mla_decode(const ChronosAttnArgs* a, void* stream) {
     if (a->batch > 0 && (a->norm_kv == nullptr || a->w_krope == nullptr || a->w_knope == nullptr ||
                          a->w_v == nullptr))
         return fail(CHRONOS_ERR_INVALID_ARG, "chronos_mla_decode: norm_kv, w_krope, w_knope and w_v are required");
-    AttnParams p = attn_params(a);
-    const size_t wbytes = mla_wstage_bytes(p, a->dtype == CHRONOS_DTYPE_FP32 ? 4 : 2);
-    p.stage_w = mla_smem_base(p) + wbytes <= static_cast<size_t>(kAttnMaxSmem) ? 1 : 0;
-    const size_t need = mla_smem_base(p) + (p.stage_w ? wbytes : 0);
-    if (need > static_cast<size_t>(kAttnMaxSmem))
-        return fail(CHRONOS_ERR_INVALID_ARG, "chronos_mla_decode: max_len %d x %d heads per kv head needs %zu "
-                    "bytes of shared memory (limit %d)", a->max_len, p.rep, need, kAttnMaxSmem);
-    if (a->batch == 0) return CHRONOS_OK;
+    const AttnParams p = attn_params(a);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     switch (a->dtype) {
-        case CHRONOS_DTYPE_BF16: return mla_impl<__nv_bfloat16>(p, a->batch, st);
-        case CHRONOS_DTYPE_FP16: return mla_impl<__half>(p, a->batch, st);
-        default: return mla_impl<float>(p, a->batch, st);
+        case CHRONOS_DTYPE_BF16: return attn_impl<__nv_bfloat16>(p, true, a->batch, st, "chronos_mla_decode");
+        case CHRONOS_DTYPE_FP16: return attn_impl<__half>(p, true, a->batch, st, "chronos_mla_decode");
+        default: return attn_impl<float>(p, true, a->batch, st, "chronos_mla_decode");
     }
 }
 
@@ -1422,15 +1566,11 @@ extern "C" int chronos_sw_decode(const ChronosAttnArgs* a, void* stream) {
         return fail(CHRONOS_ERR_INVALID_ARG, "chronos_sw_decode: rope_dim %d must equal head_dim %d, window %d "
                     ">= 1 and max_len %d == window", a->rope_dim, a->head_dim, a->window, a->max_len);
     const AttnParams p = attn_params(a);
-    if (sw_smem(p) > static_cast<size_t>(kAttnMaxSmem))
-        return fail(CHRONOS_ERR_INVALID_ARG, "chronos_sw_decode: window %d x %d heads per kv head needs %zu "
-                    "bytes of shared memory (limit %d)", a->window, p.rep, sw_smem(p), kAttnMaxSmem);
-    if (a->batch == 0) return CHRONOS_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     switch (a->dtype) {
-        case CHRONOS_DTYPE_BF16: return sw_impl<__nv_bfloat16>(p, a->batch, st);
-        case CHRONOS_DTYPE_FP16: return sw_impl<__half>(p, a->batch, st);
-        default: return sw_impl<float>(p, a->batch, st);
+        case CHRONOS_DTYPE_BF16: return attn_impl<__nv_bfloat16>(p, false, a->batch, st, "chronos_sw_decode");
+        case CHRONOS_DTYPE_FP16: return attn_impl<__half>(p, false, a->batch, st, "chronos_sw_decode");
+        default: return attn_impl<float>(p, false, a->batch, st, "chronos_sw_decode");
     }
 }
 
@@ -1450,6 +1590,34 @@ extern "C" int chronos_add_rmsnorm(const ChronosNormArgs* a, void* stream) {
         case CHRONOS_DTYPE_FP16: return norm_impl<__half>(a, st);
         default: return norm_impl<float>(a, st);
     }
+}
+
+extern "C" int chronos_argmax_rows(const void* x, int64_t rows, int32_t cols, int32_t dtype, int64_t* out,
+                                   void* stream) {
+    using namespace chronos;
+    g_last_error.clear();
+    if (rows < 0 || cols < 1 || !known_dtype(dtype))
+        return fail(CHRONOS_ERR_INVALID_ARG, "chronos_argmax_rows: rows %lld, cols %d, dtype %d",
+                    static_cast<long long>(rows), cols, dtype);
+    if (rows > 0 && (x == nullptr || out == nullptr))
+        return fail(CHRONOS_ERR_INVALID_ARG, "chronos_argmax_rows: x and out are required");
+    if (rows == 0) return CHRONOS_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const dim3 grid(static_cast<unsigned>(std::min<int64_t>(rows, 1 << 20)));
+    switch (dtype) {
+        case CHRONOS_DTYPE_BF16:
+            CHRONOS_CUDA_CHECK(launch_kernel(argmax_rows_kernel<__nv_bfloat16>, grid, dim3(kAttnThreads), 0, st,
+                                             false, static_cast<const __nv_bfloat16*>(x), rows, static_cast<int>(cols), out));
+            break;
+        case CHRONOS_DTYPE_FP16:
+            CHRONOS_CUDA_CHECK(launch_kernel(argmax_rows_kernel<__half>, grid, dim3(kAttnThreads), 0, st, false,
+                                             static_cast<const __half*>(x), rows, static_cast<int>(cols), out));
+            break;
+        default:
+            CHRONOS_CUDA_CHECK(launch_kernel(argmax_rows_kernel<float>, grid, dim3(kAttnThreads), 0, st, false,
+                                             static_cast<const float*>(x), rows, static_cast<int>(cols), out));
+    }
+    return CHRONOS_OK;
 }
 
 extern "C" size_t chronos_attn_args_size(void) { return sizeof(ChronosAttnArgs); }

@@ -423,7 +423,7 @@ class GraphedDecoder:
         hidden = m.embed_tokens(self.ids)
         out, look = m._blocks(hidden, self.cache, [self.masks[i] for i in range(len(m.layers))], decode=True)
         logits = F.linear(out[:, -1, :], self.lm.lm_head.weight)
-        self.next_ids.copy_(torch.argmax(logits, dim=-1))
+        ops.argmax_rows(logits, out=self.next_ids)
         if advance:
             self.ids.copy_(self.next_ids.view(-1, 1))
             self.cache.pos.add_(1)

@@ -440,6 +440,27 @@ def add_rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Opt
     return out
 
 
+def argmax_rows(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """torch.argmax(x, dim=-1) as one kernel (include/chronos_attention.h): the
+    index of the first maximal value of every row (NaN counts as the maximum),
+    int64 [*x.shape[:-1]]."""
+    _check_cuda(x, out)
+    if x.dtype not in _DTYPES:
+        raise TypeError(f"x {x.dtype}: bf16, fp16 or fp32 expected")
+    if not x.is_contiguous():
+        raise ValueError("argmax_rows needs a contiguous tensor")
+    cols = x.shape[-1]
+    rows = x.numel() // max(cols, 1)
+    if out is None:
+        out = torch.empty(x.shape[:-1], dtype=torch.int64, device=x.device)
+    elif out.dtype != torch.int64 or out.numel() != rows or not out.is_contiguous():
+        raise ValueError("out must be a contiguous int64 tensor with one value per row")
+    lib = N.load_library()
+    N.check(lib.chronos_argmax_rows(ctypes.c_void_p(_ptr(x)), rows, cols, _DTYPES[x.dtype],
+                                    ctypes.c_void_p(_ptr(out)), ctypes.c_void_p(_raw_stream(x.device.index))))
+    return out
+
+
 def attn_decode(kind: str, proj: torch.Tensor, pos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                 cache_a: torch.Tensor, cache_b: torch.Tensor, heads: int, kv_heads: int, head_dim: int,
                 rope_dim: int, latent: int, window: int, eps: float, norm_q: torch.Tensor,

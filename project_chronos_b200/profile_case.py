@@ -5,6 +5,8 @@
     python -m project_chronos_b200.profile_case --workload ep --calls 3
     python -m project_chronos_b200.profile_case --workload decode --tokens 64 --fused-route --calls 3
     python -m project_chronos_b200.profile_case --workload model --tokens 32 --calls 3
+    python -m project_chronos_b200.profile_case --workload attn --kind sw --tokens 32 --calls 20
+    python -m project_chronos_b200.profile_case --workload lookahead --tokens 32 --calls 20
 
 Builds the named synthetic workload on cuda:0 (``synthetic.WORKLOADS``),
 calls ``ops.moe_forward`` ``--calls`` times with an L2 flush (256 MB write)
@@ -24,7 +26,10 @@ from . import ops, synthetic as syn
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", default="prefill", choices=sorted(syn.WORKLOADS) + ["model"])
+    ap.add_argument("--workload", default="prefill",
+                    choices=sorted(syn.WORKLOADS) + ["model", "attn", "lookahead"])
+    ap.add_argument("--kind", default="sw", choices=["sw", "mla"], help="attention kind (--workload attn)")
+    ap.add_argument("--positions", type=int, default=516, help="cached positions (--workload attn)")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--calls", type=int, default=3)
     ap.add_argument("--seed", type=int, default=0)
@@ -38,6 +43,10 @@ def main(argv=None) -> int:
         return _ep(args, dev)
     if args.workload == "model":
         return _model(args, dev)
+    if args.workload == "attn":
+        return _attn(args, dev)
+    if args.workload == "lookahead":
+        return _lookahead(args, dev)
     wl = syn.named_workload(args.workload, tokens=args.tokens, seed=args.seed, device=dev)
     w = wl.weights
     s = wl.shape
@@ -90,6 +99,81 @@ def _model(args, dev) -> int:
             nxt = torch.argmax(out.logits[:, -1], dim=-1).view(-1, 1)
     ops.check_status(dev)
     print(f"model batch={b} steps={args.calls} avg_ms={total_ms / args.calls:.4f}")
+    return 0
+
+
+def _timed(fn, calls: int) -> float:
+    """Average device time of ``fn()`` over ``calls`` back-to-back calls, in µs."""
+    fn()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(calls):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(e) * 1e3 / calls
+
+
+def _attn(args, dev) -> int:
+    """One attention decode kernel of the 8-layer model's shape (synthetic.DECODE_MODEL):
+    --tokens batch rows, --positions cached tokens, random cache contents."""
+    import types
+    from .model import HybridCache, make_attention, precompute_freqs_cis
+    cfg = types.SimpleNamespace(**syn.DECODE_MODEL)
+    b = args.tokens or 32
+    layer = 0 if args.kind == "mla" else 1
+    dt = torch.bfloat16
+    attn = make_attention(layer, cfg).to(dev, dt).eval()
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    with torch.no_grad():
+        for name, p in sorted(attn.named_parameters()):
+            if name.endswith("norm.weight"):
+                p.normal_(1.0, 0.1, generator=g)
+            else:
+                p.normal_(0.0, 0.02, generator=g)
+    cache = HybridCache(cfg, b, args.positions + 8, dev, dt)
+    for t in (cache.a[layer], cache.b[layer]):
+        t.normal_(0.0, 1.0, generator=g)
+    cache.pos.fill_(args.positions)
+    cache.length = args.positions
+    cos, sin = precompute_freqs_cis(cfg.head_dim, cfg.max_position_embeddings, cfg.rope_theta)
+    cos, sin = cos.to(dev, dt), sin.to(dev, dt)
+    x = torch.randn(b, cfg.hidden_size, generator=g, device=dev, dtype=dt)
+    proj = torch.nn.functional.linear(x, attn._in_weight())
+    if args.kind == "mla":
+        fn = lambda: ops.attn_decode(  # noqa: E731
+            "mla", proj, cache.pos, cos, sin, cache.a[layer], cache.b[layer], attn.n_heads, attn.n_kv_heads,
+            attn.head_dim, attn.rope_dim, attn.kv_latent_dim, 0, attn.eps, attn.q_nope_norm.weight,
+            attn.q_rope_norm.weight, norm_kv=attn.kv_down_norm.weight, w_krope=attn.k_rope_proj.weight,
+            w_knope=attn.k_nope_proj.weight, w_v=attn.v_proj.weight)
+    else:
+        fn = lambda: ops.attn_decode(  # noqa: E731
+            "sw", proj, cache.pos, cos, sin, cache.a[layer], cache.b[layer], attn.n_heads, attn.n_kv_heads,
+            attn.head_dim, attn.head_dim, 0, attn.window_size, attn.eps, attn.q_norm.weight, attn.k_norm.weight)
+    us = _timed(fn, args.calls)
+    ops.check_status(dev)
+    print(f"attn kind={args.kind} batch={b} positions={args.positions} calls={args.calls} avg_us={us:.2f}")
+    return 0
+
+
+def _lookahead(args, dev) -> int:
+    """The lookahead router of the 8-layer model on --tokens rows."""
+    import types
+    from .lookahead import LookaheadRouter
+    cfg = types.SimpleNamespace(**syn.DECODE_MODEL)
+    m = LookaheadRouter(cfg).to(dev, torch.bfloat16).eval()
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.normal_(0.0, 0.02, generator=g)
+    n = args.tokens or 32
+    x = torch.randn(1, n, cfg.hidden_size, generator=g, device=dev, dtype=torch.bfloat16)
+    with torch.no_grad():
+        us = _timed(lambda: m(x), args.calls)
+    ops.check_status(dev)
+    print(f"lookahead tokens={n} calls={args.calls} avg_us={us:.2f}")
     return 0
 
 

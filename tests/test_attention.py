@@ -178,6 +178,7 @@ def test_decode_kernels_match_reference_modules(tag, dtype, tol):
     (4, 4, 64, 16, 32, 3, 11, 2),       # one head per kv head, a 3-slot ring
     (8, 1, 128, 64, 128, 7, 20, 1),     # 8 heads per kv head
     (2, 1, 256, 64, 256, 1, 5, 2),      # widest head, a one-slot window
+    (8, 2, 128, 32, 64, 64, 300, 1),    # 300 positions over a cluster of 8 CTAs; the ring wraps 4 times
 ])
 def test_decode_kernels_match_oracle(tag, nh, nkv, D, R, L, W, T, B):
     torch.manual_seed(nh * 1000 + D + W)
@@ -188,7 +189,7 @@ def test_decode_kernels_match_oracle(tag, nh, nkv, D, R, L, W, T, B):
           "kv_down_norm.weight": 1 + 0.1 * torch.randn(L), "k_nope_proj.weight": 0.1 * torch.randn(nkv * nope, L),
           "k_rope_proj.weight": 0.1 * torch.randn(nkv * R, L), "v_proj.weight": 0.1 * torch.randn(nkv * D, L),
           "q_norm.weight": 1 + 0.1 * torch.randn(D), "k_norm.weight": 1 + 0.1 * torch.randn(D)}
-    cos, sin = _tables(D, 64)
+    cos, sin = _tables(D, max(64, T + 1))
     width = nh * (nope + R) + L if tag == "mla" else (nh + 2 * nkv) * D
     proj = torch.randn(T, B, width)
     outs = _decode_run(tag, proj, st, cfg, D, cos, sin, torch.float32, B)
@@ -197,6 +198,27 @@ def test_decode_kernels_match_oracle(tag, nh, nkv, D, R, L, W, T, B):
         orc = _oracle_for(tag, case, {k: v.numpy() for k, v in st.items()}, cos, sin)
         want = np.stack([orc.step(proj[t, b].numpy()) for t in range(T)])
         assert O.rel_l2(outs[:, b].numpy(), want) <= 2e-5, b
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_argmax_rows_matches_torch(dtype):
+    from project_chronos_b200 import ops
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(37, 6400, generator=g).to(dtype)
+    x[3, 100] = x[3, 5000] = 50.0        # a tie: the first index wins
+    x[4, :] = 1.0                        # all equal
+    x[5, 17] = float("nan")              # NaN counts as the maximum
+    x[6, 9] = x[6, 11] = float("nan")    # the first NaN
+    x[7, -1] = 60.0                      # the last column
+    xd = x.to(DEV)
+    got = ops.argmax_rows(xd)
+    want = torch.argmax(xd, dim=-1)
+    assert got.dtype == torch.int64 and got.shape == (37,)
+    assert torch.equal(got.cpu(), want.cpu())
+    assert got[3].item() == 100 and got[4].item() == 0 and got[5].item() == 17 and got[6].item() == 9
+    y = torch.randn(2, 3, 129, device=DEV, dtype=dtype)
+    assert torch.equal(ops.argmax_rows(y), torch.argmax(y, dim=-1))
 
 
 @pytest.mark.gpu

@@ -51,7 +51,7 @@ def test_state_dict_keys_and_cpu_rejected():
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 1e-2)])
 @pytest.mark.parametrize("H,E,steps,n", [(256, 16, 2, 7), (1024, 64, 2, 32), (7168, 256, 1, 3),
-                                         (96, 5, 3, 1)])
+                                         (96, 5, 3, 1), (100, 6, 2, 9), (512, 32, 2, 300)])
 def test_kernel_matches_oracle(dtype, tol, H, E, steps, n):
     from project_chronos_b200 import LookaheadRouter
     torch.manual_seed(H + E)
