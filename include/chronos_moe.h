@@ -215,7 +215,8 @@ CHRONOS_API int chronos_moe_profile_end(float* stage_ms, int32_t* stage_launches
 CHRONOS_API uint64_t chronos_moe_kernel_launches(void);
 
 /* Process-wide switches of the launch sequence (no counterpart in the
- * reference; the results are bit-identical either way):
+ * reference; the routing is bit-identical either way, the outputs agree to the
+ * layer dtype's rounding):
  *   "fused_route"  1: a decode call (N <= 64 tokens, d_model <= 4096) routes in
  *                  ONE launch, a thread-block cluster that computes the chunk
  *                  partials, the selection and the plan; 0 (default): the logit
@@ -226,11 +227,15 @@ CHRONOS_API uint64_t chronos_moe_kernel_launches(void);
  *                  slot, the shared units sum each token's slots in choice order
  *                  (deterministic; no fp32 accumulator); 0: fp32 reduce-adds
  *                  into an accumulator.
- *   "fold_finalize"  1 (default): a call below 1024 tokens with shared experts
- *                  writes its output from the down GEMM, each 128-column tile
- *                  converted by the CTA whose contribution completes it; 0: a
- *                  separate finalize kernel.
- * Returns CHRONOS_OK, or CHRONOS_ERR_INVALID_ARG for an unknown name. */
+ *   "fold_finalize"  1: a call below 1024 tokens with shared experts writes
+ *                  its output from the down GEMM, each 128-column tile
+ *                  converted by the CTA whose contribution completes it; 0
+ *                  (default, measured faster): a separate finalize kernel.
+ *   "down_split_target"  n (default 8, 0..64): the weight-major down GEMM of a
+ *                  decode call splits K until it has about n work units per SM
+ *                  (0: no split).
+ * Returns CHRONOS_OK, or CHRONOS_ERR_INVALID_ARG for an unknown name or a value
+ * out of range. */
 CHRONOS_API int chronos_moe_set_option(const char* name, int64_t value);
 
 #ifdef __cplusplus

@@ -124,6 +124,53 @@ __global__ void __launch_bounds__(kAttnThreads) add_rmsnorm_kernel(NormParams p)
     }
 }
 
+// The same with one warp per row (rows of width <= 256 * VPL, width % 8 == 0,
+// 16-byte aligned): each lane keeps its VPL 8-column groups in registers, one
+// warp sum, no block barrier.  8 rows per block.
+template <typename T, int VPL>
+__global__ void __launch_bounds__(kAttnThreads) add_rmsnorm_warp_kernel(NormParams p) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * kAttnWarps + warp;
+    if (r >= p.rows) return;
+    const int nv = p.width / 8;
+    const int64_t base = r * p.width;
+    const T* x = static_cast<const T*>(p.x) + base;
+    const T* res = p.residual != nullptr ? static_cast<const T*>(p.residual) + base : nullptr;
+    float v[VPL][8];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const int c8 = lane + 32 * i;
+        if (c8 < nv) {
+            load8<T>(x + c8 * 8, v[i]);
+            if (res != nullptr) {
+                float rr[8];
+                load8<T>(res + c8 * 8, rr);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[i][u] = round_to<T>(v[i][u] + rr[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) ss = fmaf(v[i][u], v[i][u], ss);
+        }
+    }
+    const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(p.width) + p.eps);
+    T* sum_out = p.sum_out != nullptr ? static_cast<T*>(p.sum_out) + base : nullptr;
+    T* out = static_cast<T*>(p.out) + base;
+    const T* w = static_cast<const T*>(p.weight);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const int c8 = lane + 32 * i;
+        if (c8 < nv) {
+            if (sum_out != nullptr) store8<T>(sum_out + c8 * 8, v[i]);
+            float wv[8], o[8];
+            load8<T>(w + c8 * 8, wv);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) o[u] = wv[u] * (v[i][u] * inv);
+            store8<T>(out + c8 * 8, o);
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // arg-max of every row (the greedy pick of a decode step): the index of the
 // first maximal value, NaN counting as the maximum (as torch.argmax does).
@@ -174,50 +221,68 @@ __device__ __forceinline__ void stage_rows(T* dst, const T* src, int count) {
         reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
 }
 
+// Lanes per cached row in the weighted sums: one lane per 8-column group,
+// rounded up to a power of two (at least 4), so 32 / LPP rows per warp step.
+__host__ __device__ constexpr int attn_lpp(int groups) {
+    return groups <= 4 ? 4 : groups <= 8 ? 8 : groups <= 16 ? 16 : 32;
+}
+
 // Weighted sum of `n` cached rows for every head of the group:
-// out[h][c] = sum_t p[h][t] * row_t[c] for the `width` columns of a row, rows
-// `stride` elements apart; the row at `fresh_t` comes from shared memory
-// (`fresh`, fp32) instead.  Warps take 8-column groups, lanes take every 32nd
-// row (many independent 16-byte loads in flight), and a warp reduction
-// gathers the lanes; `emit(h, c, value)` receives each result.
-template <typename T, typename Emit>
+// out[h][c] = sum_t p[h][t] * row_t[c] for the `width` (<= 256) columns of a
+// row, rows `stride` elements apart; the row at `fresh_t` comes from shared
+// memory (`fresh`, fp32) instead.  Lanes take 8-column groups (16-byte loads,
+// a row read by consecutive lanes), the 32 / LPP row slots of a warp and the 8
+// warps take every (8 * 32 / LPP)-th row; the slots are summed by shuffles,
+// the warps through `red` [8][REP][width] in shared memory, in warp order.
+// `emit(h, c, value)` receives each result.  Every thread of the block calls it.
+template <typename T, int REP, typename Emit>
 __device__ __forceinline__ void weighted_rows(const T* rows, int64_t stride, int n, int width, const float* p,
-                                              int p_stride, int rep, int fresh_t, const float* fresh, int warp,
-                                              int lane, Emit&& emit) {
-    for (int cg = warp; cg < width / 8; cg += kAttnWarps) {
-        float acc[kAttnMaxRep][8];
+                                              int p_stride, int fresh_t, const float* fresh, float* red,
+                                              int warp, int lane, Emit&& emit) {
+    const int G = width / 8;
+    const int lpp = attn_lpp(G), pp = 32 / lpp;
+    const int gl = lane % lpp, ps = lane / lpp;
+    float acc[REP][8];
 #pragma unroll
-        for (int h = 0; h < kAttnMaxRep; ++h)
+    for (int h = 0; h < REP; ++h)
 #pragma unroll
-            for (int u = 0; u < 8; ++u) acc[h][u] = 0.0f;
-#pragma unroll 4
-        for (int t = lane; t < n; t += 32) {
+        for (int u = 0; u < 8; ++u) acc[h][u] = 0.0f;
+    if (gl < G) {
+#pragma unroll 2
+        for (int t = warp * pp + ps; t < n; t += kAttnWarps * pp) {
             float v[8];
             if (t == fresh_t) {
 #pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = fresh[cg * 8 + u];
+                for (int u = 0; u < 8; ++u) v[u] = fresh[gl * 8 + u];
             } else {
-                load8<T>(rows + static_cast<int64_t>(t) * stride + cg * 8, v);
+                load8<T>(rows + static_cast<int64_t>(t) * stride + gl * 8, v);
             }
 #pragma unroll
-            for (int h = 0; h < kAttnMaxRep; ++h) {
-                if (h < rep) {
-                    const float ph = p[h * p_stride + t];
+            for (int h = 0; h < REP; ++h) {
+                const float ph = p[h * p_stride + t];
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) acc[h][u] = fmaf(ph, v[u], acc[h][u]);
-                }
+                for (int u = 0; u < 8; ++u) acc[h][u] = fmaf(ph, v[u], acc[h][u]);
             }
         }
+    }
+    for (int o = lpp; o < 32; o <<= 1)
 #pragma unroll
-        for (int h = 0; h < kAttnMaxRep; ++h) {
-            if (h < rep) {
+        for (int h = 0; h < REP; ++h)
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const float r = warp_sum(acc[h][u]);
-                    if (lane == 0) emit(h, cg * 8 + u, r);
-                }
-            }
+            for (int u = 0; u < 8; ++u) acc[h][u] += __shfl_xor_sync(0xffffffffu, acc[h][u], o);
+    if (ps == 0 && gl < G)
+#pragma unroll
+        for (int h = 0; h < REP; ++h) {
+            float4* dst = reinterpret_cast<float4*>(red + (warp * REP + h) * width + gl * 8);
+            dst[0] = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+            dst[1] = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
         }
+    __syncthreads();
+    for (int i = threadIdx.x; i < REP * width; i += kAttnThreads) {
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) v += red[w * REP * width + i];
+        emit(i / width, i % width, v);
     }
 }
 
@@ -231,27 +296,27 @@ __device__ __forceinline__ void weighted_rows(const T* rows, int64_t stride, int
 // CTA then forms the weighted sum of its positions, and the partial sums are
 // added in CTA order.  Four cluster barriers, reached by every thread of every
 // CTA; the last keeps each CTA's shared memory alive until its peers have read
-// it.
+// it.  The kernels are instantiated per REP (query heads per kv head).
 // ---------------------------------------------------------------------------
 
 // Scores of positions [t_lo, t_hi) for every head of the group into
 // sc[h * cap + t - t_lo].  Four lanes per position (lane sub takes the 8-column
 // groups sub, sub + 4, ...), summed by two butterfly steps.  Column group
-// q < w1/8 comes from `rows1` (row stride st1, query q1 [rep][w1]), the others
-// from `rows2` (st2, q2 [rep][w2]); the row at `fresh_t` comes from shared
-// memory (f1, f2) instead.
-template <typename T>
+// q < w1/8 comes from `rows1` (row stride st1, query q1 [REP][w1]), the others
+// from `rows2` (st2, q2 [REP][w2]); the row at `fresh_t` comes from shared
+// memory (f1, f2) instead.  Queries are 16-byte aligned in shared memory.
+template <typename T, int REP>
 __device__ __forceinline__ void split_scores(const T* rows1, int64_t st1, const float* q1, int w1, const float* f1,
                                              const T* rows2, int64_t st2, const float* q2, int w2,
-                                             const float* f2, int t_lo, int t_hi, int fresh_t, int rep,
-                                             float scale, float* sc, int cap, int warp, int lane) {
+                                             const float* f2, int t_lo, int t_hi, int fresh_t, float scale,
+                                             float* sc, int cap, int warp, int lane) {
     const int g1 = w1 / 8, gall = g1 + w2 / 8, sub = lane & 3;
     for (int base = t_lo + warp * 8; base < t_hi; base += kAttnWarps * 8) {   // uniform per warp
         const int t = base + (lane >> 2);
         const bool ok = t < t_hi;
-        float acc[kAttnMaxRep];
+        float acc[REP];
 #pragma unroll
-        for (int h = 0; h < kAttnMaxRep; ++h) acc[h] = 0.0f;
+        for (int h = 0; h < REP; ++h) acc[h] = 0.0f;
         if (ok) {
             const bool fresh = t == fresh_t;
 #pragma unroll 4
@@ -270,39 +335,46 @@ __device__ __forceinline__ void split_scores(const T* rows1, int64_t st1, const 
                 const float* qq = first ? q1 + c : q2 + c;
                 const int qs = first ? w1 : w2;
 #pragma unroll
-                for (int h = 0; h < kAttnMaxRep; ++h)
-                    if (h < rep)
-#pragma unroll
-                        for (int u = 0; u < 8; ++u) acc[h] = fmaf(qq[h * qs + u], v[u], acc[h]);
+                for (int h = 0; h < REP; ++h) {
+                    const float4 a = reinterpret_cast<const float4*>(qq + h * qs)[0];
+                    const float4 b = reinterpret_cast<const float4*>(qq + h * qs)[1];
+                    acc[h] = fmaf(a.x, v[0], acc[h]);
+                    acc[h] = fmaf(a.y, v[1], acc[h]);
+                    acc[h] = fmaf(a.z, v[2], acc[h]);
+                    acc[h] = fmaf(a.w, v[3], acc[h]);
+                    acc[h] = fmaf(b.x, v[4], acc[h]);
+                    acc[h] = fmaf(b.y, v[5], acc[h]);
+                    acc[h] = fmaf(b.z, v[6], acc[h]);
+                    acc[h] = fmaf(b.w, v[7], acc[h]);
+                }
             }
         }
 #pragma unroll
-        for (int h = 0; h < kAttnMaxRep; ++h) {
+        for (int h = 0; h < REP; ++h) {
             acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 1);
             acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 2);
         }
         if (ok && sub == 0)
 #pragma unroll
-            for (int h = 0; h < kAttnMaxRep; ++h)
-                if (h < rep) sc[h * cap + (t - t_lo)] = acc[h] * scale;
+            for (int h = 0; h < REP; ++h) sc[h * cap + (t - t_lo)] = acc[h] * scale;
     }
 }
 
 // The cluster-wide softmax of the scores sc[h * cap + i], i < cnt, rounded to T
-// in place.  red[0..rep) and red[kAttnMaxRep..+rep) are this CTA's published
+// in place.  red[0..REP) and red[kAttnMaxRep..+REP) are this CTA's published
 // maximum and sum.  Contains two cluster barriers.
-template <typename T>
+template <typename T, int REP>
 __device__ __forceinline__ void split_softmax(cooperative_groups::cluster_group& cluster, float* sc, int cap,
-                                              int cnt, int rep, float* red, int warp, int lane) {
+                                              int cnt, float* red, int warp, int lane) {
     const int splits = static_cast<int>(cluster.num_blocks());
-    for (int h = warp; h < rep; h += kAttnWarps) {
+    for (int h = warp; h < REP; h += kAttnWarps) {
         float m = -INFINITY;
         for (int i = lane; i < cnt; i += 32) m = fmaxf(m, sc[h * cap + i]);
         m = warp_max(m);
         if (lane == 0) red[h] = m;
     }
     cluster.sync();
-    for (int h = warp; h < rep; h += kAttnWarps) {
+    for (int h = warp; h < REP; h += kAttnWarps) {
         float m = lane < splits ? cluster.map_shared_rank(red, lane)[h] : -INFINITY;
         m = warp_max(m);
         float sum = 0.0f;
@@ -315,7 +387,7 @@ __device__ __forceinline__ void split_softmax(cooperative_groups::cluster_group&
         if (lane == 0) red[kAttnMaxRep + h] = sum;
     }
     cluster.sync();
-    for (int h = warp; h < rep; h += kAttnWarps) {
+    for (int h = warp; h < REP; h += kAttnWarps) {
         float tot = 0.0f;
         if (lane == 0)
             for (int r = 0; r < splits; ++r) tot += cluster.map_shared_rank(red, r)[kAttnMaxRep + h];
@@ -324,17 +396,32 @@ __device__ __forceinline__ void split_softmax(cooperative_groups::cluster_group&
     }
 }
 
+// Start moving rows [t_lo, t_hi) of a cache (`bytes` per row, rows `stride`
+// elements apart) towards L2 while the CTA computes its query.
+template <typename T>
+__device__ __forceinline__ void prefetch_rows(const T* rows, int64_t stride, int t_lo, int t_hi, int bytes) {
+    const int lines = (bytes + 127) / 128;
+    for (int i = threadIdx.x; i < (t_hi - t_lo) * lines; i += kAttnThreads) {
+        const int t = t_lo + i / lines, l = i % lines;
+        prefetch_l2(reinterpret_cast<const uint8_t*>(rows + static_cast<int64_t>(t) * stride) + l * 128);
+    }
+}
+
+// Floats of the weighted-sum reduction buffer of a CTA.
+__host__ __device__ constexpr int attn_red_floats(int rep, int width) { return kAttnWarps * rep * width; }
+
 // ---------------------------------------------------------------------------
 // MLA decode (hybrid_attention.py:116-179 with a cache, S = 1)
 // ---------------------------------------------------------------------------
-template <typename T>
-__global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) {
+template <typename T, int REP>
+__global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) mla_decode_kernel(AttnParams p) {
     namespace cg = cooperative_groups;
+    constexpr int rep = REP;
     extern __shared__ __align__(16) float msm[];
     cg::cluster_group cluster = cg::this_cluster();
     const int splits = p.splits;
     const int sidx = blockIdx.x % splits, g = blockIdx.x / splits, b = blockIdx.y;
-    const int rep = p.rep, nope = p.nope, R = p.rope_dim, L = p.latent, D = p.head_dim, cap = p.cap;
+    const int nope = p.nope, R = p.rope_dim, L = p.latent, D = p.head_dim, cap = p.cap;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // this CTA's output rows d0 .. d1 - 1 of the value up-projection
     const int dper = (D + splits - 1) / splits;
@@ -358,7 +445,8 @@ __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) 
     float* krn = cnew + L;                 // [R]
     float* tmp = krn + R;                  // [(rep+1)*R] rotated q_rope heads and k_rope
     float* red = tmp + (rep + 1) * R;      // [2 * kAttnMaxRep]
-    float* sc = red + 2 * kAttnMaxRep;     // [rep][cap]
+    float* wred = red + 2 * kAttnMaxRep;   // [kAttnWarps][rep][L] weighted-sum reduction
+    float* sc = wred + attn_red_floats(rep, L);   // [rep][cap]
     const int pos = *p.pos;
     T* out = static_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.heads + g * rep) * D;
     if (pos < 0 || pos >= p.max_len || pos >= p.table_len) {   // outside the cache: no access
@@ -368,6 +456,14 @@ __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) 
     const int n = pos + 1;
     const int width = p.heads * (nope + R) + L;
     const T* row = static_cast<const T*>(p.proj) + static_cast<int64_t>(b) * width;
+    T* cache_c = static_cast<T*>(p.cache_a) + static_cast<int64_t>(b) * p.max_len * L;
+    T* cache_k = static_cast<T*>(p.cache_b) + static_cast<int64_t>(b) * p.max_len * p.kv_heads * R;
+    // this CTA's positions, their cache rows on their way while the query is formed
+    const int chunk = (n + splits - 1) / splits;
+    const int t_lo = min(n, sidx * chunk), t_hi = min(n, t_lo + chunk), cnt = t_hi - t_lo;
+    prefetch_rows<T>(cache_c, L, t_lo, t_hi, L * static_cast<int>(sizeof(T)));
+    prefetch_rows<T>(cache_k + g * R, static_cast<int64_t>(p.kv_heads) * R, t_lo, t_hi,
+                     R * static_cast<int>(sizeof(T)));
     if (p.stage_w) {
         stage_rows<T>(wstage, wkn_g, nope * L);
         stage_rows<T>(wstage + nope * L, wkr_g, R * L);
@@ -416,8 +512,6 @@ __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) 
     }
     __syncthreads();
     // append the new token to the cache (by CTA 0 of the cluster; the latent once, by group 0)
-    T* cache_c = static_cast<T*>(p.cache_a) + static_cast<int64_t>(b) * p.max_len * L;
-    T* cache_k = static_cast<T*>(p.cache_b) + static_cast<int64_t>(b) * p.max_len * p.kv_heads * R;
     if (sidx == 0) {
         if (g == 0)
             for (int j = threadIdx.x; j < L; j += kAttnThreads)
@@ -426,16 +520,14 @@ __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) 
             cache_k[(static_cast<int64_t>(pos) * p.kv_heads + g) * R + r] = from_f32<T>(krn[r]);
     }
     // this CTA's positions: latent against q_abs, rope key against q_rope
-    const int chunk = (n + splits - 1) / splits;
-    const int t_lo = min(n, sidx * chunk), t_hi = min(n, t_lo + chunk), cnt = t_hi - t_lo;
-    split_scores<T>(cache_c, L, qabs, L, cnew, cache_k + g * R, static_cast<int64_t>(p.kv_heads) * R, qr, R, krn,
-                    t_lo, t_hi, pos, rep, p.scale, sc, cap, warp, lane);
+    split_scores<T, REP>(cache_c, L, qabs, L, cnew, cache_k + g * R, static_cast<int64_t>(p.kv_heads) * R, qr, R,
+                         krn, t_lo, t_hi, pos, p.scale, sc, cap, warp, lane);
     __syncthreads();
-    split_softmax<T>(cluster, sc, cap, cnt, rep, red, warp, lane);
+    split_softmax<T, REP>(cluster, sc, cap, cnt, red, warp, lane);
     __syncthreads();
     // this CTA's weighted latent sum_t p_t c_t per head
-    weighted_rows<T>(cache_c + static_cast<int64_t>(t_lo) * L, L, cnt, L, sc, cap, rep, pos - t_lo, cnew, warp,
-                     lane, [&](int h, int c, float v) { part[h * L + c] = v; });
+    weighted_rows<T, REP>(cache_c + static_cast<int64_t>(t_lo) * L, L, cnt, L, sc, cap, pos - t_lo, cnew, wred,
+                          warp, lane, [&](int h, int c, float v) { part[h * L + c] = v; });
     cluster.sync();
     for (int i = threadIdx.x; i < rep * L; i += kAttnThreads) {
         float v = 0.0f;
@@ -446,21 +538,18 @@ __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) 
     // out = W_v ctx for this CTA's rows: the value up-projection applied once to the weighted latent
     for (int d = d0 + warp; d < d1; d += kAttnWarps) {
         const T* wrow = wv + static_cast<int64_t>(d - d0) * L;
-        float acc[kAttnMaxRep];
+        float acc[REP];
 #pragma unroll
-        for (int h = 0; h < kAttnMaxRep; ++h) acc[h] = 0.0f;
+        for (int h = 0; h < REP; ++h) acc[h] = 0.0f;
         for (int j = lane; j < L; j += 32) {
             const float w = to_f32<T>(wrow[j]);
 #pragma unroll
-            for (int h = 0; h < kAttnMaxRep; ++h)
-                if (h < rep) acc[h] = fmaf(w, ctx[h * L + j], acc[h]);
+            for (int h = 0; h < REP; ++h) acc[h] = fmaf(w, ctx[h * L + j], acc[h]);
         }
 #pragma unroll
-        for (int h = 0; h < kAttnMaxRep; ++h) {
-            if (h < rep) {
-                const float v = warp_sum(acc[h]);
-                if (lane == 0) out[h * D + d] = from_f32<T>(v);
-            }
+        for (int h = 0; h < REP; ++h) {
+            const float v = warp_sum(acc[h]);
+            if (lane == 0) out[h * D + d] = from_f32<T>(v);
         }
     }
     cluster.sync();   // no CTA leaves while a peer may still read its partial sums
@@ -469,14 +558,15 @@ __global__ void __launch_bounds__(kAttnThreads) mla_decode_kernel(AttnParams p) 
 // ---------------------------------------------------------------------------
 // sliding-window decode (hybrid_attention.py:213-258 with a cache, S = 1)
 // ---------------------------------------------------------------------------
-template <typename T>
-__global__ void __launch_bounds__(kAttnThreads) sw_decode_kernel(AttnParams p) {
+template <typename T, int REP>
+__global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) sw_decode_kernel(AttnParams p) {
     namespace cg = cooperative_groups;
+    constexpr int rep = REP;
     extern __shared__ __align__(16) float ssm[];
     cg::cluster_group cluster = cg::this_cluster();
     const int splits = p.splits;
     const int sidx = blockIdx.x % splits, g = blockIdx.x / splits, b = blockIdx.y;
-    const int rep = p.rep, D = p.head_dim, W = p.window, cap = p.cap;
+    const int D = p.head_dim, W = p.window, cap = p.cap;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float* q = ssm;                        // [rep][D]
     float* kn = q + rep * D;               // [D]
@@ -484,7 +574,8 @@ __global__ void __launch_bounds__(kAttnThreads) sw_decode_kernel(AttnParams p) {
     float* tmp = vn + D;                   // [(rep+1)*D]
     float* part = tmp + (rep + 1) * D;     // [rep][D] this CTA's weighted values
     float* red = part + rep * D;           // [2 * kAttnMaxRep]
-    float* sc = red + 2 * kAttnMaxRep;     // [rep][cap]
+    float* wred = red + 2 * kAttnMaxRep;   // [kAttnWarps][rep][D] weighted-sum reduction
+    float* sc = wred + attn_red_floats(rep, D);   // [rep][cap]
     const int pos = *p.pos;
     T* out = static_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.heads + g * rep) * D;
     const int rpos = pos < W ? pos : W;    // the cache length before this token
@@ -496,6 +587,14 @@ __global__ void __launch_bounds__(kAttnThreads) sw_decode_kernel(AttnParams p) {
     const int n = pos + 1 < W ? pos + 1 : W;
     const int width = (p.heads + 2 * p.kv_heads) * D;
     const T* row = static_cast<const T*>(p.proj) + static_cast<int64_t>(b) * width;
+    T* kc = static_cast<T*>(p.cache_a) + static_cast<int64_t>(b) * W * p.kv_heads * D;
+    T* vc = static_cast<T*>(p.cache_b) + static_cast<int64_t>(b) * W * p.kv_heads * D;
+    const int64_t rs = static_cast<int64_t>(p.kv_heads) * D;
+    // this CTA's ring slots, their keys and values on their way while the query is formed
+    const int chunk = (n + splits - 1) / splits;
+    const int t_lo = min(n, sidx * chunk), t_hi = min(n, t_lo + chunk), cnt = t_hi - t_lo;
+    prefetch_rows<T>(kc + g * D, rs, t_lo, t_hi, D * static_cast<int>(sizeof(T)));
+    prefetch_rows<T>(vc + g * D, rs, t_lo, t_hi, D * static_cast<int>(sizeof(T)));
     for (int i = threadIdx.x; i < rep * D; i += kAttnThreads) q[i] = to_f32<T>(row[(g * rep) * D + i]);
     for (int i = threadIdx.x; i < D; i += kAttnThreads) {
         kn[i] = to_f32<T>(row[(p.heads + g) * D + i]);
@@ -519,24 +618,19 @@ __global__ void __launch_bounds__(kAttnThreads) sw_decode_kernel(AttnParams p) {
         (h < rep ? q + h * D : kn)[e] = tmp[i];
     }
     __syncthreads();
-    T* kc = static_cast<T*>(p.cache_a) + static_cast<int64_t>(b) * W * p.kv_heads * D;
-    T* vc = static_cast<T*>(p.cache_b) + static_cast<int64_t>(b) * W * p.kv_heads * D;
     if (sidx == 0)
         for (int i = threadIdx.x; i < D; i += kAttnThreads) {
             kc[(static_cast<int64_t>(slot) * p.kv_heads + g) * D + i] = from_f32<T>(kn[i]);
             vc[(static_cast<int64_t>(slot) * p.kv_heads + g) * D + i] = from_f32<T>(vn[i]);
         }
-    // this CTA's ring slots; the new token's slot comes from shared memory
-    const int chunk = (n + splits - 1) / splits;
-    const int t_lo = min(n, sidx * chunk), t_hi = min(n, t_lo + chunk), cnt = t_hi - t_lo;
-    const int64_t rs = static_cast<int64_t>(p.kv_heads) * D;
-    split_scores<T>(kc + g * D, rs, q, D, kn, kc, rs, q, 0, kn, t_lo, t_hi, slot, rep, p.scale, sc, cap, warp,
-                    lane);
+    // scores of this CTA's ring slots; the new token's slot comes from shared memory
+    split_scores<T, REP>(kc + g * D, rs, q, D, kn, kc, rs, q, 0, kn, t_lo, t_hi, slot, p.scale, sc, cap, warp,
+                         lane);
     __syncthreads();
-    split_softmax<T>(cluster, sc, cap, cnt, rep, red, warp, lane);
+    split_softmax<T, REP>(cluster, sc, cap, cnt, red, warp, lane);
     __syncthreads();
-    weighted_rows<T>(vc + static_cast<int64_t>(t_lo) * rs + g * D, rs, cnt, D, sc, cap, rep, slot - t_lo, vn,
-                     warp, lane, [&](int h, int c, float v) { part[h * D + c] = v; });
+    weighted_rows<T, REP>(vc + static_cast<int64_t>(t_lo) * rs + g * D, rs, cnt, D, sc, cap, slot - t_lo, vn,
+                          wred, warp, lane, [&](int h, int c, float v) { part[h * D + c] = v; });
     cluster.sync();
     // this CTA's share of the outputs: the partial sums added in CTA order
     const int per = (rep * D + splits - 1) / splits;

@@ -73,9 +73,16 @@ std::atomic<bool> g_fused_route_enabled{false};
 std::atomic<bool> g_two_phase_enabled{true};
 
 // Weight-major calls with shared experts: the down GEMM writes the output as
-// each column tile completes (no finalize kernel).  Set by
-// chronos_moe_set_option("fold_finalize", 0/1).
-std::atomic<bool> g_fold_enabled{true};
+// each column tile completes (no finalize kernel).  Off by default: waiting
+// for each unit's reduce-adds before counting it in stalls the epilogue, and
+// measured slower than the finalize kernel it replaces (decode batches of 32
+// and 64 tokens: 225 and 265 us per call with it, 198 and 203 us without).
+// Set by chronos_moe_set_option("fold_finalize", 0/1).
+std::atomic<bool> g_fold_enabled{false};
+
+// Weight-major down GEMM: K is split until the call has about this many units
+// per SM (0: no split).  Set by chronos_moe_set_option("down_split_target", n).
+std::atomic<int> g_down_split_target{8};
 
 inline void count_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
 
@@ -767,7 +774,7 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
         const int64_t tiles_est = groups_est * ((N + bn_dn - 1) / bn_dn);
         // the down epilogue reduces anyway, so K splits only cost reduce traffic:
         // aim at >= 8 units per SM for an even finish
-        const int target = 8 * sm_count();
+        const int target = g_down_split_target.load() * sm_count();
         while (tiles_est * mt_dn * splits_dn < target && splits_dn * 2 * 4 <= kt_total)
             splits_dn *= 2;
         kt_dn = (kt_total + splits_dn - 1) / splits_dn;
@@ -1084,6 +1091,12 @@ extern "C" int chronos_moe_set_option(const char* name, int64_t value) {
         g_two_phase_enabled.store(value != 0);
         return CHRONOS_OK;
     }
+    if (name != nullptr && std::strcmp(name, "down_split_target") == 0) {
+        if (value < 0 || value > 64) return fail(CHRONOS_ERR_INVALID_ARG, "down_split_target %lld (0..64)",
+                                                 static_cast<long long>(value));
+        g_down_split_target.store(static_cast<int>(value));
+        return CHRONOS_OK;
+    }
     return fail(CHRONOS_ERR_INVALID_ARG, "unknown option %s", name ? name : "(null)");
 }
 
@@ -1262,9 +1275,13 @@ int lookahead_impl(const ChronosLookaheadArgs* a, cudaStream_t st) {
     auto aligned16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
     p.vec1 = (p.h % 8 == 0 && aligned16(p.x) && aligned16(p.w1)) ? 1 : 0;
     p.vec2 = (p.inner % 8 == 0 && aligned16(p.w2)) ? 1 : 0;
-    p.tb = std::max(1, std::min<int>(kLookaheadMaxTB, kLookaheadXBytes / (p.h * 4)));
     // one CTA per 32 W1 rows (a pass of 8 warps x 4 rows), at most 8
     int cs = std::min(kLookaheadMaxCluster, std::max(1, (p.inner + 31) / 32));
+    // tokens per cluster: up to 8 (every W1 row read once per 8 tokens), fewer
+    // when that leaves SMs idle (a 32-token decode batch: 2 per cluster, 128 CTAs)
+    const int64_t fill = (p.n * cs + sm_count() - 1) / sm_count();
+    p.tb = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({static_cast<int64_t>(kLookaheadMaxTB), fill,
+                                                                    kLookaheadXBytes / (p.h * 4)})));
     size_t smem = 0;
     for (;; cs /= 2) {
         p.rpc = (p.inner + cs - 1) / cs;
@@ -1396,6 +1413,7 @@ size_t mla_smem_base(const AttnParams& p) {
                             + p.latent + p.rope_dim    // cnew, krn
                             + (rep + 1) * p.rope_dim   // tmp
                             + 2 * kAttnMaxRep          // red
+                            + attn_red_floats(p.rep, p.latent)   // weighted-sum reduction
                             + rep * p.cap);            // scores
 }
 
@@ -1406,27 +1424,16 @@ size_t sw_smem(const AttnParams& p) {
                             + (rep + 1) * p.head_dim   // tmp
                             + rep * p.head_dim         // part
                             + 2 * kAttnMaxRep          // red
+                            + attn_red_floats(p.rep, p.head_dim)   // weighted-sum reduction
                             + rep * p.cap);            // scores
 }
 
-// CTAs per (kv head, batch row) pair: about two CTAs per SM in all, at most a
-// portable cluster of 8.
-int attn_splits(int64_t items) {
-    static int sms[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    int& n = sms[dev & 63];
-    if (n == 0 && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n = 148;
-    const int64_t target = 2 * static_cast<int64_t>(n);
-    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(kAttnMaxSplits, (target + items - 1) / items)));
-}
-
-// Whether a cluster of `splits` CTAs of `kernel` with `smem` bytes each can be
-// placed on this GPU (checked once per kernel, device and shape).
-bool attn_cluster_fits(void (*kernel)(AttnParams), int splits, size_t smem) {
-    if (splits <= 1) return true;
+// How many clusters of `splits` CTAs of `kernel` with `smem` bytes each this
+// GPU runs at once (0: none can be placed); queried once per kernel, device
+// and shape.
+int attn_active_clusters(void (*kernel)(AttnParams), int splits, size_t smem) {
     static std::mutex mu;
-    static std::map<std::tuple<const void*, int, int, size_t>, bool> seen;
+    static std::map<std::tuple<const void*, int, int, size_t>, int> seen;
     int dev = 0;
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lk(mu);
@@ -1445,10 +1452,10 @@ bool attn_cluster_fits(void (*kernel)(AttnParams), int splits, size_t smem) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;
-    const bool ok = cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) == cudaSuccess && clusters >= 1;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) clusters = 0;
     cudaGetLastError();   // a refused query leaves no error behind
-    seen[key] = ok;
-    return ok;
+    seen[key] = clusters;
+    return clusters;
 }
 
 // Split the positions over `splits` CTAs: the score capacity per CTA and, for
@@ -1462,31 +1469,37 @@ size_t attn_layout(AttnParams& p, bool mla, int splits, size_t elem) {
     return base + (p.stage_w ? w : 0);
 }
 
-// Choose the split of this call: the parallel choice, raised until shared
-// memory fits, lowered while the cluster cannot be placed.  0 or an error.
+// Choose the split of this call: the most CTAs per (kv head, row) pair (at
+// most a portable cluster of 8) whose clusters all run in one wave; the fewest
+// whose shared memory fits when no split runs in one wave.  0 or an error.
 int attn_plan(AttnParams& p, bool mla, int batch, size_t elem, void (*kernel)(AttnParams), size_t* smem,
               const char* what) {
-    int splits = attn_splits(static_cast<int64_t>(p.kv_heads) * std::max(1, batch));
-    *smem = attn_layout(p, mla, splits, elem);
-    while (*smem > static_cast<size_t>(kAttnMaxSmem) && splits < kAttnMaxSplits)
-        *smem = attn_layout(p, mla, ++splits, elem);
+    int s_min = 1;
+    *smem = attn_layout(p, mla, s_min, elem);
+    while (*smem > static_cast<size_t>(kAttnMaxSmem) && s_min < kAttnMaxSplits)
+        *smem = attn_layout(p, mla, ++s_min, elem);
     if (*smem > static_cast<size_t>(kAttnMaxSmem))
         return fail(CHRONOS_ERR_INVALID_ARG, "%s: %d cached positions x %d heads per kv head need %zu bytes of "
                     "shared memory per CTA at %d CTAs per head group (limit %d)", what,
-                    mla ? p.max_len : p.window, p.rep, *smem, splits, kAttnMaxSmem);
+                    mla ? p.max_len : p.window, p.rep, *smem, s_min, kAttnMaxSmem);
     if (batch == 0) return CHRONOS_OK;
-    if (int rc = set_smem(kernel, static_cast<int>(*smem))) return rc;
-    while (splits > 1 && !attn_cluster_fits(kernel, splits, *smem)) {
-        const size_t next = attn_layout(p, mla, splits - 1, elem);
-        if (next > static_cast<size_t>(kAttnMaxSmem)) break;
-        --splits;
-        *smem = next;
-        if (int rc = set_smem(kernel, static_cast<int>(*smem))) return rc;
+    const int64_t items = static_cast<int64_t>(p.kv_heads) * batch;
+    int best = 0;
+    for (int sp = kAttnMaxSplits; sp >= s_min && best == 0; --sp) {
+        const size_t sm = attn_layout(p, mla, sp, elem);
+        if (int rc = set_smem(kernel, static_cast<int>(sm))) return rc;
+        if (attn_active_clusters(kernel, sp, sm) >= items) best = sp;
     }
-    if (!attn_cluster_fits(kernel, splits, *smem))
-        return fail(CHRONOS_ERR_CUDA, "%s: a cluster of %d CTAs with %zu bytes of shared memory cannot be placed",
-                    what, splits, *smem);
-    return CHRONOS_OK;
+    if (best == 0) {
+        best = s_min;
+        while (best <= kAttnMaxSplits && attn_active_clusters(kernel, best, attn_layout(p, mla, best, elem)) < 1)
+            ++best;
+        if (best > kAttnMaxSplits)
+            return fail(CHRONOS_ERR_CUDA, "%s: no cluster of %d..%d CTAs can be placed", what, s_min,
+                        kAttnMaxSplits);
+    }
+    *smem = attn_layout(p, mla, best, elem);
+    return set_smem(kernel, static_cast<int>(*smem));
 }
 
 int attn_launch(void (*kernel)(AttnParams), const AttnParams& p, int batch, size_t smem, cudaStream_t st) {
@@ -1507,9 +1520,28 @@ int attn_launch(void (*kernel)(AttnParams), const AttnParams& p, int batch, size
     return CHRONOS_OK;
 }
 
+// The decode kernel for `rep` query heads per kv head (1..8).
+template <typename T, int REP>
+void (*attn_kernel_rep(bool mla))(AttnParams) {
+    return mla ? mla_decode_kernel<T, REP> : sw_decode_kernel<T, REP>;
+}
+template <typename T>
+void (*attn_kernel(bool mla, int rep))(AttnParams) {
+    switch (rep) {
+        case 1: return attn_kernel_rep<T, 1>(mla);
+        case 2: return attn_kernel_rep<T, 2>(mla);
+        case 3: return attn_kernel_rep<T, 3>(mla);
+        case 4: return attn_kernel_rep<T, 4>(mla);
+        case 5: return attn_kernel_rep<T, 5>(mla);
+        case 6: return attn_kernel_rep<T, 6>(mla);
+        case 7: return attn_kernel_rep<T, 7>(mla);
+        default: return attn_kernel_rep<T, 8>(mla);
+    }
+}
+
 template <typename T>
 int attn_impl(AttnParams p, bool mla, int batch, cudaStream_t st, const char* what) {
-    void (*kernel)(AttnParams) = mla ? mla_decode_kernel<T> : sw_decode_kernel<T>;
+    void (*kernel)(AttnParams) = attn_kernel<T>(mla, p.rep);
     size_t smem = 0;
     if (int rc = attn_plan(p, mla, batch, sizeof(T), kernel, &smem, what)) return rc;
     if (batch == 0) return CHRONOS_OK;
@@ -1527,6 +1559,19 @@ int norm_impl(const ChronosNormArgs* a, cudaStream_t st) {
     p.sum_out = a->sum_out;
     p.weight = a->weight;
     p.out = a->out;
+    auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    if (a->width % 8 == 0 && a->width <= 8 * 256 && a16(a->x) && a16(a->weight) && a16(a->out) &&
+        (a->residual == nullptr || a16(a->residual)) && (a->sum_out == nullptr || a16(a->sum_out))) {
+        // one warp per row, the row in registers
+        const unsigned grid = static_cast<unsigned>((a->rows + kAttnWarps - 1) / kAttnWarps);
+        const int vpl = (a->width + 255) / 256;
+        void (*kernel)(NormParams) = vpl <= 1 ? add_rmsnorm_warp_kernel<T, 1>
+                                     : vpl <= 2 ? add_rmsnorm_warp_kernel<T, 2>
+                                     : vpl <= 4 ? add_rmsnorm_warp_kernel<T, 4>
+                                                : add_rmsnorm_warp_kernel<T, 8>;
+        CHRONOS_CUDA_CHECK(launch_kernel(kernel, dim3(grid), dim3(kAttnThreads), 0, st, false, p));
+        return CHRONOS_OK;
+    }
     const int smem = static_cast<int>(sizeof(float) * (a->width + kAttnWarps));
     if (int rc = set_smem(add_rmsnorm_kernel<T>, smem)) return rc;
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(a->rows, 1 << 20));

@@ -35,10 +35,15 @@ def main(argv=None) -> int:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--fused-route", action="store_true",
                     help="decode routing as one cluster launch (chronos_moe_set_option)")
+    ap.add_argument("--option", action="append", default=[], metavar="NAME=VALUE",
+                    help="any chronos_moe_set_option switch, e.g. down_split_target=4")
     args = ap.parse_args(argv)
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     ops.set_option("fused_route", 1 if args.fused_route else 0)
+    for opt in args.option:
+        name, _, value = opt.partition("=")
+        ops.set_option(name, int(value))
     if args.workload == "ep":
         return _ep(args, dev)
     if args.workload == "model":

@@ -392,7 +392,7 @@ def test_folded_finalize_matches_finalize_kernel(n):
             torch.cuda.synchronize()
             ops.check_status()
     finally:
-        ops.set_option("fold_finalize", 1)
+        ops.set_option("fold_finalize", 0)
     for y in outs[1:]:
         assert O.rel_l2(y, outs[0]) <= 1e-3
     emu, idx, _, _ = _oracle(wl, 4, True, avail=avail, emulate=True)
