@@ -67,6 +67,9 @@ extern "C" {
 /* topk_idx / topk_weight are INPUTS produced by an earlier
  * chronos_moe_route call (the host-hook slow path); routing is skipped. */
 #define CHRONOS_FLAG_PREROUTED 0x1
+/* avail is a residency mask: a_e = 1 where avail[e] > 0, else 0 (the caller's
+ * mask passed as it is, no thresholding pass before the call). */
+#define CHRONOS_FLAG_AVAIL_MASK 0x2
 
 typedef struct ChronosMoeShape {
     int64_t num_tokens;  /* N = B*S (x.view(-1, H), moe_chronos.py:110-111); 0 is allowed */
@@ -221,12 +224,12 @@ CHRONOS_API uint64_t chronos_moe_kernel_launches(void);
  *                  ONE launch, a thread-block cluster that computes the chunk
  *                  partials, the selection and the plan; 0 (default): the logit
  *                  kernel and the select + plan kernel.
- *   "two_phase_combine"  1 (default): a large call whose shared experts run last
- *                  in the token-major down GEMM combines in two phases: routed
- *                  units store coef * expert(x) rounded to the layer dtype per
- *                  slot, the shared units sum each token's slots in choice order
- *                  (deterministic; no fp32 accumulator); 0: fp32 reduce-adds
- *                  into an accumulator.
+ *   "two_phase_combine"  1: a large call whose shared experts run last in the
+ *                  token-major down GEMM combines in two phases: routed units
+ *                  store coef * expert(x) rounded to the layer dtype per slot,
+ *                  the shared units sum each token's slots in choice order
+ *                  (deterministic; no fp32 accumulator); 0 (default, measured
+ *                  faster): fp32 reduce-adds into an accumulator.
  *   "fold_finalize"  1: a call below 1024 tokens with shared experts writes
  *                  its output from the down GEMM, each 128-column tile
  *                  converted by the CTA whose contribution completes it; 0

@@ -36,6 +36,7 @@ DTYPE_FP16 = 1
 DTYPE_FP32 = 2
 
 FLAG_PREROUTED = 0x1
+FLAG_AVAIL_MASK = 0x2
 
 ABI_VERSION = 2
 

@@ -136,12 +136,14 @@ __global__ void __launch_bounds__(kAttnThreads) add_rmsnorm_warp_kernel(NormPara
     const int64_t base = r * p.width;
     const T* x = static_cast<const T*>(p.x) + base;
     const T* res = p.residual != nullptr ? static_cast<const T*>(p.residual) + base : nullptr;
-    float v[VPL][8];
+    const T* w = static_cast<const T*>(p.weight);
+    float v[VPL][8], wv[VPL][8];
     float ss = 0.0f;
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
         const int c8 = lane + 32 * i;
         if (c8 < nv) {
+            load8<T>(w + c8 * 8, wv[i]);   // issued with the row's loads, used after the sum
             load8<T>(x + c8 * 8, v[i]);
             if (res != nullptr) {
                 float rr[8];
@@ -156,16 +158,14 @@ __global__ void __launch_bounds__(kAttnThreads) add_rmsnorm_warp_kernel(NormPara
     const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(p.width) + p.eps);
     T* sum_out = p.sum_out != nullptr ? static_cast<T*>(p.sum_out) + base : nullptr;
     T* out = static_cast<T*>(p.out) + base;
-    const T* w = static_cast<const T*>(p.weight);
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
         const int c8 = lane + 32 * i;
         if (c8 < nv) {
             if (sum_out != nullptr) store8<T>(sum_out + c8 * 8, v[i]);
-            float wv[8], o[8];
-            load8<T>(w + c8 * 8, wv);
+            float o[8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) o[u] = wv[u] * (v[i][u] * inv);
+            for (int u = 0; u < 8; ++u) o[u] = wv[i][u] * (v[i][u] * inv);
             store8<T>(out + c8 * 8, o);
         }
     }

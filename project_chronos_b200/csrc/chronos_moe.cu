@@ -68,9 +68,11 @@ std::atomic<uint64_t> g_kernel_launches{0};
 std::atomic<bool> g_fused_route_enabled{false};
 
 // Prefill-sized calls (token-major down GEMM, shared experts last): combine the
-// routed rows in two phases (stores + an ordered per-token sum) instead of fp32
-// reduce-adds.  Set by chronos_moe_set_option("two_phase_combine", 0/1).
-std::atomic<bool> g_two_phase_enabled{true};
+// routed rows in two phases (stores + an ordered per-token sum, bitwise
+// reproducible) instead of fp32 reduce-adds.  Off by default: measured slower
+// (8192-token prefill 1.30 ms with it, 1.14 ms without).  Set by
+// chronos_moe_set_option("two_phase_combine", 0/1).
+std::atomic<bool> g_two_phase_enabled{false};
 
 // Weight-major calls with shared experts: the down GEMM writes the output as
 // each column tile completes (no finalize kernel).  Off by default: waiting
@@ -352,6 +354,7 @@ RouteParams route_params(const ChronosMoeArgs* a, const Ptrs& w, bool prerouted,
     rp.w = a->router_w;
     rp.bias = a->router_bias;
     rp.avail = a->avail;
+    rp.avail_mask = (a->flags & CHRONOS_FLAG_AVAIL_MASK) ? 1 : 0;
     rp.slot_of_expert = a->slot_of_expert;
     rp.n = s.num_tokens;
     rp.h = s.hidden;

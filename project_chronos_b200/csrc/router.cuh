@@ -38,6 +38,7 @@ struct RouteParams {
     const void* w;
     const float* bias;
     const float* avail;
+    int avail_mask;  // 1: a_e = (avail[e] > 0)
     const int32_t* slot_of_expert;
     int64_t n;
     int h, e, k, num_shared, norm_topk, prerouted;
@@ -343,6 +344,7 @@ constexpr int kSelectThreads = 512;
 
 __device__ __forceinline__ float expert_avail(const RouteParams& p, int e) {
     float a = p.avail ? p.avail[e] : 1.0f;
+    if (p.avail_mask) a = a > 0.0f ? 1.0f : 0.0f;
     if (p.slot_of_expert && p.slot_of_expert[e] < 0) a = 0.0f;
     return a;
 }

@@ -598,6 +598,7 @@ class ChronosMOEFeedForward(nn.Module):
         else:
             # ---- fast path: one call, no host synchronisation ----
             on_demand = _NO_ON_DEMAND
+            avail_is_mask = False
             if not masked:
                 a_np = None
                 avail_t = None
@@ -607,6 +608,13 @@ class ChronosMOEFeedForward(nn.Module):
                 if mask_np is not None:
                     a_np = ((mask_np > 0.0) & (live > 0)).astype(np.float32)
                     avail_t = self._avail_tensor(a_np, dev)
+                elif not has_placeholder:
+                    # every expert live: the kernels threshold the mask themselves
+                    # (one snapshot copy instead of three elementwise passes)
+                    a_np = None
+                    m = available_expert_mask.detach()
+                    avail_t = (m.clone() if m.dtype == torch.float32 else m.to(torch.float32)).contiguous()
+                    avail_is_mask = True
                 else:
                     a_np = None
                     avail_t = (available_expert_mask.to(torch.float32) > 0).to(torch.float32) * \
@@ -624,7 +632,8 @@ class ChronosMOEFeedForward(nn.Module):
                     a_np = None
                     avail_t = avail_dev
             out = self._layer_call(pool, bias)(x_flat, avail=avail_t, want_probs=True,
-                                               want_stats=masked, want_topk=self.training)
+                                               want_stats=masked, want_topk=self.training,
+                                               avail_is_mask=avail_is_mask)
             probs = out["probs"]
             if masked:
                 if a_np is None:

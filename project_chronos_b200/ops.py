@@ -255,7 +255,9 @@ class LayerCall:
         return size
 
     def __call__(self, x: torch.Tensor, avail: Optional[torch.Tensor] = None, want_probs: bool = True,
-                 want_stats: bool = False, want_topk: bool = False) -> dict:
+                 want_stats: bool = False, want_topk: bool = False, avail_is_mask: bool = False) -> dict:
+        """``avail_is_mask``: ``avail`` is a residency mask, a_e = (avail[e] > 0),
+        thresholded by the kernels (CHRONOS_FLAG_AVAIL_MASK)."""
         if not x.is_cuda or x.dtype != self.dtype:
             raise TypeError(f"x must be a CUDA {self.dtype} tensor")
         x = x.contiguous()
@@ -284,6 +286,8 @@ class LayerCall:
         a.expert_mass = _ptr(mass)
         a.workspace = ws.data_ptr()
         a.workspace_bytes = ws.numel()
+        if avail_is_mask and avail is not None:
+            a.flags |= N.FLAG_AVAIL_MASK
         if torch.cuda.current_device() == dev.index:
             rc = self._lib.chronos_moe_forward(ctypes.byref(a), ctypes.c_void_p(stream))
         else:

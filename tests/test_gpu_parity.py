@@ -365,7 +365,7 @@ def test_two_phase_combine_matches_reduce_adds(n, h, e, k, f, s):
             torch.cuda.synchronize()
             ops.check_status()
     finally:
-        ops.set_option("two_phase_combine", 1)
+        ops.set_option("two_phase_combine", 0)
     red, two, two_again = (_np(o["y"]) for o in outs)
     assert np.array_equal(two, two_again)
     assert O.rel_l2(two, red) <= 3e-3
