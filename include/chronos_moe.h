@@ -234,9 +234,18 @@ CHRONOS_API uint64_t chronos_moe_kernel_launches(void);
  *                  its output from the down GEMM, each 128-column tile
  *                  converted by the CTA whose contribution completes it; 0
  *                  (default, measured faster): a separate finalize kernel.
- *   "down_split_target"  n (default 8, 0..64): the weight-major down GEMM of a
- *                  decode call splits K until it has about n work units per SM
- *                  (0: no split).
+ *   "down_split_target"  -1 (default): the weight-major down GEMM of a decode
+ *                  call halves K when that fills the last round of work units
+ *                  more than 5 % better; n in 0..64: split until it has about n
+ *                  units per SM (0: no split).
+ *   "gateup_split"  1: a decode call (N <= 64) whose gate/up units would not
+ *                  cover the SMs splits the routed units along K (2 or 4 ways);
+ *                  the split completing a tile sums the fp32 partials in split
+ *                  order and applies SiLU-mul; 0 (default, measured faster): never.
+ *                  Set it before sizing a workspace (it reserves the partials).
+ *   "select_plan_one_block"  1: decode calls of 9..32 tokens select and plan
+ *                  in one block of a warp per token; 0 (default, measured
+ *                  faster): blocks of 8 tokens and a last-block plan.
  * Returns CHRONOS_OK, or CHRONOS_ERR_INVALID_ARG for an unknown name or a value
  * out of range. */
 CHRONOS_API int chronos_moe_set_option(const char* name, int64_t value);

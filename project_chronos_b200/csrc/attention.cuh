@@ -361,8 +361,10 @@ __device__ __forceinline__ void split_scores(const T* rows1, int64_t st1, const 
 }
 
 // The cluster-wide softmax of the scores sc[h * cap + i], i < cnt, rounded to T
-// in place.  red[0..REP) and red[kAttnMaxRep..+REP) are this CTA's published
-// maximum and sum.  Contains two cluster barriers.
+// in place.  Each CTA publishes its maximum m_r and sum l_r = sum exp(s - m_r)
+// per head (red[0..REP) and red[kAttnMaxRep..+REP)); after one cluster barrier
+// every CTA forms M = max m_r and L = sum_r l_r exp(m_r - M) in CTA order and
+// rounds p = exp(s - M) / L.
 template <typename T, int REP>
 __device__ __forceinline__ void split_softmax(cooperative_groups::cluster_group& cluster, float* sc, int cap,
                                               int cnt, float* red, int warp, int lane) {
@@ -371,28 +373,25 @@ __device__ __forceinline__ void split_softmax(cooperative_groups::cluster_group&
         float m = -INFINITY;
         for (int i = lane; i < cnt; i += 32) m = fmaxf(m, sc[h * cap + i]);
         m = warp_max(m);
-        if (lane == 0) red[h] = m;
-    }
-    cluster.sync();
-    for (int h = warp; h < REP; h += kAttnWarps) {
-        float m = lane < splits ? cluster.map_shared_rank(red, lane)[h] : -INFINITY;
-        m = warp_max(m);
         float sum = 0.0f;
-        for (int i = lane; i < cnt; i += 32) {
-            const float e = __expf(sc[h * cap + i] - m);
-            sc[h * cap + i] = e;
-            sum += e;
-        }
+        for (int i = lane; i < cnt; i += 32) sum += __expf(sc[h * cap + i] - m);
         sum = warp_sum(sum);
-        if (lane == 0) red[kAttnMaxRep + h] = sum;
+        if (lane == 0) {
+            red[h] = m;
+            red[kAttnMaxRep + h] = sum;
+        }
     }
     cluster.sync();
     for (int h = warp; h < REP; h += kAttnWarps) {
+        float mr = lane < splits ? cluster.map_shared_rank(red, lane)[h] : -INFINITY;
+        const float lr = lane < splits ? cluster.map_shared_rank(red, lane)[kAttnMaxRep + h] : 0.0f;
+        const float M = warp_max(mr);
+        // l_r exp(m_r - M), summed by lane 0 in CTA order (an empty CTA adds 0)
+        const float term = lr > 0.0f ? lr * __expf(mr - M) : 0.0f;
         float tot = 0.0f;
-        if (lane == 0)
-            for (int r = 0; r < splits; ++r) tot += cluster.map_shared_rank(red, r)[kAttnMaxRep + h];
-        const float inv = 1.0f / __shfl_sync(0xffffffffu, tot, 0);
-        for (int i = lane; i < cnt; i += 32) sc[h * cap + i] = round_to<T>(sc[h * cap + i] * inv);
+        for (int r = 0; r < splits; ++r) tot += __shfl_sync(0xffffffffu, term, r);
+        const float inv = 1.0f / tot;
+        for (int i = lane; i < cnt; i += 32) sc[h * cap + i] = round_to<T>(__expf(sc[h * cap + i] - M) * inv);
     }
 }
 
@@ -501,27 +500,25 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) mla_decode_ker
     // RoPE at `pos` on q_rope (every head) and on the new k_rope
     const T* crow = static_cast<const T*>(p.cos) + static_cast<int64_t>(pos) * D;
     const T* srow = static_cast<const T*>(p.sin) + static_cast<int64_t>(pos) * D;
+    // rotated q_rope heads and k_rope: tmp [rep][R] and tmp + rep*R [R]
     for (int i = threadIdx.x; i < (rep + 1) * R; i += kAttnThreads) {
         const int h = i / R, e = i % R;
         tmp[i] = rope_value<T>(h < rep ? qr + h * R : krn, e, R, crow, srow);
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < (rep + 1) * R; i += kAttnThreads) {
-        const int h = i / R, e = i % R;
-        (h < rep ? qr + h * R : krn)[e] = tmp[i];
-    }
-    __syncthreads();
+    const float* qrot = tmp;
+    const float* krot = tmp + rep * R;
     // append the new token to the cache (by CTA 0 of the cluster; the latent once, by group 0)
     if (sidx == 0) {
         if (g == 0)
             for (int j = threadIdx.x; j < L; j += kAttnThreads)
                 cache_c[static_cast<int64_t>(pos) * L + j] = from_f32<T>(cnew[j]);
         for (int r = threadIdx.x; r < R; r += kAttnThreads)
-            cache_k[(static_cast<int64_t>(pos) * p.kv_heads + g) * R + r] = from_f32<T>(krn[r]);
+            cache_k[(static_cast<int64_t>(pos) * p.kv_heads + g) * R + r] = from_f32<T>(krot[r]);
     }
     // this CTA's positions: latent against q_abs, rope key against q_rope
-    split_scores<T, REP>(cache_c, L, qabs, L, cnew, cache_k + g * R, static_cast<int64_t>(p.kv_heads) * R, qr, R,
-                         krn, t_lo, t_hi, pos, p.scale, sc, cap, warp, lane);
+    split_scores<T, REP>(cache_c, L, qabs, L, cnew, cache_k + g * R, static_cast<int64_t>(p.kv_heads) * R, qrot, R,
+                         krot, t_lo, t_hi, pos, p.scale, sc, cap, warp, lane);
     __syncthreads();
     split_softmax<T, REP>(cluster, sc, cap, cnt, red, warp, lane);
     __syncthreads();
@@ -608,24 +605,22 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) sw_decode_kern
     __syncthreads();
     const T* crow = static_cast<const T*>(p.cos) + static_cast<int64_t>(rpos) * D;
     const T* srow = static_cast<const T*>(p.sin) + static_cast<int64_t>(rpos) * D;
+    // rotated queries and key: tmp [rep][D] and tmp + rep*D [D]
     for (int i = threadIdx.x; i < (rep + 1) * D; i += kAttnThreads) {
         const int h = i / D, e = i % D;
         tmp[i] = rope_value<T>(h < rep ? q + h * D : kn, e, D, crow, srow);
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < (rep + 1) * D; i += kAttnThreads) {
-        const int h = i / D, e = i % D;
-        (h < rep ? q + h * D : kn)[e] = tmp[i];
-    }
-    __syncthreads();
+    const float* qrot = tmp;
+    const float* krot = tmp + rep * D;
     if (sidx == 0)
         for (int i = threadIdx.x; i < D; i += kAttnThreads) {
-            kc[(static_cast<int64_t>(slot) * p.kv_heads + g) * D + i] = from_f32<T>(kn[i]);
+            kc[(static_cast<int64_t>(slot) * p.kv_heads + g) * D + i] = from_f32<T>(krot[i]);
             vc[(static_cast<int64_t>(slot) * p.kv_heads + g) * D + i] = from_f32<T>(vn[i]);
         }
     // scores of this CTA's ring slots; the new token's slot comes from shared memory
-    split_scores<T, REP>(kc + g * D, rs, q, D, kn, kc, rs, q, 0, kn, t_lo, t_hi, slot, p.scale, sc, cap, warp,
-                         lane);
+    split_scores<T, REP>(kc + g * D, rs, qrot, D, krot, kc, rs, qrot, 0, krot, t_lo, t_hi, slot, p.scale, sc,
+                         cap, warp, lane);
     __syncthreads();
     split_softmax<T, REP>(cluster, sc, cap, cnt, red, warp, lane);
     __syncthreads();

@@ -12,6 +12,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <cmath>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -83,8 +84,16 @@ std::atomic<bool> g_two_phase_enabled{false};
 std::atomic<bool> g_fold_enabled{false};
 
 // Weight-major down GEMM: K is split until the call has about this many units
-// per SM (0: no split).  Set by chronos_moe_set_option("down_split_target", n).
-std::atomic<int> g_down_split_target{8};
+// per SM (0: no split); -1 (default): the split that best fills the last round
+// of units (see forward_impl).  Set by chronos_moe_set_option("down_split_target", n).
+std::atomic<int> g_down_split_target{-1};
+
+// Decode batches of 9..32 tokens: selection + plan in one block of a warp per
+// token (no ticket) instead of blocks of 8 tokens and a last-block plan.  Off by
+// default: measured slower (32 tokens: 200.6-201.5 us per decode call with it,
+// 196.3-196.9 without; 8-layer model 795 vs 785 us per step).  Set by
+// chronos_moe_set_option("select_plan_one_block", 0/1).
+std::atomic<bool> g_select_one_block{false};
 
 inline void count_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
 
@@ -144,8 +153,38 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 struct Layout {
     size_t grp_count, grp_off, act_rows, act_xrow, act_hrow, act_wslot, act_eid, ustart_gu, partials,
         ustart_dn, hdr, pos, sel_coef, shared_coef, topk_idx, topk_w, slot_tok, slot_coef, slot_map, pair_slot,
-        tile_cnt, xp, hid, y_acc, total;
+        tile_cnt, gu_cnt, gu_part, xp, hid, y_acc, total;
 };
+
+// Decode gate/up K splits (weight-major, dense mode, N <= 64): when the call's
+// routed and shared units would not cover the SMs (a batch of one token: 6
+// routed experts x 11 weight-row tiles + 22 shared units for 148 SMs), the
+// routed units are split along K (2 or 4 ways, >= 4 k tiles each) and the last
+// split of a tile to finish sums the fp32 partials in split order and applies
+// SiLU-mul.  The shared experts' units run before the plan exists and stay
+// whole.  A function of the shape and the SM count, so the workspace layout
+// and the call agree.  Off by default: measured slower (batch 1: 53.6-54.3 us
+// per call split, 51.4 unsplit; the split gate/up kernel alone 36.7 vs 24.6 us
+// in a serialised replay): the extra routed units all start after the routing
+// wait, and the CTAs that get two of them finish last.  Set by
+// chronos_moe_set_option("gateup_split", 0/1) before sizing a workspace.
+std::atomic<bool> g_gateup_split_enabled{false};
+
+int sm_count();
+
+int gateup_splits(const ChronosMoeShape& s) {
+    if (!g_gateup_split_enabled || s.num_tokens < 1 || s.num_tokens > kSelectPlanMaxTokens ||
+        s.dtype == CHRONOS_DTYPE_FP32 || s.hidden % kTcBK || s.ffn % kTcBK)
+        return 1;
+    const int kt = s.hidden / kTcBK;
+    const int mt = (s.ffn + kTcBM - 1) / kTcBM;
+    const double draws = static_cast<double>(s.num_tokens) * s.top_k;
+    const double routed = s.num_experts * (1.0 - std::pow(1.0 - 1.0 / s.num_experts, draws));
+    const double pre = static_cast<double>(s.num_shared) * mt;
+    int sp = 1;
+    while (routed * mt * sp + pre < sm_count() && sp < 4 && kt / (2 * sp) >= 4) sp *= 2;
+    return sp;
+}
 
 Layout make_layout(const ChronosMoeShape& s) {
     Layout L{};
@@ -180,6 +219,14 @@ Layout make_layout(const ChronosMoeShape& s) {
     L.slot_map = N <= static_cast<size_t>(kSelectPlanMaxTokens) ? take(4 * E * N) : off;
     L.pair_slot = take(4 * N * K);
     L.tile_cnt = take(4 * ((H + 127) / 128));
+    {
+        // decode gate/up K-split partials: [routed tile][split][G, U][token][128 rows] fp32
+        const size_t sp = static_cast<size_t>(gateup_splits(s));
+        const size_t routed = std::min(E, N * K);
+        const size_t mt = (F + 127) / 128;
+        L.gu_cnt = sp > 1 ? take(4 * routed * mt) : off;
+        L.gu_part = sp > 1 ? take(4 * routed * mt * sp * 2 * N * 128) : off;
+    }
     // x rows in expert order for the gate/up GEMM; once that GEMM is done, the
     // two-phase down GEMM's scaled slot rows (same size) go here
     L.xp = take(es * N * K * H);
@@ -513,9 +560,22 @@ int launch_route(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, bool p
 template <typename T>
 int launch_select_plan(const RouteParams& rp, const PlanParams& pp, const ScatterParams& sp, int num_experts,
                        bool pdl, cudaStream_t st) {
-    const dim3 g(static_cast<unsigned>((rp.n + kSelectPlanWarps - 1) / kSelectPlanWarps)), b(kSelectPlanThreads);
     int32_t* ticket = rp.grp_count + num_experts;
     cudaError_t err;
+    if (g_select_one_block && rp.n > kSelectPlanWarps && rp.n <= kSelectPlanWideThreads / 32) {
+        // 9..32 tokens: one block of a warp per token, no ticket, fence or re-reads
+        constexpr int NT = kSelectPlanWideThreads;
+        const dim3 g(1), b(NT);
+        switch (experts_per_lane(num_experts)) {
+            case 1: err = launch_kernel(route_select_plan_kernel<T, 1, NT>, g, b, 0, st, pdl, rp, pp, sp, ticket); break;
+            case 2: err = launch_kernel(route_select_plan_kernel<T, 2, NT>, g, b, 0, st, pdl, rp, pp, sp, ticket); break;
+            case 4: err = launch_kernel(route_select_plan_kernel<T, 4, NT>, g, b, 0, st, pdl, rp, pp, sp, ticket); break;
+            default: err = launch_kernel(route_select_plan_kernel<T, 8, NT>, g, b, 0, st, pdl, rp, pp, sp, ticket); break;
+        }
+        CHRONOS_CUDA_CHECK(err);
+        return CHRONOS_OK;
+    }
+    const dim3 g(static_cast<unsigned>((rp.n + kSelectPlanWarps - 1) / kSelectPlanWarps)), b(kSelectPlanThreads);
     switch (experts_per_lane(num_experts)) {
         case 1: err = launch_kernel(route_select_plan_kernel<T, 1>, g, b, 0, st, pdl, rp, pp, sp, ticket); break;
         case 2: err = launch_kernel(route_select_plan_kernel<T, 2>, g, b, 0, st, pdl, rp, pp, sp, ticket); break;
@@ -540,7 +600,7 @@ int launch_tc(const CUtensorMap& a0r, const CUtensorMap& a1r, const CUtensorMap&
 
 template <typename T, int BN, int BN_DN, bool TM_DN = false>
 int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int kt_per_split_dn, int slot,
-                   bool direct, bool shared_last, bool two_phase = false, bool fold = false) {
+                   bool direct, bool shared_last, bool two_phase = false, bool fold = false, int gu_splits = 1) {
     const ChronosMoeShape& s = a->shape;
     const int dt = s.dtype;
     const uint64_t N = static_cast<uint64_t>(s.num_tokens), H = s.hidden, F = s.ffn;
@@ -605,6 +665,14 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
         // decode: the shared experts' units run before the plan of the call exists
         pg.pre_units = static_cast<int>(S) * pg.m_tiles;
         pg.sh_hrow = static_cast<int64_t>(N * K);
+    }
+    if (kDense && gu_splits > 1) {
+        // routed units split along K; the shared (pre-plan) units stay whole
+        pg.kt_per_split = (pg.k_tiles + gu_splits - 1) / gu_splits;
+        pg.gu_splits = gu_splits;
+        pg.gu_cnt = w.at<int32_t>(w.L->gu_cnt);
+        pg.gu_part = w.at<float>(w.L->gu_part);
+        pg.num_shared = static_cast<int>(S);
     }
     prof_mark(slot, CHRONOS_STAGE_GATEUP, st);
     if constexpr (BN == kTmTokens) {
@@ -770,16 +838,35 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
                       : tc  ? (s.hidden + kTcBM - 1) / kTcBM
                             : (s.hidden + kSimtTile - 1) / kSimtTile;
 
+    // decode gate/up K split (dense mode only; the layout reserved its partials)
+    const int gu_splits = (tc && N <= kSelectPlanMaxTokens) ? gateup_splits(s) : 1;
     int splits_dn = 1, kt_dn = s.ffn / kTcBK;
     if (tc && !tm_dn) {
         const int kt_total = s.ffn / kTcBK;
-        const int64_t groups_est = std::min<int64_t>(s.num_experts, N * s.top_k) + s.num_shared;
-        const int64_t tiles_est = groups_est * ((N + bn_dn - 1) / bn_dn);
-        // the down epilogue reduces anyway, so K splits only cost reduce traffic:
-        // aim at >= 8 units per SM for an even finish
-        const int target = g_down_split_target.load() * sm_count();
-        while (tiles_est * mt_dn * splits_dn < target && splits_dn * 2 * 4 <= kt_total)
-            splits_dn *= 2;
+        // expected distinct routed experts of N*k draws over E, plus the shared ones
+        const double draws = static_cast<double>(N) * s.top_k;
+        const double groups_est =
+            s.num_experts * (1.0 - std::pow(1.0 - 1.0 / s.num_experts, draws)) + s.num_shared;
+        const double tiles_est = groups_est * static_cast<double>((N + bn_dn - 1) / bn_dn) * mt_dn;
+        const int target_units = g_down_split_target.load();
+        if (target_units >= 0) {
+            const double target = static_cast<double>(target_units) * sm_count();
+            while (tiles_est * splits_dn < target && splits_dn * 2 * 4 <= kt_total) splits_dn *= 2;
+        } else {
+            // halve K when that fills the last round of units clearly better
+            // (every unit's epilogue reduces anyway; the split adds reduce
+            // traffic and per-unit overhead, charged 5 %; measured: 4-way
+            // splits and splits of already-full rounds are slower)
+            double best = -1.0;
+            for (int sp = 1; sp * 4 <= kt_total && sp <= 2; sp *= 2) {
+                const double units = tiles_est * sp / sm_count();
+                const double score = units / std::ceil(units) - 0.05 * std::log2(static_cast<double>(sp));
+                if (score > best + 1e-9) {
+                    best = score;
+                    splits_dn = sp;
+                }
+            }
+        }
         kt_dn = (kt_total + splits_dn - 1) / splits_dn;
         splits_dn = (kt_total + kt_dn - 1) / kt_dn;
     }
@@ -853,6 +940,9 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     pp.ustart_dn = w.at<int32_t>(L.ustart_dn);
     pp.tile_cnt = fold ? w.at<int32_t>(L.tile_cnt) : nullptr;
     pp.n_tile_cnt = fold ? mt_dn : 0;
+    pp.splits_gu = (tc && bn <= kSelectPlanMaxTokens) ? gu_splits : 1;
+    pp.gu_cnt = pp.splits_gu > 1 ? w.at<int32_t>(L.gu_cnt) : nullptr;
+    pp.n_gu_cnt = pp.splits_gu > 1 ? static_cast<int>(std::min<int64_t>(s.num_experts, N * s.top_k)) * mt_gu : 0;
     // the plan is computed inside the scatter launch (stage "plan" stays empty)
     prof_mark(slot, CHRONOS_STAGE_SCATTER, st);
 
@@ -896,9 +986,9 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
             return fail(CHRONOS_ERR_INVALID_ARG, "internal: fp32 on the tensor-core path");
         } else {
             switch (bn) {
-                case 16: rc = launch_tc_pair<T, 16, 16>(a, w, st, kt_dn, slot, direct, shared_last, false, fold); break;
-                case 32: rc = launch_tc_pair<T, 32, 32>(a, w, st, kt_dn, slot, direct, shared_last, false, fold); break;
-                case 64: rc = launch_tc_pair<T, 64, 64>(a, w, st, kt_dn, slot, direct, shared_last, false, fold); break;
+                case 16: rc = launch_tc_pair<T, 16, 16>(a, w, st, kt_dn, slot, direct, shared_last, false, fold, gu_splits); break;
+                case 32: rc = launch_tc_pair<T, 32, 32>(a, w, st, kt_dn, slot, direct, shared_last, false, fold, gu_splits); break;
+                case 64: rc = launch_tc_pair<T, 64, 64>(a, w, st, kt_dn, slot, direct, shared_last, false, fold, gu_splits); break;
                 default:
                     rc = tm_dn ? launch_tc_pair<T, 128, 128, true>(a, w, st, kt_dn, slot, direct, shared_last,
                                                                     two_phase)
@@ -1094,9 +1184,17 @@ extern "C" int chronos_moe_set_option(const char* name, int64_t value) {
         g_two_phase_enabled.store(value != 0);
         return CHRONOS_OK;
     }
+    if (name != nullptr && std::strcmp(name, "gateup_split") == 0) {
+        g_gateup_split_enabled.store(value != 0);
+        return CHRONOS_OK;
+    }
+    if (name != nullptr && std::strcmp(name, "select_plan_one_block") == 0) {
+        g_select_one_block.store(value != 0);
+        return CHRONOS_OK;
+    }
     if (name != nullptr && std::strcmp(name, "down_split_target") == 0) {
-        if (value < 0 || value > 64) return fail(CHRONOS_ERR_INVALID_ARG, "down_split_target %lld (0..64)",
-                                                 static_cast<long long>(value));
+        if (value < -1 || value > 64) return fail(CHRONOS_ERR_INVALID_ARG, "down_split_target %lld (-1..64)",
+                                                  static_cast<long long>(value));
         g_down_split_target.store(static_cast<int>(value));
         return CHRONOS_OK;
     }

@@ -97,6 +97,16 @@ struct TcGemmParams {
     // finalize kernel follows.
     int32_t* tile_cnt;
     void* y_fold;
+    // Dense gate/up, routed units split along K (gu_splits > 1): each split
+    // writes its fp32 G and U columns of the call's tokens to
+    // gu_part[tile][split][G, U][token][128], counts itself in gu_cnt[tile]
+    // (tile = (group - num_shared) * m_tiles + weight-row tile, zeroed by the
+    // plan), and the split completing the tile sums the partials in split
+    // order and writes silu(G) * U.
+    int gu_splits;
+    int num_shared;
+    int32_t* gu_cnt;
+    float* gu_part;
 };
 
 __host__ __device__ constexpr int tc_stage_bytes(int bn, bool gateup) {
@@ -436,11 +446,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     if (!planned) load_plan();
                     if (u >= total) break;
                 }
-                // without K splits every unit spans the whole K: no unit decode on this path
+                // without K splits every unit spans the whole K: no unit decode on this path;
+                // the dense gate/up's pre-plan (shared) units are never split
                 const bool sfu = !GATEUP && u >= total_main;
-                const int split = (unsplit || sfu) ? 0 : tc_decode(p, num_active, u, BN, splits_unused).split;
+                const bool pre = GATEUP && DENSE && u < pre_units;
+                const int split =
+                    (unsplit || sfu || pre) ? 0 : tc_decode(p, num_active, u, BN, splits_unused).split;
                 const int kt0 = split * p.kt_per_split;
-                const int kt1 = sfu ? p.sf_shared * p.k_tiles : min(p.k_tiles, kt0 + p.kt_per_split);
+                const int kt1 = sfu   ? p.sf_shared * p.k_tiles
+                                : pre ? p.k_tiles
+                                      : min(p.k_tiles, kt0 + p.kt_per_split);
                 if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, kPipelineLimitNs, abort_flag)) {
                     *abort_flag = 1;
                     report_status(p.status, CHRONOS_ERR_PIPELINE_TIMEOUT);
@@ -499,6 +514,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // once its reduce-adds are complete (one unit later: no wait on the newest)
         int fold_pending = -1;
         volatile int* fold_last = abort_flag + 2;
+        volatile int* gu_last = abort_flag + 3;  // split gate/up: this CTA completed the tile
         auto fold_retire = [&](int tile) {
             fence_proxy_async_global();
             epilogue_bar_sync(128);
@@ -674,6 +690,79 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int m0 = w.mtile * kTcBM;
             const int ncols = min(kTcBM, p.out_cols - m0);
             constexpr int SUB = tc_staging_rows(BN, GATEUP);
+            if constexpr (GATEUP && DENSE) {
+                if (p.gu_splits > 1 && u >= pre_units) {
+                    // ---- routed unit of a K-split tile ----
+                    const int nt = static_cast<int>(p.n_tokens);  // <= BN
+                    const int tile = (w.a - p.num_shared) * p.m_tiles + w.mtile;
+                    const int64_t tstride = static_cast<int64_t>(nt) * kTcBM;  // one of G / U of one split
+                    float* part = p.gu_part + (static_cast<int64_t>(tile) * p.gu_splits + w.split) * 2 * tstride;
+#pragma unroll 1
+                    for (int c = 0; c < nt; c += 16) {  // uniform: the TMEM loads are warp-wide
+                        float g[16], uu[16];
+                        tmem_ld16(taddr + c, g);
+                        tmem_ld16(taddr + BN + c, uu);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            if (c + j < nt) {
+                                part[(c + j) * kTcBM + row_in_tile] = g[j];
+                                part[tstride + (c + j) * kTcBM + row_in_tile] = uu[j];
+                            }
+                        }
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&tempty[acc]);  // accumulator copied out: back to the MMA warp
+                    __threadfence();
+                    epilogue_bar_sync(128);
+                    if (et == 0) {
+                        const int done = atomicAdd(p.gu_cnt + tile, 1) + 1;
+                        const bool last = done == p.gu_splits;
+                        if (last) __threadfence();
+                        *gu_last = last ? 1 : 0;
+                    }
+                    epilogue_bar_sync(128);
+                    if (*gu_last) {
+                        // every split's partial is in: sum in split order, SiLU-mul
+                        __threadfence();
+                        const float* tb = p.gu_part + static_cast<int64_t>(tile) * p.gu_splits * 2 * tstride;
+#pragma unroll 1
+                        for (int c0 = 0; c0 < BN; c0 += SUB) {
+                            if (c0 >= nt) break;
+                            if (c0 > 0) {
+                                bulk_wait_read();
+                                epilogue_bar_sync(128);
+                            }
+#pragma unroll 1
+                            for (int c = c0; c < c0 + SUB; ++c) {
+                                float gs = 0.0f, us = 0.0f;
+                                if (c < nt) {
+                                    for (int sp = 0; sp < p.gu_splits; ++sp) {
+                                        gs += __ldcg(tb + sp * 2 * tstride + c * kTcBM + row_in_tile);
+                                        us += __ldcg(tb + (sp * 2 + 1) * tstride + c * kTcBM + row_in_tile);
+                                    }
+                                }
+                                reinterpret_cast<T*>(staging + (c - c0) * ROW_BYTES)[row_in_tile] =
+                                    from_f32<T>(silu_f32(gs) * us);
+                            }
+                            fence_proxy_async_smem();
+                            epilogue_bar_sync(128);
+                            for (int r = et; r < SUB; r += 128) {
+                                const int tok = c0 + r;
+                                if (tok >= nt) continue;
+                                const int64_t slot =
+                                    eid < 0 ? hrow0 + tok : p.slot_map[static_cast<int64_t>(eid) * p.n_tokens + tok];
+                                if (slot < 0) continue;
+                                bulk_store(static_cast<T*>(p.hid) + slot * p.f + m0, staging + r * ROW_BYTES,
+                                           static_cast<uint32_t>(ncols * sizeof(T)));
+                            }
+                            bulk_commit();
+                        }
+                    }
+                    if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+                    continue;
+                }
+            }
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += SUB) {
                 if (c0 > 0) {
@@ -1271,6 +1360,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 *ep_ok = ok ? 1 : 0;
             }
             if (sfu) sf_ready = true;
+            // two-phase shared units: this token's slot rows, read once per unit
+            // (all k loads in flight together)
+            constexpr int kPairBatch = 8;
+            constexpr int kPairMax = 2 * kPairBatch;  // >= kMaxTopK
+            int sls[kPairMax];
+#pragma unroll
+            for (int q2 = 0; q2 < kPairMax; ++q2)
+                sls[q2] = (sfu && two_phase && out_row >= 0 && q2 < p.k_pairs)
+                              ? __ldcg(p.pair_slot + out_row * p.k_pairs + q2)
+                              : -1;
             bulk_wait_read();  // this thread's previous copies are done reading its row
             epilogue_bar_sync(128);
             if (!*ep_ok) break;
@@ -1319,22 +1418,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     for (int c = 0; c < PASS; c += 16) {
                         float yv[16];
                         if (sfu && two_phase) {
-                            // the token's routed contributions, in choice order
+                            // the token's routed contributions, in choice order; the
+                            // loads of up to 8 slot rows are issued before any is used
 #pragma unroll
                             for (int j = 0; j < 16; ++j) yv[j] = 0.0f;
-                            if (out_row >= 0) {
-                                for (int q2 = 0; q2 < p.k_pairs; ++q2) {
-                                    const int sl = __ldcg(p.pair_slot + out_row * p.k_pairs + q2);
-                                    if (sl < 0) continue;
-                                    const uint4* src = reinterpret_cast<const uint4*>(
-                                        static_cast<const T*>(p.ys) + static_cast<int64_t>(sl) * p.h + n0 + c0 + c);
-                                    const uint4 v0 = __ldcg(src), v1 = __ldcg(src + 1);
-                                    const T* e0 = reinterpret_cast<const T*>(&v0);
-                                    const T* e1 = reinterpret_cast<const T*>(&v1);
 #pragma unroll
-                                    for (int j = 0; j < 8; ++j) {
-                                        yv[j] += to_f32<T>(e0[j]);
-                                        yv[8 + j] += to_f32<T>(e1[j]);
+                            for (int qb = 0; qb < kPairMax; qb += kPairBatch) {
+                                if (qb >= p.k_pairs) break;
+                                uint4 v[kPairBatch][2];
+#pragma unroll
+                                for (int j = 0; j < kPairBatch; ++j) {
+                                    if (sls[qb + j] >= 0) {
+                                        const uint4* src = reinterpret_cast<const uint4*>(
+                                            static_cast<const T*>(p.ys) + static_cast<int64_t>(sls[qb + j]) * p.h +
+                                            n0 + c0 + c);
+                                        v[j][0] = __ldcg(src);
+                                        v[j][1] = __ldcg(src + 1);
+                                    }
+                                }
+#pragma unroll
+                                for (int j = 0; j < kPairBatch; ++j) {
+                                    if (sls[qb + j] < 0) continue;
+                                    const T* e0 = reinterpret_cast<const T*>(&v[j][0]);
+                                    const T* e1 = reinterpret_cast<const T*>(&v[j][1]);
+#pragma unroll
+                                    for (int u = 0; u < 8; ++u) {
+                                        yv[u] += to_f32<T>(e0[u]);
+                                        yv[8 + u] += to_f32<T>(e1[u]);
                                     }
                                 }
                             }

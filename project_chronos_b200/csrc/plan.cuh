@@ -51,6 +51,9 @@ struct PlanParams {
     int32_t* ustart_dn;  // [A + 1]
     int32_t* tile_cnt;   // [n_tile_cnt] down output-tile counters (folded finalize), zeroed here; or null
     int n_tile_cnt;
+    int splits_gu;       // K splits of a routed gate/up tile (decode, dense mode); shared tiles whole
+    int32_t* gu_cnt;     // [n_gu_cnt] routed gate/up tile arrival counters, zeroed here; or null
+    int n_gu_cnt;
 };
 
 constexpr int kPlanThreads = 256;  // >= the 256 experts the ABI accepts: one expert per thread
@@ -95,7 +98,7 @@ __device__ __forceinline__ void plan_tables(const PlanParams& p, int cnt, int in
     const int is_act = (tid < E && cnt > 0) ? 1 : 0;
     const int tt = (cnt + p.tok_tile - 1) / p.tok_tile;
     const int tt_dn = (cnt + p.tok_tile_dn - 1) / p.tok_tile_dn;
-    const int ugu = is_act ? tt * p.mt_gu : 0;
+    const int ugu = is_act ? tt * p.mt_gu * (p.splits_gu > 1 ? p.splits_gu : 1) : 0;
     const int udn = is_act ? tt_dn * p.mt_dn * p.splits_dn : 0;
     const int inc_act = block_inclusive_scan<NT>(is_act, s_scratch);
     const int inc_gu = block_inclusive_scan<NT>(ugu, s_scratch);
@@ -127,6 +130,7 @@ __device__ __forceinline__ void plan_tables(const PlanParams& p, int cnt, int in
         }
     }
     for (int i = tid; i < p.n_tile_cnt; i += NT) p.tile_cnt[i] = 0;
+    for (int i = tid; i < p.n_gu_cnt; i += NT) p.gu_cnt[i] = 0;
     if (tid < S) {
         p.act_rows[tid] = N;
         p.act_xrow[tid] = 0;
@@ -248,38 +252,39 @@ __global__ void __launch_bounds__(kScatterThreads) plan_scatter_kernel(PlanParam
 constexpr int kSelectPlanThreads = kPlanThreads;
 constexpr int kSelectPlanWarps = kSelectPlanThreads / 32;
 constexpr int kSelectPlanMaxTokens = 64;
+constexpr int kSelectPlanWideThreads = 1024;   // one block, one warp per token, up to 32 tokens
 
-template <typename T, int EPL>
-__global__ void __launch_bounds__(kSelectPlanThreads)
+template <typename T, int EPL, int NT = kSelectPlanThreads>
+__global__ void __launch_bounds__(NT)
     route_select_plan_kernel(RouteParams rp, PlanParams pp, ScatterParams sp, int32_t* ticket) {
     __shared__ int s_off[kMaxExperts];
-    __shared__ int s_scratch[kSelectPlanWarps];
+    __shared__ int s_scratch[(NT / 32)];
     __shared__ int s_tot[4];
     __shared__ int s_last;
-    // one block (<= 8 tokens): group counts by shared-memory atomics and the
+    // one block (<= NT / 32 tokens): group counts by shared-memory atomics and the
     // per-(token, choice) results kept in shared memory, no ticket or re-reads
-    constexpr int kPairs = kSelectPlanWarps * kMaxTopK;
+    constexpr int kPairs = (NT / 32) * kMaxTopK;
     __shared__ int s_cnt[kMaxExperts];
     __shared__ int s_pe[kPairs];
     __shared__ int s_pp[kPairs];
     __shared__ float s_pc[kPairs];
-    __shared__ float s_sc[kSelectPlanWarps];
+    __shared__ float s_sc[(NT / 32)];
     const bool single = gridDim.x == 1;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t gtid = static_cast<int64_t>(blockIdx.x) * kSelectPlanThreads + tid;
-    const int64_t gthreads = static_cast<int64_t>(gridDim.x) * kSelectPlanThreads;
+    const int64_t gtid = static_cast<int64_t>(blockIdx.x) * NT + tid;
+    const int64_t gthreads = static_cast<int64_t>(gridDim.x) * NT;
     pdl_trigger();
     if (sp.slot_map != nullptr)
         for (int64_t i = gtid; i < static_cast<int64_t>(sp.e) * sp.n; i += gthreads) sp.slot_map[i] = -1;
     if (single) {
-        for (int i = tid; i < kMaxExperts; i += kSelectPlanThreads) s_cnt[i] = 0;
+        for (int i = tid; i < kMaxExperts; i += NT) s_cnt[i] = 0;
         __syncthreads();
     }
     pdl_wait();  // chunk partials and zeroed counters from the logit kernel
 
     // 1) one warp per token: select, position within the expert group
     const int k = rp.k;
-    const int64_t t = static_cast<int64_t>(blockIdx.x) * kSelectPlanWarps + warp;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * (NT / 32) + warp;
     if (t < rp.n) {
         if (rp.y_acc != nullptr) {
             float4* yv = reinterpret_cast<float4*>(rp.y_acc + t * rp.h);
@@ -319,14 +324,14 @@ __global__ void __launch_bounds__(kSelectPlanThreads)
 
     // 3) plan: group offsets and the GEMM work tables
     const int cnt = tid < pp.e ? (single ? s_cnt[tid] : __ldcg(rp.grp_count + tid)) : 0;
-    const int inc = block_inclusive_scan<kSelectPlanThreads>(cnt, s_scratch);
+    const int inc = block_inclusive_scan<NT>(cnt, s_scratch);
     if (tid < pp.e) s_off[tid] = inc - cnt;
-    plan_tables<kSelectPlanThreads>(pp, cnt, inc, s_scratch, s_tot);
+    plan_tables<NT>(pp, cnt, inc, s_scratch, s_tot);
     __syncthreads();
 
     // 4) slot tables, one thread per (token, choice)
     const int64_t total = rp.n * k;
-    for (int64_t i = tid; i < total; i += kSelectPlanThreads) {
+    for (int64_t i = tid; i < total; i += NT) {
         const int64_t tt = i / k;
         const int j = static_cast<int>(i % k);
         const int ps = single ? s_pp[i] : __ldcg(rp.pos + i);

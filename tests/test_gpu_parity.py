@@ -397,3 +397,34 @@ def test_folded_finalize_matches_finalize_kernel(n):
         assert O.rel_l2(y, outs[0]) <= 1e-3
     emu, idx, _, _ = _oracle(wl, 4, True, avail=avail, emulate=True)
     assert O.rel_l2(outs[-1], emu) <= 3e-3
+
+
+@pytest.mark.parametrize("h,e,k,f,s,n", [
+    (2048, 64, 6, 1408, 2, 1),    # the DeepSeek-MoE-16B decode shape, one token: 2-way split
+    (2048, 64, 6, 512, 2, 1),     # few weight-row tiles: 4-way split
+    (2048, 64, 6, 1408, 2, 2),
+    (1024, 16, 2, 2048, 1, 1),
+])
+def test_gateup_k_split_matches_unsplit(h, e, k, f, s, n):
+    """Decode calls whose gate/up units would not cover the SMs split the routed
+    units along K; the split completing a tile sums the fp32 partials in split
+    order.  Against the unsplit path, the oracle, and itself on consecutive calls
+    (the tile counters are re-armed by every call's plan; the down GEMM's fp32
+    reduce-adds land in any order, so repeated calls agree to rounding, not bitwise)."""
+    ops = _ops()
+    wl = _workload(h, e, k, f, s, n, seed=n + f, avail_p=0.8)
+    avail = wl.mask.to(torch.float32)
+    outs = []
+    try:
+        for split in (1, 1, 0):
+            ops.set_option("gateup_split", split)
+            outs.append(_np(_run(wl, k, True, avail=avail)["y"]))
+            torch.cuda.synchronize()
+            ops.check_status()
+    finally:
+        ops.set_option("gateup_split", 0)
+    split, split_again, whole = outs
+    assert O.rel_l2(split_again, split) <= 1e-3
+    assert O.rel_l2(split, whole) <= 1e-3
+    emu, *_ = _oracle(wl, k, True, avail=avail, emulate=True)
+    assert O.rel_l2(split, emu) <= 3e-3
