@@ -42,15 +42,22 @@ typedef struct ChronosEpDispatchArgs {
     int32_t num_chunks;        /* C >= 1 dividing E/G: each rank's local experts split into C
                                   chunks of E/(G*C); send rows ordered by (expert chunk,
                                   destination rank); C * G <= CHRONOS_EP_MAX_RANKS */
+    int32_t meta_pairs;        /* 0 or 1: one send row per available selection, send_meta
+                                  [rows, 2]; P >= min(k, E/G) (C = 1): deduplicated, one
+                                  send row per (token, destination rank), send_meta
+                                  [rows, P, 2] = that rank's available selections of the
+                                  token in choice order, padded with (-1, 0.0f) */
     const void* x;             /* [N, H] */
     const int32_t* topk_idx;   /* [N, k] global expert ids (chronos_moe_route) */
     const float* topk_weight;  /* [N, k] */
     const float* avail;        /* [E] availability a_e in [0, 1], or NULL for all 1 */
     int32_t* send_counts;      /* [C, G] out: selections of each expert chunk sent to each rank */
     void* send_x;              /* [N*k, H] out: x rows grouped by destination rank */
-    int32_t* send_meta;        /* [N*k, 2] out: (expert id local to the destination rank,
-                                  fp32 bits of w * a) per send row */
-    int32_t* pair_slot;        /* [N*k] out: send row of selection (t, j), -1 when a = 0 */
+    int32_t* send_meta;        /* [N*k, P or 1, 2] out: (expert id local to the destination
+                                  rank, fp32 bits of w * a) per send row and selection */
+    int32_t* pair_slot;        /* [N*k] out: send row of selection (t, j), -1 when a = 0 (and,
+                                  deduplicated, for all but the token's first selection on
+                                  each rank) */
     float* shared_weight;      /* [N, k] out: w * (1 - a), the shared experts' share */
     int32_t* scratch;          /* [N*k] int32 scratch */
 } ChronosEpDispatchArgs;
@@ -60,7 +67,11 @@ typedef struct ChronosEpDispatchArgs {
  * rank 0, ...), so each chunk's rows form one contiguous all-to-all send
  * buffer and a receiver can run each chunk's experts as soon as it lands
  * (reading each expert's weights once); within a group the row order is
- * unspecified.  Selections with a_e = 0 are not sent. */
+ * unspecified.  Selections with a_e = 0 are not sent.  Deduplicated
+ * (meta_pairs > 1), a token's selections on one rank share one row, so the
+ * exchange carries each x row at most once per destination and the
+ * receiver runs its experts on the row with top_k = P (pre-routed, padding
+ * selections skipped). */
 CHRONOS_API int chronos_ep_dispatch(const ChronosEpDispatchArgs* args, void* cuda_stream);
 
 typedef struct ChronosEpCombineArgs {

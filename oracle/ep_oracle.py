@@ -13,7 +13,10 @@ same arguments and results as ``project_chronos_b200.ops``:
 * ``ep_dispatch`` — include/chronos_ep.h: rows grouped by (expert chunk, destination rank),
   metadata (local expert, w*a), ``pair_slot``, shared share w*(1-a); inside a
   rank this restatement orders rows by (token, choice), the kernel's order is
-  unspecified and nothing downstream depends on it;
+  unspecified and nothing downstream depends on it.  ``dedup``: one row per
+  (token, destination rank), opened by the token's first available selection
+  there, metadata [P, 2] = that rank's selections in choice order, padded with
+  (-1, 0.0);
 * ``moe_forward`` — the blended layer (``moe_oracle.moe_forward``) on pre-routed
   selections, with ``slot_of_expert < 0`` meaning a = 0;
 * ``ep_combine``  — y_t = y_shared_t + sum_j rows[pair_slot(t, j)].
@@ -46,7 +49,7 @@ class CpuEpBackend:
                     probs=torch.from_numpy(probs) if want_probs else None, counts=None, mass=None)
 
     @staticmethod
-    def ep_dispatch(x, topk_idx, topk_weight, num_experts, world_size, avail=None, num_chunks=1):
+    def ep_dispatch(x, topk_idx, topk_weight, num_experts, world_size, avail=None, num_chunks=1, dedup=False):
         xn = x.detach()
         idx = topk_idx.to(torch.int64).numpy()
         wt = topk_weight.to(torch.float32).numpy()
@@ -59,11 +62,21 @@ class CpuEpBackend:
         num_chunks = max(1, int(num_chunks))
         dest = idx // epr
         key = ((idx % epr) // (epr // num_chunks)) * world_size + dest
+        pairs = min(k, epr) if dedup and num_chunks == 1 else 1
         sent = a > 0
+        if pairs > 1:   # only a token's first available selection on each rank opens a row
+            for t in range(n):
+                seen = set()
+                for j in range(k):
+                    if sent[t, j]:
+                        if dest[t, j] in seen:
+                            sent[t, j] = False
+                        seen.add(dest[t, j])
         counts = np.array([int(np.sum(sent & (key == q))) for q in range(num_chunks * world_size)], np.int32)
         offs = np.concatenate([[0], np.cumsum(counts)[:-1]]).astype(np.int64)
         send_x = torch.zeros(n * k, xn.shape[1], dtype=xn.dtype)
-        meta = np.zeros((n * k, 2), np.int32)
+        meta = np.zeros((n * k, pairs, 2), np.int32)
+        meta[:, :, 0] = -1
         pair_slot = np.full(n * k, -1, np.int32)
         fill = offs.copy()
         for i in range(n * k):                       # (token, choice) order inside a rank
@@ -76,11 +89,13 @@ class CpuEpBackend:
             fill[q] += 1
             pair_slot[i] = s
             send_x[s] = xn[t]
-            meta[s, 0] = idx[t, j] - g * epr
-            meta[s, 1] = np.float32(wt[t, j] * a[t, j]).view(np.int32)
+            picks = [jj for jj in range(j, k) if a[t, jj] > 0 and dest[t, jj] == g] if pairs > 1 else [j]
+            for qq, jj in enumerate(picks):
+                meta[s, qq, 0] = idx[t, jj] - g * epr
+                meta[s, qq, 1] = np.float32(wt[t, jj] * a[t, jj]).view(np.int32)
         return dict(send_counts=torch.from_numpy(counts).view(num_chunks, world_size), send_x=send_x,
                     send_meta=torch.from_numpy(meta), pair_slot=torch.from_numpy(pair_slot),
-                    shared_weight=torch.from_numpy(shared_w))
+                    shared_weight=torch.from_numpy(shared_w), pairs=pairs)
 
     @staticmethod
     def moe_forward(x, router_w, w_gate, w_up, w_down, sh_gate, sh_up, sh_down, top_k, norm_topk,
@@ -92,7 +107,12 @@ class CpuEpBackend:
         if slot_of_expert is not None:
             a = np.where(slot_of_expert.cpu().numpy() < 0, np.float32(0.0), a).astype(np.float32)
         if topk is not None:
-            route_out = (topk[0].to(torch.int32).numpy(), topk[1].to(torch.float32).numpy(), None)
+            # padding selections (expert -1) contribute nothing: weight 0 on expert 0
+            ti = topk[0].to(torch.int32).numpy().copy()
+            tw = topk[1].to(torch.float32).numpy().copy()
+            tw[ti < 0] = 0.0
+            ti[ti < 0] = 0
+            route_out = (ti, tw, None)
         else:
             idx, wt, probs, _l = O.route(xn, _np(router_w), int(top_k), bool(norm_topk), _np(router_bias))
             route_out = (idx, wt, probs)

@@ -112,6 +112,7 @@ class ChronosEpDispatchArgs(ctypes.Structure):
         ("world_size", ctypes.c_int32),
         ("dtype", ctypes.c_int32),
         ("num_chunks", ctypes.c_int32),
+        ("meta_pairs", ctypes.c_int32),
         ("x", ctypes.c_void_p),
         ("topk_idx", ctypes.c_void_p),
         ("topk_weight", ctypes.c_void_p),

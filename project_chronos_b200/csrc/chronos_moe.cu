@@ -1232,6 +1232,7 @@ int ep_dispatch_impl(const ChronosEpDispatchArgs* a, cudaStream_t st) {
     const int chunks = a->num_chunks < 1 ? 1 : a->num_chunks;
     p.chunks = chunks;
     p.chunk_experts = p.epr / chunks;
+    p.pairs = a->meta_pairs > 1 ? a->meta_pairs : 1;
     p.topk_idx = a->topk_idx;
     p.topk_w = a->topk_weight;
     p.avail = a->avail;
@@ -1287,6 +1288,12 @@ extern "C" int chronos_ep_dispatch(const ChronosEpDispatchArgs* a, void* stream)
     if ((a->num_experts / a->world_size) % (a->num_chunks < 1 ? 1 : a->num_chunks) != 0)
         return fail(CHRONOS_ERR_INVALID_ARG, "num_chunks %d does not divide the %d experts of a rank",
                     a->num_chunks, a->num_experts / a->world_size);
+    if (a->meta_pairs > 1 &&
+        (a->num_chunks > 1 || a->meta_pairs > kMaxTopKEp ||
+         a->meta_pairs < std::min(a->top_k, a->num_experts / a->world_size)))
+        return fail(CHRONOS_ERR_INVALID_ARG, "meta_pairs %d: deduplicated rows need one expert chunk and "
+                    "min(top_k %d, experts per rank %d) <= meta_pairs <= %d", a->meta_pairs, a->top_k,
+                    a->num_experts / a->world_size, kMaxTopKEp);
     if (a->send_counts == nullptr) return fail(CHRONOS_ERR_INVALID_ARG, "send_counts is required");
     if (a->num_tokens > 0 &&
         (a->x == nullptr || a->topk_idx == nullptr || a->topk_weight == nullptr || a->send_x == nullptr ||

@@ -11,6 +11,12 @@
 //                    counts + position; metadata (local expert, w*a) and the x
 //                    row copied with 16-byte vectors, every load of a lane
 //                    issued before its stores.
+// With `pairs` > 1 (one expert chunk) the rows are deduplicated: one send row
+// per (token, destination rank), opened by the token's first available
+// selection on that rank, its metadata [pairs][2] listing every available
+// selection of the token on that rank in choice order (padding: expert -1);
+// the other selections' pair_slot is -1, their contribution comes back in the
+// opening selection's row.
 // ep_combine_kernel folds the returned rows back: one block per token,
 // y_t = y_shared_t + sum_j recv[pair_slot(t, j)] in fp32, j ascending, so the
 // result does not depend on the (atomic) order of rows inside a rank.
@@ -31,6 +37,8 @@ struct EpParams {
     int h, e, k, g, epr;
     int chunks;             // expert chunks per rank (1: unchunked)
     int chunk_experts;      // local experts per chunk (epr / chunks)
+    int pairs;              // > 1: one send row per (token, destination rank) carrying up to
+                            // `pairs` selections (deduplicated); 1: one row per selection
     const int32_t* topk_idx;
     const float* topk_w;
     const float* avail;
@@ -49,6 +57,18 @@ __device__ __forceinline__ float ep_avail(const EpParams& p, int e) {
     return a > 1.0f ? 1.0f : (a > 0.0f ? a : 0.0f);
 }
 
+// Deduplicated dispatch: selection j of token t opens the send row of its
+// destination rank when it is the token's first available selection bound
+// for that rank (the rank's other selections of the token ride in that row's
+// metadata).
+__device__ __forceinline__ bool ep_first_for_rank(const EpParams& p, int64_t t, int j, int dest) {
+    for (int q = 0; q < j; ++q) {
+        const int eq = p.topk_idx[t * p.k + q];
+        if (ep_avail(p, eq) > 0.0f && eq / p.epr == dest) return false;
+    }
+    return true;
+}
+
 __global__ void __launch_bounds__(kEpPackThreads) ep_count_kernel(EpParams p) {
     pdl_trigger();
     const int64_t i = static_cast<int64_t>(blockIdx.x) * kEpPackThreads + threadIdx.x;
@@ -57,8 +77,10 @@ __global__ void __launch_bounds__(kEpPackThreads) ep_count_kernel(EpParams p) {
     const float w = p.topk_w[i];
     const float a = ep_avail(p, e);
     p.shared_w[i] = w * (1.0f - a);
-    const int key = a > 0.0f ? ((e % p.epr) / p.chunk_experts) * p.g + e / p.epr : 0;
-    p.pos[i] = a > 0.0f ? atomicAdd(&p.counts[key], 1) : -1;
+    bool opens = a > 0.0f;
+    if (opens && p.pairs > 1) opens = ep_first_for_rank(p, i / p.k, static_cast<int>(i % p.k), e / p.epr);
+    const int key = opens ? ((e % p.epr) / p.chunk_experts) * p.g + e / p.epr : 0;
+    p.pos[i] = opens ? atomicAdd(&p.counts[key], 1) : -1;
 }
 
 template <typename T>
@@ -89,12 +111,31 @@ __global__ void __launch_bounds__(kEpPackThreads) ep_pack_kernel(EpParams p) {
     const int dest = e / p.epr;
     const int key = ((e % p.epr) / p.chunk_experts) * p.g + dest;
     const int64_t slot = static_cast<int64_t>(s_off[key]) + ps;
+    const int64_t t = gw / p.k;
     if (lane == 0) {
         p.pair_slot[gw] = static_cast<int32_t>(slot);
-        p.send_meta[2 * slot] = e - dest * p.epr;
-        p.send_meta[2 * slot + 1] = __float_as_int(p.topk_w[gw] * ep_avail(p, e));
+        if (p.pairs > 1) {
+            // the token's available selections on this rank, in choice order, padded
+            int32_t* m = p.send_meta + 2 * slot * p.pairs;
+            int q = 0;
+            for (int j = static_cast<int>(gw % p.k); j < p.k && q < p.pairs; ++j) {
+                const int ej = p.topk_idx[t * p.k + j];
+                const float aj = ep_avail(p, ej);
+                if (aj > 0.0f && ej / p.epr == dest) {
+                    m[2 * q] = ej - dest * p.epr;
+                    m[2 * q + 1] = __float_as_int(p.topk_w[t * p.k + j] * aj);
+                    ++q;
+                }
+            }
+            for (; q < p.pairs; ++q) {
+                m[2 * q] = -1;
+                m[2 * q + 1] = __float_as_int(0.0f);
+            }
+        } else {
+            p.send_meta[2 * slot] = e - dest * p.epr;
+            p.send_meta[2 * slot + 1] = __float_as_int(p.topk_w[gw] * ep_avail(p, e));
+        }
     }
-    const int64_t t = gw / p.k;
     const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.x) + t * p.h);
     uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.send_x) + slot * p.h);
     const int n16 = p.h * static_cast<int>(sizeof(T)) / 16;

@@ -343,6 +343,7 @@ __global__ void __launch_bounds__(kTiledThreads, 2) route_tiled_kernel(RoutePara
 constexpr int kSelectThreads = 512;
 
 __device__ __forceinline__ float expert_avail(const RouteParams& p, int e) {
+    if (e < 0 || e >= p.e) return 0.0f;  // a padding selection of a pre-routed row
     float a = p.avail ? p.avail[e] : 1.0f;
     if (p.avail_mask) a = a > 0.0f ? 1.0f : 0.0f;
     if (p.slot_of_expert && p.slot_of_expert[e] < 0) a = 0.0f;

@@ -79,6 +79,9 @@ class ExpertParallelMoE(nn.Module):
         # the CTAs the expert GEMMs may use while chunks are exchanged beside them
         self.chunks = 1
         self.gemm_ctas = 132
+        # unchunked exchange: one row per (token, destination rank), every selection of
+        # the token on that rank in the row's metadata (False: one row per selection)
+        self.dedup = True
         # optional phase timing: a list that each forward appends
         # {phase: torch.cuda.Event} to (events on the compute stream)
         self.phase_events = None
@@ -164,7 +167,11 @@ class ExpertParallelMoE(nn.Module):
                 if self.experts_per_rank % c == 0)
         # with chunks, the exchange runs beside the expert GEMMs: leave it SMs
         max_ctas = 0 if C == 1 else self.gemm_ctas
-        d = be.ep_dispatch(xf, r["topk_idx"], r["topk_weight"], E, G, avail=avail, num_chunks=C)
+        # one row per (token, destination rank) when unchunked: each x row crosses
+        # to a rank once, carrying all of the token's selections there
+        d = be.ep_dispatch(xf, r["topk_idx"], r["topk_weight"], E, G, avail=avail, num_chunks=C,
+                           dedup=self.dedup)
+        P = int(d.get("pairs", 1))
 
         mark("dispatched")
         # 3: counts [C, G] -> per destination [G, C]; one host sync for every split size
@@ -186,7 +193,7 @@ class ExpertParallelMoE(nn.Module):
         for c in range(C):
             lo, hi = send_off[c], send_off[c + 1]
             rx = torch.empty(sum(rc[c]), H, dtype=dt, device=dev)
-            rm = torch.empty(sum(rc[c]), 2, dtype=torch.int32, device=dev)
+            rm = torch.empty(sum(rc[c]), P, 2, dtype=torch.int32, device=dev)
             works.append((self._exchange(rx, d["send_x"][lo:hi], rc[c], sc[c], async_op=True),
                           self._exchange(rm, d["send_meta"][lo:hi], rc[c], sc[c], async_op=True)))
             recv_x.append(rx)
@@ -215,10 +222,10 @@ class ExpertParallelMoE(nn.Module):
             if c == 0:
                 mark("rows_arrived")
             rm = recv_meta[c]
-            eid = rm[:, 0:1].contiguous()
-            wgt = rm[:, 1:2].contiguous().view(torch.float32)
+            eid = rm[:, :, 0].contiguous()                      # [rows, P], -1 = padding
+            wgt = rm[:, :, 1].contiguous().view(torch.float32)  # [rows, P] w * a
             y_loc = be.moe_forward(recv_x[c], local_router, self.w_gate, self.w_up, self.w_down, None,
-                                   None, None, 1, False, want_probs=False, topk=[eid, wgt],
+                                   None, None, P, False, want_probs=False, topk=[eid, wgt],
                                    max_ctas=max_ctas)["y"]
             back_works.append(self._exchange(back[send_off[c]:send_off[c + 1]], y_loc, sc[c], rc[c],
                                              async_op=True))

@@ -336,14 +336,17 @@ def moe_route(x: torch.Tensor, router_w: torch.Tensor, top_k: int, norm_topk: bo
 
 
 def ep_dispatch(x: torch.Tensor, topk_idx: torch.Tensor, topk_weight: torch.Tensor, num_experts: int,
-                world_size: int, avail: Optional[torch.Tensor] = None, num_chunks: int = 1) -> dict:
+                world_size: int, avail: Optional[torch.Tensor] = None, num_chunks: int = 1,
+                dedup: bool = False) -> dict:
     """Send buffers of one rank for expert parallelism (include/chronos_ep.h).
 
     Rows are ordered by (expert chunk, destination rank): each rank's E/G local
     experts split into ``num_chunks`` chunks (which must divide E/G).
-    Returns dict(send_counts [C, G] int32, send_x [N*k, H], send_meta [N*k, 2] int32
+    Returns dict(send_counts [C, G] int32, send_x [N*k, H], send_meta [N*k, P, 2] int32
     (local expert id, fp32 bits of w*a), pair_slot [N*k] int32, shared_weight [N, k]
-    fp32); the first ``send_counts.sum()`` rows of the send buffers are used."""
+    fp32, pairs P); the first ``send_counts.sum()`` rows of the send buffers are used.
+    ``dedup`` (one chunk): one row per (token, destination rank), P = min(k, E/G)
+    selections per row (padding: expert -1); else one row per selection, P = 1."""
     _check_cuda(x, topk_idx, topk_weight, avail)
     x = x.contiguous()
     n, h = x.shape
@@ -355,15 +358,16 @@ def ep_dispatch(x: torch.Tensor, topk_idx: torch.Tensor, topk_weight: torch.Tens
     topk_weight = topk_weight.to(torch.float32).contiguous()
     av = None if avail is None else avail.to(device=dev, dtype=torch.float32).contiguous()
     num_chunks = max(1, int(num_chunks))
+    pairs = min(k, int(num_experts) // int(world_size)) if dedup and num_chunks == 1 else 1
     out = dict(send_counts=torch.empty(num_chunks, world_size, dtype=torch.int32, device=dev),
                send_x=torch.empty(n * k, h, dtype=x.dtype, device=dev),
-               send_meta=torch.empty(n * k, 2, dtype=torch.int32, device=dev),
+               send_meta=torch.empty(n * k, pairs, 2, dtype=torch.int32, device=dev),
                pair_slot=torch.empty(n * k, dtype=torch.int32, device=dev),
                shared_weight=torch.empty(n, k, dtype=torch.float32, device=dev))
     scratch = torch.empty(max(n * k, 1), dtype=torch.int32, device=dev)
     args = N.ChronosEpDispatchArgs(
         num_tokens=n, hidden=h, num_experts=int(num_experts), top_k=k, world_size=int(world_size),
-        dtype=_DTYPES[x.dtype], num_chunks=num_chunks, x=_ptr(x), topk_idx=_ptr(topk_idx), topk_weight=_ptr(topk_weight),
+        dtype=_DTYPES[x.dtype], num_chunks=num_chunks, meta_pairs=pairs if pairs > 1 else 0, x=_ptr(x), topk_idx=_ptr(topk_idx), topk_weight=_ptr(topk_weight),
         avail=_ptr(av), send_counts=_ptr(out["send_counts"]), send_x=_ptr(out["send_x"]),
         send_meta=_ptr(out["send_meta"]),
         pair_slot=_ptr(out["pair_slot"]), shared_weight=_ptr(out["shared_weight"]),
@@ -372,6 +376,7 @@ def ep_dispatch(x: torch.Tensor, topk_idx: torch.Tensor, topk_weight: torch.Tens
     stream = torch.cuda.current_stream(dev).cuda_stream
     with torch.cuda.device(dev):
         N.check(lib.chronos_ep_dispatch(ctypes.byref(args), ctypes.c_void_p(stream)))
+    out["pairs"] = pairs
     return out
 
 

@@ -27,9 +27,12 @@ def _route(x, router, k):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("world,n,chunks", [(1, 7, 1), (2, 33, 1), (4, 300, 1), (8, 1, 1), (2, 33, 4),
-                                            (8, 300, 2), (4, 5, 4), (1, 40, 16)])
-def test_dispatch_and_combine_match_oracle(dtype, world, n, chunks):
+@pytest.mark.parametrize("world,n,chunks,dedup", [(1, 7, 1, False), (2, 33, 1, False), (4, 300, 1, False),
+                                                  (8, 1, 1, False), (2, 33, 4, False), (8, 300, 2, False),
+                                                  (4, 5, 4, False), (1, 40, 16, False), (1, 7, 1, True),
+                                                  (2, 33, 1, True), (4, 300, 1, True), (8, 300, 1, True),
+                                                  (16, 64, 1, True)])
+def test_dispatch_and_combine_match_oracle(dtype, world, n, chunks, dedup):
     from oracle.ep_oracle import CpuEpBackend
     from project_chronos_b200 import ops
     E, k, H = 16, 4, 256
@@ -39,9 +42,11 @@ def test_dispatch_and_combine_match_oracle(dtype, world, n, chunks):
     avail = (torch.rand(E, generator=g) > 0.25).float()
     avail[3] = 0.5
     r = _route(x, router, k)
-    d = ops.ep_dispatch(x, r["topk_idx"], r["topk_weight"], E, world, avail=avail.to(DEV), num_chunks=chunks)
+    d = ops.ep_dispatch(x, r["topk_idx"], r["topk_weight"], E, world, avail=avail.to(DEV), num_chunks=chunks,
+                        dedup=dedup)
     ref = CpuEpBackend.ep_dispatch(x.cpu(), r["topk_idx"].cpu(), r["topk_weight"].cpu(), E, world, avail,
-                                   num_chunks=chunks)
+                                   num_chunks=chunks, dedup=dedup)
+    assert d["pairs"] == ref["pairs"] == (min(k, E // world) if dedup else 1)
     assert d["send_counts"].cpu().tolist() == ref["send_counts"].tolist()
     assert torch.equal(d["shared_weight"].cpu(), ref["shared_weight"])
     ps = d["pair_slot"].cpu()
