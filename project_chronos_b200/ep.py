@@ -36,6 +36,8 @@ with CPU stand-ins in tests.
 """
 from __future__ import annotations
 
+import contextlib
+
 from typing import Optional
 
 import torch
@@ -85,6 +87,15 @@ class ExpertParallelMoE(nn.Module):
         # optional phase timing: a list that each forward appends
         # {phase: torch.cuda.Event} to (events on the compute stream)
         self.phase_events = None
+
+    def _side_stream(self, dev) -> torch.cuda.Stream:
+        """One side stream per device for the shared experts' term."""
+        streams = self.__dict__.setdefault("_side_streams", {})
+        st = streams.get(dev.index)
+        if st is None:
+            st = torch.cuda.Stream(device=dev)
+            streams[dev.index] = st
+        return st
 
     @classmethod
     def from_stacked(cls, config, router: torch.Tensor, gate: torch.Tensor, up: torch.Tensor,
@@ -174,6 +185,24 @@ class ExpertParallelMoE(nn.Module):
         P = int(d.get("pairs", 1))
 
         mark("dispatched")
+        # the shared experts' term needs only the routing: on a CUDA device it runs on a
+        # side stream from here, so the GPU has work while the host waits for the split
+        # sizes below (the row exchange still overlaps it, as before)
+        y_shared = None
+        side = None
+        if self.num_shared:
+            cur = torch.cuda.current_stream(dev) if xf.is_cuda else None
+            if cur is not None:
+                side = self._side_stream(dev)
+                side.wait_stream(cur)
+            with (torch.cuda.stream(side) if side is not None else contextlib.nullcontext()):
+                no_slot = torch.full((E,), -1, dtype=torch.int32, device=dev)
+                y_shared = be.moe_forward(
+                    xf, self.router, self.w_gate, self.w_up, self.w_down, self.sh_gate, self.sh_up,
+                    self.sh_down, k, self.norm_topk_prob, avail=torch.zeros(E, dtype=torch.float32, device=dev),
+                    slot_of_expert=no_slot, want_probs=False,
+                    topk=[r["topk_idx"], d["shared_weight"]])["y"]
+                mark("shared_done")
         # 3: counts [C, G] -> per destination [G, C]; one host sync for every split size
         send_gc = d["send_counts"].reshape(C, G).t().contiguous()
         recv_gc = torch.empty_like(send_gc)
@@ -200,21 +229,12 @@ class ExpertParallelMoE(nn.Module):
             recv_meta.append(rm)
 
         mark("counts_exchanged")
-        y_shared = None
-        if self.num_shared:
-            no_slot = torch.full((E,), -1, dtype=torch.int32, device=dev)
-            y_shared = be.moe_forward(
-                xf, self.router, self.w_gate, self.w_up, self.w_down, self.sh_gate, self.sh_up,
-                self.sh_down, k, self.norm_topk_prob, avail=torch.zeros(E, dtype=torch.float32, device=dev),
-                slot_of_expert=no_slot, want_probs=False,
-                topk=[r["topk_idx"], d["shared_weight"]])["y"]
 
         # 4-5: per expert chunk, as it lands: its experts on its rows, rows sent back
         # (the return of chunk c overlaps the experts of chunk c + 1)
         local_router = torch.empty(self.experts_per_rank, H, dtype=dt, device=dev)
         back = torch.empty(n_send, H, dtype=dt, device=dev)
         back_works = []
-        mark("shared_done")
         for c in range(C):
             for w in works[c]:
                 if w is not None:
@@ -236,6 +256,10 @@ class ExpertParallelMoE(nn.Module):
         mark("rows_returned")
 
         # 6: fold the returned rows and the shared term
+        if side is not None:
+            cur = torch.cuda.current_stream(dev)
+            cur.wait_stream(side)
+            y_shared.record_stream(cur)
         y = be.ep_combine(back, d["pair_slot"], k, y_shared=y_shared, num_tokens=xf.shape[0])
         mark("combined")
         if marks is not None:
