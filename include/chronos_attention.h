@@ -91,6 +91,8 @@ typedef struct ChronosNormArgs {
     int32_t width;        /* <= 16384 */
     int32_t dtype;
     float eps;
+    int32_t x_fp32;       /* 1: x is fp32 (e.g. a layer's fp32 accumulator, CHRONOS_FLAG_ACC_OUT),
+                             rounded to dtype as it is read; 0: x is dtype */
     const void* x;        /* [rows, width] */
     const void* residual; /* [rows, width] added to x first, or NULL */
     void* sum_out;        /* x + residual (rounded), or NULL; may alias x or residual */

@@ -70,6 +70,11 @@ extern "C" {
 /* avail is a residency mask: a_e = 1 where avail[e] > 0, else 0 (the caller's
  * mask passed as it is, no thresholding pass before the call). */
 #define CHRONOS_FLAG_AVAIL_MASK 0x2
+/* y is an fp32 [N, H] buffer (16-byte aligned) that receives the layer's fp32
+ * accumulator itself: no rounding to the layer dtype, no finalize pass.  For a
+ * caller whose next kernel reads the output anyway (a residual add + RMSNorm
+ * that rounds it to the layer dtype first, chronos_add_rmsnorm's x_fp32). */
+#define CHRONOS_FLAG_ACC_OUT 0x4
 
 typedef struct ChronosMoeShape {
     int64_t num_tokens;  /* N = B*S (x.view(-1, H), moe_chronos.py:110-111); 0 is allowed */

@@ -37,6 +37,7 @@ DTYPE_FP32 = 2
 
 FLAG_PREROUTED = 0x1
 FLAG_AVAIL_MASK = 0x2
+FLAG_ACC_OUT = 0x4
 
 ABI_VERSION = 2
 
@@ -193,6 +194,7 @@ class ChronosNormArgs(ctypes.Structure):
         ("width", ctypes.c_int32),
         ("dtype", ctypes.c_int32),
         ("eps", ctypes.c_float),
+        ("x_fp32", ctypes.c_int32),
         ("x", ctypes.c_void_p),
         ("residual", ctypes.c_void_p),
         ("sum_out", ctypes.c_void_p),

@@ -47,6 +47,7 @@ struct NormParams {
     int64_t rows;
     int width;
     float eps;
+    int x_fp32;  // 1: x is fp32, rounded to T as read
     const void* x;
     const void* residual;
     void* sum_out;
@@ -105,7 +106,7 @@ __global__ void __launch_bounds__(kAttnThreads) add_rmsnorm_kernel(NormParams p)
         const int64_t base = r * p.width;
         float ss = 0.0f;
         for (int c = threadIdx.x; c < p.width; c += kAttnThreads) {
-            float v = to_f32<T>(x[base + c]);
+            float v = p.x_fp32 ? round_to<T>(static_cast<const float*>(p.x)[base + c]) : to_f32<T>(x[base + c]);
             if (res != nullptr) v = round_to<T>(v + to_f32<T>(res[base + c]));
             if (sum_out != nullptr) sum_out[base + c] = from_f32<T>(v);
             xs[c] = v;
@@ -144,7 +145,13 @@ __global__ void __launch_bounds__(kAttnThreads) add_rmsnorm_warp_kernel(NormPara
         const int c8 = lane + 32 * i;
         if (c8 < nv) {
             load8<T>(w + c8 * 8, wv[i]);   // issued with the row's loads, used after the sum
-            load8<T>(x + c8 * 8, v[i]);
+            if (p.x_fp32) {
+                load8<float>(static_cast<const float*>(p.x) + base + c8 * 8, v[i]);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[i][u] = round_to<T>(v[i][u]);
+            } else {
+                load8<T>(x + c8 * 8, v[i]);
+            }
             if (res != nullptr) {
                 float rr[8];
                 load8<T>(res + c8 * 8, rr);

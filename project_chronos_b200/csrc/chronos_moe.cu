@@ -382,8 +382,10 @@ int set_smem(K kernel, int bytes) {
 struct Ptrs {
     uint8_t* ws;
     const Layout* L;
+    float* acc_out = nullptr;  // the caller's fp32 output as the accumulator (CHRONOS_FLAG_ACC_OUT)
     template <typename P>
     P* at(size_t off) const { return reinterpret_cast<P*>(ws + off); }
+    float* y_acc() const { return acc_out != nullptr ? acc_out : at<float>(L->y_acc); }
 };
 
 // ---------------------------------------------------------------------------
@@ -419,7 +421,7 @@ RouteParams route_params(const ChronosMoeArgs* a, const Ptrs& w, bool prerouted,
     rp.pos = w.at<int32_t>(w.L->pos);
     rp.sel_coef = w.at<float>(w.L->sel_coef);
     rp.shared_coef = w.at<float>(w.L->shared_coef);
-    rp.y_acc = (zero_acc && y_direct == nullptr) ? w.at<float>(w.L->y_acc) : nullptr;
+    rp.y_acc = (zero_acc && y_direct == nullptr) ? w.y_acc() : nullptr;
     rp.y_direct = y_direct;
     rp.partials = w.at<float>(w.L->partials);
     rp.nchunks = route_chunks(s.hidden);
@@ -641,7 +643,7 @@ int launch_tc_pair(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int 
     p.f = static_cast<int>(F);
     p.h = static_cast<int>(H);
     p.hid = w.ws + w.L->hid;
-    p.y_acc = w.at<float>(w.L->y_acc);
+    p.y_acc = w.y_acc();
     p.slot_tok = w.at<int32_t>(w.L->slot_tok);
     p.slot_coef = w.at<float>(w.L->slot_coef);
     p.ready_flags = a->ready_flags;
@@ -737,7 +739,7 @@ int launch_simt(const ChronosMoeArgs* a, const Ptrs& w, cudaStream_t st, int slo
     p.x = a->x;
     p.hid_in = w.ws + w.L->hid;
     p.hid_out = w.ws + w.L->hid;
-    p.y_acc = w.at<float>(w.L->y_acc);
+    p.y_acc = w.y_acc();
     p.slot_tok = w.at<int32_t>(w.L->slot_tok);
     p.slot_coef = w.at<float>(w.L->slot_coef);
     p.ready_flags = a->ready_flags;
@@ -874,7 +876,14 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     // one contribution per token (k = 1, no shared experts, e.g. the rows an
     // expert-parallel rank received): the down GEMM stores the output rows
     // itself; no fp32 accumulator, no finalize pass
-    const bool direct = tc && s.top_k == 1 && s.num_shared == 0 && aligned16(a->y);
+    // the caller takes the fp32 accumulator as the output: every path that writes
+    // the layer dtype itself (direct, shared-last, folded finalize) is off
+    const bool acc_out = (a->flags & CHRONOS_FLAG_ACC_OUT) != 0;
+    if (acc_out) {
+        if (!aligned16(a->y)) return fail(CHRONOS_ERR_INVALID_ARG, "CHRONOS_FLAG_ACC_OUT: y must be 16-byte aligned");
+        w.acc_out = static_cast<float*>(a->y);
+    }
+    const bool direct = tc && !acc_out && s.top_k == 1 && s.num_shared == 0 && aligned16(a->y);
     if (direct) {
         splits_dn = 1;
         kt_dn = s.ffn / kTcBK;
@@ -883,7 +892,7 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     // product per output tile, whose epilogue adds the routed accumulator and
     // writes the output (no finalize pass, no shared reduce-adds)
     // (when its tiles, one per 128 or BN tokens and output-column tile, cover the SMs)
-    const bool shared_last = tc && !direct && s.num_shared > 0 && aligned16(a->y) &&
+    const bool shared_last = tc && !direct && !acc_out && s.num_shared > 0 && aligned16(a->y) &&
                              (N + bn_dn - 1) / bn_dn * mt_dn >= sm_count();
     // token-major shared-last calls combine in two phases: the routed units store
     // their scaled rows (layer dtype) into the expert-ordered x buffer, dead once
@@ -892,7 +901,7 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     const bool two_phase = tm_dn && shared_last && g_two_phase_enabled;
     // weight-major calls with shared experts (every output tile has units): the
     // down GEMM writes the output tile by tile as the last contribution lands
-    const bool fold = tc && !tm_dn && !direct && !shared_last && s.num_shared > 0 && g_fold_enabled;
+    const bool fold = tc && !tm_dn && !direct && !shared_last && !acc_out && s.num_shared > 0 && g_fold_enabled;
 
     int rc;
     // counters: zeroed by the logit kernel, or here when routing is skipped
@@ -1003,14 +1012,14 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
     if (rc) return rc;
 
     prof_mark(slot, CHRONOS_STAGE_FINALIZE, st);
-    if (direct || shared_last || fold) {
+    if (direct || shared_last || fold || acc_out) {
         prof_mark(slot, kBoundaries - 1, st);
         return CHRONOS_OK;
     }
     const int64_t count4 = N * s.hidden / 4;
     const int blocks = static_cast<int>(std::min<int64_t>((count4 + 255) / 256, 8 * sm_count()));
     CHRONOS_CUDA_CHECK(launch_kernel(finalize_kernel<T>, dim3(blocks), dim3(256), 0, st, true,
-                                     static_cast<const float*>(w.at<float>(L.y_acc)),
+                                     static_cast<const float*>(w.y_acc()),
                                      static_cast<T*>(a->y), count4));
     prof_ran(slot, CHRONOS_STAGE_FINALIZE);
     prof_mark(slot, kBoundaries - 1, st);
@@ -1662,6 +1671,7 @@ int norm_impl(const ChronosNormArgs* a, cudaStream_t st) {
     p.rows = a->rows;
     p.width = a->width;
     p.eps = a->eps;
+    p.x_fp32 = a->x_fp32 ? 1 : 0;
     p.x = a->x;
     p.residual = a->residual;
     p.sum_out = a->sum_out;

@@ -308,7 +308,11 @@ class ChronosModel(nn.Module):
                 attn = layer.self_attn.prefill(h_in, cos, sin, cache)
             mlp_in = layer.post_attention_layernorm(attn, residual=hidden, sum_out=hidden)
             mask = masks[i] if masks else None
-            pending = layer.mlp(mlp_in, mask)
+            if decode and i > 0 and hasattr(layer.mlp, "forward_acc"):
+                # the next norm rounds the layer's fp32 accumulator itself (no finalize pass)
+                pending = layer.mlp.forward_acc(mlp_in, mask)
+            else:
+                pending = layer.mlp(mlp_in, mask)
             if i == 0:   # the lookahead router reads block 0's output (model_chronos.py:155-156)
                 hidden = hidden + pending
                 pending = None

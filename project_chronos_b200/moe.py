@@ -415,6 +415,19 @@ class ChronosMOEFeedForward(nn.Module):
     # ------------------------------------------------------------------
     def forward(self, x: torch.Tensor, available_expert_mask: Optional[torch.Tensor] = None
                 ) -> torch.Tensor:
+        return self._forward(x, available_expert_mask, acc_out=False)
+
+    def forward_acc(self, x: torch.Tensor, available_expert_mask: Optional[torch.Tensor] = None
+                    ) -> torch.Tensor:
+        """``forward`` whose result is the layer's fp32 accumulator, not yet rounded
+        to the layer dtype (CHRONOS_FLAG_ACC_OUT: no finalize pass), for a caller
+        whose next kernel reads it and rounds it (``ops.add_rmsnorm`` with an fp32
+        x).  Calls that take the host-hook path return ``forward``'s output in the
+        layer dtype; the caller accepts either."""
+        return self._forward(x, available_expert_mask, acc_out=True)
+
+    def _forward(self, x: torch.Tensor, available_expert_mask: Optional[torch.Tensor], acc_out: bool
+                 ) -> torch.Tensor:
         if not x.is_cuda:
             raise RuntimeError("ChronosMOEFeedForward (sm_100a kernels) needs CUDA tensors; "
                                f"got x on {x.device}")
@@ -633,7 +646,7 @@ class ChronosMOEFeedForward(nn.Module):
                     avail_t = avail_dev
             out = self._layer_call(pool, bias)(x_flat, avail=avail_t, want_probs=True,
                                                want_stats=masked, want_topk=self.training,
-                                               avail_is_mask=avail_is_mask)
+                                               avail_is_mask=avail_is_mask, acc_out=acc_out)
             probs = out["probs"]
             if masked:
                 if a_np is None:

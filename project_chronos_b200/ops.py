@@ -255,9 +255,12 @@ class LayerCall:
         return size
 
     def __call__(self, x: torch.Tensor, avail: Optional[torch.Tensor] = None, want_probs: bool = True,
-                 want_stats: bool = False, want_topk: bool = False, avail_is_mask: bool = False) -> dict:
+                 want_stats: bool = False, want_topk: bool = False, avail_is_mask: bool = False,
+                 acc_out: bool = False) -> dict:
         """``avail_is_mask``: ``avail`` is a residency mask, a_e = (avail[e] > 0),
-        thresholded by the kernels (CHRONOS_FLAG_AVAIL_MASK)."""
+        thresholded by the kernels (CHRONOS_FLAG_AVAIL_MASK).  ``acc_out``: ``y`` is
+        the layer's fp32 accumulator, not rounded to the layer dtype
+        (CHRONOS_FLAG_ACC_OUT; for a caller whose next kernel rounds it)."""
         if not x.is_cuda or x.dtype != self.dtype:
             raise TypeError(f"x must be a CUDA {self.dtype} tensor")
         x = x.contiguous()
@@ -265,7 +268,7 @@ class LayerCall:
         dev = self.dev
         stream = _raw_stream(dev.index)
         ws = shared_workspace.get(dev, stream, self._workspace_bytes(n))
-        y = torch.empty(n, self.h, dtype=self.dtype, device=dev)
+        y = torch.empty(n, self.h, dtype=torch.float32 if acc_out else self.dtype, device=dev)
         probs = torch.empty(n, self.e, dtype=self.dtype, device=dev) if want_probs else None
         topk_idx = torch.empty(n, self.k, dtype=torch.int32, device=dev) if want_topk else None
         topk_w = torch.empty(n, self.k, dtype=torch.float32, device=dev) if want_topk else None
@@ -288,6 +291,8 @@ class LayerCall:
         a.workspace_bytes = ws.numel()
         if avail_is_mask and avail is not None:
             a.flags |= N.FLAG_AVAIL_MASK
+        if acc_out:
+            a.flags |= N.FLAG_ACC_OUT
         if torch.cuda.current_device() == dev.index:
             rc = self._lib.chronos_moe_forward(ctypes.byref(a), ctypes.c_void_p(stream))
         else:
@@ -432,16 +437,26 @@ def lookahead_forward(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, num_e
 def add_rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None,
                 sum_out: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """RMSNorm(x + residual) * weight over the last dim (include/chronos_attention.h);
-    ``sum_out`` (may be ``x`` or ``residual``) receives x + residual."""
+    ``sum_out`` (may be ``x`` or ``residual``) receives x + residual.  The layer
+    dtype is ``weight``'s; an fp32 ``x`` with a bf16/fp16 ``weight`` (a MoE
+    layer's fp32 accumulator) is rounded to that dtype as it is read."""
     _check_cuda(x, weight, residual, sum_out, out)
-    if x.dtype not in _DTYPES or weight.dtype != x.dtype:
+    dt = weight.dtype
+    x_fp32 = x.dtype == torch.float32 and dt != torch.float32
+    if dt not in _DTYPES or (x.dtype != dt and not x_fp32):
         raise TypeError(f"x {x.dtype} / weight {weight.dtype}: one supported dtype expected")
+    for t in (residual, sum_out, out):
+        if t is not None and t.dtype != dt:
+            raise TypeError("residual, sum_out and out must have weight's dtype")
     w = x.shape[-1]
     for t in (x, residual, sum_out, out):
         if t is not None and not t.is_contiguous():
             raise ValueError("add_rmsnorm needs contiguous tensors")
-    out = torch.empty_like(x) if out is None else out
-    args = N.ChronosNormArgs(rows=x.numel() // max(w, 1), width=w, dtype=_DTYPES[x.dtype], eps=float(eps),
+    if x_fp32 and sum_out is not None and sum_out.data_ptr() == x.data_ptr():
+        raise ValueError("sum_out cannot alias an fp32 x")
+    out = torch.empty(x.shape, dtype=dt, device=x.device) if out is None else out
+    args = N.ChronosNormArgs(rows=x.numel() // max(w, 1), width=w, dtype=_DTYPES[dt], eps=float(eps),
+                             x_fp32=1 if x_fp32 else 0,
                              x=_ptr(x), residual=_ptr(residual), sum_out=_ptr(sum_out),
                              weight=_ptr(weight.contiguous()), out=_ptr(out))
     lib = N.load_library()

@@ -241,6 +241,52 @@ def test_add_rmsnorm(dtype):
     assert (plain.float() - want2.float()).norm() / want2.float().norm() <= tol
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("width", [1024, 2048, 4096])
+def test_add_rmsnorm_reads_an_fp32_accumulator(width):
+    """An fp32 x with a bf16 weight (a MoE layer's fp32 accumulator) is rounded
+    to bf16 as it is read: bitwise the same as rounding it first."""
+    from project_chronos_b200 import ops
+    torch.manual_seed(width)
+    acc = torch.randn(33, width, device=DEV) * 3
+    r = torch.randn(33, width, device=DEV).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(width, device=DEV)).to(torch.bfloat16)
+    r1, r2 = r.clone(), r.clone()
+    got = ops.add_rmsnorm(acc, w, 1e-5, residual=r1, sum_out=r1)
+    want = ops.add_rmsnorm(acc.to(torch.bfloat16), w, 1e-5, residual=r2, sum_out=r2)
+    torch.cuda.synchronize()
+    assert got.dtype == torch.bfloat16
+    assert torch.equal(got, want) and torch.equal(r1, r2)
+
+
+@pytest.mark.gpu
+def test_moe_forward_acc_is_the_unrounded_output():
+    """ChronosMOEFeedForward.forward_acc: the fp32 accumulator (CHRONOS_FLAG_ACC_OUT,
+    no finalize pass) rounds to forward's output (to the order of the fp32 adds)."""
+    import types
+    from project_chronos_b200 import synthetic as syn
+    from project_chronos_b200.moe import ChronosMOEFeedForward
+    shape = syn.MoEShape(512, 16, 2, 256, 1)
+    for n in (1, 32, 300):
+        wl = syn.make_workload(shape, n, seed=n, dtype=torch.bfloat16, device=DEV, avail_p=0.8)
+        w = wl.weights
+        cfg = types.SimpleNamespace(hidden_size=512, num_experts=16, num_experts_per_tok=2,
+                                    moe_intermediate_size=256, num_shared_experts=1, norm_topk_prob=True,
+                                    router_aux_loss_coef=5e-4, fallback_mask_prob=0.0, hidden_act="silu",
+                                    dropout=0.0, intermediate_size=256)
+        m = ChronosMOEFeedForward.from_stacked(cfg, w.router, w.gate, w.up, w.down, w.sh_gate, w.sh_up,
+                                               w.sh_down).eval()
+        m.mask_semantics = "residency"
+        mask = wl.mask.to(DEV, torch.float32)
+        with torch.no_grad():
+            y = m(wl.x.view(1, n, 512), mask)
+            acc = m.forward_acc(wl.x.view(1, n, 512), mask)
+        torch.cuda.synchronize()
+        assert acc.dtype == torch.float32 and acc.shape == y.shape
+        rel = ((acc.to(torch.bfloat16).float() - y.float()).norm() / y.float().norm()).item()
+        assert rel <= 1e-3, (n, rel)
+
+
 def _model(dtype):
     from project_chronos_b200 import synthetic as syn
     from project_chronos_b200.model import ChronosForCausalLM
