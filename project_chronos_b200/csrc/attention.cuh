@@ -77,6 +77,17 @@ __device__ __forceinline__ void warp_rmsnorm(float* v, int len, const T* w, floa
     __syncwarp();
 }
 
+// warp_rmsnorm with the norm weight already in shared memory (fp32).
+template <typename T>
+__device__ __forceinline__ void warp_rmsnorm_s(float* v, int len, const float* w, float eps, int lane) {
+    float ss = 0.0f;
+    for (int i = lane; i < len; i += 32) ss = fmaf(v[i], v[i], ss);
+    const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(len) + eps);
+    __syncwarp();
+    for (int i = lane; i < len; i += 32) v[i] = round_to<T>(w[i] * (v[i] * inv));
+    __syncwarp();
+}
+
 // RoPE as the reference writes it (minimind apply_rotary_pos_emb):
 // x*cos + rotate_half(x)*sin over `len` values, with cos/sin the first `len`
 // columns of the table row; each product and the sum rounded to T.  `tmp`
@@ -86,6 +97,14 @@ __device__ __forceinline__ float rope_value(const float* x, int i, int len, cons
     const int half = len >> 1;
     const float rot = i < half ? -x[i + half] : x[i - half];
     return round_to<T>(round_to<T>(x[i] * to_f32<T>(crow[i])) + round_to<T>(rot * to_f32<T>(srow[i])));
+}
+
+// rope_value with the cos/sin row already in shared memory (fp32).
+template <typename T>
+__device__ __forceinline__ float rope_value_s(const float* x, int i, int len, const float* c, const float* sn) {
+    const int half = len >> 1;
+    const float rot = i < half ? -x[i + half] : x[i - half];
+    return round_to<T>(round_to<T>(x[i] * c[i]) + round_to<T>(rot * sn[i]));
 }
 
 // ---------------------------------------------------------------------------
@@ -450,26 +469,18 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) mla_decode_ker
     float* cnew = part + rep * L;          // [L]
     float* krn = cnew + L;                 // [R]
     float* tmp = krn + R;                  // [(rep+1)*R] rotated q_rope heads and k_rope
-    float* red = tmp + (rep + 1) * R;      // [2 * kAttnMaxRep]
+    float* wqn = tmp + (rep + 1) * R;      // [nope] q_nope norm weight
+    float* wqr = wqn + nope;               // [R] q_rope norm weight
+    float* wkv = wqr + R;                  // [L] latent norm weight
+    float* cs = wkv + L;                   // [R] cos row
+    float* sn = cs + R;                    // [R] sin row
+    float* red = sn + R;                   // [2 * kAttnMaxRep]
     float* wred = red + 2 * kAttnMaxRep;   // [kAttnWarps][rep][L] weighted-sum reduction
     float* sc = wred + attn_red_floats(rep, L);   // [rep][cap]
-    const int pos = *p.pos;
-    T* out = static_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.heads + g * rep) * D;
-    if (pos < 0 || pos >= p.max_len || pos >= p.table_len) {   // outside the cache: no access
-        for (int i = threadIdx.x; i < rep * D; i += kAttnThreads) out[i] = from_f32<T>(0.0f);
-        return;   // every CTA of the cluster returns here (same pos)
-    }
-    const int n = pos + 1;
+    // what does not depend on the position first: the weight slices, this token's
+    // projections, the norm weights
     const int width = p.heads * (nope + R) + L;
     const T* row = static_cast<const T*>(p.proj) + static_cast<int64_t>(b) * width;
-    T* cache_c = static_cast<T*>(p.cache_a) + static_cast<int64_t>(b) * p.max_len * L;
-    T* cache_k = static_cast<T*>(p.cache_b) + static_cast<int64_t>(b) * p.max_len * p.kv_heads * R;
-    // this CTA's positions, their cache rows on their way while the query is formed
-    const int chunk = (n + splits - 1) / splits;
-    const int t_lo = min(n, sidx * chunk), t_hi = min(n, t_lo + chunk), cnt = t_hi - t_lo;
-    prefetch_rows<T>(cache_c, L, t_lo, t_hi, L * static_cast<int>(sizeof(T)));
-    prefetch_rows<T>(cache_k + g * R, static_cast<int64_t>(p.kv_heads) * R, t_lo, t_hi,
-                     R * static_cast<int>(sizeof(T)));
     if (p.stage_w) {
         stage_rows<T>(wstage, wkn_g, nope * L);
         stage_rows<T>(wstage + nope * L, wkr_g, R * L);
@@ -479,13 +490,44 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) mla_decode_ker
         qn[i] = to_f32<T>(row[(g * rep) * nope + i]);
     for (int i = threadIdx.x; i < rep * R; i += kAttnThreads)
         qr[i] = to_f32<T>(row[p.heads * nope + (g * rep) * R + i]);
-    for (int i = threadIdx.x; i < L; i += kAttnThreads) cnew[i] = to_f32<T>(row[p.heads * (nope + R) + i]);
+    for (int i = threadIdx.x; i < L; i += kAttnThreads) {
+        cnew[i] = to_f32<T>(row[p.heads * (nope + R) + i]);
+        wkv[i] = to_f32<T>(static_cast<const T*>(p.norm_kv)[i]);
+    }
+    for (int i = threadIdx.x; i < nope; i += kAttnThreads) wqn[i] = to_f32<T>(static_cast<const T*>(p.norm_q)[i]);
+    for (int i = threadIdx.x; i < R; i += kAttnThreads) wqr[i] = to_f32<T>(static_cast<const T*>(p.norm_q2)[i]);
+    const int pos = *p.pos;
+    T* out = static_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.heads + g * rep) * D;
+    if (pos < 0 || pos >= p.max_len || pos >= p.table_len) {   // outside the cache: no access
+        for (int i = threadIdx.x; i < rep * D; i += kAttnThreads) out[i] = from_f32<T>(0.0f);
+        return;   // every CTA of the cluster returns here (same pos)
+    }
+    const int n = pos + 1;
+    T* cache_c = static_cast<T*>(p.cache_a) + static_cast<int64_t>(b) * p.max_len * L;
+    T* cache_k = static_cast<T*>(p.cache_b) + static_cast<int64_t>(b) * p.max_len * p.kv_heads * R;
+    // the rotary row (its first R columns), and this CTA's cache rows on their way
+    for (int i = threadIdx.x; i < R; i += kAttnThreads) {
+        cs[i] = to_f32<T>(static_cast<const T*>(p.cos)[static_cast<int64_t>(pos) * D + i]);
+        sn[i] = to_f32<T>(static_cast<const T*>(p.sin)[static_cast<int64_t>(pos) * D + i]);
+    }
+    const int chunk = (n + splits - 1) / splits;
+    const int t_lo = min(n, sidx * chunk), t_hi = min(n, t_lo + chunk), cnt = t_hi - t_lo;
+    prefetch_rows<T>(cache_c, L, t_lo, t_hi, L * static_cast<int>(sizeof(T)));
+    prefetch_rows<T>(cache_k + g * R, static_cast<int64_t>(p.kv_heads) * R, t_lo, t_hi,
+                     R * static_cast<int>(sizeof(T)));
     __syncthreads();
-    // per-head RMSNorms of q_nope and q_rope, RMSNorm of the latent
+    // per-head RMSNorms of q_nope and q_rope (each q_rope head then rotated by its
+    // warp into tmp [rep][R]), RMSNorm of the latent
     for (int v = warp; v < 2 * rep + 1; v += kAttnWarps) {
-        if (v < rep) warp_rmsnorm<T>(qn + v * nope, nope, static_cast<const T*>(p.norm_q), p.eps, lane);
-        else if (v < 2 * rep) warp_rmsnorm<T>(qr + (v - rep) * R, R, static_cast<const T*>(p.norm_q2), p.eps, lane);
-        else warp_rmsnorm<T>(cnew, L, static_cast<const T*>(p.norm_kv), p.eps, lane);
+        if (v < rep) {
+            warp_rmsnorm_s<T>(qn + v * nope, nope, wqn, p.eps, lane);
+        } else if (v < 2 * rep) {
+            float* vec = qr + (v - rep) * R;
+            warp_rmsnorm_s<T>(vec, R, wqr, p.eps, lane);
+            for (int e = lane; e < R; e += 32) tmp[(v - rep) * R + e] = rope_value_s<T>(vec, e, R, cs, sn);
+        } else {
+            warp_rmsnorm_s<T>(cnew, L, wkv, p.eps, lane);
+        }
     }
     __syncthreads();
     // k_rope of the new token: k_rope_proj(c), a warp per output (rounded as the bf16 linear rounds)
@@ -504,14 +546,8 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) mla_decode_ker
         qabs[i] = acc;
     }
     __syncthreads();
-    // RoPE at `pos` on q_rope (every head) and on the new k_rope
-    const T* crow = static_cast<const T*>(p.cos) + static_cast<int64_t>(pos) * D;
-    const T* srow = static_cast<const T*>(p.sin) + static_cast<int64_t>(pos) * D;
-    // rotated q_rope heads and k_rope: tmp [rep][R] and tmp + rep*R [R]
-    for (int i = threadIdx.x; i < (rep + 1) * R; i += kAttnThreads) {
-        const int h = i / R, e = i % R;
-        tmp[i] = rope_value<T>(h < rep ? qr + h * R : krn, e, R, crow, srow);
-    }
+    // RoPE at `pos` on the new k_rope: tmp + rep*R [R]
+    for (int e = threadIdx.x; e < R; e += kAttnThreads) tmp[rep * R + e] = rope_value_s<T>(krn, e, R, cs, sn);
     __syncthreads();
     const float* qrot = tmp;
     const float* krot = tmp + rep * R;
@@ -576,10 +612,24 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) sw_decode_kern
     float* kn = q + rep * D;               // [D]
     float* vn = kn + D;                    // [D]
     float* tmp = vn + D;                   // [(rep+1)*D]
-    float* part = tmp + (rep + 1) * D;     // [rep][D] this CTA's weighted values
+    float* wq = tmp + (rep + 1) * D;       // [D] q norm weight
+    float* wk = wq + D;                    // [D] k norm weight
+    float* cs = wk + D;                    // [D] cos row
+    float* sn = cs + D;                    // [D] sin row
+    float* part = sn + D;                  // [rep][D] this CTA's weighted values
     float* red = part + rep * D;           // [2 * kAttnMaxRep]
     float* wred = red + 2 * kAttnMaxRep;   // [kAttnWarps][rep][D] weighted-sum reduction
     float* sc = wred + attn_red_floats(rep, D);   // [rep][cap]
+    // what does not depend on the position first: this token's projections, the norm weights
+    const int width = (p.heads + 2 * p.kv_heads) * D;
+    const T* row = static_cast<const T*>(p.proj) + static_cast<int64_t>(b) * width;
+    for (int i = threadIdx.x; i < rep * D; i += kAttnThreads) q[i] = to_f32<T>(row[(g * rep) * D + i]);
+    for (int i = threadIdx.x; i < D; i += kAttnThreads) {
+        kn[i] = to_f32<T>(row[(p.heads + g) * D + i]);
+        vn[i] = to_f32<T>(row[(p.heads + p.kv_heads + g) * D + i]);
+        wq[i] = to_f32<T>(static_cast<const T*>(p.norm_q)[i]);
+        wk[i] = to_f32<T>(static_cast<const T*>(p.norm_q2)[i]);
+    }
     const int pos = *p.pos;
     T* out = static_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.heads + g * rep) * D;
     const int rpos = pos < W ? pos : W;    // the cache length before this token
@@ -589,33 +639,25 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) sw_decode_kern
     }
     const int slot = pos % W;
     const int n = pos + 1 < W ? pos + 1 : W;
-    const int width = (p.heads + 2 * p.kv_heads) * D;
-    const T* row = static_cast<const T*>(p.proj) + static_cast<int64_t>(b) * width;
     T* kc = static_cast<T*>(p.cache_a) + static_cast<int64_t>(b) * W * p.kv_heads * D;
     T* vc = static_cast<T*>(p.cache_b) + static_cast<int64_t>(b) * W * p.kv_heads * D;
     const int64_t rs = static_cast<int64_t>(p.kv_heads) * D;
-    // this CTA's ring slots, their keys and values on their way while the query is formed
+    // the rotary row, and this CTA's ring slots on their way while the query is formed
+    for (int i = threadIdx.x; i < D; i += kAttnThreads) {
+        cs[i] = to_f32<T>(static_cast<const T*>(p.cos)[static_cast<int64_t>(rpos) * D + i]);
+        sn[i] = to_f32<T>(static_cast<const T*>(p.sin)[static_cast<int64_t>(rpos) * D + i]);
+    }
     const int chunk = (n + splits - 1) / splits;
     const int t_lo = min(n, sidx * chunk), t_hi = min(n, t_lo + chunk), cnt = t_hi - t_lo;
     prefetch_rows<T>(kc + g * D, rs, t_lo, t_hi, D * static_cast<int>(sizeof(T)));
     prefetch_rows<T>(vc + g * D, rs, t_lo, t_hi, D * static_cast<int>(sizeof(T)));
-    for (int i = threadIdx.x; i < rep * D; i += kAttnThreads) q[i] = to_f32<T>(row[(g * rep) * D + i]);
-    for (int i = threadIdx.x; i < D; i += kAttnThreads) {
-        kn[i] = to_f32<T>(row[(p.heads + g) * D + i]);
-        vn[i] = to_f32<T>(row[(p.heads + p.kv_heads + g) * D + i]);
-    }
     __syncthreads();
+    // per warp: a head's RMSNorm, then its rotation into tmp [rep][D] (queries) and
+    // tmp + rep*D [D] (the new key), with no block barrier between the two
     for (int v = warp; v < rep + 1; v += kAttnWarps) {
-        if (v < rep) warp_rmsnorm<T>(q + v * D, D, static_cast<const T*>(p.norm_q), p.eps, lane);
-        else warp_rmsnorm<T>(kn, D, static_cast<const T*>(p.norm_q2), p.eps, lane);
-    }
-    __syncthreads();
-    const T* crow = static_cast<const T*>(p.cos) + static_cast<int64_t>(rpos) * D;
-    const T* srow = static_cast<const T*>(p.sin) + static_cast<int64_t>(rpos) * D;
-    // rotated queries and key: tmp [rep][D] and tmp + rep*D [D]
-    for (int i = threadIdx.x; i < (rep + 1) * D; i += kAttnThreads) {
-        const int h = i / D, e = i % D;
-        tmp[i] = rope_value<T>(h < rep ? q + h * D : kn, e, D, crow, srow);
+        float* vec = v < rep ? q + v * D : kn;
+        warp_rmsnorm_s<T>(vec, D, v < rep ? wq : wk, p.eps, lane);
+        for (int e = lane; e < D; e += 32) tmp[v * D + e] = rope_value_s<T>(vec, e, D, cs, sn);
     }
     __syncthreads();
     const float* qrot = tmp;

@@ -1529,6 +1529,8 @@ size_t mla_smem_base(const AttnParams& p) {
                             + 3 * rep * p.latent       // qabs, ctx, part
                             + p.latent + p.rope_dim    // cnew, krn
                             + (rep + 1) * p.rope_dim   // tmp
+                            + p.nope + p.rope_dim + p.latent   // norm weights
+                            + 2 * p.rope_dim           // cos, sin
                             + 2 * kAttnMaxRep          // red
                             + attn_red_floats(p.rep, p.latent)   // weighted-sum reduction
                             + rep * p.cap);            // scores
@@ -1539,6 +1541,7 @@ size_t sw_smem(const AttnParams& p) {
     return sizeof(float) * (rep * p.head_dim           // q
                             + 2 * p.head_dim           // kn, vn
                             + (rep + 1) * p.head_dim   // tmp
+                            + 4 * p.head_dim           // norm weights, cos, sin
                             + rep * p.head_dim         // part
                             + 2 * kAttnMaxRep          // red
                             + attn_red_floats(p.rep, p.head_dim)   // weighted-sum reduction

@@ -53,6 +53,19 @@ def test_ep_two_ranks_match_single_device_oracle(scenario):
     assert res[1][3][0] == res[0][4][1]
 
 
+def test_ep_four_ranks_deduplicated_rows_match_single_device_oracle():
+    """World 4: one send row per (token, destination rank) with up to P = 2 of the
+    token's selections on that rank; every rank's output equals the oracle and
+    what rank i sends to rank j is what j receives from i."""
+    res = _run("all", world=4)
+    for status, rank, val, sc, rc in res:
+        assert status == "ok", (rank, val)
+        assert val < 1e-5, (rank, val)
+    for i in range(4):
+        for j in range(4):
+            assert res[i][3][j] == res[j][4][i]
+
+
 def test_injected_rank_failure_ends_the_collective_with_an_error():
     res = _run("fail", timeout=90)
     by_rank = {r[1]: r for r in res}
