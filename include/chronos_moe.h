@@ -240,8 +240,8 @@ CHRONOS_API uint64_t chronos_moe_kernel_launches(void);
  *                  converted by the CTA whose contribution completes it; 0
  *                  (default, measured faster): a separate finalize kernel.
  *   "down_split_target"  -1 (default): the weight-major down GEMM of a decode
- *                  call halves K when that fills the last round of work units
- *                  more than 5 % better; n in 0..64: split until it has about n
+ *                  call halves K once its unsplit work units fill at least two
+ *                  rounds of the SMs; n in 0..64: split until it has about n
  *                  units per SM (0: no split).
  *   "gateup_split"  1: a decode call (N <= 64) whose gate/up units would not
  *                  cover the SMs splits the routed units along K (2 or 4 ways);

@@ -855,19 +855,12 @@ int forward_impl(const ChronosMoeArgs* a, cudaStream_t st) {
             const double target = static_cast<double>(target_units) * sm_count();
             while (tiles_est * splits_dn < target && splits_dn * 2 * 4 <= kt_total) splits_dn *= 2;
         } else {
-            // halve K when that fills the last round of units clearly better
-            // (every unit's epilogue reduces anyway; the split adds reduce
-            // traffic and per-unit overhead, charged 5 %; measured: 4-way
-            // splits and splits of already-full rounds are slower)
-            double best = -1.0;
-            for (int sp = 1; sp * 4 <= kt_total && sp <= 2; sp *= 2) {
-                const double units = tiles_est * sp / sm_count();
-                const double score = units / std::ceil(units) - 0.05 * std::log2(static_cast<double>(sp));
-                if (score > best + 1e-9) {
-                    best = score;
-                    splits_dn = sp;
-                }
-            }
+            // halve K once the unsplit units fill at least two rounds of the SMs: the
+            // half-size units shorten the last round's tail.  With fewer units the
+            // split only adds reduce traffic and per-unit work (measured: batch 1 of
+            // the 64-expert shape and the 16-expert model shape are faster unsplit,
+            // batches 8 and 32 faster split, 64 even)
+            if (tiles_est >= 2.0 * sm_count() && kt_total >= 8) splits_dn = 2;
         }
         kt_dn = (kt_total + splits_dn - 1) / splits_dn;
         splits_dn = (kt_total + kt_dn - 1) / kt_dn;
