@@ -251,6 +251,18 @@ CHRONOS_API uint64_t chronos_moe_kernel_launches(void);
  *   "select_plan_one_block"  1: decode calls of 9..32 tokens select and plan
  *                  in one block of a warp per token; 0 (default, measured
  *                  faster): blocks of 8 tokens and a last-block plan.
+ *   "gateup_prefetch_mb"  0..1024, default 128: in a decode call that leaves
+ *                  an expert unselected with probability (1 - k/E)^N <= 10 %
+ *                  and has no slot_of_expert map, each gate/up CTA past the
+ *                  shared experts' units prefetches into L2, while the routing
+ *                  kernels run, the first k tiles of the routed unit it would
+ *                  run first if every available expert were selected (at most
+ *                  this many MB over all CTAs); 0: off.  A hint only.
+ *   "model_pdl"  1: chronos_add_rmsnorm, the attention decode kernels,
+ *                  chronos_lookahead_forward and chronos_argmax_rows launch as
+ *                  programmatic dependents of the previous kernel on the stream
+ *                  (their blocks start early and wait for it before touching
+ *                  memory); 0 (default, measured faster): ordinary stream order.
  * Returns CHRONOS_OK, or CHRONOS_ERR_INVALID_ARG for an unknown name or a value
  * out of range. */
 CHRONOS_API int chronos_moe_set_option(const char* name, int64_t value);

@@ -121,6 +121,7 @@ __global__ void __launch_bounds__(kAttnThreads) add_rmsnorm_kernel(NormParams p)
     const T* w = static_cast<const T*>(p.weight);
     T* sum_out = static_cast<T*>(p.sum_out);
     T* out = static_cast<T*>(p.out);
+    pdl_wait();   // launched early behind the kernel that writes x (programmatic launch)
     for (int64_t r = blockIdx.x; r < p.rows; r += gridDim.x) {
         const int64_t base = r * p.width;
         float ss = 0.0f;
@@ -151,6 +152,7 @@ template <typename T, int VPL>
 __global__ void __launch_bounds__(kAttnThreads) add_rmsnorm_warp_kernel(NormParams p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t r = static_cast<int64_t>(blockIdx.x) * kAttnWarps + warp;
+    pdl_wait();   // launched early behind the kernel that writes x (programmatic launch)
     if (r >= p.rows) return;
     const int nv = p.width / 8;
     const int64_t base = r * p.width;
@@ -214,13 +216,35 @@ __global__ void __launch_bounds__(kAttnThreads) argmax_rows_kernel(const T* x, i
     __shared__ float s_v[kAttnWarps];
     __shared__ int s_i[kAttnWarps];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();   // launched early behind the kernel that writes x (programmatic launch)
+    // rows of 8-element groups on 16-byte boundaries: each thread loads up to 4
+    // groups at once (one memory round trip for rows of up to 8192 elements)
+    const bool vec = cols % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
         const T* row = x + r * cols;
         float bv = -INFINITY;
         int bi = cols;
-        for (int c = threadIdx.x; c < cols; c += kAttnThreads) {
-            const float v = to_f32<T>(row[c]);
-            if (argmax_better(v, c, bv, bi)) { bv = v; bi = c; }
+        if (vec) {
+            const int G = cols / 8;
+            for (int g0 = threadIdx.x; g0 < G; g0 += 4 * kAttnThreads) {
+                float v[4][8];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (g0 + j * kAttnThreads < G) load8<T>(row + (g0 + j * kAttnThreads) * 8, v[j]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int g = g0 + j * kAttnThreads;
+                    if (g < G)
+#pragma unroll
+                        for (int u = 0; u < 8; ++u)
+                            if (argmax_better(v[j][u], g * 8 + u, bv, bi)) { bv = v[j][u]; bi = g * 8 + u; }
+                }
+            }
+        } else {
+            for (int c = threadIdx.x; c < cols; c += kAttnThreads) {
+                const float v = to_f32<T>(row[c]);
+                if (argmax_better(v, c, bv, bi)) { bv = v; bi = c; }
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -444,6 +468,7 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) mla_decode_ker
     constexpr int rep = REP;
     extern __shared__ __align__(16) float msm[];
     cg::cluster_group cluster = cg::this_cluster();
+    pdl_wait();   // launched early behind the projection that writes proj (programmatic launch)
     const int splits = p.splits;
     const int sidx = blockIdx.x % splits, g = blockIdx.x / splits, b = blockIdx.y;
     const int nope = p.nope, R = p.rope_dim, L = p.latent, D = p.head_dim, cap = p.cap;
@@ -604,6 +629,7 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) sw_decode_kern
     constexpr int rep = REP;
     extern __shared__ __align__(16) float ssm[];
     cg::cluster_group cluster = cg::this_cluster();
+    pdl_wait();   // launched early behind the projection that writes proj (programmatic launch)
     const int splits = p.splits;
     const int sidx = blockIdx.x % splits, g = blockIdx.x / splits, b = blockIdx.y;
     const int D = p.head_dim, W = p.window, cap = p.cap;

@@ -107,6 +107,16 @@ struct TcGemmParams {
     int num_shared;
     int32_t* gu_cnt;
     float* gu_part;
+    // Dense gate/up, batches that select nearly every expert: before waiting for
+    // the plan, a CTA past the shared units prefetches into L2 the first spec_kt
+    // k tiles of the routed unit it would run first if all spec_experts experts
+    // (weight slot = expert id) were active.  A hint: a wrong guess only moves
+    // bytes while the HBM is otherwise idle.  0: no prefetch.
+    // spec_avail (null: every expert available): the call's availability input;
+    // experts with spec_avail[e] <= 0 form no group, so the guess skips them.
+    int spec_kt;
+    int spec_experts;
+    const float* spec_avail;
 };
 
 __host__ __device__ constexpr int tc_stage_bytes(int bn, bool gateup) {
@@ -321,6 +331,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // decode tiles (one token tile per group): weights streamed once, evict first
         constexpr bool kStreamA = BN <= 64;
         const uint64_t pol_a = kStreamA ? l2_evict_first_policy() : 0ull;
+        if constexpr (GATEUP && DENSE) {
+            if (p.spec_kt > 0 && static_cast<int>(blockIdx.x) >= pre_units) {
+                // routed unit r = blockIdx.x - pre_units is weight-row tile r % m_tiles of
+                // the (r / m_tiles)-th available expert when every available expert is
+                // selected (groups in expert order)
+                const int r = static_cast<int>(blockIdx.x) - pre_units;
+                const int q = r / p.m_tiles;
+                int e = q;
+                if (p.spec_avail != nullptr) {
+                    // the q-th expert with availability > 0: a warp scan over the input
+                    e = -1;
+                    int seen = 0;
+                    for (int base = 0; base < p.spec_experts && e < 0; base += 32) {
+                        const int ee = base + lane;
+                        const uint32_t m =
+                            __ballot_sync(0xffffffffu, ee < p.spec_experts && p.spec_avail[ee] > 0.0f);
+                        const int c = __popc(m);
+                        if (q < seen + c) {
+                            uint32_t mm = m;
+                            for (int i = 0; i < q - seen; ++i) mm &= mm - 1u;
+                            e = base + __ffs(static_cast<int>(mm)) - 1;
+                        }
+                        seen += c;
+                    }
+                }
+                if (lane == 0 && e >= 0 && e < p.spec_experts) {
+                    const int a_row = e * p.w_rows + (r - q * p.m_tiles) * kTcBM;
+                    for (int kt = 0; kt < p.spec_kt && kt < p.k_tiles; ++kt) {
+                        tma_prefetch_2d(&tm_a0r, kt * kTcBK, a_row);
+                        tma_prefetch_2d(&tm_a1r, kt * kTcBK, a_row);
+                    }
+                }
+            }
+        }
         for (int u = blockIdx.x;; u += gridDim.x) {
             if (u >= pre_units) {
                 if (!planned) load_plan();

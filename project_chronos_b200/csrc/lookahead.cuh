@@ -55,6 +55,7 @@ __global__ void __launch_bounds__(kLookaheadThreads) lookahead_kernel(LookaheadP
     namespace cg = cooperative_groups;
     extern __shared__ __align__(16) float la_smem[];
     cg::cluster_group cluster = cg::this_cluster();
+    pdl_wait();   // launched early behind the kernel that writes x (programmatic launch)
     const int rank = static_cast<int>(cluster.block_rank());
     const int cs = static_cast<int>(cluster.num_blocks());
     const int tb = p.tb, H = p.h, rpc = p.rpc, inner = p.inner, ek = p.e * p.k;

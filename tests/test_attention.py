@@ -219,6 +219,12 @@ def test_argmax_rows_matches_torch(dtype):
     assert got[3].item() == 100 and got[4].item() == 0 and got[5].item() == 17 and got[6].item() == 9
     y = torch.randn(2, 3, 129, device=DEV, dtype=dtype)
     assert torch.equal(ops.argmax_rows(y), torch.argmax(y, dim=-1))
+    # rows longer than one pass of 4 x 256 8-element groups per block
+    z = torch.randn(3, 8800, generator=g).to(dtype)
+    z[0, 8799] = 70.0
+    z[1, 8200] = z[1, 8300] = 70.0
+    zd = z.to(DEV)
+    assert torch.equal(ops.argmax_rows(zd).cpu(), torch.argmax(zd, dim=-1).cpu())
 
 
 @pytest.mark.gpu
@@ -353,3 +359,32 @@ def test_graphed_decoder_matches_eager_steps():
     with torch.no_grad():
         first = gd.step().clone()
         assert torch.equal(gd.ids.view(-1), first)
+
+
+@pytest.mark.gpu
+def test_model_steps_do_not_depend_on_programmatic_launch():
+    """The norm, attention, lookahead and arg-max kernels launch early behind their
+    predecessor (programmatic launch) and wait for it before touching memory; with
+    the switch off they launch after it.  Teacher-forced eager steps agree."""
+    from project_chronos_b200 import ops
+    c, m = _model(torch.bfloat16)
+    d = np.load(f"{G.GOLDEN}/{c['name']}.npz")
+    ids = torch.from_numpy(d["ids"]).to(DEV)
+    P, T = c["prompt"], c["steps"]
+    runs = []
+    try:
+        for pdl in (1, 0):
+            ops.set_option("model_pdl", pdl)
+            with torch.no_grad():
+                o, _ = m(ids[:, :P], use_cache=True)
+                cache = o.past_key_values
+                steps = []
+                for t in range(T):
+                    o, _ = m(ids[:, P + t:P + t + 1], past_key_values=cache, use_cache=True)
+                    steps.append(o.logits[:, -1].float().cpu().numpy())
+            runs.append(steps)
+    finally:
+        ops.set_option("model_pdl", 0)
+    for t in range(T):
+        assert O.rel_l2(runs[0][t], runs[1][t]) <= 2e-3, t
+        assert O.rel_l2(runs[0][t], d["logits_fp32"][t + 1]) <= 1e-2, t

@@ -428,3 +428,34 @@ def test_gateup_k_split_matches_unsplit(h, e, k, f, s, n):
     assert O.rel_l2(split, whole) <= 1e-3
     emu, *_ = _oracle(wl, k, True, avail=avail, emulate=True)
     assert O.rel_l2(split, emu) <= 3e-3
+
+
+@pytest.mark.parametrize("h,e,k,f,s,n,avail_p", [
+    (2048, 64, 6, 1408, 2, 32, 0.9),   # the DeepSeek-MoE-16B decode shape: two 32-expert mask words
+    (2048, 64, 6, 1408, 2, 64, None),
+    (1024, 16, 2, 2048, 1, 32, 0.85),  # the 8-layer model's MoE shape
+    (512, 40, 4, 256, 0, 48, 0.5),     # no shared experts; most CTAs' guesses land on no unit
+])
+def test_gateup_l2_prefetch_is_only_a_hint(h, e, k, f, s, n, avail_p):
+    """Batches that select nearly every expert let the gate/up GEMM's idle CTAs
+    prefetch their first routed unit into L2 before the plan exists (a guess from
+    the availability input).  The results must not depend on it: prefetch on
+    (128 MB budget, the default), off, and a budget of one k tile, against the
+    oracle."""
+    ops = _ops()
+    wl = _workload(h, e, k, f, s, n, seed=n + e, avail_p=avail_p)
+    avail = None if wl.mask is None else wl.mask.to(torch.float32)
+    outs = []
+    try:
+        for mb in (128, 0, 1):
+            ops.set_option("gateup_prefetch_mb", mb)
+            outs.append(_np(_run(wl, k, True, avail=avail)["y"]))
+            torch.cuda.synchronize()
+            ops.check_status()
+    finally:
+        ops.set_option("gateup_prefetch_mb", 128)
+    on, off, small = outs
+    assert O.rel_l2(on, off) <= 1e-3
+    assert O.rel_l2(small, off) <= 1e-3
+    emu, *_ = _oracle(wl, k, True, avail=avail, emulate=True)
+    assert O.rel_l2(on, emu) <= 3e-3
