@@ -258,6 +258,9 @@ def test_decode_loop_replay(tmp_path, monkeypatch, policy):
         mgr.warm_up([0, 1])
         for step in range(6):
             if prev_lp is not None:
+                # the previous step's kernels are done: the timed region holds the two
+                # read-backs of the predictions and the queueing, not a wait on the GPU
+                torch.cuda.synchronize()
                 t0 = time.monotonic()
                 ram_ids = sorted({e for ids in mgr.predicted_experts(prev_lp) for e in ids})
                 mgr.prefetch_experts_to_ram(ram_ids)
