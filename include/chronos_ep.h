@@ -60,6 +60,14 @@ typedef struct ChronosEpDispatchArgs {
                                   each rank) */
     float* shared_weight;      /* [N, k] out: w * (1 - a), the shared experts' share */
     int32_t* scratch;          /* [N*k] int32 scratch */
+    int64_t seg_rows;          /* 0: rows packed (rank g's rows follow rank g-1's).  > 0 (one
+                                  chunk): fixed all-to-all segments, rank g's rows at
+                                  [g * seg_rows, g * seg_rows + send_counts[g]); the rest of
+                                  each segment gets padding metadata (expert -1, weight 0) and
+                                  unspecified x rows.  seg_rows >= N (deduplicated) or
+                                  N * min(k, E/G); send_x and send_meta then hold G * seg_rows
+                                  rows.  With equal splits no host needs the counts before the
+                                  exchange. */
 } ChronosEpDispatchArgs;
 
 /* Builds the send buffers of one rank: rows are grouped by (expert chunk,

@@ -16,7 +16,8 @@ same arguments and results as ``project_chronos_b200.ops``:
   unspecified and nothing downstream depends on it.  ``dedup``: one row per
   (token, destination rank), opened by the token's first available selection
   there, metadata [P, 2] = that rank's selections in choice order, padded with
-  (-1, 0.0);
+  (-1, 0.0); ``seg_rows`` > 0: rank g's rows start at g * seg_rows, the rest of
+  each segment is padding metadata (fixed all-to-all splits);
 * ``moe_forward`` — the blended layer (``moe_oracle.moe_forward``) on pre-routed
   selections, with ``slot_of_expert < 0`` meaning a = 0;
 * ``ep_combine``  — y_t = y_shared_t + sum_j rows[pair_slot(t, j)].
@@ -49,7 +50,8 @@ class CpuEpBackend:
                     probs=torch.from_numpy(probs) if want_probs else None, counts=None, mass=None)
 
     @staticmethod
-    def ep_dispatch(x, topk_idx, topk_weight, num_experts, world_size, avail=None, num_chunks=1, dedup=False):
+    def ep_dispatch(x, topk_idx, topk_weight, num_experts, world_size, avail=None, num_chunks=1, dedup=False,
+                    seg_rows=0):
         xn = x.detach()
         idx = topk_idx.to(torch.int64).numpy()
         wt = topk_weight.to(torch.float32).numpy()
@@ -73,9 +75,16 @@ class CpuEpBackend:
                             sent[t, j] = False
                         seen.add(dest[t, j])
         counts = np.array([int(np.sum(sent & (key == q))) for q in range(num_chunks * world_size)], np.int32)
-        offs = np.concatenate([[0], np.cumsum(counts)[:-1]]).astype(np.int64)
-        send_x = torch.zeros(n * k, xn.shape[1], dtype=xn.dtype)
-        meta = np.zeros((n * k, pairs, 2), np.int32)
+        seg_rows = int(seg_rows)
+        if seg_rows > 0:
+            assert num_chunks == 1 and counts.max(initial=0) <= seg_rows
+            offs = np.arange(world_size, dtype=np.int64) * seg_rows
+            rows = world_size * seg_rows
+        else:
+            offs = np.concatenate([[0], np.cumsum(counts)[:-1]]).astype(np.int64)
+            rows = n * k
+        send_x = torch.zeros(rows, xn.shape[1], dtype=xn.dtype)
+        meta = np.zeros((rows, pairs, 2), np.int32)
         meta[:, :, 0] = -1
         pair_slot = np.full(n * k, -1, np.int32)
         fill = offs.copy()

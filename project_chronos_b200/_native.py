@@ -124,6 +124,7 @@ class ChronosEpDispatchArgs(ctypes.Structure):
         ("pair_slot", ctypes.c_void_p),
         ("shared_weight", ctypes.c_void_p),
         ("scratch", ctypes.c_void_p),
+        ("seg_rows", ctypes.c_int64),
     ]
 
 

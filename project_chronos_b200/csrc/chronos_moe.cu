@@ -1276,13 +1276,16 @@ int ep_dispatch_impl(const ChronosEpDispatchArgs* a, cudaStream_t st) {
     p.send_meta = a->send_meta;
     p.pair_slot = a->pair_slot;
     p.shared_w = a->shared_weight;
+    p.seg_rows = a->seg_rows > 0 ? a->seg_rows : 0;
     CHRONOS_CUDA_CHECK(cudaMemsetAsync(a->send_counts, 0, sizeof(int32_t) * a->world_size * chunks, st));
     const int64_t pairs = p.n * p.k;
-    if (pairs == 0) return CHRONOS_OK;
-    const unsigned cb = static_cast<unsigned>((pairs + kEpPackThreads - 1) / kEpPackThreads);
+    // no selections: nothing to send, unless fixed segments need their padding metadata
+    if (pairs == 0 && p.seg_rows == 0) return CHRONOS_OK;
+    const int64_t work = std::max<int64_t>(pairs, 1);
+    const unsigned cb = static_cast<unsigned>((work + kEpPackThreads - 1) / kEpPackThreads);
     CHRONOS_CUDA_CHECK(launch_kernel(ep_count_kernel, dim3(cb), dim3(kEpPackThreads), 0, st, false, p));
     const int64_t wpb = kEpPackThreads / 32;
-    const unsigned pb = static_cast<unsigned>((pairs + wpb - 1) / wpb);
+    const unsigned pb = static_cast<unsigned>((work + wpb - 1) / wpb);
     CHRONOS_CUDA_CHECK(launch_kernel(ep_pack_kernel<T>, dim3(pb), dim3(kEpPackThreads), 0, st, true, p));
     return CHRONOS_OK;
 }
@@ -1329,6 +1332,16 @@ extern "C" int chronos_ep_dispatch(const ChronosEpDispatchArgs* a, void* stream)
                     "min(top_k %d, experts per rank %d) <= meta_pairs <= %d", a->meta_pairs, a->top_k,
                     a->num_experts / a->world_size, kMaxTopKEp);
     if (a->send_counts == nullptr) return fail(CHRONOS_ERR_INVALID_ARG, "send_counts is required");
+    if (a->seg_rows < 0 ||
+        (a->seg_rows > 0 &&
+         (a->num_chunks > 1 ||
+          a->seg_rows < a->num_tokens * (a->meta_pairs > 1 ? 1 : std::min(a->top_k, a->num_experts / a->world_size)) ||
+          a->seg_rows * a->world_size > (int64_t(1) << 31) - 1)))
+        return fail(CHRONOS_ERR_INVALID_ARG, "seg_rows %lld: fixed segments need one expert chunk and room for "
+                    "every row a rank can receive (num_tokens, or num_tokens * min(top_k, experts per rank) "
+                    "without deduplication)", static_cast<long long>(a->seg_rows));
+    if (a->seg_rows > 0 && a->send_meta == nullptr)
+        return fail(CHRONOS_ERR_INVALID_ARG, "send_meta is required with fixed segments");
     if (a->num_tokens > 0 &&
         (a->x == nullptr || a->topk_idx == nullptr || a->topk_weight == nullptr || a->send_x == nullptr ||
          a->send_meta == nullptr || a->pair_slot == nullptr ||

@@ -8,7 +8,8 @@
 //                    position among those bound for (expert chunk, rank e/epr)
 //                    (global atomics on C*G counters, zeroed by the caller);
 //   ep_pack_kernel   one warp per (token, choice): send row = prefix of the
-//                    counts + position; metadata (local expert, w*a) and the x
+//                    counts + position (or, with fixed segments, rank * seg_rows
+//                    + position); metadata (local expert, w*a) and the x
 //                    row copied with 16-byte vectors, every load of a lane
 //                    issued before its stores.
 // With `pairs` > 1 (one expert chunk) the rows are deduplicated: one send row
@@ -39,6 +40,9 @@ struct EpParams {
     int chunk_experts;      // local experts per chunk (epr / chunks)
     int pairs;              // > 1: one send row per (token, destination rank) carrying up to
                             // `pairs` selections (deduplicated); 1: one row per selection
+    int64_t seg_rows;       // > 0 (one chunk): rank g's rows start at row g * seg_rows (fixed
+                            // all-to-all splits); the unused rows of each segment get padding
+                            // metadata.  0: rows packed by the prefix sums of the counts
     const int32_t* topk_idx;
     const float* topk_w;
     const float* avail;
@@ -99,7 +103,22 @@ __global__ void __launch_bounds__(kEpPackThreads) ep_pack_kernel(EpParams p) {
         }
         s_off[lane] = v - c;
     }
+    if (p.seg_rows > 0 && tid < 32) s_off[lane] = lane < p.g ? static_cast<int>(lane * p.seg_rows) : 0;
     __syncthreads();
+    if (p.seg_rows > 0) {
+        // padding metadata (expert -1, weight 0) for the rows of each segment past its count
+        const int64_t total = p.g * p.seg_rows;
+        const int64_t stride = static_cast<int64_t>(gridDim.x) * kEpPackThreads;
+        for (int64_t r = static_cast<int64_t>(blockIdx.x) * kEpPackThreads + tid; r < total; r += stride) {
+            const int g = static_cast<int>(r / p.seg_rows);
+            if (r - g * p.seg_rows < p.counts[g]) continue;
+            int32_t* m = p.send_meta + 2 * r * p.pairs;
+            for (int q = 0; q < p.pairs; ++q) {
+                m[2 * q] = -1;
+                m[2 * q + 1] = __float_as_int(0.0f);
+            }
+        }
+    }
     const int64_t gw = static_cast<int64_t>(blockIdx.x) * (kEpPackThreads / 32) + (tid >> 5);
     if (gw >= p.n * p.k) return;
     const int ps = p.pos[gw];

@@ -131,9 +131,12 @@ __host__ __device__ constexpr int tc_stage_row_bytes(bool gateup) {
 // Dynamic shared memory of one CTA: the per-CTA limit (227 KB) minus the
 // 1024-byte alignment slack, the barriers (256 B) and the per-unit slot tables.
 __host__ __device__ constexpr int tc_ring_budget(int bn) { return 232448 - 1024 - 256 - 4 * bn * 4; }
+// At most kTcMaxStages stages: the barrier block (256 B) holds 2 * stages + 5
+// mbarriers and the CTA's flag words.
+constexpr int kTcMaxStages = 8;
 __host__ __device__ constexpr int tc_stages_with(int bn, bool gateup, int sub) {
-    return (tc_ring_budget(bn) - sub * tc_stage_row_bytes(gateup)) / tc_stage_bytes(bn, gateup) > 8
-               ? 8
+    return (tc_ring_budget(bn) - sub * tc_stage_row_bytes(gateup)) / tc_stage_bytes(bn, gateup) > kTcMaxStages
+               ? kTcMaxStages
                : (tc_ring_budget(bn) - sub * tc_stage_row_bytes(gateup)) / tc_stage_bytes(bn, gateup);
 }
 // Rows staged at a time.  Gate/up: the most (128, 64, 32 or 16, at most BN)
@@ -252,6 +255,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     static_assert(2 * ACC_COLS <= 512, "two accumulator buffers must fit in TMEM");
     static_assert(STAGES >= 2, "shared memory holds fewer than two pipeline stages");
     static_assert(tc_smem_bytes(BN, GATEUP) <= 232448, "shared memory over the per-CTA limit");
+    static_assert((2 * STAGES + 5) * 8 + 20 <= 256, "barriers and flag words over their 256 bytes");
 
     extern __shared__ uint8_t tc_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(

@@ -14,7 +14,10 @@ call instead):
 3. all-to-all of the counts (the one host synchronisation: NCCL's variable
    all-to-all needs the split sizes), then of the rows and metadata (NCCL over
    NVLink), in C chunks of each rank's experts, all issued at once; the shared
-   term (1 + sum w(1-a)) * mean_j Shared_j(x) is computed while the rows travel;
+   term (1 + sum w(1-a)) * mean_j Shared_j(x) is computed while the rows travel.
+   With ``segment_rows`` > 0 (the same on every rank) the send buffers hold one
+   fixed segment of that many rows per destination and both exchanges use equal
+   splits: no counts, no host synchronisation, padding rows (expert -1) travel;
 4. as each chunk lands, its rows through the grouped expert kernels
    (pre-routed, k = 1): w*a*SwiGLU_e(x) per row (with C > 1 on at most
    ``gemm_ctas`` SMs, leaving the rest to the exchange);
@@ -84,6 +87,11 @@ class ExpertParallelMoE(nn.Module):
         # unchunked exchange: one row per (token, destination rank), every selection of
         # the token on that rank in the row's metadata (False: one row per selection)
         self.dedup = True
+        # > 0: fixed all-to-all segments of this many rows per destination rank (every
+        # rank must use the same value, and a forward's rows per destination must fit:
+        # its token count when deduplicated); 0: split sizes exchanged and read on the host
+        self.segment_rows = 0
+        self.last_send_counts_dev = None
         # optional phase timing: a list that each forward appends
         # {phase: torch.cuda.Event} to (events on the compute stream)
         self.phase_events = None
@@ -132,6 +140,13 @@ class ExpertParallelMoE(nn.Module):
             stack(sh, "up_proj") if sh else None, stack(sh, "down_proj") if sh else None,
             group=group, backend=backend, local=True)
 
+    def read_send_counts(self):
+        """Rows sent to each rank by the last forward (a host read of the device
+        counts when the exchange used fixed segments)."""
+        if self.last_send_counts is not None or self.last_send_counts_dev is None:
+            return self.last_send_counts
+        return [int(v) for v in self.last_send_counts_dev.reshape(-1).cpu().tolist()]
+
     # ------------------------------------------------------------------
     def _exchange(self, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits, async_op=False):
         if self.world == 1:  # a single rank sends everything to itself
@@ -178,10 +193,15 @@ class ExpertParallelMoE(nn.Module):
                 if self.experts_per_rank % c == 0)
         # with chunks, the exchange runs beside the expert GEMMs: leave it SMs
         max_ctas = 0 if C == 1 else self.gemm_ctas
+        seg = int(self.segment_rows) if C == 1 else 0
+        if seg:
+            need = xf.shape[0] if self.dedup else xf.shape[0] * min(k, self.experts_per_rank)
+            if need > seg:
+                raise ValueError(f"{need} rows per destination do not fit segment_rows {seg}")
         # one row per (token, destination rank) when unchunked: each x row crosses
         # to a rank once, carrying all of the token's selections there
         d = be.ep_dispatch(xf, r["topk_idx"], r["topk_weight"], E, G, avail=avail, num_chunks=C,
-                           dedup=self.dedup)
+                           dedup=self.dedup, seg_rows=seg)
         P = int(d.get("pairs", 1))
 
         mark("dispatched")
@@ -203,15 +223,22 @@ class ExpertParallelMoE(nn.Module):
                     slot_of_expert=no_slot, want_probs=False,
                     topk=[r["topk_idx"], d["shared_weight"]])["y"]
                 mark("shared_done")
-        # 3: counts [C, G] -> per destination [G, C]; one host sync for every split size
-        send_gc = d["send_counts"].reshape(C, G).t().contiguous()
-        recv_gc = torch.empty_like(send_gc)
-        self._exchange(recv_gc, send_gc, None, None)
-        both = torch.cat([send_gc.reshape(-1), recv_gc.reshape(-1)]).cpu().tolist()
-        sc = [[both[g * C + c] for g in range(G)] for c in range(C)]          # sent, [c][g]
-        rc = [[both[G * C + g * C + c] for g in range(G)] for c in range(C)]  # received, [c][g]
-        self.last_send_counts = [sum(sc[c][g] for c in range(C)) for g in range(G)]
-        self.last_recv_counts = [sum(rc[c][g] for c in range(C)) for g in range(G)]
+        if seg:
+            # 3 (fixed segments): equal splits, nothing for the host to wait for
+            sc = rc = [[seg] * G]
+            self.last_send_counts = self.last_recv_counts = None
+            self.last_send_counts_dev = d["send_counts"]
+        else:
+            # 3: counts [C, G] -> per destination [G, C]; one host sync for every split size
+            send_gc = d["send_counts"].reshape(C, G).t().contiguous()
+            recv_gc = torch.empty_like(send_gc)
+            self._exchange(recv_gc, send_gc, None, None)
+            both = torch.cat([send_gc.reshape(-1), recv_gc.reshape(-1)]).cpu().tolist()
+            sc = [[both[g * C + c] for g in range(G)] for c in range(C)]          # sent, [c][g]
+            rc = [[both[G * C + g * C + c] for g in range(G)] for c in range(C)]  # received, [c][g]
+            self.last_send_counts = [sum(sc[c][g] for c in range(C)) for g in range(G)]
+            self.last_recv_counts = [sum(rc[c][g] for c in range(C)) for g in range(G)]
+            self.last_send_counts_dev = None
         send_off = [0]
         for c in range(C):
             send_off.append(send_off[-1] + sum(sc[c]))

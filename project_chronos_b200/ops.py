@@ -342,7 +342,7 @@ def moe_route(x: torch.Tensor, router_w: torch.Tensor, top_k: int, norm_topk: bo
 
 def ep_dispatch(x: torch.Tensor, topk_idx: torch.Tensor, topk_weight: torch.Tensor, num_experts: int,
                 world_size: int, avail: Optional[torch.Tensor] = None, num_chunks: int = 1,
-                dedup: bool = False) -> dict:
+                dedup: bool = False, seg_rows: int = 0) -> dict:
     """Send buffers of one rank for expert parallelism (include/chronos_ep.h).
 
     Rows are ordered by (expert chunk, destination rank): each rank's E/G local
@@ -351,7 +351,10 @@ def ep_dispatch(x: torch.Tensor, topk_idx: torch.Tensor, topk_weight: torch.Tens
     (local expert id, fp32 bits of w*a), pair_slot [N*k] int32, shared_weight [N, k]
     fp32, pairs P); the first ``send_counts.sum()`` rows of the send buffers are used.
     ``dedup`` (one chunk): one row per (token, destination rank), P = min(k, E/G)
-    selections per row (padding: expert -1); else one row per selection, P = 1."""
+    selections per row (padding: expert -1); else one row per selection, P = 1.
+    ``seg_rows`` > 0 (one chunk): fixed segments, rank g's rows at g * seg_rows (the
+    buffers hold world_size * seg_rows rows, unused rows carry padding metadata), so
+    an all-to-all with equal splits needs no counts on the host."""
     _check_cuda(x, topk_idx, topk_weight, avail)
     x = x.contiguous()
     n, h = x.shape
@@ -364,9 +367,11 @@ def ep_dispatch(x: torch.Tensor, topk_idx: torch.Tensor, topk_weight: torch.Tens
     av = None if avail is None else avail.to(device=dev, dtype=torch.float32).contiguous()
     num_chunks = max(1, int(num_chunks))
     pairs = min(k, int(num_experts) // int(world_size)) if dedup and num_chunks == 1 else 1
+    seg_rows = max(0, int(seg_rows))
+    rows = int(world_size) * seg_rows if seg_rows else n * k
     out = dict(send_counts=torch.empty(num_chunks, world_size, dtype=torch.int32, device=dev),
-               send_x=torch.empty(n * k, h, dtype=x.dtype, device=dev),
-               send_meta=torch.empty(n * k, pairs, 2, dtype=torch.int32, device=dev),
+               send_x=torch.empty(rows, h, dtype=x.dtype, device=dev),
+               send_meta=torch.empty(rows, pairs, 2, dtype=torch.int32, device=dev),
                pair_slot=torch.empty(n * k, dtype=torch.int32, device=dev),
                shared_weight=torch.empty(n, k, dtype=torch.float32, device=dev))
     scratch = torch.empty(max(n * k, 1), dtype=torch.int32, device=dev)
@@ -376,7 +381,7 @@ def ep_dispatch(x: torch.Tensor, topk_idx: torch.Tensor, topk_weight: torch.Tens
         avail=_ptr(av), send_counts=_ptr(out["send_counts"]), send_x=_ptr(out["send_x"]),
         send_meta=_ptr(out["send_meta"]),
         pair_slot=_ptr(out["pair_slot"]), shared_weight=_ptr(out["shared_weight"]),
-        scratch=_ptr(scratch))
+        scratch=_ptr(scratch), seg_rows=seg_rows)
     lib = N.load_library()
     stream = torch.cuda.current_stream(dev).cuda_stream
     with torch.cuda.device(dev):

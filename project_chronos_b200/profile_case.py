@@ -7,6 +7,7 @@
     python -m project_chronos_b200.profile_case --workload model --tokens 32 --calls 3
     python -m project_chronos_b200.profile_case --workload attn --kind sw --tokens 32 --calls 20
     python -m project_chronos_b200.profile_case --workload lookahead --tokens 32 --calls 20
+    python -m project_chronos_b200.profile_case --workload model-pieces --tokens 32
 
 Builds the named synthetic workload on cuda:0 (``synthetic.WORKLOADS``),
 calls ``ops.moe_forward`` ``--calls`` times with an L2 flush (256 MB write)
@@ -27,7 +28,7 @@ from . import ops, synthetic as syn
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--workload", default="prefill",
-                    choices=sorted(syn.WORKLOADS) + ["model", "attn", "lookahead"])
+                    choices=sorted(syn.WORKLOADS) + ["model", "model-pieces", "attn", "lookahead"])
     ap.add_argument("--kind", default="sw", choices=["sw", "mla"], help="attention kind (--workload attn)")
     ap.add_argument("--positions", type=int, default=516, help="cached positions (--workload attn)")
     ap.add_argument("--tokens", type=int, default=None)
@@ -48,6 +49,8 @@ def main(argv=None) -> int:
         return _ep(args, dev)
     if args.workload == "model":
         return _model(args, dev)
+    if args.workload == "model-pieces":
+        return _model_pieces(args, dev)
     if args.workload == "attn":
         return _attn(args, dev)
     if args.workload == "lookahead":
@@ -104,6 +107,108 @@ def _model(args, dev) -> int:
             nxt = torch.argmax(out.logits[:, -1], dim=-1).view(-1, 1)
     ops.check_status(dev)
     print(f"model batch={b} steps={args.calls} avg_ms={total_ms / args.calls:.4f}")
+    return 0
+
+
+def _graph_chain_us(fn, reps: int = 20, iters: int = 20) -> float:
+    """Device time of one ``fn()`` inside a CUDA graph of ``reps`` back-to-back calls
+    (launch gaps included, as in a graph-replayed decode step), in us."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(reps):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        graph.replay()
+    e.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(e) * 1e3 / (iters * reps)
+
+
+def _model_pieces(args, dev) -> int:
+    """The 8-layer model's graph-replayed decode step (synthetic.DECODE_MODEL, a
+    512-token prompt of --tokens rows), then each piece of a step alone as a chain
+    of graph-captured calls: the residual add + RMSNorm (fp32 MoE accumulator or
+    bf16 input), the input projection and o_proj (cuBLAS), the two attention
+    decode kernels, one MoE layer (fp32 hand-off, and with its finalize), one whole
+    sliding-window block, the lookahead router, the LM head and the greedy pick."""
+    import json
+    import types
+    import torch.nn.functional as F
+    from .model import ChronosForCausalLM, GraphedDecoder
+    cfg = types.SimpleNamespace(**syn.DECODE_MODEL)
+    lm = ChronosForCausalLM.on_device(cfg, dev, torch.bfloat16)
+    syn.init_model_(lm, args.seed, dev)
+    lm.eval()
+    B, H = args.tokens or 32, cfg.hidden_size
+    g = torch.Generator(device=dev).manual_seed(args.seed + 1)
+    ids = torch.randint(0, cfg.vocab_size, (B, 512), generator=g, device=dev)
+    res = {}
+    with torch.no_grad():
+        out, _ = lm(ids, use_cache=True, cache_capacity=512 + 200)
+        cache = out.past_key_values
+        dec = GraphedDecoder(lm, cache)
+        for _ in range(3):
+            dec.step()
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(50):
+            dec.step()
+        e.record()
+        torch.cuda.synchronize()
+        res["step"] = a.elapsed_time(e) * 1e3 / 50
+        m = lm.model
+        L0, L1 = m.layers[0], m.layers[1]
+        hid = torch.randn(B, 1, H, generator=g, device=dev, dtype=torch.bfloat16)
+        acc = torch.randn(B, 1, H, generator=g, device=dev, dtype=torch.float32)
+        bf = torch.randn(B, 1, H, generator=g, device=dev, dtype=torch.bfloat16)
+        x2 = bf.view(B, H)
+        cos, sin = m.freqs_cos, m.freqs_sin
+        a0, a1 = L0.self_attn, L1.self_attn
+        p0, p1 = F.linear(x2, a0._in_weight()), F.linear(x2, a1._in_weight())
+        mask = dec.masks[1]
+        res["norm_fp32_acc"] = _graph_chain_us(lambda: L1.input_layernorm(acc, residual=hid, sum_out=hid))
+        res["norm_bf16"] = _graph_chain_us(lambda: L1.post_attention_layernorm(bf, residual=hid, sum_out=hid))
+        res["in_proj_sw"] = _graph_chain_us(lambda: F.linear(x2, a1._in_weight()))
+        res["in_proj_mla"] = _graph_chain_us(lambda: F.linear(x2, a0._in_weight()))
+        res["o_proj"] = _graph_chain_us(lambda: F.linear(x2, a1.o_proj.weight))
+        res["attn_sw"] = _graph_chain_us(lambda: ops.attn_decode(
+            "sw", p1, cache.pos, cos, sin, cache.a[1], cache.b[1], a1.n_heads, a1.n_kv_heads, a1.head_dim,
+            a1.head_dim, 0, a1.window_size, a1.eps, a1.q_norm.weight, a1.k_norm.weight))
+        res["attn_mla"] = _graph_chain_us(lambda: ops.attn_decode(
+            "mla", p0, cache.pos, cos, sin, cache.a[0], cache.b[0], a0.n_heads, a0.n_kv_heads, a0.head_dim,
+            a0.rope_dim, a0.kv_latent_dim, 0, a0.eps, a0.q_nope_norm.weight, a0.q_rope_norm.weight,
+            norm_kv=a0.kv_down_norm.weight, w_krope=a0.k_rope_proj.weight, w_knope=a0.k_nope_proj.weight,
+            w_v=a0.v_proj.weight))
+        res["moe_fp32_handoff"] = _graph_chain_us(lambda: L1.mlp.forward_acc(bf, mask), reps=8)
+        res["moe_with_finalize"] = _graph_chain_us(lambda: L1.mlp(bf, mask), reps=8)
+
+        def block():
+            h_in = L1.input_layernorm(acc, residual=hid, sum_out=hid)
+            at = a1.decode(h_in.view(B, H), cos, sin, cache).view(B, 1, H)
+            mi = L1.post_attention_layernorm(at, residual=hid, sum_out=hid)
+            return L1.mlp.forward_acc(mi, mask)
+        res["block_sw"] = _graph_chain_us(block, reps=8)
+        res["lookahead"] = _graph_chain_us(lambda: m.lookahead_router(hid), reps=8)
+        res["lm_head"] = _graph_chain_us(lambda: F.linear(x2, lm.lm_head.weight))
+        logits = F.linear(x2, lm.lm_head.weight)
+        nxt = torch.empty(B, dtype=torch.long, device=dev)
+        res["argmax"] = _graph_chain_us(lambda: ops.argmax_rows(logits, out=nxt))
+    ops.check_status(dev)
+    print(json.dumps({k + "_us": round(v, 2) for k, v in res.items()}))
     return 0
 
 

@@ -29,6 +29,14 @@ def _cfg(E, k, H, F, S):
                                  moe_intermediate_size=F, num_shared_experts=S, norm_topk_prob=True)
 
 
+def _ref(x, w, k, mask):
+    from oracle import moe_oracle as O
+    ref, _, _, _ = O.moe_forward(x.numpy(), w["router"].numpy(), w["gate"].numpy(), w["up"].numpy(),
+                                 w["down"].numpy(), w["sh_gate"].numpy(), w["sh_up"].numpy(),
+                                 w["sh_down"].numpy(), k, True, avail=None if mask is None else mask.numpy())
+    return ref
+
+
 def cpu_rank(rank, world, port, q, scenario):
     import numpy as np
     import torch
@@ -52,7 +60,12 @@ def cpu_rank(rank, world, port, q, scenario):
                                            w["down"], w["sh_gate"], w["sh_up"], w["sh_down"],
                                            backend=CpuEpBackend())
         m.chunks = 3 if scenario == "mask" else 1
+        if scenario == "fixed":
+            m.segment_rows = 16   # every rank's tokens (at most 14) fit one segment
         y = m(x, available_expert_mask=mask)
+        if scenario == "fixed":
+            q.put(("ok", rank, O.rel_l2(y.numpy(), _ref(x, w, k, mask)), m.read_send_counts(), None))
+            return
         ref, _, _, _ = O.moe_forward(x.numpy(), w["router"].numpy(), w["gate"].numpy(),
                                      w["up"].numpy(), w["down"].numpy(), w["sh_gate"].numpy(),
                                      w["sh_up"].numpy(), w["sh_down"].numpy(), k, True,
@@ -85,6 +98,7 @@ def gpu_rank(rank, world, port, q, cfg_d):
         x = torch.randn(n, H, generator=torch.Generator().manual_seed(100 + rank)).to(dev, dt)
         m = ExpertParallelMoE.from_stacked(_cfg(E, k, H, F, S), w["router"], w["gate"], w["up"],
                                            w["down"], w["sh_gate"], w["sh_up"], w["sh_down"])
+        m.segment_rows = int(cfg_d.get("seg", 0))
         y = m(x)
         full = ops.moe_forward(x, w["router"], w["gate"], w["up"], w["down"], w["sh_gate"], w["sh_up"],
                                w["sh_down"], k, True, want_probs=False)["y"]
@@ -92,7 +106,10 @@ def gpu_rank(rank, world, port, q, cfg_d):
         ops.check_status(dev)
         rel = (torch.linalg.vector_norm(y.float() - full.float()) /
                torch.linalg.vector_norm(full.float())).item()
-        q.put(("ok", rank, rel, m.last_send_counts, m.last_recv_counts))
+        if m.segment_rows:
+            q.put(("ok", rank, rel, m.read_send_counts(), None))
+        else:
+            q.put(("ok", rank, rel, m.last_send_counts, m.last_recv_counts))
     except Exception:
         q.put(("error", rank, traceback.format_exc(), None, None))
     finally:

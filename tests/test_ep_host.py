@@ -66,6 +66,17 @@ def test_ep_four_ranks_deduplicated_rows_match_single_device_oracle():
             assert res[i][3][j] == res[j][4][i]
 
 
+@pytest.mark.parametrize("world", [2, 4])
+def test_fixed_segments_need_no_counts_and_match_the_oracle(world):
+    """Fixed all-to-all segments (equal splits, padding rows travel): no count
+    exchange, every rank's output equals the single-device oracle."""
+    res = _run("fixed", world=world)
+    for status, rank, val, sc, rc in res:
+        assert status == "ok", (rank, val)
+        assert val < 1e-5, (rank, val)
+        assert len(sc) == world and all(0 <= c <= 16 for c in sc)
+
+
 def test_injected_rank_failure_ends_the_collective_with_an_error():
     res = _run("fail", timeout=90)
     by_rank = {r[1]: r for r in res}

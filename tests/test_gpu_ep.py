@@ -75,6 +75,42 @@ def test_dispatch_and_combine_match_oracle(dtype, world, n, chunks, dedup):
     assert torch.equal(y.cpu(), want)
 
 
+@pytest.mark.parametrize("world,n,dedup,seg", [(2, 33, True, 40), (4, 300, True, 300), (8, 300, True, 512),
+                                                (2, 33, False, 33 * 4), (4, 0, True, 8)])
+def test_fixed_segments_match_oracle(world, n, dedup, seg):
+    """Fixed all-to-all segments: rank g's rows start at g * seg, in the oracle's
+    rows (matched through pair_slot), and every row past a segment's count carries
+    padding metadata (expert -1, weight 0)."""
+    from oracle.ep_oracle import CpuEpBackend
+    from project_chronos_b200 import ops
+    E, k, H = 16, 4, 256
+    g = torch.Generator().manual_seed(world * 77 + n)
+    x = torch.randn(max(n, 1), H, generator=g).to(DEV, torch.bfloat16)[:n]
+    router = (torch.randn(E, H, generator=g) * 0.05).to(DEV, torch.bfloat16)
+    avail = (torch.rand(E, generator=g) > 0.25).float()
+    r = _route(x, router, k) if n else dict(topk_idx=torch.zeros(0, k, dtype=torch.int32, device=DEV),
+                                             topk_weight=torch.zeros(0, k, device=DEV))
+    d = ops.ep_dispatch(x, r["topk_idx"], r["topk_weight"], E, world, avail=avail.to(DEV), dedup=dedup,
+                        seg_rows=seg)
+    ref = CpuEpBackend.ep_dispatch(x.cpu(), r["topk_idx"].cpu(), r["topk_weight"].cpu(), E, world, avail,
+                                   dedup=dedup, seg_rows=seg)
+    assert d["send_x"].shape[0] == world * seg and d["send_meta"].shape[0] == world * seg
+    counts = d["send_counts"].cpu().view(-1)
+    assert counts.tolist() == ref["send_counts"].view(-1).tolist()
+    ps = d["pair_slot"].cpu()
+    sent = ps >= 0
+    assert torch.equal(sent, ref["pair_slot"] >= 0)
+    slots = ps[sent].long()
+    assert torch.equal(d["send_x"].cpu()[slots], ref["send_x"][ref["pair_slot"][sent].long()])
+    assert torch.equal(d["send_meta"].cpu()[slots], ref["send_meta"][ref["pair_slot"][sent].long()])
+    meta = d["send_meta"].cpu()
+    for gg in range(world):
+        used = sorted(v - gg * seg for v in slots.tolist() if gg * seg <= v < (gg + 1) * seg)
+        assert used == list(range(int(counts[gg])))
+        pad = meta[gg * seg + int(counts[gg]):(gg + 1) * seg]
+        assert bool((pad[..., 0] == -1).all()) and bool((pad[..., 1] == 0).all())
+
+
 @pytest.mark.parametrize("dispatch", [False, True])
 @pytest.mark.parametrize("masked", [False, True])
 def test_single_rank_layer_matches_single_device(masked, dispatch):
@@ -97,16 +133,28 @@ def test_single_rank_layer_matches_single_device(masked, dispatch):
     rel = (torch.linalg.vector_norm(y.float() - full.float()) / torch.linalg.vector_norm(full.float())).item()
     assert rel <= 1e-2
     assert m.last_send_counts == m.last_recv_counts
+    if dispatch:
+        # the same through fixed segments (padding rows travel, no host read of the counts)
+        sent = m.last_send_counts
+        m.segment_rows = n + 8
+        y2 = m(x.view(2, n // 2, H), available_expert_mask=mask).view(n, H)
+        torch.cuda.synchronize()
+        ops.check_status(torch.device(DEV))
+        rel2 = (torch.linalg.vector_norm(y2.float() - full.float()) /
+                torch.linalg.vector_norm(full.float())).item()
+        assert rel2 <= 1e-2
+        assert m.last_send_counts is None and m.read_send_counts() == sent
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_ranks_nccl_match_single_device():
+@pytest.mark.parametrize("seg", [0, 256])
+def test_two_ranks_nccl_match_single_device(seg):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    cfg = dict(E=16, k=4, H=512, F=256, S=1, n=200)
+    cfg = dict(E=16, k=4, H=512, F=256, S=1, n=200, seg=seg)
     procs = [ctx.Process(target=_ep_worker.gpu_rank, args=(r, 2, port, q, cfg)) for r in range(2)]
     for p in procs:
         p.start()
@@ -124,7 +172,8 @@ def test_two_ranks_nccl_match_single_device():
     for status, rank, val, sc, rc in res:
         assert status == "ok", val
         assert val <= 1e-2, (rank, val)
-    assert res[0][3][1] == res[1][4][0] and res[1][3][0] == res[0][4][1]
+    if not seg:
+        assert res[0][3][1] == res[1][4][0] and res[1][3][0] == res[0][4][1]
 
 
 def test_mask_is_the_arithmetic_availability_in_eval():
