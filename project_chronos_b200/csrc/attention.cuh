@@ -469,6 +469,7 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) mla_decode_ker
     extern __shared__ __align__(16) float msm[];
     cg::cluster_group cluster = cg::this_cluster();
     pdl_wait();   // launched early behind the projection that writes proj (programmatic launch)
+    const int pos = *p.pos;   // first: the rotary rows and the CTA's positions depend on it
     const int splits = p.splits;
     const int sidx = blockIdx.x % splits, g = blockIdx.x / splits, b = blockIdx.y;
     const int nope = p.nope, R = p.rope_dim, L = p.latent, D = p.head_dim, cap = p.cap;
@@ -521,7 +522,6 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) mla_decode_ker
     }
     for (int i = threadIdx.x; i < nope; i += kAttnThreads) wqn[i] = to_f32<T>(static_cast<const T*>(p.norm_q)[i]);
     for (int i = threadIdx.x; i < R; i += kAttnThreads) wqr[i] = to_f32<T>(static_cast<const T*>(p.norm_q2)[i]);
-    const int pos = *p.pos;
     T* out = static_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.heads + g * rep) * D;
     if (pos < 0 || pos >= p.max_len || pos >= p.table_len) {   // outside the cache: no access
         for (int i = threadIdx.x; i < rep * D; i += kAttnThreads) out[i] = from_f32<T>(0.0f);
@@ -630,6 +630,7 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) sw_decode_kern
     extern __shared__ __align__(16) float ssm[];
     cg::cluster_group cluster = cg::this_cluster();
     pdl_wait();   // launched early behind the projection that writes proj (programmatic launch)
+    const int pos = *p.pos;   // first: the rotary rows and the CTA's positions depend on it
     const int splits = p.splits;
     const int sidx = blockIdx.x % splits, g = blockIdx.x / splits, b = blockIdx.y;
     const int D = p.head_dim, W = p.window, cap = p.cap;
@@ -656,7 +657,6 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) sw_decode_kern
         wq[i] = to_f32<T>(static_cast<const T*>(p.norm_q)[i]);
         wk[i] = to_f32<T>(static_cast<const T*>(p.norm_q2)[i]);
     }
-    const int pos = *p.pos;
     T* out = static_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.heads + g * rep) * D;
     const int rpos = pos < W ? pos : W;    // the cache length before this token
     if (pos < 0 || rpos >= p.table_len) {
