@@ -263,13 +263,20 @@ __global__ void __launch_bounds__(kAttnThreads) argmax_rows_kernel(const T* x, i
     }
 }
 
-// Copy `count` elements (a multiple of 8) into shared memory with 16-byte vectors.
+// Start copying `count` elements (a multiple of 16 bytes) into shared memory
+// with 16-byte asynchronous copies (every copy of the block in flight at once);
+// stage_rows_wait() then __syncthreads() make them visible.
 template <typename T>
 __device__ __forceinline__ void stage_rows(T* dst, const T* src, int count) {
     constexpr int EPV = 16 / static_cast<int>(sizeof(T));
-    for (int i = threadIdx.x; i < count / EPV; i += kAttnThreads)
-        reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+    for (int i = threadIdx.x; i < count / EPV; i += kAttnThreads) {
+        const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(reinterpret_cast<uint4*>(dst) + i));
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d),
+                     "l"(reinterpret_cast<const uint4*>(src) + i)
+                     : "memory");
+    }
 }
+__device__ __forceinline__ void stage_rows_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // Lanes per cached row in the weighted sums: one lane per 8-column group,
 // rounded up to a power of two (at least 4), so 32 / LPP rows per warp step.
@@ -540,6 +547,7 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) mla_decode_ker
     prefetch_rows<T>(cache_c, L, t_lo, t_hi, L * static_cast<int>(sizeof(T)));
     prefetch_rows<T>(cache_k + g * R, static_cast<int64_t>(p.kv_heads) * R, t_lo, t_hi,
                      R * static_cast<int>(sizeof(T)));
+    if (p.stage_w) stage_rows_wait();
     __syncthreads();
     // per-head RMSNorms of q_nope and q_rope (each q_rope head then rotated by its
     // warp into tmp [rep][R]), RMSNorm of the latent
@@ -555,20 +563,44 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) mla_decode_ker
         }
     }
     __syncthreads();
-    // k_rope of the new token: k_rope_proj(c), a warp per output (rounded as the bf16 linear rounds)
-    for (int r = warp; r < R; r += kAttnWarps) {
-        float acc = 0.0f;
-        for (int j = lane; j < L; j += 32) acc = fmaf(to_f32<T>(wkr[r * L + j]), cnew[j], acc);
-        acc = warp_sum(acc);
-        if (lane == 0) krn[r] = round_to<T>(acc);
+    // k_rope of the new token: k_rope_proj(c) (rounded as the bf16 linear rounds); a
+    // warp takes 4 output rows at once so their loads and warp sums interleave
+    for (int r0 = warp * 4; r0 < R; r0 += kAttnWarps * 4) {
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int j = lane; j < L; j += 32) {
+            const float c = cnew[j];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                if (r0 + q < R) acc[q] = fmaf(to_f32<T>(wkr[(r0 + q) * L + j]), c, acc[q]);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[q] = warp_sum(acc[q]);
+        if (lane < 4 && r0 + lane < R) {
+            float v = acc[0];
+#pragma unroll
+            for (int q = 1; q < 4; ++q) v = lane == q ? acc[q] : v;
+            krn[r0 + lane] = round_to<T>(v);
+        }
     }
-    // q_abs = W_kn^T q_nope: the key up-projection folded into the query
+    // q_abs = W_kn^T q_nope: the key up-projection folded into the query (an fp32
+    // intermediate); eight terms loaded at a time into two interleaved sums
     for (int i = threadIdx.x; i < rep * L; i += kAttnThreads) {
         const int h = i / L, j = i % L;
         const float* q = qn + h * nope;
-        float acc = 0.0f;
-        for (int d = 0; d < nope; ++d) acc = fmaf(to_f32<T>(wkn[d * L + j]), q[d], acc);
-        qabs[i] = acc;
+        float a0 = 0.0f, a1 = 0.0f;
+        int d = 0;
+        for (; d + 8 <= nope; d += 8) {
+            float w[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) w[u] = to_f32<T>(wkn[(d + u) * L + j]);
+#pragma unroll
+            for (int u = 0; u < 8; u += 2) {
+                a0 = fmaf(w[u], q[d + u], a0);
+                a1 = fmaf(w[u + 1], q[d + u + 1], a1);
+            }
+        }
+        for (; d < nope; ++d) a0 = fmaf(to_f32<T>(wkn[d * L + j]), q[d], a0);
+        qabs[i] = a0 + a1;
     }
     __syncthreads();
     // RoPE at `pos` on the new k_rope: tmp + rep*R [R]
@@ -600,22 +632,35 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) mla_decode_ker
         ctx[i] = v;
     }
     __syncthreads();
-    // out = W_v ctx for this CTA's rows: the value up-projection applied once to the weighted latent
-    for (int d = d0 + warp; d < d1; d += kAttnWarps) {
+    // out = W_v ctx for this CTA's rows: the value up-projection applied once to the
+    // weighted latent; a warp takes two rows at once so their sums interleave
+    for (int d = d0 + 2 * warp; d < d1; d += 2 * kAttnWarps) {
+        const bool two = d + 1 < d1;
         const T* wrow = wv + static_cast<int64_t>(d - d0) * L;
-        float acc[REP];
+        float acc[2][REP];
 #pragma unroll
-        for (int h = 0; h < REP; ++h) acc[h] = 0.0f;
+        for (int h = 0; h < REP; ++h) acc[0][h] = acc[1][h] = 0.0f;
         for (int j = lane; j < L; j += 32) {
-            const float w = to_f32<T>(wrow[j]);
+            const float w0 = to_f32<T>(wrow[j]);
+            const float w1 = two ? to_f32<T>(wrow[L + j]) : 0.0f;
 #pragma unroll
-            for (int h = 0; h < REP; ++h) acc[h] = fmaf(w, ctx[h * L + j], acc[h]);
+            for (int h = 0; h < REP; ++h) {
+                const float c = ctx[h * L + j];
+                acc[0][h] = fmaf(w0, c, acc[0][h]);
+                acc[1][h] = fmaf(w1, c, acc[1][h]);
+            }
         }
 #pragma unroll
         for (int h = 0; h < REP; ++h) {
-            const float v = warp_sum(acc[h]);
-            if (lane == 0) out[h * D + d] = from_f32<T>(v);
+            acc[0][h] = warp_sum(acc[0][h]);
+            acc[1][h] = warp_sum(acc[1][h]);
         }
+        if (lane == 0)
+#pragma unroll
+            for (int h = 0; h < REP; ++h) {
+                out[h * D + d] = from_f32<T>(acc[0][h]);
+                if (two) out[h * D + d + 1] = from_f32<T>(acc[1][h]);
+            }
     }
     cluster.sync();   // no CTA leaves while a peer may still read its partial sums
 }
