@@ -164,10 +164,10 @@ CHRONOS_API int chronos_moe_route(const ChronosMoeArgs* args, void* cuda_stream)
  *
  * No counterpart in the reference (its layer allocates through PyTorch).
  * Some hosts cannot hand this library a workspace: an engine embedding the
- * layer through FFI with no handle on the GPU allocator, a decode loop
- * running inside a CUDA graph whose memory was fixed at capture time, or a
- * real-time server that forbids cudaMalloc after start-up because it
- * synchronises the device and can fail under fragmentation.  This entry point
+ * layer through FFI with no handle on the GPU allocator, a runtime whose
+ * device memory pool is sized once at start-up and handed out to its own
+ * tensors only, or a real-time server that forbids cudaMalloc after start-up
+ * because it synchronises the device and can fail under fragmentation.  This entry point
  * computes exactly what chronos_moe_forward computes, but ignores
  * args->workspace / args->workspace_bytes and uses one scratch array built
  * into the library (CHRONOS_NOALLOC_SCRATCH_BYTES of device memory, reserved

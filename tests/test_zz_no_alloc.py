@@ -1,8 +1,8 @@
 """chronos_moe_forward_noalloc: the layer for callers that cannot allocate GPU memory.
 
 Some hosts cannot give the library a workspace: an engine that embeds the
-layer through FFI without access to the GPU allocator, a decode loop replayed
-inside a CUDA graph whose memory was fixed at capture time, or a real-time
+layer through FFI without access to the GPU allocator, a runtime whose device
+memory pool is sized once at start-up for its own tensors, or a real-time
 server that forbids cudaMalloc after start-up.  This entry point uses a
 scratch array built into the library instead.  The tests call it through the
 C ABI (ctypes), several calls in a row on different inputs, and check each
