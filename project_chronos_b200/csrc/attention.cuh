@@ -362,79 +362,58 @@ __device__ __forceinline__ void weighted_rows(const T* rows, int64_t stride, int
 // q < w1/8 comes from `rows1` (row stride st1, query q1 [REP][w1]), the others
 // from `rows2` (st2, q2 [REP][w2]); the row at `fresh_t` comes from shared
 // memory (f1, f2) instead.  Queries are 16-byte aligned in shared memory.
-template <typename T, int REP, int NP>
+template <typename T, int REP>
 __device__ __forceinline__ void split_scores(const T* rows1, int64_t st1, const float* q1, int w1, const float* f1,
                                              const T* rows2, int64_t st2, const float* q2, int w2,
                                              const float* f2, int t_lo, int t_hi, int fresh_t, float scale,
                                              float* sc, int cap, int warp, int lane) {
     const int g1 = w1 / 8, gall = g1 + w2 / 8, sub = lane & 3;
-    constexpr int kSpan = kAttnWarps * 8;   // positions of one block pass
-    // NP positions per lane and pass, kSpan apart: all rows' loads are issued
-    // before the multiply-adds, and each query slice read from shared memory
-    // serves all of them (NP = 2 pays off when a CTA has more than kSpan positions)
-    for (int base = t_lo + warp * 8; base < t_hi; base += NP * kSpan) {   // uniform per warp
-        int tp[NP];
+    for (int base = t_lo + warp * 8; base < t_hi; base += kAttnWarps * 8) {   // uniform per warp
+        const int t = base + (lane >> 2);
+        const bool ok = t < t_hi;
+        float acc[REP];
 #pragma unroll
-        for (int s2 = 0; s2 < NP; ++s2) tp[s2] = base + (lane >> 2) + s2 * kSpan;
-        float acc[NP][REP];
-#pragma unroll
-        for (int s2 = 0; s2 < NP; ++s2)
-#pragma unroll
-            for (int h = 0; h < REP; ++h) acc[s2][h] = 0.0f;
+        for (int h = 0; h < REP; ++h) acc[h] = 0.0f;
+        if (ok) {
+            const bool fresh = t == fresh_t;
 #pragma unroll 4
-        for (int q = sub; q < gall; q += 4) {
-            const bool first = q < g1;
-            const int c = first ? q * 8 : (q - g1) * 8;
-            float v[NP][8];
-#pragma unroll
-            for (int s2 = 0; s2 < NP; ++s2) {
-                const int t = tp[s2];
-                if (t >= t_hi) {
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) v[s2][u] = 0.0f;
-                } else if (t == fresh_t) {
+            for (int q = sub; q < gall; q += 4) {
+                const bool first = q < g1;
+                const int c = first ? q * 8 : (q - g1) * 8;
+                float v[8];
+                if (fresh) {
                     const float* f = first ? f1 : f2;
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) v[s2][u] = f[c + u];
+                    for (int u = 0; u < 8; ++u) v[u] = f[c + u];
                 } else {
                     load8<T>(first ? rows1 + static_cast<int64_t>(t) * st1 + c
-                                   : rows2 + static_cast<int64_t>(t) * st2 + c, v[s2]);
+                                   : rows2 + static_cast<int64_t>(t) * st2 + c, v);
                 }
-            }
-            const float* qq = first ? q1 + c : q2 + c;
-            const int qs = first ? w1 : w2;
+                const float* qq = first ? q1 + c : q2 + c;
+                const int qs = first ? w1 : w2;
 #pragma unroll
-            for (int h = 0; h < REP; ++h) {
-                const float4 a = reinterpret_cast<const float4*>(qq + h * qs)[0];
-                const float4 b = reinterpret_cast<const float4*>(qq + h * qs)[1];
-#pragma unroll
-                for (int s2 = 0; s2 < NP; ++s2) {
-                    float r = acc[s2][h];
-                    r = fmaf(a.x, v[s2][0], r);
-                    r = fmaf(a.y, v[s2][1], r);
-                    r = fmaf(a.z, v[s2][2], r);
-                    r = fmaf(a.w, v[s2][3], r);
-                    r = fmaf(b.x, v[s2][4], r);
-                    r = fmaf(b.y, v[s2][5], r);
-                    r = fmaf(b.z, v[s2][6], r);
-                    r = fmaf(b.w, v[s2][7], r);
-                    acc[s2][h] = r;
+                for (int h = 0; h < REP; ++h) {
+                    const float4 a = reinterpret_cast<const float4*>(qq + h * qs)[0];
+                    const float4 b = reinterpret_cast<const float4*>(qq + h * qs)[1];
+                    acc[h] = fmaf(a.x, v[0], acc[h]);
+                    acc[h] = fmaf(a.y, v[1], acc[h]);
+                    acc[h] = fmaf(a.z, v[2], acc[h]);
+                    acc[h] = fmaf(a.w, v[3], acc[h]);
+                    acc[h] = fmaf(b.x, v[4], acc[h]);
+                    acc[h] = fmaf(b.y, v[5], acc[h]);
+                    acc[h] = fmaf(b.z, v[6], acc[h]);
+                    acc[h] = fmaf(b.w, v[7], acc[h]);
                 }
             }
         }
 #pragma unroll
-        for (int s2 = 0; s2 < NP; ++s2)
+        for (int h = 0; h < REP; ++h) {
+            acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 1);
+            acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 2);
+        }
+        if (ok && sub == 0)
 #pragma unroll
-            for (int h = 0; h < REP; ++h) {
-                acc[s2][h] += __shfl_xor_sync(0xffffffffu, acc[s2][h], 1);
-                acc[s2][h] += __shfl_xor_sync(0xffffffffu, acc[s2][h], 2);
-            }
-        if (sub == 0)
-#pragma unroll
-            for (int s2 = 0; s2 < NP; ++s2)
-                if (tp[s2] < t_hi)
-#pragma unroll
-                    for (int h = 0; h < REP; ++h) sc[h * cap + (tp[s2] - t_lo)] = acc[s2][h] * scale;
+            for (int h = 0; h < REP; ++h) sc[h * cap + (t - t_lo)] = acc[h] * scale;
     }
 }
 
@@ -638,12 +617,8 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) mla_decode_ker
             cache_k[(static_cast<int64_t>(pos) * p.kv_heads + g) * R + r] = from_f32<T>(krot[r]);
     }
     // this CTA's positions: latent against q_abs, rope key against q_rope
-    if (cnt > kAttnWarps * 8)   // this CTA's positions
-        split_scores<T, REP, 2>(cache_c, L, qabs, L, cnew, cache_k + g * R, static_cast<int64_t>(p.kv_heads) * R,
-                                qrot, R, krot, t_lo, t_hi, pos, p.scale, sc, cap, warp, lane);
-    else
-        split_scores<T, REP, 1>(cache_c, L, qabs, L, cnew, cache_k + g * R, static_cast<int64_t>(p.kv_heads) * R,
-                                qrot, R, krot, t_lo, t_hi, pos, p.scale, sc, cap, warp, lane);
+    split_scores<T, REP>(cache_c, L, qabs, L, cnew, cache_k + g * R, static_cast<int64_t>(p.kv_heads) * R, qrot, R,
+                         krot, t_lo, t_hi, pos, p.scale, sc, cap, warp, lane);
     __syncthreads();
     split_softmax<T, REP>(cluster, sc, cap, cnt, red, warp, lane);
     __syncthreads();
@@ -764,12 +739,8 @@ __global__ void __launch_bounds__(kAttnThreads, REP <= 4 ? 3 : 2) sw_decode_kern
             vc[(static_cast<int64_t>(slot) * p.kv_heads + g) * D + i] = from_f32<T>(vn[i]);
         }
     // scores of this CTA's ring slots; the new token's slot comes from shared memory
-    if (cnt > kAttnWarps * 8)   // this CTA's positions
-        split_scores<T, REP, 2>(kc + g * D, rs, qrot, D, krot, kc, rs, qrot, 0, krot, t_lo, t_hi, slot, p.scale,
-                                sc, cap, warp, lane);
-    else
-        split_scores<T, REP, 1>(kc + g * D, rs, qrot, D, krot, kc, rs, qrot, 0, krot, t_lo, t_hi, slot, p.scale,
-                                sc, cap, warp, lane);
+    split_scores<T, REP>(kc + g * D, rs, qrot, D, krot, kc, rs, qrot, 0, krot, t_lo, t_hi, slot, p.scale, sc,
+                         cap, warp, lane);
     __syncthreads();
     split_softmax<T, REP>(cluster, sc, cap, cnt, red, warp, lane);
     __syncthreads();
