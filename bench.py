@@ -519,7 +519,7 @@ def bench_config(args, world: int) -> dict:
     }
 
 
-E2E_MIN_STEPS = 500   # ~0.3 s: one host pause of a few ms moves the mean by ~1 %
+E2E_MIN_STEPS = 2000  # ~1.2 s: one ~100 ms host pause (seen once in 500 steps) moves the mean by ~8 %
 E2E_BATCH = 32
 E2E_LAYERS = 8
 E2E_PROMPT = 512
