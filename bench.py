@@ -468,6 +468,10 @@ def run_ours(args, dist: Dist):
                median_ms=round(float(np.median(e2e_steps_ms)), 4),
                p90_ms=round(float(np.percentile(e2e_steps_ms, 90)), 4),
                max_ms=round(float(e2e_steps_ms.max()), 4),
+               # where the slow steps were: index of the slowest, and the steps over 5x the median
+               max_step=int(e2e_steps_ms.argmax()),
+               steps_over_5x_median=[int(i) for i in np.nonzero(e2e_steps_ms > 5 * np.median(e2e_steps_ms))[0][:8]],
+               mean_without_those_ms=round(float(e2e_steps_ms[e2e_steps_ms <= 5 * np.median(e2e_steps_ms)].mean()), 4),
                over_device_step=round(e2e_ms / dec_ms_step, 3),
                path=("ChronosMOEFeedForward.forward (eager), pinned host x -> device -> host y, "
                      "copies on their own streams"))
