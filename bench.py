@@ -382,6 +382,11 @@ def run_ours(args, dist: Dist):
         gc.disable()
         try:
             for i in range(KE):
+                # a serving loop consumes each result: the host waits for step i - 2's
+                # copies before issuing step i (one step of slack keeps the GPU fed,
+                # and the host never runs hundreds of launches ahead)
+                if i >= 2:
+                    eev[i - 2][1].synchronize()
                 flush.zero_()
                 eev[i][0].record()
                 e2e_step()
